@@ -1,0 +1,171 @@
+/*
+ * loopspec_engine.h -- C ABI of the B200-native LoopSpec decode engine
+ * (libloopspec_engine.so, built for sm_100a).
+ *
+ * One engine handle serves one looped model on one GPU and runs one request
+ * at a time, like the reference's batch-1 LoopSpec server
+ * (sglang_recurrent/server/cli.py:88-89). Plain pointers and sizes only: no
+ * torch types cross this boundary. Weight pointers are device pointers owned
+ * by the caller; the engine owns its KV pool, timeline mapping table, state
+ * banks and workspaces. Every function returns 0 on success or a negative
+ * LS_E* code; ls_last_error() returns the message. Calls on one handle must
+ * not overlap (single-threaded per handle, stream-ordered inside).
+ */
+#ifndef LOOPSPEC_ENGINE_H
+#define LOOPSPEC_ENGINE_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LS_OK 0
+#define LS_EINVAL (-1)      /* invalid argument or state                       */
+#define LS_ECAPACITY (-2)   /* slots / rows / lanes exhausted (the reference's
+                               RuntimeErrors: decode_slots.py:129-134,
+                               manager.py:216-217, executor.py:87-93)         */
+#define LS_ECUDA (-3)       /* CUDA runtime or driver error                    */
+#define LS_EDEVICE (-4)     /* a kernel reported a bounded-wait timeout or a
+                               bad index (see ls_last_error)                   */
+#define LS_EPIPELINE (-5)   /* scheduler invariant violated (pipeline.py:298-421) */
+
+/* Model families / block layouts (modeling/contracts.py:179-197). */
+#define LS_FAMILY_OURO 0
+#define LS_FAMILY_RAVEN 1
+#define LS_LAYOUT_OURO 0       /* Gemma2 residual flow, sandwich RMSNorm      */
+#define LS_LAYOUT_RAVEN_PRE 1  /* Llama pre-norm                              */
+#define LS_LAYOUT_OLMO_POST 2  /* OLMo2 post-norm + QK-norm                   */
+
+typedef struct ls_model_cfg {
+  int32_t family, layout;
+  int32_t hidden, n_heads, n_kv_heads, head_dim, intermediate, vocab;
+  int32_t n_pre_layers, n_core_layers, n_post_layers;
+  int32_t stages;            /* S: total_ut_steps / mean_recurrence */
+  float rope_theta, rms_eps, embed_scale, init_std;
+  uint64_t init_seed;        /* Raven position-keyed hidden init */
+  int32_t qk_norm, adapter_bias, tie_embeddings;
+} ls_model_cfg;
+
+/* Schedule and capacities. step_size = K (--first), second_step = X =
+ * D / K (--second D), 0 = no q2 (pipeline.py:124-139). */
+typedef struct ls_sched_cfg {
+  int32_t step_size, second_step;
+  int32_t max_context;       /* max positions per timeline (prompt + output) */
+  int32_t max_prompt;        /* longest prompt accepted by ls_prefill        */
+  int32_t kv_slots;          /* KV token slots per attention layer (0: auto) */
+  int32_t request_rows;      /* timeline mapping rows (0: auto)              */
+  int32_t use_graphs;        /* capture one CUDA graph per (role, width)     */
+  int32_t use_pdl;           /* programmatic dependent launch between kernels */
+} ls_sched_cfg;
+
+/* Counters of sglang_recurrent/loopspec/executor.py:35-45 plus timing. */
+typedef struct ls_stats {
+  int64_t pipeline_cycles, pre_rows, recurrent_rows, post_rows;
+  int64_t verified_proposals, first_rejections, second_verifications;
+  int64_t second_acceptances, second_rejections;
+  int64_t decode_tokens;     /* committed tokens after the first */
+  double decode_device_ms;   /* CUDA-event time of the decode loop            */
+  double decode_host_s;      /* host clock, after first token to last commit  */
+  double prefill_device_ms;
+} ls_stats;
+
+typedef struct ls_engine ls_engine;
+
+/* Create an engine on `device` (replaces make_loopspec_runner,
+ * server/loopspec_runner.py:118-195). */
+int ls_create(const ls_model_cfg* model, const ls_sched_cfg* sched, int device, ls_engine** out);
+
+/* Borrow one bf16 weight (device pointer) under the reference's internal
+ * parameter name (RecurrentServingModel.load_weights, modeling/serving.py:142-182;
+ * names after ouro.py:19-34 / raven.py:221-255 mapping, packed qkv_proj and
+ * gate_up_proj). dtype: 0 = bf16 (the only accepted type). */
+int ls_load_weight(ls_engine* eng, const char* name, const void* dptr, int dtype,
+                   const int64_t* shape, int ndim);
+
+/* Validate the weight set, allocate pools and build TMA descriptors. */
+int ls_finalize(ls_engine* eng);
+
+/* Reset request state and prefill every timeline of the prompt (pre, all S
+ * core depths, each post endpoint with attention), then pick the first token
+ * greedily (RecurrentRequest.prefill request.py:111-192 and
+ * _sample_first_token executor.py:161-182). out_logits: optional host
+ * float[vocab] receiving the final-depth logits of the last prompt token. */
+int ls_prefill(ls_engine* eng, const int64_t* prompt, int n_prompt, float* out_logits,
+               int64_t* first_token);
+
+/* One pipeline cycle over `n_lanes` lanes (LosslessLoopSpecExecutor.forward,
+ * executor.py:293-367, without the decision policy): pre for stage-0 lanes,
+ * K core iterations for all lanes, post + greedy argmax for lanes whose last
+ * iteration is a q1/q2/final readout. lanes: int64 [n_lanes][6] =
+ * (stage, index, token, branch, parent_branch or -1, state_slot).
+ * out_decisions: int64 [n_lanes], argmax token for endpoint lanes, -1 else.
+ * out_logits: optional host float [n_lanes][vocab] (rows of non-endpoint
+ * lanes are left untouched). Synchronises once (decision readback). */
+int ls_cycle(ls_engine* eng, const int64_t* lanes, int n_lanes, int64_t* out_decisions,
+             float* out_logits);
+
+/* Keep the timelines of the surviving lanes and release the rest
+ * (BranchManager.retain_branches, branching/manager.py:453-482).
+ * branch_ids / parent_ids: int64 [n] (parent -1 for none); n = 0 ends the
+ * request and frees every branch. */
+int ls_retain(ls_engine* eng, const int64_t* branch_ids, const int64_t* parent_ids, int n);
+
+/* Whole request natively: prefill, first token, then the LoopSpec pipeline
+ * (mode 0: continue_pipelined pipeline.py:254-423 with greedy decisions
+ * decisions.py:136-184) or plain autoregressive decoding (mode 1: one token
+ * per step through pre, S core iterations and post, serving.py:216-239).
+ * stop_token < 0 disables EOS stopping. out_ids: int64 [max_new_tokens]. */
+int ls_generate(ls_engine* eng, const int64_t* prompt, int n_prompt, int max_new_tokens,
+                int mode, int64_t stop_token, int64_t* out_ids, int* n_out, ls_stats* stats);
+
+/* The native scheduler loop of ls_generate mode 0 (continue_pipelined,
+ * pipeline.py:254-423, with greedy resolve decisions.py:136-184 and the
+ * executor's state-slot pool and counters executor.py:76-107,239-290),
+ * driven by host callbacks instead of the GPU: `decide` returns the token a
+ * readout of lane (index, input token) yields (kind 0 q1, 1 q2, 2 final);
+ * `on_cycle` sees each cycle's lanes as int64 [n][7] = (stage, index,
+ * token, branch, parent|-1, origin_stage|-1, state_slot); `on_retain` sees
+ * each retention as int64 [n][2] = (branch, parent|-1) plus the accepted
+ * stage (-1 for none). Needs no GPU. */
+typedef int64_t (*ls_decide_fn)(void* user, int64_t index, int64_t token, int32_t kind);
+typedef void (*ls_cycle_fn)(void* user, const int64_t* lanes, int32_t n);
+typedef void (*ls_retain_fn)(void* user, const int64_t* pairs, int32_t n, int32_t accepted_stage);
+int ls_pipeline_simulate(int stages, int step_size, int second_step, int64_t first_token,
+                         int max_new_tokens, int64_t stop_token, ls_decide_fn decide,
+                         ls_cycle_fn on_cycle, ls_retain_fn on_retain, void* user,
+                         int64_t* out_ids, int* n_out, ls_stats* stats);
+
+/* Time one role call of `n_lanes` synthetic lanes (role 0 pre, 1 core, 2
+ * post) `iters` times with CUDA events on the engine stream, after a
+ * prefill; returns the average device milliseconds per call. Used by the
+ * benchmark's roofline report. context_len sets every lane's position. */
+int ls_time_role(ls_engine* eng, int role, int n_lanes, int context_len, int iters,
+                 double* avg_ms);
+
+/* Time one GEMM of the core layer 0 (which: 0 qkv, 1 o, 2 gate_up, 3 down,
+ * 4 lm_head) over n_lanes lanes, `iters` launches; average device ms. */
+int ls_time_gemm(ls_engine* eng, int which, int n_lanes, int iters, double* avg_ms);
+
+/* Number of kernels one role call of n_lanes launches. */
+int ls_role_kernel_count(ls_engine* eng, int role, int n_lanes, int* count);
+
+/* Run one GEMM of core layer 0 (which: 0 qkv, 1 o, 2 gate_up, 3 down,
+ * 4 lm_head, 5 Raven adapter) on host activations x (bf16 bits [n][K]) and
+ * return the split-summed fp32 result [n][rows], for kernel tests. */
+int ls_debug_gemm(ls_engine* eng, int which, int n_lanes, const uint16_t* x, float* out);
+int ls_gemm_splits(ls_engine* eng, int which, int* splits, int* rows, int* k);
+
+/* Device pointer of the engine's KV pool (K then V, each
+ * [attn_layers][kv_slots][n_kv_heads*head_dim] bf16), for tests. */
+int ls_debug_kv(ls_engine* eng, void** k_pool, void** v_pool, int* kv_slots, int* attn_layers);
+
+int ls_destroy(ls_engine* eng);
+const char* ls_last_error(ls_engine* eng);
+const char* ls_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LOOPSPEC_ENGINE_H */

@@ -93,7 +93,7 @@ PRESETS = {
     # small Raven shapes for CPU-oracle parity tests
     "tiny-raven-llama": ModelConfig(
         name="tiny-raven-llama", family="raven", layout="raven_pre", hidden=256,
-        n_heads=8, n_kv_heads=2, head_dim=32, intermediate=512, vocab=4096,
+        n_heads=4, n_kv_heads=1, head_dim=64, intermediate=512, vocab=4096,
         n_pre_layers=1, n_core_layers=2, n_post_layers=1, stages=8,
         rope_theta=50000.0, embed_scale=16.0, init_std=math.sqrt(2 / (5 * 256))),
     "tiny-raven-olmo": ModelConfig(

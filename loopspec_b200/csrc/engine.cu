@@ -1,0 +1,1746 @@
+// LoopSpec decode engine for B200 (sm_100a): host runtime and C ABI.
+//
+// The engine owns, per model: the paged KV pool (one slot per token per
+// timeline, page size 1), the timeline mapping table (row -> slot per
+// position), the hidden/injected state banks, and the workspaces of one role
+// call. A role call (pre / core / post over B lanes) is a fixed kernel
+// sequence that reads lane metadata from a device buffer, so it is captured
+// once per (role, B) as a CUDA graph and replayed after a small metadata
+// upload. The host side restates the reference's branch-timeline bookkeeping
+// (sglang_recurrent/loopspec/branching/manager.py), executor
+// (loopspec/executor.py) and scheduler loop (loopspec/pipeline.py) in C++ so a
+// whole request runs without Python in the loop.
+
+#include "../../include/loopspec_engine.h"
+#include "common.cuh"
+#include "gemm_tc.cuh"
+#include "kernels.cuh"
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstring>
+#include <functional>
+#include <map>
+#include <memory>
+#include <queue>
+#include <set>
+#include <stdexcept>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+using namespace ls;
+typedef __nv_bfloat16 bf16;
+
+namespace {
+
+struct EngineError : std::runtime_error {
+  int code;
+  EngineError(int c, const std::string& m) : std::runtime_error(m), code(c) {}
+};
+
+#define CK(x)                                                                            \
+  do {                                                                                   \
+    cudaError_t e_ = (x);                                                                \
+    if (e_ != cudaSuccess)                                                               \
+      throw EngineError(LS_ECUDA, std::string(#x) + ": " + cudaGetErrorString(e_));      \
+  } while (0)
+
+#define REQUIRE(cond, code, msg)                  \
+  do {                                                \
+    if (!(cond)) throw EngineError((code), (msg));    \
+  } while (0)
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    CK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q));
+    REQUIRE(q == cudaDriverEntryPointSuccess && p, LS_ECUDA, "cuTensorMapEncodeTiled unavailable");
+    fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// 2-D bf16 tensor map [rows][inner], 128-byte swizzle, box {64, box_rows}.
+CUtensorMap make_map_2d(const void* base, uint64_t inner, uint64_t rows, uint32_t box_rows) {
+  REQUIRE((reinterpret_cast<uintptr_t>(base) & 15) == 0, LS_EINVAL, "TMA base must be 16-byte aligned");
+  REQUIRE((inner * 2) % 16 == 0, LS_EINVAL, "TMA row pitch must be a multiple of 16 bytes");
+  CUtensorMap m;
+  cuuint64_t dims[2] = {inner, rows};
+  cuuint64_t strides[1] = {inner * 2};
+  cuuint32_t box[2] = {(cuuint32_t)kGemmBK, box_rows};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = get_encode()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
+                            strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  REQUIRE(r == CUDA_SUCCESS, LS_ECUDA, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+  return m;
+}
+
+int round_up(int x, int m) { return (x + m - 1) / m * m; }
+int cdiv(long a, long b) { return (int)((a + b - 1) / b); }
+
+struct Gemm {
+  const bf16* w = nullptr;
+  int Mw = 0, K = 0, splits = 1;
+  CUtensorMap map;
+};
+
+struct XBuf {
+  bf16* ptr = nullptr;
+  int K = 0, rows = 0;
+  std::map<int, CUtensorMap> by_bn;
+  const CUtensorMap& map(int bn) {
+    auto it = by_bn.find(bn);
+    if (it == by_bn.end()) it = by_bn.emplace(bn, make_map_2d(ptr, K, rows, bn)).first;
+    return it->second;
+  }
+};
+
+struct LayerW {
+  const bf16 *qkv = nullptr, *o = nullptr, *gu = nullptr, *down = nullptr;
+  const bf16 *n_in = nullptr, *n_pa = nullptr, *n_pf = nullptr, *n_pff = nullptr;
+  const bf16 *qn = nullptr, *kn = nullptr;
+  Gemm g_qkv, g_o, g_gu, g_down;
+};
+
+enum Role { kPre = 0, kCore = 1, kPost = 2 };
+
+struct Stack {
+  std::vector<LayerW> layers;
+  int kv_base = 0;
+};
+
+// What the last layer of a stack produces besides h.
+struct StackEnd {
+  const bf16* final_norm = nullptr;  // Ouro step_norm
+  float* bank = nullptr;             // scatter h into this bank at state_out
+  bool want_x = false;               // produce x for a following GEMM
+  const bf16* x_norm = nullptr;      // ... normalised by this weight (Raven ln_f)
+};
+
+// Launch with optional programmatic-dependent-launch attribute.
+template <typename... KArgs, typename... Args>
+void launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl,
+            Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = pdl ? attr : nullptr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  CK(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
+}
+
+double now_s() {
+  return std::chrono::duration<double>(std::chrono::steady_clock::now().time_since_epoch()).count();
+}
+
+}  // namespace
+
+// ===================================================================== timelines
+// Host bookkeeping of branch KV timelines, restating
+// sglang_recurrent/loopspec/branching/manager.py:
+//   TimelineCursor :45-63, _TimelineManager.fork :207-232 / release :234-250,
+//   BranchManager.get_or_create_cursors :357-388, _release_unused_branch
+//   :390-408, _transfer_timeline_ownership :410-429, _detach_from_unused_parent
+//   :431-451, retain_branches :453-482.
+// Rows index the device mapping table; slots index the KV pool. Both come from
+// free stacks owned here (the reference keeps a GPU-side slot ring mirrored on
+// the CPU, decode_slots.py; this engine uploads the chosen slot ids with the
+// lane metadata instead).
+namespace {
+
+struct Cursor {
+  int row = -1;
+  int seq_len = 0;
+  int pending_parent_row = -1;
+  std::vector<int> owned;   // decode slots this cursor frees on release
+};
+
+struct Node {
+  int id = 0;
+  Node* parent = nullptr;
+  std::map<int, Cursor*> cur[3];
+  int child_count = 0;
+  bool live = true;
+};
+
+class Timelines {
+ public:
+  void configure(int rows, int slots) {
+    rows_ = rows;
+    slots_ = slots;
+    reset();
+  }
+
+  void reset() {
+    for (auto& kv : nodes_) {
+      for (auto& m : kv.second->cur)
+        for (auto& c : m) delete c.second;
+      delete kv.second;
+    }
+    nodes_.clear();
+    free_rows_.clear();
+    for (int r = rows_ - 1; r >= 0; --r) free_rows_.push_back(r);
+    free_slots_.clear();
+    for (int s = slots_ - 1; s >= 0; --s) free_slots_.push_back(s);
+  }
+
+  ~Timelines() { reset(); }
+
+  int alloc_slot() {
+    REQUIRE(!free_slots_.empty(), LS_ECAPACITY, "KV slot pool exhausted");
+    int s = free_slots_.back();
+    free_slots_.pop_back();
+    return s;
+  }
+
+  int alloc_row() {
+    REQUIRE(!free_rows_.empty(), LS_ECAPACITY, "recurrent branch ran out of request-pool rows");
+    int r = free_rows_.back();
+    free_rows_.pop_back();
+    return r;
+  }
+
+  // A full-prompt timeline owned by the root; its prompt slots are returned
+  // with the whole pool at request end, as the reference's eager prefill does.
+  Cursor* create_root_cursor(int role, int depth) {
+    Node* root = node_or_null(0);
+    if (!root) {
+      root = new Node();
+      nodes_[0] = root;
+    }
+    Cursor* c = new Cursor();
+    c->row = alloc_row();
+    root->cur[role][depth] = c;
+    return c;
+  }
+
+  Node* node_or_null(int id) {
+    auto it = nodes_.find(id);
+    return it == nodes_.end() ? nullptr : it->second;
+  }
+
+  Node* get_or_create_branch(int id, int parent_id) {
+    Node* n = node_or_null(id);
+    if (n) return n;
+    Node* p = node_or_null(parent_id);
+    REQUIRE(p, LS_EPIPELINE,
+            "branch " + std::to_string(id) + " has unavailable parent " + std::to_string(parent_id));
+    n = new Node();
+    n->id = id;
+    n->parent = p;
+    p->child_count += 1;
+    nodes_[id] = n;
+    return n;
+  }
+
+  Cursor* get_or_create_cursor(int role, int depth, int branch, int parent) {
+    Node* n = get_or_create_branch(branch, parent);
+    auto it = n->cur[role].find(depth);
+    if (it != n->cur[role].end()) return it->second;
+    REQUIRE(n->parent, LS_EPIPELINE, "root branch is missing a timeline");
+    auto pit = n->parent->cur[role].find(depth);
+    REQUIRE(pit != n->parent->cur[role].end(), LS_EPIPELINE, "parent timeline missing for fork");
+    Cursor* c = new Cursor();
+    c->row = alloc_row();
+    c->seq_len = pit->second->seq_len;
+    c->pending_parent_row = pit->second->row;
+    n->cur[role][depth] = c;
+    return c;
+  }
+
+  void retain(const std::vector<std::pair<int, int>>& lanes /* (branch, parent) */) {
+    std::vector<std::pair<int, int>> sorted = lanes;
+    std::sort(sorted.begin(), sorted.end());
+    for (auto& bp : sorted)
+      if (bp.first && !node_or_null(bp.first)) get_or_create_branch(bp.first, bp.second);
+    std::set<int> keep;
+    for (auto& bp : lanes) keep.insert(bp.first);
+    std::vector<int> unused;
+    for (auto& kv : nodes_)
+      if (kv.second->live && !keep.count(kv.first)) unused.push_back(kv.first);
+    std::sort(unused.rbegin(), unused.rend());
+    for (int id : unused) {
+      Node* n = node_or_null(id);
+      if (!n) continue;
+      n->live = false;
+      release_unused(n);
+    }
+    std::vector<int> ids;
+    for (auto& kv : nodes_) ids.push_back(kv.first);
+    for (int id : ids) {
+      Node* n = node_or_null(id);
+      if (n) detach_from_unused_parent(n);
+    }
+  }
+
+  size_t live_nodes() const { return nodes_.size(); }
+  size_t free_slots() const { return free_slots_.size(); }
+  size_t free_rows() const { return free_rows_.size(); }
+
+ private:
+  void release_cursor(Cursor* c) {
+    for (int s : c->owned) free_slots_.push_back(s);
+    free_rows_.push_back(c->row);
+    delete c;
+  }
+
+  void release_unused(Node* n) {
+    while (n && !n->live && n->child_count == 0) {
+      for (auto& m : n->cur)
+        for (auto& c : m) release_cursor(c.second);
+      Node* p = n->parent;
+      nodes_.erase(n->id);
+      delete n;
+      if (!p) break;
+      p->child_count -= 1;
+      n = p;
+    }
+  }
+
+  void detach_from_unused_parent(Node* n) {
+    Node* p = n->parent;
+    if (!p || p->live || p->child_count != 1) return;
+    for (int role = 0; role < 3; ++role) {
+      auto& pc = p->cur[role];
+      auto& cc = n->cur[role];
+      for (auto it = pc.begin(); it != pc.end();) {
+        auto cit = cc.find(it->first);
+        if (cit == cc.end()) {
+          cc[it->first] = it->second;
+          it = pc.erase(it);
+        } else {
+          auto& own = cit->second->owned;
+          own.insert(own.begin(), it->second->owned.begin(), it->second->owned.end());
+          it->second->owned.clear();
+          ++it;
+        }
+      }
+    }
+    n->parent = nullptr;
+    p->child_count -= 1;
+    release_unused(p);
+  }
+
+  int rows_ = 0, slots_ = 0;
+  std::map<int, Node*> nodes_;
+  std::vector<int> free_rows_, free_slots_;
+};
+
+}  // namespace
+
+// ======================================================================= engine
+struct ls_engine {
+  ls_model_cfg mc{};
+  ls_sched_cfg sc{};
+  int device = 0;
+  int num_sms = 148;
+  std::string last_error;
+  bool finalized = false;
+
+  // schedule (pipeline.py:124-251)
+  int S = 0, K = 1, X = 0;
+  std::map<int, int> endpoint_kind;  // end stage -> 0 q1, 1 q2, 2 final
+  int max_rows = 0, depth = 0;
+
+  // weights
+  std::map<std::string, std::pair<const bf16*, std::vector<int64_t>>> weights;
+  Stack pre, core, post;
+  const bf16 *embed = nullptr, *lm_head = nullptr, *step_norm = nullptr, *final_norm = nullptr;
+  const bf16 *adapter_b = nullptr;
+  Gemm g_adapter, g_lm;
+
+  // sizes
+  int H = 0, QD = 0, KVD = 0, I = 0, V = 0, HD = 0, NH = 0, NKV = 0;
+  int cap = 0;           // lanes per role call
+  int prefill_chunk = 128;
+  int n_attn_layers = 0, n_slots = 0, rows = 0, max_ctx = 0, max_chunks = 0, bank_rows = 0;
+
+  // device memory
+  cudaStream_t stream = nullptr;
+  std::vector<void*> allocs;
+  bf16 *kpool = nullptr, *vpool = nullptr;
+  int* map = nullptr;
+  float *bank_h = nullptr, *bank_inj = nullptr;
+  int* meta_dev = nullptr;      // [3][F][cap]
+  int* meta_host = nullptr;     // pinned [kStaging][F][cap]
+  int staging_next = 0;
+  static constexpr int kStaging = 64;
+  float *h = nullptr, *r = nullptr, *q = nullptr, *part = nullptr, *o_part = nullptr,
+        *ml_part = nullptr, *logits = nullptr, *inv_freq = nullptr;
+  long part_elems = 0;
+  XBuf x_h, x_attn, x_act, x_cat;
+  long long *amax_dev = nullptr, *amax_host = nullptr;
+  float* logits_host = nullptr;
+  int* err_dev = nullptr;
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+
+  std::map<std::pair<int, int>, cudaGraphExec_t> graphs;
+  int kernels_in_call = 0;
+
+  Timelines tl;
+  int prefill_len = -1;   // len(prompt) - 1 of the current request
+
+  // ----------------------------------------------------------------- memory
+  template <typename T>
+  T* dalloc(size_t n) {
+    void* p = nullptr;
+    CK(cudaMalloc(&p, std::max<size_t>(n, 1) * sizeof(T)));
+    CK(cudaMemset(p, 0, std::max<size_t>(n, 1) * sizeof(T)));
+    allocs.push_back(p);
+    return static_cast<T*>(p);
+  }
+
+  ~ls_engine() {
+    if (device >= 0) cudaSetDevice(device);
+    for (auto& g : graphs) cudaGraphExecDestroy(g.second);
+    for (void* p : allocs) cudaFree(p);
+    if (meta_host) cudaFreeHost(meta_host);
+    if (amax_host) cudaFreeHost(amax_host);
+    if (logits_host) cudaFreeHost(logits_host);
+    if (ev0) cudaEventDestroy(ev0);
+    if (ev1) cudaEventDestroy(ev1);
+    if (stream) cudaStreamDestroy(stream);
+  }
+
+  // ---------------------------------------------------------------- weights
+  const bf16* W(const std::string& name, std::vector<int64_t> shape, bool required = true) {
+    auto it = weights.find(name);
+    if (it == weights.end()) {
+      REQUIRE(!required, LS_EINVAL, "missing weight " + name);
+      return nullptr;
+    }
+    REQUIRE(it->second.second == shape, LS_EINVAL, "weight " + name + " has the wrong shape");
+    return it->second.first;
+  }
+
+  int choose_splits(int Mw, int Kd) const {
+    const int tiles = cdiv(Mw, kGemmBM);
+    const int KB = cdiv(Kd, kGemmBK);
+    int s = (2 * num_sms + tiles / 2) / tiles;
+    return std::max(1, std::min(s, KB));
+  }
+
+  Gemm make_gemm(const bf16* w, int Mw, int Kd, int splits = 0) {
+    Gemm g;
+    g.w = w;
+    g.Mw = Mw;
+    g.K = Kd;
+    g.splits = splits > 0 ? splits : choose_splits(Mw, Kd);
+    g.map = make_map_2d(w, Kd, Mw, kGemmBM);
+    part_elems = std::max(part_elems, (long)g.splits * cap * Mw);
+    return g;
+  }
+
+  void load_stack(Stack& st, const std::string& prefix, int n) {
+    const int L = mc.layout;
+    st.layers.resize(n);
+    for (int i = 0; i < n; ++i) {
+      const std::string p = prefix + std::to_string(i) + ".";
+      LayerW& lw = st.layers[i];
+      lw.qkv = W(p + "self_attn.qkv_proj.weight", {QD + 2 * KVD, H});
+      lw.o = W(p + "self_attn.o_proj.weight", {H, QD});
+      lw.gu = W(p + "mlp.gate_up_proj.weight", {2 * I, H});
+      lw.down = W(p + "mlp.down_proj.weight", {H, I});
+      if (L == LS_LAYOUT_OURO || L == LS_LAYOUT_RAVEN_PRE)
+        lw.n_in = W(p + "input_layernorm.weight", {H});
+      lw.n_pa = W(p + "post_attention_layernorm.weight", {H});
+      if (L == LS_LAYOUT_OURO) lw.n_pf = W(p + "pre_feedforward_layernorm.weight", {H});
+      if (L == LS_LAYOUT_OURO || L == LS_LAYOUT_OLMO_POST)
+        lw.n_pff = W(p + "post_feedforward_layernorm.weight", {H});
+      if (mc.qk_norm) {
+        lw.qn = W(p + "self_attn.q_norm.weight", {QD});
+        lw.kn = W(p + "self_attn.k_norm.weight", {KVD});
+      }
+      lw.g_qkv = make_gemm(lw.qkv, QD + 2 * KVD, H);
+      lw.g_o = make_gemm(lw.o, H, QD);
+      lw.g_gu = make_gemm(lw.gu, 2 * I, H);
+      lw.g_down = make_gemm(lw.down, H, I);
+    }
+  }
+
+  // ---------------------------------------------------------------- finalize
+  void finalize() {
+    REQUIRE(!finalized, LS_EINVAL, "engine already finalized");
+    CK(cudaSetDevice(device));
+    CK(cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, device));
+    int major = 0, minor = 0;
+    CK(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device));
+    CK(cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device));
+    REQUIRE(major == 10 && minor == 0, LS_ECUDA, "this engine is built for sm_100a (B200) only");
+    CK(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+    CK(cudaEventCreate(&ev0));
+    CK(cudaEventCreate(&ev1));
+
+    H = mc.hidden;
+    NH = mc.n_heads;
+    NKV = mc.n_kv_heads;
+    HD = mc.head_dim;
+    QD = NH * HD;
+    KVD = NKV * HD;
+    I = mc.intermediate;
+    V = mc.vocab;
+    REQUIRE(NH % NKV == 0, LS_EINVAL, "n_heads must be a multiple of n_kv_heads");
+    const int G = NH / NKV;
+    REQUIRE((HD == 64 && (G == 1 || G == 2 || G == 4)) || (HD == 128 && (G == 1 || G == 2)),
+            LS_EINVAL, "unsupported head_dim / GQA group");
+    REQUIRE(H % 64 == 0 && I % 64 == 0 && QD % 64 == 0, LS_EINVAL, "hidden/intermediate must be multiples of 64");
+    REQUIRE(H <= 8192 && QD + 2 * KVD <= 12288, LS_EINVAL, "row too long for the epilogue kernels");
+
+    cap = std::max(max_rows, prefill_chunk);
+    max_ctx = sc.max_context;
+    REQUIRE(max_ctx > 1 && sc.max_prompt >= 1 && sc.max_prompt < max_ctx, LS_EINVAL,
+            "need 1 <= max_prompt < max_context");
+    max_chunks = cdiv(max_ctx, kAttnChunk);
+    bank_rows = max_rows + prefill_chunk;
+    n_attn_layers = mc.n_pre_layers + mc.n_core_layers + mc.n_post_layers;
+
+    // timelines per branch: pre (if attention), S core, one post per endpoint
+    const int n_timelines = (mc.n_pre_layers ? 1 : 0) + S +
+                            (mc.n_post_layers ? (int)endpoint_kind.size() : 0);
+    if (sc.request_rows > 0) {
+      rows = sc.request_rows;
+    } else {
+      // schedule bound of pipeline.py:195-230 plus the prompt timelines
+      std::vector<long> births = birth_sizes();
+      births.push_back(X == 0 ? 1 : births.back() + births[depth - X]);
+      std::vector<int> post_steps;
+      for (auto& e : endpoint_kind) post_steps.push_back(e.first / K + 1);
+      const int hp = mc.n_pre_layers ? 1 : 0, hq = mc.n_post_layers ? 1 : 0;
+      long total = 2L * (S + hp + hq * (long)post_steps.size());
+      for (int age = 1; age <= depth; ++age) {
+        int reached = 0;
+        for (int st : post_steps) reached += st <= age;
+        total += births[depth + 1 - age] * (K * age + hp + hq * reached);
+      }
+      rows = (int)total + n_timelines;
+    }
+    if (sc.kv_slots > 0) {
+      n_slots = sc.kv_slots;
+    } else {
+      n_slots = n_timelines * (max_ctx + 2 * max_rows) + 2 * rows;
+    }
+    tl.configure(rows, n_slots);
+
+    // weights
+    embed = W("pre_executor.embed_tokens.weight", {V, H});
+    lm_head = mc.tie_embeddings ? embed : W("post_executor.lm_head.weight", {V, H});
+    load_stack(pre, "pre_executor.blocks.", mc.n_pre_layers);
+    load_stack(core, "recurrent_executor.blocks.", mc.n_core_layers);
+    load_stack(post, "post_executor.blocks.", mc.n_post_layers);
+    pre.kv_base = 0;
+    core.kv_base = mc.n_pre_layers;
+    post.kv_base = mc.n_pre_layers + mc.n_core_layers;
+    if (mc.family == LS_FAMILY_OURO) {
+      step_norm = W("recurrent_executor.step_norm.weight", {H});
+    } else {
+      g_adapter = make_gemm(W("recurrent_executor.adapter.weight", {H, 2 * H}), H, 2 * H);
+      if (mc.adapter_bias) adapter_b = W("recurrent_executor.adapter.bias", {H});
+      final_norm = W("post_executor.final_norm.weight", {H});
+    }
+    g_lm = make_gemm(lm_head, V, H, 1);
+    REQUIRE(mc.n_core_layers > 0, LS_EINVAL, "core needs at least one layer");
+
+    // device memory
+    const long kv_elems = (long)n_attn_layers * n_slots * KVD;
+    kpool = dalloc<bf16>(kv_elems);
+    vpool = dalloc<bf16>(kv_elems);
+    map = dalloc<int>((long)rows * max_ctx);
+    bank_h = dalloc<float>((long)bank_rows * H);
+    bank_inj = dalloc<float>((long)bank_rows * H);
+    meta_dev = dalloc<int>(3L * kMetaFields * cap);
+    CK(cudaMallocHost(&meta_host, sizeof(int) * (size_t)kStaging * kMetaFields * cap));
+    h = dalloc<float>((long)cap * H);
+    r = dalloc<float>((long)cap * H);
+    q = dalloc<float>((long)cap * QD);
+    part = dalloc<float>(part_elems);
+    o_part = dalloc<float>((long)cap * NH * max_chunks * HD);
+    ml_part = dalloc<float>((long)cap * NH * max_chunks * 2);
+    logits = dalloc<float>((long)cap * V);
+    const int xrows = round_up(cap, 256);
+    auto mkx = [&](XBuf& xb, int Kd) {
+      xb.K = Kd;
+      xb.rows = xrows;
+      xb.ptr = dalloc<bf16>((long)xrows * Kd);
+    };
+    mkx(x_h, H);
+    mkx(x_attn, QD);
+    mkx(x_act, I);
+    if (mc.family == LS_FAMILY_RAVEN) mkx(x_cat, 2 * H);
+    amax_dev = dalloc<long long>(cap);
+    CK(cudaMallocHost(&amax_host, sizeof(long long) * cap));
+    CK(cudaMallocHost(&logits_host, sizeof(float) * (size_t)V));
+    err_dev = dalloc<int>(1);
+    std::vector<float> inv(HD / 2);
+    for (int i = 0; i < HD / 2; ++i)
+      inv[i] = (float)(1.0 / std::pow((double)mc.rope_theta, (2.0 * i) / HD));
+    inv_freq = dalloc<float>(HD / 2);
+    CK(cudaMemcpy(inv_freq, inv.data(), sizeof(float) * inv.size(), cudaMemcpyHostToDevice));
+
+    set_smem_attrs();
+    finalized = true;
+  }
+
+  std::vector<long> birth_sizes() const {
+    std::vector<long> b;
+    if (X == 0) {
+      b.assign(depth, 1);
+    } else {
+      b.assign(X, 1);
+      for (int t = X; t < depth; ++t) b.push_back(b[t - 1] + b[t - X]);
+    }
+    return b;
+  }
+
+  void set_smem_attrs() {
+#define LS_SMEM(BN, ST)                                                                    \
+  CK(cudaFuncSetAttribute(gemm_tc_kernel<BN, ST>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                          GemmSmem<BN, ST>::kTotal))
+    LS_SMEM(16, 4);
+    LS_SMEM(32, 4);
+    LS_SMEM(64, 4);
+    LS_SMEM(128, 4);
+    LS_SMEM(256, 3);
+#undef LS_SMEM
+    const int row_smem = std::max(QD + 2 * KVD, 2 * H) * (int)sizeof(float);
+    CK(cudaFuncSetAttribute(qkv_epi_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, row_smem));
+    CK(cudaFuncSetAttribute(resid_epi_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, row_smem));
+    CK(cudaFuncSetAttribute(prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, row_smem));
+  }
+};
+
+// ============================================================ role kernel chains
+namespace {
+
+Meta meta_of(ls_engine& e, int role) {
+  return Meta{e.meta_dev + (long)role * kMetaFields * e.cap, e.cap};
+}
+
+int pick_bn(int n) {
+  if (n <= 16) return 16;
+  if (n <= 32) return 32;
+  if (n <= 64) return 64;
+  if (n <= 128) return 128;
+  return 256;
+}
+
+void gemm(ls_engine& e, const Gemm& g, XBuf& x, float* out, int n, int x_row0 = 0) {
+  REQUIRE(n >= 1 && x_row0 + n <= x.rows, LS_EINVAL, "GEMM lane count out of range");
+  const int bn = pick_bn(n);
+  const CUtensorMap& xm = x.map(bn);
+  dim3 grid(cdiv(g.Mw, kGemmBM), g.splits, cdiv(n, bn));
+  const long ss = (long)e.cap * g.Mw;
+  const bool pdl = e.sc.use_pdl != 0;
+  const dim3 blk(kGemmThreads);
+#define LS_GEMM(BN, ST)                                                                      \
+  launch(gemm_tc_kernel<BN, ST>, grid, blk, GemmSmem<BN, ST>::kTotal, e.stream, pdl, g.map, xm, \
+         out, g.Mw, g.K, n, x_row0, g.splits, ss, e.err_dev)
+  switch (bn) {
+    case 16: LS_GEMM(16, 4); break;
+    case 32: LS_GEMM(32, 4); break;
+    case 64: LS_GEMM(64, 4); break;
+    case 128: LS_GEMM(128, 4); break;
+    default: LS_GEMM(256, 3); break;
+  }
+#undef LS_GEMM
+  e.kernels_in_call++;
+}
+
+template <typename... KArgs, typename... Args>
+void klaunch(ls_engine& e, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+             Args&&... args) {
+  launch(kernel, grid, block, smem, e.stream, e.sc.use_pdl != 0, std::forward<Args>(args)...);
+  e.kernels_in_call++;
+}
+
+void map_update(ls_engine& e, Meta meta, int n) {
+  klaunch(e, map_update_kernel, dim3(n), dim3(128), 0, meta, n, e.map, e.max_ctx, e.rows, e.err_dev);
+}
+
+void attention(ls_engine& e, Meta meta, int n, const bf16* kp, const bf16* vp) {
+  AttnArgs a{meta, e.NH, e.NKV, e.q, e.map, e.max_ctx, e.rows, kp, vp, e.n_slots,
+             e.max_chunks, e.o_part, e.ml_part, 1.0f / std::sqrt((float)e.HD), e.err_dev};
+  const dim3 grid(n, e.NKV, e.max_chunks), blk(kAttnThreads);
+  const int G = e.NH / e.NKV;
+  if (e.HD == 128 && G == 1) klaunch(e, attn_kernel<128, 1>, grid, blk, 0, a);
+  else if (e.HD == 128 && G == 2) klaunch(e, attn_kernel<128, 2>, grid, blk, 0, a);
+  else if (e.HD == 64 && G == 1) klaunch(e, attn_kernel<64, 1>, grid, blk, 0, a);
+  else if (e.HD == 64 && G == 2) klaunch(e, attn_kernel<64, 2>, grid, blk, 0, a);
+  else klaunch(e, attn_kernel<64, 4>, grid, blk, 0, a);
+  klaunch(e, attn_combine_kernel, dim3(n, e.NH), dim3(e.HD), 0, meta, e.NH, e.HD, e.max_chunks,
+          (const float*)e.o_part, (const float*)e.ml_part, e.x_attn.ptr);
+}
+
+ResidArgs resid_base(ls_engine& e, Meta meta, const Gemm& g) {
+  ResidArgs a{};
+  a.meta = meta;
+  a.H = e.H;
+  a.part = e.part;
+  a.splits = g.splits;
+  a.split_stride = (long)e.cap * g.Mw;
+  a.bank_rows = e.bank_rows;
+  a.eps = e.mc.rms_eps;
+  a.err = e.err_dev;
+  return a;
+}
+
+void resid(ls_engine& e, const ResidArgs& a, int n) {
+  klaunch(e, resid_epi_kernel, dim3(n), dim3(256), (size_t)e.H * sizeof(float), a);
+}
+
+// Norm applied to the input of a layer's first GEMM (none for OLMo2 post-norm).
+const bf16* input_norm(const ls_engine& e, const LayerW& w) {
+  return e.mc.layout == LS_LAYOUT_OLMO_POST ? nullptr : w.n_in;
+}
+
+// One stack of decoder layers over n lanes. Input: h (fp32) and x_h = bf16 of
+// the first layer's normalised input. Layer formulas:
+//   ouro      r = h + rms(attn(rms(h)*n_in))*n_pa ; h = r + rms(mlp(rms(r)*n_pf))*n_pff
+//   raven_pre r = h + attn(rms(h)*n_in)           ; h = r + mlp(rms(r)*n_pa)
+//   olmo_post r = h + rms(attn(h))*n_pa           ; h = r + rms(mlp(r))*n_pff
+// (ouro.py:37-82 over SGLang Gemma2DecoderLayer; raven.py:258-265 / Llama;
+//  Olmo2DecoderLayer, contracts.py:191-196.)
+void run_stack(ls_engine& e, Stack& st, int n, Meta meta, const StackEnd& end) {
+  const int L = e.mc.layout;
+  const int nl = (int)st.layers.size();
+  for (int l = 0; l < nl; ++l) {
+    LayerW& w = st.layers[l];
+    const long kvoff = (long)(st.kv_base + l) * e.n_slots * e.KVD;
+    bf16* kp = e.kpool + kvoff;
+    bf16* vp = e.vpool + kvoff;
+
+    gemm(e, w.g_qkv, e.x_h, e.part, n);
+    QkvArgs qa{meta, e.NH, e.NKV, e.HD, e.part, w.g_qkv.splits, (long)e.cap * w.g_qkv.Mw,
+               w.qn, w.kn, e.inv_freq, e.mc.rms_eps, e.q, kp, vp, e.n_slots, e.err_dev};
+    klaunch(e, qkv_epi_kernel, dim3(n), dim3(256), (size_t)(e.QD + 2 * e.KVD) * sizeof(float), qa);
+    attention(e, meta, n, kp, vp);
+    gemm(e, w.g_o, e.x_attn, e.part, n);
+
+    ResidArgs ra = resid_base(e, meta, w.g_o);
+    ra.resid = e.h;
+    ra.out_h = e.r;
+    ra.x = e.x_h.ptr;
+    if (L == LS_LAYOUT_OURO) {
+      ra.a_norm_w = w.n_pa;
+      ra.x_norm_w = w.n_pf;
+    } else if (L == LS_LAYOUT_RAVEN_PRE) {
+      ra.x_norm_w = w.n_pa;
+    } else {
+      ra.a_norm_w = w.n_pa;
+    }
+    resid(e, ra, n);
+
+    gemm(e, w.g_gu, e.x_h, e.part, n);
+    klaunch(e, act_epi_kernel, dim3(cdiv(e.I, 256), n), dim3(256), 0, (const float*)e.part,
+            w.g_gu.splits, (long)e.cap * w.g_gu.Mw, e.I, e.x_act.ptr);
+    gemm(e, w.g_down, e.x_act, e.part, n);
+
+    ResidArgs rb = resid_base(e, meta, w.g_down);
+    rb.resid = e.r;
+    rb.out_h = e.h;
+    if (L != LS_LAYOUT_RAVEN_PRE) rb.a_norm_w = w.n_pff;
+    const bool last = l + 1 == nl;
+    if (!last) {
+      rb.x = e.x_h.ptr;
+      rb.x_norm_w = input_norm(e, st.layers[l + 1]);
+    } else {
+      rb.final_norm_w = end.final_norm;
+      rb.bank = end.bank;
+      if (end.want_x) {
+        rb.x = e.x_h.ptr;
+        rb.x_norm_w = end.x_norm;
+      }
+    }
+    resid(e, rb, n);
+  }
+}
+
+struct PostOpts {
+  bool layers = true;     // run coda layers (post timelines)
+  bool head = true;       // run lm_head + argmax
+  int head_lane0 = 0;     // first lane of the head
+  int head_lanes = -1;    // number of lanes through the head (-1: all)
+};
+
+void prep(ls_engine& e, Meta meta, int n, bool embed_mode, float* bank_out, bool want_x,
+          const bf16* x_norm) {
+  PrepArgs pa{};
+  pa.meta = meta;
+  pa.B = n;
+  pa.H = e.H;
+  pa.embed = embed_mode ? e.embed : nullptr;
+  pa.embed_scale = e.mc.embed_scale;
+  pa.bank_in = e.bank_h;
+  pa.bank_rows = e.bank_rows;
+  pa.h = e.h;
+  pa.bank_out = bank_out;
+  pa.x = want_x ? e.x_h.ptr : nullptr;
+  pa.x_norm_w = x_norm;
+  pa.eps = e.mc.rms_eps;
+  pa.vocab = e.V;
+  pa.err = e.err_dev;
+  klaunch(e, prep_kernel, dim3(n), dim3(256), (size_t)e.H * sizeof(float), pa);
+}
+
+// The kernel chain of one role call over n lanes whose metadata is in the
+// role's device metadata buffer.
+void enqueue_role(ls_engine& e, int role, int n, const PostOpts& po = PostOpts()) {
+  Meta meta = meta_of(e, role);
+  e.kernels_in_call = 0;
+  const bool ouro = e.mc.family == LS_FAMILY_OURO;
+  if (role == kPre) {
+    if (ouro) {
+      // Ouro pre = embedding only (ouro.py:101-136); write it to the bank.
+      prep(e, meta, n, true, e.bank_h, false, nullptr);
+    } else {
+      // Raven pre: embed*scale, prelude, then the position-keyed hidden init
+      // with the prelude output kept as the injection (components.py:117-149).
+      if (!e.pre.layers.empty()) map_update(e, meta, n);
+      prep(e, meta, n, true, nullptr, !e.pre.layers.empty(),
+           e.pre.layers.empty() ? nullptr : input_norm(e, e.pre.layers[0]));
+      if (!e.pre.layers.empty()) run_stack(e, e.pre, n, meta, StackEnd());
+      klaunch(e, raven_init_kernel, dim3(n), dim3(256), 0, meta, e.H, (const float*)e.h, e.bank_h,
+              e.bank_inj, e.bank_rows, (unsigned long long)e.mc.init_seed, e.mc.init_std,
+              e.mc.embed_scale, e.err_dev);
+    }
+  } else if (role == kCore) {
+    map_update(e, meta, n);
+    StackEnd end;
+    end.bank = e.bank_h;
+    if (ouro) {
+      // one core iteration = all layers then step_norm (ouro.py:93-98)
+      prep(e, meta, n, false, nullptr, true, input_norm(e, e.core.layers[0]));
+      end.final_norm = e.step_norm;
+    } else {
+      // adapter(cat(hidden, injected)) then the core blocks (raven.py:271-281)
+      klaunch(e, cat_state_kernel, dim3(n), dim3(256), 0, meta, e.H, (const float*)e.bank_h,
+              (const float*)e.bank_inj, e.bank_rows, e.x_cat.ptr, e.err_dev);
+      gemm(e, e.g_adapter, e.x_cat, e.part, n);
+      ResidArgs ra = resid_base(e, meta, e.g_adapter);
+      ra.bias = e.adapter_b;
+      ra.out_h = e.h;
+      ra.x = e.x_h.ptr;
+      ra.x_norm_w = input_norm(e, e.core.layers[0]);
+      resid(e, ra, n);
+    }
+    run_stack(e, e.core, n, meta, end);
+  } else {
+    // post: coda layers (own timelines), final norm, lm_head (components.py:175-194)
+    const bool has_layers = !e.post.layers.empty();
+    if (has_layers && po.layers) {
+      map_update(e, meta, n);
+      prep(e, meta, n, false, nullptr, true, input_norm(e, e.post.layers[0]));
+      StackEnd end;
+      end.want_x = true;
+      end.x_norm = e.final_norm;
+      run_stack(e, e.post, n, meta, end);
+    } else if (!has_layers) {
+      prep(e, meta, n, false, nullptr, true, e.final_norm);
+    }
+    if (po.head) {
+      const int lanes = po.head_lanes < 0 ? n : po.head_lanes;
+      gemm(e, e.g_lm, e.x_h, e.logits, lanes, po.head_lane0);
+      klaunch(e, argmax_kernel, dim3(lanes), dim3(1024), 0, (const float*)e.logits, e.V, (long)e.V,
+              e.amax_dev);
+    }
+  }
+}
+
+int* stage_meta(ls_engine& e) {
+  if (e.staging_next >= ls_engine::kStaging) {
+    CK(cudaStreamSynchronize(e.stream));
+    e.staging_next = 0;
+  }
+  int* p = e.meta_host + (long)e.staging_next++ * kMetaFields * e.cap;
+  std::fill(p, p + kMetaFields * e.cap, -1);
+  return p;
+}
+
+void upload_meta(ls_engine& e, int role, const int* host) {
+  CK(cudaMemcpyAsync(e.meta_dev + (long)role * kMetaFields * e.cap, host,
+                     sizeof(int) * kMetaFields * e.cap, cudaMemcpyHostToDevice, e.stream));
+}
+
+void run_role(ls_engine& e, int role, int n, const int* host_meta, bool graphable,
+              const PostOpts& po = PostOpts()) {
+  REQUIRE(n >= 1 && n <= e.cap, LS_ECAPACITY, "role call wider than the lane capacity");
+  upload_meta(e, role, host_meta);
+  if (!(graphable && e.sc.use_graphs)) {
+    enqueue_role(e, role, n, po);
+    return;
+  }
+  const auto key = std::make_pair(role, n);
+  auto it = e.graphs.find(key);
+  if (it == e.graphs.end()) {
+    CK(cudaStreamBeginCapture(e.stream, cudaStreamCaptureModeThreadLocal));
+    try {
+      enqueue_role(e, role, n);
+    } catch (...) {
+      cudaGraph_t g = nullptr;
+      cudaStreamEndCapture(e.stream, &g);
+      if (g) cudaGraphDestroy(g);
+      throw;
+    }
+    cudaGraph_t g = nullptr;
+    CK(cudaStreamEndCapture(e.stream, &g));
+    cudaGraphExec_t ge = nullptr;
+    const cudaError_t ie = cudaGraphInstantiate(&ge, g, 0);
+    cudaGraphDestroy(g);
+    CK(ie);
+    it = e.graphs.emplace(key, ge).first;
+  }
+  CK(cudaGraphLaunch(it->second, e.stream));
+}
+
+void check_device(ls_engine& e) {
+  int err = 0;
+  CK(cudaMemcpy(&err, e.err_dev, sizeof(int), cudaMemcpyDeviceToHost));
+  if (err != kDevOk) {
+    CK(cudaMemset(e.err_dev, 0, sizeof(int)));
+    static const char* names[] = {"ok", "TMA stage wait timed out", "free-stage wait timed out",
+                                  "accumulator wait timed out", "metadata index out of range"};
+    throw EngineError(LS_EDEVICE, std::string("device reported: ") +
+                                      (err > 0 && err < 5 ? names[err] : "unknown error"));
+  }
+}
+
+}  // namespace
+
+// ============================================================ request execution
+namespace {
+
+void put(ls_engine& e, int* m, int field, int b, int v) { m[field * e.cap + b] = v; }
+
+// Fill one lane of a role call. With a cursor, allocate the KV slot that this
+// token's K/V gets on that timeline and describe a pending fork copy.
+// Returns the slot (or -1).
+int fill_lane(ls_engine& e, int* m, int b, int token, int pos, Cursor* c, int state_in,
+              int state_out) {
+  put(e, m, kMetaToken, b, token);
+  put(e, m, kMetaPos, b, pos);
+  put(e, m, kMetaStateIn, b, state_in);
+  put(e, m, kMetaStateOut, b, state_out);
+  if (!c) return -1;
+  REQUIRE(c->seq_len == pos, LS_EPIPELINE,
+          "timeline length " + std::to_string(c->seq_len) + " does not match position " +
+              std::to_string(pos));
+  REQUIRE(pos < e.max_ctx, LS_ECAPACITY, "context longer than max_context");
+  const int slot = e.tl.alloc_slot();
+  put(e, m, kMetaRow, b, c->row);
+  put(e, m, kMetaSlot, b, slot);
+  put(e, m, kMetaForkRow, b, c->pending_parent_row);
+  put(e, m, kMetaForkLen, b, c->pending_parent_row >= 0 ? c->seq_len : 0);
+  return slot;
+}
+
+// After submission: the cursor owns its new slot and its fork is done
+// (request.py:216-222).
+void advance(Cursor* c, int slot, bool owned) {
+  if (owned) c->owned.push_back(slot);
+  c->pending_parent_row = -1;
+  c->seq_len += 1;
+}
+
+long long prefill(ls_engine& e, const int64_t* prompt, int P, float* logits_out) {
+  REQUIRE(e.finalized, LS_EINVAL, "engine not finalized");
+  REQUIRE(P >= 1 && P <= e.sc.max_prompt, LS_EINVAL, "prompt length out of range");
+  for (int i = 0; i < P; ++i)
+    REQUIRE(prompt[i] >= 0 && prompt[i] < e.V, LS_EINVAL, "prompt token out of vocabulary");
+  CK(cudaSetDevice(e.device));
+  CK(cudaStreamSynchronize(e.stream));
+  e.tl.reset();
+  e.staging_next = 0;
+  e.prefill_len = P - 1;
+  CK(cudaMemsetAsync(e.err_dev, 0, sizeof(int), e.stream));
+  CK(cudaEventRecord(e.ev0, e.stream));
+
+  const bool pre_attn = e.mc.n_pre_layers > 0, post_attn = e.mc.n_post_layers > 0;
+  Cursor* pre_c = pre_attn ? e.tl.create_root_cursor(kPre, 0) : nullptr;
+  std::vector<Cursor*> core_c(e.S);
+  for (int s = 0; s < e.S; ++s) core_c[s] = e.tl.create_root_cursor(kCore, s);
+  std::map<int, Cursor*> post_c;
+  if (post_attn)
+    for (auto& ep : e.endpoint_kind) post_c[ep.first] = e.tl.create_root_cursor(kPost, ep.first);
+
+  const int chunk = e.prefill_chunk;
+  for (int c0 = 0; c0 < P; c0 += chunk) {
+    const int n = std::min(chunk, P - c0);
+    const bool last_chunk = c0 + n == P;
+    std::vector<int> slots(n);
+    int* m = stage_meta(e);
+    for (int j = 0; j < n; ++j)
+      slots[j] = fill_lane(e, m, j, (int)prompt[c0 + j], c0 + j, pre_c, -1, e.max_rows + j);
+    run_role(e, kPre, n, m, false);
+    if (pre_c)
+      for (int j = 0; j < n; ++j) advance(pre_c, slots[j], false);
+    for (int s = 0; s < e.S; ++s) {
+      m = stage_meta(e);
+      for (int j = 0; j < n; ++j)
+        slots[j] = fill_lane(e, m, j, (int)prompt[c0 + j], c0 + j, core_c[s], e.max_rows + j,
+                             e.max_rows + j);
+      run_role(e, kCore, n, m, false);
+      for (int j = 0; j < n; ++j) advance(core_c[s], slots[j], false);
+      if (post_attn && e.endpoint_kind.count(s)) {
+        m = stage_meta(e);
+        for (int j = 0; j < n; ++j)
+          slots[j] = fill_lane(e, m, j, 0, c0 + j, post_c[s], e.max_rows + j, -1);
+        PostOpts po;
+        po.head = last_chunk && s == e.S - 1;
+        po.head_lane0 = n - 1;
+        po.head_lanes = 1;
+        run_role(e, kPost, n, m, false, po);
+        for (int j = 0; j < n; ++j) advance(post_c[s], slots[j], false);
+      }
+    }
+    if (!post_attn && last_chunk) {
+      m = stage_meta(e);
+      fill_lane(e, m, 0, 0, P - 1, nullptr, e.max_rows + n - 1, -1);
+      run_role(e, kPost, 1, m, false);
+    }
+  }
+  CK(cudaEventRecord(e.ev1, e.stream));
+  CK(cudaMemcpyAsync(e.amax_host, e.amax_dev, sizeof(long long), cudaMemcpyDeviceToHost, e.stream));
+  if (logits_out)
+    CK(cudaMemcpyAsync(e.logits_host, e.logits, sizeof(float) * e.V, cudaMemcpyDeviceToHost, e.stream));
+  CK(cudaStreamSynchronize(e.stream));
+  e.staging_next = 0;
+  check_device(e);
+  if (logits_out) std::memcpy(logits_out, e.logits_host, sizeof(float) * e.V);
+  return e.amax_host[0];
+}
+
+struct CycleLane {
+  int stage, index, token, branch, parent, state;
+  int origin = -1;   // scheduler bookkeeping only (trace output)
+};
+
+// One pipeline cycle (executor.py:293-367 without the decision policy):
+// pre for stage-0 lanes, K core iterations for all lanes, post + argmax for
+// readout lanes. dec[i] = argmax token for readout lanes, -1 otherwise.
+void cycle(ls_engine& e, const std::vector<CycleLane>& lanes, std::vector<long long>& dec,
+           float* logits_out) {
+  REQUIRE(e.prefill_len >= 0, LS_EINVAL, "no prefilled request");
+  const int B = (int)lanes.size();
+  REQUIRE(B >= 1 && B <= e.max_rows, LS_ECAPACITY, "speculative tree exceeded branch row limit");
+  const bool pre_attn = e.mc.n_pre_layers > 0, post_attn = e.mc.n_post_layers > 0;
+  std::vector<int> pos(B), pre_rows, ends(B), ep_rows;
+  for (int i = 0; i < B; ++i) {
+    const CycleLane& l = lanes[i];
+    REQUIRE(l.state >= 0 && l.state < e.max_rows, LS_EINVAL, "state slot out of range");
+    REQUIRE(l.stage >= 0 && l.stage + e.K <= e.S && l.stage % e.K == 0, LS_EINVAL, "bad lane stage");
+    REQUIRE(l.index >= 1, LS_EINVAL, "bad lane index");
+    REQUIRE(l.token >= 0 && l.token < e.V, LS_EINVAL, "lane token out of vocabulary");
+    pos[i] = e.prefill_len + l.index;
+    ends[i] = l.stage + e.K - 1;
+    if (l.stage == 0) pre_rows.push_back(i);
+    if (e.endpoint_kind.count(ends[i])) ep_rows.push_back(i);
+  }
+  std::vector<int> slots(B);
+  if (!pre_rows.empty()) {
+    int* m = stage_meta(e);
+    std::vector<Cursor*> cs(pre_rows.size(), nullptr);
+    for (size_t j = 0; j < pre_rows.size(); ++j) {
+      const CycleLane& l = lanes[pre_rows[j]];
+      if (pre_attn) cs[j] = e.tl.get_or_create_cursor(kPre, 0, l.branch, l.parent);
+      slots[j] = fill_lane(e, m, (int)j, l.token, pos[pre_rows[j]], cs[j], -1, l.state);
+    }
+    run_role(e, kPre, (int)pre_rows.size(), m, true);
+    for (size_t j = 0; j < pre_rows.size(); ++j)
+      if (cs[j]) advance(cs[j], slots[j], true);
+  }
+  for (int off = 0; off < e.K; ++off) {
+    int* m = stage_meta(e);
+    std::vector<Cursor*> cs(B);
+    for (int i = 0; i < B; ++i) {
+      const CycleLane& l = lanes[i];
+      cs[i] = e.tl.get_or_create_cursor(kCore, l.stage + off, l.branch, l.parent);
+      slots[i] = fill_lane(e, m, i, l.token, pos[i], cs[i], l.state, l.state);
+    }
+    run_role(e, kCore, B, m, true);
+    for (int i = 0; i < B; ++i) advance(cs[i], slots[i], true);
+  }
+  dec.assign(B, -1);
+  if (ep_rows.empty()) return;
+  const int M = (int)ep_rows.size();
+  int* m = stage_meta(e);
+  std::vector<Cursor*> cs(M, nullptr);
+  for (int j = 0; j < M; ++j) {
+    const CycleLane& l = lanes[ep_rows[j]];
+    if (post_attn) cs[j] = e.tl.get_or_create_cursor(kPost, ends[ep_rows[j]], l.branch, l.parent);
+    slots[j] = fill_lane(e, m, j, l.token, pos[ep_rows[j]], cs[j], l.state, -1);
+  }
+  run_role(e, kPost, M, m, true);
+  for (int j = 0; j < M; ++j)
+    if (cs[j]) advance(cs[j], slots[j], true);
+  CK(cudaMemcpyAsync(e.amax_host, e.amax_dev, sizeof(long long) * M, cudaMemcpyDeviceToHost, e.stream));
+  if (logits_out) {
+    for (int j = 0; j < M; ++j)
+      CK(cudaMemcpyAsync(logits_out + (long)ep_rows[j] * e.V, e.logits + (long)j * e.V,
+                         sizeof(float) * e.V, cudaMemcpyDeviceToHost, e.stream));
+  }
+  CK(cudaStreamSynchronize(e.stream));
+  e.staging_next = 0;
+  check_device(e);
+  for (int j = 0; j < M; ++j) dec[ep_rows[j]] = e.amax_host[j];
+}
+
+// ----------------------------------------------------- native scheduler loop
+// Restates continue_pipelined (pipeline.py:254-423), the executor's slot pool
+// and metric counting (executor.py:76-107, 239-290) and greedy resolve
+// (decisions.py:136-184). -1 stands for Python's None.
+struct PLane {
+  int stage = 0, index = 0, token = 0, state = -1, branch = 0, parent = -1, origin = -1;
+  int first_token = -1, second_token = -1;
+};
+
+struct StatePool {
+  std::priority_queue<int, std::vector<int>, std::greater<int>> free_;
+  std::set<int> live_;
+  explicit StatePool(int n) {
+    for (int i = 0; i < n; ++i) free_.push(i);
+  }
+  int acquire() {
+    REQUIRE(!free_.empty(), LS_ECAPACITY, "pipeline requires more recurrent state slots than configured");
+    const int s = free_.top();
+    free_.pop();
+    live_.insert(s);
+    return s;
+  }
+  void retain(const std::vector<PLane>& lanes) {
+    std::set<int> keep;
+    for (auto& l : lanes)
+      if (l.state >= 0) keep.insert(l.state);
+    for (auto it = live_.begin(); it != live_.end();) {
+      if (!keep.count(*it)) {
+        free_.push(*it);
+        it = live_.erase(it);
+      } else {
+        ++it;
+      }
+    }
+  }
+};
+
+bool descends_from(int b, int anc, const std::map<int, int>& parents) {
+  while (b != -1 && b != anc) {
+    auto it = parents.find(b);
+    b = it == parents.end() ? -1 : it->second;
+  }
+  return b == anc;
+}
+
+std::map<int, int> prune_ancestry(const std::vector<PLane>& lanes, int root,
+                                  const std::map<int, int>& parents) {
+  std::set<int> live{root};
+  for (auto& l : lanes) {
+    int b = l.branch;
+    while (b != root) {
+      auto it = parents.find(b);
+      REQUIRE(b != -1 && it != parents.end(), LS_EPIPELINE, "pipeline branch escaped the selected ancestry");
+      live.insert(b);
+      b = it->second;
+    }
+  }
+  std::map<int, int> out;
+  for (int b : live) out[b] = b == root ? -1 : parents.at(b);
+  return out;
+}
+
+void retain_timelines(ls_engine& e, const std::vector<PLane>& lanes) {
+  std::vector<std::pair<int, int>> bp;
+  for (auto& l : lanes) bp.emplace_back(l.branch, l.parent);
+  e.tl.retain(bp);
+}
+
+// What the scheduler loop needs from an executor: the schedule, one cycle of
+// model execution (decisions per lane, -1 for non-readout lanes) and branch
+// retention. The engine binds these to the GPU; ls_pipeline_simulate binds
+// them to a host decision callback so the same loop is testable without a GPU.
+struct SchedHooks {
+  int S = 0, K = 1, X = 0, max_rows = 0;
+  std::map<int, int> endpoint_kind;
+  std::function<void(const std::vector<CycleLane>&, std::vector<long long>&)> forward;
+  std::function<void(const std::vector<PLane>&, int accepted_stage)> retain;
+  std::function<bool(const std::vector<long long>&)> should_stop;
+};
+
+std::vector<long long> run_loopspec(SchedHooks& e, long long first, int max_new, ls_stats& st,
+                                    double& decode_t0) {
+  std::vector<long long> committed{first};
+  auto should_stop = [&](void) {
+    if (decode_t0 < 0) decode_t0 = now_s();
+    return e.should_stop(committed);
+  };
+  if (should_stop()) {
+    e.retain({}, -1);
+    return committed;
+  }
+  if (max_new == 1) {
+    e.retain({}, -1);
+    return committed;
+  }
+  const int q1 = e.K - 1, q2 = e.X ? e.K * e.X - 1 : -1, final_stage = e.S - 1;
+  StatePool pool(e.max_rows);
+  int next_branch = 1;
+  std::map<int, int> parents{{0, -1}};
+  std::vector<PLane> lanes(1);
+  lanes[0].index = 1;
+  lanes[0].token = (int)first;
+  std::vector<CycleLane> cl;
+  std::vector<long long> dec;
+  while ((int)committed.size() < max_new) {
+    // executor.forward
+    cl.clear();
+    for (auto& l : lanes) {
+      if (l.state < 0) l.state = pool.acquire();  // written back as result.state
+      cl.push_back({l.stage, l.index, l.token, l.branch, l.parent, l.state, l.origin});
+    }
+    e.forward(cl, dec);
+    st.pipeline_cycles += 1;
+    st.recurrent_rows += (int64_t)lanes.size() * e.K;
+    for (auto& l : lanes) {
+      st.pre_rows += l.stage == 0;
+      st.post_rows += e.endpoint_kind.count(l.stage + e.K - 1);
+    }
+    // continue_pipelined body
+    std::vector<PLane> following, children;
+    int final_idx = -1;
+    long long final_pred = 0;
+    int accepted_stage = -1;
+    for (size_t i = 0; i < lanes.size(); ++i) {
+      PLane& l = lanes[i];
+      const int end_stage = l.stage + e.K - 1;
+      auto kit = e.endpoint_kind.find(end_stage);
+      const int kind = kit == e.endpoint_kind.end() ? -1 : kit->second;
+      const long long pred = dec[i];
+      if (end_stage == final_stage) {
+        REQUIRE(final_idx < 0, LS_EPIPELINE, "multiple branches reached the final stage");
+        final_idx = (int)i;
+        final_pred = pred;
+        // greedy final verification (decisions.py:163-170) and metrics
+        if (l.first_token >= 0) {
+          const bool fr = pred != l.first_token;
+          bool sr = false;
+          if (!fr) accepted_stage = q1;
+          else if (l.second_token >= 0) {
+            sr = pred != l.second_token;
+            if (!sr) accepted_stage = q2;
+          }
+          const bool sv = fr && l.second_token >= 0;
+          st.first_rejections += fr;
+          st.second_verifications += sv;
+          st.second_acceptances += sv && accepted_stage == q2;
+          st.second_rejections += sv && sr;
+        }
+        st.verified_proposals += 1;
+        continue;
+      }
+      l.stage = end_stage + 1;
+      const bool proposed = kind == 0 || (kind == 1 && (l.first_token < 0 || pred != l.first_token));
+      if ((end_stage == q1 || end_stage == q2) && kind >= 0 && proposed) {
+        if (end_stage == q1) l.first_token = (int)pred;
+        else l.second_token = (int)pred;
+        if (l.index + 1 < max_new) {
+          PLane c;
+          c.stage = 0;
+          c.index = l.index + 1;
+          c.token = (int)pred;
+          c.branch = next_branch;
+          c.parent = l.branch;
+          c.origin = end_stage;
+          children.push_back(c);
+          parents[next_branch] = l.branch;
+          next_branch++;
+        }
+      }
+      following.push_back(l);
+    }
+    following.insert(following.end(), children.begin(), children.end());
+    if (final_idx >= 0) {
+      const PLane fl = lanes[final_idx];
+      REQUIRE(fl.index == (int)committed.size(), LS_EPIPELINE, "pipeline attempted to commit out of order");
+      committed.push_back(final_pred);
+      if (should_stop()) {
+        lanes.clear();
+        pool.retain(lanes);
+        e.retain({}, -1);
+        return committed;
+      }
+      accepted_stage = fl.first_token >= 0 ? accepted_stage : -1;
+      if (fl.index + 1 < max_new) {
+        int sel = -1;
+        for (size_t j = 0; j < following.size(); ++j) {
+          const PLane& c = following[j];
+          if (c.parent == fl.branch && c.token == final_pred && c.origin == accepted_stage &&
+              accepted_stage >= 0) {
+            sel = (int)j;
+            break;
+          }
+        }
+        int keep;
+        if (sel < 0) {
+          PLane c;
+          c.stage = 0;
+          c.index = fl.index + 1;
+          c.token = (int)final_pred;
+          c.branch = next_branch;
+          c.parent = fl.branch;
+          c.origin = final_stage;
+          parents[next_branch] = fl.branch;
+          next_branch++;
+          following.push_back(c);
+          keep = c.branch;
+        } else {
+          keep = following[sel].branch;
+        }
+        std::vector<PLane> kept;
+        for (auto& c : following)
+          if (descends_from(c.branch, keep, parents)) kept.push_back(c);
+        following.swap(kept);
+        parents = prune_ancestry(following, keep, parents);
+      } else {
+        following.clear();
+        accepted_stage = -1;
+      }
+    }
+    REQUIRE((int)following.size() <= e.max_rows, LS_EPIPELINE, "speculative tree exceeded branch row limit");
+    lanes.swap(following);
+    pool.retain(lanes);
+    e.retain(lanes, accepted_stage);
+    REQUIRE(!lanes.empty() || (int)committed.size() >= max_new, LS_EPIPELINE,
+            "pipeline drained before generation completed");
+  }
+  return committed;
+}
+
+std::vector<long long> run_ar(ls_engine& e, long long first, int max_new, long long stop_token,
+                              double& decode_t0) {
+  std::vector<long long> committed{first};
+  decode_t0 = now_s();
+  if (stop_token >= 0 && first == stop_token) return committed;
+  const bool pre_attn = e.mc.n_pre_layers > 0, post_attn = e.mc.n_post_layers > 0;
+  int index = 1;
+  while ((int)committed.size() < max_new) {
+    const int tok = (int)committed.back();
+    const int pos = e.prefill_len + index;
+    int* m = stage_meta(e);
+    Cursor* c = pre_attn ? e.tl.get_or_create_cursor(kPre, 0, 0, -1) : nullptr;
+    int slot = fill_lane(e, m, 0, tok, pos, c, -1, 0);
+    run_role(e, kPre, 1, m, true);
+    if (c) advance(c, slot, true);
+    for (int s = 0; s < e.S; ++s) {
+      m = stage_meta(e);
+      c = e.tl.get_or_create_cursor(kCore, s, 0, -1);
+      slot = fill_lane(e, m, 0, tok, pos, c, 0, 0);
+      run_role(e, kCore, 1, m, true);
+      advance(c, slot, true);
+    }
+    m = stage_meta(e);
+    c = post_attn ? e.tl.get_or_create_cursor(kPost, e.S - 1, 0, -1) : nullptr;
+    slot = fill_lane(e, m, 0, tok, pos, c, 0, -1);
+    run_role(e, kPost, 1, m, true);
+    if (c) advance(c, slot, true);
+    CK(cudaMemcpyAsync(e.amax_host, e.amax_dev, sizeof(long long), cudaMemcpyDeviceToHost, e.stream));
+    CK(cudaStreamSynchronize(e.stream));
+    e.staging_next = 0;
+    check_device(e);
+    committed.push_back(e.amax_host[0]);
+    index++;
+    if (stop_token >= 0 && committed.back() == stop_token) break;
+  }
+  e.tl.retain({});
+  return committed;
+}
+
+SchedHooks engine_hooks(ls_engine& e, long long stop_token) {
+  SchedHooks hk;
+  hk.S = e.S;
+  hk.K = e.K;
+  hk.X = e.X;
+  hk.max_rows = e.max_rows;
+  hk.endpoint_kind = e.endpoint_kind;
+  hk.forward = [&e](const std::vector<CycleLane>& cl, std::vector<long long>& dec) {
+    cycle(e, cl, dec, nullptr);
+  };
+  hk.retain = [&e](const std::vector<PLane>& lanes, int) { retain_timelines(e, lanes); };
+  hk.should_stop = [stop_token](const std::vector<long long>& ids) {
+    return stop_token >= 0 && ids.back() == stop_token;
+  };
+  return hk;
+}
+
+int fail(ls_engine* e, const std::exception& ex) {
+  const EngineError* ee = dynamic_cast<const EngineError*>(&ex);
+  if (e) e->last_error = ex.what();
+  return ee ? ee->code : LS_EINVAL;
+}
+
+}  // namespace
+
+// ======================================================================== C ABI
+extern "C" {
+
+const char* ls_version(void) { return "loopspec-b200 0.1.0 (sm_100a)"; }
+
+const char* ls_last_error(ls_engine* e) { return e ? e->last_error.c_str() : "null engine"; }
+
+int ls_create(const ls_model_cfg* model, const ls_sched_cfg* sched, int device, ls_engine** out) {
+  if (!model || !sched || !out) return LS_EINVAL;
+  *out = nullptr;
+  std::unique_ptr<ls_engine> e(new ls_engine());
+  try {
+    e->mc = *model;
+    e->sc = *sched;
+    e->device = device;
+    REQUIRE(model->family == LS_FAMILY_OURO || model->family == LS_FAMILY_RAVEN, LS_EINVAL, "bad family");
+    REQUIRE(model->layout >= 0 && model->layout <= 2, LS_EINVAL, "bad layout");
+    REQUIRE((model->family == LS_FAMILY_OURO) == (model->layout == LS_LAYOUT_OURO), LS_EINVAL,
+            "Ouro uses the ouro layout; Raven uses raven_pre or olmo_post");
+    REQUIRE(model->stages > 0, LS_EINVAL, "stages S must be a positive integer");
+    // PipelineSchedule.__post_init__ (pipeline.py:132-139)
+    const int S = model->stages, K = sched->step_size, X = sched->second_step;
+    REQUIRE(K >= 1 && K < S && S % K == 0, LS_EINVAL,
+            "step_size K must be a positive divisor of S with K < S");
+    REQUIRE(X == 0 || (X > 1 && X < S / K), LS_EINVAL, "second_step X must satisfy 1 < X < S/K");
+    e->S = S;
+    e->K = K;
+    e->X = X;
+    e->depth = S / K;
+    e->endpoint_kind[K - 1] = 0;
+    if (X) e->endpoint_kind[K * X - 1] = 1;
+    e->endpoint_kind[S - 1] = 2;
+    long rows = 0;
+    for (long b : e->birth_sizes()) rows += b;
+    e->max_rows = (int)rows;
+    CK(cudaSetDevice(device));
+  } catch (const std::exception& ex) {
+    return fail(nullptr, ex);
+  }
+  *out = e.release();
+  return LS_OK;
+}
+
+int ls_load_weight(ls_engine* e, const char* name, const void* dptr, int dtype, const int64_t* shape,
+                   int ndim) {
+  if (!e || !name || !dptr || !shape || ndim < 1 || ndim > 4) return LS_EINVAL;
+  try {
+    REQUIRE(!e->finalized, LS_EINVAL, "weights must be loaded before ls_finalize");
+    REQUIRE(dtype == 0, LS_EINVAL, "only bf16 weights are accepted");
+    REQUIRE((reinterpret_cast<uintptr_t>(dptr) & 15) == 0, LS_EINVAL, "weight pointer must be 16-byte aligned");
+    e->weights[name] = {static_cast<const bf16*>(dptr), std::vector<int64_t>(shape, shape + ndim)};
+  } catch (const std::exception& ex) {
+    return fail(e, ex);
+  }
+  return LS_OK;
+}
+
+int ls_finalize(ls_engine* e) {
+  if (!e) return LS_EINVAL;
+  try {
+    e->finalize();
+  } catch (const std::exception& ex) {
+    return fail(e, ex);
+  }
+  return LS_OK;
+}
+
+int ls_prefill(ls_engine* e, const int64_t* prompt, int n, float* out_logits, int64_t* first) {
+  if (!e || !prompt || !first) return LS_EINVAL;
+  try {
+    *first = prefill(*e, prompt, n, out_logits);
+  } catch (const std::exception& ex) {
+    return fail(e, ex);
+  }
+  return LS_OK;
+}
+
+int ls_cycle(ls_engine* e, const int64_t* lanes, int n, int64_t* out_dec, float* out_logits) {
+  if (!e || !lanes || !out_dec || n < 1) return LS_EINVAL;
+  try {
+    CK(cudaSetDevice(e->device));
+    std::vector<CycleLane> cl(n);
+    for (int i = 0; i < n; ++i) {
+      const int64_t* l = lanes + 6 * i;
+      cl[i] = {(int)l[0], (int)l[1], (int)l[2], (int)l[3], (int)l[4], (int)l[5], -1};
+    }
+    std::vector<long long> dec;
+    cycle(*e, cl, dec, out_logits);
+    for (int i = 0; i < n; ++i) out_dec[i] = dec[i];
+  } catch (const std::exception& ex) {
+    return fail(e, ex);
+  }
+  return LS_OK;
+}
+
+int ls_retain(ls_engine* e, const int64_t* branch_ids, const int64_t* parent_ids, int n) {
+  if (!e || n < 0 || (n > 0 && (!branch_ids || !parent_ids))) return LS_EINVAL;
+  try {
+    std::vector<std::pair<int, int>> bp;
+    for (int i = 0; i < n; ++i) bp.emplace_back((int)branch_ids[i], (int)parent_ids[i]);
+    e->tl.retain(bp);
+  } catch (const std::exception& ex) {
+    return fail(e, ex);
+  }
+  return LS_OK;
+}
+
+int ls_generate(ls_engine* e, const int64_t* prompt, int n_prompt, int max_new, int mode,
+                int64_t stop_token, int64_t* out_ids, int* n_out, ls_stats* stats) {
+  if (!e || !prompt || !out_ids || !n_out || max_new < 1 || (mode != 0 && mode != 1)) return LS_EINVAL;
+  try {
+    ls_stats st{};
+    const long long first = prefill(*e, prompt, n_prompt, nullptr);
+    float pms = 0.f;
+    CK(cudaEventElapsedTime(&pms, e->ev0, e->ev1));
+    st.prefill_device_ms = pms;
+    REQUIRE(e->prefill_len + max_new < e->max_ctx, LS_ECAPACITY, "prompt + max_new_tokens exceeds max_context");
+    double t0 = -1.0;
+    CK(cudaEventRecord(e->ev0, e->stream));
+    std::vector<long long> ids;
+    if (mode == 0) {
+      SchedHooks hk = engine_hooks(*e, stop_token);
+      ids = run_loopspec(hk, first, max_new, st, t0);
+    } else {
+      ids = run_ar(*e, first, max_new, stop_token, t0);
+    }
+    CK(cudaEventRecord(e->ev1, e->stream));
+    CK(cudaEventSynchronize(e->ev1));
+    const double t1 = now_s();
+    float dms = 0.f;
+    CK(cudaEventElapsedTime(&dms, e->ev0, e->ev1));
+    st.decode_device_ms = dms;
+    st.decode_host_s = t0 >= 0 ? t1 - t0 : 0.0;
+    st.decode_tokens = std::max<int64_t>((int64_t)ids.size() - 1, 0);
+    for (size_t i = 0; i < ids.size(); ++i) out_ids[i] = ids[i];
+    *n_out = (int)ids.size();
+    if (stats) *stats = st;
+  } catch (const std::exception& ex) {
+    return fail(e, ex);
+  }
+  return LS_OK;
+}
+
+int ls_pipeline_simulate(int stages, int step_size, int second_step, int64_t first_token,
+                         int max_new_tokens, int64_t stop_token, ls_decide_fn decide,
+                         ls_cycle_fn on_cycle, ls_retain_fn on_retain, void* user,
+                         int64_t* out_ids, int* n_out, ls_stats* stats) {
+  if (!decide || !out_ids || !n_out || max_new_tokens < 1) return LS_EINVAL;
+  try {
+    const int S = stages, K = step_size, X = second_step;
+    REQUIRE(S > 0, LS_EINVAL, "stages S must be a positive integer");
+    REQUIRE(K >= 1 && K < S && S % K == 0, LS_EINVAL, "step_size K must be a positive divisor of S with K < S");
+    REQUIRE(X == 0 || (X > 1 && X < S / K), LS_EINVAL, "second_step X must satisfy 1 < X < S/K");
+    SchedHooks hk;
+    hk.S = S;
+    hk.K = K;
+    hk.X = X;
+    hk.endpoint_kind[K - 1] = 0;
+    if (X) hk.endpoint_kind[K * X - 1] = 1;
+    hk.endpoint_kind[S - 1] = 2;
+    const int depth = S / K;
+    std::vector<long> b;
+    if (X == 0) b.assign(depth, 1);
+    else {
+      b.assign(X, 1);
+      for (int t = X; t < depth; ++t) b.push_back(b[t - 1] + b[t - X]);
+    }
+    for (long v : b) hk.max_rows += (int)v;
+    hk.forward = [&](const std::vector<CycleLane>& cl, std::vector<long long>& dec) {
+      std::vector<int64_t> rows;
+      for (auto& l : cl) {
+        const int64_t r[7] = {l.stage, l.index, l.token, l.branch, l.parent, l.origin, l.state};
+        rows.insert(rows.end(), r, r + 7);
+      }
+      if (on_cycle) on_cycle(user, rows.data(), (int32_t)cl.size());
+      dec.assign(cl.size(), -1);
+      for (size_t i = 0; i < cl.size(); ++i) {
+        auto it = hk.endpoint_kind.find(cl[i].stage + K - 1);
+        if (it != hk.endpoint_kind.end()) dec[i] = decide(user, cl[i].index, cl[i].token, it->second);
+      }
+    };
+    hk.retain = [&](const std::vector<PLane>& lanes, int accepted) {
+      std::vector<int64_t> pairs;
+      for (auto& l : lanes) {
+        pairs.push_back(l.branch);
+        pairs.push_back(l.parent);
+      }
+      if (on_retain) on_retain(user, pairs.data(), (int32_t)lanes.size(), accepted);
+    };
+    hk.should_stop = [stop_token](const std::vector<long long>& ids) {
+      return stop_token >= 0 && ids.back() == stop_token;
+    };
+    ls_stats st{};
+    double t0 = -1.0;
+    std::vector<long long> ids = run_loopspec(hk, first_token, max_new_tokens, st, t0);
+    st.decode_tokens = std::max<int64_t>((int64_t)ids.size() - 1, 0);
+    for (size_t i = 0; i < ids.size(); ++i) out_ids[i] = ids[i];
+    *n_out = (int)ids.size();
+    if (stats) *stats = st;
+  } catch (const std::exception& ex) {
+    return fail(nullptr, ex);
+  }
+  return LS_OK;
+}
+
+int ls_role_kernel_count(ls_engine* e, int role, int n, int* count) {
+  if (!e || !count || role < 0 || role > 2 || n < 1) return LS_EINVAL;
+  try {
+    REQUIRE(e->finalized, LS_EINVAL, "engine not finalized");
+    // Count by capturing the chain into a throwaway graph.
+    CK(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
+    try {
+      enqueue_role(*e, role, n);
+    } catch (...) {
+      cudaGraph_t g = nullptr;
+      cudaStreamEndCapture(e->stream, &g);
+      if (g) cudaGraphDestroy(g);
+      throw;
+    }
+    cudaGraph_t g = nullptr;
+    CK(cudaStreamEndCapture(e->stream, &g));
+    size_t nodes = 0;
+    cudaGraphGetNodes(g, nullptr, &nodes);
+    cudaGraphDestroy(g);
+    *count = (int)nodes;
+  } catch (const std::exception& ex) {
+    return fail(e, ex);
+  }
+  return LS_OK;
+}
+
+int ls_time_role(ls_engine* e, int role, int n, int context_len, int iters, double* avg_ms) {
+  if (!e || !avg_ms || role < 0 || role > 2 || n < 1 || iters < 1) return LS_EINVAL;
+  try {
+    REQUIRE(e->prefill_len >= 0, LS_EINVAL, "ls_time_role needs a prefilled request");
+    REQUIRE(n <= e->max_rows, LS_ECAPACITY, "too many lanes");
+    const int P = e->prefill_len + 1;
+    REQUIRE(context_len >= 1 && context_len <= P, LS_EINVAL, "context_len must not exceed the prompt");
+    // Synthetic lanes: fresh rows forking the root's first timeline of the
+    // role at context_len - 1, each appending one token there. This overwrites
+    // nothing of the request's timelines but consumes rows/slots until the
+    // next ls_prefill, which resets the pools.
+    const bool attn = role == kCore || (role == kPre && e->mc.n_pre_layers) ||
+                      (role == kPost && e->mc.n_post_layers);
+    int* m = stage_meta(*e);
+    for (int b = 0; b < n; ++b) {
+      Cursor c;
+      if (attn) {
+        Cursor* root = e->tl.get_or_create_cursor(role, role == kPost ? e->S - 1 : 0, 0, -1);
+        c.row = e->tl.alloc_row();
+        c.seq_len = context_len - 1;
+        c.pending_parent_row = root->row;
+      }
+      fill_lane(*e, m, b, 1, context_len - 1, attn ? &c : nullptr, b, b);
+    }
+    run_role(*e, role, n, m, true);  // warm-up (captures the graph)
+    CK(cudaEventRecord(e->ev0, e->stream));
+    for (int i = 0; i < iters; ++i) run_role(*e, role, n, m, true);
+    CK(cudaEventRecord(e->ev1, e->stream));
+    CK(cudaEventSynchronize(e->ev1));
+    e->staging_next = 0;
+    check_device(*e);
+    float ms = 0.f;
+    CK(cudaEventElapsedTime(&ms, e->ev0, e->ev1));
+    *avg_ms = ms / iters;
+  } catch (const std::exception& ex) {
+    return fail(e, ex);
+  }
+  return LS_OK;
+}
+
+int ls_time_gemm(ls_engine* e, int which, int n, int iters, double* avg_ms) {
+  if (!e || !avg_ms || which < 0 || which > 4 || n < 1 || iters < 1) return LS_EINVAL;
+  try {
+    REQUIRE(e->finalized, LS_EINVAL, "engine not finalized");
+    REQUIRE(n <= e->cap, LS_ECAPACITY, "too many lanes");
+    LayerW& w = e->core.layers[0];
+    const Gemm* g[] = {&w.g_qkv, &w.g_o, &w.g_gu, &w.g_down, &e->g_lm};
+    XBuf* x[] = {&e->x_h, &e->x_attn, &e->x_h, &e->x_act, &e->x_h};
+    float* out = which == 4 ? e->logits : e->part;
+    gemm(*e, *g[which], *x[which], out, n);
+    CK(cudaEventRecord(e->ev0, e->stream));
+    for (int i = 0; i < iters; ++i) gemm(*e, *g[which], *x[which], out, n);
+    CK(cudaEventRecord(e->ev1, e->stream));
+    CK(cudaEventSynchronize(e->ev1));
+    check_device(*e);
+    float ms = 0.f;
+    CK(cudaEventElapsedTime(&ms, e->ev0, e->ev1));
+    *avg_ms = ms / iters;
+  } catch (const std::exception& ex) {
+    return fail(e, ex);
+  }
+  return LS_OK;
+}
+
+int ls_debug_gemm(ls_engine* e, int which, int n, const uint16_t* x_host, float* out_host) {
+  if (!e || !x_host || !out_host || which < 0 || which > 5 || n < 1) return LS_EINVAL;
+  try {
+    REQUIRE(e->finalized, LS_EINVAL, "engine not finalized");
+    REQUIRE(n <= e->cap, LS_ECAPACITY, "too many lanes");
+    REQUIRE(which != 5 || e->mc.family == LS_FAMILY_RAVEN, LS_EINVAL, "no adapter in this model");
+    LayerW& w = e->core.layers[0];
+    const Gemm* g[] = {&w.g_qkv, &w.g_o, &w.g_gu, &w.g_down, &e->g_lm, &e->g_adapter};
+    XBuf* x[] = {&e->x_h, &e->x_attn, &e->x_h, &e->x_act, &e->x_h, &e->x_cat};
+    const Gemm& gm = *g[which];
+    XBuf& xb = *x[which];
+    CK(cudaMemcpyAsync(xb.ptr, x_host, sizeof(uint16_t) * (size_t)n * gm.K, cudaMemcpyHostToDevice, e->stream));
+    float* out = which == 4 ? e->logits : e->part;
+    gemm(*e, gm, xb, out, n);
+    std::vector<float> part((size_t)gm.splits * e->cap * gm.Mw);
+    CK(cudaMemcpyAsync(part.data(), out, sizeof(float) * part.size(), cudaMemcpyDeviceToHost, e->stream));
+    CK(cudaStreamSynchronize(e->stream));
+    check_device(*e);
+    for (int b = 0; b < n; ++b)
+      for (int m = 0; m < gm.Mw; ++m) {
+        float v = 0.f;
+        for (int s = 0; s < gm.splits; ++s) v += part[((size_t)s * e->cap + b) * gm.Mw + m];
+        out_host[(size_t)b * gm.Mw + m] = v;
+      }
+  } catch (const std::exception& ex) {
+    return fail(e, ex);
+  }
+  return LS_OK;
+}
+
+int ls_gemm_splits(ls_engine* e, int which, int* splits, int* rows, int* k) {
+  if (!e || !e->finalized || which < 0 || which > 5) return LS_EINVAL;
+  LayerW& w = e->core.layers[0];
+  const Gemm* g[] = {&w.g_qkv, &w.g_o, &w.g_gu, &w.g_down, &e->g_lm, &e->g_adapter};
+  if (splits) *splits = g[which]->splits;
+  if (rows) *rows = g[which]->Mw;
+  if (k) *k = g[which]->K;
+  return LS_OK;
+}
+
+int ls_debug_kv(ls_engine* e, void** k, void** v, int* slots, int* layers) {
+  if (!e || !e->finalized) return LS_EINVAL;
+  if (k) *k = e->kpool;
+  if (v) *v = e->vpool;
+  if (slots) *slots = e->n_slots;
+  if (layers) *layers = e->n_attn_layers;
+  return LS_OK;
+}
+
+int ls_destroy(ls_engine* e) {
+  if (!e) return LS_EINVAL;
+  if (e->stream) cudaStreamSynchronize(e->stream);
+  delete e;
+  return LS_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,155 @@
+"""Python handle over the C-ABI engine (no torch types cross the boundary).
+
+`Engine` owns one libloopspec_engine.so handle, keeps the caller's weight
+tensors alive (the engine borrows their device pointers), and converts
+between Python lists / numpy arrays and the plain int64 / float buffers of
+include/loopspec_engine.h.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+
+from . import _lib
+from .config import ModelConfig
+from .schedule import PipelineSchedule
+
+
+def _i64p(a):
+    return a.ctypes.data_as(ctypes.POINTER(ctypes.c_int64))
+
+
+def _f32p(a):
+    return None if a is None else a.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+
+
+class Engine:
+    """One looped model on one GPU, one request at a time."""
+
+    def __init__(self, cfg: ModelConfig, schedule: PipelineSchedule, weights: dict, *,
+                 device: int = 0, max_context: int = 4096, max_prompt: int | None = None,
+                 kv_slots: int = 0, request_rows: int = 0, use_graphs: bool = True,
+                 use_pdl: bool = True):
+        if schedule.stages != cfg.stages:
+            raise ValueError("schedule stages must equal the model's recurrence count")
+        self.cfg = cfg
+        self.schedule = schedule
+        self.L = _lib.lib()
+        mc = _lib.ModelCfg(
+            family=_lib.FAMILY[cfg.family], layout=_lib.LAYOUT[cfg.layout],
+            hidden=cfg.hidden, n_heads=cfg.n_heads, n_kv_heads=cfg.n_kv_heads,
+            head_dim=cfg.head_dim, intermediate=cfg.intermediate, vocab=cfg.vocab,
+            n_pre_layers=cfg.n_pre_layers, n_core_layers=cfg.n_core_layers,
+            n_post_layers=cfg.n_post_layers, stages=cfg.stages, rope_theta=cfg.rope_theta,
+            rms_eps=cfg.rms_eps, embed_scale=cfg.embed_scale, init_std=cfg.init_std,
+            init_seed=cfg.init_seed, qk_norm=int(cfg.qk_norm),
+            adapter_bias=int(cfg.adapter_bias), tie_embeddings=int(cfg.tie_embeddings))
+        sc = _lib.SchedCfg(
+            step_size=schedule.step_size, second_step=schedule.second_step or 0,
+            max_context=max_context, max_prompt=max_prompt or max_context // 2,
+            kv_slots=kv_slots, request_rows=request_rows, use_graphs=int(use_graphs),
+            use_pdl=int(use_pdl))
+        handle = ctypes.c_void_p()
+        code = self.L.ls_create(ctypes.byref(mc), ctypes.byref(sc), device, ctypes.byref(handle))
+        if code != _lib.LS_OK:
+            raise _lib.EngineError(code, "ls_create rejected the configuration")
+        self.h = handle
+        self._weights = {}
+        try:
+            for name, t in weights.items():
+                self._load(name, t)
+            _lib.check(self.L.ls_finalize(self.h), self.h)
+        except Exception:
+            self.close()
+            raise
+        self.prefill_len = None
+
+    def _load(self, name, t):
+        import torch
+        if t.dtype != torch.bfloat16 or not t.is_cuda or not t.is_contiguous():
+            raise ValueError(f"{name}: weights must be contiguous bf16 CUDA tensors")
+        self._weights[name] = t
+        shape = np.asarray(t.shape, dtype=np.int64)
+        _lib.check(self.L.ls_load_weight(self.h, name.encode(), ctypes.c_void_p(t.data_ptr()), 0,
+                                         _i64p(shape), len(shape)), self.h)
+
+    # ----------------------------------------------------------------- calls
+    def prefill(self, prompt_ids, want_logits=False):
+        p = np.ascontiguousarray(prompt_ids, dtype=np.int64)
+        first = np.zeros(1, dtype=np.int64)
+        logits = np.zeros(self.cfg.vocab, dtype=np.float32) if want_logits else None
+        _lib.check(self.L.ls_prefill(self.h, _i64p(p), len(p), _f32p(logits), _i64p(first)), self.h)
+        self.prefill_len = len(p) - 1
+        return (int(first[0]), logits) if want_logits else int(first[0])
+
+    def cycle(self, lanes, want_logits=False):
+        """lanes: int array [n, 6] (stage, index, token, branch, parent|-1, state)."""
+        a = np.ascontiguousarray(lanes, dtype=np.int64).reshape(-1, 6)
+        dec = np.zeros(len(a), dtype=np.int64)
+        logits = np.zeros((len(a), self.cfg.vocab), dtype=np.float32) if want_logits else None
+        _lib.check(self.L.ls_cycle(self.h, _i64p(a), len(a), _i64p(dec), _f32p(logits)), self.h)
+        return (dec, logits) if want_logits else dec
+
+    def retain(self, pairs):
+        b = np.ascontiguousarray([p[0] for p in pairs], dtype=np.int64)
+        p = np.ascontiguousarray([-1 if p[1] is None else p[1] for p in pairs], dtype=np.int64)
+        _lib.check(self.L.ls_retain(self.h, _i64p(b), _i64p(p), len(b)), self.h)
+
+    def generate(self, prompt_ids, max_new_tokens, *, mode="loopspec", stop_token=None):
+        p = np.ascontiguousarray(prompt_ids, dtype=np.int64)
+        out = np.zeros(max_new_tokens, dtype=np.int64)
+        n = ctypes.c_int32()
+        st = _lib.Stats()
+        _lib.check(self.L.ls_generate(
+            self.h, _i64p(p), len(p), max_new_tokens, 0 if mode == "loopspec" else 1,
+            -1 if stop_token is None else int(stop_token), _i64p(out), ctypes.byref(n),
+            ctypes.byref(st)), self.h)
+        self.prefill_len = None
+        return out[: n.value].tolist(), st.as_dict()
+
+    def time_role(self, role, n_lanes, context_len, iters=20):
+        ms = ctypes.c_double()
+        r = {"pre": 0, "core": 1, "post": 2}[role]
+        _lib.check(self.L.ls_time_role(self.h, r, n_lanes, context_len, iters, ctypes.byref(ms)), self.h)
+        return ms.value
+
+    def time_gemm(self, which, n_lanes, iters=50):
+        ms = ctypes.c_double()
+        w = {"qkv": 0, "o": 1, "gate_up": 2, "down": 3, "lm_head": 4}[which]
+        _lib.check(self.L.ls_time_gemm(self.h, w, n_lanes, iters, ctypes.byref(ms)), self.h)
+        return ms.value
+
+    def kernel_count(self, role, n_lanes):
+        c = ctypes.c_int32()
+        r = {"pre": 0, "core": 1, "post": 2}[role]
+        _lib.check(self.L.ls_role_kernel_count(self.h, r, n_lanes, ctypes.byref(c)), self.h)
+        return c.value
+
+    GEMMS = {"qkv": 0, "o": 1, "gate_up": 2, "down": 3, "lm_head": 4, "adapter": 5}
+
+    def debug_gemm(self, which, x_bf16_bits):
+        """x: uint16 numpy [n, K] (bf16 bits) -> float32 [n, rows] (core layer 0 weights)."""
+        w = self.GEMMS[which]
+        splits, rows, k = ctypes.c_int32(), ctypes.c_int32(), ctypes.c_int32()
+        _lib.check(self.L.ls_gemm_splits(self.h, w, ctypes.byref(splits), ctypes.byref(rows),
+                                         ctypes.byref(k)), self.h)
+        x = np.ascontiguousarray(x_bf16_bits, dtype=np.uint16)
+        assert x.shape[1] == k.value
+        out = np.zeros((x.shape[0], rows.value), dtype=np.float32)
+        _lib.check(self.L.ls_debug_gemm(self.h, w, x.shape[0],
+                                        x.ctypes.data_as(ctypes.POINTER(ctypes.c_uint16)),
+                                        _f32p(out)), self.h)
+        return out, splits.value
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.L.ls_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

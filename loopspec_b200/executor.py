@@ -1,0 +1,150 @@
+"""Request-level entry points over the engine, mirroring the reference API.
+
+* `B200Executor` implements the reference's PipelineExecutor protocol
+  (sglang_recurrent/loopspec/pipeline.py:59-82) the way
+  LosslessLoopSpecExecutor does (loopspec/executor.py:110-397): it prefills
+  in its constructor, keeps the state-slot pool and the counters on the host,
+  and runs each cycle (pre / K core / post + argmax) as one `ls_cycle` call on
+  the GPU. Any `continue_pipelined` -- the reference's own included -- can
+  drive it; this is the engine's parity mode.
+* `generate_loopspec` has the reference signature (executor.py:400-423) and
+  runs the whole request inside the engine (`ls_generate`): prefill, first
+  token and the native scheduler loop, with no Python per cycle.
+* `generate_autoregressive` is the unrolled baseline (serving.py:216-239).
+"""
+
+from __future__ import annotations
+
+import heapq
+from typing import Callable, Sequence
+
+from .decisions import GreedyDecisionPolicy
+from .engine import Engine
+from .schedule import LOOPSPEC_METRICS, PipelineLane, PipelineResult
+
+
+class _StateSlotPool:
+    """Lowest free bank row first (executor.py:76-107)."""
+
+    def __init__(self, capacity):
+        self.capacity = capacity
+        self._free = list(range(capacity))
+        self._live = set()
+
+    def acquire(self):
+        if not self._free:
+            raise RuntimeError("pipeline requires more recurrent state slots than "
+                               f"configured (max_rows={self.capacity})")
+        s = heapq.heappop(self._free)
+        self._live.add(s)
+        return s
+
+    def retain(self, slots):
+        keep = set(slots)
+        released = self._live - keep
+        self._live &= keep
+        for s in released:
+            heapq.heappush(self._free, s)
+
+
+class B200Executor:
+    """PipelineExecutor for one request on a B200 engine (greedy decisions)."""
+
+    def __init__(self, engine: Engine, prompt_ids: Sequence[int], max_new_tokens: int, *,
+                 sampling=None, generator=None,
+                 should_stop: Callable[[Sequence[int]], bool] | None = None,
+                 record_logits: bool = False):
+        if sampling is not None:
+            raise NotImplementedError("the parity executor runs greedy decisions only")
+        if not prompt_ids:
+            raise ValueError("the prompt must contain at least one token")
+        self.engine = engine
+        self.schedule = engine.schedule
+        self.endpoint_kind = self.schedule.endpoint_kinds
+        self.decisions = GreedyDecisionPolicy()
+        self._slots = _StateSlotPool(self.schedule.max_rows)
+        self._should_stop = should_stop or (lambda ids: False)
+        self.metrics = dict.fromkeys(LOOPSPEC_METRICS, 0)
+        self.record_logits = record_logits
+        self.logits_log = []
+        self._first = engine.prefill(list(prompt_ids))
+
+    def first_token(self):
+        return self._first
+
+    def should_stop(self, ids):
+        return self._should_stop(ids)
+
+    def finish_without_pipeline(self):
+        self.engine.retain([])
+
+    def forward(self, lanes: Sequence[PipelineLane]) -> list[PipelineResult]:
+        sch = self.schedule
+        K = sch.step_size
+        slots = [l.state if l.state is not None else self._slots.acquire() for l in lanes]
+        rows = [[l.stage, l.index, l.token, l.branch,
+                 -1 if l.parent_branch is None else l.parent_branch, slots[i]]
+                for i, l in enumerate(lanes)]
+        if self.record_logits:
+            dec, logits = self.engine.cycle(rows, want_logits=True)
+        else:
+            dec, logits = self.engine.cycle(rows), None
+        ends = [l.stage + K - 1 for l in lanes]
+        endpoints = {i: self.endpoint_kind[e] for i, e in enumerate(ends) if e in self.endpoint_kind}
+        m = self.metrics
+        m["pipeline_cycles"] += 1
+        m["pre_rows"] += sum(l.stage == 0 for l in lanes)
+        m["recurrent_rows"] += len(lanes) * K
+        m["post_rows"] += len(endpoints)
+        out = []
+        for i, l in enumerate(lanes):
+            kind = endpoints.get(i)
+            if kind is None:
+                out.append(PipelineResult(state=slots[i], prediction=0))
+                continue
+            if logits is not None:
+                self.logits_log.append((l.index, ends[i], logits[i].copy()))
+            o = self.decisions.resolve(l, kind, [int(dec[i])], None, sch)
+            if kind == "final":
+                m["verified_proposals"] += 1
+                sv = o.first_rejected and l.second_token is not None
+                m["first_rejections"] += o.first_rejected
+                m["second_verifications"] += sv
+                m["second_acceptances"] += sv and o.accepted_stage == sch.second_stage
+                m["second_rejections"] += sv and o.second_rejected
+            out.append(PipelineResult(state=slots[i], prediction=o.prediction, proposed=o.proposed,
+                                      proposal_state=None, accepted_stage=o.accepted_stage,
+                                      proposal_action=o.proposal_action))
+        return out
+
+    def retain_branches(self, lanes: Sequence[PipelineLane], accepted_stage=None) -> None:
+        self._slots.retain(l.state for l in lanes if l.state is not None)
+        self.engine.retain([(l.branch, l.parent_branch) for l in lanes])
+
+    def stats(self):
+        return dict(self.metrics)
+
+
+def generate_loopspec(runner: Engine, prompt_ids: Sequence[int], max_new_tokens: int, *,
+                      sampling=None, generator=None, should_stop=None, stop_token=None):
+    """Generate completion ids for one prompt; returns (ids, stats).
+
+    Same meaning as the reference's generate_loopspec: ids exclude the prompt
+    and uncommitted drafts; stats hold the executor counters and
+    decode_tokens (excluding the first token), plus decode timing.
+    `stop_token` ends generation when committed (EOS); a `should_stop`
+    callback is not supported on this fast path.
+    """
+    if sampling is not None:
+        raise NotImplementedError("sampling runs through the sampling engine path")
+    if should_stop is not None:
+        raise NotImplementedError("use stop_token, or drive B200Executor for callbacks")
+    if max_new_tokens <= 0:
+        raise ValueError("a committed first token requires a positive budget")
+    return runner.generate(list(prompt_ids), max_new_tokens, mode="loopspec", stop_token=stop_token)
+
+
+def generate_autoregressive(runner: Engine, prompt_ids: Sequence[int], max_new_tokens: int, *,
+                            stop_token=None):
+    """Plain decoding: every token runs pre, all S core iterations, post."""
+    return runner.generate(list(prompt_ids), max_new_tokens, mode="ar", stop_token=stop_token)

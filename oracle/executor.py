@@ -244,6 +244,31 @@ def generate_ar_oracle(model, stages, prompt_ids, max_new_tokens, *,
             return out
 
 
+def teacher_forced_logits(model, schedule, tokens, start):
+    """Logits of every readout depth at positions >= start for a fixed token path.
+
+    tokens = prompt + committed completion; position p feeds tokens[p]. For
+    post roles with attention each endpoint depth has its own timeline, as in
+    LoopSpec (request.py:157-176). Returns {(position, end_stage): logits}.
+    """
+    cfg = model.cfg
+    S = schedule.stages
+    ends = schedule.endpoint_stages
+    tl_pre = Timeline(cfg["n_pre_layers"]) if cfg["n_pre_layers"] else None
+    tl_core = [Timeline(cfg["n_core_layers"]) for _ in range(S)]
+    tl_post = {e: Timeline(cfg["n_post_layers"]) for e in ends} if cfg["n_post_layers"] else None
+    out = {}
+    for pos, tok in enumerate(tokens):
+        h, inj = model.pre(tok, pos, tl_pre)
+        for s in range(S):
+            h = model.core(h, inj, pos, tl_core[s])
+            if s in ends and (tl_post is not None or pos >= start):
+                lg = model.post(h, pos, tl_post[s] if tl_post is not None else None)
+                if pos >= start:
+                    out[(pos, s)] = lg
+    return out
+
+
 __all__ = [
     "OracleLoopSpecExecutor", "StateSlotPool", "PipelineSchedule", "PipelineLane",
     "generate_loopspec_oracle", "generate_ar_oracle", "argmax_first",

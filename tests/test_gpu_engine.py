@@ -1,0 +1,155 @@
+"""GPU parity tests of the CUDA engine (through the C ABI) against the CPU oracle.
+
+Tolerances: GEMMs vs a torch fp32 matmul of the same bf16 operands 2e-3
+relative to the output scale; per-token logits vs the fp32 oracle (run on the
+bf16-rounded weights) 2e-2 max-abs; integer work
+(committed tokens, counters, greedy argmax) exact.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from loopspec_b200.config import get_config
+from loopspec_b200.engine import Engine
+from loopspec_b200.executor import B200Executor
+from loopspec_b200.schedule import PipelineSchedule
+from loopspec_b200.weights import init_random_weights
+from oracle.executor import generate_ar_oracle, teacher_forced_logits
+from oracle.model import OracleModel
+from oracle.pipeline import continue_pipelined
+
+pytestmark = pytest.mark.gpu
+
+LOGIT_TOL = 2e-2
+
+
+def _build():
+    from loopspec_b200.build import build
+    build()
+
+
+def make(name, K, X, seed=0, **kw):
+    _build()
+    cfg = get_config(name)
+    w32 = init_random_weights(cfg, seed, dtype=torch.float32)
+    wdev = {k: v.to("cuda:0", torch.bfloat16).contiguous() for k, v in w32.items()}
+    eng = Engine(cfg, PipelineSchedule(cfg.stages, K, X), wdev, device=0,
+                 max_context=kw.pop("max_context", 512), max_prompt=kw.pop("max_prompt", 256), **kw)
+    wq = {k: v.to(torch.bfloat16).to(torch.float32) for k, v in w32.items()}
+    return cfg, eng, OracleModel(cfg.as_dict(), wq)
+
+
+def prompt_for(cfg, n, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randint(0, cfg.vocab, (n,), generator=g).tolist()
+
+
+def bf16_bits(x):
+    return x.to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+
+
+@pytest.mark.parametrize("name,which", [
+    ("tiny", "qkv"), ("tiny", "o"), ("tiny", "gate_up"), ("tiny", "down"), ("tiny", "lm_head"),
+    ("tiny-raven-llama", "adapter"), ("tiny-raven-llama", "qkv"),
+])
+@pytest.mark.parametrize("n", [1, 3, 16, 17, 40, 128])
+def test_gemm_matches_torch(name, which, n):
+    cfg, eng, _ = make(name, 1, None if cfg_stages(name) <= 4 else 2)
+    g = torch.Generator().manual_seed(n)
+    wname = {
+        "qkv": "recurrent_executor.blocks.0.self_attn.qkv_proj.weight",
+        "o": "recurrent_executor.blocks.0.self_attn.o_proj.weight",
+        "gate_up": "recurrent_executor.blocks.0.mlp.gate_up_proj.weight",
+        "down": "recurrent_executor.blocks.0.mlp.down_proj.weight",
+        "lm_head": "post_executor.lm_head.weight",
+        "adapter": "recurrent_executor.adapter.weight",
+    }[which]
+    W = eng._weights[wname].float().cpu()
+    x = torch.randn(n, W.shape[1], generator=g)
+    xb = x.to(torch.bfloat16)
+    out, splits = eng.debug_gemm(which, bf16_bits(x))
+    ref = (xb.float() @ W.T).numpy()
+    scale = float(np.abs(ref).max())
+    assert np.abs(out - ref).max() <= 2e-3 * scale + 1e-5, (which, n, splits)
+    eng.close()
+
+
+def cfg_stages(name):
+    return get_config(name).stages
+
+
+@pytest.mark.parametrize("name,K,X", [("tiny", 1, 2), ("tiny-raven-llama", 2, 2), ("tiny-raven-olmo", 1, 4)])
+def test_prefill_logits_match_oracle(name, K, X):
+    cfg, eng, om = make(name, K, X)
+    prompt = prompt_for(cfg, 40)
+    first, logits = eng.prefill(prompt, want_logits=True)
+    rec = []
+    generate_ar_oracle(om, cfg.stages, prompt, 1, record=rec)
+    ref = rec[0][2].numpy()
+    assert np.abs(logits - ref).max() <= LOGIT_TOL
+    assert first == int(np.argmax(logits))
+    eng.close()
+
+
+@pytest.mark.parametrize("name,K,X,n_new", [
+    ("tiny", 1, 2, 48), ("tiny", 1, None, 32), ("tiny", 2, None, 24),
+    ("tiny-raven-llama", 2, 2, 24), ("tiny-raven-olmo", 1, 4, 24),
+])
+def test_loopspec_equals_ar_and_reference_scheduler(name, K, X, n_new):
+    cfg, eng, om = make(name, K, X)
+    sch = eng.schedule
+    prompt = prompt_for(cfg, 32, seed=1)
+    native, st = eng.generate(prompt, n_new, mode="loopspec")
+    ar, _ = eng.generate(prompt, n_new, mode="ar")
+    assert native == ar                                   # greedy LoopSpec == AR
+    ex = B200Executor(eng, prompt, n_new, record_logits=True)
+    driven = continue_pipelined(ex.first_token(), n_new, ex)   # restated reference scheduler
+    assert driven == native
+    for key, val in ex.metrics.items():
+        assert st[key] == val, key                        # integer work bit-exact
+    assert st["decode_tokens"] == len(native) - 1
+    # per-token logits (final depth, committed path) vs the fp32 oracle
+    P = len(prompt)
+    tf = teacher_forced_logits(om, sch, prompt + driven[:-1], P)
+    finals = [(i, lg) for (i, e, lg) in ex.logits_log if e == sch.stages - 1]
+    assert len(finals) == len(driven) - 1
+    worst = max(float(np.abs(lg - tf[(P - 1 + i, sch.stages - 1)].numpy()).max())
+                for i, lg in finals)
+    assert worst <= LOGIT_TOL, worst
+    eng.close()
+
+
+def test_lanes_above_sixteen_keep_batch_invariance():
+    # S=8, K=1, X=4 reaches 18 live lanes, so the N=32 tensor-core tile is used
+    cfg, eng, _ = make("tiny-raven-olmo", 1, 4)
+    assert eng.schedule.max_rows > 16
+    prompt = prompt_for(cfg, 24, seed=2)
+    native, st = eng.generate(prompt, 40, mode="loopspec")
+    ar, _ = eng.generate(prompt, 40, mode="ar")
+    assert native == ar
+    eng.close()
+
+
+def test_graphs_and_pdl_do_not_change_results():
+    cfg, eng, _ = make("tiny", 1, 2, use_graphs=False, use_pdl=False)
+    prompt = prompt_for(cfg, 20, seed=3)
+    base, st0 = eng.generate(prompt, 24)
+    eng.close()
+    _, eng2, _ = make("tiny", 1, 2, use_graphs=True, use_pdl=True)
+    fast, st1 = eng2.generate(prompt, 24)
+    assert base == fast
+    assert st0["pipeline_cycles"] == st1["pipeline_cycles"]
+    eng2.close()
+
+
+def test_capacity_errors_are_reported_not_faulted():
+    from loopspec_b200._lib import EngineError
+    cfg, eng, _ = make("tiny", 1, 2, max_context=64, max_prompt=32)
+    with pytest.raises(EngineError):
+        eng.generate(prompt_for(cfg, 40), 8)        # prompt longer than max_prompt
+    with pytest.raises(EngineError):
+        eng.generate(prompt_for(cfg, 30), 60)       # prompt + new > max_context
+    ids, _ = eng.generate(prompt_for(cfg, 8), 8)    # engine still usable
+    assert len(ids) == 8
+    eng.close()
