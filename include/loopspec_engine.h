@@ -151,9 +151,10 @@ int ls_time_gemm(ls_engine* eng, int which, int n_lanes, int iters, double* avg_
 int ls_role_kernel_count(ls_engine* eng, int role, int n_lanes, int* count);
 
 /* Run one GEMM of core layer 0 (which: 0 qkv, 1 o, 2 gate_up, 3 down,
- * 4 lm_head, 5 Raven adapter) on host activations x (bf16 bits [n][K]) and
- * return the split-summed fp32 result [n][rows], for kernel tests. */
-int ls_debug_gemm(ls_engine* eng, int which, int n_lanes, const uint16_t* x, float* out);
+ * 4 lm_head, 5 Raven adapter) on host activations x (fp32 [n][K], fed as a
+ * bf16 hi/lo pair per lane like every engine GEMM) and return the
+ * split-summed fp32 result [n][rows], for kernel tests. */
+int ls_debug_gemm(ls_engine* eng, int which, int n_lanes, const float* x, float* out);
 int ls_gemm_splits(ls_engine* eng, int which, int* splits, int* rows, int* k);
 
 /* Device pointer of the engine's KV pool (K then V, each

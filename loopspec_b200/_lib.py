@@ -82,7 +82,7 @@ SIGNATURES = [
     ("ls_time_role", _i32, [_P, _i32, _i32, _i32, _i32, ctypes.POINTER(_f64)]),
     ("ls_time_gemm", _i32, [_P, _i32, _i32, _i32, ctypes.POINTER(_f64)]),
     ("ls_role_kernel_count", _i32, [_P, _i32, _i32, ctypes.POINTER(_i32)]),
-    ("ls_debug_gemm", _i32, [_P, _i32, _i32, ctypes.POINTER(ctypes.c_uint16), _PF32]),
+    ("ls_debug_gemm", _i32, [_P, _i32, _i32, _PF32, _PF32]),
     ("ls_gemm_splits", _i32, [_P, _i32, ctypes.POINTER(_i32), ctypes.POINTER(_i32), ctypes.POINTER(_i32)]),
     ("ls_debug_kv", _i32, [_P, ctypes.POINTER(_P), ctypes.POINTER(_P), ctypes.POINTER(_i32),
                            ctypes.POINTER(_i32)]),

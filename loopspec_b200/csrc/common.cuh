@@ -27,6 +27,14 @@ constexpr uint32_t kWaitLimit = 1u << 24;
 __device__ __forceinline__ float bf2f(__nv_bfloat16 v) { return __bfloat162float(v); }
 __device__ __forceinline__ __nv_bfloat16 f2bf(float v) { return __float2bfloat16_rn(v); }
 
+// GEMM activations are stored as a bf16 (hi, lo) row pair per lane: row 2b
+// holds bf16(v), row 2b+1 holds bf16(v - bf16(v)); the GEMM sums both.
+__device__ __forceinline__ void store_pair(__nv_bfloat16* x, long K, int b, long i, float v) {
+  const __nv_bfloat16 hi = f2bf(v);
+  x[(2L * b) * K + i] = hi;
+  x[(2L * b + 1) * K + i] = f2bf(v - bf2f(hi));
+}
+
 __device__ __forceinline__ void unpack8(const uint4& u, float* f) {
   const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&u);
 #pragma unroll

@@ -572,7 +572,7 @@ struct ls_engine {
     o_part = dalloc<float>((long)cap * NH * max_chunks * HD);
     ml_part = dalloc<float>((long)cap * NH * max_chunks * 2);
     logits = dalloc<float>((long)cap * V);
-    const int xrows = round_up(cap, 256);
+    const int xrows = round_up(2 * cap, 256);  // (hi, lo) row pair per lane
     auto mkx = [&](XBuf& xb, int Kd) {
       xb.K = Kd;
       xb.rows = xrows;
@@ -639,11 +639,13 @@ int pick_bn(int n) {
   return 256;
 }
 
-void gemm(ls_engine& e, const Gemm& g, XBuf& x, float* out, int n, int x_row0 = 0) {
-  REQUIRE(n >= 1 && x_row0 + n <= x.rows, LS_EINVAL, "GEMM lane count out of range");
-  const int bn = pick_bn(n);
+// n lanes = 2n activation rows (hi/lo pairs) starting at lane `lane0`.
+void gemm(ls_engine& e, const Gemm& g, XBuf& x, float* out, int n, int lane0 = 0) {
+  REQUIRE(n >= 1 && 2 * (lane0 + n) <= x.rows, LS_EINVAL, "GEMM lane count out of range");
+  const int bn = pick_bn(2 * n);
   const CUtensorMap& xm = x.map(bn);
-  dim3 grid(cdiv(g.Mw, kGemmBM), g.splits, cdiv(n, bn));
+  const int x_row0 = 2 * lane0;
+  dim3 grid(cdiv(g.Mw, kGemmBM), g.splits, cdiv(2 * n, bn));
   const long ss = (long)e.cap * g.Mw;
   const bool pdl = e.sc.use_pdl != 0;
   const dim3 blk(kGemmThreads);
@@ -928,15 +930,17 @@ void put(ls_engine& e, int* m, int field, int b, int v) { m[field * e.cap + b] =
 
 // Fill one lane of a role call. With a cursor, allocate the KV slot that this
 // token's K/V gets on that timeline and describe a pending fork copy.
+// `ahead` counts lanes of the same timeline filled earlier in this call
+// (prefill feeds a whole prompt chunk of one timeline at once).
 // Returns the slot (or -1).
 int fill_lane(ls_engine& e, int* m, int b, int token, int pos, Cursor* c, int state_in,
-              int state_out) {
+              int state_out, int ahead = 0) {
   put(e, m, kMetaToken, b, token);
   put(e, m, kMetaPos, b, pos);
   put(e, m, kMetaStateIn, b, state_in);
   put(e, m, kMetaStateOut, b, state_out);
   if (!c) return -1;
-  REQUIRE(c->seq_len == pos, LS_EPIPELINE,
+  REQUIRE(c->seq_len + ahead == pos, LS_EPIPELINE,
           "timeline length " + std::to_string(c->seq_len) + " does not match position " +
               std::to_string(pos));
   REQUIRE(pos < e.max_ctx, LS_ECAPACITY, "context longer than max_context");
@@ -984,7 +988,7 @@ long long prefill(ls_engine& e, const int64_t* prompt, int P, float* logits_out)
     std::vector<int> slots(n);
     int* m = stage_meta(e);
     for (int j = 0; j < n; ++j)
-      slots[j] = fill_lane(e, m, j, (int)prompt[c0 + j], c0 + j, pre_c, -1, e.max_rows + j);
+      slots[j] = fill_lane(e, m, j, (int)prompt[c0 + j], c0 + j, pre_c, -1, e.max_rows + j, j);
     run_role(e, kPre, n, m, false);
     if (pre_c)
       for (int j = 0; j < n; ++j) advance(pre_c, slots[j], false);
@@ -992,13 +996,13 @@ long long prefill(ls_engine& e, const int64_t* prompt, int P, float* logits_out)
       m = stage_meta(e);
       for (int j = 0; j < n; ++j)
         slots[j] = fill_lane(e, m, j, (int)prompt[c0 + j], c0 + j, core_c[s], e.max_rows + j,
-                             e.max_rows + j);
+                             e.max_rows + j, j);
       run_role(e, kCore, n, m, false);
       for (int j = 0; j < n; ++j) advance(core_c[s], slots[j], false);
       if (post_attn && e.endpoint_kind.count(s)) {
         m = stage_meta(e);
         for (int j = 0; j < n; ++j)
-          slots[j] = fill_lane(e, m, j, 0, c0 + j, post_c[s], e.max_rows + j, -1);
+          slots[j] = fill_lane(e, m, j, 0, c0 + j, post_c[s], e.max_rows + j, -1, j);
         PostOpts po;
         po.head = last_chunk && s == e.S - 1;
         po.head_lane0 = n - 1;
@@ -1687,7 +1691,7 @@ int ls_time_gemm(ls_engine* e, int which, int n, int iters, double* avg_ms) {
   return LS_OK;
 }
 
-int ls_debug_gemm(ls_engine* e, int which, int n, const uint16_t* x_host, float* out_host) {
+int ls_debug_gemm(ls_engine* e, int which, int n, const float* x_host, float* out_host) {
   if (!e || !x_host || !out_host || which < 0 || which > 5 || n < 1) return LS_EINVAL;
   try {
     REQUIRE(e->finalized, LS_EINVAL, "engine not finalized");
@@ -1698,7 +1702,16 @@ int ls_debug_gemm(ls_engine* e, int which, int n, const uint16_t* x_host, float*
     XBuf* x[] = {&e->x_h, &e->x_attn, &e->x_h, &e->x_act, &e->x_h, &e->x_cat};
     const Gemm& gm = *g[which];
     XBuf& xb = *x[which];
-    CK(cudaMemcpyAsync(xb.ptr, x_host, sizeof(uint16_t) * (size_t)n * gm.K, cudaMemcpyHostToDevice, e->stream));
+    std::vector<bf16> xs((size_t)2 * n * gm.K);
+    for (int b = 0; b < n; ++b)
+      for (int k = 0; k < gm.K; ++k) {
+        const float v = x_host[(size_t)b * gm.K + k];
+        const bf16 hi = __float2bfloat16_rn(v);
+        xs[(size_t)(2 * b) * gm.K + k] = hi;
+        xs[(size_t)(2 * b + 1) * gm.K + k] = __float2bfloat16_rn(v - __bfloat162float(hi));
+      }
+    CK(cudaMemcpyAsync(xb.ptr, xs.data(), sizeof(bf16) * xs.size(), cudaMemcpyHostToDevice, e->stream));
+    CK(cudaStreamSynchronize(e->stream));
     float* out = which == 4 ? e->logits : e->part;
     gemm(*e, gm, xb, out, n);
     std::vector<float> part((size_t)gm.splits * e->cap * gm.Mw);

@@ -3,7 +3,8 @@
 //   part[s][n][m] = sum_{k in split s} W[m][k] * X[n][k]
 //
 // W is a bf16 weight [Mw, K] (row-major, K contiguous); X is the bf16 lane
-// activation [Ncap, K]. Weight rows fill the 128-row M side of tcgen05.mma and
+// activation [2 * Ncap, K] holding a (hi, lo) row pair per lane, starting at
+// row x_row0. Weight rows fill the 128-row M side of tcgen05.mma and
 // decode lanes sit on N (16..256), so a handful of lanes still uses the full
 // tensor-core M width. Each CTA owns one 128-row tile, one K split and one
 // N tile; TMA streams 128x64 weight boxes and BNx64 activation boxes into a
@@ -117,22 +118,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
   __syncthreads();
 
-  // Epilogue: TMEM lane = weight row, TMEM column = lane index n.
+  // Epilogue: TMEM lane = weight row, TMEM column = activation row. Each lane
+  // n owns two activation rows, 2n = bf16(x) and 2n+1 = bf16(x - bf16(x)), so
+  // its output is the sum of two adjacent accumulator columns: activations
+  // enter at ~16 mantissa bits for the price of idle tensor-core work only.
   const bool have = mbar_wait(acc_bar, 0, err, kDevTimeoutAcc);
   tc_fence_after();
   const int row = m0 + warp * 32 + lane;
   float* out = part + (long)split * split_stride;
 #pragma unroll 1
   for (int c0 = 0; c0 < BN; c0 += 8) {
-    if (n0 + c0 >= n_valid) break;
+    if (n0 + c0 >= 2 * n_valid) break;
     uint32_t r[8];
     tmem_ld_32x32b_x8(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, r);
     tmem_ld_wait();
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int n = n0 + c0 + j;
+    for (int j = 0; j < 4; ++j) {
+      const int n = (n0 + c0) / 2 + j;
       if (n < n_valid && row < Mw) {
-        out[(long)n * Mw + row] = (have && nkb > 0) ? __uint_as_float(r[j]) : 0.f;
+        const float v = __uint_as_float(r[2 * j]) + __uint_as_float(r[2 * j + 1]);
+        out[(long)n * Mw + row] = (have && nkb > 0) ? v : 0.f;
       }
     }
   }

@@ -113,7 +113,7 @@ __global__ void prep_kernel(PrepArgs a) {
     for (int i = threadIdx.x; i < H; i += blockDim.x) {
       float v = row[i];
       if (a.x_norm_w) v = v * inv * bf2f(a.x_norm_w[i]);
-      a.x[(long)b * H + i] = f2bf(v);
+      store_pair(a.x, H, b, i, v);
     }
   }
 }
@@ -131,8 +131,8 @@ __global__ void cat_state_kernel(Meta meta, int H, const float* __restrict__ ban
     return;
   }
   for (int i = threadIdx.x; i < H; i += blockDim.x) {
-    x[(long)b * 2 * H + i] = f2bf(bank_h[(long)si * H + i]);
-    x[(long)b * 2 * H + H + i] = f2bf(bank_inj[(long)si * H + i]);
+    store_pair(x, 2L * H, b, i, bank_h[(long)si * H + i]);
+    store_pair(x, 2L * H, b, H + i, bank_inj[(long)si * H + i]);
   }
 }
 
@@ -211,7 +211,7 @@ __global__ void resid_epi_kernel(ResidArgs a) {
     for (int i = threadIdx.x; i < H; i += blockDim.x) {
       float v = row[i];
       if (a.x_norm_w) v = v * inv * bf2f(a.x_norm_w[i]);
-      a.x[(long)b * H + i] = f2bf(v);
+      store_pair(a.x, H, b, i, v);
     }
   }
 }
@@ -232,7 +232,7 @@ __global__ void act_epi_kernel(const float* __restrict__ part, int splits, long 
     u += pb[(long)s * split_stride + I + i];
   }
   const float sg = g / (1.f + expf(-g));
-  x[(long)b * I + i] = f2bf(sg * u);
+  store_pair(x, I, b, i, sg * u);
 }
 
 // ------------------------------------------------------------- QKV epilogue
@@ -496,7 +496,7 @@ __global__ void attn_combine_kernel(Meta meta, int nh, int hd, int max_chunks,
       ll += ml_part[(base + c) * 2 + 1] * w;
       aa += o_part[(base + c) * hd + d] * w;
     }
-    x[(long)b * nh * hd + h * hd + d] = f2bf(ll > 0.f ? aa / ll : 0.f);
+    store_pair(x, (long)nh * hd, b, h * hd + d, ll > 0.f ? aa / ll : 0.f);
   }
 }
 

@@ -129,18 +129,16 @@ class Engine:
 
     GEMMS = {"qkv": 0, "o": 1, "gate_up": 2, "down": 3, "lm_head": 4, "adapter": 5}
 
-    def debug_gemm(self, which, x_bf16_bits):
-        """x: uint16 numpy [n, K] (bf16 bits) -> float32 [n, rows] (core layer 0 weights)."""
+    def debug_gemm(self, which, x):
+        """x: float32 numpy [n, K] -> float32 [n, rows] (core layer 0 weights)."""
         w = self.GEMMS[which]
         splits, rows, k = ctypes.c_int32(), ctypes.c_int32(), ctypes.c_int32()
         _lib.check(self.L.ls_gemm_splits(self.h, w, ctypes.byref(splits), ctypes.byref(rows),
                                          ctypes.byref(k)), self.h)
-        x = np.ascontiguousarray(x_bf16_bits, dtype=np.uint16)
+        x = np.ascontiguousarray(x, dtype=np.float32)
         assert x.shape[1] == k.value
         out = np.zeros((x.shape[0], rows.value), dtype=np.float32)
-        _lib.check(self.L.ls_debug_gemm(self.h, w, x.shape[0],
-                                        x.ctypes.data_as(ctypes.POINTER(ctypes.c_uint16)),
-                                        _f32p(out)), self.h)
+        _lib.check(self.L.ls_debug_gemm(self.h, w, x.shape[0], _f32p(x), _f32p(out)), self.h)
         return out, splits.value
 
     def close(self):
