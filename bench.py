@@ -1,0 +1,340 @@
+#!/usr/bin/env python
+"""LoopSpec decode benchmark (BASELINE.json configs[1] by default).
+
+Workload: Ouro-1.4B architecture, random init (seed 0), bf16 weights, batch 1,
+a 512-token prompt of uniform-random ids, 1024 greedy new tokens, LoopSpec
+first=1 second=2 (K=1, X=2), with the autoregressive path timed beside it.
+One step = one request through the public API (`generate_loopspec`).
+
+value   decode tokens/s (tokens after the first, as the reference's
+        generation_metrics, server/metrics.py:21-30) = sum of decode tokens of
+        all ranks / max over ranks of CUDA-event decode time; inputs already
+        resident in HBM.
+e2e     the same tokens / host wall time of the whole generate_loopspec call
+        (prompt upload, prefill, decode, readbacks), max over ranks.
+--impl reference   the reference algorithm's CPU implementation (the oracle
+        port: reference scheduler restated + fp32 model roles) on the host
+        cores, on a bounded sample of the same workload.
+Multi-GPU: one process per GPU, independent request replicas (weak scaling).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+from loopspec_b200.config import get_config  # noqa: E402
+from loopspec_b200.schedule import PipelineSchedule, accept_length  # noqa: E402
+
+METRIC = "decode tokens/s/GPU (bs=1, 1-8 B200), LoopSpec vs AR speedup, mean accepted len"
+UNIT = "tokens/s"
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=3)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", default="engine", choices=["engine", "reference"])
+    p.add_argument("--config", default="ouro-1.4b")
+    p.add_argument("--prompt", type=int, default=512)
+    p.add_argument("--new-tokens", type=int, default=1024)
+    p.add_argument("--first", type=int, default=1)
+    p.add_argument("--second", type=int, default=2)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def dist_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), \
+        int(os.environ.get("LOCAL_RANK", 0))
+
+
+def make_prompt(cfg, n, seed):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randint(0, cfg.vocab, (n,), generator=g).tolist()
+
+
+def schedule_for(cfg, args):
+    from loopspec_b200.config import parse_loopspec_flags
+    K, X = parse_loopspec_flags(cfg.stages, args.first, args.second)
+    return PipelineSchedule(cfg.stages, K, X)
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region (one GPU)."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu):
+        self.gpu = gpu
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        self.proc.wait(timeout=10)
+        rows = []
+        for line in open(self.path):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) >= 9:
+                rows.append(f)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(rows)}
+
+
+def bytes_per_decode(cfg, sch, stats, prompt_len):
+    """Algorithmic HBM bytes of the decode loop (weights + KV), per the
+    per-cycle formula K*W_core + [post]*W_lm + sum over lanes/iterations of KV reads."""
+    cycles = stats["pipeline_cycles"]
+    W_core = cfg.core_weight_bytes()
+    W_lm = cfg.vocab * cfg.hidden * 2
+    kv_tok = cfg.n_core_layers * cfg.kv_bytes_per_token_layer()
+    L = prompt_len + stats["decode_tokens"] / 2.0
+    post_calls = cycles if stats["post_rows"] else 0
+    return cycles * sch.step_size * W_core + post_calls * W_lm + stats["recurrent_rows"] * L * kv_tok
+
+
+def cpu_baseline(cfg, sch, args, threads):
+    """The oracle (reference algorithm, CPU, fp32) on a bounded sample."""
+    from oracle.executor import generate_loopspec_oracle
+    from oracle.model import OracleModel
+    from loopspec_b200.weights import init_random_weights
+    torch.set_num_threads(threads)
+    w = init_random_weights(cfg, 0, device="cpu", dtype=torch.float32)
+    model = OracleModel(cfg.as_dict(), w)
+    del w
+    prompt = make_prompt(cfg, 8, 7)
+    n_new = 5
+    t0 = time.perf_counter()
+    ids, st = generate_loopspec_oracle(model, sch, prompt, n_new)
+    dt = time.perf_counter() - t0
+    # oracle processes prompt tokens one at a time through all depths; count
+    # decode tokens only, against the whole sample's time (conservative)
+    return {"value": round(st["decode_tokens"] / dt, 4), "unit": UNIT, "cores": threads,
+            "kind": "port",
+            "sample": f"{cfg.name} fp32 oracle, 8-token prompt, {n_new} LoopSpec "
+                      f"K={sch.step_size} X={sch.second_step} greedy tokens, time incl. prefill"}
+
+
+def reference_arm(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    cfg = get_config(args.config)
+    sch = schedule_for(cfg, args)
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    from oracle.executor import generate_loopspec_oracle
+    from oracle.model import OracleModel
+    from loopspec_b200.weights import init_random_weights
+    w = init_random_weights(cfg, 0, device="cpu", dtype=torch.float32)
+    model = OracleModel(cfg.as_dict(), w)
+    del w
+    n_prompt, n_new = 8, 4
+    times, toks = [], []
+    for i in range(args.warmup + args.steps):
+        prompt = make_prompt(cfg, n_prompt, 100 + i)
+        t0 = time.perf_counter()
+        ids, st = generate_loopspec_oracle(model, sch, prompt, n_new)
+        dt = time.perf_counter() - t0
+        if i >= args.warmup:
+            times.append(dt)
+            toks.append(st["decode_tokens"])
+    value = sum(toks) / sum(times)
+    sample = (f"{cfg.name} fp32 oracle on {threads} host threads: {n_prompt}-token prompt, "
+              f"{n_new} greedy LoopSpec tokens per step (time incl. the prompt pass)")
+    line = {"metric": METRIC, "value": round(value, 4), "unit": UNIT, "impl": "reference",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(1e3 * sum(times) / len(times), 1), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"{cfg.name} LoopSpec first={args.first} second={args.second} "
+                                   f"greedy (bounded CPU sample)", "global_batch": 1},
+            "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": threads,
+                             "kind": "port", "sample": sample},
+            "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def engine_arm(args):
+    from loopspec_b200.engine import Engine
+    from loopspec_b200.executor import generate_autoregressive, generate_loopspec
+    from loopspec_b200.weights import init_random_weights
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+
+    def barrier():
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if dist is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum_over_ranks(x):
+        if dist is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        return float(t.item())
+
+    cfg = get_config(args.config)
+    sch = schedule_for(cfg, args)
+    weights = init_random_weights(cfg, 0, device=f"cuda:{local}", dtype=torch.bfloat16)
+    max_ctx = args.prompt + args.new_tokens + 64
+    eng = Engine(cfg, sch, weights, device=local, max_context=max_ctx, max_prompt=args.prompt)
+
+    def prompt_of(i):
+        return make_prompt(cfg, args.prompt, 1000 * rank + i)
+
+    for i in range(args.warmup):
+        generate_loopspec(eng, prompt_of(i), args.new_tokens)
+    barrier()
+    clocks = Clocks(local)
+    clocks.start()
+    dec_tok = dec_ms = wall = 0.0
+    h2d = d2h = 0
+    agg = None
+    for i in range(args.steps):
+        t0 = time.perf_counter()
+        ids, st = generate_loopspec(eng, prompt_of(args.warmup + i), args.new_tokens)
+        wall += time.perf_counter() - t0
+        dec_tok += st["decode_tokens"]
+        dec_ms += st["decode_device_ms"]
+        h2d += st["h2d_bytes"] + 8 * args.prompt
+        d2h += st["d2h_bytes"]
+        agg = st if agg is None else {k: agg[k] + st[k] for k in st}
+    barrier()
+    clk = clocks.stop()
+    dec_s_max = max_over_ranks(dec_ms / 1e3)
+    wall_max = max_over_ranks(wall)
+    tok_all = sum_over_ranks(dec_tok)
+    new_all = sum_over_ranks(args.steps * args.new_tokens)
+    value = tok_all / dec_s_max
+    e2e = new_all / wall_max
+
+    # autoregressive beside it (one request, same prompt distribution)
+    ar_ids, ar_st = generate_autoregressive(eng, prompt_of(0), args.new_tokens)
+    ar_tok_s = ar_st["decode_tokens"] / (ar_st["decode_device_ms"] / 1e3)
+
+    # roofline of the dominant kernel: the tcgen05 GEMM, over a core-weight sweep
+    lanes = max(1, round(agg["recurrent_rows"] / max(agg["pipeline_cycles"], 1) / sch.step_size))
+    launch_ms, launch_bytes = eng.time_core_gemms(lanes, iters=5)
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+        peak_gbs, peak_src = float(peaks["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        peak_gbs, peak_src = 6650.0, "fallback"
+    achieved = launch_bytes / (launch_ms / 1e3) / 1e9
+    decode_bytes = bytes_per_decode(cfg, sch, agg, args.prompt)
+    decode_gbs = decode_bytes / (dec_ms / 1e3) / 1e9
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(1e3 * wall_max / args.steps, 1),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (uniform-random prompt ids, random-init weights seed 0)",
+            "config": {"workload": f"{cfg.name} LoopSpec first={args.first} second={args.second} "
+                                   f"greedy, prompt {args.prompt}, {args.new_tokens} new tokens",
+                       "global_batch": world, "seq_len": args.prompt + args.new_tokens,
+                       "parallelism": f"replicas x{world}",
+                       "l2": "inputs larger than L2 (2.47 GB of core weights per iteration)"},
+            "loopspec_tok_s": round(value / world, 2),
+            "ar_tok_s": round(ar_tok_s, 2),
+            "speedup_vs_ar": round((value / world) / ar_tok_s, 3),
+            "mean_accept_len": round(accept_length(agg, sch), 4),
+            "counters": {k: int(agg[k]) for k in ("pipeline_cycles", "pre_rows", "recurrent_rows",
+                                                  "post_rows", "verified_proposals",
+                                                  "first_rejections", "second_verifications",
+                                                  "second_acceptances", "second_rejections",
+                                                  "decode_tokens")},
+            "roofline": {"bound": "hbm", "kernel": "gemm_tc_kernel (core weight sweep)",
+                         "achieved": round(achieved, 1), "peak": peak_gbs, "unit": "GB/s",
+                         "frac": round(achieved / peak_gbs, 4), "peak_source": peak_src,
+                         "traffic": None, "lanes": lanes,
+                         "bytes_per_launch": round(launch_bytes),
+                         "avg_launch_us": round(launch_ms * 1e3, 3)},
+            "decode_roofline": {"achieved": round(decode_gbs, 1), "peak": peak_gbs,
+                                "unit": "GB/s", "frac": round(decode_gbs / peak_gbs, 4),
+                                "bytes": "K*W_core + W_lm per post call + KV reads"},
+            "e2e": {"value": round(e2e, 2), "unit": UNIT,
+                    "h2d_bytes_per_step": int(h2d / args.steps),
+                    "d2h_bytes_per_step": int(d2h / args.steps),
+                    "note": "new tokens / wall time of generate_loopspec incl. prefill"},
+            "gpu_launches": None,
+            "clocks": clk,
+        }
+        n_kern = {r: eng.kernel_count(r, lanes) for r in ("pre", "core", "post")}
+        per_cycle = n_kern["core"] * sch.step_size + n_kern["post"] + n_kern["pre"]
+        line["gpu_launches"] = int(agg["pipeline_cycles"] * per_cycle / args.steps * args.steps)
+        line["gpu_launches_note"] = "kernels in the timed region (per-cycle graph kernel count x cycles)"
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(cfg, sch, args, os.cpu_count() or 1)
+        print(json.dumps(line), flush=True)
+    eng.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        reference_arm(args)
+    else:
+        from loopspec_b200.build import build
+        build()
+        engine_arm(args)
+
+
+if __name__ == "__main__":
+    main()

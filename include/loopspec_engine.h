@@ -68,6 +68,8 @@ typedef struct ls_stats {
   double decode_device_ms;   /* CUDA-event time of the decode loop            */
   double decode_host_s;      /* host clock, after first token to last commit  */
   double prefill_device_ms;
+  int64_t h2d_bytes;         /* host->device bytes copied for the request       */
+  int64_t d2h_bytes;         /* device->host bytes copied for the request       */
 } ls_stats;
 
 typedef struct ls_engine ls_engine;
@@ -146,6 +148,15 @@ int ls_time_role(ls_engine* eng, int role, int n_lanes, int context_len, int ite
 /* Time one GEMM of the core layer 0 (which: 0 qkv, 1 o, 2 gate_up, 3 down,
  * 4 lm_head) over n_lanes lanes, `iters` launches; average device ms. */
 int ls_time_gemm(ls_engine* eng, int which, int n_lanes, int iters, double* avg_ms);
+
+/* Time every core GEMM of one recurrent iteration (qkv, o, gate_up, down
+ * for each core layer, one launch each) over n_lanes lanes, `iters` sweeps
+ * back to back with CUDA events on the engine stream. The sweep streams all
+ * core weights (larger than L2), so no launch reads another's weights from
+ * L2. Returns the average launch time and the average algorithmic bytes of
+ * one launch (weights + activation rows read + fp32 partials written). */
+int ls_time_core_gemms(ls_engine* eng, int n_lanes, int iters, double* avg_launch_ms,
+                       double* bytes_per_launch);
 
 /* Number of kernels one role call of n_lanes launches. */
 int ls_role_kernel_count(ls_engine* eng, int role, int n_lanes, int* count);

@@ -51,6 +51,7 @@ class Stats(ctypes.Structure):
         ("second_verifications", _i64), ("second_acceptances", _i64),
         ("second_rejections", _i64), ("decode_tokens", _i64),
         ("decode_device_ms", _f64), ("decode_host_s", _f64), ("prefill_device_ms", _f64),
+        ("h2d_bytes", _i64), ("d2h_bytes", _i64),
     ]
 
     def as_dict(self):
@@ -81,6 +82,7 @@ SIGNATURES = [
                                     ctypes.POINTER(Stats)]),
     ("ls_time_role", _i32, [_P, _i32, _i32, _i32, _i32, ctypes.POINTER(_f64)]),
     ("ls_time_gemm", _i32, [_P, _i32, _i32, _i32, ctypes.POINTER(_f64)]),
+    ("ls_time_core_gemms", _i32, [_P, _i32, _i32, ctypes.POINTER(_f64), ctypes.POINTER(_f64)]),
     ("ls_role_kernel_count", _i32, [_P, _i32, _i32, ctypes.POINTER(_i32)]),
     ("ls_debug_gemm", _i32, [_P, _i32, _i32, _PF32, _PF32]),
     ("ls_gemm_splits", _i32, [_P, _i32, ctypes.POINTER(_i32), ctypes.POINTER(_i32), ctypes.POINTER(_i32)]),

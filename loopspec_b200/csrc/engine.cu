@@ -92,7 +92,9 @@ int cdiv(long a, long b) { return (int)((a + b - 1) / b); }
 struct Gemm {
   const bf16* w = nullptr;
   int Mw = 0, K = 0, splits = 1;
-  CUtensorMap map;
+  CUtensorMap map;      // 128-row weight boxes
+  CUtensorMap map64;    // 64-row boxes (gate/up halves of the SwiGLU tile)
+  bool has_map64 = false;
 };
 
 struct XBuf {
@@ -388,10 +390,12 @@ struct ls_engine {
   long long *amax_dev = nullptr, *amax_host = nullptr;
   float* logits_host = nullptr;
   int* err_dev = nullptr;
+  int* attn_tickets = nullptr;  // [cap][n_kv_heads] chunk-arrival counters, zero between calls
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
 
   std::map<std::pair<int, int>, cudaGraphExec_t> graphs;
   int kernels_in_call = 0;
+  int64_t h2d_bytes = 0, d2h_bytes = 0;   // host<->device traffic counters
 
   Timelines tl;
   int prefill_len = -1;   // len(prompt) - 1 of the current request
@@ -429,21 +433,29 @@ struct ls_engine {
     return it->second.first;
   }
 
+  // K splits per 128-row tile, aiming at about two CTAs per SM; a split group
+  // is one thread-block cluster, so at most kMaxSplits. Depends only on the
+  // weight shape (never on the batch).
   int choose_splits(int Mw, int Kd) const {
     const int tiles = cdiv(Mw, kGemmBM);
     const int KB = cdiv(Kd, kGemmBK);
     int s = (2 * num_sms + tiles / 2) / tiles;
-    return std::max(1, std::min(s, KB));
+    return std::max(1, std::min(std::min(s, KB), kMaxSplits));
   }
 
-  Gemm make_gemm(const bf16* w, int Mw, int Kd, int splits = 0) {
+  Gemm make_gemm(const bf16* w, int Mw, int Kd, int splits = 0, bool swiglu = false) {
     Gemm g;
     g.w = w;
     g.Mw = Mw;
     g.K = Kd;
     g.splits = splits > 0 ? splits : choose_splits(Mw, Kd);
     g.map = make_map_2d(w, Kd, Mw, kGemmBM);
-    part_elems = std::max(part_elems, (long)g.splits * cap * Mw);
+    if (swiglu) {
+      REQUIRE(Mw % kGemmBM == 0, LS_EINVAL, "gate_up rows must be a multiple of 128");
+      g.map64 = make_map_2d(w, Kd, Mw, kGemmBM / 2);
+      g.has_map64 = true;
+    }
+    part_elems = std::max(part_elems, (long)cap * Mw);
     return g;
   }
 
@@ -469,7 +481,7 @@ struct ls_engine {
       }
       lw.g_qkv = make_gemm(lw.qkv, QD + 2 * KVD, H);
       lw.g_o = make_gemm(lw.o, H, QD);
-      lw.g_gu = make_gemm(lw.gu, 2 * I, H);
+      lw.g_gu = make_gemm(lw.gu, 2 * I, H, 0, true);
       lw.g_down = make_gemm(lw.down, H, I);
     }
   }
@@ -500,13 +512,15 @@ struct ls_engine {
     REQUIRE((HD == 64 && (G == 1 || G == 2 || G == 4)) || (HD == 128 && (G == 1 || G == 2)),
             LS_EINVAL, "unsupported head_dim / GQA group");
     REQUIRE(H % 64 == 0 && I % 64 == 0 && QD % 64 == 0, LS_EINVAL, "hidden/intermediate must be multiples of 64");
-    REQUIRE(H <= 8192 && QD + 2 * KVD <= 12288, LS_EINVAL, "row too long for the epilogue kernels");
+    REQUIRE(H % 128 == 0 && H <= 8192 && QD + 2 * KVD <= 12288, LS_EINVAL,
+            "hidden must be a multiple of 128 and at most 8192 for the row kernels");
 
     cap = std::max(max_rows, prefill_chunk);
     max_ctx = sc.max_context;
     REQUIRE(max_ctx > 1 && sc.max_prompt >= 1 && sc.max_prompt < max_ctx, LS_EINVAL,
             "need 1 <= max_prompt < max_context");
     max_chunks = cdiv(max_ctx, kAttnChunk);
+    REQUIRE(max_chunks <= kAttnMaxChunks, LS_EINVAL, "max_context above the attention kernel's limit");
     bank_rows = max_rows + prefill_chunk;
     n_attn_layers = mc.n_pre_layers + mc.n_core_layers + mc.n_post_layers;
 
@@ -586,6 +600,7 @@ struct ls_engine {
     CK(cudaMallocHost(&amax_host, sizeof(long long) * cap));
     CK(cudaMallocHost(&logits_host, sizeof(float) * (size_t)V));
     err_dev = dalloc<int>(1);
+    attn_tickets = dalloc<int>((long)cap * NKV);
     std::vector<float> inv(HD / 2);
     for (int i = 0; i < HD / 2; ++i)
       inv[i] = (float)(1.0 / std::pow((double)mc.rope_theta, (2.0 * i) / HD));
@@ -608,19 +623,22 @@ struct ls_engine {
   }
 
   void set_smem_attrs() {
-#define LS_SMEM(BN, ST)                                                                    \
-  CK(cudaFuncSetAttribute(gemm_tc_kernel<BN, ST>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+#define LS_SMEM1(BN, ST, EPI)                                                                   \
+  CK(cudaFuncSetAttribute(gemm_tc_kernel<BN, ST, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
                           GemmSmem<BN, ST>::kTotal))
+#define LS_SMEM(BN, ST)          \
+  LS_SMEM1(BN, ST, kEpiStore);   \
+  LS_SMEM1(BN, ST, kEpiQkvRope); \
+  LS_SMEM1(BN, ST, kEpiSwiGLU)
     LS_SMEM(16, 4);
     LS_SMEM(32, 4);
     LS_SMEM(64, 4);
     LS_SMEM(128, 4);
     LS_SMEM(256, 3);
 #undef LS_SMEM
+#undef LS_SMEM1
     const int row_smem = std::max(QD + 2 * KVD, 2 * H) * (int)sizeof(float);
     CK(cudaFuncSetAttribute(qkv_epi_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, row_smem));
-    CK(cudaFuncSetAttribute(resid_epi_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, row_smem));
-    CK(cudaFuncSetAttribute(prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, row_smem));
   }
 };
 
@@ -640,18 +658,44 @@ int pick_bn(int n) {
 }
 
 // n lanes = 2n activation rows (hi/lo pairs) starting at lane `lane0`.
-void gemm(ls_engine& e, const Gemm& g, XBuf& x, float* out, int n, int lane0 = 0) {
+// Launch one weight-streaming GEMM over n lanes (2n activation rows, hi/lo
+// pairs) starting at lane `lane0`, as (m_tiles, splits, n_tiles) CTAs in
+// clusters of (1, splits, 1).
+void gemm(ls_engine& e, const Gemm& g, XBuf& x, const GemmEpi& epi, int kind, int n,
+          int lane0 = 0) {
   REQUIRE(n >= 1 && 2 * (lane0 + n) <= x.rows, LS_EINVAL, "GEMM lane count out of range");
+  REQUIRE(g.splits >= 1 && g.splits <= kMaxSplits, LS_EINVAL, "bad split count");
+  REQUIRE(kind != kEpiSwiGLU || g.has_map64, LS_EINVAL, "SwiGLU needs the 64-row weight map");
   const int bn = pick_bn(2 * n);
   const CUtensorMap& xm = x.map(bn);
   const int x_row0 = 2 * lane0;
-  dim3 grid(cdiv(g.Mw, kGemmBM), g.splits, cdiv(2 * n, bn));
-  const long ss = (long)e.cap * g.Mw;
-  const bool pdl = e.sc.use_pdl != 0;
-  const dim3 blk(kGemmThreads);
-#define LS_GEMM(BN, ST)                                                                      \
-  launch(gemm_tc_kernel<BN, ST>, grid, blk, GemmSmem<BN, ST>::kTotal, e.stream, pdl, g.map, xm, \
-         out, g.Mw, g.K, n, x_row0, g.splits, ss, e.err_dev)
+  const int m_tiles = kind == kEpiSwiGLU ? g.Mw / kGemmBM : cdiv(g.Mw, kGemmBM);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(m_tiles, g.splits, cdiv(2 * n, bn));
+  cfg.blockDim = dim3(kGemmThreads);
+  cfg.stream = e.stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = g.splits;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = e.sc.use_pdl ? 2 : 1;
+  const CUtensorMap& wm = kind == kEpiSwiGLU ? g.map64 : g.map;
+#define LS_GEMM_K(BN, ST, EPI)                                                                     \
+  do {                                                                                              \
+    cfg.dynamicSmemBytes = GemmSmem<BN, ST>::kTotal;                                                \
+    CK(cudaLaunchKernelEx(&cfg, gemm_tc_kernel<BN, ST, EPI>, wm, xm, epi, g.Mw, g.K, n, x_row0, \
+                          g.splits, e.err_dev));                                                   \
+  } while (0)
+#define LS_GEMM(BN, ST)                                           \
+  do {                                                            \
+    if (kind == kEpiQkvRope) LS_GEMM_K(BN, ST, kEpiQkvRope);      \
+    else if (kind == kEpiSwiGLU) LS_GEMM_K(BN, ST, kEpiSwiGLU);   \
+    else LS_GEMM_K(BN, ST, kEpiStore);                            \
+  } while (0)
   switch (bn) {
     case 16: LS_GEMM(16, 4); break;
     case 32: LS_GEMM(32, 4); break;
@@ -660,7 +704,18 @@ void gemm(ls_engine& e, const Gemm& g, XBuf& x, float* out, int n, int lane0 = 0
     default: LS_GEMM(256, 3); break;
   }
 #undef LS_GEMM
+#undef LS_GEMM_K
   e.kernels_in_call++;
+}
+
+GemmEpi store_to(float* out) {
+  GemmEpi ep{};
+  ep.out = out;
+  return ep;
+}
+
+void gemm_store(ls_engine& e, const Gemm& g, XBuf& x, float* out, int n, int lane0 = 0) {
+  gemm(e, g, x, store_to(out), kEpiStore, n, lane0);
 }
 
 template <typename... KArgs, typename... Args>
@@ -674,9 +729,13 @@ void map_update(ls_engine& e, Meta meta, int n) {
   klaunch(e, map_update_kernel, dim3(n), dim3(128), 0, meta, n, e.map, e.max_ctx, e.rows, e.err_dev);
 }
 
+// Threads of a per-lane row kernel: one float4 column each, at most 1024.
+int row_threads(int H) { return std::min(1024, H / 4); }
+
 void attention(ls_engine& e, Meta meta, int n, const bf16* kp, const bf16* vp) {
   AttnArgs a{meta, e.NH, e.NKV, e.q, e.map, e.max_ctx, e.rows, kp, vp, e.n_slots,
-             e.max_chunks, e.o_part, e.ml_part, 1.0f / std::sqrt((float)e.HD), e.err_dev};
+             e.max_chunks, e.o_part, e.ml_part, e.attn_tickets, e.x_attn.ptr,
+             1.0f / std::sqrt((float)e.HD), e.err_dev};
   const dim3 grid(n, e.NKV, e.max_chunks), blk(kAttnThreads);
   const int G = e.NH / e.NKV;
   if (e.HD == 128 && G == 1) klaunch(e, attn_kernel<128, 1>, grid, blk, 0, a);
@@ -684,17 +743,14 @@ void attention(ls_engine& e, Meta meta, int n, const bf16* kp, const bf16* vp) {
   else if (e.HD == 64 && G == 1) klaunch(e, attn_kernel<64, 1>, grid, blk, 0, a);
   else if (e.HD == 64 && G == 2) klaunch(e, attn_kernel<64, 2>, grid, blk, 0, a);
   else klaunch(e, attn_kernel<64, 4>, grid, blk, 0, a);
-  klaunch(e, attn_combine_kernel, dim3(n, e.NH), dim3(e.HD), 0, meta, e.NH, e.HD, e.max_chunks,
-          (const float*)e.o_part, (const float*)e.ml_part, e.x_attn.ptr);
 }
 
 ResidArgs resid_base(ls_engine& e, Meta meta, const Gemm& g) {
   ResidArgs a{};
   a.meta = meta;
   a.H = e.H;
-  a.part = e.part;
-  a.splits = g.splits;
-  a.split_stride = (long)e.cap * g.Mw;
+  (void)g;
+  a.part = e.part;   // the GEMM already reduced its K splits
   a.bank_rows = e.bank_rows;
   a.eps = e.mc.rms_eps;
   a.err = e.err_dev;
@@ -702,7 +758,9 @@ ResidArgs resid_base(ls_engine& e, Meta meta, const Gemm& g) {
 }
 
 void resid(ls_engine& e, const ResidArgs& a, int n) {
-  klaunch(e, resid_epi_kernel, dim3(n), dim3(256), (size_t)e.H * sizeof(float), a);
+  const int thr = row_threads(e.H);
+  if (cdiv(e.H / 4, thr) == 1) klaunch(e, resid_epi_kernel<1>, dim3(n), dim3(thr), 0, a);
+  else klaunch(e, resid_epi_kernel<2>, dim3(n), dim3(thr), 0, a);
 }
 
 // Norm applied to the input of a layer's first GEMM (none for OLMo2 post-norm).
@@ -726,12 +784,28 @@ void run_stack(ls_engine& e, Stack& st, int n, Meta meta, const StackEnd& end) {
     bf16* kp = e.kpool + kvoff;
     bf16* vp = e.vpool + kvoff;
 
-    gemm(e, w.g_qkv, e.x_h, e.part, n);
-    QkvArgs qa{meta, e.NH, e.NKV, e.HD, e.part, w.g_qkv.splits, (long)e.cap * w.g_qkv.Mw,
-               w.qn, w.kn, e.inv_freq, e.mc.rms_eps, e.q, kp, vp, e.n_slots, e.err_dev};
-    klaunch(e, qkv_epi_kernel, dim3(n), dim3(256), (size_t)(e.QD + 2 * e.KVD) * sizeof(float), qa);
+    if (w.qn) {
+      // OLMo2 QK-norm needs whole-row sums: plain GEMM, then the QKV kernel.
+      gemm_store(e, w.g_qkv, e.x_h, e.part, n);
+      QkvArgs qa{meta, e.NH, e.NKV, e.HD, e.part, 1, 0, w.qn, w.kn, e.inv_freq, e.mc.rms_eps,
+                 e.q, kp, vp, e.n_slots, e.err_dev};
+      klaunch(e, qkv_epi_kernel, dim3(n), dim3(256), (size_t)(e.QD + 2 * e.KVD) * sizeof(float), qa);
+    } else {
+      // RoPE and the K/V cache write run in the GEMM's reduction epilogue.
+      GemmEpi ep{};
+      ep.meta = meta.p;
+      ep.inv_freq = e.inv_freq;
+      ep.q = e.q;
+      ep.kpool = kp;
+      ep.vpool = vp;
+      ep.hd = e.HD;
+      ep.nh = e.NH;
+      ep.nkv = e.NKV;
+      ep.n_slots = e.n_slots;
+      gemm(e, w.g_qkv, e.x_h, ep, kEpiQkvRope, n);
+    }
     attention(e, meta, n, kp, vp);
-    gemm(e, w.g_o, e.x_attn, e.part, n);
+    gemm_store(e, w.g_o, e.x_attn, e.part, n);
 
     ResidArgs ra = resid_base(e, meta, w.g_o);
     ra.resid = e.h;
@@ -747,10 +821,12 @@ void run_stack(ls_engine& e, Stack& st, int n, Meta meta, const StackEnd& end) {
     }
     resid(e, ra, n);
 
-    gemm(e, w.g_gu, e.x_h, e.part, n);
-    klaunch(e, act_epi_kernel, dim3(cdiv(e.I, 256), n), dim3(256), 0, (const float*)e.part,
-            w.g_gu.splits, (long)e.cap * w.g_gu.Mw, e.I, e.x_act.ptr);
-    gemm(e, w.g_down, e.x_act, e.part, n);
+    // gate_up with SiLU(gate) * up fused into its epilogue -> x_act
+    GemmEpi eg{};
+    eg.x_act = e.x_act.ptr;
+    eg.I = e.I;
+    gemm(e, w.g_gu, e.x_h, eg, kEpiSwiGLU, n);
+    gemm_store(e, w.g_down, e.x_act, e.part, n);
 
     ResidArgs rb = resid_base(e, meta, w.g_down);
     rb.resid = e.r;
@@ -796,7 +872,9 @@ void prep(ls_engine& e, Meta meta, int n, bool embed_mode, float* bank_out, bool
   pa.eps = e.mc.rms_eps;
   pa.vocab = e.V;
   pa.err = e.err_dev;
-  klaunch(e, prep_kernel, dim3(n), dim3(256), (size_t)e.H * sizeof(float), pa);
+  const int thr = row_threads(e.H);
+  if (cdiv(e.H / 4, thr) == 1) klaunch(e, prep_kernel<1>, dim3(n), dim3(thr), 0, pa);
+  else klaunch(e, prep_kernel<2>, dim3(n), dim3(thr), 0, pa);
 }
 
 // The kernel chain of one role call over n lanes whose metadata is in the
@@ -832,7 +910,7 @@ void enqueue_role(ls_engine& e, int role, int n, const PostOpts& po = PostOpts()
       // adapter(cat(hidden, injected)) then the core blocks (raven.py:271-281)
       klaunch(e, cat_state_kernel, dim3(n), dim3(256), 0, meta, e.H, (const float*)e.bank_h,
               (const float*)e.bank_inj, e.bank_rows, e.x_cat.ptr, e.err_dev);
-      gemm(e, e.g_adapter, e.x_cat, e.part, n);
+      gemm_store(e, e.g_adapter, e.x_cat, e.part, n);
       ResidArgs ra = resid_base(e, meta, e.g_adapter);
       ra.bias = e.adapter_b;
       ra.out_h = e.h;
@@ -856,7 +934,7 @@ void enqueue_role(ls_engine& e, int role, int n, const PostOpts& po = PostOpts()
     }
     if (po.head) {
       const int lanes = po.head_lanes < 0 ? n : po.head_lanes;
-      gemm(e, e.g_lm, e.x_h, e.logits, lanes, po.head_lane0);
+      gemm_store(e, e.g_lm, e.x_h, e.logits, lanes, po.head_lane0);
       klaunch(e, argmax_kernel, dim3(lanes), dim3(1024), 0, (const float*)e.logits, e.V, (long)e.V,
               e.amax_dev);
     }
@@ -873,15 +951,17 @@ int* stage_meta(ls_engine& e) {
   return p;
 }
 
-void upload_meta(ls_engine& e, int role, const int* host) {
-  CK(cudaMemcpyAsync(e.meta_dev + (long)role * kMetaFields * e.cap, host,
-                     sizeof(int) * kMetaFields * e.cap, cudaMemcpyHostToDevice, e.stream));
+void upload_meta(ls_engine& e, int role, const int* host, int n) {
+  const size_t bytes = sizeof(int) * kMetaFields * (size_t)n;
+  CK(cudaMemcpyAsync(e.meta_dev + (long)role * kMetaFields * e.cap, host, bytes,
+                     cudaMemcpyHostToDevice, e.stream));
+  e.h2d_bytes += (int64_t)bytes;
 }
 
 void run_role(ls_engine& e, int role, int n, const int* host_meta, bool graphable,
               const PostOpts& po = PostOpts()) {
   REQUIRE(n >= 1 && n <= e.cap, LS_ECAPACITY, "role call wider than the lane capacity");
-  upload_meta(e, role, host_meta);
+  upload_meta(e, role, host_meta, n);
   if (!(graphable && e.sc.use_graphs)) {
     enqueue_role(e, role, n, po);
     return;
@@ -912,6 +992,7 @@ void run_role(ls_engine& e, int role, int n, const int* host_meta, bool graphabl
 void check_device(ls_engine& e) {
   int err = 0;
   CK(cudaMemcpy(&err, e.err_dev, sizeof(int), cudaMemcpyDeviceToHost));
+  e.d2h_bytes += sizeof(int);
   if (err != kDevOk) {
     CK(cudaMemset(e.err_dev, 0, sizeof(int)));
     static const char* names[] = {"ok", "TMA stage wait timed out", "free-stage wait timed out",
@@ -926,7 +1007,10 @@ void check_device(ls_engine& e) {
 // ============================================================ request execution
 namespace {
 
-void put(ls_engine& e, int* m, int field, int b, int v) { m[field * e.cap + b] = v; }
+void put(ls_engine& e, int* m, int field, int b, int v) {
+  (void)e;
+  m[b * kMetaFields + field] = v;
+}
 
 // Fill one lane of a role call. With a cursor, allocate the KV slot that this
 // token's K/V gets on that timeline and describe a pending fork copy.
@@ -1019,6 +1103,7 @@ long long prefill(ls_engine& e, const int64_t* prompt, int P, float* logits_out)
   }
   CK(cudaEventRecord(e.ev1, e.stream));
   CK(cudaMemcpyAsync(e.amax_host, e.amax_dev, sizeof(long long), cudaMemcpyDeviceToHost, e.stream));
+  e.d2h_bytes += sizeof(long long);
   if (logits_out)
     CK(cudaMemcpyAsync(e.logits_host, e.logits, sizeof(float) * e.V, cudaMemcpyDeviceToHost, e.stream));
   CK(cudaStreamSynchronize(e.stream));
@@ -1092,6 +1177,7 @@ void cycle(ls_engine& e, const std::vector<CycleLane>& lanes, std::vector<long l
   for (int j = 0; j < M; ++j)
     if (cs[j]) advance(cs[j], slots[j], true);
   CK(cudaMemcpyAsync(e.amax_host, e.amax_dev, sizeof(long long) * M, cudaMemcpyDeviceToHost, e.stream));
+  e.d2h_bytes += sizeof(long long) * M;
   if (logits_out) {
     for (int j = 0; j < M; ++j)
       CK(cudaMemcpyAsync(logits_out + (long)ep_rows[j] * e.V, e.logits + (long)j * e.V,
@@ -1360,6 +1446,7 @@ std::vector<long long> run_ar(ls_engine& e, long long first, int max_new, long l
     run_role(e, kPost, 1, m, true);
     if (c) advance(c, slot, true);
     CK(cudaMemcpyAsync(e.amax_host, e.amax_dev, sizeof(long long), cudaMemcpyDeviceToHost, e.stream));
+    e.d2h_bytes += sizeof(long long);
     CK(cudaStreamSynchronize(e.stream));
     e.staging_next = 0;
     check_device(e);
@@ -1508,6 +1595,7 @@ int ls_generate(ls_engine* e, const int64_t* prompt, int n_prompt, int max_new, 
   if (!e || !prompt || !out_ids || !n_out || max_new < 1 || (mode != 0 && mode != 1)) return LS_EINVAL;
   try {
     ls_stats st{};
+    e->h2d_bytes = e->d2h_bytes = 0;
     const long long first = prefill(*e, prompt, n_prompt, nullptr);
     float pms = 0.f;
     CK(cudaEventElapsedTime(&pms, e->ev0, e->ev1));
@@ -1532,6 +1620,8 @@ int ls_generate(ls_engine* e, const int64_t* prompt, int n_prompt, int max_new, 
     st.decode_tokens = std::max<int64_t>((int64_t)ids.size() - 1, 0);
     for (size_t i = 0; i < ids.size(); ++i) out_ids[i] = ids[i];
     *n_out = (int)ids.size();
+    st.h2d_bytes = e->h2d_bytes;
+    st.d2h_bytes = e->d2h_bytes;
     if (stats) *stats = st;
   } catch (const std::exception& ex) {
     return fail(e, ex);
@@ -1676,9 +1766,9 @@ int ls_time_gemm(ls_engine* e, int which, int n, int iters, double* avg_ms) {
     const Gemm* g[] = {&w.g_qkv, &w.g_o, &w.g_gu, &w.g_down, &e->g_lm};
     XBuf* x[] = {&e->x_h, &e->x_attn, &e->x_h, &e->x_act, &e->x_h};
     float* out = which == 4 ? e->logits : e->part;
-    gemm(*e, *g[which], *x[which], out, n);
+    gemm_store(*e, *g[which], *x[which], out, n);
     CK(cudaEventRecord(e->ev0, e->stream));
-    for (int i = 0; i < iters; ++i) gemm(*e, *g[which], *x[which], out, n);
+    for (int i = 0; i < iters; ++i) gemm_store(*e, *g[which], *x[which], out, n);
     CK(cudaEventRecord(e->ev1, e->stream));
     CK(cudaEventSynchronize(e->ev1));
     check_device(*e);
@@ -1713,17 +1803,11 @@ int ls_debug_gemm(ls_engine* e, int which, int n, const float* x_host, float* ou
     CK(cudaMemcpyAsync(xb.ptr, xs.data(), sizeof(bf16) * xs.size(), cudaMemcpyHostToDevice, e->stream));
     CK(cudaStreamSynchronize(e->stream));
     float* out = which == 4 ? e->logits : e->part;
-    gemm(*e, gm, xb, out, n);
-    std::vector<float> part((size_t)gm.splits * e->cap * gm.Mw);
-    CK(cudaMemcpyAsync(part.data(), out, sizeof(float) * part.size(), cudaMemcpyDeviceToHost, e->stream));
+    gemm_store(*e, gm, xb, out, n);
+    CK(cudaMemcpyAsync(out_host, out, sizeof(float) * (size_t)n * gm.Mw, cudaMemcpyDeviceToHost,
+                       e->stream));
     CK(cudaStreamSynchronize(e->stream));
     check_device(*e);
-    for (int b = 0; b < n; ++b)
-      for (int m = 0; m < gm.Mw; ++m) {
-        float v = 0.f;
-        for (int s = 0; s < gm.splits; ++s) v += part[((size_t)s * e->cap + b) * gm.Mw + m];
-        out_host[(size_t)b * gm.Mw + m] = v;
-      }
   } catch (const std::exception& ex) {
     return fail(e, ex);
   }
@@ -1737,6 +1821,51 @@ int ls_gemm_splits(ls_engine* e, int which, int* splits, int* rows, int* k) {
   if (splits) *splits = g[which]->splits;
   if (rows) *rows = g[which]->Mw;
   if (k) *k = g[which]->K;
+  return LS_OK;
+}
+
+int ls_time_core_gemms(ls_engine* e, int n, int iters, double* avg_launch_ms, double* bytes_per_launch) {
+  if (!e || !avg_launch_ms || !bytes_per_launch || n < 1 || iters < 1) return LS_EINVAL;
+  try {
+    REQUIRE(e->finalized, LS_EINVAL, "engine not finalized");
+    REQUIRE(n <= e->cap, LS_ECAPACITY, "too many lanes");
+    double bytes = 0.0;
+    int launches = 0;
+    auto sweep = [&](bool count) {
+      for (LayerW& w : e->core.layers) {
+        const Gemm* g[] = {&w.g_qkv, &w.g_o, &w.g_gu, &w.g_down};
+        XBuf* x[] = {&e->x_h, &e->x_attn, &e->x_h, &e->x_act};
+        for (int i = 0; i < 4; ++i) {
+          if (i == 2) {
+            GemmEpi eg{};
+            eg.x_act = e->x_act.ptr;
+            eg.I = e->I;
+            gemm(*e, *g[i], *x[i], eg, kEpiSwiGLU, n);
+          } else {
+            gemm_store(*e, *g[i], *x[i], e->part, n);
+          }
+          if (count) {
+            // weights + (hi, lo) activation rows read + outputs written
+            const double out_b = i == 2 ? 2.0 * 2 * n * (g[i]->Mw / 2) : 4.0 * n * g[i]->Mw;
+            bytes += 2.0 * g[i]->Mw * g[i]->K + 2.0 * 2 * n * g[i]->K + out_b;
+            launches++;
+          }
+        }
+      }
+    };
+    sweep(false);
+    CK(cudaEventRecord(e->ev0, e->stream));
+    for (int it = 0; it < iters; ++it) sweep(it == 0);
+    CK(cudaEventRecord(e->ev1, e->stream));
+    CK(cudaEventSynchronize(e->ev1));
+    check_device(*e);
+    float ms = 0.f;
+    CK(cudaEventElapsedTime(&ms, e->ev0, e->ev1));
+    *avg_launch_ms = ms / (iters * launches);
+    *bytes_per_launch = bytes / launches;
+  } catch (const std::exception& ex) {
+    return fail(e, ex);
+  }
   return LS_OK;
 }
 

@@ -11,7 +11,8 @@
 
 namespace ls {
 
-// Lane metadata: int32 [kMetaFields][cap], field-major.
+// Lane metadata: int32 [cap][kMetaFields], lane-major (one 32-byte record per
+// lane, so a role call uploads only its own lanes).
 enum MetaField : int {
   kMetaToken = 0,
   kMetaPos = 1,       // sequence position of the lane's input token
@@ -27,7 +28,7 @@ enum MetaField : int {
 struct Meta {
   const int* p;
   int cap;
-  __device__ __forceinline__ int get(int f, int b) const { return p[f * cap + b]; }
+  __device__ __forceinline__ int get(int f, int b) const { return p[b * kMetaFields + f]; }
 };
 
 // ----------------------------------------------------------- mapping update
@@ -58,9 +59,41 @@ __global__ void map_update_kernel(Meta meta, int B, int* __restrict__ map, int m
   if (threadIdx.x == 0) dst[pos] = meta.get(kMetaSlot, b);
 }
 
+// ------------------------------------------------------------- row helpers
+// The per-lane row kernels give each thread NV float4 columns and issue every
+// global load before the first use, so a row costs one memory round trip per
+// dependent phase rather than one per element.
+__device__ __forceinline__ float4 ld_f4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+
+__device__ __forceinline__ float4 ld_bf4(const __nv_bfloat16* p) {
+  const uint2 u = *reinterpret_cast<const uint2*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+  const float2 a = __bfloat1622float2(h[0]), b = __bfloat1622float2(h[1]);
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+
+__device__ __forceinline__ float4 f4_scale(float4 v, float s, float4 w) {
+  return make_float4(v.x * s * w.x, v.y * s * w.y, v.z * s * w.z, v.w * s * w.w);
+}
+
+__device__ __forceinline__ float f4_sq(float4 v) { return v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w; }
+
+// (hi, lo) pair rows for 4 consecutive columns starting at i (i % 4 == 0).
+__device__ __forceinline__ void store_pair4(__nv_bfloat16* x, long K, int b, long i, float4 v) {
+  const float f[4] = {v.x, v.y, v.z, v.w};
+  __nv_bfloat16 hi[4], lo[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    hi[k] = f2bf(f[k]);
+    lo[k] = f2bf(f[k] - bf2f(hi[k]));
+  }
+  *reinterpret_cast<uint2*>(x + (2L * b) * K + i) = *reinterpret_cast<uint2*>(hi);
+  *reinterpret_cast<uint2*>(x + (2L * b + 1) * K + i) = *reinterpret_cast<uint2*>(lo);
+}
+
 // ------------------------------------------------------------- input prep
 // h[b] = source row (embedding * scale, or state bank row); optional bank
-// write; x[b] = bf16(norm ? rms(h) * w : h).
+// write; x[b] = (hi, lo) of (norm ? rms(h) * w : h).
 struct PrepArgs {
   Meta meta;
   int B, H;
@@ -77,13 +110,13 @@ struct PrepArgs {
   int* err;
 };
 
+template <int NV>
 __global__ void prep_kernel(PrepArgs a) {
   pdl_wait();
   pdl_launch_dependents();
-  extern __shared__ float row[];
   __shared__ float red[32];
   const int b = blockIdx.x;
-  const int H = a.H;
+  const int H = a.H, H4 = H / 4;
   int src;
   if (a.embed) {
     src = a.meta.get(kMetaToken, b);
@@ -93,32 +126,39 @@ __global__ void prep_kernel(PrepArgs a) {
     if (src < 0 || src >= a.bank_rows) src = -1;
   }
   if (src < 0 && threadIdx.x == 0) atomicExch(a.err, kDevBadIndex);
+  float4 v[NV], w[NV];
   float ss = 0.f;
-  for (int i = threadIdx.x; i < H; i += blockDim.x) {
-    float v = 0.f;
-    if (src >= 0) v = a.embed ? bf2f(a.embed[(long)src * H + i]) * a.embed_scale
-                              : a.bank_in[(long)src * H + i];
-    row[i] = v;
-    ss += v * v;
-    a.h[(long)b * H + i] = v;
-  }
-  if (a.bank_out) {
-    const int so = a.meta.get(kMetaStateOut, b);
-    if (so >= 0 && so < a.bank_rows)
-      for (int i = threadIdx.x; i < H; i += blockDim.x) a.bank_out[(long)so * H + i] = row[i];
-  }
-  if (a.x) {
-    float inv = 1.f;
-    if (a.x_norm_w) inv = rsqrtf(block_sum(ss, red) / H + a.eps);
-    for (int i = threadIdx.x; i < H; i += blockDim.x) {
-      float v = row[i];
-      if (a.x_norm_w) v = v * inv * bf2f(a.x_norm_w[i]);
-      store_pair(a.x, H, b, i, v);
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int j = threadIdx.x + k * blockDim.x;
+    v[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    w[k] = make_float4(1.f, 1.f, 1.f, 1.f);
+    if (j < H4 && src >= 0) {
+      if (a.embed) {
+        const float4 e = ld_bf4(a.embed + (long)src * H + 4 * j);
+        v[k] = make_float4(e.x * a.embed_scale, e.y * a.embed_scale, e.z * a.embed_scale,
+                           e.w * a.embed_scale);
+      } else {
+        v[k] = ld_f4(a.bank_in + (long)src * H + 4 * j);
+      }
     }
+    if (j < H4 && a.x_norm_w) w[k] = ld_bf4(a.x_norm_w + 4 * j);
+    ss += f4_sq(v[k]);
+  }
+  const int so = a.bank_out ? a.meta.get(kMetaStateOut, b) : -1;
+  float inv = 1.f;
+  if (a.x && a.x_norm_w) inv = rsqrtf(block_sum(ss, red) / H + a.eps);
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int j = threadIdx.x + k * blockDim.x;
+    if (j >= H4) continue;
+    *reinterpret_cast<float4*>(a.h + (long)b * H + 4 * j) = v[k];
+    if (so >= 0 && so < a.bank_rows) *reinterpret_cast<float4*>(a.bank_out + (long)so * H + 4 * j) = v[k];
+    if (a.x) store_pair4(a.x, H, b, 4 * j, a.x_norm_w ? f4_scale(v[k], inv, w[k]) : v[k]);
   }
 }
 
-// Raven recurrent input: x[b] = [bf16(bank_h[state_in]), bf16(bank_inj[state_in])].
+// Raven recurrent input: x[b] = (hi, lo) of [bank_h[state_in], bank_inj[state_in]].
 __global__ void cat_state_kernel(Meta meta, int H, const float* __restrict__ bank_h,
                                  const float* __restrict__ bank_inj, int bank_rows,
                                  __nv_bfloat16* __restrict__ x, int* err) {
@@ -130,23 +170,23 @@ __global__ void cat_state_kernel(Meta meta, int H, const float* __restrict__ ban
     if (threadIdx.x == 0) atomicExch(err, kDevBadIndex);
     return;
   }
-  for (int i = threadIdx.x; i < H; i += blockDim.x) {
-    store_pair(x, 2L * H, b, i, bank_h[(long)si * H + i]);
-    store_pair(x, 2L * H, b, H + i, bank_inj[(long)si * H + i]);
+  for (int j = threadIdx.x; j < H / 4; j += blockDim.x) {
+    const float4 h = ld_f4(bank_h + (long)si * H + 4 * j);
+    const float4 g = ld_f4(bank_inj + (long)si * H + 4 * j);
+    store_pair4(x, 2L * H, b, 4 * j, h);
+    store_pair4(x, 2L * H, b, H + 4 * j, g);
   }
 }
 
 // ------------------------------------------------------- residual epilogue
-// a = sum_s part[s][b] (+ bias); a = a_norm ? rms(a) * wa : a;
+// a = y[b] (+ bias); a = a_norm ? rms(a) * wa : a;
 // out = (resid ? resid : 0) + a; out = final_norm ? rms(out) * wf : out;
 // out_h[b] = out; bank[state_out] = out (optional);
-// x[b] = bf16(x_norm ? rms(out) * wx : out) (optional).
+// x[b] = (hi, lo) of (x_norm ? rms(out) * wx : out) (optional).
 struct ResidArgs {
   Meta meta;
   int H;
-  const float* part;
-  int splits;
-  long split_stride;
+  const float* part;           // GEMM output y [cap][H]
   const __nv_bfloat16* bias;
   const __nv_bfloat16* a_norm_w;
   const float* resid;
@@ -160,79 +200,64 @@ struct ResidArgs {
   int* err;
 };
 
+template <int NV>
 __global__ void resid_epi_kernel(ResidArgs a) {
   pdl_wait();
   pdl_launch_dependents();
-  extern __shared__ float row[];
   __shared__ float red[32];
   const int b = blockIdx.x;
-  const int H = a.H;
-  const float* pb = a.part + (long)b * H;
+  const int H = a.H, H4 = H / 4;
+  const float4 z = make_float4(0.f, 0.f, 0.f, 0.f), one = make_float4(1.f, 1.f, 1.f, 1.f);
+  float4 v[NV], rr[NV], wa[NV], wf[NV], wx[NV];
   float ss = 0.f;
-  for (int i = threadIdx.x; i < H; i += blockDim.x) {
-    float v = pb[i];
-    for (int s = 1; s < a.splits; ++s) v += pb[(long)s * a.split_stride + i];
-    if (a.bias) v += bf2f(a.bias[i]);
-    row[i] = v;
-    ss += v * v;
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int j = threadIdx.x + k * blockDim.x;
+    const bool on = j < H4;
+    v[k] = on ? ld_f4(a.part + (long)b * H + 4 * j) : z;
+    rr[k] = on && a.resid ? ld_f4(a.resid + (long)b * H + 4 * j) : z;
+    wa[k] = on && a.a_norm_w ? ld_bf4(a.a_norm_w + 4 * j) : one;
+    wf[k] = on && a.final_norm_w ? ld_bf4(a.final_norm_w + 4 * j) : one;
+    wx[k] = on && a.x_norm_w ? ld_bf4(a.x_norm_w + 4 * j) : one;
+    if (on && a.bias) {
+      const float4 bb = ld_bf4(a.bias + 4 * j);
+      v[k] = make_float4(v[k].x + bb.x, v[k].y + bb.y, v[k].z + bb.z, v[k].w + bb.w);
+    }
+    ss += f4_sq(v[k]);
   }
+  const int so = a.bank ? a.meta.get(kMetaStateOut, b) : -1;
   if (a.a_norm_w) {
     const float inv = rsqrtf(block_sum(ss, red) / H + a.eps);
-    for (int i = threadIdx.x; i < H; i += blockDim.x) row[i] = row[i] * inv * bf2f(a.a_norm_w[i]);
+#pragma unroll
+    for (int k = 0; k < NV; ++k) v[k] = f4_scale(v[k], inv, wa[k]);
   }
   ss = 0.f;
-  for (int i = threadIdx.x; i < H; i += blockDim.x) {
-    float v = row[i];
-    if (a.resid) v += a.resid[(long)b * H + i];
-    row[i] = v;
-    ss += v * v;
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    v[k] = make_float4(v[k].x + rr[k].x, v[k].y + rr[k].y, v[k].z + rr[k].z, v[k].w + rr[k].w);
+    ss += f4_sq(v[k]);
   }
   if (a.final_norm_w) {
     const float inv = rsqrtf(block_sum(ss, red) / H + a.eps);
     ss = 0.f;
-    for (int i = threadIdx.x; i < H; i += blockDim.x) {
-      const float v = row[i] * inv * bf2f(a.final_norm_w[i]);
-      row[i] = v;
-      ss += v * v;
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      v[k] = f4_scale(v[k], inv, wf[k]);
+      ss += f4_sq(v[k]);
     }
   }
-  for (int i = threadIdx.x; i < H; i += blockDim.x) a.out_h[(long)b * H + i] = row[i];
-  if (a.bank) {
-    const int so = a.meta.get(kMetaStateOut, b);
-    if (so >= 0 && so < a.bank_rows) {
-      for (int i = threadIdx.x; i < H; i += blockDim.x) a.bank[(long)so * H + i] = row[i];
-    } else if (threadIdx.x == 0) {
-      atomicExch(a.err, kDevBadIndex);
-    }
+  float inv = 1.f;
+  if (a.x && a.x_norm_w) inv = rsqrtf(block_sum(ss, red) / H + a.eps);
+  if (a.bank && (so < 0 || so >= a.bank_rows) && threadIdx.x == 0) atomicExch(a.err, kDevBadIndex);
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int j = threadIdx.x + k * blockDim.x;
+    if (j >= H4) continue;
+    *reinterpret_cast<float4*>(a.out_h + (long)b * H + 4 * j) = v[k];
+    if (a.bank && so >= 0 && so < a.bank_rows)
+      *reinterpret_cast<float4*>(a.bank + (long)so * H + 4 * j) = v[k];
+    if (a.x) store_pair4(a.x, H, b, 4 * j, a.x_norm_w ? f4_scale(v[k], inv, wx[k]) : v[k]);
   }
-  if (a.x) {
-    float inv = 1.f;
-    if (a.x_norm_w) inv = rsqrtf(block_sum(ss, red) / H + a.eps);
-    for (int i = threadIdx.x; i < H; i += blockDim.x) {
-      float v = row[i];
-      if (a.x_norm_w) v = v * inv * bf2f(a.x_norm_w[i]);
-      store_pair(a.x, H, b, i, v);
-    }
-  }
-}
-
-// ------------------------------------------------------------ SwiGLU epilogue
-// x[b][i] = bf16(silu(g) * u), g/u = split-summed halves of the gate_up output.
-__global__ void act_epi_kernel(const float* __restrict__ part, int splits, long split_stride,
-                               int I, __nv_bfloat16* __restrict__ x) {
-  pdl_wait();
-  pdl_launch_dependents();
-  const int b = blockIdx.y;
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= I) return;
-  const float* pb = part + (long)b * 2 * I;
-  float g = pb[i], u = pb[I + i];
-  for (int s = 1; s < splits; ++s) {
-    g += pb[(long)s * split_stride + i];
-    u += pb[(long)s * split_stride + I + i];
-  }
-  const float sg = g / (1.f + expf(-g));
-  store_pair(x, I, b, i, sg * u);
 }
 
 // ------------------------------------------------------------- QKV epilogue
@@ -314,15 +339,18 @@ __global__ void qkv_epi_kernel(QkvArgs a) {
 // timeline is its mapping row: position j of the timeline lives in KV slot
 // map[row][j], so forked branches read their shared prefix through the same
 // slots as their parent. A group of G = nh/nkv query heads shares each K/V
-// row. Sub-groups of HD/8 lanes each own one position at a time and load its
-// K and V rows with 16-byte vector loads; scores are reduced with warp
-// shuffles and accumulated with an online softmax. Chunk boundaries are fixed
-// multiples of kAttnChunk and positions map to warps by index, so results do
-// not depend on the batch. Output: unnormalised partial (acc, max, sum) per
-// chunk, merged by attn_combine_kernel in chunk order.
+// row. The CTA first stages the chunk's slot ids in shared memory, then each
+// sub-group of HD/8 lanes owns a fixed set of positions and issues all of its
+// 16-byte K loads (then V loads) at once; scores are reduced with warp
+// shuffles. Chunk boundaries are fixed multiples of kAttnChunk and positions
+// map to sub-groups by index, so results do not depend on the batch.
+// Each CTA writes its unnormalised (acc, max, sum) partial; the last CTA of a
+// (lane, kv head) to finish (counted with an atomic ticket, then reset) merges
+// all chunks in chunk order and writes the attention output as the O GEMM's
+// bf16 (hi, lo) input.
 constexpr int kAttnChunk = 256;
-constexpr int kAttnThreads = 128;
-constexpr int kAttnUnroll = 4;
+constexpr int kAttnThreads = 256;
+constexpr int kAttnMaxChunks = 32;   // max_context <= 8192
 
 struct AttnArgs {
   Meta meta;
@@ -336,6 +364,8 @@ struct AttnArgs {
   int max_chunks;
   float* o_part;                   // [cap][nh][max_chunks][HD]
   float* ml_part;                  // [cap][nh][max_chunks][2]
+  int* tickets;                    // [cap][nkv], zero between calls
+  __nv_bfloat16* x;                // (hi, lo) rows [2*cap][nh*HD]
   float scale;
   int* err;
 };
@@ -344,89 +374,111 @@ template <int HD, int G>
 __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnArgs a) {
   pdl_wait();
   pdl_launch_dependents();
-  constexpr int LPP = HD / 8;          // lanes per position
-  constexpr int PPW = 32 / LPP;        // positions per warp step
+  constexpr int LPP = HD / 8;              // lanes per position (16 B each)
+  constexpr int PPW = 32 / LPP;            // positions per warp at a time
   constexpr int NW = kAttnThreads / 32;
-  constexpr int STEP = NW * PPW;
+  constexpr int NSG = NW * PPW;            // sub-groups per CTA
+  constexpr int PER = kAttnChunk / NSG;    // positions per sub-group
   const int b = blockIdx.x, g = blockIdx.y, c = blockIdx.z;
   const int T = a.meta.get(kMetaPos, b) + 1;
   const int start = c * kAttnChunk;
   if (start >= T) return;
-  const int end = min(start + kAttnChunk, T);
+  const int n_in = min(kAttnChunk, T - start);
   const int row = a.meta.get(kMetaRow, b);
   if (row < 0 || row >= a.rows || T > a.max_ctx) {
     if (threadIdx.x == 0) atomicExch(a.err, kDevBadIndex);
     return;
   }
+  __shared__ int s_slot[kAttnChunk];
+  __shared__ float sm_m[NW][G], sm_l[NW][G];
+  __shared__ float sm_acc[NW][G][HD];
+  __shared__ int s_last;
+  const int* mrow = a.map + (long)row * a.max_ctx + start;
+  for (int i = threadIdx.x; i < kAttnChunk; i += blockDim.x) {
+    int s = -1;
+    if (i < n_in) {
+      s = mrow[i];
+      if (s < 0 || s >= a.n_slots) {
+        atomicExch(a.err, kDevBadIndex);
+        s = -1;
+      }
+    }
+    s_slot[i] = s;
+  }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int sub = lane / LPP, sl = lane % LPP;
+  const int sg = warp * PPW + sub;
   const int kd = a.nkv * HD;
-  const int* mrow = a.map + (long)row * a.max_ctx;
 
   float qv[G][8];
 #pragma unroll
   for (int h = 0; h < G; ++h) {
     const float* qp = a.q + (long)b * a.nh * HD + (g * G + h) * HD + sl * 8;
+    const float4 q0 = ld_f4(qp), q1 = ld_f4(qp + 4);
+    const float qq[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
 #pragma unroll
-    for (int d = 0; d < 8; ++d) qv[h][d] = qp[d] * a.scale;
+    for (int d = 0; d < 8; ++d) qv[h][d] = qq[d] * a.scale;
+  }
+  __syncthreads();
+
+  // scores for this sub-group's PER positions (p = sg + t * NSG)
+  float sc[G][PER];
+  {
+    uint4 kr[PER];
+#pragma unroll
+    for (int t = 0; t < PER; ++t) {
+      const int slot = s_slot[sg + t * NSG];
+      kr[t] = slot >= 0 ? *reinterpret_cast<const uint4*>(a.kpool + (long)slot * kd + g * HD + sl * 8)
+                        : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int t = 0; t < PER; ++t) {
+      float kf[8];
+      unpack8(kr[t], kf);
+#pragma unroll
+      for (int h = 0; h < G; ++h) {
+        float s = 0.f;
+#pragma unroll
+        for (int d = 0; d < 8; ++d) s += qv[h][d] * kf[d];
+#pragma unroll
+        for (int o = LPP / 2; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        sc[h][t] = s_slot[sg + t * NSG] >= 0 ? s : -INFINITY;
+      }
+    }
   }
   float m[G], l[G], acc[G][8];
 #pragma unroll
   for (int h = 0; h < G; ++h) {
     m[h] = -INFINITY;
+#pragma unroll
+    for (int t = 0; t < PER; ++t) m[h] = fmaxf(m[h], sc[h][t]);
     l[h] = 0.f;
 #pragma unroll
     for (int d = 0; d < 8; ++d) acc[h][d] = 0.f;
   }
-
-  // The loop bound is warp-uniform (jb is the same for every lane of a warp),
-  // so all 32 lanes reach every shuffle below; out-of-range positions are
-  // masked through `valid`.
-  for (int jb = start + warp * PPW; jb < end; jb += STEP * kAttnUnroll) {
-    uint4 kr[kAttnUnroll], vr[kAttnUnroll];
-    bool valid[kAttnUnroll];
+  {
+    uint4 vr[PER];
 #pragma unroll
-    for (int u = 0; u < kAttnUnroll; ++u) {
-      const int j = jb + sub + u * STEP;
-      int slot = j < end ? mrow[j] : -1;
-      valid[u] = slot >= 0 && slot < a.n_slots;
-      if (j < end && !valid[u]) atomicExch(a.err, kDevBadIndex);
-      if (valid[u]) {
-        const long off = (long)slot * kd + g * HD + sl * 8;
-        kr[u] = *reinterpret_cast<const uint4*>(a.kpool + off);
-        vr[u] = *reinterpret_cast<const uint4*>(a.vpool + off);
-      }
+    for (int t = 0; t < PER; ++t) {
+      const int slot = s_slot[sg + t * NSG];
+      vr[t] = slot >= 0 ? *reinterpret_cast<const uint4*>(a.vpool + (long)slot * kd + g * HD + sl * 8)
+                        : make_uint4(0, 0, 0, 0);
     }
 #pragma unroll
-    for (int u = 0; u < kAttnUnroll; ++u) {
-      float kf[8], vf[8];
-      if (valid[u]) {
-        unpack8(kr[u], kf);
-        unpack8(vr[u], vf);
-      }
+    for (int t = 0; t < PER; ++t) {
+      float vf[8];
+      unpack8(vr[t], vf);
 #pragma unroll
       for (int h = 0; h < G; ++h) {
-        float s = 0.f;
+        const float p = m[h] == -INFINITY ? 0.f : __expf(sc[h][t] - m[h]);
+        l[h] += p;
 #pragma unroll
-        for (int d = 0; d < 8; ++d) s += qv[h][d] * (valid[u] ? kf[d] : 0.f);
-#pragma unroll
-        for (int o = LPP / 2; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-        if (valid[u]) {
-          const float mn = fmaxf(m[h], s);
-          const float corr = __expf(m[h] - mn);
-          const float p = __expf(s - mn);
-          l[h] = l[h] * corr + p;
-#pragma unroll
-          for (int d = 0; d < 8; ++d) acc[h][d] = acc[h][d] * corr + p * vf[d];
-          m[h] = mn;
-        }
+        for (int d = 0; d < 8; ++d) acc[h][d] += p * vf[d];
       }
     }
   }
 
-  // Merge sub-groups within the warp, then warps through shared memory.
-  __shared__ float sm_m[NW][G], sm_l[NW][G];
-  __shared__ float sm_acc[NW][G][HD];
+  // merge sub-groups within the warp, then warps through shared memory
 #pragma unroll
   for (int h = 0; h < G; ++h) {
 #pragma unroll
@@ -473,30 +525,48 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnArgs a) {
       a.ml_part[idx * 2 + 1] = ll;
     }
   }
-}
 
-// x[b][h*HD + d] = bf16(sum_c acc_c e^(m_c - M) / sum_c l_c e^(m_c - M)), chunks in order.
-__global__ void attn_combine_kernel(Meta meta, int nh, int hd, int max_chunks,
-                                    const float* __restrict__ o_part,
-                                    const float* __restrict__ ml_part,
-                                    __nv_bfloat16* __restrict__ x) {
-  pdl_wait();
-  pdl_launch_dependents();
-  const int b = blockIdx.x, h = blockIdx.y;
-  const int T = meta.get(kMetaPos, b) + 1;
-  int nch = (T + kAttnChunk - 1) / kAttnChunk;
-  if (nch > max_chunks) nch = max_chunks;
-  const long base = ((long)b * nh + h) * max_chunks;
-  float mm = -INFINITY;
-  for (int c = 0; c < nch; ++c) mm = fmaxf(mm, ml_part[(base + c) * 2]);
-  for (int d = threadIdx.x; d < hd; d += blockDim.x) {
-    float ll = 0.f, aa = 0.f;
-    for (int c = 0; c < nch; ++c) {
-      const float w = mm == -INFINITY ? 0.f : __expf(ml_part[(base + c) * 2] - mm);
-      ll += ml_part[(base + c) * 2 + 1] * w;
-      aa += o_part[(base + c) * hd + d] * w;
+  // last CTA of this (lane, kv head) merges the chunks in order
+  const int nch = min((T + kAttnChunk - 1) / kAttnChunk, a.max_chunks);
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int* tk = a.tickets + (long)b * a.nkv + g;
+    const int ticket = atomicAdd(tk, 1);
+    s_last = ticket == nch - 1;
+    if (s_last) *tk = 0;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  // Loads of all chunks are issued before use (L2, not L1: other CTAs wrote them).
+  for (int t = threadIdx.x; t < G * HD; t += blockDim.x) {
+    const int h = t / HD, d = t - h * HD;
+    const long base = ((long)b * a.nh + g * G + h) * a.max_chunks;
+    float cm[kAttnMaxChunks], cl[kAttnMaxChunks], co[kAttnMaxChunks];
+#pragma unroll
+    for (int cc = 0; cc < kAttnMaxChunks; ++cc) {
+      if (cc < nch) {
+        const float2 ml = __ldcg(reinterpret_cast<const float2*>(a.ml_part + (base + cc) * 2));
+        cm[cc] = ml.x;
+        cl[cc] = ml.y;
+        co[cc] = __ldcg(a.o_part + (base + cc) * HD + d);
+      }
     }
-    store_pair(x, (long)nh * hd, b, h * hd + d, ll > 0.f ? aa / ll : 0.f);
+    float mm = -INFINITY;
+#pragma unroll
+    for (int cc = 0; cc < kAttnMaxChunks; ++cc)
+      if (cc < nch) mm = fmaxf(mm, cm[cc]);
+    float ll = 0.f, aa = 0.f;
+#pragma unroll
+    for (int cc = 0; cc < kAttnMaxChunks; ++cc) {
+      if (cc < nch) {
+        const float w = mm == -INFINITY ? 0.f : __expf(cm[cc] - mm);
+        ll += cl[cc] * w;
+        aa += co[cc] * w;
+      }
+    }
+    store_pair(a.x, (long)a.nh * HD, b, (g * G + h) * HD + d, ll > 0.f ? aa / ll : 0.f);
   }
 }
 

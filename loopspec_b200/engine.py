@@ -121,6 +121,13 @@ class Engine:
         _lib.check(self.L.ls_time_gemm(self.h, w, n_lanes, iters, ctypes.byref(ms)), self.h)
         return ms.value
 
+    def time_core_gemms(self, n_lanes, iters=5):
+        """(average ms per GEMM launch, algorithmic bytes per launch) over a core-weight sweep."""
+        ms, by = ctypes.c_double(), ctypes.c_double()
+        _lib.check(self.L.ls_time_core_gemms(self.h, n_lanes, iters, ctypes.byref(ms),
+                                             ctypes.byref(by)), self.h)
+        return ms.value, by.value
+
     def kernel_count(self, role, n_lanes):
         c = ctypes.c_int32()
         r = {"pre": 0, "core": 1, "post": 2}[role]

@@ -111,7 +111,10 @@ class Timeline:
 class OracleModel:
     """Role forward math for one lane. `cfg` is a plain dict of config fields."""
 
-    def __init__(self, cfg, weights):
+    def __init__(self, cfg, weights, *, kv_bf16=False):
+        """kv_bf16: store K/V in bf16 like the reference's KV pool (SGLang keeps
+        the cache in the model dtype); all arithmetic stays fp32."""
+        self.kv_bf16 = kv_bf16
         self.cfg = cfg
         self.w = {k: v.detach().to(torch.float32).cpu() for k, v in weights.items()}
         self.family = cfg["family"]
@@ -137,6 +140,10 @@ class OracleModel:
         q = rope_neox(q.view(nh, hd), pos, self.theta)
         k = rope_neox(k.view(nkv, hd), pos, self.theta)
         v = v.view(nkv, hd)
+        if self.kv_bf16:
+            # the reference's KV pool stores K (after RoPE) and V in the model dtype
+            k = k.to(torch.bfloat16).to(torch.float32)
+            v = v.to(torch.bfloat16).to(torch.float32)
         if len(tl.k[layer]) != pos:
             raise RuntimeError(f"timeline length {len(tl.k[layer])} != position {pos}")
         tl.k[layer].append(k)
