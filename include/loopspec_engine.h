@@ -172,6 +172,26 @@ int ls_gemm_splits(ls_engine* eng, int which, int* splits, int* rows, int* k);
  * [attn_layers][kv_slots][n_kv_heads*head_dim] bf16), for tests. */
 int ls_debug_kv(ls_engine* eng, void** k_pool, void** v_pool, int* kv_slots, int* attn_layers);
 
+/* Branch-timeline paged decode attention of one layer, standalone (the
+ * engine's attention kernel; replaces SGLang's Triton decode attention as the
+ * reference drives it through req_to_token rows, cuda_graph.py:361-394).
+ * Lane i has one query q[i] (fp32 [n_heads*head_dim], RoPE applied) and
+ * attends to positions 0..lane_lens[i]-1 of mapping row lane_rows[i]:
+ * position j's K/V live in slot map[row*max_context + j] of k_pool / v_pool
+ * (bf16 [n_slots][n_kv_heads*head_dim]). Forked timelines share slots.
+ * out: fp32 [n_lanes][n_heads*head_dim]. All pointers are device memory
+ * (lane_rows / lane_lens int32 [n_lanes]). workspace: device scratch of at
+ * least ls_decode_attention_workspace_bytes() bytes, 256-byte aligned.
+ * Runs on `stream` (cudaStream_t, NULL = legacy default) and waits for it.
+ * Out-of-range rows, lengths or slots are skipped and reported as LS_EDEVICE.
+ * Handle-less: errors are read with ls_last_error(NULL). */
+size_t ls_decode_attention_workspace_bytes(int n_lanes, int n_heads, int n_kv_heads, int head_dim,
+                                           int max_context);
+int ls_decode_attention(const float* q, const void* k_pool, const void* v_pool, const int32_t* map,
+                        const int32_t* lane_rows, const int32_t* lane_lens, int n_lanes, int n_heads,
+                        int n_kv_heads, int head_dim, int n_slots, int n_rows, int max_context,
+                        void* workspace, size_t workspace_bytes, float* out, void* stream);
+
 int ls_destroy(ls_engine* eng);
 const char* ls_last_error(ls_engine* eng);
 const char* ls_version(void);

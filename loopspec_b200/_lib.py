@@ -88,6 +88,9 @@ SIGNATURES = [
     ("ls_gemm_splits", _i32, [_P, _i32, ctypes.POINTER(_i32), ctypes.POINTER(_i32), ctypes.POINTER(_i32)]),
     ("ls_debug_kv", _i32, [_P, ctypes.POINTER(_P), ctypes.POINTER(_P), ctypes.POINTER(_i32),
                            ctypes.POINTER(_i32)]),
+    ("ls_decode_attention_workspace_bytes", ctypes.c_size_t, [_i32, _i32, _i32, _i32, _i32]),
+    ("ls_decode_attention", _i32, [_P, _P, _P, _P, _P, _P, _i32, _i32, _i32, _i32, _i32, _i32,
+                                   _i32, _P, ctypes.c_size_t, _P, _P]),
     ("ls_destroy", _i32, [_P]),
     ("ls_last_error", ctypes.c_char_p, [_P]),
     ("ls_version", ctypes.c_char_p, []),
@@ -120,5 +123,4 @@ class EngineError(RuntimeError):
 
 def check(code, handle=None):
     if code != LS_OK:
-        msg = lib().ls_last_error(handle).decode() if handle else "invalid argument"
-        raise EngineError(code, msg)
+        raise EngineError(code, lib().ls_last_error(handle).decode())

@@ -40,6 +40,9 @@ struct EngineError : std::runtime_error {
   EngineError(int c, const std::string& m) : std::runtime_error(m), code(c) {}
 };
 
+// Error text of the last failed call that has no engine handle.
+thread_local std::string g_last_error;
+
 #define CK(x)                                                                            \
   do {                                                                                   \
     cudaError_t e_ = (x);                                                                \
@@ -734,8 +737,8 @@ int row_threads(int H) { return std::min(1024, H / 4); }
 
 void attention(ls_engine& e, Meta meta, int n, const bf16* kp, const bf16* vp) {
   AttnArgs a{meta, e.NH, e.NKV, e.q, e.map, e.max_ctx, e.rows, kp, vp, e.n_slots,
-             e.max_chunks, e.o_part, e.ml_part, e.attn_tickets, e.x_attn.ptr,
-             1.0f / std::sqrt((float)e.HD), e.err_dev};
+             e.max_chunks, e.o_part, e.ml_part, e.attn_tickets, e.x_attn.ptr, nullptr,
+             nullptr, nullptr, 1.0f / std::sqrt((float)e.HD), e.err_dev};
   const dim3 grid(n, e.NKV, e.max_chunks), blk(kAttnThreads);
   const int G = e.NH / e.NKV;
   if (e.HD == 128 && G == 1) klaunch(e, attn_kernel<128, 1>, grid, blk, 0, a);
@@ -1478,7 +1481,84 @@ SchedHooks engine_hooks(ls_engine& e, long long stop_token) {
 int fail(ls_engine* e, const std::exception& ex) {
   const EngineError* ee = dynamic_cast<const EngineError*>(&ex);
   if (e) e->last_error = ex.what();
+  else g_last_error = ex.what();
   return ee ? ee->code : LS_EINVAL;
+}
+
+}  // namespace
+
+// ================================================ standalone decode attention
+namespace {
+
+int fail_global(const std::exception& ex) {
+  const EngineError* ee = dynamic_cast<const EngineError*>(&ex);
+  g_last_error = ex.what();
+  return ee ? ee->code : LS_EINVAL;
+}
+
+// Scratch of one decode-attention call, carved from a byte buffer: an error
+// word, the per-chunk partials (acc, then max/sum) and the arrival tickets.
+struct AttnScratch {
+  int* err;
+  float* o_part;
+  float* ml_part;
+  int* tickets;
+  size_t ticket_bytes;
+  size_t total;
+};
+
+AttnScratch carve_attn_scratch(char* base, int n, int nh, int nkv, int hd, int max_chunks) {
+  AttnScratch s{};
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    char* p = base ? base + off : nullptr;
+    off += (bytes + 255) / 256 * 256;
+    return p;
+  };
+  s.err = reinterpret_cast<int*>(take(sizeof(int)));
+  s.o_part = reinterpret_cast<float*>(take(sizeof(float) * (size_t)n * nh * max_chunks * hd));
+  s.ml_part = reinterpret_cast<float*>(take(sizeof(float) * (size_t)n * nh * max_chunks * 2));
+  s.ticket_bytes = sizeof(int) * (size_t)n * nkv;
+  s.tickets = reinterpret_cast<int*>(take(s.ticket_bytes));
+  s.total = off;
+  return s;
+}
+
+void check_attn_shape(int n, int nh, int nkv, int hd, int n_slots, int n_rows, int max_ctx) {
+  REQUIRE(n >= 1 && nh >= 1 && nkv >= 1 && n_slots >= 1 && n_rows >= 1, LS_EINVAL,
+          "decode attention: sizes must be positive");
+  REQUIRE(nh % nkv == 0, LS_EINVAL, "decode attention: n_heads must be a multiple of n_kv_heads");
+  const int G = nh / nkv;
+  REQUIRE((hd == 64 && (G == 1 || G == 2 || G == 4)) || (hd == 128 && (G == 1 || G == 2)),
+          LS_EINVAL, "decode attention: unsupported head_dim / GQA group");
+  REQUIRE(max_ctx >= 1 && cdiv(max_ctx, kAttnChunk) <= kAttnMaxChunks, LS_EINVAL,
+          "decode attention: max_context must be in [1, 8192]");
+}
+
+// Launch one decode-attention call on `stream` using `sc` as scratch, wait
+// for it, and report a device-side index error as LS_EDEVICE.
+void run_decode_attention(const float* q, const void* k_pool, const void* v_pool, const int32_t* map,
+                          const int32_t* lane_rows, const int32_t* lane_lens, int n, int nh, int nkv,
+                          int hd, int n_slots, int n_rows, int max_ctx, const AttnScratch& sc,
+                          float* out, cudaStream_t stream) {
+  const int max_chunks = cdiv(max_ctx, kAttnChunk);
+  CK(cudaMemsetAsync(sc.err, 0, sizeof(int), stream));
+  CK(cudaMemsetAsync(sc.tickets, 0, sc.ticket_bytes, stream));   // tickets start at zero
+  AttnArgs a{Meta{nullptr, 0}, nh, nkv, q, map, max_ctx, n_rows,
+             static_cast<const bf16*>(k_pool), static_cast<const bf16*>(v_pool), n_slots,
+             max_chunks, sc.o_part, sc.ml_part, sc.tickets, nullptr, out, lane_lens, lane_rows,
+             1.0f / std::sqrt((float)hd), sc.err};
+  const dim3 grid(n, nkv, max_chunks), blk(kAttnThreads);
+  const int G = nh / nkv;
+  if (hd == 128 && G == 1) launch(attn_kernel<128, 1>, grid, blk, 0, stream, false, a);
+  else if (hd == 128 && G == 2) launch(attn_kernel<128, 2>, grid, blk, 0, stream, false, a);
+  else if (hd == 64 && G == 1) launch(attn_kernel<64, 1>, grid, blk, 0, stream, false, a);
+  else if (hd == 64 && G == 2) launch(attn_kernel<64, 2>, grid, blk, 0, stream, false, a);
+  else launch(attn_kernel<64, 4>, grid, blk, 0, stream, false, a);
+  int err = 0;
+  CK(cudaMemcpyAsync(&err, sc.err, sizeof(int), cudaMemcpyDeviceToHost, stream));
+  CK(cudaStreamSynchronize(stream));
+  REQUIRE(err == kDevOk, LS_EDEVICE, "decode attention: a lane row, length or KV slot was out of range");
 }
 
 }  // namespace
@@ -1486,9 +1566,42 @@ int fail(ls_engine* e, const std::exception& ex) {
 // ======================================================================== C ABI
 extern "C" {
 
+size_t ls_decode_attention_workspace_bytes(int n_lanes, int n_heads, int n_kv_heads, int head_dim,
+                                           int max_context) {
+  if (n_lanes < 1 || n_heads < 1 || n_kv_heads < 1 || head_dim < 1 || max_context < 1) return 0;
+  return carve_attn_scratch(nullptr, n_lanes, n_heads, n_kv_heads, head_dim,
+                            cdiv(max_context, kAttnChunk)).total;
+}
+
+int ls_decode_attention(const float* q, const void* k_pool, const void* v_pool, const int32_t* map,
+                        const int32_t* lane_rows, const int32_t* lane_lens, int n_lanes, int n_heads,
+                        int n_kv_heads, int head_dim, int n_slots, int n_rows, int max_context,
+                        void* workspace, size_t workspace_bytes, float* out, void* stream) {
+  if (!q || !k_pool || !v_pool || !map || !lane_rows || !lane_lens || !workspace || !out) {
+    g_last_error = "decode attention: null pointer argument";
+    return LS_EINVAL;
+  }
+  try {
+    check_attn_shape(n_lanes, n_heads, n_kv_heads, head_dim, n_slots, n_rows, max_context);
+    const AttnScratch sc = carve_attn_scratch(static_cast<char*>(workspace), n_lanes, n_heads,
+                                              n_kv_heads, head_dim, cdiv(max_context, kAttnChunk));
+    REQUIRE(workspace_bytes >= sc.total, LS_EINVAL,
+            "decode attention: workspace smaller than ls_decode_attention_workspace_bytes()");
+    REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 255) == 0, LS_EINVAL,
+            "decode attention: workspace must be 256-byte aligned");
+    run_decode_attention(q, k_pool, v_pool, map, lane_rows, lane_lens, n_lanes, n_heads, n_kv_heads,
+                         head_dim, n_slots, n_rows, max_context, sc, out,
+                         static_cast<cudaStream_t>(stream));
+  } catch (const std::exception& ex) {
+    return fail_global(ex);
+  }
+  return LS_OK;
+}
+
+
 const char* ls_version(void) { return "loopspec-b200 0.1.0 (sm_100a)"; }
 
-const char* ls_last_error(ls_engine* e) { return e ? e->last_error.c_str() : "null engine"; }
+const char* ls_last_error(ls_engine* e) { return e ? e->last_error.c_str() : g_last_error.c_str(); }
 
 int ls_create(const ls_model_cfg* model, const ls_sched_cfg* sched, int device, ls_engine** out) {
   if (!model || !sched || !out) return LS_EINVAL;

@@ -365,7 +365,10 @@ struct AttnArgs {
   float* o_part;                   // [cap][nh][max_chunks][HD]
   float* ml_part;                  // [cap][nh][max_chunks][2]
   int* tickets;                    // [cap][nkv], zero between calls
-  __nv_bfloat16* x;                // (hi, lo) rows [2*cap][nh*HD]
+  __nv_bfloat16* x;                // (hi, lo) rows [2*cap][nh*HD], or
+  float* out;                      // ... fp32 rows [cap][nh*HD] when non-null
+  const int* lane_len;             // optional per-lane timeline length (else pos + 1)
+  const int* lane_row;             // optional per-lane mapping row (else metadata)
   float scale;
   int* err;
 };
@@ -380,11 +383,15 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnArgs a) {
   constexpr int NSG = NW * PPW;            // sub-groups per CTA
   constexpr int PER = kAttnChunk / NSG;    // positions per sub-group
   const int b = blockIdx.x, g = blockIdx.y, c = blockIdx.z;
-  const int T = a.meta.get(kMetaPos, b) + 1;
+  const int T = a.lane_len ? a.lane_len[b] : a.meta.get(kMetaPos, b) + 1;
+  if (T < 1 || T > a.max_ctx) {
+    if (threadIdx.x == 0 && c == 0) atomicExch(a.err, kDevBadIndex);
+    return;
+  }
   const int start = c * kAttnChunk;
   if (start >= T) return;
   const int n_in = min(kAttnChunk, T - start);
-  const int row = a.meta.get(kMetaRow, b);
+  const int row = a.lane_row ? a.lane_row[b] : a.meta.get(kMetaRow, b);
   if (row < 0 || row >= a.rows || T > a.max_ctx) {
     if (threadIdx.x == 0) atomicExch(a.err, kDevBadIndex);
     return;
@@ -566,7 +573,9 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnArgs a) {
         aa += co[cc] * w;
       }
     }
-    store_pair(a.x, (long)a.nh * HD, b, (g * G + h) * HD + d, ll > 0.f ? aa / ll : 0.f);
+    const float o = ll > 0.f ? aa / ll : 0.f;
+    if (a.out) a.out[(long)b * a.nh * HD + (g * G + h) * HD + d] = o;
+    else store_pair(a.x, (long)a.nh * HD, b, (g * G + h) * HD + d, o);
   }
 }
 
