@@ -192,6 +192,26 @@ int ls_decode_attention(const float* q, const void* k_pool, const void* v_pool, 
                         int n_kv_heads, int head_dim, int n_slots, int n_rows, int max_context,
                         void* workspace, size_t workspace_bytes, float* out, void* stream);
 
+/* Allocation-free ls_decode_attention (no counterpart in the reference).
+ * For callers that cannot call cudaMalloc (code inside an allocator or
+ * memory-pool hook, runtimes that reserve all device memory up front,
+ * processes that forbid device allocation after start-up). Same arguments
+ * and result as ls_decode_attention minus the workspace: the scratch is a
+ * fixed 4 MiB array inside the library (ls_decode_attention_noalloc_limit()),
+ * held on every GPU that loads the library until exit. Shapes whose scratch
+ * (about n_lanes * n_heads * ceil(max_context/256) * head_dim * 4 bytes)
+ * exceeds it are rejected with LS_ECAPACITY. The first call on a device looks
+ * up the array's device address, so make it before any stream capture. All
+ * calls on a device share the array: the call clears what must start at
+ * zero, later calls overwrite the rest, and calls that overlap on the GPU
+ * race. Calls no cudaMalloc, cudaFree or allocating library routine. */
+int ls_decode_attention_noalloc(const float* q, const void* k_pool, const void* v_pool,
+                                const int32_t* map, const int32_t* lane_rows,
+                                const int32_t* lane_lens, int n_lanes, int n_heads, int n_kv_heads,
+                                int head_dim, int n_slots, int n_rows, int max_context, float* out,
+                                void* stream);
+size_t ls_decode_attention_noalloc_limit(void);
+
 int ls_destroy(ls_engine* eng);
 const char* ls_last_error(ls_engine* eng);
 const char* ls_version(void);

@@ -91,6 +91,9 @@ SIGNATURES = [
     ("ls_decode_attention_workspace_bytes", ctypes.c_size_t, [_i32, _i32, _i32, _i32, _i32]),
     ("ls_decode_attention", _i32, [_P, _P, _P, _P, _P, _P, _i32, _i32, _i32, _i32, _i32, _i32,
                                    _i32, _P, ctypes.c_size_t, _P, _P]),
+    ("ls_decode_attention_noalloc", _i32, [_P, _P, _P, _P, _P, _P, _i32, _i32, _i32, _i32, _i32,
+                                           _i32, _i32, _P, _P]),
+    ("ls_decode_attention_noalloc_limit", ctypes.c_size_t, []),
     ("ls_destroy", _i32, [_P]),
     ("ls_last_error", ctypes.c_char_p, [_P]),
     ("ls_version", ctypes.c_char_p, []),

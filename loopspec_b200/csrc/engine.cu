@@ -23,6 +23,7 @@
 #include <functional>
 #include <map>
 #include <memory>
+#include <mutex>
 #include <queue>
 #include <set>
 #include <stdexcept>
@@ -1561,10 +1562,78 @@ void run_decode_attention(const float* q, const void* k_pool, const void* v_pool
   REQUIRE(err == kDevOk, LS_EDEVICE, "decode attention: a lane row, length or KV slot was out of range");
 }
 
+// ---------------------------------------------- allocation-free variant
+// Some callers cannot call cudaMalloc: code running inside an allocator or
+// memory-pool hook, a runtime whose device memory is fully reserved up front,
+// or a process that forbids device allocation after start-up. For them the
+// decode attention can use this fixed scratch instead of a caller workspace.
+// Every GPU that loads the library holds these bytes until the process exits,
+// and every call on a device shares them: the last call's contents stay there
+// (the call clears its error word and arrival tickets itself), and calls
+// that overlap on the GPU race on it.
+constexpr size_t kNoAllocScratchBytes = 4u << 20;   // 4 MiB
+static __device__ __align__(256) char g_noalloc_scratch[kNoAllocScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mutex;
+char* g_noalloc_ptr[kMaxDevices] = {};
+
+// Device address of the scratch array on the current device. In host code
+// the array's name is only a host-side stand-in, so the real address is
+// looked up once per device (the first call on that device does it, with
+// that device current) and cached.
+char* noalloc_scratch_for_current_device() {
+  int dev = -1;
+  CK(cudaGetDevice(&dev));
+  REQUIRE(dev >= 0 && dev < kMaxDevices, LS_EINVAL, "device ordinal out of range");
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    CK(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+    REQUIRE(p != nullptr, LS_ECUDA, "cudaGetSymbolAddress returned no address");
+    g_noalloc_ptr[dev] = static_cast<char*>(p);
+  }
+  return g_noalloc_ptr[dev];
+}
+
 }  // namespace
 
 // ======================================================================== C ABI
 extern "C" {
+
+int ls_decode_attention_noalloc(const float* q, const void* k_pool, const void* v_pool,
+                                const int32_t* map, const int32_t* lane_rows,
+                                const int32_t* lane_lens, int n_lanes, int n_heads, int n_kv_heads,
+                                int head_dim, int n_slots, int n_rows, int max_context, float* out,
+                                void* stream) {
+  if (!q || !k_pool || !v_pool || !map || !lane_rows || !lane_lens || !out) {
+    g_last_error = "decode attention (no-alloc): null pointer argument";
+    return LS_EINVAL;
+  }
+  try {
+    check_attn_shape(n_lanes, n_heads, n_kv_heads, head_dim, n_slots, n_rows, max_context);
+    const int max_chunks = cdiv(max_context, kAttnChunk);
+    const size_t need =
+        carve_attn_scratch(nullptr, n_lanes, n_heads, n_kv_heads, head_dim, max_chunks).total;
+    REQUIRE(need <= kNoAllocScratchBytes, LS_ECAPACITY,
+            "decode attention (no-alloc): this shape needs " + std::to_string(need) +
+                " scratch bytes, above the fixed " + std::to_string(kNoAllocScratchBytes) +
+                " (lanes x heads x ceil(max_context/256) x head_dim x 4 bytes must fit); "
+                "use ls_decode_attention with a workspace");
+    char* base = noalloc_scratch_for_current_device();
+    const AttnScratch sc =
+        carve_attn_scratch(base, n_lanes, n_heads, n_kv_heads, head_dim, max_chunks);
+    run_decode_attention(q, k_pool, v_pool, map, lane_rows, lane_lens, n_lanes, n_heads, n_kv_heads,
+                         head_dim, n_slots, n_rows, max_context, sc, out,
+                         static_cast<cudaStream_t>(stream));
+  } catch (const std::exception& ex) {
+    return fail_global(ex);
+  }
+  return LS_OK;
+}
+
+size_t ls_decode_attention_noalloc_limit(void) { return kNoAllocScratchBytes; }
+
 
 size_t ls_decode_attention_workspace_bytes(int n_lanes, int n_heads, int n_kv_heads, int head_dim,
                                            int max_context) {
