@@ -53,6 +53,8 @@ def parse():
     p.add_argument("--first", type=int, default=1)
     p.add_argument("--second", type=int, default=2)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--synthetic-accept", type=float, default=0.05,
+                   help="post-norm gain of the separately reported high-acceptance run (0: skip)")
     return p.parse_args()
 
 
@@ -259,6 +261,30 @@ def engine_arm(args):
     value = tok_all / dec_s_max
     e2e = new_all / wall_max
 
+    # Separately reported: the same request on weights whose post-norm gains
+    # are scaled down (small recurrent updates, so early readouts agree with the
+    # final one). Uniform random weights reject every draft; this shows what the
+    # pipeline does when drafts are accepted. Not the headline value.
+    synth = None
+    if args.synthetic_accept and rank == 0:
+        w2 = init_random_weights(cfg, 0, device=f"cuda:{local}", dtype=torch.bfloat16)
+        for k in w2:
+            if k.endswith(("post_attention_layernorm.weight", "post_feedforward_layernorm.weight")):
+                w2[k].mul_(args.synthetic_accept)
+        eng2 = Engine(cfg, sch, w2, device=local, max_context=max_ctx, max_prompt=args.prompt)
+        generate_loopspec(eng2, prompt_of(0), args.new_tokens)
+        _, s_ls = generate_loopspec(eng2, prompt_of(1), args.new_tokens)
+        _, s_ar = generate_autoregressive(eng2, prompt_of(1), args.new_tokens)
+        ls_tps = s_ls["decode_tokens"] / (s_ls["decode_device_ms"] / 1e3)
+        ar_tps = s_ar["decode_tokens"] / (s_ar["decode_device_ms"] / 1e3)
+        synth = {"init": f"post-norm weights x{args.synthetic_accept}", "loopspec_tok_s": round(ls_tps, 2),
+                 "ar_tok_s": round(ar_tps, 2), "speedup_vs_ar": round(ls_tps / ar_tps, 3),
+                 "mean_accept_len": round(accept_length(s_ls, sch), 4),
+                 "first_rejections": int(s_ls["first_rejections"]),
+                 "decode_tokens": int(s_ls["decode_tokens"])}
+        eng2.close()
+        del w2
+
     # autoregressive beside it (one request, same prompt distribution)
     ar_ids, ar_st = generate_autoregressive(eng, prompt_of(0), args.new_tokens)
     ar_tok_s = ar_st["decode_tokens"] / (ar_st["decode_device_ms"] / 1e3)
@@ -313,10 +339,11 @@ def engine_arm(args):
             "gpu_launches": None,
             "clocks": clk,
         }
-        n_kern = {r: eng.kernel_count(r, lanes) for r in ("pre", "core", "post")}
-        per_cycle = n_kern["core"] * sch.step_size + n_kern["post"] + n_kern["pre"]
-        line["gpu_launches"] = int(agg["pipeline_cycles"] * per_cycle / args.steps * args.steps)
-        line["gpu_launches_note"] = "kernels in the timed region (per-cycle graph kernel count x cycles)"
+        line["gpu_launches"] = int(agg["decode_kernel_launches"])
+        line["gpu_launches_note"] = ("engine kernels launched by the timed decode loops "
+                                     "(counted per graph replay by the engine)")
+        if synth is not None:
+            line["synthetic_acceptance"] = synth
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(cfg, sch, args, os.cpu_count() or 1)
         print(json.dumps(line), flush=True)

@@ -70,6 +70,7 @@ typedef struct ls_stats {
   double prefill_device_ms;
   int64_t h2d_bytes;         /* host->device bytes copied for the request       */
   int64_t d2h_bytes;         /* device->host bytes copied for the request       */
+  int64_t decode_kernel_launches; /* engine kernels launched by the decode loop */
 } ls_stats;
 
 typedef struct ls_engine ls_engine;

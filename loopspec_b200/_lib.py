@@ -51,7 +51,7 @@ class Stats(ctypes.Structure):
         ("second_verifications", _i64), ("second_acceptances", _i64),
         ("second_rejections", _i64), ("decode_tokens", _i64),
         ("decode_device_ms", _f64), ("decode_host_s", _f64), ("prefill_device_ms", _f64),
-        ("h2d_bytes", _i64), ("d2h_bytes", _i64),
+        ("h2d_bytes", _i64), ("d2h_bytes", _i64), ("decode_kernel_launches", _i64),
     ]
 
     def as_dict(self):

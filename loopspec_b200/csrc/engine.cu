@@ -395,9 +395,15 @@ struct ls_engine {
   float* logits_host = nullptr;
   int* err_dev = nullptr;
   int* attn_tickets = nullptr;  // [cap][n_kv_heads] chunk-arrival counters, zero between calls
+  float* gemm_part = nullptr;   // GEMM split partial tiles
+  long gemm_part_elems = 0;
+  int* gemm_tickets = nullptr;  // GEMM per-tile split-arrival counters, zero between launches
+  long gemm_ticket_count = 0;
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
 
   std::map<std::pair<int, int>, cudaGraphExec_t> graphs;
+  std::map<std::pair<int, int>, int> graph_kernels;   // kernels per captured graph
+  int64_t kernel_launches = 0;                        // kernels launched by role calls
   int kernels_in_call = 0;
   int64_t h2d_bytes = 0, d2h_bytes = 0;   // host<->device traffic counters
 
@@ -437,9 +443,9 @@ struct ls_engine {
     return it->second.first;
   }
 
-  // K splits per 128-row tile, aiming at about two CTAs per SM; a split group
-  // is one thread-block cluster, so at most kMaxSplits. Depends only on the
-  // weight shape (never on the batch).
+  // K splits per 128-row tile, aiming at about two CTAs per SM (all resident
+  // in one wave), at most kMaxSplits. Depends only on the weight shape, never
+  // on the batch.
   int choose_splits(int Mw, int Kd) const {
     const int tiles = cdiv(Mw, kGemmBM);
     const int KB = cdiv(Kd, kGemmBK);
@@ -460,6 +466,12 @@ struct ls_engine {
       g.has_map64 = true;
     }
     part_elems = std::max(part_elems, (long)cap * Mw);
+    // scratch for the widest call of this GEMM (cap lanes)
+    const int bn = cap * 2 <= 16 ? 16 : cap * 2 <= 32 ? 32 : cap * 2 <= 64 ? 64 : cap * 2 <= 128 ? 128 : 256;
+    const long tiles = (long)cdiv(Mw, kGemmBM) * cdiv(2 * cap, bn);
+    gemm_ticket_count = std::max(gemm_ticket_count, tiles);
+    if (g.splits > 1)
+      gemm_part_elems = std::max(gemm_part_elems, tiles * g.splits * (bn / 2) * kGemmBM);
     return g;
   }
 
@@ -605,6 +617,8 @@ struct ls_engine {
     CK(cudaMallocHost(&logits_host, sizeof(float) * (size_t)V));
     err_dev = dalloc<int>(1);
     attn_tickets = dalloc<int>((long)cap * NKV);
+    gemm_part = dalloc<float>(gemm_part_elems);
+    gemm_tickets = dalloc<int>(gemm_ticket_count);
     std::vector<float> inv(HD / 2);
     for (int i = 0; i < HD / 2; ++i)
       inv[i] = (float)(1.0 / std::pow((double)mc.rope_theta, (2.0 * i) / HD));
@@ -678,20 +692,22 @@ void gemm(ls_engine& e, const Gemm& g, XBuf& x, const GemmEpi& epi, int kind, in
   cfg.gridDim = dim3(m_tiles, g.splits, cdiv(2 * n, bn));
   cfg.blockDim = dim3(kGemmThreads);
   cfg.stream = e.stream;
-  cudaLaunchAttribute attr[2];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 1;
-  attr[0].val.clusterDim.y = g.splits;
-  attr[0].val.clusterDim.z = 1;
-  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = e.sc.use_pdl ? 2 : 1;
+  cfg.numAttrs = e.sc.use_pdl ? 1 : 0;
+  GemmEpi ep = epi;
+  ep.part_ws = e.gemm_part;
+  ep.tile_tickets = e.gemm_tickets;
+  REQUIRE((long)cfg.gridDim.x * cfg.gridDim.z <= e.gemm_ticket_count, LS_EINVAL, "GEMM tile tickets too small");
+  REQUIRE((long)cfg.gridDim.x * cfg.gridDim.z * g.splits * (bn / 2) * kGemmBM <= e.gemm_part_elems ||
+              g.splits == 1, LS_EINVAL, "GEMM partial scratch too small");
   const CUtensorMap& wm = kind == kEpiSwiGLU ? g.map64 : g.map;
 #define LS_GEMM_K(BN, ST, EPI)                                                                     \
   do {                                                                                              \
     cfg.dynamicSmemBytes = GemmSmem<BN, ST>::kTotal;                                                \
-    CK(cudaLaunchKernelEx(&cfg, gemm_tc_kernel<BN, ST, EPI>, wm, xm, epi, g.Mw, g.K, n, x_row0, \
+    CK(cudaLaunchKernelEx(&cfg, gemm_tc_kernel<BN, ST, EPI>, wm, xm, ep, g.Mw, g.K, n, x_row0, \
                           g.splits, e.err_dev));                                                   \
   } while (0)
 #define LS_GEMM(BN, ST)                                           \
@@ -968,6 +984,7 @@ void run_role(ls_engine& e, int role, int n, const int* host_meta, bool graphabl
   upload_meta(e, role, host_meta, n);
   if (!(graphable && e.sc.use_graphs)) {
     enqueue_role(e, role, n, po);
+    e.kernel_launches += e.kernels_in_call;
     return;
   }
   const auto key = std::make_pair(role, n);
@@ -989,8 +1006,10 @@ void run_role(ls_engine& e, int role, int n, const int* host_meta, bool graphabl
     cudaGraphDestroy(g);
     CK(ie);
     it = e.graphs.emplace(key, ge).first;
+    e.graph_kernels[key] = e.kernels_in_call;
   }
   CK(cudaGraphLaunch(it->second, e.stream));
+  e.kernel_launches += e.graph_kernels[key];
 }
 
 void check_device(ls_engine& e) {
@@ -1784,6 +1803,7 @@ int ls_generate(ls_engine* e, const int64_t* prompt, int n_prompt, int max_new, 
     st.prefill_device_ms = pms;
     REQUIRE(e->prefill_len + max_new < e->max_ctx, LS_ECAPACITY, "prompt + max_new_tokens exceeds max_context");
     double t0 = -1.0;
+    const int64_t launches0 = e->kernel_launches;
     CK(cudaEventRecord(e->ev0, e->stream));
     std::vector<long long> ids;
     if (mode == 0) {
@@ -1804,6 +1824,7 @@ int ls_generate(ls_engine* e, const int64_t* prompt, int n_prompt, int max_new, 
     *n_out = (int)ids.size();
     st.h2d_bytes = e->h2d_bytes;
     st.d2h_bytes = e->d2h_bytes;
+    st.decode_kernel_launches = e->kernel_launches - launches0;
     if (stats) *stats = st;
   } catch (const std::exception& ex) {
     return fail(e, ex);

@@ -9,15 +9,15 @@
 // tcgen05.mma and activation rows sit on N (16..256), so a handful of decode
 // lanes still uses the full tensor-core M width.
 //
-// Grid (m_tiles, splits, n_tiles), cluster (1, splits, 1): the `splits` CTAs
-// of one m-tile each stream a fixed K range (boundaries depend only on K and
-// splits, never on the batch). TMA streams 128x64 weight boxes and BNx64
-// activation boxes into an ST-deep shared-memory ring (128-byte swizzle); one
-// thread issues the MMAs into a TMEM accumulator; four warps read it back,
-// add each lane's hi/lo columns and park the partial tile in shared memory.
-// After a cluster barrier every CTA of the cluster reduces a slice of the
-// tile's rows over all splits in split order through distributed shared
-// memory, then applies the epilogue:
+// Grid (m_tiles, splits, n_tiles): the `splits` CTAs of one m-tile each
+// stream a fixed K range (boundaries depend only on K and splits, never on the
+// batch). TMA streams 128x64 weight boxes and BNx64 activation boxes into an
+// ST-deep shared-memory ring (128-byte swizzle); one thread issues the MMAs
+// into a TMEM accumulator; four warps read it back and add each lane's hi/lo
+// columns. The last split of a tile to finish (atomic ticket) sums the splits'
+// partial tiles in split order and applies the epilogue. (Clusters with a
+// DSMEM reduction were measured slower: only 15 eight-CTA clusters fit on the
+// GPU at once, which split the GEMMs into two waves.)
 //   kEpiStore   y -> fp32 out[n][m]
 //   kEpiQkvRope q/k rows get neox RoPE at the lane's position; k and v go to
 //               the layer's KV pool at the lane's slot (bf16), q to fp32
@@ -33,7 +33,7 @@ namespace ls {
 constexpr int kGemmBM = 128;
 constexpr int kGemmBK = 64;   // 64 bf16 = 128 bytes = one swizzle row
 constexpr int kGemmThreads = 128;
-constexpr int kMaxSplits = 8; // portable cluster size
+constexpr int kMaxSplits = 16; // K splits per 128-row tile
 
 enum GemmEpiKind : int { kEpiStore = 0, kEpiQkvRope = 1, kEpiSwiGLU = 2 };
 
@@ -47,6 +47,8 @@ struct GemmEpi {
   int hd, nh, nkv, n_slots;
   __nv_bfloat16* x_act;       // swiglu: (hi, lo) rows [2*cap][I]
   int I;
+  float* part_ws;             // split partial tiles [tiles][splits][BN/2][128] (splits > 1)
+  int* tile_tickets;          // [tiles], zero between launches
 };
 
 template <int BN, int ST>
@@ -60,29 +62,6 @@ struct GemmSmem {
   // partial tile [BN/2 lanes][128 rows] fp32, parked in the drained stage ring
   static_assert(BN / 2 * kGemmBM * 4 <= ST * kStageBytes, "partial tile must fit the ring");
 };
-
-__device__ __forceinline__ uint32_t cluster_rank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-
-__device__ __forceinline__ void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
-                   : "memory");
-}
-
-__device__ __forceinline__ uint32_t map_to_rank(uint32_t smem_addr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
-  return r;
-}
-
-__device__ __forceinline__ float ld_dsmem(uint32_t addr) {
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
-  return v;
-}
 
 template <int BN, int ST, int EPI>
 __global__ void __launch_bounds__(kGemmThreads, 1)
@@ -185,13 +164,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
   __syncthreads();
 
-  // Park this split's partial tile: red[l][r] = acc[r][2l] + acc[r][2l+1]
-  // (lane l's hi and lo activation rows). The ring is drained: every TMA load
-  // was consumed by an MMA that completed before acc_bar.
+  // Park this split's partial tile in shared memory: red[l][r] = acc[r][2l] +
+  // acc[r][2l+1] (lane l's hi and lo activation rows). With K splits, each
+  // split also publishes the tile to global scratch and takes a ticket; the
+  // last split of the tile to finish sums all splits in split order (so the
+  // result does not depend on which split finished last) and runs the
+  // epilogue while the others exit. The ring is drained: every TMA load was
+  // consumed by an MMA that completed before acc_bar.
   const bool have = mbar_wait(acc_bar, 0, err, kDevTimeoutAcc);
   tc_fence_after();
   float* red = reinterpret_cast<float*>(smem);
   const int lanes_here = min(BN / 2, n_valid - n0 / 2);   // lanes of this N tile
+  const long tile_id = (long)blockIdx.z * gridDim.x + blockIdx.x;
+  const long split_floats = (long)(BN / 2) * kGemmBM;
+  float* tile_part = epi.part_ws + tile_id * splits * split_floats;
   {
     const int r = warp * 32 + lane;
 #pragma unroll 1
@@ -204,21 +190,32 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       for (int j = 0; j < 4; ++j) {
         const float s = (have && nkb > 0) ? __uint_as_float(v[2 * j]) + __uint_as_float(v[2 * j + 1]) : 0.f;
         red[(c0 / 2 + j) * kGemmBM + r] = s;
+        if (splits > 1) tile_part[split * split_floats + (c0 / 2 + j) * kGemmBM + r] = s;
       }
     }
   }
   tc_fence_before();
-  cluster_sync();   // all partial tiles of this m-tile are visible cluster-wide
+  __shared__ int s_last;
+  if (splits > 1) __threadfence();
+  __syncthreads();
+  if (warp == 2) tmem_dealloc(tmem, L::kTmemCols);
+  if (splits > 1) {
+    if (threadIdx.x == 0) {
+      int* tk = epi.tile_tickets + tile_id;
+      const int t = atomicAdd(tk, 1);
+      s_last = t == splits - 1;
+      if (s_last) *tk = 0;   // every split has arrived: ready for the next launch
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+  }
 
-  // Reduce: this CTA owns units [u0, u1) of the tile's 64 row pairs. A unit is
-  // two rows that one epilogue needs together (RoPE pair, gate/up pair, or two
-  // adjacent rows).
-  const uint32_t my_rank = cluster_rank();
-  const int u0 = (int)((long)my_rank * 64 / splits), u1 = (int)((long)(my_rank + 1) * 64 / splits);
-  const uint32_t red_base = smem_u32(red);
-  for (int item = threadIdx.x; item < (u1 - u0) * lanes_here; item += blockDim.x) {
-    const int l = item / (u1 - u0);
-    const int u = u0 + item % (u1 - u0);
+  // Epilogue over the tile's 64 row pairs. A unit is two rows that one
+  // epilogue needs together (RoPE pair, gate/up pair, or two adjacent rows).
+  for (int item = threadIdx.x; item < 64 * lanes_here; item += blockDim.x) {
+    const int l = item / 64;
+    const int u = item % 64;
     int r0, r1;
     if (EPI == kEpiQkvRope) {
       const int half = epi.hd / 2;
@@ -232,10 +229,27 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       r1 = 2 * u + 1;
     }
     float v0 = 0.f, v1 = 0.f;
-    for (int s = 0; s < splits; ++s) {
-      const uint32_t base = map_to_rank(red_base, (uint32_t)s);
-      v0 += ld_dsmem(base + (uint32_t)((l * kGemmBM + r0) * 4));
-      v1 += ld_dsmem(base + (uint32_t)((l * kGemmBM + r1) * 4));
+    if (splits == 1) {
+      v0 = red[l * kGemmBM + r0];
+      v1 = red[l * kGemmBM + r1];
+    } else {
+      // issue every split's loads first, then add them in split order
+      float a0[kMaxSplits], a1[kMaxSplits];
+#pragma unroll
+      for (int s = 0; s < kMaxSplits; ++s) {
+        if (s < splits) {
+          const float* ps = tile_part + s * split_floats + l * kGemmBM;
+          a0[s] = s == split ? red[l * kGemmBM + r0] : __ldcg(ps + r0);
+          a1[s] = s == split ? red[l * kGemmBM + r1] : __ldcg(ps + r1);
+        }
+      }
+#pragma unroll
+      for (int s = 0; s < kMaxSplits; ++s) {
+        if (s < splits) {
+          v0 += a0[s];
+          v1 += a1[s];
+        }
+      }
     }
     const int n = n0 / 2 + l;   // lane index
     if (EPI == kEpiStore) {
@@ -276,8 +290,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
   }
-  cluster_sync();   // no CTA leaves while others still read its partial tile
-  if (warp == 2) tmem_dealloc(tmem, L::kTmemCols);
 }
 
 }  // namespace ls

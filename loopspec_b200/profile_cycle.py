@@ -1,0 +1,54 @@
+"""Profiling driver: prefill one prompt, then replay one graphed role call.
+
+    python -m loopspec_b200.profile_cycle --config ouro-1.4b --prompt 600 \
+        --lanes 4 --role core --iters 3
+
+Runs the engine exactly as a decode cycle does (same kernels, same graph) on a
+prefilled request, so an ncu launch list or a single-kernel capture of the last
+replays shows the decode kernels without the prefill's. Prints the CUDA-event
+time per call and the number of kernels per call. Kernel launches before the
+first replay: the prefill's (reported as `launches_before_timed`).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+
+import torch
+
+from .build import build
+from .config import get_config
+from .engine import Engine
+from .schedule import PipelineSchedule
+from .weights import init_random_weights
+
+
+def main():
+    p = argparse.ArgumentParser()
+    p.add_argument("--config", default="ouro-1.4b")
+    p.add_argument("--prompt", type=int, default=600)
+    p.add_argument("--lanes", type=int, default=4)
+    p.add_argument("--role", default="core", choices=["pre", "core", "post"])
+    p.add_argument("--iters", type=int, default=3)
+    p.add_argument("--first", type=int, default=1)
+    p.add_argument("--second", type=int, default=2)
+    a = p.parse_args()
+    build()
+    cfg = get_config(a.config)
+    w = init_random_weights(cfg, 0, device="cuda:0", dtype=torch.bfloat16)
+    X = a.second // a.first if a.second else None
+    eng = Engine(cfg, PipelineSchedule(cfg.stages, a.first, X), w, device=0,
+                 max_context=max(2048, a.prompt + 64), max_prompt=a.prompt)
+    g = torch.Generator().manual_seed(0)
+    eng.prefill(torch.randint(0, cfg.vocab, (a.prompt,), generator=g).tolist())
+    per_call = eng.kernel_count(a.role, a.lanes)
+    ms = eng.time_role(a.role, a.lanes, a.prompt, a.iters)
+    print(json.dumps({"config": cfg.name, "role": a.role, "lanes": a.lanes, "context": a.prompt,
+                      "ms_per_call": round(ms, 4), "kernels_per_call": per_call,
+                      "timed_replays": a.iters, "warmup_replays": 1}))
+    eng.close()
+
+
+if __name__ == "__main__":
+    main()
