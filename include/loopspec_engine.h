@@ -97,14 +97,24 @@ int ls_finalize(ls_engine* eng);
 int ls_prefill(ls_engine* eng, const int64_t* prompt, int n_prompt, float* out_logits,
                int64_t* first_token);
 
+/* Sampling settings of the next request(s) (the reference's request-level
+ * {temperature, top_k, top_p} and sampling_seed, server/loopspec_scheduler.py:
+ * 316-329). Greedy iff top_k == 1 or temperature == 0 (the default). Sampled
+ * decisions follow sampling/policy.py: top-p / top-k filtered softmax, q1 draw,
+ * q2 conditional residual, final verification and the rejection fallback, all
+ * on the GPU; uniforms come from Philox4x32-10 keyed by `seed`. */
+int ls_set_sampling(ls_engine* eng, float temperature, int top_k, float top_p, uint64_t seed);
+
 /* One pipeline cycle over `n_lanes` lanes (LosslessLoopSpecExecutor.forward,
- * executor.py:293-367, without the decision policy): pre for stage-0 lanes,
- * K core iterations for all lanes, post + greedy argmax for lanes whose last
- * iteration is a q1/q2/final readout. lanes: int64 [n_lanes][6] =
- * (stage, index, token, branch, parent_branch or -1, state_slot).
- * out_decisions: int64 [n_lanes], argmax token for endpoint lanes, -1 else.
- * out_logits: optional host float [n_lanes][vocab] (rows of non-endpoint
- * lanes are left untouched). Synchronises once (decision readback). */
+ * executor.py:293-367, without the host resolve step): pre for stage-0 lanes,
+ * K core iterations for all lanes, post + decision for lanes whose last
+ * iteration is a q1/q2/final readout. lanes: int64 [n_lanes][8] =
+ * (stage, index, token, branch, parent_branch or -1, state_slot, q1 token or
+ * -1, q2 token or -1). out_decisions: int64 [n_lanes][5] per readout lane:
+ * greedy -> (argmax, 0, 0, 0, 0); sampling -> (token, proposed,
+ * accepted_code, q1_rejected, q2_rejected) as policy.py:197-283; other lanes
+ * (-1, 0, 0, 0, 0). out_logits: optional host float [n_lanes][vocab] (rows of
+ * non-readout lanes are left untouched). Synchronises once (readback). */
 int ls_cycle(ls_engine* eng, const int64_t* lanes, int n_lanes, int64_t* out_decisions,
              float* out_logits);
 

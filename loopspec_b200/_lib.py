@@ -73,6 +73,7 @@ SIGNATURES = [
     ("ls_load_weight", _i32, [_P, ctypes.c_char_p, _P, _i32, _PI64, _i32]),
     ("ls_finalize", _i32, [_P]),
     ("ls_prefill", _i32, [_P, _PI64, _i32, _PF32, _PI64]),
+    ("ls_set_sampling", _i32, [_P, _f32, _i32, _f32, _u64]),
     ("ls_cycle", _i32, [_P, _PI64, _i32, _PI64, _PF32]),
     ("ls_retain", _i32, [_P, _PI64, _PI64, _i32]),
     ("ls_generate", _i32, [_P, _PI64, _i32, _i32, _i32, _i64, _PI64, ctypes.POINTER(_i32),

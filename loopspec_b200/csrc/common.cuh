@@ -20,6 +20,30 @@ enum DeviceError : int {
   kDevBadIndex = 4,       // a metadata index was out of range (access skipped)
 };
 
+// Lane metadata: int32 [cap][kMetaFields], lane-major (one record per lane,
+// so a role call uploads only its own lanes).
+enum MetaField : int {
+  kMetaToken = 0,
+  kMetaPos = 1,       // sequence position of the lane's input token
+  kMetaRow = 2,       // mapping row of the lane's timeline in this role/depth
+  kMetaSlot = 3,      // KV slot receiving this token's K/V for this timeline
+  kMetaForkRow = 4,   // parent mapping row to copy a prefix from, or -1
+  kMetaForkLen = 5,   // prefix length to copy
+  kMetaStateIn = 6,   // state-bank row read by this role
+  kMetaStateOut = 7,  // state-bank row written by this role
+  kMetaKind = 8,      // post rows: readout kind 0 q1, 1 q2, 2 final
+  kMetaFirst = 9,     // post rows: the lane's q1 token, or -1
+  kMetaSecond = 10,   // post rows: the lane's q2 token, or -1
+  kMetaCycle = 11,    // post rows: per-request draw counter (random stream index)
+  kMetaFields = 12,
+};
+
+struct Meta {
+  const int* p;
+  int cap;
+  __device__ __forceinline__ int get(int f, int b) const { return p[b * kMetaFields + f]; }
+};
+
 // Upper bound on mbarrier polls. try_wait itself suspends for a bounded time,
 // so this caps a stuck wait at a few seconds before the kernel bails out.
 constexpr uint32_t kWaitLimit = 1u << 24;

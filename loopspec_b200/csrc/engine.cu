@@ -15,8 +15,10 @@
 #include "common.cuh"
 #include "gemm_tc.cuh"
 #include "kernels.cuh"
+#include "sampler.cuh"
 
 #include <algorithm>
+#include <array>
 #include <chrono>
 #include <cmath>
 #include <cstring>
@@ -395,6 +397,15 @@ struct ls_engine {
   float* logits_host = nullptr;
   int* err_dev = nullptr;
   int* attn_tickets = nullptr;  // [cap][n_kv_heads] chunk-arrival counters, zero between calls
+  // sampling (greedy iff disabled): parameters on the device so captured
+  // graphs read the current request's settings; q1 / q2-residual
+  // distributions per lane state slot; per-row scratch and decisions
+  bool sampling = false;
+  SampleParams sparams{1.f, 1.f, 0, 0, 0ull};
+  SampleParams* sparams_dev = nullptr;
+  float *q1_bank = nullptr, *r_bank = nullptr, *samp_work = nullptr;
+  long long *dec_dev = nullptr, *dec_host = nullptr;
+  uint32_t draw_cycle = 0;
   float* gemm_part = nullptr;   // GEMM split partial tiles
   long gemm_part_elems = 0;
   int* gemm_tickets = nullptr;  // GEMM per-tile split-arrival counters, zero between launches
@@ -427,6 +438,7 @@ struct ls_engine {
     if (meta_host) cudaFreeHost(meta_host);
     if (amax_host) cudaFreeHost(amax_host);
     if (logits_host) cudaFreeHost(logits_host);
+    if (dec_host) cudaFreeHost(dec_host);
     if (ev0) cudaEventDestroy(ev0);
     if (ev1) cudaEventDestroy(ev1);
     if (stream) cudaStreamDestroy(stream);
@@ -618,6 +630,17 @@ struct ls_engine {
     err_dev = dalloc<int>(1);
     attn_tickets = dalloc<int>((long)cap * NKV);
     gemm_part = dalloc<float>(gemm_part_elems);
+    sparams_dev = dalloc<SampleParams>(1);
+    CK(cudaMemcpy(sparams_dev, &sparams, sizeof(SampleParams), cudaMemcpyHostToDevice));
+    q1_bank = dalloc<float>((long)max_rows * V);
+    r_bank = dalloc<float>((long)max_rows * V);
+    samp_work = dalloc<float>((long)max_rows * 2 * V);
+    dec_dev = dalloc<long long>((long)cap * 5);
+    CK(cudaMallocHost(&dec_host, sizeof(long long) * 5 * (size_t)cap));
+    REQUIRE(V <= kSampleChunk * kSampleMaxChunks, LS_EINVAL, "vocabulary above the sampler's limit");
+    if (V <= kSampleSmemVocab)
+      CK(cudaFuncSetAttribute(sample_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              (int)(V * sizeof(float))));
     gemm_tickets = dalloc<int>(gemm_ticket_count);
     std::vector<float> inv(HD / 2);
     for (int i = 0; i < HD / 2; ++i)
@@ -955,8 +978,18 @@ void enqueue_role(ls_engine& e, int role, int n, const PostOpts& po = PostOpts()
     if (po.head) {
       const int lanes = po.head_lanes < 0 ? n : po.head_lanes;
       gemm_store(e, e.g_lm, e.x_h, e.logits, lanes, po.head_lane0);
-      klaunch(e, argmax_kernel, dim3(lanes), dim3(1024), 0, (const float*)e.logits, e.V, (long)e.V,
-              e.amax_dev);
+      if (e.sampling) {
+        REQUIRE(lanes <= e.max_rows, LS_ECAPACITY, "too many sampled readout rows");
+        SampleArgs sa{meta, po.head_lane0, e.logits, e.V, e.sparams_dev, e.q1_bank, e.r_bank,
+                      e.max_rows, e.samp_work, e.dec_dev, e.err_dev};
+        if (e.V <= kSampleSmemVocab)
+          klaunch(e, sample_kernel<true>, dim3(lanes), dim3(kSampleThreads), (size_t)e.V * sizeof(float), sa);
+        else
+          klaunch(e, sample_kernel<false>, dim3(lanes), dim3(kSampleThreads), 0, sa);
+      } else {
+        klaunch(e, argmax_kernel, dim3(lanes), dim3(1024), 0, (const float*)e.logits, e.V, (long)e.V,
+                e.amax_dev);
+      }
     }
   }
 }
@@ -987,7 +1020,7 @@ void run_role(ls_engine& e, int role, int n, const int* host_meta, bool graphabl
     e.kernel_launches += e.kernels_in_call;
     return;
   }
-  const auto key = std::make_pair(role, n);
+  const auto key = std::make_pair(role * 2 + (e.sampling ? 1 : 0), n);
   auto it = e.graphs.find(key);
   if (it == e.graphs.end()) {
     CK(cudaStreamBeginCapture(e.stream, cudaStreamCaptureModeThreadLocal));
@@ -1067,6 +1100,14 @@ void advance(Cursor* c, int slot, bool owned) {
   c->seq_len += 1;
 }
 
+// A readout that only draws the next token (no proposal to verify).
+void set_final_readout(ls_engine& e, int* m, int b, int draw) {
+  put(e, m, kMetaKind, b, 2);
+  put(e, m, kMetaFirst, b, -1);
+  put(e, m, kMetaSecond, b, -1);
+  put(e, m, kMetaCycle, b, draw);
+}
+
 long long prefill(ls_engine& e, const int64_t* prompt, int P, float* logits_out) {
   REQUIRE(e.finalized, LS_EINVAL, "engine not finalized");
   REQUIRE(P >= 1 && P <= e.sc.max_prompt, LS_EINVAL, "prompt length out of range");
@@ -1077,6 +1118,7 @@ long long prefill(ls_engine& e, const int64_t* prompt, int P, float* logits_out)
   e.tl.reset();
   e.staging_next = 0;
   e.prefill_len = P - 1;
+  e.draw_cycle = 0;   // the first token uses draw 0, decode cycles 1, 2, ...
   CK(cudaMemsetAsync(e.err_dev, 0, sizeof(int), e.stream));
   CK(cudaEventRecord(e.ev0, e.stream));
 
@@ -1114,6 +1156,7 @@ long long prefill(ls_engine& e, const int64_t* prompt, int P, float* logits_out)
         po.head = last_chunk && s == e.S - 1;
         po.head_lane0 = n - 1;
         po.head_lanes = 1;
+        if (po.head) set_final_readout(e, m, n - 1, 0);
         run_role(e, kPost, n, m, false, po);
         for (int j = 0; j < n; ++j) advance(post_c[s], slots[j], false);
       }
@@ -1121,11 +1164,15 @@ long long prefill(ls_engine& e, const int64_t* prompt, int P, float* logits_out)
     if (!post_attn && last_chunk) {
       m = stage_meta(e);
       fill_lane(e, m, 0, 0, P - 1, nullptr, e.max_rows + n - 1, -1);
+      set_final_readout(e, m, 0, 0);
       run_role(e, kPost, 1, m, false);
     }
   }
   CK(cudaEventRecord(e.ev1, e.stream));
-  CK(cudaMemcpyAsync(e.amax_host, e.amax_dev, sizeof(long long), cudaMemcpyDeviceToHost, e.stream));
+  if (e.sampling)
+    CK(cudaMemcpyAsync(e.amax_host, e.dec_dev, sizeof(long long), cudaMemcpyDeviceToHost, e.stream));
+  else
+    CK(cudaMemcpyAsync(e.amax_host, e.amax_dev, sizeof(long long), cudaMemcpyDeviceToHost, e.stream));
   e.d2h_bytes += sizeof(long long);
   if (logits_out)
     CK(cudaMemcpyAsync(e.logits_host, e.logits, sizeof(float) * e.V, cudaMemcpyDeviceToHost, e.stream));
@@ -1139,12 +1186,18 @@ long long prefill(ls_engine& e, const int64_t* prompt, int P, float* logits_out)
 struct CycleLane {
   int stage, index, token, branch, parent, state;
   int origin = -1;   // scheduler bookkeeping only (trace output)
+  int first = -1;    // the lane's q1 token (-1: none)
+  int second = -1;   // the lane's q2 token (-1: none)
 };
+
+// One readout decision: (token, proposed, accepted_code, q1_rejected,
+// q2_rejected) for sampling (policy.py:197-218); greedy fills [0] only.
+typedef std::array<long long, 5> Dec;
 
 // One pipeline cycle (executor.py:293-367 without the decision policy):
 // pre for stage-0 lanes, K core iterations for all lanes, post + argmax for
 // readout lanes. dec[i] = argmax token for readout lanes, -1 otherwise.
-void cycle(ls_engine& e, const std::vector<CycleLane>& lanes, std::vector<long long>& dec,
+void cycle(ls_engine& e, const std::vector<CycleLane>& lanes, std::vector<Dec>& dec,
            float* logits_out) {
   REQUIRE(e.prefill_len >= 0, LS_EINVAL, "no prefilled request");
   const int B = (int)lanes.size();
@@ -1186,7 +1239,10 @@ void cycle(ls_engine& e, const std::vector<CycleLane>& lanes, std::vector<long l
     run_role(e, kCore, B, m, true);
     for (int i = 0; i < B; ++i) advance(cs[i], slots[i], true);
   }
-  dec.assign(B, -1);
+  dec.assign(B, Dec{-1, 0, 0, 0, 0});
+  // random-stream index of this cycle's readouts: the pipeline cycle number,
+  // counted whether or not the cycle has a readout
+  const int draw = (int)(++e.draw_cycle);
   if (ep_rows.empty()) return;
   const int M = (int)ep_rows.size();
   int* m = stage_meta(e);
@@ -1195,12 +1251,23 @@ void cycle(ls_engine& e, const std::vector<CycleLane>& lanes, std::vector<long l
     const CycleLane& l = lanes[ep_rows[j]];
     if (post_attn) cs[j] = e.tl.get_or_create_cursor(kPost, ends[ep_rows[j]], l.branch, l.parent);
     slots[j] = fill_lane(e, m, j, l.token, pos[ep_rows[j]], cs[j], l.state, -1);
+    put(e, m, kMetaKind, j, e.endpoint_kind.at(ends[ep_rows[j]]));
+    put(e, m, kMetaFirst, j, l.first);
+    put(e, m, kMetaSecond, j, l.second);
+    put(e, m, kMetaCycle, j, draw);
   }
   run_role(e, kPost, M, m, true);
   for (int j = 0; j < M; ++j)
     if (cs[j]) advance(cs[j], slots[j], true);
-  CK(cudaMemcpyAsync(e.amax_host, e.amax_dev, sizeof(long long) * M, cudaMemcpyDeviceToHost, e.stream));
-  e.d2h_bytes += sizeof(long long) * M;
+  if (e.sampling) {
+    CK(cudaMemcpyAsync(e.dec_host, e.dec_dev, sizeof(long long) * 5 * M, cudaMemcpyDeviceToHost,
+                       e.stream));
+    e.d2h_bytes += sizeof(long long) * 5 * M;
+  } else {
+    CK(cudaMemcpyAsync(e.amax_host, e.amax_dev, sizeof(long long) * M, cudaMemcpyDeviceToHost,
+                       e.stream));
+    e.d2h_bytes += sizeof(long long) * M;
+  }
   if (logits_out) {
     for (int j = 0; j < M; ++j)
       CK(cudaMemcpyAsync(logits_out + (long)ep_rows[j] * e.V, e.logits + (long)j * e.V,
@@ -1209,7 +1276,13 @@ void cycle(ls_engine& e, const std::vector<CycleLane>& lanes, std::vector<long l
   CK(cudaStreamSynchronize(e.stream));
   e.staging_next = 0;
   check_device(e);
-  for (int j = 0; j < M; ++j) dec[ep_rows[j]] = e.amax_host[j];
+  for (int j = 0; j < M; ++j) {
+    if (e.sampling) {
+      for (int f = 0; f < 5; ++f) dec[ep_rows[j]][f] = e.dec_host[j * 5 + f];
+    } else {
+      dec[ep_rows[j]][0] = e.amax_host[j];
+    }
+  }
 }
 
 // ----------------------------------------------------- native scheduler loop
@@ -1286,8 +1359,9 @@ void retain_timelines(ls_engine& e, const std::vector<PLane>& lanes) {
 // them to a host decision callback so the same loop is testable without a GPU.
 struct SchedHooks {
   int S = 0, K = 1, X = 0, max_rows = 0;
+  bool sampling = false;   // decisions are sampled 5-field rows, else greedy argmax
   std::map<int, int> endpoint_kind;
-  std::function<void(const std::vector<CycleLane>&, std::vector<long long>&)> forward;
+  std::function<void(const std::vector<CycleLane>&, std::vector<Dec>&)> forward;
   std::function<void(const std::vector<PLane>&, int accepted_stage)> retain;
   std::function<bool(const std::vector<long long>&)> should_stop;
 };
@@ -1315,13 +1389,14 @@ std::vector<long long> run_loopspec(SchedHooks& e, long long first, int max_new,
   lanes[0].index = 1;
   lanes[0].token = (int)first;
   std::vector<CycleLane> cl;
-  std::vector<long long> dec;
+  std::vector<Dec> dec;
   while ((int)committed.size() < max_new) {
     // executor.forward
     cl.clear();
     for (auto& l : lanes) {
       if (l.state < 0) l.state = pool.acquire();  // written back as result.state
-      cl.push_back({l.stage, l.index, l.token, l.branch, l.parent, l.state, l.origin});
+      cl.push_back({l.stage, l.index, l.token, l.branch, l.parent, l.state, l.origin,
+                    l.first_token, l.second_token});
     }
     e.forward(cl, dec);
     st.pipeline_cycles += 1;
@@ -1340,31 +1415,42 @@ std::vector<long long> run_loopspec(SchedHooks& e, long long first, int max_new,
       const int end_stage = l.stage + e.K - 1;
       auto kit = e.endpoint_kind.find(end_stage);
       const int kind = kit == e.endpoint_kind.end() ? -1 : kit->second;
-      const long long pred = dec[i];
+      // resolve (greedy: decisions.py:136-184; sampling: policy.py:285-308)
+      const Dec& d = dec[i];
+      const long long pred = d[0];
+      bool proposed = false, fr = false, sr = false;
+      int acc = -1;
+      if (e.sampling) {
+        proposed = d[1] != 0;
+        acc = d[2] == 1 ? q1 : d[2] == 2 ? q2 : -1;
+        fr = d[3] != 0;
+        sr = d[4] != 0;
+      } else {
+        proposed = kind == 0 || (kind == 1 && (l.first_token < 0 || pred != l.first_token));
+        if (kind == 2 && l.first_token >= 0) {
+          fr = pred != l.first_token;
+          if (!fr) acc = q1;
+          else if (l.second_token >= 0) {
+            sr = pred != l.second_token;
+            if (!sr) acc = q2;
+          }
+        }
+      }
       if (end_stage == final_stage) {
         REQUIRE(final_idx < 0, LS_EPIPELINE, "multiple branches reached the final stage");
         final_idx = (int)i;
         final_pred = pred;
-        // greedy final verification (decisions.py:163-170) and metrics
-        if (l.first_token >= 0) {
-          const bool fr = pred != l.first_token;
-          bool sr = false;
-          if (!fr) accepted_stage = q1;
-          else if (l.second_token >= 0) {
-            sr = pred != l.second_token;
-            if (!sr) accepted_stage = q2;
-          }
-          const bool sv = fr && l.second_token >= 0;
-          st.first_rejections += fr;
-          st.second_verifications += sv;
-          st.second_acceptances += sv && accepted_stage == q2;
-          st.second_rejections += sv && sr;
-        }
+        accepted_stage = acc;
+        // executor.py:268-281
+        const bool sv = fr && l.second_token >= 0;
         st.verified_proposals += 1;
+        st.first_rejections += fr;
+        st.second_verifications += sv;
+        st.second_acceptances += sv && acc == q2;
+        st.second_rejections += sv && sr;
         continue;
       }
       l.stage = end_stage + 1;
-      const bool proposed = kind == 0 || (kind == 1 && (l.first_token < 0 || pred != l.first_token));
       if ((end_stage == q1 || end_stage == q2) && kind >= 0 && proposed) {
         if (end_stage == q1) l.first_token = (int)pred;
         else l.second_token = (int)pred;
@@ -1466,9 +1552,11 @@ std::vector<long long> run_ar(ls_engine& e, long long first, int max_new, long l
     m = stage_meta(e);
     c = post_attn ? e.tl.get_or_create_cursor(kPost, e.S - 1, 0, -1) : nullptr;
     slot = fill_lane(e, m, 0, tok, pos, c, 0, -1);
+    set_final_readout(e, m, 0, (int)(++e.draw_cycle));
     run_role(e, kPost, 1, m, true);
     if (c) advance(c, slot, true);
-    CK(cudaMemcpyAsync(e.amax_host, e.amax_dev, sizeof(long long), cudaMemcpyDeviceToHost, e.stream));
+    CK(cudaMemcpyAsync(e.amax_host, e.sampling ? e.dec_dev : e.amax_dev, sizeof(long long),
+                       cudaMemcpyDeviceToHost, e.stream));
     e.d2h_bytes += sizeof(long long);
     CK(cudaStreamSynchronize(e.stream));
     e.staging_next = 0;
@@ -1488,7 +1576,8 @@ SchedHooks engine_hooks(ls_engine& e, long long stop_token) {
   hk.X = e.X;
   hk.max_rows = e.max_rows;
   hk.endpoint_kind = e.endpoint_kind;
-  hk.forward = [&e](const std::vector<CycleLane>& cl, std::vector<long long>& dec) {
+  hk.sampling = e.sampling;
+  hk.forward = [&e](const std::vector<CycleLane>& cl, std::vector<Dec>& dec) {
     cycle(e, cl, dec, nullptr);
   };
   hk.retain = [&e](const std::vector<PLane>& lanes, int) { retain_timelines(e, lanes); };
@@ -1751,6 +1840,24 @@ int ls_finalize(ls_engine* e) {
   return LS_OK;
 }
 
+int ls_set_sampling(ls_engine* e, float temperature, int top_k, float top_p, uint64_t seed) {
+  if (!e) return LS_EINVAL;
+  try {
+    REQUIRE(e->finalized, LS_EINVAL, "engine not finalized");
+    REQUIRE(temperature >= 0.f && top_k >= 0 && top_p > 0.f && top_p <= 1.f, LS_EINVAL,
+            "sampling needs temperature >= 0, top_k >= 0, 0 < top_p <= 1");
+    // greedy iff top_k == 1 (temperature 0 is normalised to it), as the
+    // reference server decides (server/loopspec_scheduler.py:316-329)
+    e->sampling = !(temperature == 0.f || top_k == 1);
+    e->sparams = SampleParams{temperature == 0.f ? 1.f : temperature, top_p, top_k, 0, seed};
+    CK(cudaStreamSynchronize(e->stream));
+    CK(cudaMemcpy(e->sparams_dev, &e->sparams, sizeof(SampleParams), cudaMemcpyHostToDevice));
+  } catch (const std::exception& ex) {
+    return fail(e, ex);
+  }
+  return LS_OK;
+}
+
 int ls_prefill(ls_engine* e, const int64_t* prompt, int n, float* out_logits, int64_t* first) {
   if (!e || !prompt || !first) return LS_EINVAL;
   try {
@@ -1767,12 +1874,14 @@ int ls_cycle(ls_engine* e, const int64_t* lanes, int n, int64_t* out_dec, float*
     CK(cudaSetDevice(e->device));
     std::vector<CycleLane> cl(n);
     for (int i = 0; i < n; ++i) {
-      const int64_t* l = lanes + 6 * i;
-      cl[i] = {(int)l[0], (int)l[1], (int)l[2], (int)l[3], (int)l[4], (int)l[5], -1};
+      const int64_t* l = lanes + 8 * i;
+      cl[i] = {(int)l[0], (int)l[1], (int)l[2], (int)l[3], (int)l[4], (int)l[5], -1, (int)l[6],
+               (int)l[7]};
     }
-    std::vector<long long> dec;
+    std::vector<Dec> dec;
     cycle(*e, cl, dec, out_logits);
-    for (int i = 0; i < n; ++i) out_dec[i] = dec[i];
+    for (int i = 0; i < n; ++i)
+      for (int f = 0; f < 5; ++f) out_dec[i * 5 + f] = dec[i][f];
   } catch (const std::exception& ex) {
     return fail(e, ex);
   }
@@ -1857,17 +1966,17 @@ int ls_pipeline_simulate(int stages, int step_size, int second_step, int64_t fir
       for (int t = X; t < depth; ++t) b.push_back(b[t - 1] + b[t - X]);
     }
     for (long v : b) hk.max_rows += (int)v;
-    hk.forward = [&](const std::vector<CycleLane>& cl, std::vector<long long>& dec) {
+    hk.forward = [&](const std::vector<CycleLane>& cl, std::vector<Dec>& dec) {
       std::vector<int64_t> rows;
       for (auto& l : cl) {
         const int64_t r[7] = {l.stage, l.index, l.token, l.branch, l.parent, l.origin, l.state};
         rows.insert(rows.end(), r, r + 7);
       }
       if (on_cycle) on_cycle(user, rows.data(), (int32_t)cl.size());
-      dec.assign(cl.size(), -1);
+      dec.assign(cl.size(), Dec{-1, 0, 0, 0, 0});
       for (size_t i = 0; i < cl.size(); ++i) {
         auto it = hk.endpoint_kind.find(cl[i].stage + K - 1);
-        if (it != hk.endpoint_kind.end()) dec[i] = decide(user, cl[i].index, cl[i].token, it->second);
+        if (it != hk.endpoint_kind.end()) dec[i][0] = decide(user, cl[i].index, cl[i].token, it->second);
       }
     };
     hk.retain = [&](const std::vector<PLane>& lanes, int accepted) {

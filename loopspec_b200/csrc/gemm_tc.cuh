@@ -1,5 +1,5 @@
-// Weight-streaming GEMM on 5th-generation tensor cores (sm_100a) with an
-// in-cluster split-K reduction and fused epilogues.
+// Weight-streaming GEMM on 5th-generation tensor cores (sm_100a) with a
+// last-split split-K reduction and fused epilogues.
 //
 //   y[n][m] = sum_k W[m][k] * x[n][k]
 //
@@ -39,7 +39,7 @@ enum GemmEpiKind : int { kEpiStore = 0, kEpiQkvRope = 1, kEpiSwiGLU = 2 };
 
 struct GemmEpi {
   float* out;                 // store: out[n * Mw + m]
-  const int* meta;            // qkv: lane metadata (int32 [cap][8], pos at 1, slot at 3)
+  const int* meta;            // qkv: lane metadata (int32 [cap][kMetaFields])
   const float* inv_freq;      // qkv: [hd/2]
   float* q;                   // qkv: [cap][nh*hd]
   __nv_bfloat16* kpool;       // qkv: this layer's [slots][nkv*hd]
@@ -265,8 +265,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int hd = epi.hd, half = hd / 2;
       const int mg = m0 + r0;
       const int head = mg / hd, i = mg - head * hd;   // i < half
-      const int pos = epi.meta[n * 8 + 1];
-      const int slot = epi.meta[n * 8 + 3];
+      const int pos = epi.meta[n * kMetaFields + kMetaPos];
+      const int slot = epi.meta[n * kMetaFields + kMetaSlot];
       const int kvd = epi.nkv * hd;
       if (head < epi.nh + epi.nkv) {
         float sn, cs;

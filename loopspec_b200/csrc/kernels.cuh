@@ -11,26 +11,6 @@
 
 namespace ls {
 
-// Lane metadata: int32 [cap][kMetaFields], lane-major (one 32-byte record per
-// lane, so a role call uploads only its own lanes).
-enum MetaField : int {
-  kMetaToken = 0,
-  kMetaPos = 1,       // sequence position of the lane's input token
-  kMetaRow = 2,       // mapping row of the lane's timeline in this role/depth
-  kMetaSlot = 3,      // KV slot receiving this token's K/V for this timeline
-  kMetaForkRow = 4,   // parent mapping row to copy a prefix from, or -1
-  kMetaForkLen = 5,   // prefix length to copy
-  kMetaStateIn = 6,   // state-bank row read by this role
-  kMetaStateOut = 7,  // state-bank row written by this role
-  kMetaFields = 8,
-};
-
-struct Meta {
-  const int* p;
-  int cap;
-  __device__ __forceinline__ int get(int f, int b) const { return p[b * kMetaFields + f]; }
-};
-
 // ----------------------------------------------------------- mapping update
 // Fork: row[0:fork_len) = parent_row[0:fork_len) (O(fork_len), once per fork),
 // then row[pos] = slot. Mirrors the reference's in-graph mapping update

@@ -1,0 +1,325 @@
+// Fused top-p / top-k / temperature sampling and LoopSpec draft verification.
+//
+// One CTA (1024 threads) per readout row does, on the device and without a
+// host round trip:
+//   P = filter(softmax(logits / T)) renormalised (fp32), where top-p keeps
+//       every probability >= the largest value v with sum_{p >= v} p >= top_p
+//       and top-k every probability >= the k-th largest (ties kept; both ->
+//       the larger cutoff), as the reference's sort / cumsum / searchsorted
+//       filter (sampling/distributions.py:14-86). The cutoffs are found by
+//       bisection over fp32 bit patterns (monotone for non-negative floats)
+//       instead of a full sort.
+//   q1     draw x ~ P; keep P as the lane's q1 distribution (sampler.py:49-102)
+//   q2     r = max(P - Q1, 0), r[x] = 0; draw y ~ r; R = r / sum r; propose y
+//          iff sum r > 0 and P[x] < Q1[x] (sampler.py:178-344)
+//   final  no q1 token: draw from P; else accept x iff u0 < min(1, P[x]/Q1[x])
+//          (sampler.py:428-460); on rejection F = norm(max(P - Q1, 0)), accept
+//          the q2 token y iff u1 < min(1, F[y]/R[y]), else draw from
+//          norm(max(F - R, 0)) (or F) with u2 (sampling/rejection.py:42-97)
+// and writes the decision row (token, proposed, accepted_code, q1_rejected,
+// q2_rejected) of policy.py:197-283. Draws invert a CDF in chunks of 2048
+// tokens like the reference. Uniforms: words of Philox4x32-10 with counter
+// (cycle, row, 0, 0) and the request's seed as key, u = (w >> 8) * 2^-24.
+#pragma once
+
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace ls {
+
+constexpr int kSampleThreads = 1024;
+constexpr int kSampleChunk = 2048;
+constexpr int kSampleMaxChunks = 64;        // vocab <= 131072
+constexpr int kSampleSmemVocab = 51200;     // P kept in shared memory up to this vocab
+
+struct SampleParams {
+  float temperature;
+  float top_p;
+  int top_k;
+  int pad;
+  unsigned long long seed;
+};
+
+struct SampleArgs {
+  Meta meta;                    // readout rows: kind, first, second, state slot, cycle
+  int meta_row0;                // metadata record of row 0 (head lanes may start later)
+  const float* logits;          // [rows][V]
+  int V;
+  const SampleParams* params;   // device copy (graphs read it at run time)
+  float* q1_bank;               // [bank_rows][V] lane q1 distributions, by state slot
+  float* r_bank;                // [bank_rows][V] lane q2 residual distributions
+  int bank_rows;
+  float* work;                  // [rows][2][V] scratch (P when it does not fit smem, and W)
+  long long* decisions;         // [rows][5]
+  int* err;
+};
+
+__device__ __forceinline__ uint4 philox_words(unsigned long long seed, uint32_t c0, uint32_t c1) {
+  return philox4x32_10(make_uint4(c0, c1, 0u, 0u), (uint32_t)seed, (uint32_t)(seed >> 32));
+}
+
+// Deterministic block reductions over 1024 threads (fixed tree).
+__device__ __forceinline__ float sblock_sum(float v, float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = lane < (int)(blockDim.x >> 5) ? red[lane] : 0.f;
+  return warp_sum(t);
+}
+
+__device__ __forceinline__ float sblock_max(float v, float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  v = warp_max(v);
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = lane < (int)(blockDim.x >> 5) ? red[lane] : -INFINITY;
+  return warp_max(t);
+}
+
+// Largest value v (an element of p) with F(v) >= target, F(v) = sum or count
+// of the elements >= v, found by bisection over the bit patterns in [0, max].
+template <bool COUNT>
+__device__ float bisect_cutoff(const float* p, int V, float target, float pmax, float* red) {
+  uint32_t lo = 0u, hi = __float_as_uint(pmax) + 1u;   // F(lo) >= target > F(hi)
+  while (hi - lo > 1u) {
+    const uint32_t mid = lo + (hi - lo) / 2u;
+    const float v = __uint_as_float(mid);
+    float acc = 0.f;
+    for (int t = threadIdx.x; t < V; t += blockDim.x) {
+      const float x = p[t];
+      if (x >= v) acc += COUNT ? 1.f : x;
+    }
+    const float tot = sblock_sum(acc, red);
+    if (tot >= target) lo = mid;
+    else hi = mid;
+  }
+  return __uint_as_float(lo);
+}
+
+// Inverse-CDF draw from non-negative weights w (need not be normalised).
+// target = u * total; first 2048-chunk whose inclusive CDF exceeds target, then
+// the first token of it whose inclusive CDF exceeds target - preceding mass.
+__device__ int block_pick(const float* w, int V, float u, float* s_chunk, float* red, int* s_idx) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const int nch = (V + kSampleChunk - 1) / kSampleChunk;
+  for (int c = warp; c < nch; c += nw) {          // one warp per chunk, 64 tokens per lane
+    float a = 0.f;
+    const int base = c * kSampleChunk + lane * (kSampleChunk / 32);
+    for (int i = 0; i < kSampleChunk / 32; ++i) {
+      const int t = base + i;
+      if (t < V) a += w[t];
+    }
+    a = warp_sum(a);
+    if (lane == 0) s_chunk[c] = a;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float total = 0.f;
+    for (int c = 0; c < nch; ++c) total += s_chunk[c];
+    const float target = u * total;
+    float cdf = 0.f, pre = 0.f;
+    int ch = -1;
+    for (int c = 0; c < nch; ++c) {
+      if (cdf + s_chunk[c] > target) {
+        ch = c;
+        pre = cdf;
+        break;
+      }
+      cdf += s_chunk[c];
+    }
+    if (ch < 0) {
+      ch = 0;
+      pre = 0.f;
+    }
+    s_idx[0] = ch;
+    red[0] = target - pre;
+  }
+  __syncthreads();
+  const int ch = s_idx[0];
+  const float rem = red[0];
+  __syncthreads();
+  if (warp == 0) {
+    const int base = ch * kSampleChunk + lane * (kSampleChunk / 32);
+    float a = 0.f;
+    for (int i = 0; i < kSampleChunk / 32; ++i) {
+      const int t = base + i;
+      if (t < V) a += w[t];
+    }
+    float incl = a;                                  // inclusive scan over lanes
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float n = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += n;
+    }
+    const float excl = incl - a;
+    const unsigned hit = __ballot_sync(0xffffffffu, incl > rem);
+    int tok = ch * kSampleChunk;                     // nothing exceeds: first token of the chunk
+    if (hit) {
+      const int hl = __ffs(hit) - 1;
+      if (lane == hl) {
+        float c = excl;
+        int found = base;
+        for (int i = 0; i < kSampleChunk / 32; ++i) {
+          const int t = base + i;
+          if (t >= V) break;
+          c += w[t];
+          if (c > rem) {
+            found = t;
+            break;
+          }
+        }
+        s_idx[1] = found;
+      }
+      __syncwarp();
+    } else if (lane == 0) {
+      s_idx[1] = tok;
+    }
+  }
+  __syncthreads();
+  const int r = s_idx[1];
+  __syncthreads();
+  return r;
+}
+
+template <bool SMEM_P>
+__global__ void __launch_bounds__(kSampleThreads) sample_kernel(SampleArgs a) {
+  pdl_wait();
+  pdl_launch_dependents();
+  extern __shared__ float s_p[];
+  __shared__ float red[32];
+  __shared__ float s_chunk[kSampleMaxChunks];
+  __shared__ int s_idx[2];
+  const int row = blockIdx.x;
+  const int V = a.V;
+  const SampleParams prm = *a.params;
+  const int kind = a.meta.get(kMetaKind, a.meta_row0 + row);
+  const int first = a.meta.get(kMetaFirst, a.meta_row0 + row);
+  const int second = a.meta.get(kMetaSecond, a.meta_row0 + row);
+  const int slot = a.meta.get(kMetaStateIn, a.meta_row0 + row);
+  const uint32_t cycle = (uint32_t)a.meta.get(kMetaCycle, a.meta_row0 + row);
+  float* P = SMEM_P ? s_p : a.work + (long)row * 2 * V;
+  float* W = a.work + (long)row * 2 * V + V;
+  const float* lg = a.logits + (long)row * V;
+  const bool need_bank = kind == 0 || kind == 1 || first >= 0;
+  if (need_bank && (slot < 0 || slot >= a.bank_rows)) {
+    if (threadIdx.x == 0) atomicExch(a.err, kDevBadIndex);
+    return;
+  }
+  if ((first >= V) || (second >= V) || ((kind == 1) && first < 0)) {
+    if (threadIdx.x == 0) atomicExch(a.err, kDevBadIndex);
+    return;
+  }
+
+  // softmax(logits / T) in fp32
+  const float invT = 1.f / prm.temperature;
+  float m = -INFINITY;
+  for (int t = threadIdx.x; t < V; t += blockDim.x) m = fmaxf(m, lg[t] * invT);
+  m = sblock_max(m, red);
+  float s = 0.f;
+  for (int t = threadIdx.x; t < V; t += blockDim.x) {
+    const float e = expf(lg[t] * invT - m);
+    P[t] = e;
+    s += e;
+  }
+  s = sblock_sum(s, red);
+  float pmax = 0.f;
+  for (int t = threadIdx.x; t < V; t += blockDim.x) {
+    const float p = P[t] / s;
+    P[t] = p;
+    pmax = fmaxf(pmax, p);
+  }
+  pmax = sblock_max(pmax, red);
+  // top-k / top-p cutoffs, then renormalise over the kept support
+  const int k = prm.top_k >= V ? 0 : prm.top_k;
+  if (k > 0 || prm.top_p < 1.f) {
+    float cut = 0.f;
+    if (prm.top_p < 1.f) cut = bisect_cutoff<false>(P, V, prm.top_p, pmax, red);
+    if (k > 0) cut = fmaxf(cut, bisect_cutoff<true>(P, V, (float)k, pmax, red));
+    float kept = 0.f;
+    for (int t = threadIdx.x; t < V; t += blockDim.x) {
+      const float p = P[t] >= cut ? P[t] : 0.f;
+      P[t] = p;
+      kept += p;
+    }
+    kept = sblock_sum(kept, red);
+    for (int t = threadIdx.x; t < V; t += blockDim.x) P[t] = P[t] / kept;
+  }
+  __syncthreads();
+
+  const uint4 w4 = philox_words(prm.seed, cycle, (uint32_t)row);
+  const float u0 = (float)(w4.x >> 8) * (1.f / 16777216.f);
+  const float u1 = (float)(w4.y >> 8) * (1.f / 16777216.f);
+  const float u2 = (float)(w4.z >> 8) * (1.f / 16777216.f);
+  long long d[5] = {0, 0, 0, 0, 0};
+
+  if (kind == 0) {                                     // q1: draw and keep P
+    float* q1 = a.q1_bank + (long)slot * V;
+    for (int t = threadIdx.x; t < V; t += blockDim.x) q1[t] = P[t];
+    d[0] = block_pick(P, V, u0, s_chunk, red, s_idx);
+    d[1] = 1;
+  } else if (kind == 1) {                              // q2: conditional residual
+    const float* q1 = a.q1_bank + (long)slot * V;
+    float mass = 0.f;
+    for (int t = threadIdx.x; t < V; t += blockDim.x) {
+      const float r = t == first ? 0.f : fmaxf(P[t] - q1[t], 0.f);
+      W[t] = r;
+      mass += r;
+    }
+    mass = sblock_sum(mass, red);
+    const int y = block_pick(W, V, u0, s_chunk, red, s_idx);
+    float* R = a.r_bank + (long)slot * V;
+    for (int t = threadIdx.x; t < V; t += blockDim.x) R[t] = mass > 0.f ? W[t] / mass : 0.f;
+    const int action = mass > 0.f && P[first] < q1[first];
+    d[0] = action ? y : first;
+    d[1] = action;
+    d[2] = action;
+  } else if (first < 0) {                              // final without a proposal
+    d[0] = block_pick(P, V, u0, s_chunk, red, s_idx);
+  } else {                                             // final verification
+    const float* q1 = a.q1_bank + (long)slot * V;
+    const float acc = fminf(1.f, P[first] / q1[first]);
+    if (u0 < acc) {
+      d[0] = first;
+      d[2] = 1;
+    } else {
+      float mF = 0.f, mP = 0.f;
+      for (int t = threadIdx.x; t < V; t += blockDim.x) {
+        const float f = fmaxf(P[t] - q1[t], 0.f);
+        W[t] = f;
+        mF += f;
+        mP += P[t];
+      }
+      mF = sblock_sum(mF, red);
+      mP = sblock_sum(mP, red);
+      for (int t = threadIdx.x; t < V; t += blockDim.x)
+        W[t] = mF > 0.f ? W[t] / mF : P[t] / (mP > 0.f ? mP : 1.f);
+      __syncthreads();
+      bool acc2 = false;
+      if (second >= 0) {
+        const float* R = a.r_bank + (long)slot * V;
+        acc2 = u1 < fminf(1.f, W[second] / R[second]);
+        float mG = 0.f;
+        for (int t = threadIdx.x; t < V; t += blockDim.x) mG += fmaxf(W[t] - R[t], 0.f);
+        mG = sblock_sum(mG, red);
+        if (mG > 0.f) {
+          for (int t = threadIdx.x; t < V; t += blockDim.x) W[t] = fmaxf(W[t] - R[t], 0.f) / mG;
+        }
+        __syncthreads();
+      }
+      const int smp = block_pick(W, V, u2, s_chunk, red, s_idx);
+      d[0] = acc2 ? second : smp;
+      d[2] = acc2 ? 2 : 0;
+      d[3] = 1;
+      d[4] = second >= 0 && !acc2;
+    }
+  }
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int i = 0; i < 5; ++i) a.decisions[(long)row * 5 + i] = d[i];
+  }
+}
+
+}  // namespace ls

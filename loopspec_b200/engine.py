@@ -65,6 +65,7 @@ class Engine:
             self.close()
             raise
         self.prefill_len = None
+        self.sampling = False
 
     def _load(self, name, t):
         import torch
@@ -84,10 +85,17 @@ class Engine:
         self.prefill_len = len(p) - 1
         return (int(first[0]), logits) if want_logits else int(first[0])
 
+    def set_sampling(self, temperature=0.0, top_k=0, top_p=1.0, seed=0):
+        """Request sampling settings; greedy iff top_k == 1 or temperature == 0."""
+        _lib.check(self.L.ls_set_sampling(self.h, float(temperature), int(top_k), float(top_p),
+                                          int(seed) & 0xFFFFFFFFFFFFFFFF), self.h)
+        self.sampling = not (temperature == 0 or top_k == 1)
+
     def cycle(self, lanes, want_logits=False):
-        """lanes: int array [n, 6] (stage, index, token, branch, parent|-1, state)."""
-        a = np.ascontiguousarray(lanes, dtype=np.int64).reshape(-1, 6)
-        dec = np.zeros(len(a), dtype=np.int64)
+        """lanes: int array [n, 8] (stage, index, token, branch, parent|-1, state,
+        q1 token|-1, q2 token|-1). Returns decisions int64 [n, 5]."""
+        a = np.ascontiguousarray(lanes, dtype=np.int64).reshape(-1, 8)
+        dec = np.zeros((len(a), 5), dtype=np.int64)
         logits = np.zeros((len(a), self.cfg.vocab), dtype=np.float32) if want_logits else None
         _lib.check(self.L.ls_cycle(self.h, _i64p(a), len(a), _i64p(dec), _f32p(logits)), self.h)
         return (dec, logits) if want_logits else dec

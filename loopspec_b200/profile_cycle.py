@@ -4,10 +4,11 @@
         --lanes 4 --role core --iters 3
 
 Runs the engine exactly as a decode cycle does (same kernels, same graph) on a
-prefilled request, so an ncu launch list or a single-kernel capture of the last
-replays shows the decode kernels without the prefill's. Prints the CUDA-event
-time per call and the number of kernels per call. Kernel launches before the
-first replay: the prefill's (reported as `launches_before_timed`).
+prefilled request. The replays (one warm-up, then `--iters` timed) run inside
+the NVTX push/pop range "decode_replays", so an ncu launch list restricted to
+it (`ncu --nvtx --nvtx-include "decode_replays/" ...`) holds exactly
+(iters + 1) x kernels_per_call decode launches and none of the prefill's.
+Prints the CUDA-event time per call and the number of kernels per call.
 """
 
 from __future__ import annotations
@@ -43,10 +44,13 @@ def main():
     g = torch.Generator().manual_seed(0)
     eng.prefill(torch.randint(0, cfg.vocab, (a.prompt,), generator=g).tolist())
     per_call = eng.kernel_count(a.role, a.lanes)
+    torch.cuda.nvtx.range_push("decode_replays")
     ms = eng.time_role(a.role, a.lanes, a.prompt, a.iters)
+    torch.cuda.nvtx.range_pop()
     print(json.dumps({"config": cfg.name, "role": a.role, "lanes": a.lanes, "context": a.prompt,
                       "ms_per_call": round(ms, 4), "kernels_per_call": per_call,
-                      "timed_replays": a.iters, "warmup_replays": 1}))
+                      "timed_replays": a.iters, "warmup_replays": 1,
+                      "launches_in_range": (a.iters + 1) * per_call}))
     eng.close()
 
 
