@@ -57,6 +57,9 @@ typedef struct ls_sched_cfg {
   int32_t request_rows;      /* timeline mapping rows (0: auto)              */
   int32_t use_graphs;        /* capture one CUDA graph per (role, width)     */
   int32_t use_pdl;           /* programmatic dependent launch between kernels */
+  int32_t use_persistent;    /* 1: each role call is one persistent kernel over
+                                all SMs (phases separated by grid counters);
+                                0: one kernel per GEMM / attention / row step */
 } ls_sched_cfg;
 
 /* Counters of sglang_recurrent/loopspec/executor.py:35-45 plus timing. */
@@ -155,6 +158,20 @@ int ls_pipeline_simulate(int stages, int step_size, int second_step, int64_t fir
  * benchmark's roofline report. context_len sets every lane's position. */
 int ls_time_role(ls_engine* eng, int role, int n_lanes, int context_len, int iters,
                  double* avg_ms);
+
+/* Diagnostics (no reference counterpart): run one role call of the
+ * persistent kernel eagerly, on the same synthetic lanes as ls_time_role, and
+ * return its per-phase timing trace: out[(phase * grid + cta) * 12 + f] in
+ * globaltimer nanoseconds, f = 0 start of work, 1 arrival, 2 first
+ * accumulator ready, 3 first activation load issued, 4 work done, 5 fences
+ * done, 6 inputs seen complete by the TMA producer, 7 last GEMM segment
+ * finished, 8 last activation load issued, 9 first stage taken by the MMA
+ * issuer, 10 first segment's MMAs issued, 11 weight stages already issued
+ * when the inputs were seen complete (a count); phase index n_phases holds
+ * each CTA's kernel entry (f 0) and co-residency pass (f 1). Zero where a
+ * CTA had no such event. */
+int ls_trace_role(ls_engine* eng, int role, int n_lanes, int context_len, uint64_t* out,
+                  int64_t max_entries, int* n_phases, int* grid);
 
 /* Time one GEMM of the core layer 0 (which: 0 qkv, 1 o, 2 gate_up, 3 down,
  * 4 lm_head) over n_lanes lanes, `iters` launches; average device ms. */

@@ -14,15 +14,13 @@ import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
-SRC = os.path.join(HERE, "csrc", "engine.cu")
+# translation units compiled in parallel, then linked into one library
+SRCS = [os.path.join(HERE, "csrc", "engine.cu"), os.path.join(HERE, "csrc", "stack.cu")]
 OUT = os.path.join(HERE, "libloopspec_engine.so")
+OBJ_DIR = os.path.join(HERE, "_build")
 
-NVCC_FLAGS = [
-    "-gencode", "arch=compute_100a,code=sm_100a",
-    "-lineinfo", "-O3", "-std=c++17",
-    "-Xcompiler", "-fPIC", "-shared",
-    "-diag-suppress", "177",
-]
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+NVCC_FLAGS = [*ARCH, "-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC", "-diag-suppress", "177"]
 
 
 def _sources():
@@ -41,15 +39,27 @@ def build(force: bool = False, verbose: bool = False) -> str:
         newest = max(os.path.getmtime(p) for p in _sources())
         if os.path.getmtime(OUT) >= newest:
             return OUT
+    os.makedirs(OBJ_DIR, exist_ok=True)
+    nvcc = _nvcc()
+    jobs = []
+    for src in SRCS:
+        obj = os.path.join(OBJ_DIR, os.path.basename(src) + ".o")
+        cmd = [nvcc, *NVCC_FLAGS, *(["-Xptxas=-v"] if verbose else []), "-c", "-o", obj, src]
+        jobs.append((obj, subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True)))
+    errors = []
+    for obj, proc in jobs:
+        out, err = proc.communicate()
+        if proc.returncode != 0:
+            errors.append(out + err)
+        elif verbose:
+            sys.stderr.write(err)
+    if errors:
+        raise RuntimeError("nvcc failed:\n" + "\n".join(errors))
     tmp = OUT + ".tmp"
-    cmd = [_nvcc(), *NVCC_FLAGS, "-o", tmp, SRC]
-    if verbose:
-        cmd.insert(1, "-Xptxas=-v")
-    res = subprocess.run(cmd, capture_output=True, text=True)
+    res = subprocess.run([nvcc, *ARCH, "-shared", "-o", tmp, *(o for o, _ in jobs)],
+                         capture_output=True, text=True)
     if res.returncode != 0:
-        raise RuntimeError("nvcc failed:\n" + res.stdout + res.stderr)
-    if verbose:
-        sys.stderr.write(res.stderr)
+        raise RuntimeError("nvcc link failed:\n" + res.stdout + res.stderr)
     os.replace(tmp, OUT)
     return OUT
 

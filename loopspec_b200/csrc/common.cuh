@@ -236,4 +236,49 @@ __device__ __forceinline__ void pdl_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// ------------------------------------------------------------- row helpers
+// The per-lane row kernels give each thread NV float4 columns and issue every
+// global load before the first use, so a row costs one memory round trip per
+// dependent phase rather than one per element.
+__device__ __forceinline__ float4 ld_f4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+
+__device__ __forceinline__ float4 ld_bf4(const __nv_bfloat16* p) {
+  const uint2 u = *reinterpret_cast<const uint2*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+  const float2 a = __bfloat1622float2(h[0]), b = __bfloat1622float2(h[1]);
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+
+__device__ __forceinline__ float4 f4_scale(float4 v, float s, float4 w) {
+  return make_float4(v.x * s * w.x, v.y * s * w.y, v.z * s * w.z, v.w * s * w.w);
+}
+
+__device__ __forceinline__ float f4_sq(float4 v) { return v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w; }
+
+// (hi, lo) pair rows for 4 consecutive columns starting at i (i % 4 == 0).
+__device__ __forceinline__ void store_pair4(__nv_bfloat16* x, long K, int b, long i, float4 v) {
+  const float f[4] = {v.x, v.y, v.z, v.w};
+  __nv_bfloat16 hi[4], lo[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    hi[k] = f2bf(f[k]);
+    lo[k] = f2bf(f[k] - bf2f(hi[k]));
+  }
+  *reinterpret_cast<uint2*>(x + (2L * b) * K + i) = *reinterpret_cast<uint2*>(hi);
+  *reinterpret_cast<uint2*>(x + (2L * b + 1) * K + i) = *reinterpret_cast<uint2*>(lo);
+}
+
+// Philox4x32-10 (Salmon, Moraes, Dror, Shaw, SC'11), counter = (i/4, pos, 0, 0).
+__device__ __forceinline__ uint4 philox4x32_10(uint4 c, uint32_t k0, uint32_t k1) {
+#pragma unroll
+  for (int r = 0; r < 10; ++r) {
+    const uint32_t lo0 = 0xD2511F53u * c.x, hi0 = __umulhi(0xD2511F53u, c.x);
+    const uint32_t lo1 = 0xCD9E8D57u * c.z, hi1 = __umulhi(0xCD9E8D57u, c.z);
+    c = make_uint4(hi1 ^ c.y ^ k0, lo1, hi0 ^ c.w ^ k1, lo0);
+    k0 += 0x9E3779B9u;
+    k1 += 0xBB67AE85u;
+  }
+  return c;
+}
+
 }  // namespace ls

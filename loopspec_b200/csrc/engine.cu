@@ -16,6 +16,7 @@
 #include "gemm_tc.cuh"
 #include "kernels.cuh"
 #include "sampler.cuh"
+#include "stack_api.cuh"
 
 #include <algorithm>
 #include <array>
@@ -412,6 +413,22 @@ struct ls_engine {
   long gemm_ticket_count = 0;
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
 
+  // persistent path: one phase program per role call kind, back to back in
+  // progs_dev; the weight maps they reference; activation maps per BN class
+  static constexpr int kProgPre = 0, kProgCore = 1, kProgPostHead = 2, kProgPostNoHead = 3, kProgs = 4;
+  static constexpr int kBnClasses = 5;                 // BN 16, 32, 64, 128, 256
+  Phase* progs_dev = nullptr;
+  int prog_off[kProgs] = {}, prog_len[kProgs] = {};
+  std::vector<CUtensorMap> prog_maps[kProgs];          // weight maps of each program
+  CUtensorMap xmaps_host[kBnClasses][kXBufs];          // activation maps per BN class
+  std::unique_ptr<StackLaunch> launch_buf;             // parameter block being assembled
+  float* stk_part = nullptr;                           // [num_sms][2][BN/2][128]
+  int* stk_tickets = nullptr;
+  unsigned* stk_sync = nullptr;                        // grid counters, zero between launches
+  int stk_chunks = 0;                                  // attention chunks per (lane, head)
+  StackParams stk_base{};                              // launch fields fixed at finalize
+  unsigned long long* stk_trace = nullptr;             // set only by ls_trace_role (eager launches)
+
   std::map<std::pair<int, int>, cudaGraphExec_t> graphs;
   std::map<std::pair<int, int>, int> graph_kernels;   // kernels per captured graph
   int64_t kernel_launches = 0;                        // kernels launched by role calls
@@ -611,8 +628,10 @@ struct ls_engine {
     r = dalloc<float>((long)cap * H);
     q = dalloc<float>((long)cap * QD);
     part = dalloc<float>(part_elems);
-    o_part = dalloc<float>((long)cap * NH * max_chunks * HD);
-    ml_part = dalloc<float>((long)cap * NH * max_chunks * 2);
+    stk_chunks = cdiv(max_ctx, kStkChunk);
+    const int chunk_slots = std::max(max_chunks, stk_chunks);
+    o_part = dalloc<float>((long)cap * NH * chunk_slots * HD);
+    ml_part = dalloc<float>((long)cap * NH * chunk_slots * 2);
     logits = dalloc<float>((long)cap * V);
     const int xrows = round_up(2 * cap, 256);  // (hi, lo) row pair per lane
     auto mkx = [&](XBuf& xb, int Kd) {
@@ -649,7 +668,243 @@ struct ls_engine {
     CK(cudaMemcpy(inv_freq, inv.data(), sizeof(float) * inv.size(), cudaMemcpyHostToDevice));
 
     set_smem_attrs();
+    if (sc.use_persistent) build_programs();
     finalized = true;
+  }
+
+  // ------------------------------------------------------ persistent programs
+  // Phase programs restating enqueue_role / run_stack for the persistent
+  // kernel: the same steps, in the same order, as phases.
+  std::vector<CUtensorMap>* cur_maps = nullptr;   // maps of the program being built
+  int max_tiles = 0;
+
+  Phase ph_gemm(const Gemm& g, int xbuf, int epi, float* out, bf16* kp = nullptr, bf16* vp = nullptr,
+                bool head = false) {
+    Phase p{};
+    p.kind = kPhGemm;
+    p.xbuf = xbuf;
+    p.epi = epi;
+    p.Mw = g.Mw;
+    p.K = g.K;
+    p.KB = cdiv(g.K, kGemmBK);
+    p.m_tiles = epi == kEpiSwiGLU ? g.Mw / kGemmBM : cdiv(g.Mw, kGemmBM);
+    p.head = head ? 1 : 0;
+    p.out = out;
+    p.kpool = kp;
+    p.vpool = vp;
+    p.x_out = -1;
+    REQUIRE(epi != kEpiSwiGLU || g.has_map64, LS_EINVAL, "SwiGLU needs the 64-row weight map");
+    cur_maps->push_back(epi == kEpiSwiGLU ? g.map64 : g.map);
+    REQUIRE(cur_maps->size() <= (size_t)kStkMaxMaps, LS_EINVAL,
+            "too many weight GEMMs in one role call for the persistent kernel");
+    p.wmap = (int)cur_maps->size() - 1;
+    max_tiles = std::max(max_tiles, p.m_tiles);
+    return p;
+  }
+
+  static Phase ph_simple(int kind) {
+    Phase p{};
+    p.kind = kind;
+    p.x_out = -1;
+    return p;
+  }
+
+  static const bf16* in_norm(int layout, const LayerW& w) {
+    return layout == LS_LAYOUT_OLMO_POST ? nullptr : w.n_in;
+  }
+
+  void add_stack(std::vector<Phase>& v, Stack& st, const StackEnd& end) {
+    const int L = mc.layout;
+    const int nl = (int)st.layers.size();
+    for (int l = 0; l < nl; ++l) {
+      LayerW& w = st.layers[l];
+      const long kvoff = (long)(st.kv_base + l) * n_slots * KVD;
+      bf16* kp = kpool + kvoff;
+      bf16* vp = vpool + kvoff;
+      if (w.qn) {
+        v.push_back(ph_gemm(w.g_qkv, kXH, kEpiStore, part));
+        Phase qk = ph_simple(kPhQkNorm);
+        qk.src = part;
+        qk.q_norm_w = w.qn;
+        qk.k_norm_w = w.kn;
+        qk.kpool = kp;
+        qk.vpool = vp;
+        v.push_back(qk);
+      } else {
+        v.push_back(ph_gemm(w.g_qkv, kXH, kEpiQkvRope, nullptr, kp, vp));
+      }
+      Phase at = ph_simple(kPhAttn);
+      at.kpool = kp;
+      at.vpool = vp;
+      v.push_back(at);
+      v.push_back(ph_gemm(w.g_o, kXAttn, kEpiStore, part));
+      Phase ra = ph_simple(kPhRow);
+      ra.src = part;
+      ra.resid = h;
+      ra.out_h = r;
+      ra.x_out = kXH;
+      if (L == LS_LAYOUT_OURO) {
+        ra.a_norm_w = w.n_pa;
+        ra.x_norm_w = w.n_pf;
+      } else if (L == LS_LAYOUT_RAVEN_PRE) {
+        ra.x_norm_w = w.n_pa;
+      } else {
+        ra.a_norm_w = w.n_pa;
+      }
+      v.push_back(ra);
+      v.push_back(ph_gemm(w.g_gu, kXH, kEpiSwiGLU, nullptr));
+      v.push_back(ph_gemm(w.g_down, kXAct, kEpiStore, part));
+      Phase rb = ph_simple(kPhRow);
+      rb.src = part;
+      rb.resid = r;
+      rb.out_h = h;
+      if (L != LS_LAYOUT_RAVEN_PRE) rb.a_norm_w = w.n_pff;
+      if (l + 1 < nl) {
+        rb.x_out = kXH;
+        rb.x_norm_w = in_norm(L, st.layers[l + 1]);
+      } else {
+        rb.final_norm_w = end.final_norm;
+        rb.bank = end.bank;
+        if (end.want_x) {
+          rb.x_out = kXH;
+          rb.x_norm_w = end.x_norm;
+        }
+      }
+      v.push_back(rb);
+    }
+  }
+
+  // prep phase: h = embedding (src null) or bank[state_in]
+  Phase ph_prep(const float* src, float* bank_out, int x_out, const bf16* x_norm) {
+    Phase p = ph_simple(kPhPrep);
+    p.src = src;
+    p.out_h = h;
+    p.bank = bank_out;
+    p.x_out = x_out;
+    p.x_norm_w = x_norm;
+    return p;
+  }
+
+  void build_programs() {
+    REQUIRE(cap <= kStkMaxLanes, LS_ECAPACITY, "persistent path supports at most 128 lanes per call");
+    REQUIRE(H / 4 <= kStkRowNV * kStkWorkers, LS_EINVAL, "hidden too large for the persistent row phases");
+    const bool ouro = mc.family == LS_FAMILY_OURO;
+    const int L = mc.layout;
+    std::vector<Phase> progs[kProgs];
+    // pre (ouro.py:101-136 / components.py:117-149)
+    cur_maps = &prog_maps[kProgPre];
+    if (ouro) {
+      progs[kProgPre].push_back(ph_prep(nullptr, bank_h, -1, nullptr));
+    } else {
+      std::vector<Phase>& v = progs[kProgPre];
+      const bool layers = !pre.layers.empty();
+      if (layers) v.push_back(ph_simple(kPhMap));
+      v.push_back(ph_prep(nullptr, nullptr, layers ? kXH : -1, layers ? in_norm(L, pre.layers[0]) : nullptr));
+      if (layers) add_stack(v, pre, StackEnd());
+      v.push_back(ph_simple(kPhRavenInit));
+    }
+    // core (ouro.py:93-98 / raven.py:271-281)
+    {
+      cur_maps = &prog_maps[kProgCore];
+      std::vector<Phase>& v = progs[kProgCore];
+      v.push_back(ph_simple(kPhMap));
+      StackEnd end;
+      end.bank = bank_h;
+      if (ouro) {
+        v.push_back(ph_prep(bank_h, nullptr, kXH, in_norm(L, core.layers[0])));
+        end.final_norm = step_norm;
+      } else {
+        v.push_back(ph_simple(kPhCat));
+        v.push_back(ph_gemm(g_adapter, kXCat, kEpiStore, part));
+        Phase ra = ph_simple(kPhRow);
+        ra.src = part;
+        ra.bias = adapter_b;
+        ra.out_h = h;
+        ra.x_out = kXH;
+        ra.x_norm_w = in_norm(L, core.layers[0]);
+        v.push_back(ra);
+      }
+      add_stack(v, core, end);
+    }
+    // post (components.py:175-194), with and without the lm_head
+    for (int which : {kProgPostHead, kProgPostNoHead}) {
+      cur_maps = &prog_maps[which];
+      std::vector<Phase>& v = progs[which];
+      if (!post.layers.empty()) {
+        v.push_back(ph_simple(kPhMap));
+        v.push_back(ph_prep(bank_h, nullptr, kXH, in_norm(L, post.layers[0])));
+        StackEnd end;
+        end.want_x = true;
+        end.x_norm = final_norm;
+        add_stack(v, post, end);
+      } else {
+        v.push_back(ph_prep(bank_h, nullptr, kXH, final_norm));
+      }
+      if (which == kProgPostHead) v.push_back(ph_gemm(g_lm, kXH, kEpiStore, logits, nullptr, nullptr, true));
+    }
+    cur_maps = nullptr;
+    std::vector<Phase> all;
+    for (int i = 0; i < kProgs; ++i) {
+      prog_off[i] = (int)all.size();
+      prog_len[i] = (int)progs[i].size();
+      all.insert(all.end(), progs[i].begin(), progs[i].end());
+    }
+    progs_dev = dalloc<Phase>(all.size());
+    CK(cudaMemcpy(progs_dev, all.data(), sizeof(Phase) * all.size(), cudaMemcpyHostToDevice));
+    // activation maps for every BN class (x_cat only exists for Raven)
+    const int bns[kBnClasses] = {16, 32, 64, 128, 256};
+    for (int c = 0; c < kBnClasses; ++c) {
+      xmaps_host[c][kXH] = x_h.map(bns[c]);
+      xmaps_host[c][kXAttn] = x_attn.map(bns[c]);
+      xmaps_host[c][kXAct] = x_act.map(bns[c]);
+      xmaps_host[c][kXCat] = x_cat.ptr ? x_cat.map(bns[c]) : x_h.map(bns[c]);
+    }
+    launch_buf.reset(new StackLaunch());
+    const int bn_max = cap * 2 <= 16 ? 16 : cap * 2 <= 32 ? 32 : cap * 2 <= 64 ? 64 : cap * 2 <= 128 ? 128 : 256;
+    stk_part = dalloc<float>((long)num_sms * 2 * (bn_max / 2) * kGemmBM);
+    stk_tickets = dalloc<int>(max_tiles);
+    stk_sync = dalloc<unsigned>(4);
+    CK(stack_prepare());
+
+    StackParams& P = stk_base;
+    P.x[kXH] = x_h.ptr;
+    P.x[kXAttn] = x_attn.ptr;
+    P.x[kXAct] = x_act.ptr;
+    P.x[kXCat] = x_cat.ptr;
+    P.xK[kXH] = H;
+    P.xK[kXAttn] = QD;
+    P.xK[kXAct] = I;
+    P.xK[kXCat] = 2 * H;
+    P.h = h;
+    P.q = q;
+    P.H = H;
+    P.NH = NH;
+    P.NKV = NKV;
+    P.HD = HD;
+    P.I = I;
+    P.inv_freq = inv_freq;
+    P.eps = mc.rms_eps;
+    P.attn_scale = 1.0f / std::sqrt((float)HD);
+    P.embed = embed;
+    P.embed_scale = mc.embed_scale;
+    P.vocab = V;
+    P.map = map;
+    P.max_ctx = max_ctx;
+    P.rows = rows;
+    P.n_slots = n_slots;
+    P.bank_h = bank_h;
+    P.bank_inj = bank_inj;
+    P.bank_rows = bank_rows;
+    P.init_seed = mc.init_seed;
+    P.init_std = mc.init_std;
+    P.o_part = o_part;
+    P.ml_part = ml_part;
+    P.attn_tickets = attn_tickets;
+    P.max_chunks = stk_chunks;
+    P.part_ws = stk_part;
+    P.tile_tickets = stk_tickets;
+    P.sync = stk_sync;
+    P.err = err_dev;
   }
 
   std::vector<long> birth_sizes() const {
@@ -920,9 +1175,59 @@ void prep(ls_engine& e, Meta meta, int n, bool embed_mode, float* bank_out, bool
   else klaunch(e, prep_kernel<2>, dim3(n), dim3(thr), 0, pa);
 }
 
+// Readout decisions of the head lanes: fused sampler or greedy argmax.
+void head_decisions(ls_engine& e, Meta meta, int lane0, int lanes) {
+  if (e.sampling) {
+    REQUIRE(lanes <= e.max_rows, LS_ECAPACITY, "too many sampled readout rows");
+    SampleArgs sa{meta, lane0, e.logits, e.V, e.sparams_dev, e.q1_bank, e.r_bank,
+                  e.max_rows, e.samp_work, e.dec_dev, e.err_dev};
+    if (e.V <= kSampleSmemVocab)
+      klaunch(e, sample_kernel<true>, dim3(lanes), dim3(kSampleThreads), (size_t)e.V * sizeof(float), sa);
+    else
+      klaunch(e, sample_kernel<false>, dim3(lanes), dim3(kSampleThreads), 0, sa);
+  } else {
+    klaunch(e, argmax_kernel, dim3(lanes), dim3(1024), 0, (const float*)e.logits, e.V, (long)e.V,
+            e.amax_dev);
+  }
+}
+
+// One role call as a single persistent kernel over all SMs (stack.cuh),
+// followed by the readout decisions when the call includes the lm_head.
+void enqueue_role_persistent(ls_engine& e, int role, int n, const PostOpts& po) {
+  REQUIRE(n >= 1 && n <= kStkMaxLanes, LS_ECAPACITY, "persistent role call wider than 128 lanes");
+  const Meta meta = meta_of(e, role);
+  e.kernels_in_call = 0;
+  const int prog = role == kPre ? ls_engine::kProgPre
+                   : role == kCore ? ls_engine::kProgCore
+                   : po.head ? ls_engine::kProgPostHead : ls_engine::kProgPostNoHead;
+  StackLaunch& L = *e.launch_buf;
+  StackParams& P = L.P;
+  P = e.stk_base;
+  P.phases = e.progs_dev + e.prog_off[prog];
+  P.n_phases = e.prog_len[prog];
+  P.meta = meta;
+  P.n = n;
+  P.head_lane0 = role == kPost ? po.head_lane0 : 0;
+  P.head_n = role == kPost ? (po.head_lanes < 0 ? n : po.head_lanes) : 0;
+  REQUIRE(P.head_lane0 >= 0 && P.head_lane0 + P.head_n <= n, LS_EINVAL, "head lanes out of range");
+  const int bn = pick_bn(2 * n);
+  const int cls = bn == 16 ? 0 : bn == 32 ? 1 : bn == 64 ? 2 : bn == 128 ? 3 : 4;
+  std::memcpy(L.xmap, e.xmaps_host[cls], sizeof(L.xmap));
+  const std::vector<CUtensorMap>& maps = e.prog_maps[prog];
+  if (!maps.empty()) std::memcpy(L.wmap, maps.data(), sizeof(CUtensorMap) * maps.size());
+  P.trace = e.stk_trace;
+  CK(stack_launch(bn, e.HD, L, e.num_sms, e.stream, e.sc.use_pdl != 0));
+  e.kernels_in_call++;
+  if (role == kPost && po.head) head_decisions(e, meta, P.head_lane0, P.head_n);
+}
+
 // The kernel chain of one role call over n lanes whose metadata is in the
 // role's device metadata buffer.
 void enqueue_role(ls_engine& e, int role, int n, const PostOpts& po = PostOpts()) {
+  if (e.sc.use_persistent) {
+    enqueue_role_persistent(e, role, n, po);
+    return;
+  }
   Meta meta = meta_of(e, role);
   e.kernels_in_call = 0;
   const bool ouro = e.mc.family == LS_FAMILY_OURO;
@@ -978,18 +1283,7 @@ void enqueue_role(ls_engine& e, int role, int n, const PostOpts& po = PostOpts()
     if (po.head) {
       const int lanes = po.head_lanes < 0 ? n : po.head_lanes;
       gemm_store(e, e.g_lm, e.x_h, e.logits, lanes, po.head_lane0);
-      if (e.sampling) {
-        REQUIRE(lanes <= e.max_rows, LS_ECAPACITY, "too many sampled readout rows");
-        SampleArgs sa{meta, po.head_lane0, e.logits, e.V, e.sparams_dev, e.q1_bank, e.r_bank,
-                      e.max_rows, e.samp_work, e.dec_dev, e.err_dev};
-        if (e.V <= kSampleSmemVocab)
-          klaunch(e, sample_kernel<true>, dim3(lanes), dim3(kSampleThreads), (size_t)e.V * sizeof(float), sa);
-        else
-          klaunch(e, sample_kernel<false>, dim3(lanes), dim3(kSampleThreads), 0, sa);
-      } else {
-        klaunch(e, argmax_kernel, dim3(lanes), dim3(1024), 0, (const float*)e.logits, e.V, (long)e.V,
-                e.amax_dev);
-      }
+      head_decisions(e, meta, po.head_lane0, lanes);
     }
   }
 }
@@ -1052,9 +1346,10 @@ void check_device(ls_engine& e) {
   if (err != kDevOk) {
     CK(cudaMemset(e.err_dev, 0, sizeof(int)));
     static const char* names[] = {"ok", "TMA stage wait timed out", "free-stage wait timed out",
-                                  "accumulator wait timed out", "metadata index out of range"};
+                                  "accumulator wait timed out", "metadata index out of range",
+                                  "grid phase wait timed out", "persistent CTAs not co-resident"};
     throw EngineError(LS_EDEVICE, std::string("device reported: ") +
-                                      (err > 0 && err < 5 ? names[err] : "unknown error"));
+                                      (err > 0 && err < 7 ? names[err] : "unknown error"));
   }
 }
 
@@ -2063,6 +2358,54 @@ int ls_time_role(ls_engine* e, int role, int n, int context_len, int iters, doub
     float ms = 0.f;
     CK(cudaEventElapsedTime(&ms, e->ev0, e->ev1));
     *avg_ms = ms / iters;
+  } catch (const std::exception& ex) {
+    return fail(e, ex);
+  }
+  return LS_OK;
+}
+
+int ls_trace_role(ls_engine* e, int role, int n, int context_len, uint64_t* out, int64_t max_entries,
+                  int* n_phases, int* grid) {
+  if (!e || !out || !n_phases || !grid || role < 0 || role > 2 || n < 1) return LS_EINVAL;
+  try {
+    REQUIRE(e->sc.use_persistent, LS_EINVAL, "tracing needs the persistent path");
+    REQUIRE(e->prefill_len >= 0, LS_EINVAL, "ls_trace_role needs a prefilled request");
+    REQUIRE(n <= e->max_rows, LS_ECAPACITY, "too many lanes");
+    REQUIRE(context_len >= 1 && context_len <= e->prefill_len + 1, LS_EINVAL,
+            "context_len must not exceed the prompt");
+    const int prog = role == kPre ? ls_engine::kProgPre : role == kCore ? ls_engine::kProgCore
+                                                                        : ls_engine::kProgPostHead;
+    const long entries = (long)(e->prog_len[prog] + 1) * e->num_sms * kStkTraceFields;
+    REQUIRE(entries <= max_entries, LS_ECAPACITY, "trace buffer too small");
+    const bool attn = role == kCore || (role == kPre && e->mc.n_pre_layers) ||
+                      (role == kPost && e->mc.n_post_layers);
+    int* m = stage_meta(*e);
+    for (int b = 0; b < n; ++b) {
+      Cursor c;
+      if (attn) {
+        Cursor* root = e->tl.get_or_create_cursor(role, role == kPost ? e->S - 1 : 0, 0, -1);
+        c.row = e->tl.alloc_row();
+        c.seq_len = context_len - 1;
+        c.pending_parent_row = root->row;
+      }
+      fill_lane(*e, m, b, 1, context_len - 1, attn ? &c : nullptr, b, b);
+    }
+    run_role(*e, role, n, m, false);   // warm-up, eager
+    unsigned long long* tr = e->dalloc<unsigned long long>(entries);
+    e->stk_trace = tr;
+    try {
+      run_role(*e, role, n, m, false);
+    } catch (...) {
+      e->stk_trace = nullptr;
+      throw;
+    }
+    e->stk_trace = nullptr;
+    CK(cudaStreamSynchronize(e->stream));
+    e->staging_next = 0;
+    check_device(*e);
+    CK(cudaMemcpy(out, tr, sizeof(uint64_t) * entries, cudaMemcpyDeviceToHost));
+    *n_phases = e->prog_len[prog];
+    *grid = e->num_sms;
   } catch (const std::exception& ex) {
     return fail(e, ex);
   }

@@ -82,9 +82,13 @@ def cfg_stages(name):
     return get_config(name).stages
 
 
+PATHS = pytest.mark.parametrize("persistent", [True, False], ids=["persistent", "multikernel"])
+
+
+@PATHS
 @pytest.mark.parametrize("name,K,X", [("tiny", 1, 2), ("tiny-raven-llama", 2, 2), ("tiny-raven-olmo", 1, 4)])
-def test_prefill_logits_match_oracle(name, K, X):
-    cfg, eng, om = make(name, K, X)
+def test_prefill_logits_match_oracle(name, K, X, persistent):
+    cfg, eng, om = make(name, K, X, use_persistent=persistent)
     prompt = prompt_for(cfg, 40)
     first, logits = eng.prefill(prompt, want_logits=True)
     rec = []
@@ -95,12 +99,13 @@ def test_prefill_logits_match_oracle(name, K, X):
     eng.close()
 
 
+@PATHS
 @pytest.mark.parametrize("name,K,X,n_new", [
     ("tiny", 1, 2, 48), ("tiny", 1, None, 32), ("tiny", 2, None, 24),
     ("tiny-raven-llama", 2, 2, 24), ("tiny-raven-olmo", 1, 4, 24),
 ])
-def test_loopspec_equals_ar_and_reference_scheduler(name, K, X, n_new):
-    cfg, eng, om = make(name, K, X)
+def test_loopspec_equals_ar_and_reference_scheduler(name, K, X, n_new, persistent):
+    cfg, eng, om = make(name, K, X, use_persistent=persistent)
     sch = eng.schedule
     prompt = prompt_for(cfg, 32, seed=1)
     native, st = eng.generate(prompt, n_new, mode="loopspec")
@@ -123,9 +128,10 @@ def test_loopspec_equals_ar_and_reference_scheduler(name, K, X, n_new):
     eng.close()
 
 
-def test_lanes_above_sixteen_keep_batch_invariance():
+@PATHS
+def test_lanes_above_sixteen_keep_batch_invariance(persistent):
     # S=8, K=1, X=4 reaches 18 live lanes, so the N=32 tensor-core tile is used
-    cfg, eng, _ = make("tiny-raven-olmo", 1, 4)
+    cfg, eng, _ = make("tiny-raven-olmo", 1, 4, use_persistent=persistent)
     assert eng.schedule.max_rows > 16
     prompt = prompt_for(cfg, 24, seed=2)
     native, st = eng.generate(prompt, 40, mode="loopspec")
@@ -146,9 +152,38 @@ def test_graphs_and_pdl_do_not_change_results():
     eng2.close()
 
 
-def test_capacity_errors_are_reported_not_faulted():
+@pytest.mark.parametrize("name", ["tiny", "tiny-raven-llama", "tiny-raven-olmo"])
+def test_persistent_and_multikernel_paths_agree(name):
+    # Same model, same prompt: the two execution paths differ only in the
+    # K-split points of their GEMM reductions (fp32 rounding), which deep
+    # post-norm stacks amplify to ~1e-3 in the logits; bound 5e-3, four times
+    # tighter than the oracle tolerance both paths meet.
+    cfg = get_config(name)
+    prompt = prompt_for(cfg, 48, seed=4)
+    out = {}
+    for persistent in (True, False):
+        _, eng, _ = make(name, 1, 2, use_persistent=persistent)
+        first, logits = eng.prefill(prompt, want_logits=True)
+        ex = B200Executor(eng, prompt, 12, record_logits=True)
+        ids = continue_pipelined(ex.first_token(), 12, ex)
+        out[persistent] = (logits, ids, [lg for (_, e, lg) in ex.logits_log if e == cfg.stages - 1])
+        if persistent:
+            assert eng.kernel_count("core", 3) == 1          # one launch per role call
+        eng.close()
+    (l1, i1, f1), (l0, i0, f0) = out[True], out[False]
+    assert np.abs(l1 - l0).max() <= 5e-3
+    n = 0
+    while n < min(len(i1), len(i0)) and i1[n] == i0[n]:
+        n += 1
+    assert n >= 6                                   # both paths follow the same greedy path
+    for a, b in zip(f1[:n - 1], f0[:n - 1]):
+        assert np.abs(a - b).max() <= 5e-3
+
+
+@PATHS
+def test_capacity_errors_are_reported_not_faulted(persistent):
     from loopspec_b200._lib import EngineError
-    cfg, eng, _ = make("tiny", 1, 2, max_context=64, max_prompt=32)
+    cfg, eng, _ = make("tiny", 1, 2, max_context=64, max_prompt=32, use_persistent=persistent)
     with pytest.raises(EngineError):
         eng.generate(prompt_for(cfg, 40), 8)        # prompt longer than max_prompt
     with pytest.raises(EngineError):
