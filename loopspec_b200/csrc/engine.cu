@@ -422,8 +422,11 @@ struct ls_engine {
   std::vector<CUtensorMap> prog_maps[kProgs];          // weight maps of each program
   CUtensorMap xmaps_host[kBnClasses][kXBufs];          // activation maps per BN class
   std::unique_ptr<StackLaunch> launch_buf;             // parameter block being assembled
-  float* stk_part = nullptr;                           // [num_sms][2][BN/2][128]
-  int* stk_tickets = nullptr;
+  float* stk_part = nullptr;                           // [2][num_sms][2][BN/2][128]
+  int* stk_tickets = nullptr;                          // [2][max tiles]
+  int* stk_cnt = nullptr;                              // completion counters (per tile / kv head)
+  int* stk_tot = nullptr;                              // per-phase completion counters
+  int prog_cnt[kProgs] = {};                           // counters used by each program
   unsigned* stk_sync = nullptr;                        // grid counters, zero between launches
   int stk_chunks = 0;                                  // attention chunks per (lane, head)
   StackParams stk_base{};                              // launch fields fixed at finalize
@@ -677,6 +680,12 @@ struct ls_engine {
   // kernel: the same steps, in the same order, as phases.
   std::vector<CUtensorMap>* cur_maps = nullptr;   // maps of the program being built
   int max_tiles = 0;
+  int b_xh = -1, b_map = -1;                      // program builder: last x_h writer, mapping phase
+
+  static void set_dep(Phase& p, int i, int kind, int phase) {
+    p.dep_kind[i] = kind;
+    p.dep_phase[i] = phase;
+  }
 
   Phase ph_gemm(const Gemm& g, int xbuf, int epi, float* out, bf16* kp = nullptr, bf16* vp = nullptr,
                 bool head = false) {
@@ -686,13 +695,14 @@ struct ls_engine {
     p.epi = epi;
     p.Mw = g.Mw;
     p.K = g.K;
-    p.KB = cdiv(g.K, kGemmBK);
+    p.KB = cdiv(g.K, kStkBK);   // k-units of the persistent kernel
     p.m_tiles = epi == kEpiSwiGLU ? g.Mw / kGemmBM : cdiv(g.Mw, kGemmBM);
     p.head = head ? 1 : 0;
     p.out = out;
     p.kpool = kp;
     p.vpool = vp;
     p.x_out = -1;
+    p.cnt_off = -1;
     REQUIRE(epi != kEpiSwiGLU || g.has_map64, LS_EINVAL, "SwiGLU needs the 64-row weight map");
     cur_maps->push_back(epi == kEpiSwiGLU ? g.map64 : g.map);
     REQUIRE(cur_maps->size() <= (size_t)kStkMaxMaps, LS_EINVAL,
@@ -706,6 +716,7 @@ struct ls_engine {
     Phase p{};
     p.kind = kind;
     p.x_out = -1;
+    p.cnt_off = -1;
     return p;
   }
 
@@ -713,6 +724,11 @@ struct ls_engine {
     return layout == LS_LAYOUT_OLMO_POST ? nullptr : w.n_in;
   }
 
+  // Layers of one stack. Dependencies (what each phase's work waits for):
+  // QKV on the last x_h writer; attention on its head's QKV tiles (or the
+  // QK-norm rows) and the mapping update; O per head on attention; row A on
+  // all O tiles; gate/up on row A; down per k-block on its gate/up tile;
+  // row B on all down tiles.
   void add_stack(std::vector<Phase>& v, Stack& st, const StackEnd& end) {
     const int L = mc.layout;
     const int nl = (int)st.layers.size();
@@ -721,23 +737,39 @@ struct ls_engine {
       const long kvoff = (long)(st.kv_base + l) * n_slots * KVD;
       bf16* kp = kpool + kvoff;
       bf16* vp = vpool + kvoff;
+      int qkv_src;   // phase the attention reads q/k/v from
+      int qkv_kind;
       if (w.qn) {
-        v.push_back(ph_gemm(w.g_qkv, kXH, kEpiStore, part));
+        Phase g = ph_gemm(w.g_qkv, kXH, kEpiStore, part);
+        set_dep(g, 0, kDepTotLanes, b_xh);
+        v.push_back(g);
         Phase qk = ph_simple(kPhQkNorm);
         qk.src = part;
         qk.q_norm_w = w.qn;
         qk.k_norm_w = w.kn;
         qk.kpool = kp;
         qk.vpool = vp;
+        set_dep(qk, 0, kDepTotTiles, (int)v.size() - 1);
         v.push_back(qk);
+        qkv_src = (int)v.size() - 1;
+        qkv_kind = kDepTotLanes;
       } else {
-        v.push_back(ph_gemm(w.g_qkv, kXH, kEpiQkvRope, nullptr, kp, vp));
+        Phase g = ph_gemm(w.g_qkv, kXH, kEpiQkvRope, nullptr, kp, vp);
+        set_dep(g, 0, kDepTotLanes, b_xh);
+        v.push_back(g);
+        qkv_src = (int)v.size() - 1;
+        qkv_kind = kDepQkvHead;
       }
       Phase at = ph_simple(kPhAttn);
       at.kpool = kp;
       at.vpool = vp;
+      set_dep(at, 0, qkv_kind, qkv_src);
+      if (b_map >= 0) set_dep(at, 1, kDepTotLanes, b_map);
       v.push_back(at);
-      v.push_back(ph_gemm(w.g_o, kXAttn, kEpiStore, part));
+      const int attn = (int)v.size() - 1;
+      Phase go = ph_gemm(w.g_o, kXAttn, kEpiStore, part);
+      set_dep(go, 0, kDepKbHead, attn);
+      v.push_back(go);
       Phase ra = ph_simple(kPhRow);
       ra.src = part;
       ra.resid = h;
@@ -751,9 +783,15 @@ struct ls_engine {
       } else {
         ra.a_norm_w = w.n_pa;
       }
+      set_dep(ra, 0, kDepTotTiles, (int)v.size() - 1);
       v.push_back(ra);
-      v.push_back(ph_gemm(w.g_gu, kXH, kEpiSwiGLU, nullptr));
-      v.push_back(ph_gemm(w.g_down, kXAct, kEpiStore, part));
+      b_xh = (int)v.size() - 1;
+      Phase gu = ph_gemm(w.g_gu, kXH, kEpiSwiGLU, nullptr);
+      set_dep(gu, 0, kDepTotLanes, b_xh);
+      v.push_back(gu);
+      Phase gd = ph_gemm(w.g_down, kXAct, kEpiStore, part);
+      set_dep(gd, 0, kDepKbTile, (int)v.size() - 1);
+      v.push_back(gd);
       Phase rb = ph_simple(kPhRow);
       rb.src = part;
       rb.resid = r;
@@ -770,7 +808,9 @@ struct ls_engine {
           rb.x_norm_w = end.x_norm;
         }
       }
+      set_dep(rb, 0, kDepTotTiles, (int)v.size() - 1);
       v.push_back(rb);
+      b_xh = (int)v.size() - 1;
     }
   }
 
@@ -793,21 +833,29 @@ struct ls_engine {
     std::vector<Phase> progs[kProgs];
     // pre (ouro.py:101-136 / components.py:117-149)
     cur_maps = &prog_maps[kProgPre];
+    b_xh = b_map = -1;
     if (ouro) {
       progs[kProgPre].push_back(ph_prep(nullptr, bank_h, -1, nullptr));
     } else {
       std::vector<Phase>& v = progs[kProgPre];
       const bool layers = !pre.layers.empty();
-      if (layers) v.push_back(ph_simple(kPhMap));
+      if (layers) {
+        v.push_back(ph_simple(kPhMap));
+        b_map = 0;
+      }
       v.push_back(ph_prep(nullptr, nullptr, layers ? kXH : -1, layers ? in_norm(L, pre.layers[0]) : nullptr));
+      b_xh = (int)v.size() - 1;
       if (layers) add_stack(v, pre, StackEnd());
-      v.push_back(ph_simple(kPhRavenInit));
+      Phase ri = ph_simple(kPhRavenInit);
+      set_dep(ri, 0, kDepTotLanes, (int)v.size() - 1);   // the prelude output h
+      v.push_back(ri);
     }
     // core (ouro.py:93-98 / raven.py:271-281)
     {
       cur_maps = &prog_maps[kProgCore];
       std::vector<Phase>& v = progs[kProgCore];
       v.push_back(ph_simple(kPhMap));
+      b_map = 0;
       StackEnd end;
       end.bank = bank_h;
       if (ouro) {
@@ -815,33 +863,65 @@ struct ls_engine {
         end.final_norm = step_norm;
       } else {
         v.push_back(ph_simple(kPhCat));
-        v.push_back(ph_gemm(g_adapter, kXCat, kEpiStore, part));
+        Phase ga = ph_gemm(g_adapter, kXCat, kEpiStore, part);
+        set_dep(ga, 0, kDepTotLanes, 1);
+        v.push_back(ga);
         Phase ra = ph_simple(kPhRow);
         ra.src = part;
         ra.bias = adapter_b;
         ra.out_h = h;
         ra.x_out = kXH;
         ra.x_norm_w = in_norm(L, core.layers[0]);
+        set_dep(ra, 0, kDepTotTiles, 2);
         v.push_back(ra);
       }
+      b_xh = (int)v.size() - 1;
       add_stack(v, core, end);
     }
     // post (components.py:175-194), with and without the lm_head
     for (int which : {kProgPostHead, kProgPostNoHead}) {
       cur_maps = &prog_maps[which];
       std::vector<Phase>& v = progs[which];
+      b_map = -1;
       if (!post.layers.empty()) {
         v.push_back(ph_simple(kPhMap));
+        b_map = 0;
         v.push_back(ph_prep(bank_h, nullptr, kXH, in_norm(L, post.layers[0])));
+        b_xh = (int)v.size() - 1;
         StackEnd end;
         end.want_x = true;
         end.x_norm = final_norm;
         add_stack(v, post, end);
       } else {
         v.push_back(ph_prep(bank_h, nullptr, kXH, final_norm));
+        b_xh = (int)v.size() - 1;
       }
-      if (which == kProgPostHead) v.push_back(ph_gemm(g_lm, kXH, kEpiStore, logits, nullptr, nullptr, true));
+      if (which == kProgPostHead) {
+        Phase gh = ph_gemm(g_lm, kXH, kEpiStore, logits, nullptr, nullptr, true);
+        set_dep(gh, 0, kDepTotLanes, b_xh);
+        v.push_back(gh);
+      }
     }
+    // completion counters: one per GEMM tile and per attention kv head
+    int max_cnt = 0, max_len = 0;
+    for (int i = 0; i < kProgs; ++i) {
+      int off = 0, gi = 0;
+      for (Phase& ph : progs[i]) {
+        if (ph.kind == kPhGemm) {
+          ph.cnt_off = off;
+          off += ph.m_tiles;
+          ph.gemm_idx = gi++;
+        } else if (ph.kind == kPhAttn) {
+          ph.cnt_off = off;
+          off += NKV;
+        }
+      }
+      prog_cnt[i] = off;
+      max_cnt = std::max(max_cnt, off);
+      max_len = std::max(max_len, (int)progs[i].size());
+    }
+    stk_cnt = dalloc<int>(max_cnt);
+    stk_tot = dalloc<int>(max_len);
     cur_maps = nullptr;
     std::vector<Phase> all;
     for (int i = 0; i < kProgs; ++i) {
@@ -861,8 +941,8 @@ struct ls_engine {
     }
     launch_buf.reset(new StackLaunch());
     const int bn_max = cap * 2 <= 16 ? 16 : cap * 2 <= 32 ? 32 : cap * 2 <= 64 ? 64 : cap * 2 <= 128 ? 128 : 256;
-    stk_part = dalloc<float>((long)num_sms * 2 * (bn_max / 2) * kGemmBM);
-    stk_tickets = dalloc<int>(max_tiles);
+    stk_part = dalloc<float>(2L * num_sms * 2 * (bn_max / 2) * kGemmBM);
+    stk_tickets = dalloc<int>(2L * max_tiles);
     stk_sync = dalloc<unsigned>(4);
     CK(stack_prepare());
 
@@ -903,6 +983,9 @@ struct ls_engine {
     P.max_chunks = stk_chunks;
     P.part_ws = stk_part;
     P.tile_tickets = stk_tickets;
+    P.ticket_stride = max_tiles;
+    P.cnt = stk_cnt;
+    P.tot = stk_tot;
     P.sync = stk_sync;
     P.err = err_dev;
   }
@@ -1205,6 +1288,7 @@ void enqueue_role_persistent(ls_engine& e, int role, int n, const PostOpts& po) 
   P = e.stk_base;
   P.phases = e.progs_dev + e.prog_off[prog];
   P.n_phases = e.prog_len[prog];
+  P.n_cnt = e.prog_cnt[prog];
   P.meta = meta;
   P.n = n;
   P.head_lane0 = role == kPost ? po.head_lane0 : 0;
@@ -2375,7 +2459,7 @@ int ls_trace_role(ls_engine* e, int role, int n, int context_len, uint64_t* out,
             "context_len must not exceed the prompt");
     const int prog = role == kPre ? ls_engine::kProgPre : role == kCore ? ls_engine::kProgCore
                                                                         : ls_engine::kProgPostHead;
-    const long entries = (long)(e->prog_len[prog] + 1) * e->num_sms * kStkTraceFields;
+    const long entries = (long)(e->prog_len[prog] + 1) * e->num_sms * kStkTraceFields + 4 * 4096;
     REQUIRE(entries <= max_entries, LS_ECAPACITY, "trace buffer too small");
     const bool attn = role == kCore || (role == kPre && e->mc.n_pre_layers) ||
                       (role == kPost && e->mc.n_post_layers);

@@ -30,14 +30,20 @@
 // points depend only on (M, K, grid), never on the lanes, so a lane's result
 // does not depend on the batch it runs in.
 //
-// Phase ordering: after a CTA finishes phase p it adds 1 to the counter
-// sync[1]. Before it starts or arrives for phase p it waits until
-// sync[1] >= grid * p. A CTA is therefore never more than one phase ahead of
-// the slowest, and sync[1] >= grid * (p + 1) proves phase p complete on all
-// CTAs. All CTAs must be co-resident (one per SM, checked by a start counter
-// with a bounded wait). Every wait is bounded: on timeout the CTA records an
-// error, stops issuing work, waits for its own copies and MMAs in flight,
-// frees its TMEM and exits. Other CTAs see the error word and exit too.
+// Ordering is dataflow, not phase barriers. Each unit of work publishes a
+// completion counter after its writes (a GEMM tile, an attention (lane, kv
+// head) merge, a per-lane row), and each consumer waits only for the counters
+// of what it reads: attention for kv head g waits for the QKV tiles holding
+// g's q, k, v rows; an O-projection activation box for the heads it covers; a
+// down-projection box for the one gate/up tile that produced it; a row for
+// all tiles of its GEMM. Every buffer reuse is ordered through these chains
+// (a GEMM phase transitively waits for all tiles of the GEMM two before it),
+// so partial slots and tile tickets alternate between two sets by GEMM parity.
+// All CTAs must be co-resident (one per SM, checked by a start counter with a
+// bounded wait). Every wait is bounded: on timeout the CTA records an error,
+// stops issuing work, waits for its own copies and MMAs in flight, frees its
+// TMEM and exits; other CTAs see the error word and exit too. The last CTA to
+// exit zeroes the counters for the next launch.
 #pragma once
 
 #include "common.cuh"
@@ -48,8 +54,10 @@ namespace ls {
 
 template <int BN, int ST>
 struct StkSmem {
-  static constexpr int kA = kGemmBM * kGemmBK * 2;
-  static constexpr int kB = BN * kGemmBK * 2;
+  static constexpr int kSubA = kGemmBM * kGemmBK * 2;   // one 128 x 64 weight sub-tile
+  static constexpr int kSubB = BN * kGemmBK * 2;         // one BN x 64 activation sub-tile
+  static constexpr int kA = kSubA * kStkSub;
+  static constexpr int kB = kSubB * kStkSub;
   static constexpr int kStage = kA + kB;
   static constexpr int kRing = ST * kStage;
   static constexpr int kWork = 12288;           // worker scratch
@@ -109,6 +117,16 @@ __device__ __forceinline__ void stk_trace(const StackParams& P, int phase, int f
   if (P.trace) P.trace[((long)phase * gridDim.x + blockIdx.x) * kStkTraceFields + field] = gtime_ns();
 }
 
+// CTA 0's per-stage event log after the phase table (trace runs only):
+// [4][kStkLogMax] SM clocks of weight issue, activation issue, MMA take of
+// ring stage i, and of the input-frontier fences (by fence count).
+constexpr int kStkLogMax = 4096;
+__device__ __forceinline__ void stk_log(const StackParams& P, int kind, long long i) {
+  if (P.trace && blockIdx.x == 0 && i < kStkLogMax)
+    P.trace[(long)(P.n_phases + 1) * gridDim.x * kStkTraceFields + kind * kStkLogMax + i] =
+        (unsigned long long)clock64();
+}
+
 __device__ __forceinline__ void stk_trace_value(const StackParams& P, int phase, int field,
                                                 unsigned long long v) {
   if (P.trace) P.trace[((long)phase * gridDim.x + blockIdx.x) * kStkTraceFields + field] = v;
@@ -148,6 +166,31 @@ __device__ __forceinline__ unsigned ld_relaxed(const unsigned* p) {
 
 __device__ __forceinline__ void fence_acquire_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
 
+__device__ __forceinline__ int ld_acquire_s32(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Counter update with release semantics (cumulative over the writes of the
+// threads that synchronised with this one through a CTA barrier).
+__device__ __forceinline__ void red_release_add(int* p, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ int atom_acq_rel_add(int* p, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
+// Activations of decode widths (BN <= 32, up to 16 lanes) are copied into the
+// ring by a warp with L2 loads (generic proxy); wider calls use TMA boxes.
+template <int BN>
+struct ActPath {
+  static constexpr bool kLdg = BN <= 32;
+};
+
 // Time-bounded wait until *ctr >= target, with acquire semantics on success
 // (relaxed polls, then a fence). Gives up when another CTA has recorded an
 // error (checked every 16 polls) or after limit_ns.
@@ -156,7 +199,7 @@ __device__ __forceinline__ bool grid_wait(const unsigned* ctr, unsigned target, 
   const unsigned long long t0 = gtime_ns();
   for (uint32_t i = 0;; ++i) {
     if (ld_relaxed(ctr) >= target) {
-      fence_acquire_gpu();
+      ld_acquire(ctr);   // acquire (the counter only grows)
       return true;
     }
     if ((i & 15u) == 15u) {
@@ -167,6 +210,7 @@ __device__ __forceinline__ bool grid_wait(const unsigned* ctr, unsigned target, 
         break;
       }
     }
+    __nanosleep(kStkPollNs);   // back off: many CTAs poll the same few lines
   }
   *abort_ = 1;
   return false;
@@ -174,13 +218,45 @@ __device__ __forceinline__ bool grid_wait(const unsigned* ctr, unsigned target, 
 
 // Sum over the 192 worker threads; `red` holds 8 floats. Fixed order.
 __device__ __forceinline__ float worker_sum(float v, float* red) {
-  const int lane = threadIdx.x & 31, w = (threadIdx.x >> 5) - 2;
+  const int lane = threadIdx.x & 31, w = (threadIdx.x >> 5) - kStkWorkerTid0 / 32;
   v = warp_sum(v);
   named_bar(kBarWorkers, kStkWorkers);
   if (lane == 0) red[w] = v;
   named_bar(kBarWorkers, kStkWorkers);
   float t = lane < 6 ? red[lane] : 0.f;
   return warp_sum(t);
+}
+
+// Completion target of a phase-level dependency.
+__device__ __forceinline__ int dep_tot_target(const StackParams& P, int kind, int q) {
+  return kind == kDepTotLanes ? P.n : kind == kDepTotTiles ? P.phases[q].m_tiles : 0;
+}
+
+// One thread: wait for the phase-level (tot) dependencies of `ph`.
+__device__ __forceinline__ bool wait_tot_deps(const StackParams& P, const Phase& ph, volatile int* abort_) {
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int k = ph.dep_kind[i];
+    if (k != kDepTotLanes && k != kDepTotTiles) continue;
+    const int q = ph.dep_phase[i];
+    if (!grid_wait(reinterpret_cast<const unsigned*>(P.tot + q), (unsigned)dep_tot_target(P, k, q), abort_,
+                   P.err, kDevTimeoutGrid, kStkWaitNs))
+      return false;
+  }
+  return true;
+}
+
+// Publish work done by the 192 workers (or the 128 epilogue threads, `nthreads`):
+// after a CTA barrier one thread adds to the counters with release semantics,
+// which covers the barrier's participants' writes. `proxy`: the outputs are
+// read by TMA (async proxy), so each writer also fences its writes for it.
+__device__ __forceinline__ void publish(int bar, int nthreads, bool leader, int* c1, int* c2, bool proxy) {
+  if (proxy) fence_proxy_async_global();   // consumers read through TMA
+  named_bar(bar, nthreads);
+  if (leader) {
+    if (c1) red_release_add(c1, 1);
+    if (c2) red_release_add(c2, 1);
+  }
 }
 
 // This CTA's k-block range of a GEMM phase (empty if it takes no part).
@@ -215,6 +291,8 @@ __device__ __forceinline__ int2 tile_ctas(int t, int KB, int T, int Gw) {
 struct KbIter {
   int p, f, lo, hi;
   int KB, epi, xbuf, head, wmap;
+  int dep_kind[2], dep_off[2], dep_target[2];   // activation inputs (counter index, target)
+  int dep_kdim[2];                              // K of this GEMM (bounds a unit's columns)
   __device__ __forceinline__ void seek(const StackParams& P, int from) {
     for (p = from; p < P.n_phases; ++p) {
       const Phase& ph = P.phases[p];
@@ -228,6 +306,22 @@ struct KbIter {
         xbuf = ph.xbuf;
         head = ph.head;
         wmap = ph.wmap;
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          const int k = ph.dep_kind[i], q = ph.dep_phase[i];
+          dep_kind[i] = k;
+          dep_kdim[i] = ph.K;
+          if (k == kDepTotLanes || k == kDepTotTiles) {
+            dep_off[i] = q;
+            dep_target[i] = dep_tot_target(P, k, q);
+          } else if (k == kDepKbHead || k == kDepKbTile) {
+            dep_off[i] = P.phases[q].cnt_off;
+            dep_target[i] = k == kDepKbHead ? P.n : 1;
+          } else {
+            dep_off[i] = 0;
+            dep_target[i] = 0;
+          }
+        }
         return;
       }
     }
@@ -237,6 +331,36 @@ struct KbIter {
     if (++f == hi) seek(P, p + 1);
   }
 };
+
+// Inputs of k-unit f (columns [u * kStkBK, +kStkBK) of the GEMM's K) that are
+// produced piecewise: the attention kv heads covering those columns (O
+// projection), or the two 64-column gate/up tiles that wrote them (down
+// projection). ACQ: acquire loads; else relaxed (the caller fences).
+template <bool ACQ>
+__device__ __forceinline__ bool unit_inputs_ready(const StackParams& P, const KbIter& a, int f, int G) {
+  const int c0 = (f % a.KB) * kStkBK;
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int k = a.dep_kind[i];
+    int lo, hi;
+    if (k == kDepKbHead) {
+      const int qd = P.NH * P.HD;
+      lo = c0 / (P.HD * G);
+      hi = (min(c0 + kStkBK, qd) - 1) / (P.HD * G);
+    } else if (k == kDepKbTile) {
+      lo = c0 / kGemmBK;
+      hi = (min(c0 + kStkBK, a.dep_kdim[i]) - 1) / kGemmBK;
+    } else {
+      continue;
+    }
+    for (int x = lo; x <= hi; ++x) {
+      const int* c = P.cnt + a.dep_off[i] + x;
+      const int v = ACQ ? ld_acquire_s32(c) : (int)ld_relaxed(reinterpret_cast<const unsigned*>(c));
+      if (v < a.dep_target[i]) return false;
+    }
+  }
+  return true;
+}
 
 // ----------------------------------------------------------- TMA producers
 // Weights (warp 0): walk the CTA's k-blocks across all GEMM phases and issue
@@ -255,25 +379,34 @@ __device__ void stk_weights(const StackLaunch& L, uint8_t* smem, uint32_t full0,
   KbIter w;
   w.seek(P, 0);
   long long iw = 0;
+  int s = 0;
+  uint32_t use = 0;   // how many times stage s has been filled before
   while (w.valid(P)) {
-    const int s = (int)(iw % ST);
-    if (iw >= ST && !stk_wait(empty0 + 8 * s, (uint32_t)((iw / ST - 1) & 1), abort_, P.err, kDevTimeoutEmpty))
-      break;
+    if (use > 0 && !stk_wait(empty0 + 8 * s, (use - 1) & 1, abort_, P.err, kDevTimeoutEmpty)) break;
     const uint32_t fb = full0 + 8 * s;
-    mbar_expect_tx(fb, S::kStage);
-    const int t = w.f / w.KB, kc = (w.f % w.KB) * kGemmBK;
-    const uint32_t dst = smem_u32(smem + s * S::kStage);
+    mbar_expect_tx(fb, ActPath<BN>::kLdg ? S::kA : S::kStage);   // weights (+ a TMA activation box)
+    const int t = w.f / w.KB, kc0 = (w.f % w.KB) * kStkBK;
     const CUtensorMap* wm = &L.wmap[w.wmap];
-    if (w.epi == kEpiSwiGLU) {
-      // 64 gate rows and the matching 64 up rows
-      tma_load_2d(dst, wm, fb, kc, t * (kGemmBM / 2));
-      tma_load_2d(dst + kGemmBM / 2 * kGemmBK * 2, wm, fb, kc, P.I + t * (kGemmBM / 2));
-    } else {
-      tma_load_2d(dst, wm, fb, kc, t * kGemmBM);
+#pragma unroll
+    for (int u = 0; u < kStkSub; ++u) {
+      const uint32_t dst = smem_u32(smem + s * S::kStage + u * S::kSubA);
+      const int kc = kc0 + u * kGemmBK;   // past K: the box reads the zero fill
+      if (w.epi == kEpiSwiGLU) {
+        // 64 gate rows and the matching 64 up rows
+        tma_load_2d(dst, wm, fb, kc, t * (kGemmBM / 2));
+        tma_load_2d(dst + kGemmBM / 2 * kGemmBK * 2, wm, fb, kc, P.I + t * (kGemmBM / 2));
+      } else {
+        tma_load_2d(dst, wm, fb, kc, t * kGemmBM);
+      }
     }
+    stk_log(P, 0, iw);
     w.step(P);
     ++iw;
     *s_iw = iw;
+    if (++s == ST) {
+      s = 0;
+      ++use;
+    }
   }
   __threadfence_block();   // the final count is visible before the done flag
   *s_wdone = 1;
@@ -287,21 +420,55 @@ __device__ void stk_acts(const StackLaunch& L, uint8_t* smem, uint32_t full0, vo
   KbIter a;
   a.seek(P, 0);
   long long ia = 0;
-  int ready = 0;           // phases known complete on every CTA
   bool waited = false;     // griddepcontrol.wait done
   uint32_t polls = 0;
+  const int G = P.NH / P.NKV;
   const int head_row0 = 2 * P.head_lane0;
+  int sa = 0;   // ring stage of activation ia
   auto issue = [&]() {
-    const int s = (int)(ia % ST);
-    tma_load_2d(smem_u32(smem + s * S::kStage + S::kA), &L.xmap[a.xbuf], full0 + 8 * (uint32_t)s,
-                (a.f % a.KB) * kGemmBK, a.head ? head_row0 : 0);
+#pragma unroll
+    for (int u = 0; u < kStkSub; ++u)
+      tma_load_2d(smem_u32(smem + sa * S::kStage + S::kA + u * S::kSubB), &L.xmap[a.xbuf],
+                  full0 + 8 * (uint32_t)sa, (a.f % a.KB) * kStkBK + u * kGemmBK, a.head ? head_row0 : 0);
+    stk_log(P, 1, ia);
     a.step(P);
     ++ia;
+    if (++sa == ST) sa = 0;
+  };
+  long long n_fences = 0;
+  // Inputs are known complete for the stages of phase known_p below f = known_f.
+  // A check extends that frontier over up to 8 k-blocks at once, and only an
+  // extension pays the acquire and proxy fences.
+  int known_p = -1, known_f = 0;
+  auto kb_ready = [&](int f) -> bool { return unit_inputs_ready<false>(P, a, f, G); };
+  auto inputs_ready = [&]() -> bool {   // true: the stage at a.f may load (fences done)
+    if (known_p == a.p && a.f < known_f) return true;
+    if (known_p != a.p) {
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int k = a.dep_kind[i];
+        if ((k == kDepTotLanes || k == kDepTotTiles) &&
+            (int)ld_relaxed(reinterpret_cast<const unsigned*>(P.tot + a.dep_off[i])) < a.dep_target[i])
+          return false;
+      }
+      known_p = a.p;
+      known_f = a.f;
+    }
+    int f = known_f;
+    const int lim = min(a.hi, known_f + 8);
+    while (f < lim && kb_ready(f)) ++f;
+    if (f == known_f) return false;
+    known_f = f;
+    fence_acquire_gpu();
+    fence_proxy_async_global();            // generic writes of the producers -> TMA reads
+    stk_log(P, 3, n_fences++);
+    return true;
   };
   unsigned long long idle_since = 0;
   uint32_t idles = 0;
   auto idle = [&]() -> bool {   // false: give up
     if (*abort_) return false;
+    __nanosleep(kStkPollNs);
     if ((++idles & 63u) != 0) return true;
     const unsigned long long now = gtime_ns();
     if (idle_since == 0) idle_since = now;
@@ -324,24 +491,21 @@ __device__ void stk_acts(const StackLaunch& L, uint8_t* smem, uint32_t full0, vo
       if (!idle()) break;
       continue;
     }
-    if (ready < a.p) {
-      if (!waited) {
-        pdl_wait();
-        waited = true;
+    if (!waited) {
+      pdl_wait();
+      waited = true;
+    }
+    if (!inputs_ready()) {
+      if ((++polls & 15u) == 0 && ld_volatile(P.err) != 0) {
+        *abort_ = 1;
+        break;
       }
-      ready = (int)(ld_relaxed(P.sync + 1) / gridDim.x);
-      if (ready < a.p) {
-        if ((++polls & 15u) == 0 && ld_volatile(P.err) != 0) {
-          *abort_ = 1;
-          break;
-        }
-        if (!idle()) break;
-        continue;
-      }
-      fence_acquire_gpu();
+      if (!idle()) break;
+      continue;
+    }
+    if (P.trace && a.f == a.lo) {
       stk_trace(P, a.p, 6);
-      if (P.trace) stk_trace_value(P, a.p, 11, (unsigned long long)min((long long)(a.hi - a.f), *s_iw - ia));
-      fence_proxy_async_global();            // generic writes of earlier phases -> TMA reads
+      stk_trace_value(P, a.p, 11, (unsigned long long)min((long long)(a.hi - a.f), *s_iw - ia));
     }
     idle_since = 0;
     idles = 0;
@@ -365,6 +529,156 @@ __device__ void stk_acts(const StackLaunch& L, uint8_t* smem, uint32_t full0, vo
     stk_drain(full0 + 8 * (uint32_t)(i % ST), (uint32_t)((i / ST) & 1));
 }
 
+// Activations for decode widths (BN <= 32), by the whole warp 2: lane 0 finds
+// how many consecutive stages may be filled (weight box issued, inputs
+// complete -- acquire loads of the producers' counters, no fences), then the
+// 32 lanes copy up to NB stages' BN x 64 bf16 tiles from L2 into the ring in
+// the 128-byte-swizzled layout the MMA descriptors expect, fence the shared
+// writes for the tensor cores (async proxy) and arrive on each stage's full
+// barrier (its second arrival; the weight box brings the transaction bytes).
+template <int BN, int ST>
+__device__ void stk_acts_ldg(const StackLaunch& L, uint8_t* smem, uint32_t full0, volatile int* abort_,
+                             volatile long long* s_iw, volatile int* s_wdone) {
+  using S = StkSmem<BN, ST>;
+  const StackParams& P = L.P;
+  const int lane = threadIdx.x & 31;
+  constexpr int CPL = BN * 8 * kStkSub / 32;        // 16-byte chunks per lane per stage
+  static_assert(CPL <= 16, "activation copy keeps at most 16 chunks per lane in flight");
+  constexpr int NB = 16 / CPL;                      // stages per batch
+  KbIter a;
+  a.seek(P, 0);
+  long long ia = 0;
+  int sa = 0;
+  // lane 0 only: inputs known complete below known_f in phase known_p
+  int known_p = -1, known_f = 0;
+  bool waited = false;
+  unsigned long long idle_since = 0;
+  uint32_t idles = 0;
+  const int G = P.NH / P.NKV;
+  auto kb_ready = [&](int f) -> bool { return unit_inputs_ready<true>(P, a, f, G); };
+  for (;;) {
+    int nb = 0, stop = 0;
+    if (lane == 0) {
+      if (!a.valid(P) || *abort_) {
+        stop = 1;
+      } else {
+        if (!waited) {
+          pdl_wait();
+          waited = true;
+        }
+        if (known_p != a.p) {
+          bool ok = true;
+          bool per_kb = false;
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+            const int k = a.dep_kind[i];
+            if ((k == kDepTotLanes || k == kDepTotTiles) && ld_acquire_s32(P.tot + a.dep_off[i]) < a.dep_target[i])
+              ok = false;
+            per_kb |= k == kDepKbHead || k == kDepKbTile;
+          }
+          if (ok) {
+            known_p = a.p;
+            known_f = per_kb ? a.f : a.hi;
+          }
+        }
+        if (known_p == a.p)
+          while (known_f < a.hi && known_f < a.f + NB && kb_ready(known_f)) ++known_f;
+        const long long iw = *s_iw;
+        const long long lim = min(min((long long)NB, iw - ia), (long long)(a.hi - a.f));
+        nb = known_p == a.p ? (int)min(lim, (long long)(known_f - a.f)) : 0;
+        if (nb <= 0) {
+          nb = 0;
+          if (*s_wdone && ia >= *s_iw) {
+            *abort_ = 1;   // weights stopped early
+            stop = 1;
+          } else if ((++idles & 63u) == 0) {
+            const unsigned long long now = gtime_ns();
+            if (idle_since == 0) idle_since = now;
+            if (ld_volatile(P.err) != 0) {
+              *abort_ = 1;
+              stop = 1;
+            } else if (now - idle_since > kStkWaitNs) {
+              atomicExch(P.err, kDevTimeoutGrid);
+              *abort_ = 1;
+              stop = 1;
+            }
+          }
+        } else {
+          idle_since = 0;
+          idles = 0;
+          if (P.trace && a.f == a.lo) {
+            stk_trace(P, a.p, 6);
+            stk_trace(P, a.p, 3);
+            stk_trace_value(P, a.p, 11, (unsigned long long)min((long long)(a.hi - a.f), iw - ia));
+          }
+        }
+      }
+    }
+    stop = __shfl_sync(0xffffffffu, stop, 0);
+    nb = __shfl_sync(0xffffffffu, nb, 0);
+    if (stop) break;
+    if (nb == 0) {
+      __nanosleep(kStkPollNs);
+      continue;
+    }
+    // copy nb stages (same phase): all loads first, then the stores
+    const __nv_bfloat16* xb = P.x[a.xbuf];
+    const long K = P.xK[a.xbuf];
+    const int row0 = a.head ? 2 * P.head_lane0 : 0;
+    const int rows = 2 * (a.head ? P.head_n : P.n);
+    // chunk q of a stage: sub-tile q / (8 BN), row (q / 8) % BN, 16-byte chunk q % 8
+    uint4 v[NB][CPL];
+#pragma unroll
+    for (int k = 0; k < NB; ++k) {
+      const int kc = ((a.f + k) % a.KB) * kStkBK;
+#pragma unroll
+      for (int c = 0; c < CPL; ++c) {
+        const int q = lane + 32 * c, u = q / (8 * BN), r = (q >> 3) % BN, j = q & 7;
+        const int col = kc + u * kGemmBK + j * 8;
+        v[k][c] = (k < nb && r < rows && col < K)
+                      ? __ldcg(reinterpret_cast<const uint4*>(xb + (long)(row0 + r) * K + col))
+                      : make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < NB; ++k) {
+      if (k < nb) {
+        int st = sa + k;
+        if (st >= ST) st -= ST;
+        uint8_t* tile = smem + st * S::kStage + S::kA;
+#pragma unroll
+        for (int c = 0; c < CPL; ++c) {
+          const int q = lane + 32 * c, u = q / (8 * BN), r = (q >> 3) % BN, j = q & 7;
+          *reinterpret_cast<uint4*>(tile + u * S::kSubB + r * 128 + ((j ^ (r & 7)) << 4)) = v[k][c];
+        }
+        fence_proxy_async();   // shared writes -> tensor-core (async proxy) reads
+        __syncwarp();
+        if (lane == 0) mbar_arrive(full0 + 8 * (uint32_t)st);
+      }
+    }
+    if (lane == 0 && P.trace && a.f + nb == a.hi) stk_trace(P, a.p, 8);
+    for (int k = 0; k < nb; ++k) a.step(P);
+    ia += nb;
+    sa += nb;
+    if (sa >= ST) sa -= ST;
+  }
+  // Exit. Normally every stage has been filled. When aborting, arrive on the
+  // stages whose weight box was issued (their tiles are discarded) so their
+  // barriers complete, then wait until all boxes have landed.
+  if (lane == 0) {
+    const unsigned long long t0 = gtime_ns();
+    while (!*s_wdone && gtime_ns() - t0 < kStkWaitNs) __nanosleep(64);
+    const long long iw = *s_iw;
+    for (long long i = ia; i < iw; ++i) {
+      mbar_arrive(full0 + 8 * (uint32_t)sa);
+      if (++sa == ST) sa = 0;
+    }
+    if (ia < iw && ld_volatile(P.err) == 0) atomicExch(P.err, kDevTimeoutGrid);
+    for (long long i = iw > ST ? iw - ST : 0; i < iw; ++i)
+      stk_drain(full0 + 8 * (uint32_t)(i % ST), (uint32_t)((i / ST) & 1));
+  }
+}
+
 // ------------------------------------------------------------- MMA issuer
 // Segment j accumulates into TMEM columns [(j & 1) * BN, +BN); before reusing
 // a buffer it waits until the epilogue warps have read segment j - 2.
@@ -378,6 +692,8 @@ __device__ void stk_mma(const StackParams& P, uint8_t* smem, uint32_t full0, uin
   m.seek(P, 0);
   long i = 0;
   int seg = 0;
+  int ms = 0;          // ring stage of k-block i
+  uint32_t mpar = 0;   // its fill parity
   while (m.valid(P) && !*abort_) {
     const int p0 = m.p;
     const int t = m.f / m.KB;
@@ -390,22 +706,31 @@ __device__ void stk_mma(const StackParams& P, uint8_t* smem, uint32_t full0, uin
     const uint32_t d = tmem + (uint32_t)(b * BN);
     bool first = true, ok = true;
     do {
-      const int s = (int)(i % ST);
-      if (!stk_wait(full0 + 8 * s, (uint32_t)((i / ST) & 1), abort_, P.err, kDevTimeoutFull)) {
+      const int s = ms;
+      if (!stk_wait(full0 + 8 * s, mpar, abort_, P.err, kDevTimeoutFull)) {
         ok = false;
         break;
       }
       tc_fence_after();
+      stk_log(P, 2, i);
       if (P.trace && first && m.f == seg_lo) stk_trace(P, p0, 9);
       const uint32_t a_s = smem_u32(smem + s * S::kStage);
       const uint32_t b_s = a_s + S::kA;
 #pragma unroll
-      for (int k = 0; k < kGemmBK / 16; ++k)
-        tc_mma_bf16(d, umma_desc_sw128(a_s + 32 * k), umma_desc_sw128(b_s + 32 * k), idesc,
-                    (first && k == 0) ? 0u : 1u);
+      for (int u = 0; u < kStkSub; ++u)
+#pragma unroll
+        for (int k = 0; k < kGemmBK / 16; ++k)
+          tc_mma_bf16(d, umma_desc_sw128(a_s + u * S::kSubA + 32 * k),
+                      umma_desc_sw128(b_s + u * S::kSubB + 32 * k), idesc, (first && u == 0 && k == 0) ? 0u : 1u);
       first = false;
+      stk_log(P, 1, i);
       tc_commit(empty0 + 8 * s);
+      stk_log(P, 3, i);
       ++i;
+      if (++ms == ST) {
+        ms = 0;
+        mpar ^= 1u;
+      }
       m.step(P);
     } while (m.valid(P) && m.p == p0 && m.f < send);
     if (!ok) break;
@@ -421,9 +746,11 @@ __device__ void stk_mma(const StackParams& P, uint8_t* smem, uint32_t full0, uin
 }
 
 // ---------------------------------------------------------- GEMM epilogue
-// Partial slot of CTA c for tile t: 0 if t is the CTA's first segment, else 1.
-__device__ __forceinline__ float* seg_slot(const StackParams& P, int BNh, int c, int slot) {
-  return P.part_ws + (long)(c * 2 + slot) * BNh * kGemmBM;
+// Partial slot of CTA c for tile t: 0 if t is the CTA's first segment, else 1;
+// two sets, by the parity of the GEMM phase (a GEMM phase transitively waits
+// for every tile of the GEMM phase two before it, never for the one before).
+__device__ __forceinline__ float* seg_slot(const StackParams& P, int BNh, int par, int c, int slot) {
+  return P.part_ws + (long)((par * (int)gridDim.x + c) * 2 + slot) * BNh * kGemmBM;
 }
 
 // Sum tile t's partials over its contributors in CTA order and apply the
@@ -459,7 +786,7 @@ __device__ void stk_gemm_finish(const StackParams& P, const Phase& ph, int t, in
         a1[j] = 0.f;
         if (c <= cc.y) {
           const int lo_c = (int)((long)c * rg.T / rg.Gw);
-          const float* pp = seg_slot(P, BN / 2, c, lo_c >= t * ph.KB ? 0 : 1) + l * kGemmBM;
+          const float* pp = seg_slot(P, BN / 2, ph.gemm_idx & 1, c, lo_c >= t * ph.KB ? 0 : 1) + l * kGemmBM;
           a0[j] = __ldcg(pp + r0);
           a1[j] = __ldcg(pp + r1);
         }
@@ -532,7 +859,7 @@ __device__ bool stk_gemm_epilogue(const StackParams& P, const Phase& ph, int pha
     named_bar(kBarEpi, 128);
     if (!s_flag[0]) return false;
     tc_fence_after();
-    float* mine = seg_slot(P, BN / 2, blockIdx.x, rg.lo >= t * ph.KB ? 0 : 1);
+    float* mine = seg_slot(P, BN / 2, ph.gemm_idx & 1, blockIdx.x, rg.lo >= t * ph.KB ? 0 : 1);
     const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * BN);
 #pragma unroll 1
     for (int c0 = 0; c0 < 2 * lanes; c0 += 8) {
@@ -547,22 +874,25 @@ __device__ bool stk_gemm_epilogue(const StackParams& P, const Phase& ph, int pha
     }
     tc_fence_before();
     mbar_arrive(acce0 + 8 * b);
-    __threadfence();
     named_bar(kBarEpi, 128);
     const int2 cc = tile_ctas(t, ph.KB, rg.T, rg.Gw);
     bool last = true;
     if (cc.x != cc.y) {
+      // the ticket releases this CTA's partial (written by the 128 threads
+      // before the barrier) and acquires the others' for the last one
       if (et == 0) {
-        int* tk = P.tile_tickets + t;
-        const int ticket = atomicAdd(tk, 1);
+        int* tk = P.tile_tickets + (ph.gemm_idx & 1) * P.ticket_stride + t;
+        const int ticket = atom_acq_rel_add(tk, 1);
         s_flag[1] = ticket == cc.y - cc.x;
-        if (s_flag[1]) *tk = 0;   // all contributors arrived: ready for the next phase
+        if (s_flag[1]) *tk = 0;   // all contributors arrived: ready for the next use
       }
       named_bar(kBarEpi, 128);
       last = s_flag[1] != 0;
-      if (last) __threadfence();
     }
-    if (last) stk_gemm_finish<BN>(P, ph, t, cc, rg, lanes);
+    if (last) {
+      stk_gemm_finish<BN>(P, ph, t, cc, rg, lanes);
+      publish(kBarEpi, 128, et == 0, P.cnt + ph.cnt_off + t, P.tot + phase, !ActPath<BN>::kLdg);   // tile t stored
+    }
     named_bar(kBarEpi, 128);   // slot and flags free for the next segment
     ++seg;
     f = send;
@@ -582,8 +912,36 @@ __device__ bool stk_gemm_epilogue(const StackParams& P, const Phase& ph, int pha
 // at a time with a running max, and writes the O projection's (hi, lo) input.
 // Chunk boundaries are fixed multiples of kStkChunk and positions map to
 // sub-groups by index, so results do not depend on the batch.
+// Inputs of the attention items of kv head g: the QKV tiles holding g's q, k
+// and v rows (or the QK-norm phase), and the timeline mapping update.
+__device__ __forceinline__ bool wait_attn_inputs(const StackParams& P, const Phase& ph, int g,
+                                                 volatile int* abort_) {
+  const int G = P.NH / P.NKV, HD = P.HD, QD = P.NH * HD, KVD = P.NKV * HD;
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int k = ph.dep_kind[i], q = ph.dep_phase[i];
+    if (k == kDepQkvHead) {
+      const int* c = P.cnt + P.phases[q].cnt_off;
+      const int ranges[3][2] = {{g * G * HD, (g + 1) * G * HD},
+                                {QD + g * HD, QD + (g + 1) * HD},
+                                {QD + KVD + g * HD, QD + KVD + (g + 1) * HD}};
+      for (int r = 0; r < 3; ++r)
+        for (int t = ranges[r][0] / kGemmBM; t <= (ranges[r][1] - 1) / kGemmBM; ++t)
+          if (!grid_wait(reinterpret_cast<const unsigned*>(c + t), 1u, abort_, P.err, kDevTimeoutGrid,
+                         kStkWaitNs))
+            return false;
+    } else if (k == kDepTotLanes || k == kDepTotTiles) {
+      if (!grid_wait(reinterpret_cast<const unsigned*>(P.tot + q), (unsigned)dep_tot_target(P, k, q), abort_,
+                     P.err, kDevTimeoutGrid, kStkWaitNs))
+        return false;
+    }
+  }
+  return true;
+}
+
 template <int HD>
-__device__ void stk_attention(const StackParams& P, const Phase& ph, uint8_t* work) {
+__device__ bool stk_attention(const StackParams& P, const Phase& ph, int phase, uint8_t* work,
+                              volatile int* abort_, int* s_flag, bool proxy) {
   constexpr int GM = HD == 128 ? 2 : 4;      // query heads per KV head supported
   constexpr int LPP = HD / 8;
   constexpr int PPW = 32 / LPP;
@@ -635,6 +993,11 @@ __device__ void stk_attention(const StackParams& P, const Phase& ph, uint8_t* wo
     const int nch = (s_pref[b + 1] - s_pref[b]) / P.NKV;
     const int rem = it - s_pref[b];
     const int g = rem / nch, c = rem - g * nch;
+    if (wt == 0) s_flag[2] = wait_attn_inputs(P, ph, g, abort_);
+    named_bar(kBarWorkers, kStkWorkers);
+    if (!s_flag[2]) return false;
+    const bool first_item = it == (int)blockIdx.x;
+    if (wt == 0 && first_item) stk_trace(P, phase, 2);   // inputs complete
     const int T = P.meta.get(kMetaPos, b) + 1;
     const int row = P.meta.get(kMetaRow, b);
     const bool row_ok = row >= 0 && row < P.rows;
@@ -739,6 +1102,7 @@ __device__ void stk_attention(const StackParams& P, const Phase& ph, uint8_t* wo
       }
     }
     named_bar(kBarWorkers, kStkWorkers);
+    if (wt == 0 && first_item) stk_trace(P, phase, 4);   // scores and values done
     for (int t = wt; t < G * HD; t += kStkWorkers) {
       const int h = t / HD, d = t - h * HD;
       float mm = -INFINITY;
@@ -758,17 +1122,16 @@ __device__ void stk_attention(const StackParams& P, const Phase& ph, uint8_t* wo
         P.ml_part[idx * 2 + 1] = ll;
       }
     }
-    __threadfence();
     named_bar(kBarWorkers, kStkWorkers);
     if (wt == 0) {
       int* tk = P.attn_tickets + (long)b * P.NKV + g;
-      const int ticket = atomicAdd(tk, 1);
+      const int ticket = atom_acq_rel_add(tk, 1);   // releases this chunk, acquires the others
       s_last[0] = ticket == nch - 1;
       if (s_last[0]) *tk = 0;
     }
     named_bar(kBarWorkers, kStkWorkers);
+    if (wt == 0 && first_item) stk_trace(P, phase, 5);   // ticket taken
     if (s_last[0]) {
-      __threadfence();
       for (int t = wt; t < G * HD; t += kStkWorkers) {
         const int h = t / HD, d = t - h * HD;
         const long base = ((long)b * P.NH + g * G + h) * P.max_chunks;
@@ -804,14 +1167,16 @@ __device__ void stk_attention(const StackParams& P, const Phase& ph, uint8_t* wo
         }
         store_pair(P.x[kXAttn], (long)P.NH * HD, b, (g * G + h) * HD + d, ll > 0.f ? aa / ll : 0.f);
       }
+      publish(kBarWorkers, kStkWorkers, wt == 0, P.cnt + ph.cnt_off + g, P.tot + phase, proxy);   // (b, g) merged
     }
     named_bar(kBarWorkers, kStkWorkers);   // shared scratch free for the next item
   }
+  return true;
 }
 
 // ------------------------------------------------------------ per-lane rows
-// Rows run one lane per CTA (lanes dealt round-robin), 192 threads, each
-// thread holding NV float4 columns. With NV = 3 (H <= 2304, every preset)
+// Per-lane phases run one lane per call (lanes dealt to CTAs round-robin),
+// 192 threads, each thread holding NV float4 columns. With NV = 3 (H <= 2304, every preset)
 // all of a row's loads -- inputs, residual and the bf16 norm weights -- are
 // issued before the first use, so a row costs one memory round trip plus its
 // block reductions; larger rows (NV = 8) load the weights at use.
@@ -861,225 +1226,217 @@ __device__ __forceinline__ void stk_store_row(const StackParams& P, const Phase&
 // out = final_norm ? rms(out) * wf : out; then out_h / bank / x as in
 // resid_epi_kernel.
 template <int NV, bool UPFRONT>
-__device__ void stk_row_impl(const StackParams& P, const Phase& ph, float* red) {
+__device__ void stk_row_impl(const StackParams& P, const Phase& ph, int b, float* red) {
   const int wt = threadIdx.x - kStkWorkerTid0;
   const int H = P.H, H4 = H / 4;
-  for (int b = blockIdx.x; b < P.n; b += gridDim.x) {
-    float4 v[NV], rr[NV];
-    uint2 wa[UPFRONT ? NV : 1], wf[UPFRONT ? NV : 1], wx[UPFRONT ? NV : 1], bi[UPFRONT ? NV : 1];
+  float4 v[NV], rr[NV];
+  uint2 wa[UPFRONT ? NV : 1], wf[UPFRONT ? NV : 1], wx[UPFRONT ? NV : 1], bi[UPFRONT ? NV : 1];
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int j = wt + k * kStkWorkers;
+    const bool on = j < H4;
+    v[k] = on ? ldcg4(ph.src + (long)b * H + 4 * j) : make_float4(0.f, 0.f, 0.f, 0.f);
+    rr[k] = on && ph.resid ? ldcg4(ph.resid + (long)b * H + 4 * j) : make_float4(0.f, 0.f, 0.f, 0.f);
+    if (UPFRONT) {
+      wa[k] = on && ph.a_norm_w ? ldg_u2(ph.a_norm_w + 4 * j) : kBf16Ones;
+      wf[k] = on && ph.final_norm_w ? ldg_u2(ph.final_norm_w + 4 * j) : kBf16Ones;
+      wx[k] = on && ph.x_norm_w ? ldg_u2(ph.x_norm_w + 4 * j) : kBf16Ones;
+      bi[k] = on && ph.bias ? ldg_u2(ph.bias + 4 * j) : make_uint2(0u, 0u);
+    }
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int j = wt + k * kStkWorkers;
+    if (ph.bias && j < H4) v[k] = f4_add(v[k], UPFRONT ? bf4_of(bi[k]) : ld_bf4(ph.bias + 4 * j));
+    ss += f4_sq(v[k]);
+  }
+  if (ph.a_norm_w) {
+    const float inv = rsqrtf(worker_sum(ss, red) / H + P.eps);
 #pragma unroll
     for (int k = 0; k < NV; ++k) {
       const int j = wt + k * kStkWorkers;
-      const bool on = j < H4;
-      v[k] = on ? ldcg4(ph.src + (long)b * H + 4 * j) : make_float4(0.f, 0.f, 0.f, 0.f);
-      rr[k] = on && ph.resid ? ldcg4(ph.resid + (long)b * H + 4 * j) : make_float4(0.f, 0.f, 0.f, 0.f);
-      if (UPFRONT) {
-        wa[k] = on && ph.a_norm_w ? ldg_u2(ph.a_norm_w + 4 * j) : kBf16Ones;
-        wf[k] = on && ph.final_norm_w ? ldg_u2(ph.final_norm_w + 4 * j) : kBf16Ones;
-        wx[k] = on && ph.x_norm_w ? ldg_u2(ph.x_norm_w + 4 * j) : kBf16Ones;
-        bi[k] = on && ph.bias ? ldg_u2(ph.bias + 4 * j) : make_uint2(0u, 0u);
-      }
+      if (j < H4) v[k] = f4_scale(v[k], inv, UPFRONT ? bf4_of(wa[k]) : ld_bf4(ph.a_norm_w + 4 * j));
     }
-    float ss = 0.f;
+  }
+  ss = 0.f;
 #pragma unroll
-    for (int k = 0; k < NV; ++k) {
-      const int j = wt + k * kStkWorkers;
-      if (ph.bias && j < H4) v[k] = f4_add(v[k], UPFRONT ? bf4_of(bi[k]) : ld_bf4(ph.bias + 4 * j));
-      ss += f4_sq(v[k]);
-    }
-    if (ph.a_norm_w) {
-      const float inv = rsqrtf(worker_sum(ss, red) / H + P.eps);
-#pragma unroll
-      for (int k = 0; k < NV; ++k) {
-        const int j = wt + k * kStkWorkers;
-        if (j < H4) v[k] = f4_scale(v[k], inv, UPFRONT ? bf4_of(wa[k]) : ld_bf4(ph.a_norm_w + 4 * j));
-      }
-    }
+  for (int k = 0; k < NV; ++k) {
+    v[k] = f4_add(v[k], rr[k]);
+    ss += f4_sq(v[k]);
+  }
+  if (ph.final_norm_w) {
+    const float inv = rsqrtf(worker_sum(ss, red) / H + P.eps);
     ss = 0.f;
 #pragma unroll
     for (int k = 0; k < NV; ++k) {
-      v[k] = f4_add(v[k], rr[k]);
+      const int j = wt + k * kStkWorkers;
+      if (j < H4) v[k] = f4_scale(v[k], inv, UPFRONT ? bf4_of(wf[k]) : ld_bf4(ph.final_norm_w + 4 * j));
       ss += f4_sq(v[k]);
     }
-    if (ph.final_norm_w) {
-      const float inv = rsqrtf(worker_sum(ss, red) / H + P.eps);
-      ss = 0.f;
-#pragma unroll
-      for (int k = 0; k < NV; ++k) {
-        const int j = wt + k * kStkWorkers;
-        if (j < H4) v[k] = f4_scale(v[k], inv, UPFRONT ? bf4_of(wf[k]) : ld_bf4(ph.final_norm_w + 4 * j));
-        ss += f4_sq(v[k]);
-      }
-    }
-    stk_store_row<NV>(P, ph, b, v, ss, red, UPFRONT ? wx : nullptr);
   }
+  stk_store_row<NV>(P, ph, b, v, ss, red, UPFRONT ? wx : nullptr);
 }
 
-__device__ void stk_row(const StackParams& P, const Phase& ph, float* red) {
-  if (P.H <= 4 * 3 * kStkWorkers) stk_row_impl<3, true>(P, ph, red);
-  else stk_row_impl<kStkRowNV, false>(P, ph, red);
+__device__ void stk_row(const StackParams& P, const Phase& ph, int b, float* red) {
+  if (P.H <= 4 * 3 * kStkWorkers) stk_row_impl<3, true>(P, ph, b, red);
+  else stk_row_impl<kStkRowNV, false>(P, ph, b, red);
 }
 
 // h = embedding(token) * scale (src null) or src[state_in]; then out_h /
 // bank / x (prep_kernel semantics).
 template <int NV, bool UPFRONT>
-__device__ void stk_prep_impl(const StackParams& P, const Phase& ph, float* red) {
+__device__ void stk_prep_impl(const StackParams& P, const Phase& ph, int b, float* red) {
   const int wt = threadIdx.x - kStkWorkerTid0;
   const int H = P.H, H4 = H / 4;
-  for (int b = blockIdx.x; b < P.n; b += gridDim.x) {
-    int src;
-    if (!ph.src) {
-      src = P.meta.get(kMetaToken, b);
-      if (src < 0 || src >= P.vocab) src = -1;
-    } else {
-      src = P.meta.get(kMetaStateIn, b);
-      if (src < 0 || src >= P.bank_rows) src = -1;
-    }
-    if (src < 0 && wt == 0) atomicExch(P.err, kDevBadIndex);
-    float4 v[NV];
-    uint2 wx[UPFRONT ? NV : 1];
-    float ss = 0.f;
-#pragma unroll
-    for (int k = 0; k < NV; ++k) {
-      const int j = wt + k * kStkWorkers;
-      v[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (j < H4 && src >= 0) {
-        if (!ph.src) {
-          const float4 e = ld_bf4(P.embed + (long)src * H + 4 * j);
-          v[k] = make_float4(e.x * P.embed_scale, e.y * P.embed_scale, e.z * P.embed_scale,
-                             e.w * P.embed_scale);
-        } else {
-          v[k] = ldcg4(ph.src + (long)src * H + 4 * j);
-        }
-      }
-      if (UPFRONT) wx[k] = j < H4 && ph.x_norm_w ? ldg_u2(ph.x_norm_w + 4 * j) : kBf16Ones;
-      ss += f4_sq(v[k]);
-    }
-    stk_store_row<NV>(P, ph, b, v, ss, red, UPFRONT ? wx : nullptr);
+  int src;
+  if (!ph.src) {
+    src = P.meta.get(kMetaToken, b);
+    if (src < 0 || src >= P.vocab) src = -1;
+  } else {
+    src = P.meta.get(kMetaStateIn, b);
+    if (src < 0 || src >= P.bank_rows) src = -1;
   }
+  if (src < 0 && wt == 0) atomicExch(P.err, kDevBadIndex);
+  float4 v[NV];
+  uint2 wx[UPFRONT ? NV : 1];
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int j = wt + k * kStkWorkers;
+    v[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (j < H4 && src >= 0) {
+      if (!ph.src) {
+        const float4 e = ld_bf4(P.embed + (long)src * H + 4 * j);
+        v[k] = make_float4(e.x * P.embed_scale, e.y * P.embed_scale, e.z * P.embed_scale,
+                           e.w * P.embed_scale);
+      } else {
+        v[k] = ldcg4(ph.src + (long)src * H + 4 * j);
+      }
+    }
+    if (UPFRONT) wx[k] = j < H4 && ph.x_norm_w ? ldg_u2(ph.x_norm_w + 4 * j) : kBf16Ones;
+    ss += f4_sq(v[k]);
+  }
+  stk_store_row<NV>(P, ph, b, v, ss, red, UPFRONT ? wx : nullptr);
 }
 
-__device__ void stk_prep(const StackParams& P, const Phase& ph, float* red) {
-  if (P.H <= 4 * 3 * kStkWorkers) stk_prep_impl<3, true>(P, ph, red);
-  else stk_prep_impl<kStkRowNV, false>(P, ph, red);
+__device__ void stk_prep(const StackParams& P, const Phase& ph, int b, float* red) {
+  if (P.H <= 4 * 3 * kStkWorkers) stk_prep_impl<3, true>(P, ph, b, red);
+  else stk_prep_impl<kStkRowNV, false>(P, ph, b, red);
 }
 
 // Raven adapter input: x_cat[b] = (hi, lo) of [bank_h[state_in], bank_inj[state_in]].
-__device__ void stk_cat(const StackParams& P) {
+__device__ void stk_cat(const StackParams& P, int b) {
   const int wt = threadIdx.x - kStkWorkerTid0;
   const int H = P.H;
-  for (int b = blockIdx.x; b < P.n; b += gridDim.x) {
-    const int si = P.meta.get(kMetaStateIn, b);
-    if (si < 0 || si >= P.bank_rows) {
-      if (wt == 0) atomicExch(P.err, kDevBadIndex);
-      continue;
-    }
-    for (int j = wt; j < H / 4; j += kStkWorkers) {
-      store_pair4(P.x[kXCat], 2L * H, b, 4 * j, ldcg4(P.bank_h + (long)si * H + 4 * j));
-      store_pair4(P.x[kXCat], 2L * H, b, H + 4 * j, ldcg4(P.bank_inj + (long)si * H + 4 * j));
-    }
+  const int si = P.meta.get(kMetaStateIn, b);
+  if (si < 0 || si >= P.bank_rows) {
+    if (wt == 0) atomicExch(P.err, kDevBadIndex);
+    return;
+  }
+  for (int j = wt; j < H / 4; j += kStkWorkers) {
+    store_pair4(P.x[kXCat], 2L * H, b, 4 * j, ldcg4(P.bank_h + (long)si * H + 4 * j));
+    store_pair4(P.x[kXCat], 2L * H, b, H + 4 * j, ldcg4(P.bank_inj + (long)si * H + 4 * j));
   }
 }
 
 // Timeline mapping (map_update_kernel): fork copy, then row[pos] = slot.
-__device__ void stk_map(const StackParams& P) {
+__device__ void stk_map(const StackParams& P, int b) {
   const int wt = threadIdx.x - kStkWorkerTid0;
-  for (int b = blockIdx.x; b < P.n; b += gridDim.x) {
-    const int row = P.meta.get(kMetaRow, b), pos = P.meta.get(kMetaPos, b);
-    const int frow = P.meta.get(kMetaForkRow, b), flen = P.meta.get(kMetaForkLen, b);
-    if (row < 0 || row >= P.rows || pos < 0 || pos >= P.max_ctx ||
-        (frow >= 0 && (frow >= P.rows || flen > P.max_ctx))) {
-      if (wt == 0) atomicExch(P.err, kDevBadIndex);
-      continue;
-    }
-    int* dst = P.map + (long)row * P.max_ctx;
-    if (frow >= 0) {
-      const int* src = P.map + (long)frow * P.max_ctx;
-      for (int j = wt; j < flen; j += kStkWorkers) dst[j] = __ldcg(src + j);
-    }
-    if (wt == 0) dst[pos] = P.meta.get(kMetaSlot, b);
+  const int row = P.meta.get(kMetaRow, b), pos = P.meta.get(kMetaPos, b);
+  const int frow = P.meta.get(kMetaForkRow, b), flen = P.meta.get(kMetaForkLen, b);
+  if (row < 0 || row >= P.rows || pos < 0 || pos >= P.max_ctx ||
+      (frow >= 0 && (frow >= P.rows || flen > P.max_ctx))) {
+    if (wt == 0) atomicExch(P.err, kDevBadIndex);
+    return;
   }
+  int* dst = P.map + (long)row * P.max_ctx;
+  if (frow >= 0) {
+    const int* src = P.map + (long)frow * P.max_ctx;
+    for (int j = wt; j < flen; j += kStkWorkers) dst[j] = __ldcg(src + j);
+  }
+  if (wt == 0) dst[pos] = P.meta.get(kMetaSlot, b);
 }
 
 // OLMo2 QK-norm over the stored QKV row of each lane (src [lanes][D]), neox
 // RoPE, K/V written to the layer's pools, q kept in fp32 (qkv_epi_kernel).
-__device__ void stk_qknorm(const StackParams& P, const Phase& ph, float* red) {
+__device__ void stk_qknorm(const StackParams& P, const Phase& ph, int b, float* red) {
   const int wt = threadIdx.x - kStkWorkerTid0;
   const int hd = P.HD, half = hd / 2;
   const int qd = P.NH * hd, kd = P.NKV * hd, D = qd + 2 * kd;
-  for (int b = blockIdx.x; b < P.n; b += gridDim.x) {
-    const float* row = ph.src + (long)b * D;
-    float ssq = 0.f, ssk = 0.f;
-    for (int i = wt; i < qd + kd; i += kStkWorkers) {
-      const float v = __ldcg(row + i);
-      if (i < qd) ssq += v * v;
-      else ssk += v * v;
-    }
-    const float iq = rsqrtf(worker_sum(ssq, red) / qd + P.eps);
-    const float ik = rsqrtf(worker_sum(ssk, red) / kd + P.eps);
-    const int pos = P.meta.get(kMetaPos, b);
-    const int slot = P.meta.get(kMetaSlot, b);
-    const bool slot_ok = slot >= 0 && slot < P.n_slots;
-    if (!slot_ok && wt == 0) atomicExch(P.err, kDevBadIndex);
-    const int pairs = (P.NH + P.NKV) * half;
-    for (int t = wt; t < pairs; t += kStkWorkers) {
-      const int head = t / half, i = t - head * half;
-      const int base = head * hd;
-      const bool isq = head < P.NH;
-      const float sc = isq ? iq : ik;
-      const __nv_bfloat16* nw = isq ? ph.q_norm_w + base : ph.k_norm_w + (base - qd);
-      const float x1 = __ldcg(row + base + i) * sc * bf2f(nw[i]);
-      const float x2 = __ldcg(row + base + i + half) * sc * bf2f(nw[i + half]);
-      float sn, cs;
-      sincosf((float)pos * P.inv_freq[i], &sn, &cs);
-      const float y1 = x1 * cs - x2 * sn, y2 = x2 * cs + x1 * sn;
-      if (isq) {
-        P.q[(long)b * qd + base + i] = y1;
-        P.q[(long)b * qd + base + i + half] = y2;
-      } else if (slot_ok) {
-        __nv_bfloat16* kr = ph.kpool + (long)slot * kd + (base - qd);
-        kr[i] = f2bf(y1);
-        kr[i + half] = f2bf(y2);
-      }
-    }
-    if (slot_ok)
-      for (int i = wt; i < kd; i += kStkWorkers)
-        ph.vpool[(long)slot * kd + i] = f2bf(__ldcg(row + qd + kd + i));
+  const float* row = ph.src + (long)b * D;
+  float ssq = 0.f, ssk = 0.f;
+  for (int i = wt; i < qd + kd; i += kStkWorkers) {
+    const float v = __ldcg(row + i);
+    if (i < qd) ssq += v * v;
+    else ssk += v * v;
   }
+  const float iq = rsqrtf(worker_sum(ssq, red) / qd + P.eps);
+  const float ik = rsqrtf(worker_sum(ssk, red) / kd + P.eps);
+  const int pos = P.meta.get(kMetaPos, b);
+  const int slot = P.meta.get(kMetaSlot, b);
+  const bool slot_ok = slot >= 0 && slot < P.n_slots;
+  if (!slot_ok && wt == 0) atomicExch(P.err, kDevBadIndex);
+  const int pairs = (P.NH + P.NKV) * half;
+  for (int t = wt; t < pairs; t += kStkWorkers) {
+    const int head = t / half, i = t - head * half;
+    const int base = head * hd;
+    const bool isq = head < P.NH;
+    const float sc = isq ? iq : ik;
+    const __nv_bfloat16* nw = isq ? ph.q_norm_w + base : ph.k_norm_w + (base - qd);
+    const float x1 = __ldcg(row + base + i) * sc * bf2f(nw[i]);
+    const float x2 = __ldcg(row + base + i + half) * sc * bf2f(nw[i + half]);
+    float sn, cs;
+    sincosf((float)pos * P.inv_freq[i], &sn, &cs);
+    const float y1 = x1 * cs - x2 * sn, y2 = x2 * cs + x1 * sn;
+    if (isq) {
+      P.q[(long)b * qd + base + i] = y1;
+      P.q[(long)b * qd + base + i + half] = y2;
+    } else if (slot_ok) {
+      __nv_bfloat16* kr = ph.kpool + (long)slot * kd + (base - qd);
+      kr[i] = f2bf(y1);
+      kr[i + half] = f2bf(y2);
+    }
+  }
+  if (slot_ok)
+    for (int i = wt; i < kd; i += kStkWorkers)
+      ph.vpool[(long)slot * kd + i] = f2bf(__ldcg(row + qd + kd + i));
 }
 
 // Raven hidden init (raven_init_kernel): bank_h[state_out] = position-keyed
 // truncated normal; bank_inj[state_out] = h[b].
-__device__ void stk_raven_init(const StackParams& P) {
+__device__ void stk_raven_init(const StackParams& P, int b) {
   const int wt = threadIdx.x - kStkWorkerTid0;
   const int H = P.H;
-  for (int b = blockIdx.x; b < P.n; b += gridDim.x) {
-    const int so = P.meta.get(kMetaStateOut, b);
-    if (so < 0 || so >= P.bank_rows) {
-      if (wt == 0) atomicExch(P.err, kDevBadIndex);
-      continue;
-    }
-    const uint32_t pos = (uint32_t)P.meta.get(kMetaPos, b);
-    const double lo = 0.0013498980316300946;  // Phi(-3)
-    for (int i4 = wt; i4 < (H + 3) / 4; i4 += kStkWorkers) {
-      const uint4 w = philox4x32_10(make_uint4((uint32_t)i4, pos, 0u, 0u), (uint32_t)P.init_seed,
-                                    (uint32_t)(P.init_seed >> 32));
-      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const int i = i4 * 4 + k;
-        if (i >= H) break;
-        const double u = ((double)(ws[k] >> 8) + 0.5) / 16777216.0;
-        const double p = lo + u * (1.0 - 2.0 * lo);
-        const double x = 1.4142135623730951 * erfinv(2.0 * p - 1.0);
-        P.bank_h[(long)so * H + i] = P.init_std > 0.f ? (float)(x * P.init_std * P.embed_scale) : 0.f;
-      }
-    }
-    for (int i = wt; i < H; i += kStkWorkers) P.bank_inj[(long)so * H + i] = __ldcg(P.h + (long)b * H + i);
+  const int so = P.meta.get(kMetaStateOut, b);
+  if (so < 0 || so >= P.bank_rows) {
+    if (wt == 0) atomicExch(P.err, kDevBadIndex);
+    return;
   }
+  const uint32_t pos = (uint32_t)P.meta.get(kMetaPos, b);
+  const double lo = 0.0013498980316300946;  // Phi(-3)
+  for (int i4 = wt; i4 < (H + 3) / 4; i4 += kStkWorkers) {
+    const uint4 w = philox4x32_10(make_uint4((uint32_t)i4, pos, 0u, 0u), (uint32_t)P.init_seed,
+                                  (uint32_t)(P.init_seed >> 32));
+    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int i = i4 * 4 + k;
+      if (i >= H) break;
+      const double u = ((double)(ws[k] >> 8) + 0.5) / 16777216.0;
+      const double p = lo + u * (1.0 - 2.0 * lo);
+      const double x = 1.4142135623730951 * erfinv(2.0 * p - 1.0);
+      P.bank_h[(long)so * H + i] = P.init_std > 0.f ? (float)(x * P.init_std * P.embed_scale) : 0.f;
+    }
+  }
+  for (int i = wt; i < H; i += kStkWorkers) P.bank_inj[(long)so * H + i] = __ldcg(P.h + (long)b * H + i);
 }
 
 // ------------------------------------------------------------ worker loop
+// The workers walk the program in order. GEMM phases: the epilogue warps
+// handle this CTA's segments as their accumulators complete. Attention: this
+// CTA's items, each after its inputs. Per-lane phases: this CTA's lanes, after
+// the phase's inputs are complete. No CTA waits for phases it does not consume.
 // s_flag[0..1]: epilogue broadcasts; [2]: worker go flag; [3]: GEMM phase ok.
 template <int BN, int HD>
 __device__ void stk_workers(const StackParams& P, uint8_t* work, uint32_t accf0, uint32_t acce0,
@@ -1099,48 +1456,38 @@ __device__ void stk_workers(const StackParams& P, uint8_t* work, uint32_t accf0,
   for (int p = 0; p < P.n_phases; ++p) {
     const Phase& ph = P.phases[p];
     if (p == P.n_phases - 1) pdl_launch_dependents();
+    if (wt == 0) stk_trace(P, p, 0);
     if (ph.kind == kPhGemm) {
       bool ok = true;
-      if (wt == 0) stk_trace(P, p, 0);
-      if (threadIdx.x >= kStkEpiTid0) ok = stk_gemm_epilogue<BN>(P, ph, p, seg, accf0, acce0, tmem, abort_, s_flag);
+      if (threadIdx.x >= kStkEpiTid0 && threadIdx.x < kStkEpiTid0 + 128)   // warps 4..7 only
+        ok = stk_gemm_epilogue<BN>(P, ph, p, seg, accf0, acce0, tmem, abort_, s_flag);
       if (threadIdx.x == kStkEpiTid0) s_flag[3] = ok;
       named_bar(kBarWorkers, kStkWorkers);
       if (!s_flag[3]) return;
-    } else {
-      // inputs of this phase: every earlier phase complete on every CTA
-      if (wt == 0) s_flag[2] = grid_wait(P.sync + 1, gridDim.x * (unsigned)p, abort_, P.err, kDevTimeoutGrid,
-                                         kStkWaitNs);
+    } else if (ph.kind == kPhAttn) {
+      if (!stk_attention<HD>(P, ph, p, work, abort_, s_flag, !ActPath<BN>::kLdg)) return;
+    } else if ((int)blockIdx.x < P.n) {
+      if (wt == 0) s_flag[2] = wait_tot_deps(P, ph, abort_);
       named_bar(kBarWorkers, kStkWorkers);
       if (!s_flag[2]) return;
-      if (wt == 0) stk_trace(P, p, 0);
-      switch (ph.kind) {
-        case kPhMap: stk_map(P); break;
-        case kPhPrep: stk_prep(P, ph, red); break;
-        case kPhCat: stk_cat(P); break;
-        case kPhQkNorm: stk_qknorm(P, ph, red); break;
-        case kPhAttn: stk_attention<HD>(P, ph, work); break;
-        case kPhRow: stk_row(P, ph, red); break;
-        case kPhRavenInit: stk_raven_init(P); break;
-        default:
-          if (wt == 0) atomicExch(P.err, kDevBadIndex);
-          break;
+      if (wt == 0) stk_trace(P, p, 2);   // inputs complete
+      for (int b = blockIdx.x; b < P.n; b += gridDim.x) {
+        switch (ph.kind) {
+          case kPhMap: stk_map(P, b); break;
+          case kPhPrep: stk_prep(P, ph, b, red); break;
+          case kPhCat: stk_cat(P, b); break;
+          case kPhQkNorm: stk_qknorm(P, ph, b, red); break;
+          case kPhRow: stk_row(P, ph, b, red); break;
+          case kPhRavenInit: stk_raven_init(P, b); break;
+          default:
+            if (wt == 0) atomicExch(P.err, kDevBadIndex);
+            break;
+        }
+        if (wt == 0 && b == (int)blockIdx.x) stk_trace(P, p, 4);   // first lane's work done
+        publish(kBarWorkers, kStkWorkers, wt == 0, P.tot + p, nullptr, !ActPath<BN>::kLdg);
       }
     }
-    // publish: this phase's generic writes become visible to other CTAs and
-    // to the TMA (async proxy) loads of later phases
-    if (wt == 0) stk_trace(P, p, 4);
-    fence_proxy_async_global();
-    named_bar(kBarWorkers, kStkWorkers);
-    if (wt == 0) {
-      stk_trace(P, p, 5);
-      // a GEMM phase may end here before the previous phase completed
-      // elsewhere (a CTA with no segments); arrive only after it did
-      if (ph.kind == kPhGemm)
-        grid_wait(P.sync + 1, gridDim.x * (unsigned)p, abort_, P.err, kDevTimeoutGrid, kStkWaitNs);
-      __threadfence();
-      atomicAdd(P.sync + 1, 1u);
-      stk_trace(P, p, 1);
-    }
+    if (wt == 0) stk_trace(P, p, 1);
   }
 }
 
@@ -1165,7 +1512,7 @@ __global__ void __launch_bounds__(kStkThreads, 1) stack_kernel(const __grid_cons
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int s = 0; s < ST; ++s) {
-      mbar_init(full0 + 8 * s, 1);
+      mbar_init(full0 + 8 * s, ActPath<BN>::kLdg ? 2 : 1);   // weights (+ the activation warp)
       mbar_init(empty0 + 8 * s, 1);
     }
     mbar_init(accf0, 1);
@@ -1191,8 +1538,12 @@ __global__ void __launch_bounds__(kStkThreads, 1) stack_kernel(const __grid_cons
   if (warp == 0) {
     if (lane == 0) stk_weights<BN, ST>(L, smem, full0, empty0, abort_, s_iw, s_wdone);
     __syncwarp();
-  } else if (warp == 8) {
-    if (lane == 0) stk_acts<BN, ST>(L, smem, full0, abort_, s_iw, s_wdone);
+  } else if (warp == 2) {
+    if constexpr (ActPath<BN>::kLdg) {
+      stk_acts_ldg<BN, ST>(L, smem, full0, abort_, s_iw, s_wdone);
+    } else {
+      if (lane == 0) stk_acts<BN, ST>(L, smem, full0, abort_, s_iw, s_wdone);
+    }
     __syncwarp();
   } else if (warp == 1) {
     if (lane == 0) stk_mma<BN, ST>(P, smem, full0, empty0, accf0, acce0, fin, tmem, abort_);
@@ -1206,14 +1557,22 @@ __global__ void __launch_bounds__(kStkThreads, 1) stack_kernel(const __grid_cons
     tc_fence_after();
     tmem_dealloc(tmem, S::kTmemCols);
   }
+  // The last CTA out resets every counter for the next launch (all other
+  // CTAs have finished reading them).
   if (threadIdx.x == 0) {
     __threadfence();
-    const unsigned t = atomicAdd(P.sync + 2, 1u);
-    if (t == gridDim.x - 1) {   // last CTA out: counters ready for the next launch
-      atomicExch(P.sync + 0, 0u);
-      atomicExch(P.sync + 1, 0u);
-      atomicExch(P.sync + 2, 0u);
+    s_flag[0] = atomicAdd(P.sync + 2, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (s_flag[0]) {
+    __threadfence();
+    for (int i = threadIdx.x; i < P.n_cnt; i += blockDim.x) P.cnt[i] = 0;
+    for (int i = threadIdx.x; i < P.n_phases; i += blockDim.x) P.tot[i] = 0;
+    if (threadIdx.x == 0) {
+      P.sync[0] = 0;
+      P.sync[2] = 0;
     }
+    __threadfence();
   }
 }
 

@@ -7,20 +7,23 @@
 
 namespace ls {
 
-constexpr int kStkThreads = 288;         // warps 0 weights TMA, 1 MMA, 2..7 workers, 8 activation TMA
-constexpr int kStkWorkers = 192;       // warps 2..7
-constexpr int kStkWorkerTid0 = 64;
-constexpr int kStkEpiTid0 = 128;       // warps 4..7 read TMEM
+constexpr int kStkThreads = 288;         // warps 0 weights TMA, 1 MMA, 2 activation TMA, 3..8 workers
+constexpr int kStkWorkers = 192;       // warps 3..8
+constexpr int kStkWorkerTid0 = 96;
+static_assert(kStkWorkerTid0 <= 128 && 128 + 128 <= kStkWorkerTid0 + kStkWorkers,
+              "the epilogue warps 4..7 must be workers");
+constexpr int kStkEpiTid0 = 128;       // warps 4..7 (a subset of the workers) read TMEM
 constexpr int kStkChunk = 96;          // attention positions per work item
 constexpr int kStkRowNV = 8;           // float4 columns per worker per row: H <= 6144
 constexpr int kStkMaxLanes = 128;
 constexpr int kBarWorkers = 1, kBarEpi = 2;   // named barrier ids (0 is __syncthreads)
 constexpr unsigned long long kStkWaitNs = 2000000000ull;   // any single wait: 2 s
+constexpr unsigned kStkPollNs = 100;                        // back-off between counter polls
 constexpr unsigned long long kStkStartNs = 1000000000ull;  // co-residency check: 1 s
 
 constexpr int kStkTraceFields = 12;
 
-enum StkError : int { kDevTimeoutGrid = 5, kDevNotResident = 6 };
+enum StkError : int { kDevTimeoutGrid = 5, kDevNotResident = 6 };   // 5: a dependency wait timed out
 
 enum PhaseKind : int {
   kPhMap = 0,      // timeline mapping: fork copy + append (map_update_kernel)
@@ -35,8 +38,21 @@ enum PhaseKind : int {
 
 enum XBufId : int { kXH = 0, kXAttn = 1, kXAct = 2, kXCat = 3, kXBufs = 4 };
 
+// Dependency kinds: what a phase's work waits for (counter >= target).
+enum DepKind : int {
+  kDepNone = 0,
+  kDepTotLanes = 1,   // tot[q] >= lanes of the call (a per-lane phase finished)
+  kDepTotTiles = 2,   // tot[q] >= tiles of GEMM phase q (all its tiles stored)
+  kDepKbHead = 3,     // GEMM activation k-block kb: cnt[q][kv head of kb] >= lanes (attention q)
+  kDepKbTile = 4,     // GEMM activation k-block kb: cnt[q][kb] >= 1 (tile kb of GEMM q)
+  kDepQkvHead = 5,    // attention item of kv head g: the QKV tiles holding g's q, k, v rows
+};
+
 struct Phase {
   int kind;
+  int cnt_off;                               // this phase's per-tile / per-head counters, or -1
+  int gemm_idx;                              // ordinal among the program's GEMM phases
+  int dep_kind[2], dep_phase[2];             // inputs this phase's work waits for
   // GEMM
   int xbuf, epi, Mw, K, m_tiles, KB, head;   // head: lanes [head_lane0, +head_n)
   int wmap;                                  // index into StackLaunch::wmap
@@ -85,18 +101,21 @@ struct StackParams {
   float* ml_part;                 // [cap][NH][max_chunks][2]
   int* attn_tickets;              // [cap][NKV]
   int max_chunks;
-  float* part_ws;                 // [grid][2][BN/2][128] segment partials
-  int* tile_tickets;              // per-tile contributor counters, zero between phases
-  unsigned* sync;                 // [0] start, [1] phase arrivals, [2] exits
+  float* part_ws;                 // [2][grid][2][BN/2][128] segment partials (GEMM parity)
+  int* tile_tickets;              // [2][max tiles] contributor counters, zero between uses
+  int* cnt;                       // completion counters: per tile / per head, zero between launches
+  int* tot;                       // [n_phases] per-phase completion counters
+  int n_cnt;                      // entries of cnt (reset at exit)
+  int ticket_stride;              // tile tickets per GEMM parity
+  unsigned* sync;                 // [0] start, [2] exits
   int* err;
   // optional timing trace, [n_phases + 1][grid][kStkTraceFields] globaltimer
-  // ns, per phase: 0 start of work, 1 arrival, 2 first accumulator ready,
-  // 3 first activation load issued, 4 work done, 5 fences done, 6 producer
-  // saw the phase's inputs complete, 7 last segment finished, 8 last
-  // activation load issued, 9 MMA took its first stage, 10 MMA finished its
-  // first segment, 11 weight stages of the phase already issued when its
-  // inputs were seen complete (a count); row n_phases: kernel entry (0) and
-  // co-residency pass (1).
+  // ns, per phase and CTA: 0 start of work, 1 end of work, 2 first
+  // accumulator ready, 3 first activation load issued, 6 inputs of the first
+  // activation load seen complete, 8 last activation load issued, 9 MMA took
+  // its first stage, 10 MMA finished its first segment, 11 weight stages of
+  // the phase already issued when its inputs were seen (a count); row
+  // n_phases: kernel entry (0) and co-residency pass (1).
   unsigned long long* trace;
 };
 
@@ -112,7 +131,12 @@ struct StackLaunch {
 };
 static_assert(sizeof(StackLaunch) <= 32764, "kernel parameters above the 32 KB limit");
 
-constexpr int stk_stages(int bn) { return bn <= 16 ? 11 : bn <= 32 ? 10 : bn <= 64 ? 8 : bn <= 128 ? 6 : 4; }
+// A ring stage holds one k-unit of kStkBK = 128: two 64-wide (128-byte
+// swizzle) sub-tiles per operand, so the MMA issuer's per-stage overhead
+// (commit, barrier wait, loop) is paid once per 32 KB of weights.
+constexpr int kStkBK = 128;
+constexpr int kStkSub = kStkBK / 64;
+constexpr int stk_stages(int bn) { return bn <= 32 ? 5 : bn <= 64 ? 4 : bn <= 128 ? 3 : 2; }
 cudaError_t stack_prepare();
 cudaError_t stack_launch(int bn, int hd, const StackLaunch& L, int grid, cudaStream_t stream, bool pdl);
 size_t stack_smem_bytes(int bn);

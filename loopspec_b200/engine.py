@@ -134,6 +134,7 @@ class Engine:
                                         buf.ctypes.data_as(ctypes.POINTER(ctypes.c_uint64)), cap,
                                         ctypes.byref(nph), ctypes.byref(grid)), self.h)
         n = (nph.value + 1) * grid.value * 12
+        self.last_stage_log = buf[n:n + 4 * 4096].reshape(4, 4096)   # CTA 0 per-stage SM clocks
         return buf[:n].reshape(nph.value + 1, grid.value, 12)
 
     def time_gemm(self, which, n_lanes, iters=50):

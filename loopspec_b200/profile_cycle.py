@@ -63,6 +63,7 @@ def main():
         if a.trace_out:
             import numpy as np
             np.save(a.trace_out, tr)
+            np.save(a.trace_out.replace(".npy", "_stages.npy"), eng.last_stage_log)
         print(json.dumps(trace_summary(tr, cfg)))
     eng.close()
 
