@@ -2020,7 +2020,7 @@ void check_attn_shape(int n, int nh, int nkv, int hd, int n_slots, int n_rows, i
   REQUIRE((hd == 64 && (G == 1 || G == 2 || G == 4)) || (hd == 128 && (G == 1 || G == 2)),
           LS_EINVAL, "decode attention: unsupported head_dim / GQA group");
   REQUIRE(max_ctx >= 1 && cdiv(max_ctx, kAttnChunk) <= kAttnMaxChunks, LS_EINVAL,
-          "decode attention: max_context must be in [1, 8192]");
+          "decode attention: max_context must be in [1, 131072]");
 }
 
 // Launch one decode-attention call on `stream` using `sc` as scratch, wait

@@ -287,18 +287,19 @@ __global__ void qkv_epi_kernel(QkvArgs a) {
 // timeline is its mapping row: position j of the timeline lives in KV slot
 // map[row][j], so forked branches read their shared prefix through the same
 // slots as their parent. A group of G = nh/nkv query heads shares each K/V
-// row. The CTA first stages the chunk's slot ids in shared memory, then each
-// sub-group of HD/8 lanes owns a fixed set of positions and issues all of its
-// 16-byte K loads (then V loads) at once; scores are reduced with warp
-// shuffles. Chunk boundaries are fixed multiples of kAttnChunk and positions
-// map to sub-groups by index, so results do not depend on the batch.
-// Each CTA writes its unnormalised (acc, max, sum) partial; the last CTA of a
-// (lane, kv head) to finish (counted with an atomic ticket, then reset) merges
-// all chunks in chunk order and writes the attention output as the O GEMM's
-// bf16 (hi, lo) input.
-constexpr int kAttnChunk = 256;
+// row. The chunk's slot ids and the query are loaded together; then each
+// sub-group of HD/8 threads owns PER fixed positions and issues all of its
+// 16-byte K and V loads at once, so a CTA costs two dependent memory round
+// trips before its partial; several CTAs per SM overlap theirs. Scores are
+// reduced with warp shuffles. Chunk boundaries are fixed multiples of
+// kAttnChunk and positions map to sub-groups by index, so results do not
+// depend on the batch. Each CTA writes its unnormalised (acc, max, sum)
+// partial; the last CTA of a (lane, kv head) to finish (atomic ticket, then
+// reset) merges the chunks in chunk order, eight at a time with a running
+// max, and writes the attention output as the O GEMM's bf16 (hi, lo) input.
+constexpr int kAttnChunk = 128;
 constexpr int kAttnThreads = 256;
-constexpr int kAttnMaxChunks = 32;   // max_context <= 8192
+constexpr int kAttnMaxChunks = 1024;   // max_context <= 131072
 
 struct AttnArgs {
   Meta meta;
@@ -330,6 +331,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnArgs a) {
   constexpr int NW = kAttnThreads / 32;
   constexpr int NSG = NW * PPW;            // sub-groups per CTA
   constexpr int PER = kAttnChunk / NSG;    // positions per sub-group
+  static_assert(PER * NSG == kAttnChunk, "chunk must split evenly over sub-groups");
   const int b = blockIdx.x, g = blockIdx.y, c = blockIdx.z;
   const int T = a.lane_len ? a.lane_len[b] : a.meta.get(kMetaPos, b) + 1;
   if (T < 1 || T > a.max_ctx) {
@@ -340,7 +342,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnArgs a) {
   if (start >= T) return;
   const int n_in = min(kAttnChunk, T - start);
   const int row = a.lane_row ? a.lane_row[b] : a.meta.get(kMetaRow, b);
-  if (row < 0 || row >= a.rows || T > a.max_ctx) {
+  if (row < 0 || row >= a.rows) {
     if (threadIdx.x == 0) atomicExch(a.err, kDevBadIndex);
     return;
   }
@@ -348,23 +350,14 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnArgs a) {
   __shared__ float sm_m[NW][G], sm_l[NW][G];
   __shared__ float sm_acc[NW][G][HD];
   __shared__ int s_last;
-  const int* mrow = a.map + (long)row * a.max_ctx + start;
-  for (int i = threadIdx.x; i < kAttnChunk; i += blockDim.x) {
-    int s = -1;
-    if (i < n_in) {
-      s = mrow[i];
-      if (s < 0 || s >= a.n_slots) {
-        atomicExch(a.err, kDevBadIndex);
-        s = -1;
-      }
-    }
-    s_slot[i] = s;
-  }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int sub = lane / LPP, sl = lane % LPP;
   const int sg = warp * PPW + sub;
   const int kd = a.nkv * HD;
 
+  // slot ids of the chunk and this thread's query slice, loaded together
+  int sv = -1;
+  if (threadIdx.x < kAttnChunk && (int)threadIdx.x < n_in) sv = a.map[(long)row * a.max_ctx + start + threadIdx.x];
   float qv[G][8];
 #pragma unroll
   for (int h = 0; h < G; ++h) {
@@ -374,31 +367,36 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnArgs a) {
 #pragma unroll
     for (int d = 0; d < 8; ++d) qv[h][d] = qq[d] * a.scale;
   }
+  if (threadIdx.x < kAttnChunk) {
+    if ((int)threadIdx.x < n_in && (sv < 0 || sv >= a.n_slots)) {
+      atomicExch(a.err, kDevBadIndex);
+      sv = -1;
+    }
+    s_slot[threadIdx.x] = sv;
+  }
   __syncthreads();
 
-  // scores for this sub-group's PER positions (p = sg + t * NSG)
+  uint4 kr[PER], vr[PER];
+#pragma unroll
+  for (int t = 0; t < PER; ++t) {
+    const int slot = s_slot[sg + t * NSG];
+    const long off = (long)slot * kd + g * HD + sl * 8;
+    kr[t] = slot >= 0 ? *reinterpret_cast<const uint4*>(a.kpool + off) : make_uint4(0, 0, 0, 0);
+    vr[t] = slot >= 0 ? *reinterpret_cast<const uint4*>(a.vpool + off) : make_uint4(0, 0, 0, 0);
+  }
   float sc[G][PER];
-  {
-    uint4 kr[PER];
 #pragma unroll
-    for (int t = 0; t < PER; ++t) {
-      const int slot = s_slot[sg + t * NSG];
-      kr[t] = slot >= 0 ? *reinterpret_cast<const uint4*>(a.kpool + (long)slot * kd + g * HD + sl * 8)
-                        : make_uint4(0, 0, 0, 0);
-    }
+  for (int t = 0; t < PER; ++t) {
+    float kf[8];
+    unpack8(kr[t], kf);
 #pragma unroll
-    for (int t = 0; t < PER; ++t) {
-      float kf[8];
-      unpack8(kr[t], kf);
+    for (int h = 0; h < G; ++h) {
+      float s = 0.f;
 #pragma unroll
-      for (int h = 0; h < G; ++h) {
-        float s = 0.f;
+      for (int d = 0; d < 8; ++d) s += qv[h][d] * kf[d];
 #pragma unroll
-        for (int d = 0; d < 8; ++d) s += qv[h][d] * kf[d];
-#pragma unroll
-        for (int o = LPP / 2; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-        sc[h][t] = s_slot[sg + t * NSG] >= 0 ? s : -INFINITY;
-      }
+      for (int o = LPP / 2; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+      sc[h][t] = s_slot[sg + t * NSG] >= 0 ? s : -INFINITY;
     }
   }
   float m[G], l[G], acc[G][8];
@@ -411,25 +409,16 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnArgs a) {
 #pragma unroll
     for (int d = 0; d < 8; ++d) acc[h][d] = 0.f;
   }
-  {
-    uint4 vr[PER];
 #pragma unroll
-    for (int t = 0; t < PER; ++t) {
-      const int slot = s_slot[sg + t * NSG];
-      vr[t] = slot >= 0 ? *reinterpret_cast<const uint4*>(a.vpool + (long)slot * kd + g * HD + sl * 8)
-                        : make_uint4(0, 0, 0, 0);
-    }
+  for (int t = 0; t < PER; ++t) {
+    float vf[8];
+    unpack8(vr[t], vf);
 #pragma unroll
-    for (int t = 0; t < PER; ++t) {
-      float vf[8];
-      unpack8(vr[t], vf);
+    for (int h = 0; h < G; ++h) {
+      const float p = m[h] == -INFINITY ? 0.f : __expf(sc[h][t] - m[h]);
+      l[h] += p;
 #pragma unroll
-      for (int h = 0; h < G; ++h) {
-        const float p = m[h] == -INFINITY ? 0.f : __expf(sc[h][t] - m[h]);
-        l[h] += p;
-#pragma unroll
-        for (int d = 0; d < 8; ++d) acc[h][d] += p * vf[d];
-      }
+      for (int d = 0; d < 8; ++d) acc[h][d] += p * vf[d];
     }
   }
 
@@ -494,32 +483,38 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnArgs a) {
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-  // Loads of all chunks are issued before use (L2, not L1: other CTAs wrote them).
+  // L2 loads (other CTAs wrote the partials), eight chunks in flight at a time
   for (int t = threadIdx.x; t < G * HD; t += blockDim.x) {
     const int h = t / HD, d = t - h * HD;
     const long base = ((long)b * a.nh + g * G + h) * a.max_chunks;
-    float cm[kAttnMaxChunks], cl[kAttnMaxChunks], co[kAttnMaxChunks];
+    float mm = -INFINITY, ll = 0.f, aa = 0.f;
+    for (int c0 = 0; c0 < nch; c0 += 8) {
+      float cm[8], cl[8], co[8];
 #pragma unroll
-    for (int cc = 0; cc < kAttnMaxChunks; ++cc) {
-      if (cc < nch) {
-        const float2 ml = __ldcg(reinterpret_cast<const float2*>(a.ml_part + (base + cc) * 2));
-        cm[cc] = ml.x;
-        cl[cc] = ml.y;
-        co[cc] = __ldcg(a.o_part + (base + cc) * HD + d);
+      for (int j = 0; j < 8; ++j) {
+        cm[j] = -INFINITY;
+        cl[j] = 0.f;
+        co[j] = 0.f;
+        if (c0 + j < nch) {
+          const float2 ml = __ldcg(reinterpret_cast<const float2*>(a.ml_part + (base + c0 + j) * 2));
+          cm[j] = ml.x;
+          cl[j] = ml.y;
+          co[j] = __ldcg(a.o_part + (base + c0 + j) * HD + d);
+        }
       }
-    }
-    float mm = -INFINITY;
+      float bm = mm;
 #pragma unroll
-    for (int cc = 0; cc < kAttnMaxChunks; ++cc)
-      if (cc < nch) mm = fmaxf(mm, cm[cc]);
-    float ll = 0.f, aa = 0.f;
+      for (int j = 0; j < 8; ++j) bm = fmaxf(bm, cm[j]);
+      const float r = bm == -INFINITY ? 0.f : __expf(mm - bm);
+      ll *= r;
+      aa *= r;
 #pragma unroll
-    for (int cc = 0; cc < kAttnMaxChunks; ++cc) {
-      if (cc < nch) {
-        const float w = mm == -INFINITY ? 0.f : __expf(cm[cc] - mm);
-        ll += cl[cc] * w;
-        aa += co[cc] * w;
+      for (int j = 0; j < 8; ++j) {
+        const float w = bm == -INFINITY ? 0.f : __expf(cm[j] - bm);
+        ll += cl[j] * w;
+        aa += co[j] * w;
       }
+      mm = bm;
     }
     const float o = ll > 0.f ? aa / ll : 0.f;
     if (a.out) a.out[(long)b * a.nh * HD + (g * G + h) * HD + d] = o;
