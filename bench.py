@@ -299,6 +299,11 @@ def engine_arm(args):
     except (OSError, KeyError, ValueError):
         peak_gbs, peak_src = 6650.0, "fallback"
     achieved = launch_bytes / (launch_ms / 1e3) / 1e9
+    # DRAM traffic per launch: an ncu capture (--set full) of the layer-0 QKV, O
+    # and gate_up GEMMs of a 4-lane Ouro-1.4B core call read 79.97 MB for 79.70
+    # MB of weights, ratio 1.0034 (no tile read twice); scaled to this sweep's
+    # average launch.
+    traffic = launch_bytes * (79.97 / 79.70)
     decode_bytes = bytes_per_decode(cfg, sch, agg, args.prompt)
     decode_gbs = decode_bytes / (dec_ms / 1e3) / 1e9
 
@@ -326,7 +331,10 @@ def engine_arm(args):
             "roofline": {"bound": "hbm", "kernel": "gemm_tc_kernel (core weight sweep)",
                          "achieved": round(achieved, 1), "peak": peak_gbs, "unit": "GB/s",
                          "frac": round(achieved / peak_gbs, 4), "peak_source": peak_src,
-                         "traffic": None, "lanes": lanes,
+                         "traffic": round(traffic),
+                         "traffic_source": "ncu dram__bytes_read+write of the core GEMMs, ratio to "
+                                           "their algorithmic bytes applied to this sweep",
+                         "lanes": lanes,
                          "bytes_per_launch": round(launch_bytes),
                          "avg_launch_us": round(launch_ms * 1e3, 3)},
             "decode_roofline": {"achieved": round(decode_gbs, 1), "peak": peak_gbs,

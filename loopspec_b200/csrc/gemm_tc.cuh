@@ -33,7 +33,7 @@ namespace ls {
 constexpr int kGemmBM = 128;
 constexpr int kGemmBK = 64;   // 64 bf16 = 128 bytes = one swizzle row
 constexpr int kGemmThreads = 128;
-constexpr int kMaxSplits = 16; // K splits per 128-row tile
+constexpr int kMaxSplits = 32; // K splits per 128-row tile
 
 enum GemmEpiKind : int { kEpiStore = 0, kEpiQkvRope = 1, kEpiSwiGLU = 2 };
 
@@ -51,10 +51,14 @@ struct GemmEpi {
   int* tile_tickets;          // [tiles], zero between launches
 };
 
-template <int BN, int ST>
+// SUB 64-wide sub-tiles per ring stage along K: the MMA thread's per-stage
+// cost (barrier wait, commit) is paid once per SUB k-blocks.
+template <int BN, int ST, int SUB = 1>
 struct GemmSmem {
-  static constexpr int kABytes = kGemmBM * kGemmBK * 2;
-  static constexpr int kBBytes = BN * kGemmBK * 2;
+  static constexpr int kSubA = kGemmBM * kGemmBK * 2;
+  static constexpr int kSubB = BN * kGemmBK * 2;
+  static constexpr int kABytes = kSubA * SUB;
+  static constexpr int kBBytes = kSubB * SUB;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kBarOffset = ST * kStageBytes;
   static constexpr int kTotal = 1024 /*alignment slack*/ + kBarOffset + (2 * ST + 1) * 8 + 16;
@@ -63,12 +67,13 @@ struct GemmSmem {
   static_assert(BN / 2 * kGemmBM * 4 <= ST * kStageBytes, "partial tile must fit the ring");
 };
 
-template <int BN, int ST, int EPI>
+template <int BN, int ST, int EPI, int SUB = 1>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                    const __grid_constant__ GemmEpi epi, int Mw, int K, int n_valid, int x_row0,
                    int splits, int* err) {
-  using L = GemmSmem<BN, ST>;
+  using L = GemmSmem<BN, ST, SUB>;
+  constexpr int UK = kGemmBK * SUB;   // k elements per ring stage
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -80,7 +85,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int m0 = blockIdx.x * kGemmBM;          // tile's first output row (store / qkv)
   const int split = blockIdx.y;
   const int n0 = blockIdx.z * BN;               // first activation row of this N tile
-  const int KB = (K + kGemmBK - 1) / kGemmBK;
+  const int KB = (K + UK - 1) / UK;   // k-units (split boundaries in units)
   const int kb0 = (int)((long)split * KB / splits);
   const int kb1 = (int)((long)(split + 1) * KB / splits);
   const int nkb = kb1 - kb0;
@@ -110,14 +115,24 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   // SwiGLU tiles take rows [64t, 64t+64) of the gate half and the same rows
   // of the up half (two 64-row boxes); other tiles take 128 consecutive rows.
-  auto load_w = [&](uint32_t dst, uint32_t bar, int kc) {
-    if (EPI == kEpiSwiGLU) {
-      const int g0 = blockIdx.x * (kGemmBM / 2);
-      tma_load_2d(dst, &tmW, bar, kc, g0);
-      tma_load_2d(dst + kGemmBM / 2 * kGemmBK * 2, &tmW, bar, kc, epi.I + g0);
-    } else {
-      tma_load_2d(dst, &tmW, bar, kc, m0);
+  auto load_w = [&](uint32_t dst0, uint32_t bar, int kc0) {
+#pragma unroll
+    for (int u = 0; u < SUB; ++u) {   // past K: the box reads the zero fill
+      const uint32_t dst = dst0 + u * L::kSubA;
+      const int kc = kc0 + u * kGemmBK;
+      if (EPI == kEpiSwiGLU) {
+        const int g0 = blockIdx.x * (kGemmBM / 2);
+        tma_load_2d(dst, &tmW, bar, kc, g0);
+        tma_load_2d(dst + kGemmBM / 2 * kGemmBK * 2, &tmW, bar, kc, epi.I + g0);
+      } else {
+        tma_load_2d(dst, &tmW, bar, kc, m0);
+      }
     }
+  };
+  auto load_x = [&](uint32_t dst0, uint32_t bar, int kc0) {
+#pragma unroll
+    for (int u = 0; u < SUB; ++u)
+      tma_load_2d(dst0 + u * L::kSubB, &tmX, bar, kc0 + u * kGemmBK, x_row0 + n0);
   };
 
   // Weights do not depend on the previous kernel: issue the first ring of
@@ -127,13 +142,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     for (int i = 0; i < pre; ++i) {
       const uint32_t fb = full0 + 8 * i;
       mbar_expect_tx(fb, L::kStageBytes);
-      load_w(smem_u32(smem + i * L::kStageBytes), fb, (kb0 + i) * kGemmBK);
+      load_w(smem_u32(smem + i * L::kStageBytes), fb, (kb0 + i) * UK);
     }
     pdl_wait();
-    for (int i = 0; i < pre; ++i) {
-      tma_load_2d(smem_u32(smem + i * L::kStageBytes + L::kABytes), &tmX, full0 + 8 * i,
-                  (kb0 + i) * kGemmBK, x_row0 + n0);
-    }
+    for (int i = 0; i < pre; ++i)
+      load_x(smem_u32(smem + i * L::kStageBytes + L::kABytes), full0 + 8 * i, (kb0 + i) * UK);
     for (int i = pre; i < nkb; ++i) {
       const int s = i % ST;
       const uint32_t ph = (uint32_t)((i / ST) & 1);
@@ -141,8 +154,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const uint32_t fb = full0 + 8 * s;
       mbar_expect_tx(fb, L::kStageBytes);
       uint8_t* st = smem + s * L::kStageBytes;
-      load_w(smem_u32(st), fb, (kb0 + i) * kGemmBK);
-      tma_load_2d(smem_u32(st + L::kABytes), &tmX, fb, (kb0 + i) * kGemmBK, x_row0 + n0);
+      load_w(smem_u32(st), fb, (kb0 + i) * UK);
+      load_x(smem_u32(st + L::kABytes), fb, (kb0 + i) * UK);
     }
   } else if (warp == 1 && lane == 0) {
     constexpr uint32_t idesc = umma_idesc_bf16(kGemmBM, BN);
@@ -154,10 +167,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const uint32_t a = smem_u32(smem + s * L::kStageBytes);
       const uint32_t b = a + L::kABytes;
 #pragma unroll
-      for (int k = 0; k < kGemmBK / 16; ++k) {
-        tc_mma_bf16(tmem, umma_desc_sw128(a + 32 * k), umma_desc_sw128(b + 32 * k), idesc,
-                    (i | k) != 0);
-      }
+      for (int u = 0; u < SUB; ++u)
+#pragma unroll
+        for (int k = 0; k < kGemmBK / 16; ++k)
+          tc_mma_bf16(tmem, umma_desc_sw128(a + u * L::kSubA + 32 * k), umma_desc_sw128(b + u * L::kSubB + 32 * k),
+                      idesc, (i | u | k) != 0);
       tc_commit(empty0 + 8 * s);
     }
     tc_commit(acc_bar);
