@@ -60,6 +60,11 @@ typedef struct ls_sched_cfg {
   int32_t use_persistent;    /* 1: each role call is one persistent kernel over
                                 all SMs (phases separated by grid counters);
                                 0: one kernel per GEMM / attention / row step */
+  int32_t l2_prefetch;       /* 1: latency-bound kernels (attention, norm rows,
+                                input prep) prefetch the weights of the GEMMs
+                                that follow them into L2 (multi-kernel path;
+                                measured slower on Ouro-1.4B decode, off by
+                                default in the Python API) */
 } ls_sched_cfg;
 
 /* Counters of sglang_recurrent/loopspec/executor.py:35-45 plus timing. */

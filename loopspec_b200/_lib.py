@@ -41,6 +41,7 @@ class SchedCfg(ctypes.Structure):
         ("max_context", _i32), ("max_prompt", _i32),
         ("kv_slots", _i32), ("request_rows", _i32),
         ("use_graphs", _i32), ("use_pdl", _i32), ("use_persistent", _i32),
+        ("l2_prefetch", _i32),
     ]
 
 

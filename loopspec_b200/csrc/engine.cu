@@ -136,6 +136,7 @@ struct StackEnd {
   float* bank = nullptr;             // scatter h into this bank at state_out
   bool want_x = false;               // produce x for a following GEMM
   const bf16* x_norm = nullptr;      // ... normalised by this weight (Raven ln_f)
+  L2Prefetch pf{};                   // weights of the GEMM after the stack
 };
 
 // Launch with optional programmatic-dependent-launch attribute.
@@ -437,6 +438,11 @@ struct ls_engine {
   std::map<std::pair<int, int>, int> graph_kernels;   // kernels per captured graph
   int64_t kernel_launches = 0;                        // kernels launched by role calls
   int kernels_in_call = 0;
+  // The next launch waits for full completion of the previous kernel (no
+  // programmatic overlap). Set after the mapping update: every kernel
+  // triggers its dependents at its start, and attention reads the
+  // timeline's slot ids before its own wait.
+  bool serialize_next = false;
   int64_t h2d_bytes = 0, d2h_bytes = 0;   // host<->device traffic counters
 
   Timelines tl;
@@ -1060,7 +1066,8 @@ void gemm(ls_engine& e, const Gemm& g, XBuf& x, const GemmEpi& epi, int kind, in
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = e.sc.use_pdl ? 1 : 0;
+  cfg.numAttrs = e.sc.use_pdl && !e.serialize_next ? 1 : 0;
+  e.serialize_next = false;
   GemmEpi ep = epi;
   ep.part_ws = e.gemm_part;
   ep.tile_tickets = e.gemm_tickets;
@@ -1105,21 +1112,43 @@ void gemm_store(ls_engine& e, const Gemm& g, XBuf& x, float* out, int n, int lan
 template <typename... KArgs, typename... Args>
 void klaunch(ls_engine& e, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
              Args&&... args) {
-  launch(kernel, grid, block, smem, e.stream, e.sc.use_pdl != 0, std::forward<Args>(args)...);
+  launch(kernel, grid, block, smem, e.stream, e.sc.use_pdl != 0 && !e.serialize_next,
+         std::forward<Args>(args)...);
+  e.serialize_next = false;
   e.kernels_in_call++;
 }
 
 void map_update(ls_engine& e, Meta meta, int n) {
   klaunch(e, map_update_kernel, dim3(n), dim3(128), 0, meta, n, e.map, e.max_ctx, e.rows, e.err_dev);
+  e.serialize_next = true;
 }
 
 // Threads of a per-lane row kernel: one float4 column each, at most 1024.
 int row_threads(int H) { return std::min(1024, H / 4); }
 
-void attention(ls_engine& e, Meta meta, int n, const bf16* kp, const bf16* vp) {
+// The weights of up to two GEMMs, for a latency-bound kernel to prefetch into
+// L2 while it runs (each range capped at kL2PrefetchCap bytes, so a prefetch
+// never pushes the L2 past what the next GEMMs read).
+constexpr unsigned long long kL2PrefetchCap = 64ull << 20;
+
+L2Prefetch l2pf(const ls_engine& e, const Gemm* a, const Gemm* b = nullptr) {
+  L2Prefetch pf{};
+  if (!e.sc.l2_prefetch) return pf;
+  const Gemm* g[2] = {a, b};
+  for (int i = 0; i < 2; ++i) {
+    if (!g[i] || !g[i]->w) continue;
+    const unsigned long long bytes = 2ull * (unsigned long long)g[i]->Mw * (unsigned long long)g[i]->K;
+    pf.p[i] = g[i]->w;
+    pf.bytes[i] = std::min(bytes, kL2PrefetchCap) & ~15ull;
+  }
+  return pf;
+}
+
+void attention(ls_engine& e, Meta meta, int n, const bf16* kp, const bf16* vp,
+               const L2Prefetch& pf = L2Prefetch{}) {
   AttnArgs a{meta, e.NH, e.NKV, e.q, e.map, e.max_ctx, e.rows, kp, vp, e.n_slots,
              e.max_chunks, e.o_part, e.ml_part, e.attn_tickets, e.x_attn.ptr, nullptr,
-             nullptr, nullptr, 1.0f / std::sqrt((float)e.HD), e.err_dev};
+             nullptr, nullptr, 1.0f / std::sqrt((float)e.HD), e.err_dev, pf};
   const dim3 grid(n, e.NKV, e.max_chunks), blk(kAttnThreads);
   const int G = e.NH / e.NKV;
   if (e.HD == 128 && G == 1) klaunch(e, attn_kernel<128, 1>, grid, blk, 0, a);
@@ -1141,10 +1170,18 @@ ResidArgs resid_base(ls_engine& e, Meta meta, const Gemm& g) {
   return a;
 }
 
-void resid(ls_engine& e, const ResidArgs& a, int n) {
+// CTAs of a per-lane row kernel: one per lane, plus one prefetch-only CTA per
+// SM when it carries an L2 prefetch.
+int row_grid(const ls_engine& e, int n, const L2Prefetch& pf) {
+  return n + (pf.bytes[0] + pf.bytes[1] > 0 ? e.num_sms : 0);
+}
+
+void resid(ls_engine& e, ResidArgs a, int n) {
+  a.B = n;
   const int thr = row_threads(e.H);
-  if (cdiv(e.H / 4, thr) == 1) klaunch(e, resid_epi_kernel<1>, dim3(n), dim3(thr), 0, a);
-  else klaunch(e, resid_epi_kernel<2>, dim3(n), dim3(thr), 0, a);
+  const dim3 grid(row_grid(e, n, a.pf));
+  if (cdiv(e.H / 4, thr) == 1) klaunch(e, resid_epi_kernel<1>, grid, dim3(thr), 0, a);
+  else klaunch(e, resid_epi_kernel<2>, grid, dim3(thr), 0, a);
 }
 
 // Norm applied to the input of a layer's first GEMM (none for OLMo2 post-norm).
@@ -1188,7 +1225,7 @@ void run_stack(ls_engine& e, Stack& st, int n, Meta meta, const StackEnd& end) {
       ep.n_slots = e.n_slots;
       gemm(e, w.g_qkv, e.x_h, ep, kEpiQkvRope, n);
     }
-    attention(e, meta, n, kp, vp);
+    attention(e, meta, n, kp, vp, l2pf(e, &w.g_o, &w.g_gu));
     gemm_store(e, w.g_o, e.x_attn, e.part, n);
 
     ResidArgs ra = resid_base(e, meta, w.g_o);
@@ -1203,6 +1240,7 @@ void run_stack(ls_engine& e, Stack& st, int n, Meta meta, const StackEnd& end) {
     } else {
       ra.a_norm_w = w.n_pa;
     }
+    ra.pf = l2pf(e, &w.g_down);
     resid(e, ra, n);
 
     // gate_up with SiLU(gate) * up fused into its epilogue -> x_act
@@ -1220,9 +1258,11 @@ void run_stack(ls_engine& e, Stack& st, int n, Meta meta, const StackEnd& end) {
     if (!last) {
       rb.x = e.x_h.ptr;
       rb.x_norm_w = input_norm(e, st.layers[l + 1]);
+      rb.pf = l2pf(e, &st.layers[l + 1].g_qkv);
     } else {
       rb.final_norm_w = end.final_norm;
       rb.bank = end.bank;
+      rb.pf = end.pf;
       if (end.want_x) {
         rb.x = e.x_h.ptr;
         rb.x_norm_w = end.x_norm;
@@ -1240,8 +1280,9 @@ struct PostOpts {
 };
 
 void prep(ls_engine& e, Meta meta, int n, bool embed_mode, float* bank_out, bool want_x,
-          const bf16* x_norm) {
+          const bf16* x_norm, const L2Prefetch& pf = L2Prefetch{}) {
   PrepArgs pa{};
+  pa.pf = pf;
   pa.meta = meta;
   pa.B = n;
   pa.H = e.H;
@@ -1257,8 +1298,9 @@ void prep(ls_engine& e, Meta meta, int n, bool embed_mode, float* bank_out, bool
   pa.vocab = e.V;
   pa.err = e.err_dev;
   const int thr = row_threads(e.H);
-  if (cdiv(e.H / 4, thr) == 1) klaunch(e, prep_kernel<1>, dim3(n), dim3(thr), 0, pa);
-  else klaunch(e, prep_kernel<2>, dim3(n), dim3(thr), 0, pa);
+  const dim3 grid(row_grid(e, n, pa.pf));
+  if (cdiv(e.H / 4, thr) == 1) klaunch(e, prep_kernel<1>, grid, dim3(thr), 0, pa);
+  else klaunch(e, prep_kernel<2>, grid, dim3(thr), 0, pa);
 }
 
 // Readout decisions of the head lanes: fused sampler or greedy argmax.
@@ -1339,7 +1381,8 @@ void enqueue_role(ls_engine& e, int role, int n, const PostOpts& po = PostOpts()
     end.bank = e.bank_h;
     if (ouro) {
       // one core iteration = all layers then step_norm (ouro.py:93-98)
-      prep(e, meta, n, false, nullptr, true, input_norm(e, e.core.layers[0]));
+      prep(e, meta, n, false, nullptr, true, input_norm(e, e.core.layers[0]),
+           l2pf(e, &e.core.layers[0].g_qkv));
       end.final_norm = e.step_norm;
     } else {
       // adapter(cat(hidden, injected)) then the core blocks (raven.py:271-281)
@@ -1351,6 +1394,7 @@ void enqueue_role(ls_engine& e, int role, int n, const PostOpts& po = PostOpts()
       ra.out_h = e.h;
       ra.x = e.x_h.ptr;
       ra.x_norm_w = input_norm(e, e.core.layers[0]);
+      ra.pf = l2pf(e, &e.core.layers[0].g_qkv);
       resid(e, ra, n);
     }
     run_stack(e, e.core, n, meta, end);
@@ -1359,10 +1403,12 @@ void enqueue_role(ls_engine& e, int role, int n, const PostOpts& po = PostOpts()
     const bool has_layers = !e.post.layers.empty();
     if (has_layers && po.layers) {
       map_update(e, meta, n);
-      prep(e, meta, n, false, nullptr, true, input_norm(e, e.post.layers[0]));
+      prep(e, meta, n, false, nullptr, true, input_norm(e, e.post.layers[0]),
+           l2pf(e, &e.post.layers[0].g_qkv));
       StackEnd end;
       end.want_x = true;
       end.x_norm = e.final_norm;
+      if (po.head) end.pf = l2pf(e, &e.g_lm);
       run_stack(e, e.post, n, meta, end);
     } else if (!has_layers) {
       prep(e, meta, n, false, nullptr, true, e.final_norm);
@@ -1471,6 +1517,7 @@ int fill_lane(ls_engine& e, int* m, int b, int token, int pos, Cursor* c, int st
   put(e, m, kMetaSlot, b, slot);
   put(e, m, kMetaForkRow, b, c->pending_parent_row);
   put(e, m, kMetaForkLen, b, c->pending_parent_row >= 0 ? c->seq_len : 0);
+  put(e, m, kMetaAhead, b, ahead);
   return slot;
 }
 

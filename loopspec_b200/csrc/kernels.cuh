@@ -17,8 +17,8 @@ namespace ls {
 // (sglang_recurrent/loopspec/graph_ops.py:175-218) without its O(context) grid.
 __global__ void map_update_kernel(Meta meta, int B, int* __restrict__ map, int max_ctx, int rows,
                                   int* err) {
-  pdl_wait();
   pdl_launch_dependents();
+  pdl_wait();
   const int b = blockIdx.x;
   if (b >= B) return;
   const int row = meta.get(kMetaRow, b), pos = meta.get(kMetaPos, b);
@@ -56,14 +56,16 @@ struct PrepArgs {
   float eps;
   int vocab;
   int* err;
+  L2Prefetch pf;               // weights of the GEMMs that follow
 };
 
 template <int NV>
 __global__ void prep_kernel(PrepArgs a) {
-  pdl_wait();
   pdl_launch_dependents();
-  __shared__ float red[32];
+  l2_prefetch_share(a.pf);
   const int b = blockIdx.x;
+  if (b >= a.B) return;         // prefetch-only CTA
+  __shared__ float red[32];
   const int H = a.H, H4 = H / 4;
   int src;
   if (a.embed) {
@@ -74,23 +76,28 @@ __global__ void prep_kernel(PrepArgs a) {
     if (src < 0 || src >= a.bank_rows) src = -1;
   }
   if (src < 0 && threadIdx.x == 0) atomicExch(a.err, kDevBadIndex);
+  // The lane metadata is uploaded before the role call and the embedding
+  // table and norm weights are constant: load them before waiting on the
+  // preceding kernel; a state-bank row only after it.
   float4 v[NV], w[NV];
-  float ss = 0.f;
 #pragma unroll
   for (int k = 0; k < NV; ++k) {
     const int j = threadIdx.x + k * blockDim.x;
     v[k] = make_float4(0.f, 0.f, 0.f, 0.f);
     w[k] = make_float4(1.f, 1.f, 1.f, 1.f);
-    if (j < H4 && src >= 0) {
-      if (a.embed) {
-        const float4 e = ld_bf4(a.embed + (long)src * H + 4 * j);
-        v[k] = make_float4(e.x * a.embed_scale, e.y * a.embed_scale, e.z * a.embed_scale,
-                           e.w * a.embed_scale);
-      } else {
-        v[k] = ld_f4(a.bank_in + (long)src * H + 4 * j);
-      }
+    if (j < H4 && src >= 0 && a.embed) {
+      const float4 e = ld_bf4(a.embed + (long)src * H + 4 * j);
+      v[k] = make_float4(e.x * a.embed_scale, e.y * a.embed_scale, e.z * a.embed_scale,
+                         e.w * a.embed_scale);
     }
     if (j < H4 && a.x_norm_w) w[k] = ld_bf4(a.x_norm_w + 4 * j);
+  }
+  pdl_wait();
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int j = threadIdx.x + k * blockDim.x;
+    if (j < H4 && src >= 0 && !a.embed) v[k] = ld_f4(a.bank_in + (long)src * H + 4 * j);
     ss += f4_sq(v[k]);
   }
   const int so = a.bank_out ? a.meta.get(kMetaStateOut, b) : -1;
@@ -110,8 +117,8 @@ __global__ void prep_kernel(PrepArgs a) {
 __global__ void cat_state_kernel(Meta meta, int H, const float* __restrict__ bank_h,
                                  const float* __restrict__ bank_inj, int bank_rows,
                                  __nv_bfloat16* __restrict__ x, int* err) {
-  pdl_wait();
   pdl_launch_dependents();
+  pdl_wait();
   const int b = blockIdx.x;
   const int si = meta.get(kMetaStateIn, b);
   if (si < 0 || si >= bank_rows) {
@@ -133,7 +140,7 @@ __global__ void cat_state_kernel(Meta meta, int H, const float* __restrict__ ban
 // x[b] = (hi, lo) of (x_norm ? rms(out) * wx : out) (optional).
 struct ResidArgs {
   Meta meta;
-  int H;
+  int B, H;                    // lanes (CTAs past B only prefetch), hidden size
   const float* part;           // GEMM output y [cap][H]
   const __nv_bfloat16* bias;
   const __nv_bfloat16* a_norm_w;
@@ -146,17 +153,31 @@ struct ResidArgs {
   const __nv_bfloat16* x_norm_w;
   float eps;
   int* err;
+  L2Prefetch pf;               // weights of the GEMMs that follow
 };
 
 template <int NV>
 __global__ void resid_epi_kernel(ResidArgs a) {
-  pdl_wait();
   pdl_launch_dependents();
-  __shared__ float red[32];
+  l2_prefetch_share(a.pf);
   const int b = blockIdx.x;
+  if (b >= a.B) return;         // prefetch-only CTA
+  __shared__ float red[32];
   const int H = a.H, H4 = H / 4;
   const float4 z = make_float4(0.f, 0.f, 0.f, 0.f), one = make_float4(1.f, 1.f, 1.f, 1.f);
-  float4 v[NV], rr[NV], wa[NV], wf[NV], wx[NV];
+  float4 v[NV], rr[NV], wa[NV], wf[NV], wx[NV], bb[NV];
+  // The norm weights and the bias are constant: load them while the
+  // producing GEMM is still running, the rows after it has finished.
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int j = threadIdx.x + k * blockDim.x;
+    const bool on = j < H4;
+    wa[k] = on && a.a_norm_w ? ld_bf4(a.a_norm_w + 4 * j) : one;
+    wf[k] = on && a.final_norm_w ? ld_bf4(a.final_norm_w + 4 * j) : one;
+    wx[k] = on && a.x_norm_w ? ld_bf4(a.x_norm_w + 4 * j) : one;
+    bb[k] = on && a.bias ? ld_bf4(a.bias + 4 * j) : z;
+  }
+  pdl_wait();
   float ss = 0.f;
 #pragma unroll
   for (int k = 0; k < NV; ++k) {
@@ -164,13 +185,7 @@ __global__ void resid_epi_kernel(ResidArgs a) {
     const bool on = j < H4;
     v[k] = on ? ld_f4(a.part + (long)b * H + 4 * j) : z;
     rr[k] = on && a.resid ? ld_f4(a.resid + (long)b * H + 4 * j) : z;
-    wa[k] = on && a.a_norm_w ? ld_bf4(a.a_norm_w + 4 * j) : one;
-    wf[k] = on && a.final_norm_w ? ld_bf4(a.final_norm_w + 4 * j) : one;
-    wx[k] = on && a.x_norm_w ? ld_bf4(a.x_norm_w + 4 * j) : one;
-    if (on && a.bias) {
-      const float4 bb = ld_bf4(a.bias + 4 * j);
-      v[k] = make_float4(v[k].x + bb.x, v[k].y + bb.y, v[k].z + bb.z, v[k].w + bb.w);
-    }
+    if (a.bias) v[k] = make_float4(v[k].x + bb[k].x, v[k].y + bb[k].y, v[k].z + bb[k].z, v[k].w + bb[k].w);
     ss += f4_sq(v[k]);
   }
   const int so = a.bank ? a.meta.get(kMetaStateOut, b) : -1;
@@ -231,8 +246,8 @@ struct QkvArgs {
 };
 
 __global__ void qkv_epi_kernel(QkvArgs a) {
-  pdl_wait();
   pdl_launch_dependents();
+  pdl_wait();
   extern __shared__ float row[];
   __shared__ float red[32];
   const int b = blockIdx.x;
@@ -320,18 +335,25 @@ struct AttnArgs {
   const int* lane_row;             // optional per-lane mapping row (else metadata)
   float scale;
   int* err;
+  L2Prefetch pf;                   // weights of the GEMMs that follow
 };
 
 template <int HD, int G>
-__global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnArgs a) {
-  pdl_wait();
+__global__ void __launch_bounds__(kAttnThreads, 3) attn_kernel(AttnArgs a) {
   pdl_launch_dependents();
+  l2_prefetch_share(a.pf);
   constexpr int LPP = HD / 8;              // lanes per position (16 B each)
   constexpr int PPW = 32 / LPP;            // positions per warp at a time
   constexpr int NW = kAttnThreads / 32;
   constexpr int NSG = NW * PPW;            // sub-groups per CTA
   constexpr int PER = kAttnChunk / NSG;    // positions per sub-group
   static_assert(PER * NSG == kAttnChunk, "chunk must split evenly over sub-groups");
+  // Before waiting on the preceding kernel (the QKV projection that writes q
+  // and the newest position's K/V), load what earlier work wrote: the lane
+  // metadata (uploaded before the role call), the timeline's slot ids (the
+  // kernel after the call's mapping update is launched without programmatic
+  // overlap, so the update has completed before any later kernel starts) and
+  // the K/V rows of every older position.
   const int b = blockIdx.x, g = blockIdx.y, c = blockIdx.z;
   const int T = a.lane_len ? a.lane_len[b] : a.meta.get(kMetaPos, b) + 1;
   if (T < 1 || T > a.max_ctx) {
@@ -355,9 +377,32 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnArgs a) {
   const int sg = warp * PPW + sub;
   const int kd = a.nkv * HD;
 
-  // slot ids of the chunk and this thread's query slice, loaded together
   int sv = -1;
   if (threadIdx.x < kAttnChunk && (int)threadIdx.x < n_in) sv = a.map[(long)row * a.max_ctx + start + threadIdx.x];
+  if (threadIdx.x < kAttnChunk) {
+    if ((int)threadIdx.x < n_in && (sv < 0 || sv >= a.n_slots)) {
+      atomicExch(a.err, kDevBadIndex);
+      sv = -1;
+    }
+    s_slot[threadIdx.x] = sv;
+  }
+  __syncthreads();
+  uint4 kr[PER], vr[PER];
+  // chunk index of the first position written by this call (the QKV
+  // projection writes one position per lane; prefill puts several positions
+  // of one timeline in a call)
+  const int fresh = T - 1 - (a.lane_len ? 0 : a.meta.get(kMetaAhead, b)) - start;
+#pragma unroll
+  for (int t = 0; t < PER; ++t) {
+    const int i = sg + t * NSG;
+    const int slot = s_slot[i];
+    const long off = (long)slot * kd + g * HD + sl * 8;
+    const bool old_row = slot >= 0 && i < fresh;
+    kr[t] = old_row ? *reinterpret_cast<const uint4*>(a.kpool + off) : make_uint4(0, 0, 0, 0);
+    vr[t] = old_row ? *reinterpret_cast<const uint4*>(a.vpool + off) : make_uint4(0, 0, 0, 0);
+  }
+  pdl_wait();
+  // after the QKV projection: this thread's query slice and the newest K/V row
   float qv[G][8];
 #pragma unroll
   for (int h = 0; h < G; ++h) {
@@ -367,22 +412,15 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnArgs a) {
 #pragma unroll
     for (int d = 0; d < 8; ++d) qv[h][d] = qq[d] * a.scale;
   }
-  if (threadIdx.x < kAttnChunk) {
-    if ((int)threadIdx.x < n_in && (sv < 0 || sv >= a.n_slots)) {
-      atomicExch(a.err, kDevBadIndex);
-      sv = -1;
-    }
-    s_slot[threadIdx.x] = sv;
-  }
-  __syncthreads();
-
-  uint4 kr[PER], vr[PER];
 #pragma unroll
   for (int t = 0; t < PER; ++t) {
-    const int slot = s_slot[sg + t * NSG];
-    const long off = (long)slot * kd + g * HD + sl * 8;
-    kr[t] = slot >= 0 ? *reinterpret_cast<const uint4*>(a.kpool + off) : make_uint4(0, 0, 0, 0);
-    vr[t] = slot >= 0 ? *reinterpret_cast<const uint4*>(a.vpool + off) : make_uint4(0, 0, 0, 0);
+    const int i = sg + t * NSG;
+    const int slot = s_slot[i];
+    if (slot >= 0 && i >= fresh) {
+      const long off = (long)slot * kd + g * HD + sl * 8;
+      kr[t] = *reinterpret_cast<const uint4*>(a.kpool + off);
+      vr[t] = *reinterpret_cast<const uint4*>(a.vpool + off);
+    }
   }
   float sc[G][PER];
 #pragma unroll
@@ -527,8 +565,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnArgs a) {
 // (torch.argmax semantics, sglang_recurrent/loopspec/decisions.py:116).
 __global__ void argmax_kernel(const float* __restrict__ logits, int V, long ld,
                               long long* __restrict__ out) {
-  pdl_wait();
   pdl_launch_dependents();
+  pdl_wait();
   const int b = blockIdx.x;
   const float* r = logits + (long)b * ld;
   float best = -INFINITY;
@@ -581,8 +619,8 @@ __global__ void raven_init_kernel(Meta meta, int H, const float* __restrict__ h,
                                   float* __restrict__ bank_h, float* __restrict__ bank_inj,
                                   int bank_rows, unsigned long long seed, float std_,
                                   float scale, int* err) {
-  pdl_wait();
   pdl_launch_dependents();
+  pdl_wait();
   const int b = blockIdx.x;
   const int so = meta.get(kMetaStateOut, b);
   if (so < 0 || so >= bank_rows) {

@@ -186,8 +186,8 @@ __device__ int block_pick(const float* w, int V, float u, float* s_chunk, float*
 
 template <bool SMEM_P>
 __global__ void __launch_bounds__(kSampleThreads) sample_kernel(SampleArgs a) {
-  pdl_wait();
   pdl_launch_dependents();
+  pdl_wait();
   extern __shared__ float s_p[];
   __shared__ float red[32];
   __shared__ float s_chunk[kSampleMaxChunks];

@@ -1226,9 +1226,11 @@ __device__ __forceinline__ void stk_store_row(const StackParams& P, const Phase&
 // out = final_norm ? rms(out) * wf : out; then out_h / bank / x as in
 // resid_epi_kernel.
 template <int NV, bool UPFRONT>
-__device__ void stk_row_impl(const StackParams& P, const Phase& ph, int b, float* red) {
+__device__ void stk_row_impl(const StackParams& P, const Phase& ph, int b, float* red, int tp) {
   const int wt = threadIdx.x - kStkWorkerTid0;
   const int H = P.H, H4 = H / 4;
+  const bool tr = P.trace && wt == 0 && blockIdx.x == 0 && b == 0;
+  const long long c0 = clock64();
   float4 v[NV], rr[NV];
   uint2 wa[UPFRONT ? NV : 1], wf[UPFRONT ? NV : 1], wx[UPFRONT ? NV : 1], bi[UPFRONT ? NV : 1];
 #pragma unroll
@@ -1275,12 +1277,14 @@ __device__ void stk_row_impl(const StackParams& P, const Phase& ph, int b, float
       ss += f4_sq(v[k]);
     }
   }
+  if (tr) stk_trace_value(P, tp, 8, (unsigned long long)(clock64() - c0));   // before the stores
   stk_store_row<NV>(P, ph, b, v, ss, red, UPFRONT ? wx : nullptr);
+  if (tr) stk_trace_value(P, tp, 9, (unsigned long long)(clock64() - c0));   // stores issued
 }
 
-__device__ void stk_row(const StackParams& P, const Phase& ph, int b, float* red) {
-  if (P.H <= 4 * 3 * kStkWorkers) stk_row_impl<3, true>(P, ph, b, red);
-  else stk_row_impl<kStkRowNV, false>(P, ph, b, red);
+__device__ void stk_row(const StackParams& P, const Phase& ph, int b, float* red, int tp) {
+  if (P.H <= 4 * 3 * kStkWorkers) stk_row_impl<3, true>(P, ph, b, red, tp);
+  else stk_row_impl<kStkRowNV, false>(P, ph, b, red, tp);
 }
 
 // h = embedding(token) * scale (src null) or src[state_in]; then out_h /
@@ -1477,14 +1481,17 @@ __device__ void stk_workers(const StackParams& P, uint8_t* work, uint32_t accf0,
           case kPhPrep: stk_prep(P, ph, b, red); break;
           case kPhCat: stk_cat(P, b); break;
           case kPhQkNorm: stk_qknorm(P, ph, b, red); break;
-          case kPhRow: stk_row(P, ph, b, red); break;
+          case kPhRow: stk_row(P, ph, b, red, p); break;
           case kPhRavenInit: stk_raven_init(P, b); break;
           default:
             if (wt == 0) atomicExch(P.err, kDevBadIndex);
             break;
         }
         if (wt == 0 && b == (int)blockIdx.x) stk_trace(P, p, 4);   // first lane's work done
+        const long long cpub = clock64();
         publish(kBarWorkers, kStkWorkers, wt == 0, P.tot + p, nullptr, !ActPath<BN>::kLdg);
+        if (wt == 0 && b == (int)blockIdx.x && blockIdx.x == 0)
+          stk_trace_value(P, p, 10, (unsigned long long)(clock64() - cpub));   // publish cycles
       }
     }
     if (wt == 0) stk_trace(P, p, 1);

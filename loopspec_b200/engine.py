@@ -31,7 +31,7 @@ class Engine:
     def __init__(self, cfg: ModelConfig, schedule: PipelineSchedule, weights: dict, *,
                  device: int = 0, max_context: int = 4096, max_prompt: int | None = None,
                  kv_slots: int = 0, request_rows: int = 0, use_graphs: bool = True,
-                 use_pdl: bool = True, use_persistent: bool = False):
+                 use_pdl: bool = True, use_persistent: bool = False, l2_prefetch: bool = False):
         if schedule.stages != cfg.stages:
             raise ValueError("schedule stages must equal the model's recurrence count")
         self.cfg = cfg
@@ -50,7 +50,8 @@ class Engine:
             step_size=schedule.step_size, second_step=schedule.second_step or 0,
             max_context=max_context, max_prompt=max_prompt or max_context // 2,
             kv_slots=kv_slots, request_rows=request_rows, use_graphs=int(use_graphs),
-            use_pdl=int(use_pdl), use_persistent=int(use_persistent))
+            use_pdl=int(use_pdl), use_persistent=int(use_persistent),
+            l2_prefetch=int(l2_prefetch))
         handle = ctypes.c_void_p()
         code = self.L.ls_create(ctypes.byref(mc), ctypes.byref(sc), device, ctypes.byref(handle))
         if code != _lib.LS_OK:

@@ -39,6 +39,10 @@ def main():
     p.add_argument("--trace", action="store_true",
                    help="persistent path: print the per-phase critical-path breakdown of one call")
     p.add_argument("--trace-out", default=None, help="also save the raw trace (.npy)")
+    p.add_argument("--l2-prefetch", action="store_true",
+                   help="multi-kernel path: latency-bound kernels prefetch upcoming GEMM weights into L2")
+    p.add_argument("--sampling", action="store_true",
+                   help="post role: top-p 0.9 sampling decisions instead of greedy argmax")
     a = p.parse_args()
     build()
     cfg = get_config(a.config)
@@ -46,9 +50,11 @@ def main():
     X = a.second // a.first if a.second else None
     eng = Engine(cfg, PipelineSchedule(cfg.stages, a.first, X), w, device=0,
                  max_context=max(2048, a.prompt + 64), max_prompt=a.prompt,
-                 use_persistent=a.persistent)
+                 use_persistent=a.persistent, l2_prefetch=a.l2_prefetch)
     g = torch.Generator().manual_seed(0)
     eng.prefill(torch.randint(0, cfg.vocab, (a.prompt,), generator=g).tolist())
+    if a.sampling:
+        eng.set_sampling(1.0, 0, 0.9, 1234)
     per_call = eng.kernel_count(a.role, a.lanes)
     torch.cuda.nvtx.range_push("decode_replays")
     ms = eng.time_role(a.role, a.lanes, a.prompt, a.iters)
