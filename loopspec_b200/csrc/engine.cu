@@ -436,6 +436,11 @@ struct ls_engine {
 
   std::map<std::pair<int, int>, cudaGraphExec_t> graphs;
   std::map<std::pair<int, int>, int> graph_kernels;   // kernels per captured graph
+  std::map<std::pair<int, int>, int> graph_chunks;    // attention grid chunks per graph
+  // attention grid depth of the call being enqueued: one CTA per 128-position
+  // chunk of its longest timeline (graphs round it up to an even count and are
+  // re-captured when it changes)
+  int attn_chunks = 1;
   int64_t kernel_launches = 0;                        // kernels launched by role calls
   int kernels_in_call = 0;
   // The next launch waits for full completion of the previous kernel (no
@@ -506,7 +511,7 @@ struct ls_engine {
       g.map64 = make_map_2d(w, Kd, Mw, kGemmBM / 2);
       g.has_map64 = true;
     }
-    part_elems = std::max(part_elems, (long)cap * Mw);
+    part_elems = std::max(part_elems, (long)cap * Mw * g.splits);   // split planes
     // scratch for the widest call of this GEMM (cap lanes)
     const int bn = cap * 2 <= 16 ? 16 : cap * 2 <= 32 ? 32 : cap * 2 <= 64 ? 64 : cap * 2 <= 128 ? 128 : 256;
     const long tiles = (long)cdiv(Mw, kGemmBM) * cdiv(2 * cap, bn);
@@ -1017,7 +1022,8 @@ struct ls_engine {
 #define LS_SMEM(BN, ST)          \
   LS_SMEM1(BN, ST, kEpiStore);   \
   LS_SMEM1(BN, ST, kEpiQkvRope); \
-  LS_SMEM1(BN, ST, kEpiSwiGLU)
+  LS_SMEM1(BN, ST, kEpiSwiGLU);  \
+  LS_SMEM1(BN, ST, kEpiSplitStore)
     LS_SMEM(16, 4);
     LS_SMEM(32, 4);
     LS_SMEM(64, 4);
@@ -1085,6 +1091,7 @@ void gemm(ls_engine& e, const Gemm& g, XBuf& x, const GemmEpi& epi, int kind, in
   do {                                                            \
     if (kind == kEpiQkvRope) LS_GEMM_K(BN, ST, kEpiQkvRope);      \
     else if (kind == kEpiSwiGLU) LS_GEMM_K(BN, ST, kEpiSwiGLU);   \
+    else if (kind == kEpiSplitStore) LS_GEMM_K(BN, ST, kEpiSplitStore); \
     else LS_GEMM_K(BN, ST, kEpiStore);                            \
   } while (0)
   switch (bn) {
@@ -1107,6 +1114,14 @@ GemmEpi store_to(float* out) {
 
 void gemm_store(ls_engine& e, const Gemm& g, XBuf& x, float* out, int n, int lane0 = 0) {
   gemm(e, g, x, store_to(out), kEpiStore, n, lane0);
+}
+
+// y as g.splits partial planes [split][cap][Mw] in e.part, for a row kernel
+// that adds them in split order (no split-K ticket or re-read in the GEMM).
+void gemm_split_store(ls_engine& e, const Gemm& g, XBuf& x, int n) {
+  GemmEpi ep = store_to(e.part);
+  ep.split_stride = (long)e.cap * g.Mw;
+  gemm(e, g, x, ep, kEpiSplitStore, n);
 }
 
 template <typename... KArgs, typename... Args>
@@ -1149,7 +1164,7 @@ void attention(ls_engine& e, Meta meta, int n, const bf16* kp, const bf16* vp,
   AttnArgs a{meta, e.NH, e.NKV, e.q, e.map, e.max_ctx, e.rows, kp, vp, e.n_slots,
              e.max_chunks, e.o_part, e.ml_part, e.attn_tickets, e.x_attn.ptr, nullptr,
              nullptr, nullptr, 1.0f / std::sqrt((float)e.HD), e.err_dev, pf};
-  const dim3 grid(n, e.NKV, e.max_chunks), blk(kAttnThreads);
+  const dim3 grid(n, e.NKV, e.attn_chunks), blk(kAttnThreads);
   const int G = e.NH / e.NKV;
   if (e.HD == 128 && G == 1) klaunch(e, attn_kernel<128, 1>, grid, blk, 0, a);
   else if (e.HD == 128 && G == 2) klaunch(e, attn_kernel<128, 2>, grid, blk, 0, a);
@@ -1162,8 +1177,9 @@ ResidArgs resid_base(ls_engine& e, Meta meta, const Gemm& g) {
   ResidArgs a{};
   a.meta = meta;
   a.H = e.H;
-  (void)g;
-  a.part = e.part;   // the GEMM already reduced its K splits
+  a.part = e.part;   // the GEMM's split planes (gemm_split_store)
+  a.splits = g.splits;
+  a.split_stride = (long)e.cap * g.Mw;
   a.bank_rows = e.bank_rows;
   a.eps = e.mc.rms_eps;
   a.err = e.err_dev;
@@ -1180,8 +1196,9 @@ void resid(ls_engine& e, ResidArgs a, int n) {
   a.B = n;
   const int thr = row_threads(e.H);
   const dim3 grid(row_grid(e, n, a.pf));
-  if (cdiv(e.H / 4, thr) == 1) klaunch(e, resid_epi_kernel<1>, grid, dim3(thr), 0, a);
-  else klaunch(e, resid_epi_kernel<2>, grid, dim3(thr), 0, a);
+  if (cdiv(e.H / 4, thr) > 1) klaunch(e, resid_epi_kernel<2, 4, 1024>, grid, dim3(thr), 0, a);
+  else if (thr <= 512) klaunch(e, resid_epi_kernel<1, 8, 512>, grid, dim3(thr), 0, a);
+  else klaunch(e, resid_epi_kernel<1, 8, 1024>, grid, dim3(thr), 0, a);
 }
 
 // Norm applied to the input of a layer's first GEMM (none for OLMo2 post-norm).
@@ -1207,8 +1224,9 @@ void run_stack(ls_engine& e, Stack& st, int n, Meta meta, const StackEnd& end) {
 
     if (w.qn) {
       // OLMo2 QK-norm needs whole-row sums: plain GEMM, then the QKV kernel.
-      gemm_store(e, w.g_qkv, e.x_h, e.part, n);
-      QkvArgs qa{meta, e.NH, e.NKV, e.HD, e.part, 1, 0, w.qn, w.kn, e.inv_freq, e.mc.rms_eps,
+      gemm_split_store(e, w.g_qkv, e.x_h, n);
+      QkvArgs qa{meta, e.NH, e.NKV, e.HD, e.part, w.g_qkv.splits, (long)e.cap * w.g_qkv.Mw,
+                 w.qn, w.kn, e.inv_freq, e.mc.rms_eps,
                  e.q, kp, vp, e.n_slots, e.err_dev};
       klaunch(e, qkv_epi_kernel, dim3(n), dim3(256), (size_t)(e.QD + 2 * e.KVD) * sizeof(float), qa);
     } else {
@@ -1226,7 +1244,7 @@ void run_stack(ls_engine& e, Stack& st, int n, Meta meta, const StackEnd& end) {
       gemm(e, w.g_qkv, e.x_h, ep, kEpiQkvRope, n);
     }
     attention(e, meta, n, kp, vp, l2pf(e, &w.g_o, &w.g_gu));
-    gemm_store(e, w.g_o, e.x_attn, e.part, n);
+    gemm_split_store(e, w.g_o, e.x_attn, n);
 
     ResidArgs ra = resid_base(e, meta, w.g_o);
     ra.resid = e.h;
@@ -1248,7 +1266,7 @@ void run_stack(ls_engine& e, Stack& st, int n, Meta meta, const StackEnd& end) {
     eg.x_act = e.x_act.ptr;
     eg.I = e.I;
     gemm(e, w.g_gu, e.x_h, eg, kEpiSwiGLU, n);
-    gemm_store(e, w.g_down, e.x_act, e.part, n);
+    gemm_split_store(e, w.g_down, e.x_act, n);
 
     ResidArgs rb = resid_base(e, meta, w.g_down);
     rb.resid = e.r;
@@ -1388,7 +1406,7 @@ void enqueue_role(ls_engine& e, int role, int n, const PostOpts& po = PostOpts()
       // adapter(cat(hidden, injected)) then the core blocks (raven.py:271-281)
       klaunch(e, cat_state_kernel, dim3(n), dim3(256), 0, meta, e.H, (const float*)e.bank_h,
               (const float*)e.bank_inj, e.bank_rows, e.x_cat.ptr, e.err_dev);
-      gemm_store(e, e.g_adapter, e.x_cat, e.part, n);
+      gemm_split_store(e, e.g_adapter, e.x_cat, n);
       ResidArgs ra = resid_base(e, meta, e.g_adapter);
       ra.bias = e.adapter_b;
       ra.out_h = e.h;
@@ -1442,13 +1460,24 @@ void run_role(ls_engine& e, int role, int n, const int* host_meta, bool graphabl
               const PostOpts& po = PostOpts()) {
   REQUIRE(n >= 1 && n <= e.cap, LS_ECAPACITY, "role call wider than the lane capacity");
   upload_meta(e, role, host_meta, n);
+  int longest = 1;
+  for (int b = 0; b < n; ++b) longest = std::max(longest, host_meta[b * kMetaFields + kMetaPos] + 1);
+  const int chunks = cdiv(longest, kAttnChunk);
   if (!(graphable && e.sc.use_graphs)) {
+    e.attn_chunks = std::min(chunks, e.max_chunks);
     enqueue_role(e, role, n, po);
     e.kernel_launches += e.kernels_in_call;
     return;
   }
+  e.attn_chunks = std::min(chunks + (chunks & 1), e.max_chunks);
   const auto key = std::make_pair(role * 2 + (e.sampling ? 1 : 0), n);
   auto it = e.graphs.find(key);
+  if (it != e.graphs.end() && e.graph_chunks[key] != e.attn_chunks) {
+    CK(cudaStreamSynchronize(e.stream));
+    CK(cudaGraphExecDestroy(it->second));
+    e.graphs.erase(it);
+    it = e.graphs.end();
+  }
   if (it == e.graphs.end()) {
     CK(cudaStreamBeginCapture(e.stream, cudaStreamCaptureModeThreadLocal));
     try {
@@ -1467,6 +1496,7 @@ void run_role(ls_engine& e, int role, int n, const int* host_meta, bool graphabl
     CK(ie);
     it = e.graphs.emplace(key, ge).first;
     e.graph_kernels[key] = e.kernels_in_call;
+    e.graph_chunks[key] = e.attn_chunks;
   }
   CK(cudaGraphLaunch(it->second, e.stream));
   e.kernel_launches += e.graph_kernels[key];

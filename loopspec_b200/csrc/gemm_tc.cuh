@@ -23,6 +23,10 @@
 //               the layer's KV pool at the lane's slot (bf16), q to fp32
 //   kEpiSwiGLU  the tile holds 64 gate rows and their 64 up rows (two TMA
 //               boxes); writes silu(g) * u as the next GEMM's (hi, lo) input
+//   kEpiSplitStore  every split writes its partial tile to its own plane,
+//               out[split * split_stride + n * Mw + m], and exits: no ticket,
+//               no re-read. The consumer (a per-lane row kernel) adds the
+//               planes in split order while it loads the row.
 // A lane's result therefore never depends on the batch it runs in.
 #pragma once
 
@@ -35,7 +39,7 @@ constexpr int kGemmBK = 64;   // 64 bf16 = 128 bytes = one swizzle row
 constexpr int kGemmThreads = 128;
 constexpr int kMaxSplits = 32; // K splits per 128-row tile
 
-enum GemmEpiKind : int { kEpiStore = 0, kEpiQkvRope = 1, kEpiSwiGLU = 2 };
+enum GemmEpiKind : int { kEpiStore = 0, kEpiQkvRope = 1, kEpiSwiGLU = 2, kEpiSplitStore = 3 };
 
 struct GemmEpi {
   float* out;                 // store: out[n * Mw + m]
@@ -49,6 +53,7 @@ struct GemmEpi {
   int I;
   float* part_ws;             // split partial tiles [tiles][splits][BN/2][128] (splits > 1)
   int* tile_tickets;          // [tiles], zero between launches
+  long split_stride;          // split store: floats between split planes of out
 };
 
 // SUB 64-wide sub-tiles per ring stage along K: the MMA thread's per-stage
@@ -203,6 +208,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const float s = (have && nkb > 0) ? __uint_as_float(v[2 * j]) + __uint_as_float(v[2 * j + 1]) : 0.f;
+        if (EPI == kEpiSplitStore) {
+          if (m0 + r < Mw && c0 / 2 + j < lanes_here)
+            epi.out[split * epi.split_stride + (long)(n0 / 2 + c0 / 2 + j) * Mw + m0 + r] = s;
+          continue;
+        }
         red[(c0 / 2 + j) * kGemmBM + r] = s;
         if (splits > 1) tile_part[split * split_floats + (c0 / 2 + j) * kGemmBM + r] = s;
       }
@@ -210,9 +220,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
   tc_fence_before();
   __shared__ int s_last;
-  if (splits > 1) __threadfence();
+  if (splits > 1 && EPI != kEpiSplitStore) __threadfence();
   __syncthreads();
   if (warp == 2) tmem_dealloc(tmem, L::kTmemCols);
+  if (EPI == kEpiSplitStore) return;
   if (splits > 1) {
     if (threadIdx.x == 0) {
       int* tk = epi.tile_tickets + tile_id;

@@ -141,7 +141,9 @@ __global__ void cat_state_kernel(Meta meta, int H, const float* __restrict__ ban
 struct ResidArgs {
   Meta meta;
   int B, H;                    // lanes (CTAs past B only prefetch), hidden size
-  const float* part;           // GEMM output y [cap][H]
+  const float* part;           // GEMM output y: split planes [splits][cap][H]
+  int splits;                  // planes to add, in split order (>= 1)
+  long split_stride;           // floats between planes
   const __nv_bfloat16* bias;
   const __nv_bfloat16* a_norm_w;
   const float* resid;
@@ -156,8 +158,11 @@ struct ResidArgs {
   L2Prefetch pf;               // weights of the GEMMs that follow
 };
 
-template <int NV>
-__global__ void resid_epi_kernel(ResidArgs a) {
+// NV float4 columns per thread; BATCH split planes loaded at once (one round
+// trip for the usual 19 splits when BATCH = 20); MAXT threads at most, which
+// bounds the registers the batch may use.
+template <int NV, int BATCH, int MAXT>
+__global__ void __launch_bounds__(MAXT) resid_epi_kernel(ResidArgs a) {
   pdl_launch_dependents();
   l2_prefetch_share(a.pf);
   const int b = blockIdx.x;
@@ -183,8 +188,22 @@ __global__ void resid_epi_kernel(ResidArgs a) {
   for (int k = 0; k < NV; ++k) {
     const int j = threadIdx.x + k * blockDim.x;
     const bool on = j < H4;
-    v[k] = on ? ld_f4(a.part + (long)b * H + 4 * j) : z;
     rr[k] = on && a.resid ? ld_f4(a.resid + (long)b * H + 4 * j) : z;
+    // y = the GEMM's split planes added in split order, BATCH loads in flight
+    v[k] = z;
+    if (on) {
+      const float* py = a.part + (long)b * H + 4 * j;
+      for (int s0 = 0; s0 < a.splits; s0 += BATCH) {
+        float4 t[BATCH];
+#pragma unroll
+        for (int u = 0; u < BATCH; ++u)
+          if (s0 + u < a.splits) t[u] = ld_f4(py + (s0 + u) * a.split_stride);
+#pragma unroll
+        for (int u = 0; u < BATCH; ++u)
+          if (s0 + u < a.splits)
+            v[k] = make_float4(v[k].x + t[u].x, v[k].y + t[u].y, v[k].z + t[u].z, v[k].w + t[u].w);
+      }
+    }
     if (a.bias) v[k] = make_float4(v[k].x + bb[k].x, v[k].y + bb[k].y, v[k].z + bb[k].z, v[k].w + bb[k].w);
     ss += f4_sq(v[k]);
   }
@@ -356,7 +375,8 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attn_kernel(AttnArgs a) {
   // the K/V rows of every older position.
   const int b = blockIdx.x, g = blockIdx.y, c = blockIdx.z;
   const int T = a.lane_len ? a.lane_len[b] : a.meta.get(kMetaPos, b) + 1;
-  if (T < 1 || T > a.max_ctx) {
+  // the grid holds one CTA per chunk of the call's longest timeline
+  if (T < 1 || T > a.max_ctx || (T + kAttnChunk - 1) / kAttnChunk > (int)gridDim.z) {
     if (threadIdx.x == 0 && c == 0) atomicExch(a.err, kDevBadIndex);
     return;
   }
