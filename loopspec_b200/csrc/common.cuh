@@ -96,6 +96,17 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
   return t;
 }
 
+// Ticket for "last CTA to finish does the merge": call after a __syncthreads
+// that follows the CTA's partial-result stores, from one thread. Release
+// (cumulative over the CTA's stores ordered by the barrier) publishes them;
+// acquire lets the CTA that draws the last ticket read every other CTA's
+// partials (with L1-bypassing loads) after a second __syncthreads.
+__device__ __forceinline__ int ticket_take(int* p) {
+  int old;
+  asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], 1;" : "=r"(old) : "l"(p) : "memory");
+  return old;
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

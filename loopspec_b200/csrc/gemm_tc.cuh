@@ -220,20 +220,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
   tc_fence_before();
   __shared__ int s_last;
-  if (splits > 1 && EPI != kEpiSplitStore) __threadfence();
   __syncthreads();
   if (warp == 2) tmem_dealloc(tmem, L::kTmemCols);
   if (EPI == kEpiSplitStore) return;
   if (splits > 1) {
     if (threadIdx.x == 0) {
       int* tk = epi.tile_tickets + tile_id;
-      const int t = atomicAdd(tk, 1);
+      const int t = ticket_take(tk);
       s_last = t == splits - 1;
       if (s_last) *tk = 0;   // every split has arrived: ready for the next launch
     }
     __syncthreads();
     if (!s_last) return;
-    __threadfence();
   }
 
   // Epilogue over the tile's 64 row pairs. A unit is two rows that one

@@ -530,17 +530,15 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attn_kernel(AttnArgs a) {
 
   // last CTA of this (lane, kv head) merges the chunks in order
   const int nch = min((T + kAttnChunk - 1) / kAttnChunk, a.max_chunks);
-  __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
     int* tk = a.tickets + (long)b * a.nkv + g;
-    const int ticket = atomicAdd(tk, 1);
+    const int ticket = ticket_take(tk);
     s_last = ticket == nch - 1;
     if (s_last) *tk = 0;
   }
   __syncthreads();
   if (!s_last) return;
-  __threadfence();
   // L2 loads (other CTAs wrote the partials), eight chunks in flight at a time
   for (int t = threadIdx.x; t < G * HD; t += blockDim.x) {
     const int h = t / HD, d = t - h * HD;
