@@ -437,6 +437,12 @@ struct ls_engine {
   std::map<std::pair<int, int>, cudaGraphExec_t> graphs;
   std::map<std::pair<int, int>, int> graph_kernels;   // kernels per captured graph
   std::map<std::pair<int, int>, int> graph_chunks;    // attention grid chunks per graph
+  std::map<std::pair<int, int>, bool> graph_planes;   // decode-form QKV per graph
+  // Decode form of the call being enqueued: every lane has one new position,
+  // so the QKV projection stores split planes and attention finishes q / K / V
+  // (RoPE, pool write) itself. Prefill calls (several positions of one
+  // timeline) keep the projection's fused RoPE / KV-write epilogue.
+  bool qkv_planes = false;
   // attention grid depth of the call being enqueued: one CTA per 128-position
   // chunk of its longest timeline (graphs round it up to an even count and are
   // re-captured when it changes)
@@ -1159,11 +1165,21 @@ L2Prefetch l2pf(const ls_engine& e, const Gemm* a, const Gemm* b = nullptr) {
   return pf;
 }
 
-void attention(ls_engine& e, Meta meta, int n, const bf16* kp, const bf16* vp,
-               const L2Prefetch& pf = L2Prefetch{}) {
+// planes: the QKV projection's split planes (decode form), or null when the
+// projection's epilogue already wrote q and the new K/V.
+void attention(ls_engine& e, Meta meta, int n, bf16* kp, bf16* vp,
+               const L2Prefetch& pf = L2Prefetch{}, const Gemm* planes = nullptr) {
   AttnArgs a{meta, e.NH, e.NKV, e.q, e.map, e.max_ctx, e.rows, kp, vp, e.n_slots,
              e.max_chunks, e.o_part, e.ml_part, e.attn_tickets, e.x_attn.ptr, nullptr,
              nullptr, nullptr, 1.0f / std::sqrt((float)e.HD), e.err_dev, pf};
+  if (planes) {
+    a.qkv = e.part;
+    a.qkv_splits = planes->splits;
+    a.qkv_stride = (long)e.cap * planes->Mw;
+    a.inv_freq = e.inv_freq;
+    a.kpool_w = kp;
+    a.vpool_w = vp;
+  }
   const dim3 grid(n, e.NKV, e.attn_chunks), blk(kAttnThreads);
   const int G = e.NH / e.NKV;
   if (e.HD == 128 && G == 1) klaunch(e, attn_kernel<128, 1>, grid, blk, 0, a);
@@ -1197,7 +1213,7 @@ void resid(ls_engine& e, ResidArgs a, int n) {
   const int thr = row_threads(e.H);
   const dim3 grid(row_grid(e, n, a.pf));
   if (cdiv(e.H / 4, thr) > 1) klaunch(e, resid_epi_kernel<2, 4, 1024>, grid, dim3(thr), 0, a);
-  else if (thr <= 512) klaunch(e, resid_epi_kernel<1, 8, 512>, grid, dim3(thr), 0, a);
+  else if (thr <= 512) klaunch(e, resid_epi_kernel<1, 10, 512>, grid, dim3(thr), 0, a);
   else klaunch(e, resid_epi_kernel<1, 8, 1024>, grid, dim3(thr), 0, a);
 }
 
@@ -1229,6 +1245,9 @@ void run_stack(ls_engine& e, Stack& st, int n, Meta meta, const StackEnd& end) {
                  w.qn, w.kn, e.inv_freq, e.mc.rms_eps,
                  e.q, kp, vp, e.n_slots, e.err_dev};
       klaunch(e, qkv_epi_kernel, dim3(n), dim3(256), (size_t)(e.QD + 2 * e.KVD) * sizeof(float), qa);
+    } else if (e.qkv_planes) {
+      // decode: split planes; attention sums them and does RoPE / the KV write
+      gemm_split_store(e, w.g_qkv, e.x_h, n);
     } else {
       // RoPE and the K/V cache write run in the GEMM's reduction epilogue.
       GemmEpi ep{};
@@ -1243,7 +1262,7 @@ void run_stack(ls_engine& e, Stack& st, int n, Meta meta, const StackEnd& end) {
       ep.n_slots = e.n_slots;
       gemm(e, w.g_qkv, e.x_h, ep, kEpiQkvRope, n);
     }
-    attention(e, meta, n, kp, vp, l2pf(e, &w.g_o, &w.g_gu));
+    attention(e, meta, n, kp, vp, l2pf(e, &w.g_o, &w.g_gu), !w.qn && e.qkv_planes ? &w.g_qkv : nullptr);
     gemm_split_store(e, w.g_o, e.x_attn, n);
 
     ResidArgs ra = resid_base(e, meta, w.g_o);
@@ -1461,8 +1480,13 @@ void run_role(ls_engine& e, int role, int n, const int* host_meta, bool graphabl
   REQUIRE(n >= 1 && n <= e.cap, LS_ECAPACITY, "role call wider than the lane capacity");
   upload_meta(e, role, host_meta, n);
   int longest = 1;
-  for (int b = 0; b < n; ++b) longest = std::max(longest, host_meta[b * kMetaFields + kMetaPos] + 1);
+  bool single = true;   // no lane shares its timeline with an earlier lane of the call
+  for (int b = 0; b < n; ++b) {
+    longest = std::max(longest, host_meta[b * kMetaFields + kMetaPos] + 1);
+    single = single && host_meta[b * kMetaFields + kMetaAhead] <= 0;
+  }
   const int chunks = cdiv(longest, kAttnChunk);
+  e.qkv_planes = single;
   if (!(graphable && e.sc.use_graphs)) {
     e.attn_chunks = std::min(chunks, e.max_chunks);
     enqueue_role(e, role, n, po);
@@ -1472,7 +1496,7 @@ void run_role(ls_engine& e, int role, int n, const int* host_meta, bool graphabl
   e.attn_chunks = std::min(chunks + (chunks & 1), e.max_chunks);
   const auto key = std::make_pair(role * 2 + (e.sampling ? 1 : 0), n);
   auto it = e.graphs.find(key);
-  if (it != e.graphs.end() && e.graph_chunks[key] != e.attn_chunks) {
+  if (it != e.graphs.end() && (e.graph_chunks[key] != e.attn_chunks || e.graph_planes[key] != e.qkv_planes)) {
     CK(cudaStreamSynchronize(e.stream));
     CK(cudaGraphExecDestroy(it->second));
     e.graphs.erase(it);
@@ -1497,6 +1521,7 @@ void run_role(ls_engine& e, int role, int n, const int* host_meta, bool graphabl
     it = e.graphs.emplace(key, ge).first;
     e.graph_kernels[key] = e.kernels_in_call;
     e.graph_chunks[key] = e.attn_chunks;
+    e.graph_planes[key] = e.qkv_planes;
   }
   CK(cudaGraphLaunch(it->second, e.stream));
   e.kernel_launches += e.graph_kernels[key];

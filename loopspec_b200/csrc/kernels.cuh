@@ -355,7 +355,32 @@ struct AttnArgs {
   float scale;
   int* err;
   L2Prefetch pf;                   // weights of the GEMMs that follow
+  // Decode form (qkv non-null): the QKV projection left its split planes
+  // [splits][cap][(nh + 2 nkv) * HD] and every lane has exactly one new
+  // position (T - 1). Each CTA sums its q (split order) and applies RoPE; the
+  // CTA whose chunk holds T - 1 also forms that position's K (RoPE) and V,
+  // rounds them to bf16, writes them to the pool at the position's slot and
+  // uses them.
+  const float* qkv;
+  int qkv_splits;
+  long qkv_stride;
+  const float* inv_freq;           // [HD / 2]
+  __nv_bfloat16* kpool_w;          // kpool / vpool, writable
+  __nv_bfloat16* vpool_w;
 };
+
+// Sum of `splits` planes of element e (split order) starting at p.
+__device__ __forceinline__ float plane_sum(const float* p, int splits, long stride) {
+  float t[8], v = 0.f;
+  for (int s0 = 0; s0 < splits; s0 += 8) {
+#pragma unroll
+    for (int u = 0; u < 8; ++u) t[u] = s0 + u < splits ? __ldcg(p + (s0 + u) * stride) : 0.f;
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      if (s0 + u < splits) v += t[u];
+  }
+  return v;
+}
 
 template <int HD, int G>
 __global__ void __launch_bounds__(kAttnThreads, 3) attn_kernel(AttnArgs a) {
@@ -397,6 +422,10 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attn_kernel(AttnArgs a) {
   const int sg = warp * PPW + sub;
   const int kd = a.nkv * HD;
 
+  // decode form: RoPE angles of position T - 1 (they depend on nothing the
+  // preceding kernel writes)
+  __shared__ float s_cs[HD / 2], s_sn[HD / 2];
+  if (a.qkv && threadIdx.x < HD / 2) sincosf((float)(T - 1) * a.inv_freq[threadIdx.x], &s_sn[threadIdx.x], &s_cs[threadIdx.x]);
   int sv = -1;
   if (threadIdx.x < kAttnChunk && (int)threadIdx.x < n_in) sv = a.map[(long)row * a.max_ctx + start + threadIdx.x];
   if (threadIdx.x < kAttnChunk) {
@@ -424,22 +453,76 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attn_kernel(AttnArgs a) {
   pdl_wait();
   // after the QKV projection: this thread's query slice and the newest K/V row
   float qv[G][8];
+  if (a.qkv) {
+    // decode form: q, and (chunk holding T - 1) the new K/V, from the planes
+    constexpr int half = HD / 2;
+    __shared__ float s_raw[G * HD + 2 * HD];
+    __shared__ float s_q[G * HD];
+    __shared__ __align__(16) __nv_bfloat16 s_kv[2 * HD];
+    const bool own = fresh >= 0 && fresh < kAttnChunk;   // this chunk holds T - 1
+    const int D = (a.nh + 2 * a.nkv) * HD;
+    const float* pl = a.qkv + (long)b * D;
+    const int n_el = G * HD + (own ? 2 * HD : 0);
+    for (int e = threadIdx.x; e < n_el; e += blockDim.x) {
+      int col;
+      if (e < G * HD) col = g * G * HD + e;                                   // q of head g*G + e/HD
+      else if (e < G * HD + HD) col = (a.nh + g) * HD + (e - G * HD);         // k of kv head g
+      else col = (a.nh + a.nkv + g) * HD + (e - G * HD - HD);                 // v of kv head g
+      s_raw[e] = plane_sum(pl + col, a.qkv_splits, a.qkv_stride);
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < n_el; e += blockDim.x) {
+      if (e < G * HD + HD) {   // q or k: neox RoPE pairs (i, i + half) within a head
+        const int base = e < G * HD ? (e / HD) * HD : G * HD;
+        const int d = e - base, i = d < half ? d : d - half;
+        const float sn = s_sn[i], cs = s_cs[i];
+        const float x1 = s_raw[base + i], x2 = s_raw[base + i + half];
+        const float y = d < half ? x1 * cs - x2 * sn : x2 * cs + x1 * sn;
+        if (e < G * HD) s_q[e] = y;
+        else s_kv[d] = f2bf(y);
+      } else {
+        s_kv[e - G * HD] = f2bf(s_raw[e]);
+      }
+    }
+    __syncthreads();
+    if (own) {   // the pool keeps the new K/V for later calls, at the lane's slot
+      const int slot = a.meta.get(kMetaSlot, b);
+      if (slot < 0 || slot >= a.n_slots) {
+        if (threadIdx.x == 0) atomicExch(a.err, kDevBadIndex);
+      } else
+        for (int e = threadIdx.x; e < 2 * HD; e += blockDim.x)
+          (e < HD ? a.kpool_w : a.vpool_w)[(long)slot * kd + g * HD + (e % HD)] = s_kv[e];
+    }
 #pragma unroll
-  for (int h = 0; h < G; ++h) {
-    const float* qp = a.q + (long)b * a.nh * HD + (g * G + h) * HD + sl * 8;
-    const float4 q0 = ld_f4(qp), q1 = ld_f4(qp + 4);
-    const float qq[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+    for (int h = 0; h < G; ++h)
 #pragma unroll
-    for (int d = 0; d < 8; ++d) qv[h][d] = qq[d] * a.scale;
-  }
+      for (int d = 0; d < 8; ++d) qv[h][d] = s_q[h * HD + sl * 8 + d] * a.scale;
 #pragma unroll
-  for (int t = 0; t < PER; ++t) {
-    const int i = sg + t * NSG;
-    const int slot = s_slot[i];
-    if (slot >= 0 && i >= fresh) {
-      const long off = (long)slot * kd + g * HD + sl * 8;
-      kr[t] = *reinterpret_cast<const uint4*>(a.kpool + off);
-      vr[t] = *reinterpret_cast<const uint4*>(a.vpool + off);
+    for (int t = 0; t < PER; ++t) {
+      const int i = sg + t * NSG;
+      if (own && i == fresh && s_slot[i] >= 0) {
+        kr[t] = *reinterpret_cast<const uint4*>(s_kv + sl * 8);
+        vr[t] = *reinterpret_cast<const uint4*>(s_kv + HD + sl * 8);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+      const float* qp = a.q + (long)b * a.nh * HD + (g * G + h) * HD + sl * 8;
+      const float4 q0 = ld_f4(qp), q1 = ld_f4(qp + 4);
+      const float qq[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+      for (int d = 0; d < 8; ++d) qv[h][d] = qq[d] * a.scale;
+    }
+#pragma unroll
+    for (int t = 0; t < PER; ++t) {
+      const int i = sg + t * NSG;
+      const int slot = s_slot[i];
+      if (slot >= 0 && i >= fresh) {
+        const long off = (long)slot * kd + g * HD + sl * 8;
+        kr[t] = *reinterpret_cast<const uint4*>(a.kpool + off);
+        vr[t] = *reinterpret_cast<const uint4*>(a.vpool + off);
+      }
     }
   }
   float sc[G][PER];
