@@ -399,6 +399,7 @@ struct ls_engine {
   long long *amax_dev = nullptr, *amax_host = nullptr;
   float* logits_host = nullptr;
   int* err_dev = nullptr;
+  int* err_host = nullptr;      // pinned copy of err_dev, fetched with each step's results
   int* attn_tickets = nullptr;  // [cap][n_kv_heads] chunk-arrival counters, zero between calls
   // sampling (greedy iff disabled): parameters on the device so captured
   // graphs read the current request's settings; q1 / q2-residual
@@ -477,6 +478,7 @@ struct ls_engine {
     if (amax_host) cudaFreeHost(amax_host);
     if (logits_host) cudaFreeHost(logits_host);
     if (dec_host) cudaFreeHost(dec_host);
+    if (err_host) cudaFreeHost(err_host);
     if (ev0) cudaEventDestroy(ev0);
     if (ev1) cudaEventDestroy(ev1);
     if (stream) cudaStreamDestroy(stream);
@@ -679,6 +681,7 @@ struct ls_engine {
     samp_work = dalloc<float>((long)max_rows * 2 * V);
     dec_dev = dalloc<long long>((long)cap * 5);
     CK(cudaMallocHost(&dec_host, sizeof(long long) * 5 * (size_t)cap));
+    CK(cudaMallocHost(&err_host, sizeof(int)));
     REQUIRE(V <= kSampleChunk * kSampleMaxChunks, LS_EINVAL, "vocabulary above the sampler's limit");
     if (V <= kSampleSmemVocab)
       CK(cudaFuncSetAttribute(sample_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1527,10 +1530,26 @@ void run_role(ls_engine& e, int role, int n, const int* host_meta, bool graphabl
   e.kernel_launches += e.graph_kernels[key];
 }
 
+void raise_device_error(ls_engine& e, int err);
+
 void check_device(ls_engine& e) {
   int err = 0;
   CK(cudaMemcpy(&err, e.err_dev, sizeof(int), cudaMemcpyDeviceToHost));
   e.d2h_bytes += sizeof(int);
+  raise_device_error(e, err);
+}
+
+// Per-step form: queue the error word's copy behind the step's kernels (no
+// extra synchronisation), then, after the step's stream synchronisation,
+// check_fetched_error() reads it.
+void fetch_device_error(ls_engine& e) {
+  CK(cudaMemcpyAsync(e.err_host, e.err_dev, sizeof(int), cudaMemcpyDeviceToHost, e.stream));
+  e.d2h_bytes += sizeof(int);
+}
+
+void check_fetched_error(ls_engine& e) { raise_device_error(e, *e.err_host); }
+
+void raise_device_error(ls_engine& e, int err) {
   if (err != kDevOk) {
     CK(cudaMemset(e.err_dev, 0, sizeof(int)));
     static const char* names[] = {"ok", "TMA stage wait timed out", "free-stage wait timed out",
@@ -1757,9 +1776,10 @@ void cycle(ls_engine& e, const std::vector<CycleLane>& lanes, std::vector<Dec>& 
       CK(cudaMemcpyAsync(logits_out + (long)ep_rows[j] * e.V, e.logits + (long)j * e.V,
                          sizeof(float) * e.V, cudaMemcpyDeviceToHost, e.stream));
   }
+  fetch_device_error(e);
   CK(cudaStreamSynchronize(e.stream));
   e.staging_next = 0;
-  check_device(e);
+  check_fetched_error(e);
   for (int j = 0; j < M; ++j) {
     if (e.sampling) {
       for (int f = 0; f < 5; ++f) dec[ep_rows[j]][f] = e.dec_host[j * 5 + f];
@@ -2042,9 +2062,10 @@ std::vector<long long> run_ar(ls_engine& e, long long first, int max_new, long l
     CK(cudaMemcpyAsync(e.amax_host, e.sampling ? e.dec_dev : e.amax_dev, sizeof(long long),
                        cudaMemcpyDeviceToHost, e.stream));
     e.d2h_bytes += sizeof(long long);
+    fetch_device_error(e);
     CK(cudaStreamSynchronize(e.stream));
     e.staging_next = 0;
-    check_device(e);
+    check_fetched_error(e);
     committed.push_back(e.amax_host[0]);
     index++;
     if (stop_token >= 0 && committed.back() == stop_token) break;
