@@ -444,6 +444,8 @@ struct ls_engine {
   // (RoPE, pool write) itself. Prefill calls (several positions of one
   // timeline) keep the projection's fused RoPE / KV-write epilogue.
   bool qkv_planes = false;
+  // the call forks a timeline (some lane copies a parent's mapping prefix)
+  bool call_forks = false;
   // attention grid depth of the call being enqueued: one CTA per 128-position
   // chunk of its longest timeline (graphs round it up to an even count and are
   // re-captured when it changes)
@@ -683,9 +685,12 @@ struct ls_engine {
     CK(cudaMallocHost(&dec_host, sizeof(long long) * 5 * (size_t)cap));
     CK(cudaMallocHost(&err_host, sizeof(int)));
     REQUIRE(V <= kSampleChunk * kSampleMaxChunks, LS_EINVAL, "vocabulary above the sampler's limit");
-    if (V <= kSampleSmemVocab)
-      CK(cudaFuncSetAttribute(sample_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (V <= kSampleSmemVocab) {
+      CK(cudaFuncSetAttribute(sample_kernel<true, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                               (int)(V * sizeof(float))));
+      CK(cudaFuncSetAttribute(sample_kernel<true, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              (int)(V * sizeof(float))));
+    }
     gemm_tickets = dalloc<int>(gemm_ticket_count);
     std::vector<float> inv(HD / 2);
     for (int i = 0; i < HD / 2; ++i)
@@ -1144,7 +1149,11 @@ void klaunch(ls_engine& e, void (*kernel)(KArgs...), dim3 grid, dim3 block, size
 
 void map_update(ls_engine& e, Meta meta, int n) {
   klaunch(e, map_update_kernel, dim3(n), dim3(128), 0, meta, n, e.map, e.max_ctx, e.rows, e.err_dev);
-  e.serialize_next = true;
+  // attention reads slot ids before its wait: unless the update only appends
+  // each lane's new position and every attention layer takes it from the
+  // metadata (decode form, no fork, no QK-norm layer), later kernels start
+  // after it has completed
+  e.serialize_next = e.call_forks || !e.qkv_planes || e.mc.qk_norm != 0;
 }
 
 // Threads of a per-lane row kernel: one float4 column each, at most 1024.
@@ -1349,10 +1358,14 @@ void head_decisions(ls_engine& e, Meta meta, int lane0, int lanes) {
     REQUIRE(lanes <= e.max_rows, LS_ECAPACITY, "too many sampled readout rows");
     SampleArgs sa{meta, lane0, e.logits, e.V, e.sparams_dev, e.q1_bank, e.r_bank,
                   e.max_rows, e.samp_work, e.dec_dev, e.err_dev};
-    if (e.V <= kSampleSmemVocab)
-      klaunch(e, sample_kernel<true>, dim3(lanes), dim3(kSampleThreads), (size_t)e.V * sizeof(float), sa);
-    else
-      klaunch(e, sample_kernel<false>, dim3(lanes), dim3(kSampleThreads), 0, sa);
+    // rows in 16-byte steps when the vocabulary allows (logits, banks and
+    // scratch rows are then 16-byte aligned)
+    const size_t psm = (size_t)e.V * sizeof(float);
+    const dim3 g(lanes), b(kSampleThreads);
+    if (e.V <= kSampleSmemVocab && e.V % 4 == 0) klaunch(e, sample_kernel<true, 4>, g, b, psm, sa);
+    else if (e.V <= kSampleSmemVocab) klaunch(e, sample_kernel<true, 1>, g, b, psm, sa);
+    else if (e.V % 4 == 0) klaunch(e, sample_kernel<false, 4>, g, b, 0, sa);
+    else klaunch(e, sample_kernel<false, 1>, g, b, 0, sa);
   } else {
     klaunch(e, argmax_kernel, dim3(lanes), dim3(1024), 0, (const float*)e.logits, e.V, (long)e.V,
             e.amax_dev);
@@ -1484,12 +1497,15 @@ void run_role(ls_engine& e, int role, int n, const int* host_meta, bool graphabl
   upload_meta(e, role, host_meta, n);
   int longest = 1;
   bool single = true;   // no lane shares its timeline with an earlier lane of the call
+  bool forks = false;
   for (int b = 0; b < n; ++b) {
     longest = std::max(longest, host_meta[b * kMetaFields + kMetaPos] + 1);
     single = single && host_meta[b * kMetaFields + kMetaAhead] <= 0;
+    forks = forks || host_meta[b * kMetaFields + kMetaForkRow] >= 0;
   }
   const int chunks = cdiv(longest, kAttnChunk);
   e.qkv_planes = single;
+  e.call_forks = forks;
   if (!(graphable && e.sc.use_graphs)) {
     e.attn_chunks = std::min(chunks, e.max_chunks);
     enqueue_role(e, role, n, po);
@@ -1497,7 +1513,7 @@ void run_role(ls_engine& e, int role, int n, const int* host_meta, bool graphabl
     return;
   }
   e.attn_chunks = std::min(chunks + (chunks & 1), e.max_chunks);
-  const auto key = std::make_pair(role * 2 + (e.sampling ? 1 : 0), n);
+  const auto key = std::make_pair(role * 4 + (e.sampling ? 2 : 0) + (forks ? 1 : 0), n);
   auto it = e.graphs.find(key);
   if (it != e.graphs.end() && (e.graph_chunks[key] != e.attn_chunks || e.graph_planes[key] != e.qkv_planes)) {
     CK(cudaStreamSynchronize(e.stream));
@@ -2707,10 +2723,11 @@ int ls_time_core_gemms(ls_engine* e, int n, int iters, double* avg_launch_ms, do
             eg.I = e->I;
             gemm(*e, *g[i], *x[i], eg, kEpiSwiGLU, n);
           } else {
-            gemm_store(*e, *g[i], *x[i], e->part, n);
+            gemm_split_store(*e, *g[i], *x[i], n);   // the decode path's form (split planes)
           }
           if (count) {
-            // weights + (hi, lo) activation rows read + outputs written
+            // weights + (hi, lo) activation rows read + outputs written (the
+            // algorithmic output; split planes add splits x that, not counted)
             const double out_b = i == 2 ? 2.0 * 2 * n * (g[i]->Mw / 2) : 4.0 * n * g[i]->Mw;
             bytes += 2.0 * g[i]->Mw * g[i]->K + 2.0 * 2 * n * g[i]->K + out_b;
             launches++;

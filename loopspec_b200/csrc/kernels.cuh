@@ -394,10 +394,13 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attn_kernel(AttnArgs a) {
   static_assert(PER * NSG == kAttnChunk, "chunk must split evenly over sub-groups");
   // Before waiting on the preceding kernel (the QKV projection that writes q
   // and the newest position's K/V), load what earlier work wrote: the lane
-  // metadata (uploaded before the role call), the timeline's slot ids (the
-  // kernel after the call's mapping update is launched without programmatic
-  // overlap, so the update has completed before any later kernel starts) and
-  // the K/V rows of every older position.
+  // metadata (uploaded before the role call), the timeline's slot ids of the
+  // positions older than this call and the K/V rows of those positions. A
+  // call whose mapping update forks a timeline or appends several positions
+  // per timeline (prefill) launches the kernel after the update without
+  // programmatic overlap, so those entries are final before this kernel
+  // starts; otherwise the update only appends each lane's new position,
+  // which this kernel takes from the metadata.
   const int b = blockIdx.x, g = blockIdx.y, c = blockIdx.z;
   const int T = a.lane_len ? a.lane_len[b] : a.meta.get(kMetaPos, b) + 1;
   // the grid holds one CTA per chunk of the call's longest timeline
@@ -426,8 +429,18 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attn_kernel(AttnArgs a) {
   // preceding kernel writes)
   __shared__ float s_cs[HD / 2], s_sn[HD / 2];
   if (a.qkv && threadIdx.x < HD / 2) sincosf((float)(T - 1) * a.inv_freq[threadIdx.x], &s_sn[threadIdx.x], &s_cs[threadIdx.x]);
+  // chunk index of the first position written by this call (the QKV
+  // projection writes one position per lane; prefill puts several positions
+  // of one timeline in a call)
+  const int fresh = T - 1 - (a.lane_len ? 0 : a.meta.get(kMetaAhead, b)) - start;
   int sv = -1;
-  if (threadIdx.x < kAttnChunk && (int)threadIdx.x < n_in) sv = a.map[(long)row * a.max_ctx + start + threadIdx.x];
+  if (threadIdx.x < kAttnChunk && (int)threadIdx.x < n_in) {
+    // decode form: the new position's slot comes from the lane metadata, so
+    // its mapping entry (appended by this call's mapping update, which may
+    // still be running) is never read
+    sv = a.qkv && (int)threadIdx.x == fresh ? a.meta.get(kMetaSlot, b)
+                                            : a.map[(long)row * a.max_ctx + start + threadIdx.x];
+  }
   if (threadIdx.x < kAttnChunk) {
     if ((int)threadIdx.x < n_in && (sv < 0 || sv >= a.n_slots)) {
       atomicExch(a.err, kDevBadIndex);
@@ -437,10 +450,6 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attn_kernel(AttnArgs a) {
   }
   __syncthreads();
   uint4 kr[PER], vr[PER];
-  // chunk index of the first position written by this call (the QKV
-  // projection writes one position per lane; prefill puts several positions
-  // of one timeline in a call)
-  const int fresh = T - 1 - (a.lane_len ? 0 : a.meta.get(kMetaAhead, b)) - start;
 #pragma unroll
   for (int t = 0; t < PER; ++t) {
     const int i = sg + t * NSG;

@@ -79,18 +79,51 @@ __device__ __forceinline__ float sblock_max(float v, float* red) {
   return warp_max(t);
 }
 
+// Row loops visit E consecutive elements per step (E = 4 when V % 4 == 0: one
+// 16-byte load or store per step, else 1): thread tid takes steps tid,
+// tid + blockDim.x, ... and, within a step, elements in index order. A row's
+// sums are therefore a fixed function of the row.
+template <int E>
+struct Vf {
+  float v[E];
+};
+
+template <int E>
+__device__ __forceinline__ Vf<E> ldv(const float* p, int j) {
+  Vf<E> x;
+  if constexpr (E == 4) {
+    const float4 q = *reinterpret_cast<const float4*>(p + 4 * j);
+    x.v[0] = q.x;
+    x.v[1] = q.y;
+    x.v[2] = q.z;
+    x.v[3] = q.w;
+  } else {
+    x.v[0] = p[j];
+  }
+  return x;
+}
+
+template <int E>
+__device__ __forceinline__ void stv(float* p, int j, const Vf<E>& x) {
+  if constexpr (E == 4) *reinterpret_cast<float4*>(p + 4 * j) = make_float4(x.v[0], x.v[1], x.v[2], x.v[3]);
+  else p[j] = x.v[0];
+}
+
 // Largest value v (an element of p) with F(v) >= target, F(v) = sum or count
 // of the elements >= v, found by bisection over the bit patterns in [0, max].
-template <bool COUNT>
+template <bool COUNT, int E>
 __device__ float bisect_cutoff(const float* p, int V, float target, float pmax, float* red) {
   uint32_t lo = 0u, hi = __float_as_uint(pmax) + 1u;   // F(lo) >= target > F(hi)
   while (hi - lo > 1u) {
     const uint32_t mid = lo + (hi - lo) / 2u;
     const float v = __uint_as_float(mid);
     float acc = 0.f;
-    for (int t = threadIdx.x; t < V; t += blockDim.x) {
-      const float x = p[t];
-      if (x >= v) acc += COUNT ? 1.f : x;
+#pragma unroll 4
+    for (int j = threadIdx.x; j < V / E; j += blockDim.x) {
+      const Vf<E> x = ldv<E>(p, j);
+#pragma unroll
+      for (int i = 0; i < E; ++i)
+        if (x.v[i] >= v) acc += COUNT ? 1.f : x.v[i];
     }
     const float tot = sblock_sum(acc, red);
     if (tot >= target) lo = mid;
@@ -99,20 +132,30 @@ __device__ float bisect_cutoff(const float* p, int V, float target, float pmax, 
   return __uint_as_float(lo);
 }
 
+// Sum of w[base, base + 64) (elements past V count as 0) in index order, with
+// 16 loads in flight instead of one dependent load per element.
+__device__ __forceinline__ float seg_sum64(const float* w, int base, int V) {
+  float a = 0.f;
+#pragma unroll
+  for (int i0 = 0; i0 < 64; i0 += 16) {
+    float x[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) x[i] = base + i0 + i < V ? w[base + i0 + i] : 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) a += x[i];
+  }
+  return a;
+}
+
 // Inverse-CDF draw from non-negative weights w (need not be normalised).
 // target = u * total; first 2048-chunk whose inclusive CDF exceeds target, then
 // the first token of it whose inclusive CDF exceeds target - preceding mass.
 __device__ int block_pick(const float* w, int V, float u, float* s_chunk, float* red, int* s_idx) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   const int nch = (V + kSampleChunk - 1) / kSampleChunk;
+  static_assert(kSampleChunk / 32 == 64, "64 tokens per lane");
   for (int c = warp; c < nch; c += nw) {          // one warp per chunk, 64 tokens per lane
-    float a = 0.f;
-    const int base = c * kSampleChunk + lane * (kSampleChunk / 32);
-    for (int i = 0; i < kSampleChunk / 32; ++i) {
-      const int t = base + i;
-      if (t < V) a += w[t];
-    }
-    a = warp_sum(a);
+    const float a = warp_sum(seg_sum64(w, c * kSampleChunk + lane * 64, V));
     if (lane == 0) s_chunk[c] = a;
   }
   __syncthreads();
@@ -142,12 +185,8 @@ __device__ int block_pick(const float* w, int V, float u, float* s_chunk, float*
   const float rem = red[0];
   __syncthreads();
   if (warp == 0) {
-    const int base = ch * kSampleChunk + lane * (kSampleChunk / 32);
-    float a = 0.f;
-    for (int i = 0; i < kSampleChunk / 32; ++i) {
-      const int t = base + i;
-      if (t < V) a += w[t];
-    }
+    const int base = ch * kSampleChunk + lane * 64;
+    const float a = seg_sum64(w, base, V);
     float incl = a;                                  // inclusive scan over lanes
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -162,14 +201,23 @@ __device__ int block_pick(const float* w, int V, float u, float* s_chunk, float*
       if (lane == hl) {
         float c = excl;
         int found = base;
-        for (int i = 0; i < kSampleChunk / 32; ++i) {
-          const int t = base + i;
-          if (t >= V) break;
-          c += w[t];
-          if (c > rem) {
-            found = t;
-            break;
+        bool done = false;
+        for (int i0 = 0; i0 < 64 && !done; i0 += 16) {   // 16 loads in flight, then scan
+          float x[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) x[i] = base + i0 + i < V ? w[base + i0 + i] : 0.f;
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int t = base + i0 + i;
+            if (!done && t < V) {
+              c += x[i];
+              if (c > rem) {
+                found = t;
+                done = true;
+              }
+            }
           }
+          if (base + i0 + 16 >= V) break;
         }
         s_idx[1] = found;
       }
@@ -184,11 +232,11 @@ __device__ int block_pick(const float* w, int V, float u, float* s_chunk, float*
   return r;
 }
 
-template <bool SMEM_P>
+template <bool SMEM_P, int E>
 __global__ void __launch_bounds__(kSampleThreads) sample_kernel(SampleArgs a) {
   pdl_launch_dependents();
   pdl_wait();
-  extern __shared__ float s_p[];
+  extern __shared__ __align__(16) float s_p[];
   __shared__ float red[32];
   __shared__ float s_chunk[kSampleMaxChunks];
   __shared__ int s_idx[2];
@@ -214,38 +262,65 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(SampleArgs a) {
   }
 
   // softmax(logits / T) in fp32
+  const int NV = V / E, tid = threadIdx.x, nt = blockDim.x;
   const float invT = 1.f / prm.temperature;
   float m = -INFINITY;
-  for (int t = threadIdx.x; t < V; t += blockDim.x) m = fmaxf(m, lg[t] * invT);
+#pragma unroll 4
+  for (int j = tid; j < NV; j += nt) {
+    const Vf<E> x = ldv<E>(lg, j);
+#pragma unroll
+    for (int i = 0; i < E; ++i) m = fmaxf(m, x.v[i] * invT);
+  }
   m = sblock_max(m, red);
   float s = 0.f;
-  for (int t = threadIdx.x; t < V; t += blockDim.x) {
-    const float e = expf(lg[t] * invT - m);
-    P[t] = e;
-    s += e;
+#pragma unroll 4
+  for (int j = tid; j < NV; j += nt) {
+    Vf<E> x = ldv<E>(lg, j);
+#pragma unroll
+    for (int i = 0; i < E; ++i) {
+      x.v[i] = expf(x.v[i] * invT - m);
+      s += x.v[i];
+    }
+    stv<E>(P, j, x);
   }
   s = sblock_sum(s, red);
   float pmax = 0.f;
-  for (int t = threadIdx.x; t < V; t += blockDim.x) {
-    const float p = P[t] / s;
-    P[t] = p;
-    pmax = fmaxf(pmax, p);
+#pragma unroll 4
+  for (int j = tid; j < NV; j += nt) {
+    Vf<E> x = ldv<E>(P, j);
+#pragma unroll
+    for (int i = 0; i < E; ++i) {
+      x.v[i] = x.v[i] / s;
+      pmax = fmaxf(pmax, x.v[i]);
+    }
+    stv<E>(P, j, x);
   }
   pmax = sblock_max(pmax, red);
   // top-k / top-p cutoffs, then renormalise over the kept support
   const int k = prm.top_k >= V ? 0 : prm.top_k;
   if (k > 0 || prm.top_p < 1.f) {
     float cut = 0.f;
-    if (prm.top_p < 1.f) cut = bisect_cutoff<false>(P, V, prm.top_p, pmax, red);
-    if (k > 0) cut = fmaxf(cut, bisect_cutoff<true>(P, V, (float)k, pmax, red));
+    if (prm.top_p < 1.f) cut = bisect_cutoff<false, E>(P, V, prm.top_p, pmax, red);
+    if (k > 0) cut = fmaxf(cut, bisect_cutoff<true, E>(P, V, (float)k, pmax, red));
     float kept = 0.f;
-    for (int t = threadIdx.x; t < V; t += blockDim.x) {
-      const float p = P[t] >= cut ? P[t] : 0.f;
-      P[t] = p;
-      kept += p;
+#pragma unroll 4
+    for (int j = tid; j < NV; j += nt) {
+      Vf<E> x = ldv<E>(P, j);
+#pragma unroll
+      for (int i = 0; i < E; ++i) {
+        x.v[i] = x.v[i] >= cut ? x.v[i] : 0.f;
+        kept += x.v[i];
+      }
+      stv<E>(P, j, x);
     }
     kept = sblock_sum(kept, red);
-    for (int t = threadIdx.x; t < V; t += blockDim.x) P[t] = P[t] / kept;
+#pragma unroll 4
+    for (int j = tid; j < NV; j += nt) {
+      Vf<E> x = ldv<E>(P, j);
+#pragma unroll
+      for (int i = 0; i < E; ++i) x.v[i] = x.v[i] / kept;
+      stv<E>(P, j, x);
+    }
   }
   __syncthreads();
 
@@ -257,21 +332,34 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(SampleArgs a) {
 
   if (kind == 0) {                                     // q1: draw and keep P
     float* q1 = a.q1_bank + (long)slot * V;
-    for (int t = threadIdx.x; t < V; t += blockDim.x) q1[t] = P[t];
+#pragma unroll 4
+    for (int j = tid; j < NV; j += nt) stv<E>(q1, j, ldv<E>(P, j));
     d[0] = block_pick(P, V, u0, s_chunk, red, s_idx);
     d[1] = 1;
   } else if (kind == 1) {                              // q2: conditional residual
     const float* q1 = a.q1_bank + (long)slot * V;
     float mass = 0.f;
-    for (int t = threadIdx.x; t < V; t += blockDim.x) {
-      const float r = t == first ? 0.f : fmaxf(P[t] - q1[t], 0.f);
-      W[t] = r;
-      mass += r;
+#pragma unroll 4
+    for (int j = tid; j < NV; j += nt) {
+      const Vf<E> p = ldv<E>(P, j), q = ldv<E>(q1, j);
+      Vf<E> r;
+#pragma unroll
+      for (int i = 0; i < E; ++i) {
+        r.v[i] = j * E + i == first ? 0.f : fmaxf(p.v[i] - q.v[i], 0.f);
+        mass += r.v[i];
+      }
+      stv<E>(W, j, r);
     }
     mass = sblock_sum(mass, red);
     const int y = block_pick(W, V, u0, s_chunk, red, s_idx);
     float* R = a.r_bank + (long)slot * V;
-    for (int t = threadIdx.x; t < V; t += blockDim.x) R[t] = mass > 0.f ? W[t] / mass : 0.f;
+#pragma unroll 4
+    for (int j = tid; j < NV; j += nt) {
+      Vf<E> r = ldv<E>(W, j);
+#pragma unroll
+      for (int i = 0; i < E; ++i) r.v[i] = mass > 0.f ? r.v[i] / mass : 0.f;
+      stv<E>(R, j, r);
+    }
     const int action = mass > 0.f && P[first] < q1[first];
     d[0] = action ? y : first;
     d[1] = action;
@@ -286,26 +374,50 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(SampleArgs a) {
       d[2] = 1;
     } else {
       float mF = 0.f, mP = 0.f;
-      for (int t = threadIdx.x; t < V; t += blockDim.x) {
-        const float f = fmaxf(P[t] - q1[t], 0.f);
-        W[t] = f;
-        mF += f;
-        mP += P[t];
+#pragma unroll 4
+      for (int j = tid; j < NV; j += nt) {
+        const Vf<E> p = ldv<E>(P, j), q = ldv<E>(q1, j);
+        Vf<E> f;
+#pragma unroll
+        for (int i = 0; i < E; ++i) {
+          f.v[i] = fmaxf(p.v[i] - q.v[i], 0.f);
+          mF += f.v[i];
+          mP += p.v[i];
+        }
+        stv<E>(W, j, f);
       }
       mF = sblock_sum(mF, red);
       mP = sblock_sum(mP, red);
-      for (int t = threadIdx.x; t < V; t += blockDim.x)
-        W[t] = mF > 0.f ? W[t] / mF : P[t] / (mP > 0.f ? mP : 1.f);
+#pragma unroll 4
+      for (int j = tid; j < NV; j += nt) {
+        Vf<E> f = ldv<E>(W, j);
+        const Vf<E> p = ldv<E>(P, j);
+#pragma unroll
+        for (int i = 0; i < E; ++i) f.v[i] = mF > 0.f ? f.v[i] / mF : p.v[i] / (mP > 0.f ? mP : 1.f);
+        stv<E>(W, j, f);
+      }
       __syncthreads();
       bool acc2 = false;
       if (second >= 0) {
         const float* R = a.r_bank + (long)slot * V;
         acc2 = u1 < fminf(1.f, W[second] / R[second]);
         float mG = 0.f;
-        for (int t = threadIdx.x; t < V; t += blockDim.x) mG += fmaxf(W[t] - R[t], 0.f);
+#pragma unroll 4
+        for (int j = tid; j < NV; j += nt) {
+          const Vf<E> f = ldv<E>(W, j), r = ldv<E>(R, j);
+#pragma unroll
+          for (int i = 0; i < E; ++i) mG += fmaxf(f.v[i] - r.v[i], 0.f);
+        }
         mG = sblock_sum(mG, red);
         if (mG > 0.f) {
-          for (int t = threadIdx.x; t < V; t += blockDim.x) W[t] = fmaxf(W[t] - R[t], 0.f) / mG;
+#pragma unroll 4
+          for (int j = tid; j < NV; j += nt) {
+            Vf<E> f = ldv<E>(W, j);
+            const Vf<E> r = ldv<E>(R, j);
+#pragma unroll
+            for (int i = 0; i < E; ++i) f.v[i] = fmaxf(f.v[i] - r.v[i], 0.f) / mG;
+            stv<E>(W, j, f);
+          }
         }
         __syncthreads();
       }
