@@ -1177,6 +1177,15 @@ L2Prefetch l2pf(const ls_engine& e, const Gemm* a, const Gemm* b = nullptr) {
   return pf;
 }
 
+template <bool VLATE>
+void launch_attention(ls_engine& e, dim3 grid, dim3 blk, int G, const AttnArgs& a) {
+  if (e.HD == 128 && G == 1) klaunch(e, attn_kernel<128, 1, VLATE>, grid, blk, 0, a);
+  else if (e.HD == 128 && G == 2) klaunch(e, attn_kernel<128, 2, VLATE>, grid, blk, 0, a);
+  else if (e.HD == 64 && G == 1) klaunch(e, attn_kernel<64, 1, VLATE>, grid, blk, 0, a);
+  else if (e.HD == 64 && G == 2) klaunch(e, attn_kernel<64, 2, VLATE>, grid, blk, 0, a);
+  else klaunch(e, attn_kernel<64, 4, VLATE>, grid, blk, 0, a);
+}
+
 // planes: the QKV projection's split planes (decode form), or null when the
 // projection's epilogue already wrote q and the new K/V.
 void attention(ls_engine& e, Meta meta, int n, bf16* kp, bf16* vp,
@@ -1194,11 +1203,10 @@ void attention(ls_engine& e, Meta meta, int n, bf16* kp, bf16* vp,
   }
   const dim3 grid(n, e.NKV, e.attn_chunks), blk(kAttnThreads);
   const int G = e.NH / e.NKV;
-  if (e.HD == 128 && G == 1) klaunch(e, attn_kernel<128, 1>, grid, blk, 0, a);
-  else if (e.HD == 128 && G == 2) klaunch(e, attn_kernel<128, 2>, grid, blk, 0, a);
-  else if (e.HD == 64 && G == 1) klaunch(e, attn_kernel<64, 1>, grid, blk, 0, a);
-  else if (e.HD == 64 && G == 2) klaunch(e, attn_kernel<64, 2>, grid, blk, 0, a);
-  else klaunch(e, attn_kernel<64, 4>, grid, blk, 0, a);
+  // more than two CTAs per SM: load V after the scores (four resident CTAs per
+  // SM instead of three; measured faster from 384 CTAs up, slower at 96-160)
+  if ((long)n * e.NKV * e.attn_chunks > 2L * e.num_sms) launch_attention<true>(e, grid, blk, G, a);
+  else launch_attention<false>(e, grid, blk, G, a);
 }
 
 ResidArgs resid_base(ls_engine& e, Meta meta, const Gemm& g) {
@@ -2180,11 +2188,20 @@ void run_decode_attention(const float* q, const void* k_pool, const void* v_pool
              1.0f / std::sqrt((float)hd), sc.err};
   const dim3 grid(n, nkv, max_chunks), blk(kAttnThreads);
   const int G = nh / nkv;
-  if (hd == 128 && G == 1) launch(attn_kernel<128, 1>, grid, blk, 0, stream, false, a);
-  else if (hd == 128 && G == 2) launch(attn_kernel<128, 2>, grid, blk, 0, stream, false, a);
-  else if (hd == 64 && G == 1) launch(attn_kernel<64, 1>, grid, blk, 0, stream, false, a);
-  else if (hd == 64 && G == 2) launch(attn_kernel<64, 2>, grid, blk, 0, stream, false, a);
-  else launch(attn_kernel<64, 4>, grid, blk, 0, stream, false, a);
+  // V loaded after the scores when the grid exceeds two CTAs per SM
+  int dev = 0, sms = 148;
+  CK(cudaGetDevice(&dev));
+  CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  const bool vlate = (long)n * nkv * max_chunks > 2L * sms;
+#define LS_ATTN(HD_, G_)                                                                     \
+  (vlate ? launch(attn_kernel<HD_, G_, true>, grid, blk, 0, stream, false, a)                \
+         : launch(attn_kernel<HD_, G_, false>, grid, blk, 0, stream, false, a))
+  if (hd == 128 && G == 1) LS_ATTN(128, 1);
+  else if (hd == 128 && G == 2) LS_ATTN(128, 2);
+  else if (hd == 64 && G == 1) LS_ATTN(64, 1);
+  else if (hd == 64 && G == 2) LS_ATTN(64, 2);
+  else LS_ATTN(64, 4);
+#undef LS_ATTN
   int err = 0;
   CK(cudaMemcpyAsync(&err, sc.err, sizeof(int), cudaMemcpyDeviceToHost, stream));
   CK(cudaStreamSynchronize(stream));

@@ -382,8 +382,12 @@ __device__ __forceinline__ float plane_sum(const float* p, int splits, long stri
   return v;
 }
 
-template <int HD, int G>
-__global__ void __launch_bounds__(kAttnThreads, 3) attn_kernel(AttnArgs a) {
+// VLATE: load only K before the wait and V after the scores, so K's
+// registers hold V later; one more round trip, four CTAs per SM instead of
+// three (the launch picks it for grids above two CTAs per SM). Same
+// arithmetic either way.
+template <int HD, int G, bool VLATE>
+__global__ void __launch_bounds__(kAttnThreads, VLATE ? 4 : 3) attn_kernel(AttnArgs a) {
   pdl_launch_dependents();
   l2_prefetch_share(a.pf);
   constexpr int LPP = HD / 8;              // lanes per position (16 B each)
@@ -417,6 +421,9 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attn_kernel(AttnArgs a) {
     return;
   }
   __shared__ int s_slot[kAttnChunk];
+  __shared__ float s_raw[G * HD + 2 * HD];               // decode form: plane sums
+  __shared__ float s_q[G * HD];                          // decode form: q after RoPE
+  __shared__ __align__(16) __nv_bfloat16 s_kv[2 * HD];   // decode form: new K, V (bf16)
   __shared__ float sm_m[NW][G], sm_l[NW][G];
   __shared__ float sm_acc[NW][G][HD];
   __shared__ int s_last;
@@ -457,7 +464,7 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attn_kernel(AttnArgs a) {
     const long off = (long)slot * kd + g * HD + sl * 8;
     const bool old_row = slot >= 0 && i < fresh;
     kr[t] = old_row ? *reinterpret_cast<const uint4*>(a.kpool + off) : make_uint4(0, 0, 0, 0);
-    vr[t] = old_row ? *reinterpret_cast<const uint4*>(a.vpool + off) : make_uint4(0, 0, 0, 0);
+    if (!VLATE) vr[t] = old_row ? *reinterpret_cast<const uint4*>(a.vpool + off) : make_uint4(0, 0, 0, 0);
   }
   pdl_wait();
   // after the QKV projection: this thread's query slice and the newest K/V row
@@ -465,9 +472,6 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attn_kernel(AttnArgs a) {
   if (a.qkv) {
     // decode form: q, and (chunk holding T - 1) the new K/V, from the planes
     constexpr int half = HD / 2;
-    __shared__ float s_raw[G * HD + 2 * HD];
-    __shared__ float s_q[G * HD];
-    __shared__ __align__(16) __nv_bfloat16 s_kv[2 * HD];
     const bool own = fresh >= 0 && fresh < kAttnChunk;   // this chunk holds T - 1
     const int D = (a.nh + 2 * a.nkv) * HD;
     const float* pl = a.qkv + (long)b * D;
@@ -511,7 +515,7 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attn_kernel(AttnArgs a) {
       const int i = sg + t * NSG;
       if (own && i == fresh && s_slot[i] >= 0) {
         kr[t] = *reinterpret_cast<const uint4*>(s_kv + sl * 8);
-        vr[t] = *reinterpret_cast<const uint4*>(s_kv + HD + sl * 8);
+        if (!VLATE) vr[t] = *reinterpret_cast<const uint4*>(s_kv + HD + sl * 8);
       }
     }
   } else {
@@ -530,7 +534,7 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attn_kernel(AttnArgs a) {
       if (slot >= 0 && i >= fresh) {
         const long off = (long)slot * kd + g * HD + sl * 8;
         kr[t] = *reinterpret_cast<const uint4*>(a.kpool + off);
-        vr[t] = *reinterpret_cast<const uint4*>(a.vpool + off);
+        if (!VLATE) vr[t] = *reinterpret_cast<const uint4*>(a.vpool + off);
       }
     }
   }
@@ -547,6 +551,16 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attn_kernel(AttnArgs a) {
 #pragma unroll
       for (int o = LPP / 2; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
       sc[h][t] = s_slot[sg + t * NSG] >= 0 ? s : -INFINITY;
+    }
+  }
+  if (VLATE) {   // every V row now: the new one (decode form) from s_kv, the rest from the pool
+#pragma unroll
+    for (int t = 0; t < PER; ++t) {
+      const int i = sg + t * NSG;
+      const int slot = s_slot[i];
+      if (slot < 0) vr[t] = make_uint4(0, 0, 0, 0);
+      else if (a.qkv && i == fresh) vr[t] = *reinterpret_cast<const uint4*>(s_kv + HD + sl * 8);
+      else vr[t] = *reinterpret_cast<const uint4*>(a.vpool + (long)slot * kd + g * HD + sl * 8);
     }
   }
   float m[G], l[G], acc[G][8];
