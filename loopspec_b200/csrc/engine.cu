@@ -1177,13 +1177,21 @@ L2Prefetch l2pf(const ls_engine& e, const Gemm* a, const Gemm* b = nullptr) {
   return pf;
 }
 
-template <bool VLATE>
+template <int FORM>
 void launch_attention(ls_engine& e, dim3 grid, dim3 blk, int G, const AttnArgs& a) {
-  if (e.HD == 128 && G == 1) klaunch(e, attn_kernel<128, 1, VLATE>, grid, blk, 0, a);
-  else if (e.HD == 128 && G == 2) klaunch(e, attn_kernel<128, 2, VLATE>, grid, blk, 0, a);
-  else if (e.HD == 64 && G == 1) klaunch(e, attn_kernel<64, 1, VLATE>, grid, blk, 0, a);
-  else if (e.HD == 64 && G == 2) klaunch(e, attn_kernel<64, 2, VLATE>, grid, blk, 0, a);
-  else klaunch(e, attn_kernel<64, 4, VLATE>, grid, blk, 0, a);
+  if (e.HD == 128 && G == 1) klaunch(e, attn_kernel<128, 1, FORM>, grid, blk, 0, a);
+  else if (e.HD == 128 && G == 2) klaunch(e, attn_kernel<128, 2, FORM>, grid, blk, 0, a);
+  else if (e.HD == 64 && G == 1) klaunch(e, attn_kernel<64, 1, FORM>, grid, blk, 0, a);
+  else if (e.HD == 64 && G == 2) klaunch(e, attn_kernel<64, 2, FORM>, grid, blk, 0, a);
+  else klaunch(e, attn_kernel<64, 4, FORM>, grid, blk, 0, a);
+}
+
+// Attention form for a grid of `ctas` CTAs on `sms` SMs (measured on
+// Ouro-1.4B core calls: the early forms win up to two CTAs per SM, the
+// late-V form above; the wide-register form only while every CTA can be
+// resident beside the projection that precedes it).
+int attention_form(long ctas, int sms) {
+  return ctas <= sms ? kAttnWide : ctas <= 2L * sms ? kAttnMid : kAttnVLate;
 }
 
 // planes: the QKV projection's split planes (decode form), or null when the
@@ -1203,10 +1211,10 @@ void attention(ls_engine& e, Meta meta, int n, bf16* kp, bf16* vp,
   }
   const dim3 grid(n, e.NKV, e.attn_chunks), blk(kAttnThreads);
   const int G = e.NH / e.NKV;
-  // more than two CTAs per SM: load V after the scores (four resident CTAs per
-  // SM instead of three; measured faster from 384 CTAs up, slower at 96-160)
-  if ((long)n * e.NKV * e.attn_chunks > 2L * e.num_sms) launch_attention<true>(e, grid, blk, G, a);
-  else launch_attention<false>(e, grid, blk, G, a);
+  const int form = attention_form((long)n * e.NKV * e.attn_chunks, e.num_sms);
+  if (form == kAttnWide) launch_attention<kAttnWide>(e, grid, blk, G, a);
+  else if (form == kAttnMid) launch_attention<kAttnMid>(e, grid, blk, G, a);
+  else launch_attention<kAttnVLate>(e, grid, blk, G, a);
 }
 
 ResidArgs resid_base(ls_engine& e, Meta meta, const Gemm& g) {
@@ -2188,14 +2196,14 @@ void run_decode_attention(const float* q, const void* k_pool, const void* v_pool
              1.0f / std::sqrt((float)hd), sc.err};
   const dim3 grid(n, nkv, max_chunks), blk(kAttnThreads);
   const int G = nh / nkv;
-  // V loaded after the scores when the grid exceeds two CTAs per SM
   int dev = 0, sms = 148;
   CK(cudaGetDevice(&dev));
   CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-  const bool vlate = (long)n * nkv * max_chunks > 2L * sms;
-#define LS_ATTN(HD_, G_)                                                                     \
-  (vlate ? launch(attn_kernel<HD_, G_, true>, grid, blk, 0, stream, false, a)                \
-         : launch(attn_kernel<HD_, G_, false>, grid, blk, 0, stream, false, a))
+  const int form = attention_form((long)n * nkv * max_chunks, sms);
+#define LS_ATTN(HD_, G_)                                                                        \
+  (form == kAttnWide  ? launch(attn_kernel<HD_, G_, kAttnWide>, grid, blk, 0, stream, false, a)  \
+   : form == kAttnMid ? launch(attn_kernel<HD_, G_, kAttnMid>, grid, blk, 0, stream, false, a)   \
+                      : launch(attn_kernel<HD_, G_, kAttnVLate>, grid, blk, 0, stream, false, a))
   if (hd == 128 && G == 1) LS_ATTN(128, 1);
   else if (hd == 128 && G == 2) LS_ATTN(128, 2);
   else if (hd == 64 && G == 1) LS_ATTN(64, 1);

@@ -382,12 +382,17 @@ __device__ __forceinline__ float plane_sum(const float* p, int splits, long stri
   return v;
 }
 
-// VLATE: load only K before the wait and V after the scores, so K's
-// registers hold V later; one more round trip, four CTAs per SM instead of
-// three (the launch picks it for grids above two CTAs per SM). Same
-// arithmetic either way.
-template <int HD, int G, bool VLATE>
-__global__ void __launch_bounds__(kAttnThreads, VLATE ? 4 : 3) attn_kernel(AttnArgs a) {
+// Register budget by grid size (same arithmetic in every form):
+//   kAttnWide  (<= 1 CTA per SM): K and V before the wait, 2 CTAs' registers
+//              per SM, no spills;
+//   kAttnMid   (<= 2 CTAs per SM): K and V before the wait, 3 per SM;
+//   kAttnVLate (larger grids): only K before the wait, V after the scores in
+//              K's registers; one more round trip, 4 CTAs per SM.
+enum AttnForm : int { kAttnWide = 0, kAttnMid = 1, kAttnVLate = 2 };
+
+template <int HD, int G, int FORM>
+__global__ void __launch_bounds__(kAttnThreads, FORM + 2) attn_kernel(AttnArgs a) {
+  constexpr bool VLATE = FORM == kAttnVLate;
   pdl_launch_dependents();
   l2_prefetch_share(a.pf);
   constexpr int LPP = HD / 8;              // lanes per position (16 B each)
