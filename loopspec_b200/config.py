@@ -105,6 +105,56 @@ PRESETS = {
 }
 
 
+def config_from_hf(hf: dict, name: str | None = None) -> ModelConfig:
+    """ModelConfig from a checkpoint's HF config (config.json as a dict).
+
+    Follows the reference's reading of the two model types:
+    contracts.py:28-53 (family by model_type; Raven layout olmo_post iff
+    head_dim == 128), contracts.py:56-65 (S = total_ut_steps / mean_recurrence),
+    raven.py:87-187 (norm_eps, bias, prelude/core/coda layer counts,
+    init_values embed_scale and std, RoPE base from rope_parameters /
+    rope_theta / rope_base; nonzero test_time_noise is rejected) and
+    integrations/huggingface.py:112-179 (Raven defaults: head_dim = n_embd /
+    n_heads, std = sqrt(2 / (5 n_embd)), embed_scale = sqrt(n_embd)).
+    """
+    mt = hf.get("model_type")
+    rope = (hf.get("rope_parameters") or {}).get("rope_theta")
+    if mt == "ouro":
+        H, heads = hf["hidden_size"], hf["num_attention_heads"]
+        return ModelConfig(
+            name=name or "ouro", family="ouro", layout="ouro", hidden=H, n_heads=heads,
+            n_kv_heads=hf.get("num_key_value_heads") or heads,
+            head_dim=hf.get("head_dim") or H // heads, intermediate=hf["intermediate_size"],
+            vocab=hf["vocab_size"], n_pre_layers=0, n_core_layers=hf["num_hidden_layers"],
+            n_post_layers=0, stages=int(hf["total_ut_steps"]),
+            rope_theta=float(rope if rope is not None else hf.get("rope_theta", 10000.0)),
+            rms_eps=float(hf.get("rms_norm_eps", 1e-6)),
+            tie_embeddings=bool(hf.get("tie_word_embeddings", False)))
+    if mt != "huginn_raven":
+        raise ValueError(f"unsupported recurrent model type: {mt}")
+    noise = hf.get("test_time_noise", 0)
+    if isinstance(noise, bool) or not isinstance(noise, (int, float)) or float(noise) != 0.0:
+        raise ValueError(f"Raven serving does not support test_time_noise; got {noise!r}")
+    H, heads = hf["n_embd"], hf["n_heads"]
+    hd = hf.get("head_dim") or H // heads
+    layout = "olmo_post" if hd == 128 else "raven_pre"
+    theta = rope if rope is not None else hf.get("rope_theta", hf.get("rope_base"))
+    if theta is None:
+        raise ValueError("Raven config requires a RoPE base")
+    init = hf.get("init_values") or {}
+    return ModelConfig(
+        name=name or "raven", family="raven", layout=layout, hidden=H, n_heads=heads,
+        n_kv_heads=hf.get("num_key_value_heads") or heads, head_dim=hd,
+        intermediate=hf["intermediate_size"], vocab=hf["vocab_size"],
+        n_pre_layers=hf["n_layers_in_prelude"], n_core_layers=hf["n_layers_in_recurrent_block"],
+        n_post_layers=hf["n_layers_in_coda"], stages=int(hf["mean_recurrence"]),
+        rope_theta=float(theta), rms_eps=float(hf.get("norm_eps", 1e-6)),
+        embed_scale=float(init.get("embed_scale", math.sqrt(H))),
+        init_std=float(init.get("std", math.sqrt(2 / (5 * H)))),
+        qk_norm=layout == "olmo_post", adapter_bias=bool(hf.get("bias", False)),
+        tie_embeddings=bool(hf.get("tie_embeddings", False)))
+
+
 def get_config(name: str, **overrides) -> ModelConfig:
     cfg = PRESETS[name]
     return replace(cfg, **overrides) if overrides else cfg

@@ -700,12 +700,25 @@ __global__ void argmax_kernel(const float* __restrict__ logits, int V, long ld,
   const float* r = logits + (long)b * ld;
   float best = -INFINITY;
   int bi = 0x7fffffff;
-  for (int v = threadIdx.x; v < V; v += blockDim.x) {
-    const float x = r[v];
+  auto take = [&](float x, int v) {
     if (x > best || (x == best && v < bi)) {
       best = x;
       bi = v;
     }
+  };
+  if (((V | ld) & 3) == 0) {
+    // 16-byte loads, several in flight per thread (rows are 16-byte aligned)
+#pragma unroll 4
+    for (int j = threadIdx.x; j < V / 4; j += blockDim.x) {
+      const float4 x = *reinterpret_cast<const float4*>(r + 4 * j);
+      take(x.x, 4 * j);
+      take(x.y, 4 * j + 1);
+      take(x.z, 4 * j + 2);
+      take(x.w, 4 * j + 3);
+    }
+  } else {
+#pragma unroll 4
+    for (int v = threadIdx.x; v < V; v += blockDim.x) take(r[v], v);
   }
   __shared__ float sb[32];
   __shared__ int si[32];
