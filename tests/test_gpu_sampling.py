@@ -117,3 +117,23 @@ def test_sampling_native_loop_matches_reference_scheduler(name, K, X):
     ar, _ = generate_autoregressive(eng, p, 40)
     assert greedy == ar
     eng.close()
+
+
+def test_run_request_semantics_on_the_engine():
+    """loopspec_b200.request.run_request on the real engine: a seeded sampled
+    request reproduces exactly, greedy (top_k == 1) equals generate_loopspec,
+    and an EOS id ends the request with finish_reason "stop"."""
+    from loopspec_b200.request import run_request
+    cfg, eng = make("tiny", 1, 2)
+    p = prompt(cfg, 24, 5)
+    sp = {"max_new_tokens": 20, "temperature": 1.0, "top_p": 0.9, "top_k": -1, "sampling_seed": 77}
+    a = run_request(eng, {"input_ids": p, "sampling_params": sp})
+    b = run_request(eng, {"input_ids": p, "sampling_params": sp})
+    assert a["output_ids"] == b["output_ids"] and a["seed"] == 77 and len(a["output_ids"]) == 20
+    g = run_request(eng, {"input_ids": p, "sampling_params": {"max_new_tokens": 20, "top_k": 1}})
+    ref, _ = generate_loopspec(eng, p, 20)
+    assert g["output_ids"] == ref and g["finish_reason"] == "length"
+    eos = ref[5]
+    s = run_request(eng, {"input_ids": p, "sampling_params": {"max_new_tokens": 20, "top_k": 1}}, eos_id=eos)
+    assert s["finish_reason"] == "stop" and s["output_ids"] == ref[: ref.index(eos) + 1]
+    eng.close()
