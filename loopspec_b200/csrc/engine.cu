@@ -457,6 +457,12 @@ struct ls_engine {
   // triggers its dependents at its start, and attention reads the
   // timeline's slot ids before its own wait.
   bool serialize_next = false;
+  // Set while prefill runs: its calls are up to 128 lanes wide, where the
+  // QKV and gate_up projections are compute-bound, so they run unsplit (the
+  // epilogue then reads the tile from shared memory instead of re-reading
+  // every split's partial tile from global memory). Decode calls keep the
+  // fixed splits; both generation modes share the same prefill.
+  bool prefill_mode = false;
   int64_t h2d_bytes = 0, d2h_bytes = 0;   // host<->device traffic counters
 
   Timelines tl;
@@ -1073,13 +1079,14 @@ void gemm(ls_engine& e, const Gemm& g, XBuf& x, const GemmEpi& epi, int kind, in
           int lane0 = 0) {
   REQUIRE(n >= 1 && 2 * (lane0 + n) <= x.rows, LS_EINVAL, "GEMM lane count out of range");
   REQUIRE(g.splits >= 1 && g.splits <= kMaxSplits, LS_EINVAL, "bad split count");
+  const int splits = e.prefill_mode && (kind == kEpiQkvRope || kind == kEpiSwiGLU) ? 1 : g.splits;
   REQUIRE(kind != kEpiSwiGLU || g.has_map64, LS_EINVAL, "SwiGLU needs the 64-row weight map");
   const int bn = pick_bn(2 * n);
   const CUtensorMap& xm = x.map(bn);
   const int x_row0 = 2 * lane0;
   const int m_tiles = kind == kEpiSwiGLU ? g.Mw / kGemmBM : cdiv(g.Mw, kGemmBM);
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(m_tiles, g.splits, cdiv(2 * n, bn));
+  cfg.gridDim = dim3(m_tiles, splits, cdiv(2 * n, bn));
   cfg.blockDim = dim3(kGemmThreads);
   cfg.stream = e.stream;
   cudaLaunchAttribute attr[1];
@@ -1092,14 +1099,14 @@ void gemm(ls_engine& e, const Gemm& g, XBuf& x, const GemmEpi& epi, int kind, in
   ep.part_ws = e.gemm_part;
   ep.tile_tickets = e.gemm_tickets;
   REQUIRE((long)cfg.gridDim.x * cfg.gridDim.z <= e.gemm_ticket_count, LS_EINVAL, "GEMM tile tickets too small");
-  REQUIRE((long)cfg.gridDim.x * cfg.gridDim.z * g.splits * (bn / 2) * kGemmBM <= e.gemm_part_elems ||
-              g.splits == 1, LS_EINVAL, "GEMM partial scratch too small");
+  REQUIRE((long)cfg.gridDim.x * cfg.gridDim.z * splits * (bn / 2) * kGemmBM <= e.gemm_part_elems ||
+              splits == 1, LS_EINVAL, "GEMM partial scratch too small");
   const CUtensorMap& wm = kind == kEpiSwiGLU ? g.map64 : g.map;
 #define LS_GEMM_K(BN, ST, EPI)                                                                     \
   do {                                                                                              \
     cfg.dynamicSmemBytes = GemmSmem<BN, ST>::kTotal;                                                \
     CK(cudaLaunchKernelEx(&cfg, gemm_tc_kernel<BN, ST, EPI>, wm, xm, ep, g.Mw, g.K, n, x_row0, \
-                          g.splits, e.err_dev));                                                   \
+                          splits, e.err_dev));                                                     \
   } while (0)
 #define LS_GEMM(BN, ST)                                           \
   do {                                                            \
@@ -1656,6 +1663,11 @@ long long prefill(ls_engine& e, const int64_t* prompt, int P, float* logits_out)
   e.draw_cycle = 0;   // the first token uses draw 0, decode cycles 1, 2, ...
   CK(cudaMemsetAsync(e.err_dev, 0, sizeof(int), e.stream));
   CK(cudaEventRecord(e.ev0, e.stream));
+  struct PrefillMode {   // unsplit wide projections while prefill enqueues (see prefill_mode)
+    ls_engine& e;
+    explicit PrefillMode(ls_engine& x) : e(x) { e.prefill_mode = true; }
+    ~PrefillMode() { e.prefill_mode = false; }
+  } prefill_scope(e);
 
   const bool pre_attn = e.mc.n_pre_layers > 0, post_attn = e.mc.n_post_layers > 0;
   Cursor* pre_c = pre_attn ? e.tl.create_root_cursor(kPre, 0) : nullptr;

@@ -43,6 +43,9 @@ def main():
                    help="multi-kernel path: latency-bound kernels prefetch upcoming GEMM weights into L2")
     p.add_argument("--sampling", action="store_true",
                    help="post role: top-p 0.9 sampling decisions instead of greedy argmax")
+    p.add_argument("--prefill-only", action="store_true",
+                   help="time the prefill of a --prompt-token prompt (warm-up run, then one run "
+                        "inside the NVTX range 'prefill') instead of a decode role call")
     a = p.parse_args()
     build()
     cfg = get_config(a.config)
@@ -52,7 +55,19 @@ def main():
                  max_context=max(2048, a.prompt + 64), max_prompt=a.prompt,
                  use_persistent=a.persistent, l2_prefetch=a.l2_prefetch)
     g = torch.Generator().manual_seed(0)
-    eng.prefill(torch.randint(0, cfg.vocab, (a.prompt,), generator=g).tolist())
+    prompt = torch.randint(0, cfg.vocab, (a.prompt,), generator=g).tolist()
+    if a.prefill_only:
+        eng.generate(prompt, 1)                      # warm-up
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_push("prefill")
+        _, st = eng.generate(prompt, 1)
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
+        print(json.dumps({"config": cfg.name, "prompt": a.prompt,
+                          "prefill_device_ms": round(st["prefill_device_ms"], 3)}))
+        eng.close()
+        return
+    eng.prefill(prompt)
     if a.sampling:
         eng.set_sampling(1.0, 0, 0.9, 1234)
     per_call = eng.kernel_count(a.role, a.lanes)

@@ -155,9 +155,10 @@ def test_graphs_and_pdl_do_not_change_results():
 @pytest.mark.parametrize("name", ["tiny", "tiny-raven-llama", "tiny-raven-olmo"])
 def test_persistent_and_multikernel_paths_agree(name):
     # Same model, same prompt: the two execution paths differ only in the
-    # K-split points of their GEMM reductions (fp32 rounding), which deep
-    # post-norm stacks amplify to ~1e-3 in the logits; bound 5e-3, four times
-    # tighter than the oracle tolerance both paths meet.
+    # K-split points of their GEMM reductions (fp32 rounding; the multi-kernel
+    # prefill also runs its wide QKV and gate_up projections unsplit), which
+    # deep post-norm stacks amplify to ~6e-3 in the logits; bound 1e-2, half
+    # the oracle tolerance both paths meet.
     cfg = get_config(name)
     prompt = prompt_for(cfg, 48, seed=4)
     out = {}
@@ -171,13 +172,13 @@ def test_persistent_and_multikernel_paths_agree(name):
             assert eng.kernel_count("core", 3) == 1          # one launch per role call
         eng.close()
     (l1, i1, f1), (l0, i0, f0) = out[True], out[False]
-    assert np.abs(l1 - l0).max() <= 5e-3
+    assert np.abs(l1 - l0).max() <= 1e-2
     n = 0
     while n < min(len(i1), len(i0)) and i1[n] == i0[n]:
         n += 1
     assert n >= 6                                   # both paths follow the same greedy path
     for a, b in zip(f1[:n - 1], f0[:n - 1]):
-        assert np.abs(a - b).max() <= 5e-3
+        assert np.abs(a - b).max() <= 1e-2
 
 
 @PATHS
