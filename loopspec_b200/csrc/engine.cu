@@ -1079,9 +1079,12 @@ void gemm(ls_engine& e, const Gemm& g, XBuf& x, const GemmEpi& epi, int kind, in
           int lane0 = 0) {
   REQUIRE(n >= 1 && 2 * (lane0 + n) <= x.rows, LS_EINVAL, "GEMM lane count out of range");
   REQUIRE(g.splits >= 1 && g.splits <= kMaxSplits, LS_EINVAL, "bad split count");
-  const int splits = e.prefill_mode && (kind == kEpiQkvRope || kind == kEpiSwiGLU) ? 1 : g.splits;
+  // prefill: the wide QKV and gate_up projections run unsplit, on N tiles of
+  // at most 64 lanes so that each weight tile is shared by two CTAs
+  const bool unsplit = e.prefill_mode && (kind == kEpiQkvRope || kind == kEpiSwiGLU);
+  const int splits = unsplit ? 1 : g.splits;
   REQUIRE(kind != kEpiSwiGLU || g.has_map64, LS_EINVAL, "SwiGLU needs the 64-row weight map");
-  const int bn = pick_bn(2 * n);
+  const int bn = unsplit ? std::min(pick_bn(2 * n), 128) : pick_bn(2 * n);
   const CUtensorMap& xm = x.map(bn);
   const int x_row0 = 2 * lane0;
   const int m_tiles = kind == kEpiSwiGLU ? g.Mw / kGemmBM : cdiv(g.Mw, kGemmBM);
@@ -1098,7 +1101,8 @@ void gemm(ls_engine& e, const Gemm& g, XBuf& x, const GemmEpi& epi, int kind, in
   GemmEpi ep = epi;
   ep.part_ws = e.gemm_part;
   ep.tile_tickets = e.gemm_tickets;
-  REQUIRE((long)cfg.gridDim.x * cfg.gridDim.z <= e.gemm_ticket_count, LS_EINVAL, "GEMM tile tickets too small");
+  REQUIRE(splits == 1 || (long)cfg.gridDim.x * cfg.gridDim.z <= e.gemm_ticket_count, LS_EINVAL,
+          "GEMM tile tickets too small");
   REQUIRE((long)cfg.gridDim.x * cfg.gridDim.z * splits * (bn / 2) * kGemmBM <= e.gemm_part_elems ||
               splits == 1, LS_EINVAL, "GEMM partial scratch too small");
   const CUtensorMap& wm = kind == kEpiSwiGLU ? g.map64 : g.map;
