@@ -132,30 +132,46 @@ __device__ float bisect_cutoff(const float* p, int V, float target, float pmax, 
   return __uint_as_float(lo);
 }
 
-// Sum of w[base, base + 64) (elements past V count as 0) in index order, with
-// 16 loads in flight instead of one dependent load per element.
-__device__ __forceinline__ float seg_sum64(const float* w, int base, int V) {
-  float a = 0.f;
-#pragma unroll
-  for (int i0 = 0; i0 < 64; i0 += 16) {
-    float x[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) x[i] = base + i0 + i < V ? w[base + i0 + i] : 0.f;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) a += x[i];
-  }
-  return a;
-}
-
 // Inverse-CDF draw from non-negative weights w (need not be normalised).
 // target = u * total; first 2048-chunk whose inclusive CDF exceeds target, then
 // the first token of it whose inclusive CDF exceeds target - preceding mass.
+//
+// A chunk is walked as 64 rows of 32 consecutive tokens, one token per lane
+// (consecutive lanes read consecutive words: no shared-memory bank conflicts),
+// with a warp prefix scan per row and the row totals added in row order. The
+// chunk totals and the in-chunk search use this same order, so the chunk the
+// totals pick always contains the crossing.
+__device__ __forceinline__ float warp_incl_scan(float x) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  return x;
+}
+
+__device__ __forceinline__ float chunk_total(const float* w, int c, int V) {
+  const int lane = threadIdx.x & 31;
+  float tot = 0.f;
+  for (int i0 = 0; i0 < kSampleChunk / 32; i0 += 8) {
+    float x[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int t = c * kSampleChunk + (i0 + j) * 32 + lane;
+      x[j] = t < V ? w[t] : 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) tot += __shfl_sync(0xffffffffu, warp_incl_scan(x[j]), 31);
+  }
+  return tot;
+}
+
 __device__ int block_pick(const float* w, int V, float u, float* s_chunk, float* red, int* s_idx) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   const int nch = (V + kSampleChunk - 1) / kSampleChunk;
-  static_assert(kSampleChunk / 32 == 64, "64 tokens per lane");
-  for (int c = warp; c < nch; c += nw) {          // one warp per chunk, 64 tokens per lane
-    const float a = warp_sum(seg_sum64(w, c * kSampleChunk + lane * 64, V));
+  for (int c = warp; c < nch; c += nw) {          // one warp per chunk
+    const float a = chunk_total(w, c, V);
     if (lane == 0) s_chunk[c] = a;
   }
   __syncthreads();
@@ -185,46 +201,26 @@ __device__ int block_pick(const float* w, int V, float u, float* s_chunk, float*
   const float rem = red[0];
   __syncthreads();
   if (warp == 0) {
-    const int base = ch * kSampleChunk + lane * 64;
-    const float a = seg_sum64(w, base, V);
-    float incl = a;                                  // inclusive scan over lanes
+    int found = -1;                                  // nothing exceeds: first token of the chunk
+    float pre = 0.f;
+    for (int i0 = 0; i0 < kSampleChunk / 32 && found < 0; i0 += 8) {
+      float x[8];
 #pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const float n = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += n;
-    }
-    const float excl = incl - a;
-    const unsigned hit = __ballot_sync(0xffffffffu, incl > rem);
-    int tok = ch * kSampleChunk;                     // nothing exceeds: first token of the chunk
-    if (hit) {
-      const int hl = __ffs(hit) - 1;
-      if (lane == hl) {
-        float c = excl;
-        int found = base;
-        bool done = false;
-        for (int i0 = 0; i0 < 64 && !done; i0 += 16) {   // 16 loads in flight, then scan
-          float x[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) x[i] = base + i0 + i < V ? w[base + i0 + i] : 0.f;
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int t = base + i0 + i;
-            if (!done && t < V) {
-              c += x[i];
-              if (c > rem) {
-                found = t;
-                done = true;
-              }
-            }
-          }
-          if (base + i0 + 16 >= V) break;
-        }
-        s_idx[1] = found;
+      for (int j = 0; j < 8; ++j) {
+        const int t = ch * kSampleChunk + (i0 + j) * 32 + lane;
+        x[j] = t < V ? w[t] : 0.f;
       }
-      __syncwarp();
-    } else if (lane == 0) {
-      s_idx[1] = tok;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (found < 0) {                             // warp-uniform
+          const float incl = warp_incl_scan(x[j]);
+          const unsigned hit = __ballot_sync(0xffffffffu, pre + incl > rem);
+          if (hit) found = ch * kSampleChunk + (i0 + j) * 32 + (__ffs(hit) - 1);
+          else pre += __shfl_sync(0xffffffffu, incl, 31);
+        }
+      }
     }
+    if (lane == 0) s_idx[1] = found >= 0 ? found : ch * kSampleChunk;
   }
   __syncthreads();
   const int r = s_idx[1];
