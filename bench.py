@@ -55,7 +55,25 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--synthetic-accept", type=float, default=0.05,
                    help="post-norm gain of the separately reported high-acceptance run (0: skip)")
+    p.add_argument("--temperature", type=float, default=0.0,
+                   help="> 0: sampled decoding (with --top-p / --top-k) instead of greedy")
+    p.add_argument("--top-p", type=float, default=1.0)
+    p.add_argument("--top-k", type=int, default=0)
+    p.add_argument("--seed", type=int, default=1234, help="sampling seed of request i is seed + i")
     return p.parse_args()
+
+
+def decode_mode(args):
+    if args.temperature <= 0:
+        return "greedy"
+    return f"sampled T={args.temperature} top_p={args.top_p} top_k={args.top_k} seed={args.seed}+i"
+
+
+def sampling_of(args):
+    """None (greedy) or the request sampling dict of generate_loopspec."""
+    if args.temperature <= 0:
+        return None
+    return {"temperature": args.temperature, "top_p": args.top_p, "top_k": args.top_k}
 
 
 def dist_env():
@@ -235,8 +253,9 @@ def engine_arm(args):
     def prompt_of(i):
         return make_prompt(cfg, args.prompt, 1000 * rank + i)
 
+    samp = sampling_of(args)
     for i in range(args.warmup):
-        generate_loopspec(eng, prompt_of(i), args.new_tokens)
+        generate_loopspec(eng, prompt_of(i), args.new_tokens, sampling=samp, seed=args.seed + i)
     barrier()
     clocks = Clocks(local)
     clocks.start()
@@ -245,7 +264,8 @@ def engine_arm(args):
     agg = None
     for i in range(args.steps):
         t0 = time.perf_counter()
-        ids, st = generate_loopspec(eng, prompt_of(args.warmup + i), args.new_tokens)
+        ids, st = generate_loopspec(eng, prompt_of(args.warmup + i), args.new_tokens, sampling=samp,
+                                    seed=args.seed + args.warmup + i)
         wall += time.perf_counter() - t0
         dec_tok += st["decode_tokens"]
         dec_ms += st["decode_device_ms"]
@@ -286,7 +306,8 @@ def engine_arm(args):
         del w2
 
     # autoregressive beside it (one request, same prompt distribution)
-    ar_ids, ar_st = generate_autoregressive(eng, prompt_of(0), args.new_tokens)
+    ar_ids, ar_st = generate_autoregressive(eng, prompt_of(0), args.new_tokens, sampling=samp,
+                                            seed=args.seed)
     ar_tok_s = ar_st["decode_tokens"] / (ar_st["decode_device_ms"] / 1e3)
 
     # roofline of the dominant kernel: the tcgen05 GEMM, over a core-weight sweep
@@ -315,7 +336,7 @@ def engine_arm(args):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (uniform-random prompt ids, random-init weights seed 0)",
             "config": {"workload": f"{cfg.name} LoopSpec first={args.first} second={args.second} "
-                                   f"greedy, prompt {args.prompt}, {args.new_tokens} new tokens",
+                                   f"{decode_mode(args)}, prompt {args.prompt}, {args.new_tokens} new tokens",
                        "global_batch": world, "seq_len": args.prompt + args.new_tokens,
                        "parallelism": f"replicas x{world}",
                        "l2": "inputs larger than L2 (2.47 GB of core weights per iteration)"},
