@@ -1048,7 +1048,7 @@ struct ls_engine {
     LS_SMEM(32, 4);
     LS_SMEM(64, 4);
     LS_SMEM(128, 3);
-    LS_SMEM(256, 3);
+    LS_SMEM(256, 2);
 #undef LS_SMEM
 #undef LS_SMEM1
     const int row_smem = std::max(QD + 2 * KVD, 2 * H) * (int)sizeof(float);
@@ -1124,7 +1124,7 @@ void gemm(ls_engine& e, const Gemm& g, XBuf& x, const GemmEpi& epi, int kind, in
     case 32: LS_GEMM(32, 4); break;
     case 64: LS_GEMM(64, 4); break;
     case 128: LS_GEMM(128, 3); break;
-    default: LS_GEMM(256, 3); break;
+    default: LS_GEMM(256, 2); break;
   }
 #undef LS_GEMM
 #undef LS_GEMM_K
