@@ -320,11 +320,12 @@ def engine_arm(args):
     except (OSError, KeyError, ValueError):
         peak_gbs, peak_src = 6650.0, "fallback"
     achieved = launch_bytes / (launch_ms / 1e3) / 1e9
-    # DRAM traffic per launch: an ncu capture (--set full) of the layer-0 QKV, O
-    # and gate_up GEMMs of a 4-lane Ouro-1.4B core call read 79.97 MB for 79.70
-    # MB of weights, ratio 1.0034 (no tile read twice); scaled to this sweep's
-    # average launch.
-    traffic = launch_bytes * (79.97 / 79.70)
+    # DRAM traffic per launch: an ncu capture (dram__bytes_read/write.sum) of the
+    # layer-0 QKV, O, gate_up and down projections of a 4-lane Ouro-1.4B core call
+    # in their decode form read 103.234 MB and wrote 0 B for 103.203 MB of
+    # algorithmic bytes (ratio 1.0003: no tile read twice, the split planes stay in
+    # L2); scaled to this sweep's average launch.
+    traffic = launch_bytes * (103.234 / 103.203)
     decode_bytes = bytes_per_decode(cfg, sch, agg, args.prompt)
     decode_gbs = decode_bytes / (dec_ms / 1e3) / 1e9
 
@@ -353,8 +354,9 @@ def engine_arm(args):
                          "achieved": round(achieved, 1), "peak": peak_gbs, "unit": "GB/s",
                          "frac": round(achieved / peak_gbs, 4), "peak_source": peak_src,
                          "traffic": round(traffic),
-                         "traffic_source": "ncu dram__bytes_read+write of the core GEMMs, ratio to "
-                                           "their algorithmic bytes applied to this sweep",
+                         "traffic_source": "ncu dram__bytes_read+write of one layer's four core GEMMs "
+                                           "(profiles/dram_core_gemms_ouro1.4b_4lanes.md), ratio "
+                                           "to their algorithmic bytes applied to this sweep",
                          "lanes": lanes,
                          "bytes_per_launch": round(launch_bytes),
                          "avg_launch_us": round(launch_ms * 1e3, 3)},
