@@ -2598,26 +2598,37 @@ int ls_time_role(ls_engine* e, int role, int n, int context_len, int iters, doub
     REQUIRE(n <= e->max_rows, LS_ECAPACITY, "too many lanes");
     const int P = e->prefill_len + 1;
     REQUIRE(context_len >= 1 && context_len <= P, LS_EINVAL, "context_len must not exceed the prompt");
-    // Synthetic lanes: fresh rows forking the root's first timeline of the
-    // role at context_len - 1, each appending one token there. This overwrites
-    // nothing of the request's timelines but consumes rows/slots until the
-    // next ls_prefill, which resets the pools.
+    // Synthetic lanes, as decode lanes at different depths: lane b gets a
+    // fresh row forking the request's timeline of depth b mod S (core; pre
+    // and post have one depth) at context_len - 1 and appends one token
+    // there, so up to S lanes read distinct K/V. The fork runs once, in a
+    // warm-up call; the timed calls only append, like decode calls. This
+    // overwrites nothing of the request's timelines but consumes rows/slots
+    // until the next ls_prefill, which resets the pools.
     const bool attn = role == kCore || (role == kPre && e->mc.n_pre_layers) ||
                       (role == kPost && e->mc.n_post_layers);
     int* m = stage_meta(*e);
     for (int b = 0; b < n; ++b) {
       Cursor c;
       if (attn) {
-        Cursor* root = e->tl.get_or_create_cursor(role, role == kPost ? e->S - 1 : 0, 0, -1);
+        const int depth = role == kPost ? e->S - 1 : role == kCore ? b % e->S : 0;
+        Cursor* root = e->tl.get_or_create_cursor(role, depth, 0, -1);
         c.row = e->tl.alloc_row();
         c.seq_len = context_len - 1;
         c.pending_parent_row = root->row;
       }
       fill_lane(*e, m, b, 1, context_len - 1, attn ? &c : nullptr, b, b);
     }
-    run_role(*e, role, n, m, true);  // warm-up (captures the graph)
+    run_role(*e, role, n, m, true);  // forks the rows
+    int* m2 = stage_meta(*e);
+    std::copy(m, m + kMetaFields * e->cap, m2);
+    for (int b = 0; b < n; ++b) {
+      put(*e, m2, kMetaForkRow, b, -1);
+      put(*e, m2, kMetaForkLen, b, 0);
+    }
+    run_role(*e, role, n, m2, true);  // warm-up of the append-only call (captures its graph)
     CK(cudaEventRecord(e->ev0, e->stream));
-    for (int i = 0; i < iters; ++i) run_role(*e, role, n, m, true);
+    for (int i = 0; i < iters; ++i) run_role(*e, role, n, m2, true);
     CK(cudaEventRecord(e->ev1, e->stream));
     CK(cudaEventSynchronize(e->ev1));
     e->staging_next = 0;
