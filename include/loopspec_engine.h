@@ -97,6 +97,26 @@ int ls_load_weight(ls_engine* eng, const char* name, const void* dptr, int dtype
 /* Validate the weight set, allocate pools and build TMA descriptors. */
 int ls_finalize(ls_engine* eng);
 
+/* Tensor parallelism (one process per GPU). Each rank creates its engine
+ * from its shard: n_heads, n_kv_heads and intermediate divided by the rank
+ * count, q/k/v rows and gate/up rows of its heads and columns, o_proj and
+ * down_proj columns of the same, q_norm / k_norm entries of its heads, all
+ * other weights whole. After ls_finalize, ls_tp_init allocates the rank's
+ * exchange region and writes LS_TP_HANDLE_BYTES describing it (CUDA IPC
+ * handle, PCI bus id, layout size); the caller gathers every rank's bytes in
+ * rank order (any host collective) and passes them to ls_tp_attach. From
+ * then on every rank must make the same calls with the same arguments: the
+ * layers add all ranks' O / down partials and QK-norm sums in rank order
+ * over NVLink, so all ranks compute identical rows and decisions. A peer
+ * that stops publishing makes the waiting ranks fail with LS_EDEVICE after a
+ * bounded wait. Ranks must be on distinct GPUs, the persistent path is not
+ * supported, and ls_tp_init must precede the first role call. The reference
+ * rejects tensor parallelism for LoopSpec (cli.py:97-108); the target is
+ * TP-N greedy output equal to TP-1 output. */
+#define LS_TP_HANDLE_BYTES 128
+int ls_tp_init(ls_engine* eng, int rank, int ranks, void* handle_out);
+int ls_tp_attach(ls_engine* eng, const void* handles);
+
 /* Reset request state and prefill every timeline of the prompt (pre, all S
  * core depths, each post endpoint with attention), then pick the first token
  * greedily (RecurrentRequest.prefill request.py:111-192 and

@@ -65,6 +65,7 @@ RETAIN_FN = ctypes.CFUNCTYPE(None, ctypes.c_void_p, ctypes.POINTER(ctypes.c_int6
                              ctypes.c_int32)
 
 _P = ctypes.c_void_p
+TP_HANDLE_BYTES = 128   # LS_TP_HANDLE_BYTES
 _PI64 = ctypes.POINTER(_i64)
 _PF32 = ctypes.POINTER(_f32)
 
@@ -73,6 +74,8 @@ SIGNATURES = [
     ("ls_create", _i32, [ctypes.POINTER(ModelCfg), ctypes.POINTER(SchedCfg), _i32, ctypes.POINTER(_P)]),
     ("ls_load_weight", _i32, [_P, ctypes.c_char_p, _P, _i32, _PI64, _i32]),
     ("ls_finalize", _i32, [_P]),
+    ("ls_tp_init", _i32, [_P, _i32, _i32, _P]),
+    ("ls_tp_attach", _i32, [_P, _P]),
     ("ls_prefill", _i32, [_P, _PI64, _i32, _PF32, _PI64]),
     ("ls_set_sampling", _i32, [_P, _f32, _i32, _f32, _u64]),
     ("ls_cycle", _i32, [_P, _PI64, _i32, _PI64, _PF32]),

@@ -18,6 +18,8 @@ enum DeviceError : int {
   kDevTimeoutEmpty = 2,   // producer waited too long for a free stage
   kDevTimeoutAcc = 3,     // epilogue waited too long for the accumulator
   kDevBadIndex = 4,       // a metadata index was out of range (access skipped)
+  // 5 and 6 belong to the persistent path (stack_api.cuh)
+  kDevTimeoutPeer = 7,    // a tensor-parallel peer did not publish its partials in time
 };
 
 // Lane metadata: int32 [cap][kMetaFields], lane-major (one record per lane,
@@ -292,6 +294,16 @@ __device__ __forceinline__ void l2_prefetch_share(const L2Prefetch& pf) {
 // global load before the first use, so a row costs one memory round trip per
 // dependent phase rather than one per element.
 __device__ __forceinline__ float4 ld_f4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+
+__device__ __forceinline__ float4 ldcg4(const float* p) { return __ldcg(reinterpret_cast<const float4*>(p)); }
+
+__device__ __forceinline__ int ld_volatile(const int* p) { return *reinterpret_cast<const volatile int*>(p); }
+
+__device__ __forceinline__ unsigned long long gtime_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
 
 __device__ __forceinline__ float4 ld_bf4(const __nv_bfloat16* p) {
   const uint2 u = *reinterpret_cast<const uint2*>(p);

@@ -465,6 +465,17 @@ struct ls_engine {
   bool prefill_mode = false;
   int64_t h2d_bytes = 0, d2h_bytes = 0;   // host<->device traffic counters
 
+  // Tensor parallelism (ls_tp_init / ls_tp_attach): this rank's exchange
+  // region, one allocation so that one IPC handle maps it: flags and epoch
+  // (first 256 bytes), the O and down projections' split planes, the QK-norm
+  // sums. tp_base holds every rank's region in rank order (this rank's own
+  // included); the layers exchange only once tp_ranks > 1 (after attach).
+  int tp_ranks = 1, tp_rank = 0, tp_want = 1;
+  char* tp_region = nullptr;
+  size_t tp_bytes = 0, tp_off_o = 0, tp_off_d = 0, tp_off_qk = 0;
+  std::vector<char*> tp_base;
+  std::vector<void*> tp_opened;   // peer mappings, closed before the engine frees memory
+
   Timelines tl;
   int prefill_len = -1;   // len(prompt) - 1 of the current request
 
@@ -481,6 +492,7 @@ struct ls_engine {
   ~ls_engine() {
     if (device >= 0) cudaSetDevice(device);
     for (auto& g : graphs) cudaGraphExecDestroy(g.second);
+    for (void* p : tp_opened) cudaIpcCloseMemHandle(p);
     for (void* p : allocs) cudaFree(p);
     if (meta_host) cudaFreeHost(meta_host);
     if (amax_host) cudaFreeHost(amax_host);
@@ -1143,8 +1155,8 @@ void gemm_store(ls_engine& e, const Gemm& g, XBuf& x, float* out, int n, int lan
 
 // y as g.splits partial planes [split][cap][Mw] in e.part, for a row kernel
 // that adds them in split order (no split-K ticket or re-read in the GEMM).
-void gemm_split_store(ls_engine& e, const Gemm& g, XBuf& x, int n) {
-  GemmEpi ep = store_to(e.part);
+void gemm_split_store(ls_engine& e, const Gemm& g, XBuf& x, int n, float* planes = nullptr) {
+  GemmEpi ep = store_to(planes ? planes : e.part);
   ep.split_stride = (long)e.cap * g.Mw;
   gemm(e, g, x, ep, kEpiSplitStore, n);
 }
@@ -1256,6 +1268,36 @@ void resid(ls_engine& e, ResidArgs a, int n) {
   else klaunch(e, resid_epi_kernel<1, 8, 1024>, grid, dim3(thr), 0, a);
 }
 
+// ------------------------------------------------------- tensor parallelism
+constexpr size_t kTpEpochOff = 64;   // byte offset of the epoch counter in a region
+
+// Every rank's buffer at byte offset `off` of its region, in rank order.
+TpView tp_view(const ls_engine& e, size_t off) {
+  TpView t{};
+  t.ranks = e.tp_ranks;
+  t.epoch = reinterpret_cast<const int*>(e.tp_region + kTpEpochOff);
+  for (int r = 0; r < e.tp_ranks; ++r) {
+    t.flags[r] = reinterpret_cast<const int*>(e.tp_base[r]);
+    t.data[r] = reinterpret_cast<const float*>(e.tp_base[r] + off);
+  }
+  return t;
+}
+
+void tp_publish(ls_engine& e, int slot) {
+  klaunch(e, tp_publish_kernel, dim3(1), dim3(32), 0, reinterpret_cast<int*>(e.tp_region + kTpEpochOff),
+          reinterpret_cast<int*>(e.tp_region), slot);
+}
+
+// A row-sharded projection (O or down): this rank's split planes go to its
+// exchange region and are published; the residual kernel that follows adds
+// every rank's planes.
+void tp_split_store(ls_engine& e, const Gemm& g, XBuf& x, int n, ResidArgs& ra, size_t off, int slot) {
+  gemm_split_store(e, g, x, n, reinterpret_cast<float*>(e.tp_region + off));
+  tp_publish(e, slot);
+  ra.tp = tp_view(e, off);
+  ra.tp_slot = slot;
+}
+
 // Norm applied to the input of a layer's first GEMM (none for OLMo2 post-norm).
 const bf16* input_norm(const ls_engine& e, const LayerW& w) {
   return e.mc.layout == LS_LAYOUT_OLMO_POST ? nullptr : w.n_in;
@@ -1283,7 +1325,17 @@ void run_stack(ls_engine& e, Stack& st, int n, Meta meta, const StackEnd& end) {
       QkvArgs qa{meta, e.NH, e.NKV, e.HD, e.part, w.g_qkv.splits, (long)e.cap * w.g_qkv.Mw,
                  w.qn, w.kn, e.inv_freq, e.mc.rms_eps,
                  e.q, kp, vp, e.n_slots, e.err_dev};
-      klaunch(e, qkv_epi_kernel, dim3(n), dim3(256), (size_t)(e.QD + 2 * e.KVD) * sizeof(float), qa);
+      const size_t smem = (size_t)(e.QD + 2 * e.KVD) * sizeof(float);
+      if (e.tp_ranks > 1) {
+        // the norm spans every rank's heads: exchange the sums of squares
+        qa.tp = tp_view(e, e.tp_off_qk);
+        qa.tp_sums = reinterpret_cast<float*>(e.tp_region + e.tp_off_qk);
+        qa.tp_phase = 1;
+        klaunch(e, qkv_epi_kernel, dim3(n), dim3(256), smem, qa);
+        tp_publish(e, kTpSlotQk);
+        qa.tp_phase = 2;
+      }
+      klaunch(e, qkv_epi_kernel, dim3(n), dim3(256), smem, qa);
     } else if (e.qkv_planes) {
       // decode: split planes; attention sums them and does RoPE / the KV write
       gemm_split_store(e, w.g_qkv, e.x_h, n);
@@ -1302,9 +1354,9 @@ void run_stack(ls_engine& e, Stack& st, int n, Meta meta, const StackEnd& end) {
       gemm(e, w.g_qkv, e.x_h, ep, kEpiQkvRope, n);
     }
     attention(e, meta, n, kp, vp, l2pf(e, &w.g_o, &w.g_gu), !w.qn && e.qkv_planes ? &w.g_qkv : nullptr);
-    gemm_split_store(e, w.g_o, e.x_attn, n);
-
     ResidArgs ra = resid_base(e, meta, w.g_o);
+    if (e.tp_ranks > 1) tp_split_store(e, w.g_o, e.x_attn, n, ra, e.tp_off_o, kTpSlotO);
+    else gemm_split_store(e, w.g_o, e.x_attn, n);
     ra.resid = e.h;
     ra.out_h = e.r;
     ra.x = e.x_h.ptr;
@@ -1324,9 +1376,9 @@ void run_stack(ls_engine& e, Stack& st, int n, Meta meta, const StackEnd& end) {
     eg.x_act = e.x_act.ptr;
     eg.I = e.I;
     gemm(e, w.g_gu, e.x_h, eg, kEpiSwiGLU, n);
-    gemm_split_store(e, w.g_down, e.x_act, n);
-
     ResidArgs rb = resid_base(e, meta, w.g_down);
+    if (e.tp_ranks > 1) tp_split_store(e, w.g_down, e.x_act, n, rb, e.tp_off_d, kTpSlotDown);
+    else gemm_split_store(e, w.g_down, e.x_act, n);
     rb.resid = e.r;
     rb.out_h = e.h;
     if (L != LS_LAYOUT_RAVEN_PRE) rb.a_norm_w = w.n_pff;
@@ -1597,9 +1649,10 @@ void raise_device_error(ls_engine& e, int err) {
     CK(cudaMemset(e.err_dev, 0, sizeof(int)));
     static const char* names[] = {"ok", "TMA stage wait timed out", "free-stage wait timed out",
                                   "accumulator wait timed out", "metadata index out of range",
-                                  "grid phase wait timed out", "persistent CTAs not co-resident"};
+                                  "grid phase wait timed out", "persistent CTAs not co-resident",
+                                  "tensor-parallel peer wait timed out"};
     throw EngineError(LS_EDEVICE, std::string("device reported: ") +
-                                      (err > 0 && err < 7 ? names[err] : "unknown error"));
+                                      (err > 0 && err < 8 ? names[err] : "unknown error"));
   }
 }
 
@@ -2396,6 +2449,85 @@ int ls_finalize(ls_engine* e) {
   if (!e) return LS_EINVAL;
   try {
     e->finalize();
+  } catch (const std::exception& ex) {
+    return fail(e, ex);
+  }
+  return LS_OK;
+}
+
+int ls_tp_init(ls_engine* e, int rank, int ranks, void* handle_out) {
+  if (!e || !handle_out) return LS_EINVAL;
+  try {
+    REQUIRE(e->finalized, LS_EINVAL, "engine not finalized");
+    REQUIRE(e->tp_region == nullptr, LS_EINVAL, "tensor parallelism already initialised");
+    REQUIRE(ranks >= 2 && ranks <= kTpMax && rank >= 0 && rank < ranks, LS_EINVAL,
+            "tensor parallelism needs 2..8 ranks and 0 <= rank < ranks");
+    REQUIRE(!e->sc.use_persistent, LS_EINVAL, "tensor parallelism runs on the multi-kernel path only");
+    REQUIRE(e->graphs.empty(), LS_EINVAL, "initialise tensor parallelism before the first role call");
+    CK(cudaSetDevice(e->device));
+    // planes of the widest O / down projection of any stack
+    int so = 1, sd = 1;
+    for (const Stack* st : {&e->pre, &e->core, &e->post})
+      for (const LayerW& w : st->layers) {
+        so = std::max(so, w.g_o.splits);
+        sd = std::max(sd, w.g_down.splits);
+      }
+    auto up = [](size_t b) { return (b + 255) & ~size_t(255); };
+    e->tp_off_o = 256;
+    e->tp_off_d = e->tp_off_o + up(sizeof(float) * (size_t)so * e->cap * e->H);
+    e->tp_off_qk = e->tp_off_d + up(sizeof(float) * (size_t)sd * e->cap * e->H);
+    e->tp_bytes = e->tp_off_qk + up(sizeof(float) * 2 * (size_t)e->cap);
+    e->tp_region = e->dalloc<char>(e->tp_bytes);   // zeroed: flags and epoch start at 0
+    cudaIpcMemHandle_t h;
+    CK(cudaIpcGetMemHandle(&h, e->tp_region));
+    unsigned char* out = static_cast<unsigned char*>(handle_out);
+    std::memset(out, 0, LS_TP_HANDLE_BYTES);
+    std::memcpy(out, &h, sizeof(h));
+    CK(cudaDeviceGetPCIBusId(reinterpret_cast<char*>(out) + sizeof(h), LS_TP_HANDLE_BYTES - (int)sizeof(h) - 8,
+                             e->device));
+    std::memcpy(out + LS_TP_HANDLE_BYTES - 8, &e->tp_bytes, 8);
+    e->tp_rank = rank;
+    e->tp_want = ranks;
+  } catch (const std::exception& ex) {
+    return fail(e, ex);
+  }
+  return LS_OK;
+}
+
+int ls_tp_attach(ls_engine* e, const void* handles) {
+  if (!e || !handles) return LS_EINVAL;
+  try {
+    REQUIRE(e->tp_region != nullptr && e->tp_ranks == 1, LS_EINVAL, "call ls_tp_init once, then ls_tp_attach once");
+    CK(cudaSetDevice(e->device));
+    const unsigned char* in = static_cast<const unsigned char*>(handles);
+    const int n = e->tp_want;
+    const int bus_len = LS_TP_HANDLE_BYTES - (int)sizeof(cudaIpcMemHandle_t) - 8;
+    std::vector<std::string> bus(n);
+    for (int r = 0; r < n; ++r) {
+      const char* b = reinterpret_cast<const char*>(in + (size_t)r * LS_TP_HANDLE_BYTES + sizeof(cudaIpcMemHandle_t));
+      bus[r] = std::string(b, strnlen(b, bus_len));
+      size_t bytes = 0;
+      std::memcpy(&bytes, in + (size_t)(r + 1) * LS_TP_HANDLE_BYTES - 8, 8);
+      REQUIRE(bytes == e->tp_bytes, LS_EINVAL, "tensor-parallel ranks disagree on the exchange layout");
+      for (int q = 0; q < r; ++q)
+        // ranks wait on one another inside kernels, so each needs its own GPU
+        REQUIRE(bus[q] != bus[r], LS_EINVAL, "two tensor-parallel ranks share one GPU");
+    }
+    std::vector<char*> base(n, nullptr);
+    for (int r = 0; r < n; ++r) {
+      if (r == e->tp_rank) {
+        base[r] = e->tp_region;
+        continue;
+      }
+      cudaIpcMemHandle_t h;
+      std::memcpy(&h, in + (size_t)r * LS_TP_HANDLE_BYTES, sizeof(h));
+      void* p = nullptr;
+      CK(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+      e->tp_opened.push_back(p);
+      base[r] = static_cast<char*>(p);
+    }
+    e->tp_base = base;
+    e->tp_ranks = n;
   } catch (const std::exception& ex) {
     return fail(e, ex);
   }

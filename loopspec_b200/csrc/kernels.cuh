@@ -133,6 +133,78 @@ __global__ void cat_state_kernel(Meta meta, int H, const float* __restrict__ ban
   }
 }
 
+// --------------------------------------------------------- tensor parallel
+// The ranks of a tensor-parallel group hold 1/T of the heads and of the MLP
+// columns each. They exchange partial rows through memory every rank has
+// mapped from its peers (CUDA IPC): the O and down projections' split planes,
+// and the per-lane sums of squares of OLMo2's QK-norm. A rank publishes an
+// exchange by advancing its epoch counter and raising its flag for the
+// exchange's slot to the new epoch. A consumer waits (bounded) until every
+// rank's flag for that slot has reached its own epoch, then reads all ranks'
+// partials in rank order, so every rank computes bit-identical rows. The
+// producer does not overwrite a published buffer before every consumer has
+// read it: a rank writes a slot's buffer again only after it has consumed
+// the next exchange, which each peer publishes after its last read of the
+// buffer.
+constexpr int kTpMax = 8;
+constexpr int kTpSlotO = 0, kTpSlotDown = 1, kTpSlotQk = 2, kTpSlots = 3;
+constexpr unsigned long long kTpWaitNs = 10000000000ull;   // 10 s per exchange
+
+struct TpView {
+  int ranks;                    // > 1: this kernel adds the peers' partials
+  const int* epoch;             // this rank's exchange counter
+  const int* flags[kTpMax];     // each rank's flags [kTpSlots], in rank order
+  const float* data[kTpMax];    // each rank's buffer of this exchange
+};
+
+__device__ __forceinline__ int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_sys(int* p, int v) {
+  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Thread 0 waits for every rank's flag of `slot` to reach this rank's epoch.
+// Returns false for the whole CTA when the wait gave up (error recorded, or
+// another kernel had already recorded one).
+__device__ bool tp_wait(const TpView& t, int slot, int* err) {
+  __shared__ int ok;
+  if (threadIdx.x == 0) {
+    const int want = ld_volatile(t.epoch);
+    const unsigned long long t0 = gtime_ns();
+    int good = 1;
+    for (int r = 0; r < t.ranks && good; ++r) {
+      for (uint32_t i = 0; ld_acquire_sys(t.flags[r] + slot) < want; ++i) {
+        if ((i & 63u) == 63u && (ld_volatile(err) != 0 || gtime_ns() - t0 > kTpWaitNs)) {
+          if (ld_volatile(err) == 0) atomicExch(err, kDevTimeoutPeer);
+          good = 0;
+          break;
+        }
+        __nanosleep(32);
+      }
+    }
+    ok = good;
+  }
+  __syncthreads();
+  return ok != 0;
+}
+
+// Publish this rank's partials of one exchange once the producing kernel has
+// completed: advance the epoch and raise this rank's flag of `slot` to it.
+__global__ void tp_publish_kernel(int* epoch, int* flags, int slot) {
+  pdl_launch_dependents();
+  pdl_wait();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    const int e = *epoch + 1;
+    *epoch = e;
+    st_release_sys(flags + slot, e);
+  }
+}
+
 // ------------------------------------------------------- residual epilogue
 // a = y[b] (+ bias); a = a_norm ? rms(a) * wa : a;
 // out = (resid ? resid : 0) + a; out = final_norm ? rms(out) * wf : out;
@@ -156,6 +228,8 @@ struct ResidArgs {
   float eps;
   int* err;
   L2Prefetch pf;               // weights of the GEMMs that follow
+  TpView tp;                   // ranks > 1: y = every rank's planes, rank by rank
+  int tp_slot;
 };
 
 // NV float4 columns per thread; BATCH split planes loaded at once (one round
@@ -183,25 +257,32 @@ __global__ void __launch_bounds__(MAXT) resid_epi_kernel(ResidArgs a) {
     bb[k] = on && a.bias ? ld_bf4(a.bias + 4 * j) : z;
   }
   pdl_wait();
+  const bool tp = a.tp.ranks > 1;
+  if (tp && !tp_wait(a.tp, a.tp_slot, a.err)) return;
+  const int n_src = tp ? a.tp.ranks : 1;
   float ss = 0.f;
 #pragma unroll
   for (int k = 0; k < NV; ++k) {
     const int j = threadIdx.x + k * blockDim.x;
     const bool on = j < H4;
     rr[k] = on && a.resid ? ld_f4(a.resid + (long)b * H + 4 * j) : z;
-    // y = the GEMM's split planes added in split order, BATCH loads in flight
+    // y = the GEMM's split planes added in split order (rank by rank under
+    // tensor parallelism; peers' planes over NVLink), BATCH loads in flight
     v[k] = z;
     if (on) {
-      const float* py = a.part + (long)b * H + 4 * j;
-      for (int s0 = 0; s0 < a.splits; s0 += BATCH) {
-        float4 t[BATCH];
+      for (int src = 0; src < n_src; ++src) {
+        const float* py = (tp ? a.tp.data[src] : a.part) + (long)b * H + 4 * j;
+        for (int s0 = 0; s0 < a.splits; s0 += BATCH) {
+          float4 t[BATCH];
 #pragma unroll
-        for (int u = 0; u < BATCH; ++u)
-          if (s0 + u < a.splits) t[u] = ld_f4(py + (s0 + u) * a.split_stride);
+          for (int u = 0; u < BATCH; ++u)
+            if (s0 + u < a.splits) t[u] = tp ? ldcg4(py + (s0 + u) * a.split_stride)
+                                             : ld_f4(py + (s0 + u) * a.split_stride);
 #pragma unroll
-        for (int u = 0; u < BATCH; ++u)
-          if (s0 + u < a.splits)
-            v[k] = make_float4(v[k].x + t[u].x, v[k].y + t[u].y, v[k].z + t[u].z, v[k].w + t[u].w);
+          for (int u = 0; u < BATCH; ++u)
+            if (s0 + u < a.splits)
+              v[k] = make_float4(v[k].x + t[u].x, v[k].y + t[u].y, v[k].z + t[u].z, v[k].w + t[u].w);
+        }
       }
     }
     if (a.bias) v[k] = make_float4(v[k].x + bb[k].x, v[k].y + bb[k].y, v[k].z + bb[k].z, v[k].w + bb[k].w);
@@ -262,6 +343,12 @@ struct QkvArgs {
   __nv_bfloat16* vpool;
   int n_slots;
   int* err;
+  // Tensor parallel QK-norm (q_norm_w set, tp.ranks > 1): phase 1 writes this
+  // rank's (sum q^2, sum k^2) of each lane to tp_sums and returns; phase 2
+  // adds every rank's sums in rank order and normalises by the whole width.
+  TpView tp;
+  int tp_phase;
+  float* tp_sums;   // this rank's [cap][2]
 };
 
 __global__ void qkv_epi_kernel(QkvArgs a) {
@@ -271,6 +358,8 @@ __global__ void qkv_epi_kernel(QkvArgs a) {
   __shared__ float red[32];
   const int b = blockIdx.x;
   const int qd = a.nh * a.hd, kd = a.nkv * a.hd, D = qd + 2 * kd;
+  const bool tp = a.q_norm_w && a.tp.ranks > 1;
+  if (tp && a.tp_phase == 2 && !tp_wait(a.tp, kTpSlotQk, a.err)) return;
   const float* pb = a.part + (long)b * D;
   float ssq = 0.f, ssk = 0.f;
   for (int i = threadIdx.x; i < D; i += blockDim.x) {
@@ -280,7 +369,27 @@ __global__ void qkv_epi_kernel(QkvArgs a) {
     if (i < qd) ssq += v * v;
     else if (i < qd + kd) ssk += v * v;
   }
-  if (a.q_norm_w) {
+  if (tp && a.tp_phase == 1) {
+    ssq = block_sum(ssq, red);
+    ssk = block_sum(ssk, red);
+    if (threadIdx.x == 0) {
+      a.tp_sums[2L * b] = ssq;
+      a.tp_sums[2L * b + 1] = ssk;
+    }
+    return;
+  }
+  if (tp) {
+    ssq = 0.f;
+    ssk = 0.f;
+    for (int r = 0; r < a.tp.ranks; ++r) {
+      ssq += __ldcg(a.tp.data[r] + 2L * b);
+      ssk += __ldcg(a.tp.data[r] + 2L * b + 1);
+    }
+    const float iq = rsqrtf(ssq / ((float)qd * a.tp.ranks) + a.eps);
+    const float ik = rsqrtf(ssk / ((float)kd * a.tp.ranks) + a.eps);
+    for (int i = threadIdx.x; i < qd + kd; i += blockDim.x)
+      row[i] = i < qd ? row[i] * iq * bf2f(a.q_norm_w[i]) : row[i] * ik * bf2f(a.k_norm_w[i - qd]);
+  } else if (a.q_norm_w) {
     const float iq = rsqrtf(block_sum(ssq, red) / qd + a.eps);
     const float ik = rsqrtf(block_sum(ssk, red) / kd + a.eps);
     for (int i = threadIdx.x; i < qd + kd; i += blockDim.x)

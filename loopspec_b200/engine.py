@@ -77,6 +77,22 @@ class Engine:
         _lib.check(self.L.ls_load_weight(self.h, name.encode(), ctypes.c_void_p(t.data_ptr()), 0,
                                          _i64p(shape), len(shape)), self.h)
 
+    # ------------------------------------------------------ tensor parallel
+    def tp_init(self, rank: int, ranks: int) -> bytes:
+        """Allocate this rank's exchange region; returns the bytes every peer
+        needs to map it (ls_tp_init)."""
+        buf = ctypes.create_string_buffer(_lib.TP_HANDLE_BYTES)
+        _lib.check(self.L.ls_tp_init(self.h, int(rank), int(ranks), buf), self.h)
+        return buf.raw
+
+    def tp_attach(self, handles) -> None:
+        """Map every rank's region (ls_tp_attach); `handles` in rank order."""
+        blob = b"".join(handles)
+        if any(len(h) != _lib.TP_HANDLE_BYTES for h in handles):
+            raise ValueError("each handle must be LS_TP_HANDLE_BYTES long")
+        buf = ctypes.create_string_buffer(blob, len(blob))
+        _lib.check(self.L.ls_tp_attach(self.h, buf), self.h)
+
     # ----------------------------------------------------------------- calls
     def prefill(self, prompt_ids, want_logits=False):
         p = np.ascontiguousarray(prompt_ids, dtype=np.int64)

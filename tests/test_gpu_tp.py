@@ -1,0 +1,129 @@
+"""Tensor parallelism on 2 GPUs (skipped with fewer): OLMo2-layout Raven with
+QK-norm and Llama-layout Raven with GQA (2 KV heads), split over 2 ranks in 2 processes.
+
+Checks: every rank computes bit-identical logits; the TP logits match the
+float32 oracle of the whole model; greedy LoopSpec equals AR under TP; TP
+tokens equal the single-GPU engine's. Each rank reaches a barrier before it
+releases its engine, so no rank frees memory its peer may still read."""
+
+import datetime
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+from loopspec_b200.config import get_config
+from loopspec_b200.schedule import PipelineSchedule
+from loopspec_b200.weights import init_random_weights
+
+pytestmark = pytest.mark.gpu
+
+LOGIT_TOL = 2e-2   # as the single-GPU engine against the oracle
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _prompt(cfg, n, seed):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randint(0, cfg.vocab, (n,), generator=g).tolist()
+
+
+def _rank_main(rank, ranks, port, name, over, K, X, prompt, n_new, q):
+    import torch.distributed as dist
+    from loopspec_b200.tp import make_tp_engine
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=ranks, timeout=datetime.timedelta(seconds=120))
+    out = {"rank": rank}
+    eng = None
+    try:
+        cfg = get_config(name, **over)
+        w32 = init_random_weights(cfg, 0, dtype=torch.float32)
+        w = {k: v.to(f"cuda:{rank}", torch.bfloat16).contiguous() for k, v in w32.items()}
+        eng = make_tp_engine(cfg, PipelineSchedule(cfg.stages, K, X), w, rank, ranks, device=rank,
+                             max_context=512, max_prompt=256)
+    except Exception as ex:
+        out["error"] = repr(ex)
+    try:
+        # every rank learns whether all engines exist before any kernel runs
+        built = [None] * ranks
+        dist.all_gather_object(built, "error" not in out)
+        if all(built):
+            try:
+                out["first"], out["logits"] = eng.prefill(prompt, want_logits=True)
+                out["loopspec"], _ = eng.generate(prompt, n_new, mode="loopspec")
+                out["ar"], _ = eng.generate(prompt, n_new, mode="ar")
+            except Exception as ex:   # a peer's bounded waits end its calls too
+                out["error"] = repr(ex)
+        elif "error" not in out:
+            out["error"] = "a peer failed to build its engine"
+        dist.barrier()   # no rank's kernels read a peer's memory past this point
+    finally:
+        if eng is not None:
+            eng.close()
+        q.put(out)
+        dist.destroy_process_group()
+
+
+def _run_tp(name, over, K, X, prompt, n_new, ranks=2):
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main, args=(r, ranks, port, name, over, K, X, prompt, n_new, q))
+             for r in range(ranks)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(ranks):
+        o = q.get(timeout=600)
+        res[o["rank"]] = o
+    for p in procs:
+        p.join(timeout=120)
+    for r in range(ranks):
+        assert "error" not in res[r], res[r]["error"]
+    assert all(p.exitcode == 0 for p in procs)
+    return [res[r] for r in range(ranks)]
+
+
+# tiny-raven-llama has one KV head; two let its GQA heads split over 2 ranks
+@pytest.mark.parametrize("name,over,K,X,n_new", [("tiny-raven-olmo", {}, 1, 4, 24),
+                                                 ("tiny-raven-llama", {"n_kv_heads": 2}, 2, 2, 24)])
+def test_tp2_matches_single_gpu_and_oracle(name, over, K, X, n_new):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    from loopspec_b200.engine import Engine
+    from oracle.model import OracleModel
+    cfg = get_config(name, **over)
+    prompt = _prompt(cfg, 32, seed=1)
+    ranks = _run_tp(name, over, K, X, prompt, n_new)
+    r0 = ranks[0]
+    for o in ranks[1:]:
+        assert np.array_equal(o["logits"], r0["logits"])   # bit-identical rows on every rank
+        assert o["loopspec"] == r0["loopspec"] and o["ar"] == r0["ar"]
+    assert r0["loopspec"] == r0["ar"]                    # greedy LoopSpec == AR under TP
+
+    w32 = init_random_weights(cfg, 0, dtype=torch.float32)
+    wq = {k: v.to(torch.bfloat16).to(torch.float32) for k, v in w32.items()}
+    om = OracleModel(cfg.as_dict(), wq, kv_bf16=True)
+    from oracle.executor import generate_ar_oracle
+    rec = []
+    generate_ar_oracle(om, cfg.stages, prompt, 1, record=rec)
+    assert np.abs(r0["logits"] - rec[0][2].numpy()).max() <= LOGIT_TOL
+    assert r0["first"] == int(np.argmax(r0["logits"]))
+
+    wdev = {k: v.to("cuda:0", torch.bfloat16).contiguous() for k, v in w32.items()}
+    eng = Engine(cfg, PipelineSchedule(cfg.stages, K, X), wdev, device=0, max_context=512, max_prompt=256)
+    try:
+        _, logits1 = eng.prefill(prompt, want_logits=True)
+        single, _ = eng.generate(prompt, n_new, mode="loopspec")
+    finally:
+        eng.close()
+    assert np.abs(r0["logits"] - logits1).max() <= LOGIT_TOL
+    assert r0["loopspec"] == single
