@@ -60,6 +60,9 @@ def parse():
     p.add_argument("--top-p", type=float, default=1.0)
     p.add_argument("--top-k", type=int, default=0)
     p.add_argument("--seed", type=int, default=1234, help="sampling seed of request i is seed + i")
+    p.add_argument("--tp", action="store_true",
+                   help="under torchrun: one request split over the ranks by tensor parallelism "
+                        "(heads and MLP columns; strong scaling) instead of one replica per GPU")
     return p.parse_args()
 
 
@@ -248,10 +251,18 @@ def engine_arm(args):
     sch = schedule_for(cfg, args)
     weights = init_random_weights(cfg, 0, device=f"cuda:{local}", dtype=torch.bfloat16)
     max_ctx = args.prompt + args.new_tokens + 64
-    eng = Engine(cfg, sch, weights, device=local, max_context=max_ctx, max_prompt=args.prompt)
+    tp = args.tp and world > 1
+    if tp:
+        from loopspec_b200.tp import make_tp_engine
+        eng = make_tp_engine(cfg, sch, weights, rank, world, device=local, max_context=max_ctx,
+                             max_prompt=args.prompt)
+        del weights
+    else:
+        eng = Engine(cfg, sch, weights, device=local, max_context=max_ctx, max_prompt=args.prompt)
 
     def prompt_of(i):
-        return make_prompt(cfg, args.prompt, 1000 * rank + i)
+        # under tensor parallelism every rank serves the same request
+        return make_prompt(cfg, args.prompt, (0 if tp else 1000 * rank) + i)
 
     samp = sampling_of(args)
     for i in range(args.warmup):
@@ -276,8 +287,8 @@ def engine_arm(args):
     clk = clocks.stop()
     dec_s_max = max_over_ranks(dec_ms / 1e3)
     wall_max = max_over_ranks(wall)
-    tok_all = sum_over_ranks(dec_tok)
-    new_all = sum_over_ranks(args.steps * args.new_tokens)
+    tok_all = dec_tok if tp else sum_over_ranks(dec_tok)
+    new_all = args.steps * args.new_tokens if tp else sum_over_ranks(args.steps * args.new_tokens)
     value = tok_all / dec_s_max
     e2e = new_all / wall_max
 
@@ -286,7 +297,7 @@ def engine_arm(args):
     # final one). Uniform random weights reject every draft; this shows what the
     # pipeline does when drafts are accepted. Not the headline value.
     synth = None
-    if args.synthetic_accept and rank == 0:
+    if args.synthetic_accept and rank == 0 and not tp:
         w2 = init_random_weights(cfg, 0, device=f"cuda:{local}", dtype=torch.bfloat16)
         for k in w2:
             if k.endswith(("post_attention_layernorm.weight", "post_feedforward_layernorm.weight")):
@@ -326,7 +337,8 @@ def engine_arm(args):
     # algorithmic bytes (ratio 1.0003: no tile read twice, the split planes stay in
     # L2); scaled to this sweep's average launch.
     traffic = launch_bytes * (103.234 / 103.203)
-    decode_bytes = bytes_per_decode(cfg, sch, agg, args.prompt)
+    # per rank: under tensor parallelism its shard of the core and its KV heads
+    decode_bytes = bytes_per_decode(eng.cfg, sch, agg, args.prompt)
     decode_gbs = decode_bytes / (dec_ms / 1e3) / 1e9
 
     if rank == 0:
@@ -334,16 +346,17 @@ def engine_arm(args):
             "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(1e3 * wall_max / args.steps, 1),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "higher_is_better": True, "scaling": "strong" if tp else "weak", "vs_baseline": None,
+            "dtype": "bf16",
             "data": "synthetic (uniform-random prompt ids, random-init weights seed 0)",
             "config": {"workload": f"{cfg.name} LoopSpec first={args.first} second={args.second} "
                                    f"{decode_mode(args)}, prompt {args.prompt}, {args.new_tokens} new tokens",
-                       "global_batch": world, "seq_len": args.prompt + args.new_tokens,
-                       "parallelism": f"replicas x{world}",
+                       "global_batch": 1 if tp else world, "seq_len": args.prompt + args.new_tokens,
+                       "parallelism": f"tp{world}" if tp else f"replicas x{world}",
                        "l2": "inputs larger than L2 (2.47 GB of core weights per iteration)"},
-            "loopspec_tok_s": round(value / world, 2),
+            "loopspec_tok_s": round(value if tp else value / world, 2),
             "ar_tok_s": round(ar_tok_s, 2),
-            "speedup_vs_ar": round((value / world) / ar_tok_s, 3),
+            "speedup_vs_ar": round((value if tp else value / world) / ar_tok_s, 3),
             "mean_accept_len": round(accept_length(agg, sch), 4),
             "counters": {k: int(agg[k]) for k in ("pipeline_cycles", "pre_rows", "recurrent_rows",
                                                   "post_rows", "verified_proposals",
@@ -378,6 +391,9 @@ def engine_arm(args):
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(cfg, sch, args, os.cpu_count() or 1)
         print(json.dumps(line), flush=True)
+    # under tensor parallelism a peer's last kernels may still read this
+    # rank's exchange region: release the engine only after every rank is done
+    barrier()
     eng.close()
     if dist is not None:
         dist.barrier()

@@ -1263,9 +1263,17 @@ void resid(ls_engine& e, ResidArgs a, int n) {
   a.B = n;
   const int thr = row_threads(e.H);
   const dim3 grid(row_grid(e, n, a.pf));
-  if (cdiv(e.H / 4, thr) > 1) klaunch(e, resid_epi_kernel<2, 4, 1024>, grid, dim3(thr), 0, a);
-  else if (thr <= 512) klaunch(e, resid_epi_kernel<1, 10, 512>, grid, dim3(thr), 0, a);
-  else klaunch(e, resid_epi_kernel<1, 8, 1024>, grid, dim3(thr), 0, a);
+  if (a.tp.ranks > 1) {
+    if (cdiv(e.H / 4, thr) > 1) klaunch(e, resid_epi_kernel<2, 4, 1024, true>, grid, dim3(thr), 0, a);
+    else if (thr <= 512) klaunch(e, resid_epi_kernel<1, 10, 512, true>, grid, dim3(thr), 0, a);
+    else klaunch(e, resid_epi_kernel<1, 8, 1024, true>, grid, dim3(thr), 0, a);
+  } else if (cdiv(e.H / 4, thr) > 1) {
+    klaunch(e, resid_epi_kernel<2, 4, 1024, false>, grid, dim3(thr), 0, a);
+  } else if (thr <= 512) {
+    klaunch(e, resid_epi_kernel<1, 10, 512, false>, grid, dim3(thr), 0, a);
+  } else {
+    klaunch(e, resid_epi_kernel<1, 8, 1024, false>, grid, dim3(thr), 0, a);
+  }
 }
 
 // ------------------------------------------------------- tensor parallelism

@@ -234,8 +234,9 @@ struct ResidArgs {
 
 // NV float4 columns per thread; BATCH split planes loaded at once (one round
 // trip for the usual 19 splits when BATCH = 20); MAXT threads at most, which
-// bounds the registers the batch may use.
-template <int NV, int BATCH, int MAXT>
+// bounds the registers the batch may use. TP: add every rank's planes (a
+// separate instantiation, so the single-GPU kernel carries none of it).
+template <int NV, int BATCH, int MAXT, bool TP>
 __global__ void __launch_bounds__(MAXT) resid_epi_kernel(ResidArgs a) {
   pdl_launch_dependents();
   l2_prefetch_share(a.pf);
@@ -257,9 +258,8 @@ __global__ void __launch_bounds__(MAXT) resid_epi_kernel(ResidArgs a) {
     bb[k] = on && a.bias ? ld_bf4(a.bias + 4 * j) : z;
   }
   pdl_wait();
-  const bool tp = a.tp.ranks > 1;
-  if (tp && !tp_wait(a.tp, a.tp_slot, a.err)) return;
-  const int n_src = tp ? a.tp.ranks : 1;
+  if (TP && !tp_wait(a.tp, a.tp_slot, a.err)) return;
+  const int n_src = TP ? a.tp.ranks : 1;
   float ss = 0.f;
 #pragma unroll
   for (int k = 0; k < NV; ++k) {
@@ -271,12 +271,12 @@ __global__ void __launch_bounds__(MAXT) resid_epi_kernel(ResidArgs a) {
     v[k] = z;
     if (on) {
       for (int src = 0; src < n_src; ++src) {
-        const float* py = (tp ? a.tp.data[src] : a.part) + (long)b * H + 4 * j;
+        const float* py = (TP ? a.tp.data[src] : a.part) + (long)b * H + 4 * j;
         for (int s0 = 0; s0 < a.splits; s0 += BATCH) {
           float4 t[BATCH];
 #pragma unroll
           for (int u = 0; u < BATCH; ++u)
-            if (s0 + u < a.splits) t[u] = tp ? ldcg4(py + (s0 + u) * a.split_stride)
+            if (s0 + u < a.splits) t[u] = TP ? ldcg4(py + (s0 + u) * a.split_stride)
                                              : ld_f4(py + (s0 + u) * a.split_stride);
 #pragma unroll
           for (int u = 0; u < BATCH; ++u)
