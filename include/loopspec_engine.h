@@ -160,6 +160,17 @@ int ls_retain(ls_engine* eng, const int64_t* branch_ids, const int64_t* parent_i
 int ls_generate(ls_engine* eng, const int64_t* prompt, int n_prompt, int max_new_tokens,
                 int mode, int64_t stop_token, int64_t* out_ids, int* n_out, ls_stats* stats);
 
+/* ls_generate with a commit callback: after every commit (the first token
+ * included) on_commit(user, ids, n) receives the whole committed output so
+ * far, as the reference's should_stop does (loopspec_scheduler.py:331-346,
+ * pipeline.py:64); a nonzero return ends the request there. This carries
+ * streaming at interval 1 and caller-side stop rules; stop_token still ends
+ * at EOS. The callback runs on the calling thread between GPU steps. */
+typedef int (*ls_commit_fn)(void* user, const int64_t* ids, int n);
+int ls_generate_stream(ls_engine* eng, const int64_t* prompt, int n_prompt, int max_new_tokens,
+                       int mode, int64_t stop_token, ls_commit_fn on_commit, void* user,
+                       int64_t* out_ids, int* n_out, ls_stats* stats);
+
 /* The native scheduler loop of ls_generate mode 0 (continue_pipelined,
  * pipeline.py:254-423, with greedy resolve decisions.py:136-184 and the
  * executor's state-slot pool and counters executor.py:76-107,239-290),

@@ -61,6 +61,7 @@ class Stats(ctypes.Structure):
 
 DECIDE_FN = ctypes.CFUNCTYPE(ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int32)
 CYCLE_FN = ctypes.CFUNCTYPE(None, ctypes.c_void_p, ctypes.POINTER(ctypes.c_int64), ctypes.c_int32)
+COMMIT_FN = ctypes.CFUNCTYPE(ctypes.c_int32, ctypes.c_void_p, ctypes.POINTER(ctypes.c_int64), ctypes.c_int32)
 RETAIN_FN = ctypes.CFUNCTYPE(None, ctypes.c_void_p, ctypes.POINTER(ctypes.c_int64), ctypes.c_int32,
                              ctypes.c_int32)
 
@@ -82,6 +83,8 @@ SIGNATURES = [
     ("ls_retain", _i32, [_P, _PI64, _PI64, _i32]),
     ("ls_generate", _i32, [_P, _PI64, _i32, _i32, _i32, _i64, _PI64, ctypes.POINTER(_i32),
                            ctypes.POINTER(Stats)]),
+    ("ls_generate_stream", _i32, [_P, _PI64, _i32, _i32, _i32, _i64, COMMIT_FN, _P, _PI64,
+                                  ctypes.POINTER(_i32), ctypes.POINTER(Stats)]),
     ("ls_pipeline_simulate", _i32, [_i32, _i32, _i32, _i64, _i32, _i64, DECIDE_FN, CYCLE_FN,
                                     RETAIN_FN, _P, _PI64, ctypes.POINTER(_i32),
                                     ctypes.POINTER(Stats)]),

@@ -2140,11 +2140,23 @@ std::vector<long long> run_loopspec(SchedHooks& e, long long first, int max_new,
   return committed;
 }
 
-std::vector<long long> run_ar(ls_engine& e, long long first, int max_new, long long stop_token,
+using StopRule = std::function<bool(const std::vector<long long>&)>;
+
+// Stop after a commit when the caller's callback asks to (it sees the whole
+// committed output, as the reference's should_stop does), or at the EOS id.
+StopRule stop_rule(long long stop_token, ls_commit_fn fn, void* user) {
+  return [stop_token, fn, user](const std::vector<long long>& ids) {
+    static_assert(sizeof(long long) == sizeof(int64_t), "committed ids are passed as int64");
+    if (fn && fn(user, reinterpret_cast<const int64_t*>(ids.data()), (int)ids.size()) != 0) return true;
+    return stop_token >= 0 && ids.back() == stop_token;
+  };
+}
+
+std::vector<long long> run_ar(ls_engine& e, long long first, int max_new, const StopRule& stop,
                               double& decode_t0) {
   std::vector<long long> committed{first};
   decode_t0 = now_s();
-  if (stop_token >= 0 && first == stop_token) return committed;
+  if (stop(committed)) return committed;
   const bool pre_attn = e.mc.n_pre_layers > 0, post_attn = e.mc.n_post_layers > 0;
   int index = 1;
   while ((int)committed.size() < max_new) {
@@ -2177,13 +2189,13 @@ std::vector<long long> run_ar(ls_engine& e, long long first, int max_new, long l
     check_fetched_error(e);
     committed.push_back(e.amax_host[0]);
     index++;
-    if (stop_token >= 0 && committed.back() == stop_token) break;
+    if (stop(committed)) break;
   }
   e.tl.retain({});
   return committed;
 }
 
-SchedHooks engine_hooks(ls_engine& e, long long stop_token) {
+SchedHooks engine_hooks(ls_engine& e, StopRule stop) {
   SchedHooks hk;
   hk.S = e.S;
   hk.K = e.K;
@@ -2195,9 +2207,7 @@ SchedHooks engine_hooks(ls_engine& e, long long stop_token) {
     cycle(e, cl, dec, nullptr);
   };
   hk.retain = [&e](const std::vector<PLane>& lanes, int) { retain_timelines(e, lanes); };
-  hk.should_stop = [stop_token](const std::vector<long long>& ids) {
-    return stop_token >= 0 && ids.back() == stop_token;
-  };
+  hk.should_stop = std::move(stop);
   return hk;
 }
 
@@ -2602,8 +2612,9 @@ int ls_retain(ls_engine* e, const int64_t* branch_ids, const int64_t* parent_ids
   return LS_OK;
 }
 
-int ls_generate(ls_engine* e, const int64_t* prompt, int n_prompt, int max_new, int mode,
-                int64_t stop_token, int64_t* out_ids, int* n_out, ls_stats* stats) {
+namespace {
+int generate_request(ls_engine* e, const int64_t* prompt, int n_prompt, int max_new, int mode,
+                     const StopRule& stop, int64_t* out_ids, int* n_out, ls_stats* stats) {
   if (!e || !prompt || !out_ids || !n_out || max_new < 1 || (mode != 0 && mode != 1)) return LS_EINVAL;
   try {
     ls_stats st{};
@@ -2618,10 +2629,10 @@ int ls_generate(ls_engine* e, const int64_t* prompt, int n_prompt, int max_new, 
     CK(cudaEventRecord(e->ev0, e->stream));
     std::vector<long long> ids;
     if (mode == 0) {
-      SchedHooks hk = engine_hooks(*e, stop_token);
+      SchedHooks hk = engine_hooks(*e, stop);
       ids = run_loopspec(hk, first, max_new, st, t0);
     } else {
-      ids = run_ar(*e, first, max_new, stop_token, t0);
+      ids = run_ar(*e, first, max_new, stop, t0);
     }
     CK(cudaEventRecord(e->ev1, e->stream));
     CK(cudaEventSynchronize(e->ev1));
@@ -2641,6 +2652,21 @@ int ls_generate(ls_engine* e, const int64_t* prompt, int n_prompt, int max_new, 
     return fail(e, ex);
   }
   return LS_OK;
+}
+}  // namespace
+
+int ls_generate(ls_engine* e, const int64_t* prompt, int n_prompt, int max_new, int mode,
+                int64_t stop_token, int64_t* out_ids, int* n_out, ls_stats* stats) {
+  return generate_request(e, prompt, n_prompt, max_new, mode, stop_rule(stop_token, nullptr, nullptr),
+                          out_ids, n_out, stats);
+}
+
+int ls_generate_stream(ls_engine* e, const int64_t* prompt, int n_prompt, int max_new, int mode,
+                       int64_t stop_token, ls_commit_fn on_commit, void* user, int64_t* out_ids,
+                       int* n_out, ls_stats* stats) {
+  if (!on_commit) return LS_EINVAL;
+  return generate_request(e, prompt, n_prompt, max_new, mode, stop_rule(stop_token, on_commit, user),
+                          out_ids, n_out, stats);
 }
 
 int ls_pipeline_simulate(int stages, int step_size, int second_step, int64_t first_token,

@@ -122,15 +122,36 @@ class Engine:
         p = np.ascontiguousarray([-1 if p[1] is None else p[1] for p in pairs], dtype=np.int64)
         _lib.check(self.L.ls_retain(self.h, _i64p(b), _i64p(p), len(b)), self.h)
 
-    def generate(self, prompt_ids, max_new_tokens, *, mode="loopspec", stop_token=None):
+    def generate(self, prompt_ids, max_new_tokens, *, mode="loopspec", stop_token=None,
+                 should_stop=None):
+        """One request natively (ls_generate). should_stop(ids) -> bool, if
+        given, sees the whole committed output after every commit and ends the
+        request when it returns True (ls_generate_stream)."""
         p = np.ascontiguousarray(prompt_ids, dtype=np.int64)
         out = np.zeros(max_new_tokens, dtype=np.int64)
         n = ctypes.c_int32()
         st = _lib.Stats()
-        _lib.check(self.L.ls_generate(
-            self.h, _i64p(p), len(p), max_new_tokens, 0 if mode == "loopspec" else 1,
-            -1 if stop_token is None else int(stop_token), _i64p(out), ctypes.byref(n),
-            ctypes.byref(st)), self.h)
+        m = 0 if mode == "loopspec" else 1
+        stop = -1 if stop_token is None else int(stop_token)
+        if should_stop is None:
+            code = self.L.ls_generate(self.h, _i64p(p), len(p), max_new_tokens, m, stop, _i64p(out),
+                                      ctypes.byref(n), ctypes.byref(st))
+        else:
+            failure = []
+
+            def on_commit(_user, ids, k):
+                try:
+                    return 1 if should_stop([ids[i] for i in range(k)]) else 0
+                except BaseException as ex:   # end the request, re-raise after it returns
+                    failure.append(ex)
+                    return 1
+            cb = _lib.COMMIT_FN(on_commit)
+            code = self.L.ls_generate_stream(self.h, _i64p(p), len(p), max_new_tokens, m, stop, cb, None,
+                                             _i64p(out), ctypes.byref(n), ctypes.byref(st))
+            if failure:
+                self.prefill_len = None
+                raise failure[0]
+        _lib.check(code, self.h)
         self.prefill_len = None
         return out[: n.value].tolist(), st.as_dict()
 

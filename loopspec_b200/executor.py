@@ -174,14 +174,14 @@ def generate_loopspec(runner: Engine, prompt_ids: Sequence[int], max_new_tokens:
     fixing the random stream; ids exclude the prompt and uncommitted drafts;
     stats hold the executor counters and decode_tokens (excluding the first
     token), plus decode timing. `stop_token` ends generation when committed
-    (EOS); a `should_stop` callback runs through B200Executor instead.
+    (EOS); `should_stop(ids)` sees the whole committed output after every
+    commit and ends generation when it returns True (pipeline.py:64).
     """
-    if should_stop is not None:
-        raise NotImplementedError("use stop_token, or drive B200Executor for callbacks")
     if max_new_tokens <= 0:
         raise ValueError("a committed first token requires a positive budget")
     apply_sampling(runner, sampling, generator, seed)
-    return runner.generate(list(prompt_ids), max_new_tokens, mode="loopspec", stop_token=stop_token)
+    return runner.generate(list(prompt_ids), max_new_tokens, mode="loopspec", stop_token=stop_token,
+                           should_stop=should_stop)
 
 
 def generate_autoregressive(runner: Engine, prompt_ids: Sequence[int], max_new_tokens: int, *,

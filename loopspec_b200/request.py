@@ -11,7 +11,9 @@ tokenized request:
                                   selects greedy decisions, otherwise
                                   temperature / top_k / top_p sampling keyed by
                                   the request's sampling_seed; generation ends
-                                  at the EOS id or at max_new_tokens.
+                                  at the EOS id or at max_new_tokens; a served
+                                  request yields its generation_metrics record
+                                  (:364-375, server/metrics.py).
 The HTTP server, tokenizer and detokenizer processes, streaming transport and
 stop strings stay out of scope (they need SGLang's request objects). Field
 names follow SGLang's tokenized request and its sampling_params.
@@ -23,6 +25,7 @@ import secrets
 from typing import Any, Sequence
 
 from .executor import apply_sampling
+from .metrics import request_metrics
 
 _ROUTING = ("bootstrap_host", "bootstrap_port", "bootstrap_room", "bootstrap_pair_key",
             "decode_tp_size", "routed_dp_rank", "disagg_prefill_dp_rank")
@@ -65,18 +68,23 @@ def unsupported_options(request: dict) -> list[str]:
     return [label for hit, label in checks if hit]
 
 
-def run_request(engine: Any, request: dict, eos_id: int | None = None) -> dict:
+def run_request(engine: Any, request: dict, eos_id: int | None = None, stream=None) -> dict:
     """Serve one tokenized request on `engine` (a loopspec_b200.engine.Engine).
 
     request = {"input_ids": [...], "sampling_params": {...}, ...}. Returns
     {"output_ids", "finish_reason" ("abort" | "length" | "stop"), "message",
-    "seed" (the sampling stream used, None for greedy), "stats"}. A sampled
+    "seed" (the sampling stream used, None for greedy), "stats", "metrics"
+    (the generation_metrics fields; None when no model work ran)}. A sampled
     request without sampling_seed draws a fresh seed, as the reference draws
-    from the device's default generator.
+    from the device's default generator. When the request asks to stream and
+    `stream` is given, stream(ids) receives the whole committed output after
+    every commit that does not finish the request (interval 1,
+    loopspec_scheduler.py:331-346); the finished output is the return value.
     """
     def done(reason, message="", ids=(), seed=None, stats=None):
         return {"output_ids": list(ids), "finish_reason": reason, "message": message,
-                "seed": seed, "stats": stats or {}}
+                "seed": seed, "stats": stats or {},
+                "metrics": request_metrics(list(ids), stats) if stats else None}
 
     unsupported = unsupported_options(request)
     if unsupported:
@@ -98,6 +106,14 @@ def run_request(engine: Any, request: dict, eos_id: int | None = None) -> dict:
         apply_sampling(engine, {"temperature": p.get("temperature", 1.0),
                                 "top_k": max(0, int(p.get("top_k", -1))),
                                 "top_p": p.get("top_p", 1.0)}, seed=seed)
-    out, stats = engine.generate(list(ids), max_new, mode="loopspec", stop_token=eos_id)
+    should_stop = None
+    if stream is not None and request.get("stream"):
+        def should_stop(committed):
+            finished = len(committed) >= max_new or (eos_id is not None and committed[-1] == eos_id)
+            if not finished:
+                stream(list(committed))
+            return False
+    out, stats = engine.generate(list(ids), max_new, mode="loopspec", stop_token=eos_id,
+                                 should_stop=should_stop)
     reason = "stop" if eos_id is not None and out and out[-1] == eos_id else "length"
     return done(reason, ids=out, seed=seed, stats=stats)

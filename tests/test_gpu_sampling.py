@@ -137,3 +137,30 @@ def test_run_request_semantics_on_the_engine():
     s = run_request(eng, {"input_ids": p, "sampling_params": {"max_new_tokens": 20, "top_k": 1}}, eos_id=eos)
     assert s["finish_reason"] == "stop" and s["output_ids"] == ref[: ref.index(eos) + 1]
     eng.close()
+
+
+@pytest.mark.parametrize("mode", ["loopspec", "ar"])
+def test_commit_callback_sees_growing_output_and_can_stop(mode):
+    """ls_generate_stream: the callback sees the whole committed output after
+    every commit (first token included), each a prefix of the next; stopping
+    early returns a prefix of the unrestricted output; the generation metrics
+    of run_request come from the same statistics."""
+    cfg, eng = make("tiny", 1, 2)
+    p = prompt(cfg, 24, 6)
+    full, _ = eng.generate(p, 30, mode=mode)
+    seen = []
+    out, st = eng.generate(p, 30, mode=mode, should_stop=lambda ids: seen.append(list(ids)) or False)
+    assert out == full and seen[0] == full[:1] and seen[-1] == full
+    assert all(a == b[: len(a)] and len(b) > len(a) for a, b in zip(seen, seen[1:]))
+    short, _ = eng.generate(p, 30, mode=mode, should_stop=lambda ids: len(ids) >= 7)
+    assert len(short) >= 7 and short == full[: len(short)]
+    if mode == "ar":
+        assert len(short) == 7
+    from loopspec_b200.request import run_request
+    streamed = []
+    res = run_request(eng, {"input_ids": p, "stream": True,
+                            "sampling_params": {"max_new_tokens": 30, "top_k": 1}}, stream=streamed.append)
+    if mode == "loopspec":
+        assert res["output_ids"] == full and streamed[-1] == full[: len(streamed[-1])]
+        assert res["metrics"]["decode_tokens"] == 29 and res["metrics"]["decode_seconds"] > 0
+    eng.close()

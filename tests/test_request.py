@@ -15,12 +15,20 @@ class FakeEngine:
     def set_sampling(self, temperature=0.0, top_k=0, top_p=1.0, seed=0):
         self.sampling_calls.append((temperature, top_k, top_p, seed))
 
-    def generate(self, ids, max_new, *, mode, stop_token=None):
+    def generate(self, ids, max_new, *, mode, stop_token=None, should_stop=None):
         self.calls.append((list(ids), max_new, mode, stop_token))
         out = list(self.out[:max_new])
         if stop_token is not None and stop_token in out:
             out = out[: out.index(stop_token) + 1]
-        return out, {"decode_tokens": len(out) - 1}
+        if should_stop is not None:   # one commit per token
+            for i in range(1, len(out) + 1):
+                if should_stop(out[:i]):
+                    out = out[:i]
+                    break
+        stats = {"pipeline_cycles": 2 * len(out), "verified_proposals": len(out), "first_rejections": 1,
+                 "second_verifications": 1, "second_acceptances": 0, "second_rejections": 1,
+                 "decode_tokens": len(out) - 1, "decode_host_s": 0.25}
+        return out, stats
 
 
 def test_supported_requests_list_nothing():
@@ -78,3 +86,25 @@ def test_greedy_seeded_sampling_and_finish_reasons():
     r = run_request(eng, {"input_ids": [1], "sampling_params": {"max_new_tokens": 1, "top_p": 0.9}})
     assert r["seed"] is not None and eng.sampling_calls[-1][3] == r["seed"]   # fresh seed, reported
     assert eng.calls[-1] == ([1], 1, "loopspec", None)
+
+
+def test_served_request_carries_its_generation_metrics():
+    eng = FakeEngine([7, 8, 9, 10, 11])
+    res = run_request(eng, {"input_ids": [1, 2], "sampling_params": {"max_new_tokens": 5, "top_k": 1}})
+    m = res["metrics"]
+    assert (m["decode_tokens"], m["decode_seconds"], m["decode_tok_s"]) == (4, 0.25, 16.0)
+    assert (m["pipeline_cycles"], m["first_accept"], m["second_skip"]) == (10, 4, 0)
+    aborted = run_request(eng, {"input_ids": [], "sampling_params": {}})
+    assert aborted["metrics"] is None
+
+
+def test_streamed_request_sends_every_unfinished_commit():
+    eng = FakeEngine([7, 8, 9, 2, 11])
+    sent = []
+    req = {"input_ids": [1], "stream": True, "sampling_params": {"max_new_tokens": 5, "top_k": 1}}
+    res = run_request(eng, req, eos_id=2, stream=sent.append)
+    assert res["output_ids"] == [7, 8, 9, 2] and res["finish_reason"] == "stop"
+    assert sent == [[7], [7, 8], [7, 8, 9]]        # the finishing commit is the return value
+    sent.clear()
+    run_request(eng, dict(req, stream=False), eos_id=2, stream=sent.append)
+    assert sent == []                              # the request did not ask to stream
