@@ -236,6 +236,13 @@ int ls_gemm_splits(ls_engine* eng, int which, int* splits, int* rows, int* k);
  * [attn_layers][kv_slots][n_kv_heads*head_dim] bf16), for tests. */
 int ls_debug_kv(ls_engine* eng, void** k_pool, void** v_pool, int* kv_slots, int* attn_layers);
 
+/* Failure-detection test of the tensor-parallel exchange on one GPU: after
+ * ls_tp_init(eng, rank, 2, ...), attach a zeroed region of this GPU as the
+ * other rank's. Its flags never rise, so the first exchange waits wait_ms,
+ * records "tensor-parallel peer wait timed out" and later exchanges give up
+ * at once; the call then fails with LS_EDEVICE and the context stays usable. */
+int ls_debug_tp_silent_peer(ls_engine* eng, int wait_ms);
+
 /* Branch-timeline paged decode attention of one layer, standalone (the
  * engine's attention kernel; replaces SGLang's Triton decode attention as the
  * reference drives it through req_to_token rows, cuda_graph.py:361-394).

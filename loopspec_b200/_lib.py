@@ -77,6 +77,7 @@ SIGNATURES = [
     ("ls_finalize", _i32, [_P]),
     ("ls_tp_init", _i32, [_P, _i32, _i32, _P]),
     ("ls_tp_attach", _i32, [_P, _P]),
+    ("ls_debug_tp_silent_peer", _i32, [_P, _i32]),
     ("ls_prefill", _i32, [_P, _PI64, _i32, _PF32, _PI64]),
     ("ls_set_sampling", _i32, [_P, _f32, _i32, _f32, _u64]),
     ("ls_cycle", _i32, [_P, _PI64, _i32, _PI64, _PF32]),

@@ -475,6 +475,7 @@ struct ls_engine {
   size_t tp_bytes = 0, tp_off_o = 0, tp_off_d = 0, tp_off_qk = 0;
   std::vector<char*> tp_base;
   std::vector<void*> tp_opened;   // peer mappings, closed before the engine frees memory
+  unsigned long long tp_wait_ns = kTpWaitNs;
 
   Timelines tl;
   int prefill_len = -1;   // len(prompt) - 1 of the current request
@@ -1283,6 +1284,7 @@ constexpr size_t kTpEpochOff = 64;   // byte offset of the epoch counter in a re
 TpView tp_view(const ls_engine& e, size_t off) {
   TpView t{};
   t.ranks = e.tp_ranks;
+  t.wait_ns = e.tp_wait_ns;
   t.epoch = reinterpret_cast<const int*>(e.tp_region + kTpEpochOff);
   for (int r = 0; r < e.tp_ranks; ++r) {
     t.flags[r] = reinterpret_cast<const int*>(e.tp_base[r]);
@@ -2546,6 +2548,26 @@ int ls_tp_attach(ls_engine* e, const void* handles) {
     }
     e->tp_base = base;
     e->tp_ranks = n;
+  } catch (const std::exception& ex) {
+    return fail(e, ex);
+  }
+  return LS_OK;
+}
+
+int ls_debug_tp_silent_peer(ls_engine* e, int wait_ms) {
+  if (!e) return LS_EINVAL;
+  try {
+    REQUIRE(e->tp_region != nullptr && e->tp_ranks == 1 && e->tp_want == 2, LS_EINVAL,
+            "call ls_tp_init with 2 ranks first, and no ls_tp_attach");
+    REQUIRE(wait_ms >= 1 && wait_ms <= 10000, LS_EINVAL, "wait limit must be 1..10000 ms");
+    CK(cudaSetDevice(e->device));
+    // a zeroed region of this GPU stands in for the peer: its flags never rise
+    char* silent = e->dalloc<char>(e->tp_bytes);
+    e->tp_base.assign(2, nullptr);
+    e->tp_base[e->tp_rank] = e->tp_region;
+    e->tp_base[1 - e->tp_rank] = silent;
+    e->tp_wait_ns = 1000000ull * (unsigned long long)wait_ms;
+    e->tp_ranks = 2;
   } catch (const std::exception& ex) {
     return fail(e, ex);
   }

@@ -148,13 +148,14 @@ __global__ void cat_state_kernel(Meta meta, int H, const float* __restrict__ ban
 // buffer.
 constexpr int kTpMax = 8;
 constexpr int kTpSlotO = 0, kTpSlotDown = 1, kTpSlotQk = 2, kTpSlots = 3;
-constexpr unsigned long long kTpWaitNs = 10000000000ull;   // 10 s per exchange
+constexpr unsigned long long kTpWaitNs = 10000000000ull;   // default limit per exchange: 10 s
 
 struct TpView {
   int ranks;                    // > 1: this kernel adds the peers' partials
   const int* epoch;             // this rank's exchange counter
   const int* flags[kTpMax];     // each rank's flags [kTpSlots], in rank order
   const float* data[kTpMax];    // each rank's buffer of this exchange
+  unsigned long long wait_ns;   // give up on a peer after this long
 };
 
 __device__ __forceinline__ int ld_acquire_sys(const int* p) {
@@ -178,7 +179,7 @@ __device__ bool tp_wait(const TpView& t, int slot, int* err) {
     int good = 1;
     for (int r = 0; r < t.ranks && good; ++r) {
       for (uint32_t i = 0; ld_acquire_sys(t.flags[r] + slot) < want; ++i) {
-        if ((i & 63u) == 63u && (ld_volatile(err) != 0 || gtime_ns() - t0 > kTpWaitNs)) {
+        if ((i & 63u) == 63u && (ld_volatile(err) != 0 || gtime_ns() - t0 > t.wait_ns)) {
           if (ld_volatile(err) == 0) atomicExch(err, kDevTimeoutPeer);
           good = 0;
           break;

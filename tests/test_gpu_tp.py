@@ -127,3 +127,39 @@ def test_tp2_matches_single_gpu_and_oracle(name, over, K, X, n_new):
         eng.close()
     assert np.abs(r0["logits"] - logits1).max() <= LOGIT_TOL
     assert r0["loopspec"] == single
+
+
+def test_a_silent_peer_ends_the_call_with_a_device_error_and_the_context_survives():
+    """Failure detection on one GPU: rank 0 of 2 whose peer never publishes
+    (a zeroed local region stands in for it). The first exchange waits 200 ms,
+    records the timeout, later exchanges give up at once, and the call fails
+    with LS_EDEVICE; afterwards the device still runs a single-GPU engine."""
+    import time
+    from loopspec_b200 import _lib
+    from loopspec_b200.engine import Engine
+    from loopspec_b200.tp import shard_config, shard_weights
+    cfg = get_config("tiny-raven-olmo")
+    w32 = init_random_weights(cfg, 0, dtype=torch.float32)
+    w = {k: v.to("cuda:0", torch.bfloat16).contiguous() for k, v in w32.items()}
+    sch = PipelineSchedule(cfg.stages, 1, 4)
+    eng = Engine(shard_config(cfg, 2), sch, shard_weights(w, cfg, 0, 2), device=0, max_context=512,
+                 max_prompt=256)
+    try:
+        eng.tp_init(0, 2)
+        _lib.check(eng.L.ls_debug_tp_silent_peer(eng.h, 200), eng.h)
+        prompt = _prompt(cfg, 16, seed=4)
+        t0 = time.perf_counter()
+        with pytest.raises(_lib.EngineError) as info:
+            eng.generate(prompt, 4)
+        assert info.value.code == _lib.LS_EDEVICE
+        assert "tensor-parallel peer wait timed out" in str(info.value)
+        assert time.perf_counter() - t0 < 20
+    finally:
+        eng.close()
+    single = Engine(cfg, sch, w, device=0, max_context=512, max_prompt=256)
+    try:
+        a, _ = single.generate(_prompt(cfg, 16, seed=4), 6, mode="loopspec")
+        b, _ = single.generate(_prompt(cfg, 16, seed=4), 6, mode="ar")
+        assert a == b and len(a) == 6
+    finally:
+        single.close()
