@@ -34,7 +34,7 @@ def _prompt(cfg, n, seed):
     return torch.randint(0, cfg.vocab, (n,), generator=g).tolist()
 
 
-def _rank_main(rank, ranks, port, name, over, K, X, prompt, n_new, q):
+def _rank_main(rank, ranks, port, name, over, K, X, prompt, n_new, q, sampling=None):
     import torch.distributed as dist
     from loopspec_b200.tp import make_tp_engine
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
@@ -57,7 +57,12 @@ def _rank_main(rank, ranks, port, name, over, K, X, prompt, n_new, q):
         if all(built):
             try:
                 out["first"], out["logits"] = eng.prefill(prompt, want_logits=True)
+                if sampling is not None:
+                    eng.set_sampling(**sampling)
                 out["loopspec"], _ = eng.generate(prompt, n_new, mode="loopspec")
+                if sampling is not None:   # the same seed again: the same draws
+                    eng.set_sampling(**sampling)
+                    out["again"], _ = eng.generate(prompt, n_new, mode="loopspec")
                 out["ar"], _ = eng.generate(prompt, n_new, mode="ar")
             except Exception as ex:   # a peer's bounded waits end its calls too
                 out["error"] = repr(ex)
@@ -71,12 +76,12 @@ def _rank_main(rank, ranks, port, name, over, K, X, prompt, n_new, q):
         dist.destroy_process_group()
 
 
-def _run_tp(name, over, K, X, prompt, n_new, ranks=2):
+def _run_tp(name, over, K, X, prompt, n_new, ranks=2, sampling=None):
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, ranks, port, name, over, K, X, prompt, n_new, q))
+    procs = [ctx.Process(target=_rank_main, args=(r, ranks, port, name, over, K, X, prompt, n_new, q, sampling))
              for r in range(ranks)]
     for p in procs:
         p.start()
@@ -163,3 +168,18 @@ def test_a_silent_peer_ends_the_call_with_a_device_error_and_the_context_survive
         assert a == b and len(a) == 6
     finally:
         single.close()
+
+
+def test_tp2_sampled_decode_draws_the_same_tokens_on_every_rank():
+    """Top-p sampling under TP: identical logits and the same seed give every
+    rank the same draws (the host loops then stay in step), and the seed
+    reproduces them."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    cfg = get_config("tiny-raven-olmo")
+    samp = {"temperature": 1.0, "top_k": 0, "top_p": 0.9, "seed": 321}
+    ranks = _run_tp("tiny-raven-olmo", {}, 1, 4, _prompt(cfg, 32, seed=2), 24, sampling=samp)
+    r0 = ranks[0]
+    assert len(r0["loopspec"]) == 24 and r0["again"] == r0["loopspec"]
+    for o in ranks[1:]:
+        assert o["loopspec"] == r0["loopspec"] and o["again"] == r0["again"]
