@@ -16,6 +16,7 @@ request with at most one output token logs (0, 0.0).
 from __future__ import annotations
 
 import json
+import math
 from logging import Logger
 from typing import Mapping
 
@@ -64,3 +65,26 @@ def log_decode_metrics(logger: Logger, decode_tokens: int, decode_seconds: float
                        loopspec_stats: Mapping[str, int] | None = None) -> None:
     """Emit one record, as the reference's function of the same name."""
     logger.info("%s", format_record(decode_metrics(decode_tokens, decode_seconds, loopspec_stats)))
+
+
+def record_valid(m) -> bool:
+    """The reference's acceptance rule for a record (experiment_tools/
+    result_parser.py:102-141): non-negative int decode_tokens and finite
+    non-negative decode_seconds; if any rejection field is present, all five
+    are non-negative ints with decode_tokens == first_accept + first_reject and
+    second_skip + second_accept + second_reject == first_reject."""
+    if not isinstance(m, dict):
+        return False
+    t, sec = m.get("decode_tokens"), m.get("decode_seconds")
+    if not (type(t) is int and t >= 0 and isinstance(sec, (int, float)) and not isinstance(sec, bool)
+            and math.isfinite(sec) and sec >= 0):
+        return False
+    fields = ("first_accept", "first_reject", "second_skip", "second_accept", "second_reject")
+    vals = [m.get(f) for f in fields]
+    if any(v is not None for v in vals):
+        if not all(type(v) is int and v >= 0 for v in vals):
+            return False
+        if t != m["first_accept"] + m["first_reject"] or \
+                m["second_skip"] + m["second_accept"] + m["second_reject"] != m["first_reject"]:
+            return False
+    return True

@@ -1,10 +1,14 @@
-"""Record generation_metrics lines from the REFERENCE's log_decode_metrics.
+"""Record generation_metrics lines from the REFERENCE's log_decode_metrics,
+and the reference result parser's verdict on a set of records.
 
-Loads sglang_recurrent/server/metrics.py from the reference tree by file path
-(it imports only json and logging), calls log_decode_metrics for every case
-below with a capturing logger, and writes the (inputs, line) pairs to
-metrics_records.json beside this script. Run here (where the reference tree is
-mounted):  python tests/golden/make_metrics_golden.py [reference_root]
+Loads sglang_recurrent/server/metrics.py and experiment_tools/result_parser.py
+from the reference tree by file path (both import only the standard library).
+Calls log_decode_metrics for every case below with a capturing logger and
+writes the (inputs, line) pairs to metrics_records.json. Asks
+GenerationMetrics._valid about every record of VALIDITY (valid ones and ones
+that break each rule) and writes (record, verdict) pairs to
+metrics_validity.json. Run here (where the reference tree is mounted):
+python tests/golden/make_metrics_golden.py [reference_root]
 """
 
 from __future__ import annotations
@@ -28,6 +32,25 @@ CASES = [
                    "second_verifications": 127, "second_acceptances": 1, "second_rejections": 126}),
     (64, 0.25, None),
     (0, 1.5, None),
+]
+
+
+_OK = {"decode_seconds": 2.0, "decode_tokens": 10, "decode_tok_s": 5.0, "pipeline_cycles": 40,
+       "first_accept": 4, "first_reject": 6, "second_skip": 1, "second_accept": 2, "second_reject": 3}
+VALIDITY = [
+    _OK,
+    {"decode_seconds": 0.0, "decode_tokens": 0, "decode_tok_s": None},
+    {"decode_seconds": 1.5, "decode_tokens": 3, "decode_tok_s": 2.0},
+    dict(_OK, decode_tokens=11),                    # tokens != first_accept + first_reject
+    dict(_OK, second_skip=2),                       # second fields do not add up
+    dict(_OK, first_accept=-1, decode_tokens=5),    # negative field
+    dict(_OK, decode_seconds=float("inf")),
+    dict(_OK, decode_seconds=-1.0),
+    dict(_OK, decode_tokens=10.0),                  # float token count
+    dict(_OK, decode_seconds=True),
+    {k: v for k, v in _OK.items() if k != "second_reject"},   # partial rejection fields
+    {"decode_seconds": 1.0},
+    [1, 2],
 ]
 
 
@@ -56,7 +79,14 @@ def main(root):
                     "line": cap.lines[-1]})
     with open(os.path.join(HERE, "metrics_records.json"), "w") as f:
         json.dump(out, f, indent=1)
-    print(f"wrote {len(out)} records")
+    spec = importlib.util.spec_from_file_location(
+        "ref_result_parser", os.path.join(root, "experiment_tools", "result_parser.py"))
+    parser = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(parser)
+    verdicts = [{"record": r, "valid": bool(parser.GenerationMetrics._valid(r))} for r in VALIDITY]
+    with open(os.path.join(HERE, "metrics_validity.json"), "w") as f:
+        json.dump(verdicts, f, indent=1)
+    print(f"wrote {len(out)} records and {len(verdicts)} verdicts")
 
 
 if __name__ == "__main__":

@@ -163,4 +163,6 @@ def test_commit_callback_sees_growing_output_and_can_stop(mode):
     if mode == "loopspec":
         assert res["output_ids"] == full and streamed[-1] == full[: len(streamed[-1])]
         assert res["metrics"]["decode_tokens"] == 29 and res["metrics"]["decode_seconds"] > 0
+        from loopspec_b200.metrics import record_valid
+        assert record_valid(res["metrics"])      # the reference parser's consistency rules
     eng.close()

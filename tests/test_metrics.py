@@ -34,3 +34,28 @@ def test_request_interval_excludes_the_first_token():
     one = request_metrics([5], st)
     assert (one["decode_tokens"], one["decode_seconds"], one["decode_tok_s"]) == (0, 0.0, None)
     assert "pipeline_cycles" not in request_metrics([5, 6], st, loopspec=False)
+
+
+def test_validity_rule_matches_the_reference_parser():
+    from loopspec_b200.metrics import record_valid
+    cases = json.load(open(os.path.join(os.path.dirname(__file__), "golden", "metrics_validity.json")))
+    assert any(c["valid"] for c in cases) and any(not c["valid"] for c in cases)
+    for c in cases:
+        assert record_valid(c["record"]) == c["valid"], c["record"]
+
+
+def test_native_scheduler_counters_pass_the_reference_log_checks():
+    # Every scripted schedule case (stops, rejections at both stages, early
+    # EOS): the record of its committed output satisfies the parser's rules.
+    import sys
+    sys.path.insert(0, os.path.join(os.path.dirname(__file__), "golden"))
+    from scripted_executor import CASES, _mix, hash_decision
+    from loopspec_b200.metrics import decode_metrics, record_valid
+    from loopspec_b200.simulate import simulate_pipeline
+    for S, K, X, q1, q2, n, seed, vocab, stop in CASES:
+        first = _mix(seed, 0, 0, 9) % vocab
+        ids, stats, _ = simulate_pipeline(
+            S, K, X, first, n, lambda i, t, k: hash_decision(seed, vocab, q1, q2, i, t, k), stop_token=stop)
+        rec = decode_metrics(max(len(ids) - 1, 0), 1.0, {k: int(v) for k, v in stats.items()
+                                                          if not isinstance(v, float)})
+        assert record_valid(rec), (S, K, X, q1, q2, n, seed, stop, rec)
