@@ -85,6 +85,20 @@ def cfg_stages(name):
 PATHS = pytest.mark.parametrize("persistent", [True, False], ids=["persistent", "multikernel"])
 
 
+@pytest.mark.parametrize("name,K,X", [("tiny", 1, 2), ("tiny-raven-llama", 2, 2), ("tiny-raven-olmo", 1, 4)])
+def test_multi_chunk_prefill_logits_match_oracle(name, K, X):
+    # 300 prompt tokens: three prefill chunks (128, 128, 44 lanes), so later
+    # chunks attend to positions written by earlier calls as well as their own
+    cfg, eng, om = make(name, K, X, max_context=640, max_prompt=320)
+    prompt = prompt_for(cfg, 300, seed=9)
+    first, logits = eng.prefill(prompt, want_logits=True)
+    rec = []
+    generate_ar_oracle(om, cfg.stages, prompt, 1, record=rec)
+    assert np.abs(logits - rec[0][2].numpy()).max() <= LOGIT_TOL
+    assert first == int(np.argmax(logits))
+    eng.close()
+
+
 @PATHS
 @pytest.mark.parametrize("name,K,X", [("tiny", 1, 2), ("tiny-raven-llama", 2, 2), ("tiny-raven-olmo", 1, 4)])
 def test_prefill_logits_match_oracle(name, K, X, persistent):
