@@ -107,13 +107,19 @@ def run_request(engine: Any, request: dict, eos_id: int | None = None, stream=No
                                 "top_k": max(0, int(p.get("top_k", -1))),
                                 "top_p": p.get("top_p", 1.0)}, seed=seed)
     should_stop = None
+    seen: list = []
     if stream is not None and request.get("stream"):
         def should_stop(committed):
+            seen[:] = committed
             finished = len(committed) >= max_new or (eos_id is not None and committed[-1] == eos_id)
             if not finished:
                 stream(list(committed))
             return False
     out, stats = engine.generate(list(ids), max_new, mode="loopspec", stop_token=eos_id,
                                  should_stop=should_stop)
+    # the callback and the executor must agree on the whole committed sequence
+    # (loopspec_scheduler.py:356-358)
+    if should_stop is not None and list(seen) != list(out):
+        raise RuntimeError("LoopSpec request state diverged from pipeline output")
     reason = "stop" if eos_id is not None and out and out[-1] == eos_id else "length"
     return done(reason, ids=out, seed=seed, stats=stats)

@@ -108,3 +108,15 @@ def test_streamed_request_sends_every_unfinished_commit():
     sent.clear()
     run_request(eng, dict(req, stream=False), eos_id=2, stream=sent.append)
     assert sent == []                              # the request did not ask to stream
+
+
+def test_divergent_engine_output_is_an_error():
+    class Divergent(FakeEngine):
+        def generate(self, ids, max_new, *, mode, stop_token=None, should_stop=None):
+            out, st = super().generate(ids, max_new, mode=mode, stop_token=stop_token,
+                                       should_stop=should_stop)
+            return out[:-1] + [out[-1] + 1], st      # returns a token it never committed
+    eng = Divergent([7, 8, 9])
+    req = {"input_ids": [1], "stream": True, "sampling_params": {"max_new_tokens": 3, "top_k": 1}}
+    with pytest.raises(RuntimeError, match="diverged"):
+        run_request(eng, req, stream=lambda ids: None)
