@@ -13,7 +13,7 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 from loopspec_b200.config import get_config
-from loopspec_b200.tp import check_divisible, exchange_handles, shard_config, shard_weights
+from loopspec_b200.tp import check_divisible, exchange_handles, make_tp_engine, shard_config, shard_weights
 from loopspec_b200.weights import init_random_weights
 
 
@@ -177,3 +177,11 @@ def test_exchange_handles_returns_every_rank_in_rank_order():
         assert pr.exitcode == 0
     for r in range(ranks):
         assert res[r] == [bytes([t + 1]) * 128 for t in range(ranks)]
+
+
+def test_make_tp_engine_refuses_the_persistent_path_before_any_gpu_work():
+    cfg = get_config("tiny-raven-olmo")
+    with pytest.raises(ValueError, match="multi-kernel"):
+        make_tp_engine(cfg, None, {}, 0, 2, device=0, use_persistent=True)
+    with pytest.raises(ValueError):
+        shard_weights({}, get_config("raven-olmo"), 0, 3)
