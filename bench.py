@@ -1,5 +1,5 @@
 #!/usr/bin/env python
-"""LoopSpec decode benchmark (BASELINE.json configs[1] by default).
+"""LoopSpec decode benchmark (the Ouro-1.4B batch-1 configuration by default).
 
 Workload: Ouro-1.4B architecture, random init (seed 0), bf16 weights, batch 1,
 a 512-token prompt of uniform-random ids, 1024 greedy new tokens, LoopSpec
@@ -34,6 +34,7 @@ sys.path.insert(0, ROOT)
 
 import torch  # noqa: E402
 
+from loopspec_b200 import roofline  # noqa: E402
 from loopspec_b200.config import get_config  # noqa: E402
 from loopspec_b200.schedule import PipelineSchedule, accept_length  # noqa: E402
 
@@ -138,18 +139,6 @@ class Clocks:
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
                 "samples": len(rows)}
-
-
-def bytes_per_decode(cfg, sch, stats, prompt_len):
-    """Algorithmic HBM bytes of the decode loop (weights + KV), per the
-    per-cycle formula K*W_core + [post]*W_lm + sum over lanes/iterations of KV reads."""
-    cycles = stats["pipeline_cycles"]
-    W_core = cfg.core_weight_bytes()
-    W_lm = cfg.vocab * cfg.hidden * 2
-    kv_tok = cfg.n_core_layers * cfg.kv_bytes_per_token_layer()
-    L = prompt_len + stats["decode_tokens"] / 2.0
-    post_calls = cycles if stats["post_rows"] else 0
-    return cycles * sch.step_size * W_core + post_calls * W_lm + stats["recurrent_rows"] * L * kv_tok
 
 
 L2_BYTES = 126 * 2**20   # B200 L2
@@ -285,11 +274,16 @@ def engine_arm(args):
     dec_tok = dec_ms = wall = 0.0
     h2d = d2h = 0
     agg = None
+    useful = 0
+    first_ids = None
     for i in range(args.steps):
         t0 = time.perf_counter()
         ids, st = generate_loopspec(eng, prompt_of(args.warmup + i), args.new_tokens, sampling=samp,
                                     seed=args.seed + args.warmup + i)
         wall += time.perf_counter() - t0
+        if first_ids is None:
+            first_ids = ids
+        useful += roofline.useful_bytes(eng.cfg, st["decode_tokens"], args.prompt)
         dec_tok += st["decode_tokens"]
         dec_ms += st["decode_device_ms"]
         h2d += st["h2d_bytes"] + 8 * args.prompt
@@ -328,10 +322,13 @@ def engine_arm(args):
         eng2.close()
         del w2
 
-    # autoregressive beside it (one request, same prompt distribution)
-    ar_ids, ar_st = generate_autoregressive(eng, prompt_of(0), args.new_tokens, sampling=samp,
-                                            seed=args.seed)
+    # autoregressive beside it, on the first timed request's prompt: greedy
+    # LoopSpec must commit exactly the AR tokens
+    ar_ids, ar_st = generate_autoregressive(eng, prompt_of(args.warmup), args.new_tokens, sampling=samp,
+                                            seed=args.seed + args.warmup)
     ar_tok_s = ar_st["decode_tokens"] / (ar_st["decode_device_ms"] / 1e3)
+    ar_gbs = roofline.decode_bytes(eng.cfg, ar_st) / (ar_st["decode_device_ms"] / 1e3) / 1e9
+    greedy_equal_ar = (list(first_ids) == list(ar_ids)) if samp is None else None
 
     # roofline of the dominant kernel: the tcgen05 GEMM, over a core-weight sweep
     lanes = max(1, round(agg["recurrent_rows"] / max(agg["pipeline_cycles"], 1) / sch.step_size))
@@ -349,9 +346,12 @@ def engine_arm(args):
     # algorithmic bytes (ratio 1.0003: no tile read twice, the split planes stay in
     # L2); scaled to this sweep's average launch.
     traffic = launch_bytes * (103.234 / 103.203)
-    # per rank: under tensor parallelism its shard of the core and its KV heads
-    decode_bytes = bytes_per_decode(eng.cfg, sch, agg, args.prompt)
+    # per rank: under tensor parallelism its shard of the core and its KV heads.
+    # All bytes moved (rejected lanes included), and the AR bytes of the
+    # committed tokens (the useful work), over the same decode time.
+    decode_bytes = roofline.decode_bytes(eng.cfg, agg)
     decode_gbs = decode_bytes / (dec_ms / 1e3) / 1e9
+    useful_gbs = useful / (dec_ms / 1e3) / 1e9
 
     if rank == 0:
         line = {
@@ -374,20 +374,30 @@ def engine_arm(args):
                                                   "post_rows", "verified_proposals",
                                                   "first_rejections", "second_verifications",
                                                   "second_acceptances", "second_rejections",
-                                                  "decode_tokens")},
+                                                  "decode_tokens", "pre_calls", "core_calls",
+                                                  "core_kv_positions", "post_calls")},
+            "decode_device_s": round(dec_ms / 1e3, 4),
             "roofline": {"bound": "hbm", "kernel": "gemm_tc_kernel (core weight sweep)",
                          "achieved": round(achieved, 1), "peak": peak_gbs, "unit": "GB/s",
                          "frac": round(achieved / peak_gbs, 4), "peak_source": peak_src,
                          "traffic": round(traffic),
                          "traffic_source": "ncu dram__bytes_read+write of one layer's four core GEMMs "
-                                           "(profiles/dram_core_gemms_ouro1.4b_4lanes.md), ratio "
-                                           "to their algorithmic bytes applied to this sweep",
+                                           "(4 lanes), ratio to their algorithmic bytes applied to "
+                                           "this sweep",
                          "lanes": lanes,
                          "bytes_per_launch": round(launch_bytes),
                          "avg_launch_us": round(launch_ms * 1e3, 3)},
             "decode_roofline": {"achieved": round(decode_gbs, 1), "peak": peak_gbs,
                                 "unit": "GB/s", "frac": round(decode_gbs / peak_gbs, 4),
-                                "bytes": "K*W_core + W_lm per post call + KV reads"},
+                                "bytes": round(decode_bytes),
+                                "bytes_formula": "core_calls*W_core + pre_calls*W_pre + "
+                                                 "post_calls*(W_post+W_lm) + (core_kv_positions + "
+                                                 "recurrent_rows)*KV_row (from counters)",
+                                "useful_achieved": round(useful_gbs, 1),
+                                "useful_frac": round(useful_gbs / peak_gbs, 4),
+                                "useful_formula": "AR bytes of the committed tokens",
+                                "ar_frac": round(ar_gbs / peak_gbs, 4)},
+            "greedy_equal_ar": greedy_equal_ar,
             "e2e": {"value": round(e2e, 2), "unit": UNIT,
                     "h2d_bytes_per_step": int(h2d / args.steps),
                     "d2h_bytes_per_step": int(d2h / args.steps),
@@ -400,6 +410,10 @@ def engine_arm(args):
                                      "(counted per graph replay by the engine)")
         if synth is not None:
             line["synthetic_acceptance"] = synth
+        if decode_gbs > peak_gbs:
+            # more bytes per second than the measured copy peak: the byte
+            # count, not the engine, is wrong
+            line["decode_roofline"]["error"] = "achieved above the measured HBM peak"
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(cfg, sch, args, os.cpu_count() or 1)
         print(json.dumps(line), flush=True)

@@ -57,14 +57,6 @@ typedef struct ls_sched_cfg {
   int32_t request_rows;      /* timeline mapping rows (0: auto)              */
   int32_t use_graphs;        /* capture one CUDA graph per (role, width)     */
   int32_t use_pdl;           /* programmatic dependent launch between kernels */
-  int32_t use_persistent;    /* 1: each role call is one persistent kernel over
-                                all SMs (phases separated by grid counters);
-                                0: one kernel per GEMM / attention / row step */
-  int32_t l2_prefetch;       /* 1: latency-bound kernels (attention, norm rows,
-                                input prep) prefetch the weights of the GEMMs
-                                that follow them into L2 (multi-kernel path;
-                                measured slower on Ouro-1.4B decode, off by
-                                default in the Python API) */
 } ls_sched_cfg;
 
 /* Counters of sglang_recurrent/loopspec/executor.py:35-45 plus timing. */
@@ -79,6 +71,12 @@ typedef struct ls_stats {
   int64_t h2d_bytes;         /* host->device bytes copied for the request       */
   int64_t d2h_bytes;         /* device->host bytes copied for the request       */
   int64_t decode_kernel_launches; /* engine kernels launched by the decode loop */
+  /* Work of the decode loop, for the bytes-moved roofline: */
+  int64_t pre_calls;         /* pre role calls that ran prelude layers        */
+  int64_t core_calls;        /* core role calls (one per core iteration)      */
+  int64_t core_kv_positions; /* sum over core lanes of the timeline length
+                                each attended (KV rows read per core layer)   */
+  int64_t post_calls;        /* post role calls that ran the lm_head          */
 } ls_stats;
 
 typedef struct ls_engine ls_engine;
@@ -109,8 +107,8 @@ int ls_finalize(ls_engine* eng);
  * layers add all ranks' O / down partials and QK-norm sums in rank order
  * over NVLink, so all ranks compute identical rows and decisions. A peer
  * that stops publishing makes the waiting ranks fail with LS_EDEVICE after a
- * bounded wait. Ranks must be on distinct GPUs, the persistent path is not
- * supported, and ls_tp_init must precede the first role call. The reference
+ * bounded wait. Ranks must be on distinct GPUs, and ls_tp_init must precede
+ * the first role call. The reference
  * rejects tensor parallelism for LoopSpec (cli.py:97-108); the target is
  * TP-N greedy output equal to TP-1 output. */
 #define LS_TP_HANDLE_BYTES 128
@@ -195,20 +193,6 @@ int ls_pipeline_simulate(int stages, int step_size, int second_step, int64_t fir
 int ls_time_role(ls_engine* eng, int role, int n_lanes, int context_len, int iters,
                  double* avg_ms);
 
-/* Diagnostics (no reference counterpart): run one role call of the
- * persistent kernel eagerly, on the same synthetic lanes as ls_time_role, and
- * return its per-phase timing trace: out[(phase * grid + cta) * 12 + f] in
- * globaltimer nanoseconds, f = 0 start of work, 1 arrival, 2 first
- * accumulator ready, 3 first activation load issued, 4 work done, 5 fences
- * done, 6 inputs seen complete by the TMA producer, 7 last GEMM segment
- * finished, 8 last activation load issued, 9 first stage taken by the MMA
- * issuer, 10 first segment's MMAs issued, 11 weight stages already issued
- * when the inputs were seen complete (a count); phase index n_phases holds
- * each CTA's kernel entry (f 0) and co-residency pass (f 1). Zero where a
- * CTA had no such event. */
-int ls_trace_role(ls_engine* eng, int role, int n_lanes, int context_len, uint64_t* out,
-                  int64_t max_entries, int* n_phases, int* grid);
-
 /* Time one GEMM of the core layer 0 (which: 0 qkv, 1 o, 2 gate_up, 3 down,
  * 4 lm_head) over n_lanes lanes, `iters` launches; average device ms. */
 int ls_time_gemm(ls_engine* eng, int which, int n_lanes, int iters, double* avg_ms);
@@ -270,12 +254,16 @@ int ls_decode_attention(const float* q, const void* k_pool, const void* v_pool, 
  * and result as ls_decode_attention minus the workspace: the scratch is a
  * fixed 4 MiB array inside the library (ls_decode_attention_noalloc_limit()),
  * held on every GPU that loads the library until exit. Shapes whose scratch
- * (about n_lanes * n_heads * ceil(max_context/256) * head_dim * 4 bytes)
- * exceeds it are rejected with LS_ECAPACITY. The first call on a device looks
- * up the array's device address, so make it before any stream capture. All
- * calls on a device share the array: the call clears what must start at
- * zero, later calls overwrite the rest, and calls that overlap on the GPU
- * race. Calls no cudaMalloc, cudaFree or allocating library routine. */
+ * (about n_lanes * n_heads * ceil(max_context/128) * (head_dim + 2) * 4
+ * bytes: one partial per 128-position chunk) exceeds it are rejected with
+ * LS_ECAPACITY. The first call on a device looks up the array's device
+ * address and keeps it for the life of the process (a device reset would
+ * make it stale), so make that first call before any stream capture. Like
+ * ls_decode_attention, each call waits for `stream` to finish before it
+ * returns. All calls on a device share the array: the call clears what must
+ * start at zero, later calls overwrite the rest, and calls that overlap on
+ * the GPU race. Calls no cudaMalloc, cudaFree or allocating library
+ * routine. */
 int ls_decode_attention_noalloc(const float* q, const void* k_pool, const void* v_pool,
                                 const int32_t* map, const int32_t* lane_rows,
                                 const int32_t* lane_lens, int n_lanes, int n_heads, int n_kv_heads,

@@ -40,8 +40,7 @@ class SchedCfg(ctypes.Structure):
         ("step_size", _i32), ("second_step", _i32),
         ("max_context", _i32), ("max_prompt", _i32),
         ("kv_slots", _i32), ("request_rows", _i32),
-        ("use_graphs", _i32), ("use_pdl", _i32), ("use_persistent", _i32),
-        ("l2_prefetch", _i32),
+        ("use_graphs", _i32), ("use_pdl", _i32),
     ]
 
 
@@ -53,6 +52,7 @@ class Stats(ctypes.Structure):
         ("second_rejections", _i64), ("decode_tokens", _i64),
         ("decode_device_ms", _f64), ("decode_host_s", _f64), ("prefill_device_ms", _f64),
         ("h2d_bytes", _i64), ("d2h_bytes", _i64), ("decode_kernel_launches", _i64),
+        ("pre_calls", _i64), ("core_calls", _i64), ("core_kv_positions", _i64), ("post_calls", _i64),
     ]
 
     def as_dict(self):
@@ -90,8 +90,6 @@ SIGNATURES = [
                                     RETAIN_FN, _P, _PI64, ctypes.POINTER(_i32),
                                     ctypes.POINTER(Stats)]),
     ("ls_time_role", _i32, [_P, _i32, _i32, _i32, _i32, ctypes.POINTER(_f64)]),
-    ("ls_trace_role", _i32, [_P, _i32, _i32, _i32, ctypes.POINTER(_u64), _i64, ctypes.POINTER(_i32),
-                             ctypes.POINTER(_i32)]),
     ("ls_time_gemm", _i32, [_P, _i32, _i32, _i32, ctypes.POINTER(_f64)]),
     ("ls_time_core_gemms", _i32, [_P, _i32, _i32, ctypes.POINTER(_f64), ctypes.POINTER(_f64)]),
     ("ls_role_kernel_count", _i32, [_P, _i32, _i32, ctypes.POINTER(_i32)]),

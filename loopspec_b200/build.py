@@ -15,7 +15,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 # translation units compiled in parallel, then linked into one library
-SRCS = [os.path.join(HERE, "csrc", "engine.cu"), os.path.join(HERE, "csrc", "stack.cu")]
+SRCS = [os.path.join(HERE, "csrc", "engine.cu")]
 OUT = os.path.join(HERE, "libloopspec_engine.so")
 OBJ_DIR = os.path.join(HERE, "_build")
 

@@ -18,7 +18,7 @@ enum DeviceError : int {
   kDevTimeoutEmpty = 2,   // producer waited too long for a free stage
   kDevTimeoutAcc = 3,     // epilogue waited too long for the accumulator
   kDevBadIndex = 4,       // a metadata index was out of range (access skipped)
-  // 5 and 6 belong to the persistent path (stack_api.cuh)
+  // 5 and 6 are unused
   kDevTimeoutPeer = 7,    // a tensor-parallel peer did not publish its partials in time
 };
 
@@ -248,45 +248,6 @@ __host__ __device__ constexpr uint32_t umma_idesc_bf16(int M, int N) {
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-}
-
-// ------------------------------------------------------------ L2 prefetch
-// Weight ranges that the next GEMMs of a role call will stream. A
-// latency-bound kernel (attention, a norm row, input prep) leaves HBM idle, so
-// it hands these ranges to the memory system as bulk L2 prefetches
-// (cp.async.bulk.prefetch.L2: no completion, no shared memory, a hint that
-// cannot fault on the addresses given); the GEMM's TMA loads then hit L2.
-// Bytes are whole multiples of 16 (the host rounds down).
-struct L2Prefetch {
-  const void* p[2];
-  unsigned long long bytes[2];
-};
-
-constexpr unsigned kL2PrefetchChunk = 16384;
-
-__device__ __forceinline__ void l2_prefetch_bulk(const void* p, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
-}
-
-// This CTA's share of the prefetch: chunk j of the concatenated ranges goes
-// to CTA j % n_cta, thread (j / n_cta) % blockDim.x. One SM issues L2
-// requests at a few hundred GB/s, so a prefetch must be spread over (nearly)
-// all SMs to run at HBM speed: kernels with one CTA per lane are launched
-// with extra prefetch-only CTAs.
-__device__ __forceinline__ void l2_prefetch_share(const L2Prefetch& pf) {
-  const unsigned long long n0 = (pf.bytes[0] + kL2PrefetchChunk - 1) / kL2PrefetchChunk;
-  const unsigned long long n1 = (pf.bytes[1] + kL2PrefetchChunk - 1) / kL2PrefetchChunk;
-  if (n0 + n1 == 0) return;
-  const unsigned long long n_cta = (unsigned long long)gridDim.x * gridDim.y * gridDim.z;
-  const unsigned long long cta =
-      blockIdx.x + (unsigned long long)gridDim.x * (blockIdx.y + (unsigned long long)gridDim.y * blockIdx.z);
-  for (unsigned long long j = cta + n_cta * threadIdx.x; j < n0 + n1; j += n_cta * blockDim.x) {
-    const int r = j < n0 ? 0 : 1;
-    const unsigned long long off = (j < n0 ? j : j - n0) * kL2PrefetchChunk;
-    const unsigned long long left = pf.bytes[r] - off;
-    l2_prefetch_bulk(static_cast<const char*>(pf.p[r]) + off,
-                     (uint32_t)(left < kL2PrefetchChunk ? left : kL2PrefetchChunk));
-  }
 }
 
 // ------------------------------------------------------------- row helpers

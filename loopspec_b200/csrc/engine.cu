@@ -16,7 +16,6 @@
 #include "gemm_tc.cuh"
 #include "kernels.cuh"
 #include "sampler.cuh"
-#include "stack_api.cuh"
 
 #include <algorithm>
 #include <array>
@@ -136,7 +135,6 @@ struct StackEnd {
   float* bank = nullptr;             // scatter h into this bank at state_out
   bool want_x = false;               // produce x for a following GEMM
   const bf16* x_norm = nullptr;      // ... normalised by this weight (Raven ln_f)
-  L2Prefetch pf{};                   // weights of the GEMM after the stack
 };
 
 // Launch with optional programmatic-dependent-launch attribute.
@@ -416,25 +414,6 @@ struct ls_engine {
   long gemm_ticket_count = 0;
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
 
-  // persistent path: one phase program per role call kind, back to back in
-  // progs_dev; the weight maps they reference; activation maps per BN class
-  static constexpr int kProgPre = 0, kProgCore = 1, kProgPostHead = 2, kProgPostNoHead = 3, kProgs = 4;
-  static constexpr int kBnClasses = 5;                 // BN 16, 32, 64, 128, 256
-  Phase* progs_dev = nullptr;
-  int prog_off[kProgs] = {}, prog_len[kProgs] = {};
-  std::vector<CUtensorMap> prog_maps[kProgs];          // weight maps of each program
-  CUtensorMap xmaps_host[kBnClasses][kXBufs];          // activation maps per BN class
-  std::unique_ptr<StackLaunch> launch_buf;             // parameter block being assembled
-  float* stk_part = nullptr;                           // [2][num_sms][2][BN/2][128]
-  int* stk_tickets = nullptr;                          // [2][max tiles]
-  int* stk_cnt = nullptr;                              // completion counters (per tile / kv head)
-  int* stk_tot = nullptr;                              // per-phase completion counters
-  int prog_cnt[kProgs] = {};                           // counters used by each program
-  unsigned* stk_sync = nullptr;                        // grid counters, zero between launches
-  int stk_chunks = 0;                                  // attention chunks per (lane, head)
-  StackParams stk_base{};                              // launch fields fixed at finalize
-  unsigned long long* stk_trace = nullptr;             // set only by ls_trace_role (eager launches)
-
   std::map<std::pair<int, int>, cudaGraphExec_t> graphs;
   std::map<std::pair<int, int>, int> graph_kernels;   // kernels per captured graph
   std::map<std::pair<int, int>, int> graph_chunks;    // attention grid chunks per graph
@@ -451,6 +430,8 @@ struct ls_engine {
   // re-captured when it changes)
   int attn_chunks = 1;
   int64_t kernel_launches = 0;                        // kernels launched by role calls
+  // work counters of role calls (decode stats are differences around the loop)
+  int64_t pre_calls = 0, core_calls = 0, core_kv_positions = 0, post_calls = 0;
   int kernels_in_call = 0;
   // The next launch waits for full completion of the previous kernel (no
   // programmatic overlap). Set after the mapping update: every kernel
@@ -674,10 +655,8 @@ struct ls_engine {
     r = dalloc<float>((long)cap * H);
     q = dalloc<float>((long)cap * QD);
     part = dalloc<float>(part_elems);
-    stk_chunks = cdiv(max_ctx, kStkChunk);
-    const int chunk_slots = std::max(max_chunks, stk_chunks);
-    o_part = dalloc<float>((long)cap * NH * chunk_slots * HD);
-    ml_part = dalloc<float>((long)cap * NH * chunk_slots * 2);
+    o_part = dalloc<float>((long)cap * NH * max_chunks * HD);
+    ml_part = dalloc<float>((long)cap * NH * max_chunks * 2);
     logits = dalloc<float>((long)cap * V);
     const int xrows = round_up(2 * cap, 256);  // (hi, lo) row pair per lane
     auto mkx = [&](XBuf& xb, int Kd) {
@@ -718,323 +697,7 @@ struct ls_engine {
     CK(cudaMemcpy(inv_freq, inv.data(), sizeof(float) * inv.size(), cudaMemcpyHostToDevice));
 
     set_smem_attrs();
-    if (sc.use_persistent) build_programs();
     finalized = true;
-  }
-
-  // ------------------------------------------------------ persistent programs
-  // Phase programs restating enqueue_role / run_stack for the persistent
-  // kernel: the same steps, in the same order, as phases.
-  std::vector<CUtensorMap>* cur_maps = nullptr;   // maps of the program being built
-  int max_tiles = 0;
-  int b_xh = -1, b_map = -1;                      // program builder: last x_h writer, mapping phase
-
-  static void set_dep(Phase& p, int i, int kind, int phase) {
-    p.dep_kind[i] = kind;
-    p.dep_phase[i] = phase;
-  }
-
-  Phase ph_gemm(const Gemm& g, int xbuf, int epi, float* out, bf16* kp = nullptr, bf16* vp = nullptr,
-                bool head = false) {
-    Phase p{};
-    p.kind = kPhGemm;
-    p.xbuf = xbuf;
-    p.epi = epi;
-    p.Mw = g.Mw;
-    p.K = g.K;
-    p.KB = cdiv(g.K, kStkBK);   // k-units of the persistent kernel
-    p.m_tiles = epi == kEpiSwiGLU ? g.Mw / kGemmBM : cdiv(g.Mw, kGemmBM);
-    p.head = head ? 1 : 0;
-    p.out = out;
-    p.kpool = kp;
-    p.vpool = vp;
-    p.x_out = -1;
-    p.cnt_off = -1;
-    REQUIRE(epi != kEpiSwiGLU || g.has_map64, LS_EINVAL, "SwiGLU needs the 64-row weight map");
-    cur_maps->push_back(epi == kEpiSwiGLU ? g.map64 : g.map);
-    REQUIRE(cur_maps->size() <= (size_t)kStkMaxMaps, LS_EINVAL,
-            "too many weight GEMMs in one role call for the persistent kernel");
-    p.wmap = (int)cur_maps->size() - 1;
-    max_tiles = std::max(max_tiles, p.m_tiles);
-    return p;
-  }
-
-  static Phase ph_simple(int kind) {
-    Phase p{};
-    p.kind = kind;
-    p.x_out = -1;
-    p.cnt_off = -1;
-    return p;
-  }
-
-  static const bf16* in_norm(int layout, const LayerW& w) {
-    return layout == LS_LAYOUT_OLMO_POST ? nullptr : w.n_in;
-  }
-
-  // Layers of one stack. Dependencies (what each phase's work waits for):
-  // QKV on the last x_h writer; attention on its head's QKV tiles (or the
-  // QK-norm rows) and the mapping update; O per head on attention; row A on
-  // all O tiles; gate/up on row A; down per k-block on its gate/up tile;
-  // row B on all down tiles.
-  void add_stack(std::vector<Phase>& v, Stack& st, const StackEnd& end) {
-    const int L = mc.layout;
-    const int nl = (int)st.layers.size();
-    for (int l = 0; l < nl; ++l) {
-      LayerW& w = st.layers[l];
-      const long kvoff = (long)(st.kv_base + l) * n_slots * KVD;
-      bf16* kp = kpool + kvoff;
-      bf16* vp = vpool + kvoff;
-      int qkv_src;   // phase the attention reads q/k/v from
-      int qkv_kind;
-      if (w.qn) {
-        Phase g = ph_gemm(w.g_qkv, kXH, kEpiStore, part);
-        set_dep(g, 0, kDepTotLanes, b_xh);
-        v.push_back(g);
-        Phase qk = ph_simple(kPhQkNorm);
-        qk.src = part;
-        qk.q_norm_w = w.qn;
-        qk.k_norm_w = w.kn;
-        qk.kpool = kp;
-        qk.vpool = vp;
-        set_dep(qk, 0, kDepTotTiles, (int)v.size() - 1);
-        v.push_back(qk);
-        qkv_src = (int)v.size() - 1;
-        qkv_kind = kDepTotLanes;
-      } else {
-        Phase g = ph_gemm(w.g_qkv, kXH, kEpiQkvRope, nullptr, kp, vp);
-        set_dep(g, 0, kDepTotLanes, b_xh);
-        v.push_back(g);
-        qkv_src = (int)v.size() - 1;
-        qkv_kind = kDepQkvHead;
-      }
-      Phase at = ph_simple(kPhAttn);
-      at.kpool = kp;
-      at.vpool = vp;
-      set_dep(at, 0, qkv_kind, qkv_src);
-      if (b_map >= 0) set_dep(at, 1, kDepTotLanes, b_map);
-      v.push_back(at);
-      const int attn = (int)v.size() - 1;
-      Phase go = ph_gemm(w.g_o, kXAttn, kEpiStore, part);
-      set_dep(go, 0, kDepKbHead, attn);
-      v.push_back(go);
-      Phase ra = ph_simple(kPhRow);
-      ra.src = part;
-      ra.resid = h;
-      ra.out_h = r;
-      ra.x_out = kXH;
-      if (L == LS_LAYOUT_OURO) {
-        ra.a_norm_w = w.n_pa;
-        ra.x_norm_w = w.n_pf;
-      } else if (L == LS_LAYOUT_RAVEN_PRE) {
-        ra.x_norm_w = w.n_pa;
-      } else {
-        ra.a_norm_w = w.n_pa;
-      }
-      set_dep(ra, 0, kDepTotTiles, (int)v.size() - 1);
-      v.push_back(ra);
-      b_xh = (int)v.size() - 1;
-      Phase gu = ph_gemm(w.g_gu, kXH, kEpiSwiGLU, nullptr);
-      set_dep(gu, 0, kDepTotLanes, b_xh);
-      v.push_back(gu);
-      Phase gd = ph_gemm(w.g_down, kXAct, kEpiStore, part);
-      set_dep(gd, 0, kDepKbTile, (int)v.size() - 1);
-      v.push_back(gd);
-      Phase rb = ph_simple(kPhRow);
-      rb.src = part;
-      rb.resid = r;
-      rb.out_h = h;
-      if (L != LS_LAYOUT_RAVEN_PRE) rb.a_norm_w = w.n_pff;
-      if (l + 1 < nl) {
-        rb.x_out = kXH;
-        rb.x_norm_w = in_norm(L, st.layers[l + 1]);
-      } else {
-        rb.final_norm_w = end.final_norm;
-        rb.bank = end.bank;
-        if (end.want_x) {
-          rb.x_out = kXH;
-          rb.x_norm_w = end.x_norm;
-        }
-      }
-      set_dep(rb, 0, kDepTotTiles, (int)v.size() - 1);
-      v.push_back(rb);
-      b_xh = (int)v.size() - 1;
-    }
-  }
-
-  // prep phase: h = embedding (src null) or bank[state_in]
-  Phase ph_prep(const float* src, float* bank_out, int x_out, const bf16* x_norm) {
-    Phase p = ph_simple(kPhPrep);
-    p.src = src;
-    p.out_h = h;
-    p.bank = bank_out;
-    p.x_out = x_out;
-    p.x_norm_w = x_norm;
-    return p;
-  }
-
-  void build_programs() {
-    REQUIRE(cap <= kStkMaxLanes, LS_ECAPACITY, "persistent path supports at most 128 lanes per call");
-    REQUIRE(H / 4 <= kStkRowNV * kStkWorkers, LS_EINVAL, "hidden too large for the persistent row phases");
-    const bool ouro = mc.family == LS_FAMILY_OURO;
-    const int L = mc.layout;
-    std::vector<Phase> progs[kProgs];
-    // pre (ouro.py:101-136 / components.py:117-149)
-    cur_maps = &prog_maps[kProgPre];
-    b_xh = b_map = -1;
-    if (ouro) {
-      progs[kProgPre].push_back(ph_prep(nullptr, bank_h, -1, nullptr));
-    } else {
-      std::vector<Phase>& v = progs[kProgPre];
-      const bool layers = !pre.layers.empty();
-      if (layers) {
-        v.push_back(ph_simple(kPhMap));
-        b_map = 0;
-      }
-      v.push_back(ph_prep(nullptr, nullptr, layers ? kXH : -1, layers ? in_norm(L, pre.layers[0]) : nullptr));
-      b_xh = (int)v.size() - 1;
-      if (layers) add_stack(v, pre, StackEnd());
-      Phase ri = ph_simple(kPhRavenInit);
-      set_dep(ri, 0, kDepTotLanes, (int)v.size() - 1);   // the prelude output h
-      v.push_back(ri);
-    }
-    // core (ouro.py:93-98 / raven.py:271-281)
-    {
-      cur_maps = &prog_maps[kProgCore];
-      std::vector<Phase>& v = progs[kProgCore];
-      v.push_back(ph_simple(kPhMap));
-      b_map = 0;
-      StackEnd end;
-      end.bank = bank_h;
-      if (ouro) {
-        v.push_back(ph_prep(bank_h, nullptr, kXH, in_norm(L, core.layers[0])));
-        end.final_norm = step_norm;
-      } else {
-        v.push_back(ph_simple(kPhCat));
-        Phase ga = ph_gemm(g_adapter, kXCat, kEpiStore, part);
-        set_dep(ga, 0, kDepTotLanes, 1);
-        v.push_back(ga);
-        Phase ra = ph_simple(kPhRow);
-        ra.src = part;
-        ra.bias = adapter_b;
-        ra.out_h = h;
-        ra.x_out = kXH;
-        ra.x_norm_w = in_norm(L, core.layers[0]);
-        set_dep(ra, 0, kDepTotTiles, 2);
-        v.push_back(ra);
-      }
-      b_xh = (int)v.size() - 1;
-      add_stack(v, core, end);
-    }
-    // post (components.py:175-194), with and without the lm_head
-    for (int which : {kProgPostHead, kProgPostNoHead}) {
-      cur_maps = &prog_maps[which];
-      std::vector<Phase>& v = progs[which];
-      b_map = -1;
-      if (!post.layers.empty()) {
-        v.push_back(ph_simple(kPhMap));
-        b_map = 0;
-        v.push_back(ph_prep(bank_h, nullptr, kXH, in_norm(L, post.layers[0])));
-        b_xh = (int)v.size() - 1;
-        StackEnd end;
-        end.want_x = true;
-        end.x_norm = final_norm;
-        add_stack(v, post, end);
-      } else {
-        v.push_back(ph_prep(bank_h, nullptr, kXH, final_norm));
-        b_xh = (int)v.size() - 1;
-      }
-      if (which == kProgPostHead) {
-        Phase gh = ph_gemm(g_lm, kXH, kEpiStore, logits, nullptr, nullptr, true);
-        set_dep(gh, 0, kDepTotLanes, b_xh);
-        v.push_back(gh);
-      }
-    }
-    // completion counters: one per GEMM tile and per attention kv head
-    int max_cnt = 0, max_len = 0;
-    for (int i = 0; i < kProgs; ++i) {
-      int off = 0, gi = 0;
-      for (Phase& ph : progs[i]) {
-        if (ph.kind == kPhGemm) {
-          ph.cnt_off = off;
-          off += ph.m_tiles;
-          ph.gemm_idx = gi++;
-        } else if (ph.kind == kPhAttn) {
-          ph.cnt_off = off;
-          off += NKV;
-        }
-      }
-      prog_cnt[i] = off;
-      max_cnt = std::max(max_cnt, off);
-      max_len = std::max(max_len, (int)progs[i].size());
-    }
-    stk_cnt = dalloc<int>(max_cnt);
-    stk_tot = dalloc<int>(max_len);
-    cur_maps = nullptr;
-    std::vector<Phase> all;
-    for (int i = 0; i < kProgs; ++i) {
-      prog_off[i] = (int)all.size();
-      prog_len[i] = (int)progs[i].size();
-      all.insert(all.end(), progs[i].begin(), progs[i].end());
-    }
-    progs_dev = dalloc<Phase>(all.size());
-    CK(cudaMemcpy(progs_dev, all.data(), sizeof(Phase) * all.size(), cudaMemcpyHostToDevice));
-    // activation maps for every BN class (x_cat only exists for Raven)
-    const int bns[kBnClasses] = {16, 32, 64, 128, 256};
-    for (int c = 0; c < kBnClasses; ++c) {
-      xmaps_host[c][kXH] = x_h.map(bns[c]);
-      xmaps_host[c][kXAttn] = x_attn.map(bns[c]);
-      xmaps_host[c][kXAct] = x_act.map(bns[c]);
-      xmaps_host[c][kXCat] = x_cat.ptr ? x_cat.map(bns[c]) : x_h.map(bns[c]);
-    }
-    launch_buf.reset(new StackLaunch());
-    const int bn_max = cap * 2 <= 16 ? 16 : cap * 2 <= 32 ? 32 : cap * 2 <= 64 ? 64 : cap * 2 <= 128 ? 128 : 256;
-    stk_part = dalloc<float>(2L * num_sms * 2 * (bn_max / 2) * kGemmBM);
-    stk_tickets = dalloc<int>(2L * max_tiles);
-    stk_sync = dalloc<unsigned>(4);
-    CK(stack_prepare());
-
-    StackParams& P = stk_base;
-    P.x[kXH] = x_h.ptr;
-    P.x[kXAttn] = x_attn.ptr;
-    P.x[kXAct] = x_act.ptr;
-    P.x[kXCat] = x_cat.ptr;
-    P.xK[kXH] = H;
-    P.xK[kXAttn] = QD;
-    P.xK[kXAct] = I;
-    P.xK[kXCat] = 2 * H;
-    P.h = h;
-    P.q = q;
-    P.H = H;
-    P.NH = NH;
-    P.NKV = NKV;
-    P.HD = HD;
-    P.I = I;
-    P.inv_freq = inv_freq;
-    P.eps = mc.rms_eps;
-    P.attn_scale = 1.0f / std::sqrt((float)HD);
-    P.embed = embed;
-    P.embed_scale = mc.embed_scale;
-    P.vocab = V;
-    P.map = map;
-    P.max_ctx = max_ctx;
-    P.rows = rows;
-    P.n_slots = n_slots;
-    P.bank_h = bank_h;
-    P.bank_inj = bank_inj;
-    P.bank_rows = bank_rows;
-    P.init_seed = mc.init_seed;
-    P.init_std = mc.init_std;
-    P.o_part = o_part;
-    P.ml_part = ml_part;
-    P.attn_tickets = attn_tickets;
-    P.max_chunks = stk_chunks;
-    P.part_ws = stk_part;
-    P.tile_tickets = stk_tickets;
-    P.ticket_stride = max_tiles;
-    P.cnt = stk_cnt;
-    P.tot = stk_tot;
-    P.sync = stk_sync;
-    P.err = err_dev;
   }
 
   std::vector<long> birth_sizes() const {
@@ -1183,24 +846,6 @@ void map_update(ls_engine& e, Meta meta, int n) {
 // Threads of a per-lane row kernel: one float4 column each, at most 1024.
 int row_threads(int H) { return std::min(1024, H / 4); }
 
-// The weights of up to two GEMMs, for a latency-bound kernel to prefetch into
-// L2 while it runs (each range capped at kL2PrefetchCap bytes, so a prefetch
-// never pushes the L2 past what the next GEMMs read).
-constexpr unsigned long long kL2PrefetchCap = 64ull << 20;
-
-L2Prefetch l2pf(const ls_engine& e, const Gemm* a, const Gemm* b = nullptr) {
-  L2Prefetch pf{};
-  if (!e.sc.l2_prefetch) return pf;
-  const Gemm* g[2] = {a, b};
-  for (int i = 0; i < 2; ++i) {
-    if (!g[i] || !g[i]->w) continue;
-    const unsigned long long bytes = 2ull * (unsigned long long)g[i]->Mw * (unsigned long long)g[i]->K;
-    pf.p[i] = g[i]->w;
-    pf.bytes[i] = std::min(bytes, kL2PrefetchCap) & ~15ull;
-  }
-  return pf;
-}
-
 template <int FORM>
 void launch_attention(ls_engine& e, dim3 grid, dim3 blk, int G, const AttnArgs& a) {
   if (e.HD == 128 && G == 1) klaunch(e, attn_kernel<128, 1, FORM>, grid, blk, 0, a);
@@ -1220,11 +865,10 @@ int attention_form(long ctas, int sms) {
 
 // planes: the QKV projection's split planes (decode form), or null when the
 // projection's epilogue already wrote q and the new K/V.
-void attention(ls_engine& e, Meta meta, int n, bf16* kp, bf16* vp,
-               const L2Prefetch& pf = L2Prefetch{}, const Gemm* planes = nullptr) {
+void attention(ls_engine& e, Meta meta, int n, bf16* kp, bf16* vp, const Gemm* planes = nullptr) {
   AttnArgs a{meta, e.NH, e.NKV, e.q, e.map, e.max_ctx, e.rows, kp, vp, e.n_slots,
              e.max_chunks, e.o_part, e.ml_part, e.attn_tickets, e.x_attn.ptr, nullptr,
-             nullptr, nullptr, 1.0f / std::sqrt((float)e.HD), e.err_dev, pf};
+             nullptr, nullptr, 1.0f / std::sqrt((float)e.HD), e.err_dev};
   if (planes) {
     a.qkv = e.part;
     a.qkv_splits = planes->splits;
@@ -1254,16 +898,10 @@ ResidArgs resid_base(ls_engine& e, Meta meta, const Gemm& g) {
   return a;
 }
 
-// CTAs of a per-lane row kernel: one per lane, plus one prefetch-only CTA per
-// SM when it carries an L2 prefetch.
-int row_grid(const ls_engine& e, int n, const L2Prefetch& pf) {
-  return n + (pf.bytes[0] + pf.bytes[1] > 0 ? e.num_sms : 0);
-}
-
 void resid(ls_engine& e, ResidArgs a, int n) {
   a.B = n;
   const int thr = row_threads(e.H);
-  const dim3 grid(row_grid(e, n, a.pf));
+  const dim3 grid(n);
   if (a.tp.ranks > 1) {
     if (cdiv(e.H / 4, thr) > 1) klaunch(e, resid_epi_kernel<2, 4, 1024, true>, grid, dim3(thr), 0, a);
     else if (thr <= 512) klaunch(e, resid_epi_kernel<1, 10, 512, true>, grid, dim3(thr), 0, a);
@@ -1363,7 +1001,7 @@ void run_stack(ls_engine& e, Stack& st, int n, Meta meta, const StackEnd& end) {
       ep.n_slots = e.n_slots;
       gemm(e, w.g_qkv, e.x_h, ep, kEpiQkvRope, n);
     }
-    attention(e, meta, n, kp, vp, l2pf(e, &w.g_o, &w.g_gu), !w.qn && e.qkv_planes ? &w.g_qkv : nullptr);
+    attention(e, meta, n, kp, vp, !w.qn && e.qkv_planes ? &w.g_qkv : nullptr);
     ResidArgs ra = resid_base(e, meta, w.g_o);
     if (e.tp_ranks > 1) tp_split_store(e, w.g_o, e.x_attn, n, ra, e.tp_off_o, kTpSlotO);
     else gemm_split_store(e, w.g_o, e.x_attn, n);
@@ -1378,7 +1016,6 @@ void run_stack(ls_engine& e, Stack& st, int n, Meta meta, const StackEnd& end) {
     } else {
       ra.a_norm_w = w.n_pa;
     }
-    ra.pf = l2pf(e, &w.g_down);
     resid(e, ra, n);
 
     // gate_up with SiLU(gate) * up fused into its epilogue -> x_act
@@ -1396,11 +1033,9 @@ void run_stack(ls_engine& e, Stack& st, int n, Meta meta, const StackEnd& end) {
     if (!last) {
       rb.x = e.x_h.ptr;
       rb.x_norm_w = input_norm(e, st.layers[l + 1]);
-      rb.pf = l2pf(e, &st.layers[l + 1].g_qkv);
     } else {
       rb.final_norm_w = end.final_norm;
       rb.bank = end.bank;
-      rb.pf = end.pf;
       if (end.want_x) {
         rb.x = e.x_h.ptr;
         rb.x_norm_w = end.x_norm;
@@ -1418,9 +1053,8 @@ struct PostOpts {
 };
 
 void prep(ls_engine& e, Meta meta, int n, bool embed_mode, float* bank_out, bool want_x,
-          const bf16* x_norm, const L2Prefetch& pf = L2Prefetch{}) {
+          const bf16* x_norm) {
   PrepArgs pa{};
-  pa.pf = pf;
   pa.meta = meta;
   pa.B = n;
   pa.H = e.H;
@@ -1436,7 +1070,7 @@ void prep(ls_engine& e, Meta meta, int n, bool embed_mode, float* bank_out, bool
   pa.vocab = e.V;
   pa.err = e.err_dev;
   const int thr = row_threads(e.H);
-  const dim3 grid(row_grid(e, n, pa.pf));
+  const dim3 grid(n);
   if (cdiv(e.H / 4, thr) == 1) klaunch(e, prep_kernel<1>, grid, dim3(thr), 0, pa);
   else klaunch(e, prep_kernel<2>, grid, dim3(thr), 0, pa);
 }
@@ -1461,44 +1095,9 @@ void head_decisions(ls_engine& e, Meta meta, int lane0, int lanes) {
   }
 }
 
-// One role call as a single persistent kernel over all SMs (stack.cuh),
-// followed by the readout decisions when the call includes the lm_head.
-void enqueue_role_persistent(ls_engine& e, int role, int n, const PostOpts& po) {
-  REQUIRE(n >= 1 && n <= kStkMaxLanes, LS_ECAPACITY, "persistent role call wider than 128 lanes");
-  const Meta meta = meta_of(e, role);
-  e.kernels_in_call = 0;
-  const int prog = role == kPre ? ls_engine::kProgPre
-                   : role == kCore ? ls_engine::kProgCore
-                   : po.head ? ls_engine::kProgPostHead : ls_engine::kProgPostNoHead;
-  StackLaunch& L = *e.launch_buf;
-  StackParams& P = L.P;
-  P = e.stk_base;
-  P.phases = e.progs_dev + e.prog_off[prog];
-  P.n_phases = e.prog_len[prog];
-  P.n_cnt = e.prog_cnt[prog];
-  P.meta = meta;
-  P.n = n;
-  P.head_lane0 = role == kPost ? po.head_lane0 : 0;
-  P.head_n = role == kPost ? (po.head_lanes < 0 ? n : po.head_lanes) : 0;
-  REQUIRE(P.head_lane0 >= 0 && P.head_lane0 + P.head_n <= n, LS_EINVAL, "head lanes out of range");
-  const int bn = pick_bn(2 * n);
-  const int cls = bn == 16 ? 0 : bn == 32 ? 1 : bn == 64 ? 2 : bn == 128 ? 3 : 4;
-  std::memcpy(L.xmap, e.xmaps_host[cls], sizeof(L.xmap));
-  const std::vector<CUtensorMap>& maps = e.prog_maps[prog];
-  if (!maps.empty()) std::memcpy(L.wmap, maps.data(), sizeof(CUtensorMap) * maps.size());
-  P.trace = e.stk_trace;
-  CK(stack_launch(bn, e.HD, L, e.num_sms, e.stream, e.sc.use_pdl != 0));
-  e.kernels_in_call++;
-  if (role == kPost && po.head) head_decisions(e, meta, P.head_lane0, P.head_n);
-}
-
 // The kernel chain of one role call over n lanes whose metadata is in the
 // role's device metadata buffer.
 void enqueue_role(ls_engine& e, int role, int n, const PostOpts& po = PostOpts()) {
-  if (e.sc.use_persistent) {
-    enqueue_role_persistent(e, role, n, po);
-    return;
-  }
   Meta meta = meta_of(e, role);
   e.kernels_in_call = 0;
   const bool ouro = e.mc.family == LS_FAMILY_OURO;
@@ -1523,8 +1122,7 @@ void enqueue_role(ls_engine& e, int role, int n, const PostOpts& po = PostOpts()
     end.bank = e.bank_h;
     if (ouro) {
       // one core iteration = all layers then step_norm (ouro.py:93-98)
-      prep(e, meta, n, false, nullptr, true, input_norm(e, e.core.layers[0]),
-           l2pf(e, &e.core.layers[0].g_qkv));
+      prep(e, meta, n, false, nullptr, true, input_norm(e, e.core.layers[0]));
       end.final_norm = e.step_norm;
     } else {
       // adapter(cat(hidden, injected)) then the core blocks (raven.py:271-281)
@@ -1536,7 +1134,6 @@ void enqueue_role(ls_engine& e, int role, int n, const PostOpts& po = PostOpts()
       ra.out_h = e.h;
       ra.x = e.x_h.ptr;
       ra.x_norm_w = input_norm(e, e.core.layers[0]);
-      ra.pf = l2pf(e, &e.core.layers[0].g_qkv);
       resid(e, ra, n);
     }
     run_stack(e, e.core, n, meta, end);
@@ -1545,12 +1142,10 @@ void enqueue_role(ls_engine& e, int role, int n, const PostOpts& po = PostOpts()
     const bool has_layers = !e.post.layers.empty();
     if (has_layers && po.layers) {
       map_update(e, meta, n);
-      prep(e, meta, n, false, nullptr, true, input_norm(e, e.post.layers[0]),
-           l2pf(e, &e.post.layers[0].g_qkv));
+      prep(e, meta, n, false, nullptr, true, input_norm(e, e.post.layers[0]));
       StackEnd end;
       end.want_x = true;
       end.x_norm = e.final_norm;
-      if (po.head) end.pf = l2pf(e, &e.g_lm);
       run_stack(e, e.post, n, meta, end);
     } else if (!has_layers) {
       prep(e, meta, n, false, nullptr, true, e.final_norm);
@@ -1587,7 +1182,11 @@ void run_role(ls_engine& e, int role, int n, const int* host_meta, bool graphabl
   int longest = 1;
   bool single = true;   // no lane shares its timeline with an earlier lane of the call
   bool forks = false;
+  if (role == kPre && e.mc.n_pre_layers > 0) e.pre_calls++;
+  if (role == kCore) e.core_calls++;
+  if (role == kPost && po.head) e.post_calls++;
   for (int b = 0; b < n; ++b) {
+    if (role == kCore) e.core_kv_positions += host_meta[b * kMetaFields + kMetaPos] + 1;
     longest = std::max(longest, host_meta[b * kMetaFields + kMetaPos] + 1);
     single = single && host_meta[b * kMetaFields + kMetaAhead] <= 0;
     forks = forks || host_meta[b * kMetaFields + kMetaForkRow] >= 0;
@@ -1659,7 +1258,7 @@ void raise_device_error(ls_engine& e, int err) {
     CK(cudaMemset(e.err_dev, 0, sizeof(int)));
     static const char* names[] = {"ok", "TMA stage wait timed out", "free-stage wait timed out",
                                   "accumulator wait timed out", "metadata index out of range",
-                                  "grid phase wait timed out", "persistent CTAs not co-resident",
+                                  "unused (5)", "unused (6)",
                                   "tensor-parallel peer wait timed out"};
     throw EngineError(LS_EDEVICE, std::string("device reported: ") +
                                       (err > 0 && err < 8 ? names[err] : "unknown error"));
@@ -2324,7 +1923,9 @@ char* g_noalloc_ptr[kMaxDevices] = {};
 // Device address of the scratch array on the current device. In host code
 // the array's name is only a host-side stand-in, so the real address is
 // looked up once per device (the first call on that device does it, with
-// that device current) and cached.
+// that device current) and cached for the life of the process: the cache
+// assumes the device is not reset (cudaDeviceReset) while the library is
+// loaded.
 char* noalloc_scratch_for_current_device() {
   int dev = -1;
   CK(cudaGetDevice(&dev));
@@ -2361,7 +1962,7 @@ int ls_decode_attention_noalloc(const float* q, const void* k_pool, const void* 
     REQUIRE(need <= kNoAllocScratchBytes, LS_ECAPACITY,
             "decode attention (no-alloc): this shape needs " + std::to_string(need) +
                 " scratch bytes, above the fixed " + std::to_string(kNoAllocScratchBytes) +
-                " (lanes x heads x ceil(max_context/256) x head_dim x 4 bytes must fit); "
+                " (lanes x heads x ceil(max_context/128) x (head_dim + 2) x 4 bytes must fit); "
                 "use ls_decode_attention with a workspace");
     char* base = noalloc_scratch_for_current_device();
     const AttnScratch sc =
@@ -2482,7 +2083,6 @@ int ls_tp_init(ls_engine* e, int rank, int ranks, void* handle_out) {
     REQUIRE(e->tp_region == nullptr, LS_EINVAL, "tensor parallelism already initialised");
     REQUIRE(ranks >= 2 && ranks <= kTpMax && rank >= 0 && rank < ranks, LS_EINVAL,
             "tensor parallelism needs 2..8 ranks and 0 <= rank < ranks");
-    REQUIRE(!e->sc.use_persistent, LS_EINVAL, "tensor parallelism runs on the multi-kernel path only");
     REQUIRE(e->graphs.empty(), LS_EINVAL, "initialise tensor parallelism before the first role call");
     CK(cudaSetDevice(e->device));
     // planes of the widest O / down projection of any stack
@@ -2648,6 +2248,8 @@ int generate_request(ls_engine* e, const int64_t* prompt, int n_prompt, int max_
     REQUIRE(e->prefill_len + max_new < e->max_ctx, LS_ECAPACITY, "prompt + max_new_tokens exceeds max_context");
     double t0 = -1.0;
     const int64_t launches0 = e->kernel_launches;
+    const int64_t pre0 = e->pre_calls, core0 = e->core_calls, kv0 = e->core_kv_positions,
+                  post0 = e->post_calls;
     CK(cudaEventRecord(e->ev0, e->stream));
     std::vector<long long> ids;
     if (mode == 0) {
@@ -2669,6 +2271,10 @@ int generate_request(ls_engine* e, const int64_t* prompt, int n_prompt, int max_
     st.h2d_bytes = e->h2d_bytes;
     st.d2h_bytes = e->d2h_bytes;
     st.decode_kernel_launches = e->kernel_launches - launches0;
+    st.pre_calls = e->pre_calls - pre0;
+    st.core_calls = e->core_calls - core0;
+    st.core_kv_positions = e->core_kv_positions - kv0;
+    st.post_calls = e->post_calls - post0;
     if (stats) *stats = st;
   } catch (const std::exception& ex) {
     return fail(e, ex);
@@ -2824,54 +2430,6 @@ int ls_time_role(ls_engine* e, int role, int n, int context_len, int iters, doub
     float ms = 0.f;
     CK(cudaEventElapsedTime(&ms, e->ev0, e->ev1));
     *avg_ms = ms / iters;
-  } catch (const std::exception& ex) {
-    return fail(e, ex);
-  }
-  return LS_OK;
-}
-
-int ls_trace_role(ls_engine* e, int role, int n, int context_len, uint64_t* out, int64_t max_entries,
-                  int* n_phases, int* grid) {
-  if (!e || !out || !n_phases || !grid || role < 0 || role > 2 || n < 1) return LS_EINVAL;
-  try {
-    REQUIRE(e->sc.use_persistent, LS_EINVAL, "tracing needs the persistent path");
-    REQUIRE(e->prefill_len >= 0, LS_EINVAL, "ls_trace_role needs a prefilled request");
-    REQUIRE(n <= e->max_rows, LS_ECAPACITY, "too many lanes");
-    REQUIRE(context_len >= 1 && context_len <= e->prefill_len + 1, LS_EINVAL,
-            "context_len must not exceed the prompt");
-    const int prog = role == kPre ? ls_engine::kProgPre : role == kCore ? ls_engine::kProgCore
-                                                                        : ls_engine::kProgPostHead;
-    const long entries = (long)(e->prog_len[prog] + 1) * e->num_sms * kStkTraceFields + 4 * 4096;
-    REQUIRE(entries <= max_entries, LS_ECAPACITY, "trace buffer too small");
-    const bool attn = role == kCore || (role == kPre && e->mc.n_pre_layers) ||
-                      (role == kPost && e->mc.n_post_layers);
-    int* m = stage_meta(*e);
-    for (int b = 0; b < n; ++b) {
-      Cursor c;
-      if (attn) {
-        Cursor* root = e->tl.get_or_create_cursor(role, role == kPost ? e->S - 1 : 0, 0, -1);
-        c.row = e->tl.alloc_row();
-        c.seq_len = context_len - 1;
-        c.pending_parent_row = root->row;
-      }
-      fill_lane(*e, m, b, 1, context_len - 1, attn ? &c : nullptr, b, b);
-    }
-    run_role(*e, role, n, m, false);   // warm-up, eager
-    unsigned long long* tr = e->dalloc<unsigned long long>(entries);
-    e->stk_trace = tr;
-    try {
-      run_role(*e, role, n, m, false);
-    } catch (...) {
-      e->stk_trace = nullptr;
-      throw;
-    }
-    e->stk_trace = nullptr;
-    CK(cudaStreamSynchronize(e->stream));
-    e->staging_next = 0;
-    check_device(*e);
-    CK(cudaMemcpy(out, tr, sizeof(uint64_t) * entries, cudaMemcpyDeviceToHost));
-    *n_phases = e->prog_len[prog];
-    *grid = e->num_sms;
   } catch (const std::exception& ex) {
     return fail(e, ex);
   }

@@ -56,15 +56,13 @@ struct PrepArgs {
   float eps;
   int vocab;
   int* err;
-  L2Prefetch pf;               // weights of the GEMMs that follow
 };
 
 template <int NV>
 __global__ void prep_kernel(PrepArgs a) {
   pdl_launch_dependents();
-  l2_prefetch_share(a.pf);
   const int b = blockIdx.x;
-  if (b >= a.B) return;         // prefetch-only CTA
+  if (b >= a.B) return;
   __shared__ float red[32];
   const int H = a.H, H4 = H / 4;
   int src;
@@ -213,7 +211,7 @@ __global__ void tp_publish_kernel(int* epoch, int* flags, int slot) {
 // x[b] = (hi, lo) of (x_norm ? rms(out) * wx : out) (optional).
 struct ResidArgs {
   Meta meta;
-  int B, H;                    // lanes (CTAs past B only prefetch), hidden size
+  int B, H;                    // lanes, hidden size
   const float* part;           // GEMM output y: split planes [splits][cap][H]
   int splits;                  // planes to add, in split order (>= 1)
   long split_stride;           // floats between planes
@@ -228,7 +226,6 @@ struct ResidArgs {
   const __nv_bfloat16* x_norm_w;
   float eps;
   int* err;
-  L2Prefetch pf;               // weights of the GEMMs that follow
   TpView tp;                   // ranks > 1: y = every rank's planes, rank by rank
   int tp_slot;
 };
@@ -240,9 +237,8 @@ struct ResidArgs {
 template <int NV, int BATCH, int MAXT, bool TP>
 __global__ void __launch_bounds__(MAXT) resid_epi_kernel(ResidArgs a) {
   pdl_launch_dependents();
-  l2_prefetch_share(a.pf);
   const int b = blockIdx.x;
-  if (b >= a.B) return;         // prefetch-only CTA
+  if (b >= a.B) return;
   __shared__ float red[32];
   const int H = a.H, H4 = H / 4;
   const float4 z = make_float4(0.f, 0.f, 0.f, 0.f), one = make_float4(1.f, 1.f, 1.f, 1.f);
@@ -464,7 +460,6 @@ struct AttnArgs {
   const int* lane_row;             // optional per-lane mapping row (else metadata)
   float scale;
   int* err;
-  L2Prefetch pf;                   // weights of the GEMMs that follow
   // Decode form (qkv non-null): the QKV projection left its split planes
   // [splits][cap][(nh + 2 nkv) * HD] and every lane has exactly one new
   // position (T - 1). Each CTA sums its q (split order) and applies RoPE; the
@@ -504,7 +499,6 @@ template <int HD, int G, int FORM>
 __global__ void __launch_bounds__(kAttnThreads, FORM + 2) attn_kernel(AttnArgs a) {
   constexpr bool VLATE = FORM == kAttnVLate;
   pdl_launch_dependents();
-  l2_prefetch_share(a.pf);
   constexpr int LPP = HD / 8;              // lanes per position (16 B each)
   constexpr int PPW = 32 / LPP;            // positions per warp at a time
   constexpr int NW = kAttnThreads / 32;

@@ -31,7 +31,7 @@ class Engine:
     def __init__(self, cfg: ModelConfig, schedule: PipelineSchedule, weights: dict, *,
                  device: int = 0, max_context: int = 4096, max_prompt: int | None = None,
                  kv_slots: int = 0, request_rows: int = 0, use_graphs: bool = True,
-                 use_pdl: bool = True, use_persistent: bool = False, l2_prefetch: bool = False):
+                 use_pdl: bool = True):
         if schedule.stages != cfg.stages:
             raise ValueError("schedule stages must equal the model's recurrence count")
         self.cfg = cfg
@@ -50,8 +50,7 @@ class Engine:
             step_size=schedule.step_size, second_step=schedule.second_step or 0,
             max_context=max_context, max_prompt=max_prompt or max_context // 2,
             kv_slots=kv_slots, request_rows=request_rows, use_graphs=int(use_graphs),
-            use_pdl=int(use_pdl), use_persistent=int(use_persistent),
-            l2_prefetch=int(l2_prefetch))
+            use_pdl=int(use_pdl))
         handle = ctypes.c_void_p()
         code = self.L.ls_create(ctypes.byref(mc), ctypes.byref(sc), device, ctypes.byref(handle))
         if code != _lib.LS_OK:
@@ -160,20 +159,6 @@ class Engine:
         r = {"pre": 0, "core": 1, "post": 2}[role]
         _lib.check(self.L.ls_time_role(self.h, r, n_lanes, context_len, iters, ctypes.byref(ms)), self.h)
         return ms.value
-
-    def trace_role(self, role, n_lanes, context_len):
-        """Per-phase globaltimer trace of one persistent role call: array [phases + 1, grid, 12]."""
-        import numpy as np
-        r = {"pre": 0, "core": 1, "post": 2}[role]
-        cap = 1 << 22
-        buf = np.zeros(cap, dtype=np.uint64)
-        nph, grid = ctypes.c_int32(), ctypes.c_int32()
-        _lib.check(self.L.ls_trace_role(self.h, r, n_lanes, context_len,
-                                        buf.ctypes.data_as(ctypes.POINTER(ctypes.c_uint64)), cap,
-                                        ctypes.byref(nph), ctypes.byref(grid)), self.h)
-        n = (nph.value + 1) * grid.value * 12
-        self.last_stage_log = buf[n:n + 4 * 4096].reshape(4, 4096)   # CTA 0 per-stage SM clocks
-        return buf[:n].reshape(nph.value + 1, grid.value, 12)
 
     def time_gemm(self, which, n_lanes, iters=50):
         ms = ctypes.c_double()

@@ -34,13 +34,6 @@ def main():
     p.add_argument("--iters", type=int, default=3)
     p.add_argument("--first", type=int, default=1)
     p.add_argument("--second", type=int, default=2)
-    p.add_argument("--persistent", action="store_true",
-                   help="one persistent kernel per role call instead of one kernel per step")
-    p.add_argument("--trace", action="store_true",
-                   help="persistent path: print the per-phase critical-path breakdown of one call")
-    p.add_argument("--trace-out", default=None, help="also save the raw trace (.npy)")
-    p.add_argument("--l2-prefetch", action="store_true",
-                   help="multi-kernel path: latency-bound kernels prefetch upcoming GEMM weights into L2")
     p.add_argument("--sampling", action="store_true",
                    help="post role: top-p 0.9 sampling decisions instead of greedy argmax")
     p.add_argument("--prefill-only", action="store_true",
@@ -52,8 +45,7 @@ def main():
     w = init_random_weights(cfg, 0, device="cuda:0", dtype=torch.bfloat16)
     X = a.second // a.first if a.second else None
     eng = Engine(cfg, PipelineSchedule(cfg.stages, a.first, X), w, device=0,
-                 max_context=max(2048, a.prompt + 64), max_prompt=a.prompt,
-                 use_persistent=a.persistent, l2_prefetch=a.l2_prefetch)
+                 max_context=max(2048, a.prompt + 64), max_prompt=a.prompt)
     g = torch.Generator().manual_seed(0)
     prompt = torch.randint(0, cfg.vocab, (a.prompt,), generator=g).tolist()
     if a.prefill_only:
@@ -74,54 +66,12 @@ def main():
     torch.cuda.nvtx.range_push("decode_replays")
     ms = eng.time_role(a.role, a.lanes, a.prompt, a.iters)
     torch.cuda.nvtx.range_pop()
-    print(json.dumps({"config": cfg.name, "path": "persistent" if a.persistent else "multikernel",
+    print(json.dumps({"config": cfg.name,
                       "role": a.role, "lanes": a.lanes, "context": a.prompt,
                       "ms_per_call": round(ms, 4), "kernels_per_call": per_call,
                       "timed_replays": a.iters, "warmup_replays": 1,
                       "launches_in_range": (a.iters + 1) * per_call}))
-    if a.trace and a.persistent:
-        tr = eng.trace_role(a.role, a.lanes, a.prompt)
-        if a.trace_out:
-            import numpy as np
-            np.save(a.trace_out, tr)
-            np.save(a.trace_out.replace(".npy", "_stages.npy"), eng.last_stage_log)
-        print(json.dumps(trace_summary(tr, cfg)))
     eng.close()
-
-
-def trace_summary(tr, cfg):
-    """Critical path of one persistent call from its globaltimer trace.
-
-    Phase p completes when its last CTA arrives (C_p); its latency is
-    C_p - C_{p-1}. For GEMM phases the latency splits into `to_acc` (previous
-    completion to the median CTA's first ready accumulator: activation load +
-    MMAs) and `tail` (the rest: epilogue, reduction, barrier).
-    """
-    import numpy as np
-    tr = tr.astype(np.int64)
-    nph = tr.shape[0] - 1
-    coresident = int(tr[nph, :, 1].max())
-    entry = tr[nph, :, 0]
-    prev = coresident
-    out = {"phases": nph, "total_us": round((int(tr[nph - 1, :, 1].max()) - int(entry[entry > 0].min())) / 1e3, 2),
-           "launch_to_coresident_us": round((coresident - int(entry[entry > 0].min())) / 1e3, 2)}
-    layer = ["qkv", "attn", "o", "row_a", "gate_up", "down", "row_b"]
-    head = 2 if cfg.family == "ouro" else 0
-    agg = {}
-    for p in range(nph):
-        done = int(tr[p, :, 1].max())
-        lat = done - prev
-        acc = tr[p, :, 2]
-        name = layer[(p - head) % 7] if cfg.family == "ouro" and p >= head else f"phase{p}"
-        d = agg.setdefault(name, {"n": 0, "lat": 0.0, "to_acc": 0.0})
-        d["n"] += 1
-        d["lat"] += lat / 1e3
-        if (acc > 0).any():
-            d["to_acc"] += (float(np.median(acc[acc > 0])) - prev) / 1e3
-        prev = done
-    out["per_kind_avg_us"] = {k: {"lat": round(v["lat"] / v["n"], 2), "to_acc": round(v["to_acc"] / v["n"], 2),
-                                  "n": v["n"]} for k, v in agg.items()}
-    return out
 
 
 if __name__ == "__main__":

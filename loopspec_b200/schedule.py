@@ -56,11 +56,11 @@ class PipelineSchedule:
     def __post_init__(self):
         S, K, X = self.stages, self.step_size, self.second_step
         if not isinstance(S, int) or S <= 0:
-            raise ValueError(f"stages S must be a positive integer, got {S}")
+            raise ValueError(f"the recurrence count must be at least 1 (got S={S})")
         if not isinstance(K, int) or not 1 <= K < S or S % K:
-            raise ValueError(f"step_size K must be a positive divisor of S with K < S; got K={K}, S={S}")
+            raise ValueError(f"--first must divide the recurrence count and be smaller than it (got K={K}, S={S})")
         if X is not None and (not isinstance(X, int) or not 1 < X < S // K):
-            raise ValueError(f"second_step X must satisfy 1 < X < S/K so K*X < S; got X={X}, S/K={S // K}")
+            raise ValueError(f"--second must be a multiple of --first strictly between it and the recurrence count (got X={X}, S/K={S // K})")
 
     @property
     def depth(self) -> int:

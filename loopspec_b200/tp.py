@@ -91,8 +91,6 @@ def make_tp_engine(cfg: ModelConfig, schedule, weights: dict, rank: int, ranks: 
     handle in rank order; the default gathers them over torch.distributed.
     All ranks must call this together, and later make the same engine calls."""
     from .engine import Engine
-    if engine_kw.get("use_persistent"):
-        raise ValueError("tensor parallelism runs on the multi-kernel path only")
     eng = Engine(shard_config(cfg, ranks), schedule, shard_weights(weights, cfg, rank, ranks),
                  device=device, **engine_kw)
     try:

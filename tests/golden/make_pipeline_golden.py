@@ -33,7 +33,7 @@ def load_reference(root):
 
 
 def main():
-    root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("LOOPSPEC_REFERENCE", "/root/reference")
     pipeline, resolve = load_reference(root)
     traces = [run_case(c, pipeline.continue_pipelined, pipeline.PipelineSchedule,
                        pipeline.PipelineResult, resolve) for c in CASES]
