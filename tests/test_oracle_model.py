@@ -110,3 +110,68 @@ def test_oracle_loopspec_equals_ar(name, K, X):
     assert ls == ar
     assert stats["decode_tokens"] == 11
     assert stats["verified_proposals"] == stats["decode_tokens"]
+
+
+def _ouro_tf_layer(cfg, w, prefix):
+    """transformers' Gemma2DecoderLayer with Llama attention / MLP and plain
+    RMSNorm modules swapped in, as the reference's OuroDecoderLayer subclasses
+    SGLang's Gemma2DecoderLayer and replaces the same four parts
+    (sglang_recurrent/modeling/ouro.py:37-82): Gemma2's residual flow, Llama's
+    fused-QKV attention with neox RoPE and SiLU MLP, x * rsqrt(mean x^2 + eps) * w."""
+    from transformers import Gemma2Config, LlamaConfig
+    from transformers.models.gemma2.modeling_gemma2 import Gemma2DecoderLayer
+    from transformers.models.llama.modeling_llama import (LlamaAttention, LlamaMLP, LlamaRMSNorm,
+                                                          LlamaRotaryEmbedding)
+    lc = LlamaConfig(hidden_size=cfg.hidden, num_attention_heads=cfg.n_heads,
+                     num_key_value_heads=cfg.n_kv_heads, head_dim=cfg.head_dim,
+                     intermediate_size=cfg.intermediate, rms_norm_eps=cfg.rms_eps,
+                     rope_theta=cfg.rope_theta, attention_bias=False, mlp_bias=False)
+    lc._attn_implementation = "eager"
+    gc = Gemma2Config(hidden_size=cfg.hidden, num_attention_heads=cfg.n_heads,
+                      num_key_value_heads=cfg.n_kv_heads, head_dim=cfg.head_dim,
+                      intermediate_size=cfg.intermediate, rms_norm_eps=cfg.rms_eps)
+    gc._attn_implementation = "eager"
+    layer = Gemma2DecoderLayer(gc, 0)
+    layer.self_attn = LlamaAttention(lc, 0)
+    layer.mlp = LlamaMLP(lc)
+    for name in ("input_layernorm", "post_attention_layernorm", "pre_feedforward_layernorm",
+                 "post_feedforward_layernorm"):
+        setattr(layer, name, LlamaRMSNorm(cfg.hidden, eps=cfg.rms_eps))
+    nh, nkv, hd, I = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.intermediate
+    qkv = w[prefix + "self_attn.qkv_proj.weight"]
+    gu = w[prefix + "mlp.gate_up_proj.weight"]
+    sd = {
+        "self_attn.q_proj.weight": qkv[: nh * hd],
+        "self_attn.k_proj.weight": qkv[nh * hd:(nh + nkv) * hd],
+        "self_attn.v_proj.weight": qkv[(nh + nkv) * hd:],
+        "self_attn.o_proj.weight": w[prefix + "self_attn.o_proj.weight"],
+        "mlp.gate_proj.weight": gu[:I], "mlp.up_proj.weight": gu[I:],
+        "mlp.down_proj.weight": w[prefix + "mlp.down_proj.weight"],
+    }
+    for name in ("input_layernorm", "post_attention_layernorm", "pre_feedforward_layernorm",
+                 "post_feedforward_layernorm"):
+        sd[name + ".weight"] = w[prefix + name + ".weight"]
+    layer.load_state_dict(sd)
+    return layer.eval(), LlamaRotaryEmbedding(lc)
+
+
+def test_ouro_layer_matches_the_gemma2_residual_flow():
+    cfg = get_config("tiny")
+    w = init_random_weights(cfg, 3, dtype=torch.float32)
+    g = torch.Generator().manual_seed(6)
+    for k in list(w):
+        if k.endswith("norm.weight"):
+            w[k] = 1.0 + 0.1 * torch.randn(w[k].shape, generator=g)
+    m = OracleModel(cfg.as_dict(), w)
+    prefix = "recurrent_executor.blocks.1."
+    layer, rot = _ouro_tf_layer(cfg, w, prefix)
+    L = 9
+    x = torch.randn(1, L, cfg.hidden, generator=g)
+    pos = torch.arange(L)[None]
+    mask = torch.full((L, L), float("-inf")).triu(1)[None, None]
+    with torch.no_grad():
+        ref = layer(x, attention_mask=mask, position_ids=pos, position_embeddings=rot(x, pos))
+        ref = ref[0] if isinstance(ref, tuple) else ref
+        tl = Timeline(1)
+        got = torch.stack([m.layer(prefix, x[0, p], p, tl, 0) for p in range(L)])
+    torch.testing.assert_close(got, ref[0], atol=2e-5, rtol=2e-5)
