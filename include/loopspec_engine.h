@@ -2,9 +2,10 @@
  * loopspec_engine.h -- C ABI of the B200-native LoopSpec decode engine
  * (libloopspec_engine.so, built for sm_100a).
  *
- * One engine handle serves one looped model on one GPU and runs one request
- * at a time, like the reference's batch-1 LoopSpec server
- * (sglang_recurrent/server/cli.py:88-89). Plain pointers and sizes only: no
+ * One engine handle serves one looped model on one GPU. It runs one request
+ * at a time through the reference-shaped entry points, like the reference's
+ * batch-1 LoopSpec server (sglang_recurrent/server/cli.py:88-89), and up to
+ * max_requests together through ls_generate_batch. Plain pointers and sizes only: no
  * torch types cross this boundary. Weight pointers are device pointers owned
  * by the caller; the engine owns its KV pool, timeline mapping table, state
  * banks and workspaces. Every function returns 0 on success or a negative
@@ -57,6 +58,8 @@ typedef struct ls_sched_cfg {
   int32_t request_rows;      /* timeline mapping rows (0: auto)              */
   int32_t use_graphs;        /* capture one CUDA graph per (role, width)     */
   int32_t use_pdl;           /* programmatic dependent launch between kernels */
+  int32_t max_requests;      /* requests ls_generate_batch serves together (0: 1);
+                                request_rows / kv_slots size each of them      */
 } ls_sched_cfg;
 
 /* Counters of sglang_recurrent/loopspec/executor.py:35-45 plus timing. */
@@ -168,6 +171,26 @@ typedef int (*ls_commit_fn)(void* user, const int64_t* ids, int n);
 int ls_generate_stream(ls_engine* eng, const int64_t* prompt, int n_prompt, int max_new_tokens,
                        int mode, int64_t stop_token, ls_commit_fn on_commit, void* user,
                        int64_t* out_ids, int* n_out, ls_stats* stats);
+
+/* Several requests decoded together (no counterpart in the reference, whose
+ * LoopSpec server runs one request at a time, server/cli.py:88-89). Each
+ * request is prefilled in turn, then every cycle runs one pre, K core and one
+ * post call over the lanes of all running requests (mode 0: one
+ * continue_pipelined per request, pipeline.py:254-423; mode 1: one
+ * autoregressive step per running request). Each request keeps its own branch
+ * timelines, state slots, random-stream cycle and seed (seeds[i], or the
+ * ls_set_sampling seed + i when seeds is NULL), and every kernel computes a
+ * lane's numbers independently of the other lanes of its call, so request i
+ * commits exactly what it commits alone with the same seed. prompts: the
+ * n_requests prompts back to back, prompt_lens[i] tokens each (n_requests <=
+ * max_requests). out_ids: int64 [n_requests][max_new_tokens]; n_out: int32
+ * [n_requests]. per_request (optional, [n_requests]): each request's scheduler
+ * counters and tokens, with the batch's decode time; total (optional): their
+ * sums, the batch's work counters, copy volumes and decode time. */
+int ls_generate_batch(ls_engine* eng, const int64_t* prompts, const int32_t* prompt_lens,
+                      int n_requests, int max_new_tokens, int mode, int64_t stop_token,
+                      const uint64_t* seeds, int64_t* out_ids, int32_t* n_out,
+                      ls_stats* per_request, ls_stats* total);
 
 /* The native scheduler loop of ls_generate mode 0 (continue_pipelined,
  * pipeline.py:254-423, with greedy resolve decisions.py:136-184 and the

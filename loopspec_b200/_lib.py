@@ -40,7 +40,7 @@ class SchedCfg(ctypes.Structure):
         ("step_size", _i32), ("second_step", _i32),
         ("max_context", _i32), ("max_prompt", _i32),
         ("kv_slots", _i32), ("request_rows", _i32),
-        ("use_graphs", _i32), ("use_pdl", _i32),
+        ("use_graphs", _i32), ("use_pdl", _i32), ("max_requests", _i32),
     ]
 
 
@@ -86,6 +86,9 @@ SIGNATURES = [
                            ctypes.POINTER(Stats)]),
     ("ls_generate_stream", _i32, [_P, _PI64, _i32, _i32, _i32, _i64, COMMIT_FN, _P, _PI64,
                                   ctypes.POINTER(_i32), ctypes.POINTER(Stats)]),
+    ("ls_generate_batch", _i32, [_P, _PI64, ctypes.POINTER(_i32), _i32, _i32, _i32, _i64,
+                                 ctypes.POINTER(_u64), _PI64, ctypes.POINTER(_i32),
+                                 ctypes.POINTER(Stats), ctypes.POINTER(Stats)]),
     ("ls_pipeline_simulate", _i32, [_i32, _i32, _i32, _i64, _i32, _i64, DECIDE_FN, CYCLE_FN,
                                     RETAIN_FN, _P, _PI64, ctypes.POINTER(_i32),
                                     ctypes.POINTER(Stats)]),

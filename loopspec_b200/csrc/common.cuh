@@ -38,7 +38,10 @@ enum MetaField : int {
   kMetaSecond = 10,   // post rows: the lane's q2 token, or -1
   kMetaCycle = 11,    // post rows: per-request draw counter (random stream index)
   kMetaAhead = 12,    // lanes of the same timeline filled earlier in this call
-  kMetaFields = 13,
+  kMetaDrawRow = 13,  // post rows: index among the request's readouts of this cycle
+  kMetaSeedLo = 14,   // post rows: the request's sampling seed, low / high 32 bits
+  kMetaSeedHi = 15,
+  kMetaFields = 16,
 };
 
 struct Meta {

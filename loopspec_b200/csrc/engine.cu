@@ -190,9 +190,14 @@ struct Node {
 
 class Timelines {
  public:
-  void configure(int rows, int slots) {
+  // A request owns mapping rows [row_base, row_base + rows) and KV slots
+  // [slot_base, slot_base + slots); requests batched in one engine get
+  // disjoint ranges.
+  void configure(int rows, int slots, int row_base = 0, int slot_base = 0) {
     rows_ = rows;
     slots_ = slots;
+    row_base_ = row_base;
+    slot_base_ = slot_base;
     reset();
   }
 
@@ -204,9 +209,9 @@ class Timelines {
     }
     nodes_.clear();
     free_rows_.clear();
-    for (int r = rows_ - 1; r >= 0; --r) free_rows_.push_back(r);
+    for (int r = rows_ - 1; r >= 0; --r) free_rows_.push_back(row_base_ + r);
     free_slots_.clear();
-    for (int s = slots_ - 1; s >= 0; --s) free_slots_.push_back(s);
+    for (int s = slots_ - 1; s >= 0; --s) free_slots_.push_back(slot_base_ + s);
   }
 
   ~Timelines() { reset(); }
@@ -346,11 +351,24 @@ class Timelines {
     release_unused(p);
   }
 
-  int rows_ = 0, slots_ = 0;
+  int rows_ = 0, slots_ = 0, row_base_ = 0, slot_base_ = 0;
   std::map<int, Node*> nodes_;
   std::vector<int> free_rows_, free_slots_;
 };
 
+}  // namespace
+
+namespace {
+// One request of a batch: its branch timelines (disjoint mapping rows and KV
+// slots), prompt length, random-stream cycle counter and sampling seed. Its
+// recurrent state slots are [state_base, state_base + max_rows).
+struct Request {
+  Timelines tl;
+  int prefill_len = -1;     // len(prompt) - 1
+  uint32_t draw_cycle = 0;  // the first token uses draw 0, decode cycles 1, 2, ...
+  unsigned long long seed = 0;
+  int state_base = 0;
+};
 }  // namespace
 
 // ======================================================================= engine
@@ -407,7 +425,6 @@ struct ls_engine {
   SampleParams* sparams_dev = nullptr;
   float *q1_bank = nullptr, *r_bank = nullptr, *samp_work = nullptr;
   long long *dec_dev = nullptr, *dec_host = nullptr;
-  uint32_t draw_cycle = 0;
   float* gemm_part = nullptr;   // GEMM split partial tiles
   long gemm_part_elems = 0;
   int* gemm_tickets = nullptr;  // GEMM per-tile split-arrival counters, zero between launches
@@ -458,8 +475,10 @@ struct ls_engine {
   std::vector<void*> tp_opened;   // peer mappings, closed before the engine frees memory
   unsigned long long tp_wait_ns = kTpWaitNs;
 
-  Timelines tl;
-  int prefill_len = -1;   // len(prompt) - 1 of the current request
+  // Requests served together (ls_generate_batch); single-request entry points
+  // use reqs[0]. max_state = max_req * max_rows state slots in the banks.
+  std::vector<Request> reqs;
+  int max_req = 1, max_state = 0;
 
   // ----------------------------------------------------------------- memory
   template <typename T>
@@ -587,13 +606,16 @@ struct ls_engine {
     REQUIRE(H % 128 == 0 && H <= 8192 && QD + 2 * KVD <= 12288, LS_EINVAL,
             "hidden must be a multiple of 128 and at most 8192 for the row kernels");
 
-    cap = std::max(max_rows, prefill_chunk);
+    max_req = std::max(1, sc.max_requests);
+    REQUIRE(max_req <= 64, LS_EINVAL, "at most 64 requests per batch");
+    max_state = max_req * max_rows;
+    cap = std::max(max_state, prefill_chunk);
     max_ctx = sc.max_context;
     REQUIRE(max_ctx > 1 && sc.max_prompt >= 1 && sc.max_prompt < max_ctx, LS_EINVAL,
             "need 1 <= max_prompt < max_context");
     max_chunks = cdiv(max_ctx, kAttnChunk);
     REQUIRE(max_chunks <= kAttnMaxChunks, LS_EINVAL, "max_context above the attention kernel's limit");
-    bank_rows = max_rows + prefill_chunk;
+    bank_rows = max_state + prefill_chunk;   // state slots, then prefill scratch rows
     n_attn_layers = mc.n_pre_layers + mc.n_core_layers + mc.n_post_layers;
 
     // timelines per branch: pre (if attention), S core, one post per endpoint
@@ -621,7 +643,15 @@ struct ls_engine {
     } else {
       n_slots = n_timelines * (max_ctx + 2 * max_rows) + 2 * rows;
     }
-    tl.configure(rows, n_slots);
+    // per-request capacities (request_rows / kv_slots size one request),
+    // disjoint ranges per request
+    reqs.assign(max_req, Request());
+    for (int i = 0; i < max_req; ++i) {
+      reqs[i].tl.configure(rows, n_slots, i * rows, i * n_slots);
+      reqs[i].state_base = i * max_rows;
+    }
+    rows *= max_req;
+    n_slots *= max_req;
 
     // weights
     embed = W("pre_executor.embed_tokens.weight", {V, H});
@@ -676,9 +706,9 @@ struct ls_engine {
     gemm_part = dalloc<float>(gemm_part_elems);
     sparams_dev = dalloc<SampleParams>(1);
     CK(cudaMemcpy(sparams_dev, &sparams, sizeof(SampleParams), cudaMemcpyHostToDevice));
-    q1_bank = dalloc<float>((long)max_rows * V);
-    r_bank = dalloc<float>((long)max_rows * V);
-    samp_work = dalloc<float>((long)max_rows * 2 * V);
+    q1_bank = dalloc<float>((long)max_state * V);
+    r_bank = dalloc<float>((long)max_state * V);
+    samp_work = dalloc<float>((long)max_state * 2 * V);
     dec_dev = dalloc<long long>((long)cap * 5);
     CK(cudaMallocHost(&dec_host, sizeof(long long) * 5 * (size_t)cap));
     CK(cudaMallocHost(&err_host, sizeof(int)));
@@ -1078,9 +1108,9 @@ void prep(ls_engine& e, Meta meta, int n, bool embed_mode, float* bank_out, bool
 // Readout decisions of the head lanes: fused sampler or greedy argmax.
 void head_decisions(ls_engine& e, Meta meta, int lane0, int lanes) {
   if (e.sampling) {
-    REQUIRE(lanes <= e.max_rows, LS_ECAPACITY, "too many sampled readout rows");
+    REQUIRE(lanes <= e.max_state, LS_ECAPACITY, "too many sampled readout rows");
     SampleArgs sa{meta, lane0, e.logits, e.V, e.sparams_dev, e.q1_bank, e.r_bank,
-                  e.max_rows, e.samp_work, e.dec_dev, e.err_dev};
+                  e.max_state, e.samp_work, e.dec_dev, e.err_dev};
     // rows in 16-byte steps when the vocabulary allows (logits, banks and
     // scratch rows are then 16-byte aligned)
     const size_t psm = (size_t)e.V * sizeof(float);
@@ -1276,11 +1306,11 @@ void put(ls_engine& e, int* m, int field, int b, int v) {
 }
 
 // Fill one lane of a role call. With a cursor, allocate the KV slot that this
-// token's K/V gets on that timeline and describe a pending fork copy.
-// `ahead` counts lanes of the same timeline filled earlier in this call
-// (prefill feeds a whole prompt chunk of one timeline at once).
+// token's K/V gets on that timeline (from the lane's request) and describe a
+// pending fork copy. `ahead` counts lanes of the same timeline filled earlier
+// in this call (prefill feeds a whole prompt chunk of one timeline at once).
 // Returns the slot (or -1).
-int fill_lane(ls_engine& e, int* m, int b, int token, int pos, Cursor* c, int state_in,
+int fill_lane(ls_engine& e, Timelines& tl, int* m, int b, int token, int pos, Cursor* c, int state_in,
               int state_out, int ahead = 0) {
   put(e, m, kMetaToken, b, token);
   put(e, m, kMetaPos, b, pos);
@@ -1291,7 +1321,7 @@ int fill_lane(ls_engine& e, int* m, int b, int token, int pos, Cursor* c, int st
           "timeline length " + std::to_string(c->seq_len) + " does not match position " +
               std::to_string(pos));
   REQUIRE(pos < e.max_ctx, LS_ECAPACITY, "context longer than max_context");
-  const int slot = e.tl.alloc_slot();
+  const int slot = tl.alloc_slot();
   put(e, m, kMetaRow, b, c->row);
   put(e, m, kMetaSlot, b, slot);
   put(e, m, kMetaForkRow, b, c->pending_parent_row);
@@ -1308,25 +1338,35 @@ void advance(Cursor* c, int slot, bool owned) {
   c->seq_len += 1;
 }
 
+// The random stream of a readout row: the request's seed and cycle counter,
+// and the row's index among the request's readouts of that cycle.
+void set_draw(ls_engine& e, int* m, int b, const Request& R, int draw, int draw_row) {
+  put(e, m, kMetaCycle, b, draw);
+  put(e, m, kMetaDrawRow, b, draw_row);
+  put(e, m, kMetaSeedLo, b, (int)(uint32_t)(R.seed & 0xFFFFFFFFull));
+  put(e, m, kMetaSeedHi, b, (int)(uint32_t)(R.seed >> 32));
+}
+
 // A readout that only draws the next token (no proposal to verify).
-void set_final_readout(ls_engine& e, int* m, int b, int draw) {
+void set_final_readout(ls_engine& e, int* m, int b, const Request& R, int draw, int draw_row) {
   put(e, m, kMetaKind, b, 2);
   put(e, m, kMetaFirst, b, -1);
   put(e, m, kMetaSecond, b, -1);
-  put(e, m, kMetaCycle, b, draw);
+  set_draw(e, m, b, R, draw, draw_row);
 }
 
-long long prefill(ls_engine& e, const int64_t* prompt, int P, float* logits_out) {
+long long prefill(ls_engine& e, Request& R, const int64_t* prompt, int P, float* logits_out) {
   REQUIRE(e.finalized, LS_EINVAL, "engine not finalized");
   REQUIRE(P >= 1 && P <= e.sc.max_prompt, LS_EINVAL, "prompt length out of range");
   for (int i = 0; i < P; ++i)
     REQUIRE(prompt[i] >= 0 && prompt[i] < e.V, LS_EINVAL, "prompt token out of vocabulary");
   CK(cudaSetDevice(e.device));
   CK(cudaStreamSynchronize(e.stream));
-  e.tl.reset();
+  Timelines& tl = R.tl;
+  tl.reset();
   e.staging_next = 0;
-  e.prefill_len = P - 1;
-  e.draw_cycle = 0;   // the first token uses draw 0, decode cycles 1, 2, ...
+  R.prefill_len = P - 1;
+  R.draw_cycle = 0;   // the first token uses draw 0, decode cycles 1, 2, ...
   CK(cudaMemsetAsync(e.err_dev, 0, sizeof(int), e.stream));
   CK(cudaEventRecord(e.ev0, e.stream));
   struct PrefillMode {   // unsplit wide projections while prefill enqueues (see prefill_mode)
@@ -1336,13 +1376,15 @@ long long prefill(ls_engine& e, const int64_t* prompt, int P, float* logits_out)
   } prefill_scope(e);
 
   const bool pre_attn = e.mc.n_pre_layers > 0, post_attn = e.mc.n_post_layers > 0;
-  Cursor* pre_c = pre_attn ? e.tl.create_root_cursor(kPre, 0) : nullptr;
+  Cursor* pre_c = pre_attn ? tl.create_root_cursor(kPre, 0) : nullptr;
   std::vector<Cursor*> core_c(e.S);
-  for (int s = 0; s < e.S; ++s) core_c[s] = e.tl.create_root_cursor(kCore, s);
+  for (int s = 0; s < e.S; ++s) core_c[s] = tl.create_root_cursor(kCore, s);
   std::map<int, Cursor*> post_c;
   if (post_attn)
-    for (auto& ep : e.endpoint_kind) post_c[ep.first] = e.tl.create_root_cursor(kPost, ep.first);
+    for (auto& ep : e.endpoint_kind) post_c[ep.first] = tl.create_root_cursor(kPost, ep.first);
 
+  // prompt lanes use the scratch bank rows after every request's state slots
+  const int scratch = e.max_state;
   const int chunk = e.prefill_chunk;
   for (int c0 = 0; c0 < P; c0 += chunk) {
     const int n = std::min(chunk, P - c0);
@@ -1350,34 +1392,34 @@ long long prefill(ls_engine& e, const int64_t* prompt, int P, float* logits_out)
     std::vector<int> slots(n);
     int* m = stage_meta(e);
     for (int j = 0; j < n; ++j)
-      slots[j] = fill_lane(e, m, j, (int)prompt[c0 + j], c0 + j, pre_c, -1, e.max_rows + j, j);
+      slots[j] = fill_lane(e, tl, m, j, (int)prompt[c0 + j], c0 + j, pre_c, -1, scratch + j, j);
     run_role(e, kPre, n, m, false);
     if (pre_c)
       for (int j = 0; j < n; ++j) advance(pre_c, slots[j], false);
     for (int s = 0; s < e.S; ++s) {
       m = stage_meta(e);
       for (int j = 0; j < n; ++j)
-        slots[j] = fill_lane(e, m, j, (int)prompt[c0 + j], c0 + j, core_c[s], e.max_rows + j,
-                             e.max_rows + j, j);
+        slots[j] = fill_lane(e, tl, m, j, (int)prompt[c0 + j], c0 + j, core_c[s], scratch + j,
+                             scratch + j, j);
       run_role(e, kCore, n, m, false);
       for (int j = 0; j < n; ++j) advance(core_c[s], slots[j], false);
       if (post_attn && e.endpoint_kind.count(s)) {
         m = stage_meta(e);
         for (int j = 0; j < n; ++j)
-          slots[j] = fill_lane(e, m, j, 0, c0 + j, post_c[s], e.max_rows + j, -1, j);
+          slots[j] = fill_lane(e, tl, m, j, 0, c0 + j, post_c[s], scratch + j, -1, j);
         PostOpts po;
         po.head = last_chunk && s == e.S - 1;
         po.head_lane0 = n - 1;
         po.head_lanes = 1;
-        if (po.head) set_final_readout(e, m, n - 1, 0);
+        if (po.head) set_final_readout(e, m, n - 1, R, 0, 0);
         run_role(e, kPost, n, m, false, po);
         for (int j = 0; j < n; ++j) advance(post_c[s], slots[j], false);
       }
     }
     if (!post_attn && last_chunk) {
       m = stage_meta(e);
-      fill_lane(e, m, 0, 0, P - 1, nullptr, e.max_rows + n - 1, -1);
-      set_final_readout(e, m, 0, 0);
+      fill_lane(e, tl, m, 0, 0, P - 1, nullptr, scratch + n - 1, -1);
+      set_final_readout(e, m, 0, R, 0, 0);
       run_role(e, kPost, 1, m, false);
     }
   }
@@ -1397,36 +1439,46 @@ long long prefill(ls_engine& e, const int64_t* prompt, int P, float* logits_out)
 }
 
 struct CycleLane {
-  int stage, index, token, branch, parent, state;
+  int stage, index, token, branch, parent, state;   // state: global state slot
   int origin = -1;   // scheduler bookkeeping only (trace output)
   int first = -1;    // the lane's q1 token (-1: none)
   int second = -1;   // the lane's q2 token (-1: none)
+  int req = 0;       // the lane's request (index into the engine's batch)
 };
 
 // One readout decision: (token, proposed, accepted_code, q1_rejected,
 // q2_rejected) for sampling (policy.py:197-218); greedy fills [0] only.
 typedef std::array<long long, 5> Dec;
 
-// One pipeline cycle (executor.py:293-367 without the decision policy):
-// pre for stage-0 lanes, K core iterations for all lanes, post + argmax for
-// readout lanes. dec[i] = argmax token for readout lanes, -1 otherwise.
+// One pipeline cycle (executor.py:293-367 without the decision policy) over
+// the lanes of one or more requests: pre for stage-0 lanes, K core iterations
+// for all lanes, post + decision for readout lanes, each role as one call
+// over every request's lanes. dec[i] = the readout lane's decision, -1
+// otherwise. Each request present advances its own random-stream cycle.
 void cycle(ls_engine& e, const std::vector<CycleLane>& lanes, std::vector<Dec>& dec,
            float* logits_out) {
-  REQUIRE(e.prefill_len >= 0, LS_EINVAL, "no prefilled request");
   const int B = (int)lanes.size();
-  REQUIRE(B >= 1 && B <= e.max_rows, LS_ECAPACITY, "speculative tree exceeded branch row limit");
+  REQUIRE(B >= 1 && B <= e.max_state, LS_ECAPACITY, "speculative tree exceeded branch row limit");
   const bool pre_attn = e.mc.n_pre_layers > 0, post_attn = e.mc.n_post_layers > 0;
   std::vector<int> pos(B), pre_rows, ends(B), ep_rows;
+  // random-stream index of this cycle's readouts: the request's pipeline
+  // cycle number, counted whether or not the cycle has a readout
+  std::vector<int> draw(e.reqs.size(), -1);
   for (int i = 0; i < B; ++i) {
     const CycleLane& l = lanes[i];
-    REQUIRE(l.state >= 0 && l.state < e.max_rows, LS_EINVAL, "state slot out of range");
+    REQUIRE(l.req >= 0 && l.req < (int)e.reqs.size(), LS_EINVAL, "lane request out of range");
+    Request& R = e.reqs[l.req];
+    REQUIRE(R.prefill_len >= 0, LS_EINVAL, "no prefilled request");
+    REQUIRE(l.state >= R.state_base && l.state < R.state_base + e.max_rows, LS_EINVAL,
+            "state slot out of range");
     REQUIRE(l.stage >= 0 && l.stage + e.K <= e.S && l.stage % e.K == 0, LS_EINVAL, "bad lane stage");
     REQUIRE(l.index >= 1, LS_EINVAL, "bad lane index");
     REQUIRE(l.token >= 0 && l.token < e.V, LS_EINVAL, "lane token out of vocabulary");
-    pos[i] = e.prefill_len + l.index;
+    pos[i] = R.prefill_len + l.index;
     ends[i] = l.stage + e.K - 1;
     if (l.stage == 0) pre_rows.push_back(i);
     if (e.endpoint_kind.count(ends[i])) ep_rows.push_back(i);
+    if (draw[l.req] < 0) draw[l.req] = (int)(++R.draw_cycle);
   }
   std::vector<int> slots(B);
   if (!pre_rows.empty()) {
@@ -1434,8 +1486,9 @@ void cycle(ls_engine& e, const std::vector<CycleLane>& lanes, std::vector<Dec>& 
     std::vector<Cursor*> cs(pre_rows.size(), nullptr);
     for (size_t j = 0; j < pre_rows.size(); ++j) {
       const CycleLane& l = lanes[pre_rows[j]];
-      if (pre_attn) cs[j] = e.tl.get_or_create_cursor(kPre, 0, l.branch, l.parent);
-      slots[j] = fill_lane(e, m, (int)j, l.token, pos[pre_rows[j]], cs[j], -1, l.state);
+      Timelines& tl = e.reqs[l.req].tl;
+      if (pre_attn) cs[j] = tl.get_or_create_cursor(kPre, 0, l.branch, l.parent);
+      slots[j] = fill_lane(e, tl, m, (int)j, l.token, pos[pre_rows[j]], cs[j], -1, l.state);
     }
     run_role(e, kPre, (int)pre_rows.size(), m, true);
     for (size_t j = 0; j < pre_rows.size(); ++j)
@@ -1446,28 +1499,28 @@ void cycle(ls_engine& e, const std::vector<CycleLane>& lanes, std::vector<Dec>& 
     std::vector<Cursor*> cs(B);
     for (int i = 0; i < B; ++i) {
       const CycleLane& l = lanes[i];
-      cs[i] = e.tl.get_or_create_cursor(kCore, l.stage + off, l.branch, l.parent);
-      slots[i] = fill_lane(e, m, i, l.token, pos[i], cs[i], l.state, l.state);
+      Timelines& tl = e.reqs[l.req].tl;
+      cs[i] = tl.get_or_create_cursor(kCore, l.stage + off, l.branch, l.parent);
+      slots[i] = fill_lane(e, tl, m, i, l.token, pos[i], cs[i], l.state, l.state);
     }
     run_role(e, kCore, B, m, true);
     for (int i = 0; i < B; ++i) advance(cs[i], slots[i], true);
   }
   dec.assign(B, Dec{-1, 0, 0, 0, 0});
-  // random-stream index of this cycle's readouts: the pipeline cycle number,
-  // counted whether or not the cycle has a readout
-  const int draw = (int)(++e.draw_cycle);
   if (ep_rows.empty()) return;
   const int M = (int)ep_rows.size();
   int* m = stage_meta(e);
   std::vector<Cursor*> cs(M, nullptr);
+  std::vector<int> rows_of(e.reqs.size(), 0);   // readout rows per request so far
   for (int j = 0; j < M; ++j) {
     const CycleLane& l = lanes[ep_rows[j]];
-    if (post_attn) cs[j] = e.tl.get_or_create_cursor(kPost, ends[ep_rows[j]], l.branch, l.parent);
-    slots[j] = fill_lane(e, m, j, l.token, pos[ep_rows[j]], cs[j], l.state, -1);
+    Request& R = e.reqs[l.req];
+    if (post_attn) cs[j] = R.tl.get_or_create_cursor(kPost, ends[ep_rows[j]], l.branch, l.parent);
+    slots[j] = fill_lane(e, R.tl, m, j, l.token, pos[ep_rows[j]], cs[j], l.state, -1);
     put(e, m, kMetaKind, j, e.endpoint_kind.at(ends[ep_rows[j]]));
     put(e, m, kMetaFirst, j, l.first);
     put(e, m, kMetaSecond, j, l.second);
-    put(e, m, kMetaCycle, j, draw);
+    set_draw(e, m, j, R, draw[l.req], rows_of[l.req]++);
   }
   run_role(e, kPost, M, m, true);
   for (int j = 0; j < M; ++j)
@@ -1561,63 +1614,74 @@ std::map<int, int> prune_ancestry(const std::vector<PLane>& lanes, int root,
   return out;
 }
 
-void retain_timelines(ls_engine& e, const std::vector<PLane>& lanes) {
-  std::vector<std::pair<int, int>> bp;
-  for (auto& l : lanes) bp.emplace_back(l.branch, l.parent);
-  e.tl.retain(bp);
-}
-
-// What the scheduler loop needs from an executor: the schedule, one cycle of
-// model execution (decisions per lane, -1 for non-readout lanes) and branch
-// retention. The engine binds these to the GPU; ls_pipeline_simulate binds
-// them to a host decision callback so the same loop is testable without a GPU.
+// What the scheduler loop needs from an executor besides the cycle itself:
+// the schedule, how decisions are resolved, branch retention and the stop
+// rule of one request. The engine binds retention to the request's GPU
+// timelines; ls_pipeline_simulate binds it to a host callback so the same
+// loop is testable without a GPU.
 struct SchedHooks {
   int S = 0, K = 1, X = 0, max_rows = 0;
   bool sampling = false;   // decisions are sampled 5-field rows, else greedy argmax
   std::map<int, int> endpoint_kind;
-  std::function<void(const std::vector<CycleLane>&, std::vector<Dec>&)> forward;
   std::function<void(const std::vector<PLane>&, int accepted_stage)> retain;
   std::function<bool(const std::vector<long long>&)> should_stop;
 };
 
-std::vector<long long> run_loopspec(SchedHooks& e, long long first, int max_new, ls_stats& st,
-                                    double& decode_t0) {
-  std::vector<long long> committed{first};
-  auto should_stop = [&](void) {
-    if (decode_t0 < 0) decode_t0 = now_s();
-    return e.should_stop(committed);
-  };
-  if (should_stop()) {
-    e.retain({}, -1);
-    return committed;
-  }
-  if (max_new == 1) {
-    e.retain({}, -1);
-    return committed;
-  }
-  const int q1 = e.K - 1, q2 = e.X ? e.K * e.X - 1 : -1, final_stage = e.S - 1;
-  StatePool pool(e.max_rows);
+// One request's pipeline (continue_pipelined, pipeline.py:254-423) as a state
+// machine, so that the lanes of several requests can share each cycle:
+// gather() adds this cycle's lanes, consume() takes their decisions and runs
+// the loop body (resolve, commit, branch selection, pruning, retention).
+struct PipelineRun {
+  const SchedHooks& hk;
+  int req, state_base, max_new;
+  std::vector<long long> committed;
+  ls_stats st{};
+  StatePool pool;
   int next_branch = 1;
   std::map<int, int> parents{{0, -1}};
-  std::vector<PLane> lanes(1);
-  lanes[0].index = 1;
-  lanes[0].token = (int)first;
-  std::vector<CycleLane> cl;
-  std::vector<Dec> dec;
-  while ((int)committed.size() < max_new) {
-    // executor.forward
-    cl.clear();
+  std::vector<PLane> lanes;
+  bool done = false;
+  double* decode_t0;
+
+  PipelineRun(const SchedHooks& h, int r, int base, long long first, int mx, double* t0)
+      : hk(h), req(r), state_base(base), max_new(mx), committed{first}, pool(h.max_rows),
+        decode_t0(t0) {
+    if (stop() || max_new == 1) {
+      hk.retain({}, -1);
+      done = true;
+      return;
+    }
+    lanes.resize(1);
+    lanes[0].index = 1;
+    lanes[0].token = (int)first;
+  }
+
+  bool stop() {
+    if (*decode_t0 < 0) *decode_t0 = now_s();
+    return hk.should_stop(committed);
+  }
+
+  // executor.forward's lanes: every live lane, with a state slot
+  void gather(std::vector<CycleLane>& cl) {
     for (auto& l : lanes) {
       if (l.state < 0) l.state = pool.acquire();  // written back as result.state
-      cl.push_back({l.stage, l.index, l.token, l.branch, l.parent, l.state, l.origin,
-                    l.first_token, l.second_token});
+      CycleLane c{l.stage, l.index, l.token, l.branch, l.parent, state_base + l.state};
+      c.origin = l.origin;
+      c.first = l.first_token;
+      c.second = l.second_token;
+      c.req = req;
+      cl.push_back(c);
     }
-    e.forward(cl, dec);
+  }
+
+  // dec: this request's decisions, in gather() order
+  void consume(const Dec* dec) {
+    const int q1 = hk.K - 1, q2 = hk.X ? hk.K * hk.X - 1 : -1, final_stage = hk.S - 1;
     st.pipeline_cycles += 1;
-    st.recurrent_rows += (int64_t)lanes.size() * e.K;
+    st.recurrent_rows += (int64_t)lanes.size() * hk.K;
     for (auto& l : lanes) {
       st.pre_rows += l.stage == 0;
-      st.post_rows += e.endpoint_kind.count(l.stage + e.K - 1);
+      st.post_rows += hk.endpoint_kind.count(l.stage + hk.K - 1);
     }
     // continue_pipelined body
     std::vector<PLane> following, children;
@@ -1626,15 +1690,15 @@ std::vector<long long> run_loopspec(SchedHooks& e, long long first, int max_new,
     int accepted_stage = -1;
     for (size_t i = 0; i < lanes.size(); ++i) {
       PLane& l = lanes[i];
-      const int end_stage = l.stage + e.K - 1;
-      auto kit = e.endpoint_kind.find(end_stage);
-      const int kind = kit == e.endpoint_kind.end() ? -1 : kit->second;
+      const int end_stage = l.stage + hk.K - 1;
+      auto kit = hk.endpoint_kind.find(end_stage);
+      const int kind = kit == hk.endpoint_kind.end() ? -1 : kit->second;
       // resolve (greedy: decisions.py:136-184; sampling: policy.py:285-308)
       const Dec& d = dec[i];
       const long long pred = d[0];
       bool proposed = false, fr = false, sr = false;
       int acc = -1;
-      if (e.sampling) {
+      if (hk.sampling) {
         proposed = d[1] != 0;
         acc = d[2] == 1 ? q1 : d[2] == 2 ? q2 : -1;
         fr = d[3] != 0;
@@ -1688,11 +1752,12 @@ std::vector<long long> run_loopspec(SchedHooks& e, long long first, int max_new,
       const PLane fl = lanes[final_idx];
       REQUIRE(fl.index == (int)committed.size(), LS_EPIPELINE, "pipeline attempted to commit out of order");
       committed.push_back(final_pred);
-      if (should_stop()) {
+      if (stop()) {
         lanes.clear();
         pool.retain(lanes);
-        e.retain({}, -1);
-        return committed;
+        hk.retain({}, -1);
+        done = true;
+        return;
       }
       accepted_stage = fl.first_token >= 0 ? accepted_stage : -1;
       if (fl.index + 1 < max_new) {
@@ -1731,14 +1796,36 @@ std::vector<long long> run_loopspec(SchedHooks& e, long long first, int max_new,
         accepted_stage = -1;
       }
     }
-    REQUIRE((int)following.size() <= e.max_rows, LS_EPIPELINE, "speculative tree exceeded branch row limit");
+    REQUIRE((int)following.size() <= hk.max_rows, LS_EPIPELINE, "speculative tree exceeded branch row limit");
     lanes.swap(following);
     pool.retain(lanes);
-    e.retain(lanes, accepted_stage);
+    hk.retain(lanes, accepted_stage);
     REQUIRE(!lanes.empty() || (int)committed.size() >= max_new, LS_EPIPELINE,
             "pipeline drained before generation completed");
+    if ((int)committed.size() >= max_new) done = true;
   }
-  return committed;
+};
+
+using Forward = std::function<void(const std::vector<CycleLane>&, std::vector<Dec>&)>;
+
+// Run the pipelines of several requests until all are done, each cycle over
+// the lanes of every request still running.
+void drive(std::vector<std::unique_ptr<PipelineRun>>& runs, const Forward& forward) {
+  std::vector<CycleLane> cl;
+  std::vector<Dec> dec;
+  std::vector<size_t> off(runs.size());
+  for (;;) {
+    cl.clear();
+    for (size_t i = 0; i < runs.size(); ++i) {
+      off[i] = cl.size();
+      if (!runs[i]->done) runs[i]->gather(cl);
+    }
+    if (cl.empty()) return;
+    forward(cl, dec);
+    for (size_t i = 0; i < runs.size(); ++i)
+      if (!runs[i]->done && off[i] < cl.size() && cl[off[i]].req == runs[i]->req)
+        runs[i]->consume(dec.data() + off[i]);
+  }
 }
 
 using StopRule = std::function<bool(const std::vector<long long>&)>;
@@ -1753,50 +1840,68 @@ StopRule stop_rule(long long stop_token, ls_commit_fn fn, void* user) {
   };
 }
 
-std::vector<long long> run_ar(ls_engine& e, long long first, int max_new, const StopRule& stop,
-                              double& decode_t0) {
-  std::vector<long long> committed{first};
+// Autoregressive decoding of several requests together (serving.py:216-239):
+// per step one lane per running request through pre, S core iterations and
+// post, each role as one call over all of them.
+void run_ar(ls_engine& e, std::vector<std::vector<long long>>& committed, std::vector<int>& reqs,
+            const std::vector<StopRule>& stop, int max_new, double& decode_t0) {
+  const int n = (int)reqs.size();
   decode_t0 = now_s();
-  if (stop(committed)) return committed;
+  std::vector<char> done(n, 0);
+  for (int i = 0; i < n; ++i) done[i] = stop[i](committed[i]) || (int)committed[i].size() >= max_new;
   const bool pre_attn = e.mc.n_pre_layers > 0, post_attn = e.mc.n_post_layers > 0;
-  int index = 1;
-  while ((int)committed.size() < max_new) {
-    const int tok = (int)committed.back();
-    const int pos = e.prefill_len + index;
-    int* m = stage_meta(e);
-    Cursor* c = pre_attn ? e.tl.get_or_create_cursor(kPre, 0, 0, -1) : nullptr;
-    int slot = fill_lane(e, m, 0, tok, pos, c, -1, 0);
-    run_role(e, kPre, 1, m, true);
-    if (c) advance(c, slot, true);
-    for (int s = 0; s < e.S; ++s) {
-      m = stage_meta(e);
-      c = e.tl.get_or_create_cursor(kCore, s, 0, -1);
-      slot = fill_lane(e, m, 0, tok, pos, c, 0, 0);
-      run_role(e, kCore, 1, m, true);
-      advance(c, slot, true);
+  std::vector<int> act, tok, pos, slot;
+  std::vector<Cursor*> c;
+  for (;;) {
+    act.clear();
+    for (int i = 0; i < n; ++i)
+      if (!done[i]) act.push_back(i);
+    if (act.empty()) break;
+    const int B = (int)act.size();
+    tok.assign(B, 0);
+    pos.assign(B, 0);
+    slot.assign(B, -1);
+    c.assign(B, nullptr);
+    for (int j = 0; j < B; ++j) {
+      Request& R = e.reqs[reqs[act[j]]];
+      tok[j] = (int)committed[act[j]].back();
+      pos[j] = R.prefill_len + (int)committed[act[j]].size();   // index = tokens committed so far
     }
-    m = stage_meta(e);
-    c = post_attn ? e.tl.get_or_create_cursor(kPost, e.S - 1, 0, -1) : nullptr;
-    slot = fill_lane(e, m, 0, tok, pos, c, 0, -1);
-    set_final_readout(e, m, 0, (int)(++e.draw_cycle));
-    run_role(e, kPost, 1, m, true);
-    if (c) advance(c, slot, true);
-    CK(cudaMemcpyAsync(e.amax_host, e.sampling ? e.dec_dev : e.amax_dev, sizeof(long long),
-                       cudaMemcpyDeviceToHost, e.stream));
-    e.d2h_bytes += sizeof(long long);
+    auto role = [&](int r, int depth) {
+      int* m = stage_meta(e);
+      const bool attn = r == kCore || (r == kPre && pre_attn) || (r == kPost && post_attn);
+      for (int j = 0; j < B; ++j) {
+        Request& R = e.reqs[reqs[act[j]]];
+        c[j] = attn ? R.tl.get_or_create_cursor(r, depth, 0, -1) : nullptr;
+        slot[j] = fill_lane(e, R.tl, m, j, tok[j], pos[j], c[j], r == kPre ? -1 : R.state_base,
+                            r == kPost ? -1 : R.state_base);
+        if (r == kPost) set_final_readout(e, m, j, R, (int)(++R.draw_cycle), 0);
+      }
+      run_role(e, r, B, m, true);
+      for (int j = 0; j < B; ++j)
+        if (c[j]) advance(c[j], slot[j], true);
+    };
+    role(kPre, 0);
+    for (int s = 0; s < e.S; ++s) role(kCore, s);
+    role(kPost, e.S - 1);
+    long long* src = e.sampling ? e.dec_dev : e.amax_dev;
+    const int stride = e.sampling ? 5 : 1;
+    CK(cudaMemcpyAsync(e.dec_host, src, sizeof(long long) * stride * B, cudaMemcpyDeviceToHost, e.stream));
+    e.d2h_bytes += sizeof(long long) * stride * B;
     fetch_device_error(e);
     CK(cudaStreamSynchronize(e.stream));
     e.staging_next = 0;
     check_fetched_error(e);
-    committed.push_back(e.amax_host[0]);
-    index++;
-    if (stop(committed)) break;
+    for (int j = 0; j < B; ++j) {
+      const int i = act[j];
+      committed[i].push_back(e.dec_host[j * stride]);
+      if (stop[i](committed[i]) || (int)committed[i].size() >= max_new) done[i] = 1;
+    }
   }
-  e.tl.retain({});
-  return committed;
+  for (int i = 0; i < n; ++i) e.reqs[reqs[i]].tl.retain({});
 }
 
-SchedHooks engine_hooks(ls_engine& e, StopRule stop) {
+SchedHooks engine_hooks(ls_engine& e, int req, StopRule stop) {
   SchedHooks hk;
   hk.S = e.S;
   hk.K = e.K;
@@ -1804,10 +1909,11 @@ SchedHooks engine_hooks(ls_engine& e, StopRule stop) {
   hk.max_rows = e.max_rows;
   hk.endpoint_kind = e.endpoint_kind;
   hk.sampling = e.sampling;
-  hk.forward = [&e](const std::vector<CycleLane>& cl, std::vector<Dec>& dec) {
-    cycle(e, cl, dec, nullptr);
+  hk.retain = [&e, req](const std::vector<PLane>& lanes, int) {
+    std::vector<std::pair<int, int>> bp;
+    for (auto& l : lanes) bp.emplace_back(l.branch, l.parent);
+    e.reqs[req].tl.retain(bp);
   };
-  hk.retain = [&e](const std::vector<PLane>& lanes, int) { retain_timelines(e, lanes); };
   hk.should_stop = std::move(stop);
   return hk;
 }
@@ -2195,7 +2301,9 @@ int ls_set_sampling(ls_engine* e, float temperature, int top_k, float top_p, uin
 int ls_prefill(ls_engine* e, const int64_t* prompt, int n, float* out_logits, int64_t* first) {
   if (!e || !prompt || !first) return LS_EINVAL;
   try {
-    *first = prefill(*e, prompt, n, out_logits);
+    REQUIRE(e->finalized, LS_EINVAL, "engine not finalized");
+    e->reqs[0].seed = e->sparams.seed;
+    *first = prefill(*e, e->reqs[0], prompt, n, out_logits);
   } catch (const std::exception& ex) {
     return fail(e, ex);
   }
@@ -2205,12 +2313,14 @@ int ls_prefill(ls_engine* e, const int64_t* prompt, int n, float* out_logits, in
 int ls_cycle(ls_engine* e, const int64_t* lanes, int n, int64_t* out_dec, float* out_logits) {
   if (!e || !lanes || !out_dec || n < 1) return LS_EINVAL;
   try {
+    REQUIRE(e->finalized, LS_EINVAL, "engine not finalized");
     CK(cudaSetDevice(e->device));
     std::vector<CycleLane> cl(n);
     for (int i = 0; i < n; ++i) {
       const int64_t* l = lanes + 8 * i;
-      cl[i] = {(int)l[0], (int)l[1], (int)l[2], (int)l[3], (int)l[4], (int)l[5], -1, (int)l[6],
-               (int)l[7]};
+      cl[i] = CycleLane{(int)l[0], (int)l[1], (int)l[2], (int)l[3], (int)l[4], (int)l[5]};
+      cl[i].first = (int)l[6];
+      cl[i].second = (int)l[7];
     }
     std::vector<Dec> dec;
     cycle(*e, cl, dec, out_logits);
@@ -2225,9 +2335,10 @@ int ls_cycle(ls_engine* e, const int64_t* lanes, int n, int64_t* out_dec, float*
 int ls_retain(ls_engine* e, const int64_t* branch_ids, const int64_t* parent_ids, int n) {
   if (!e || n < 0 || (n > 0 && (!branch_ids || !parent_ids))) return LS_EINVAL;
   try {
+    REQUIRE(e->finalized, LS_EINVAL, "engine not finalized");
     std::vector<std::pair<int, int>> bp;
     for (int i = 0; i < n; ++i) bp.emplace_back((int)branch_ids[i], (int)parent_ids[i]);
-    e->tl.retain(bp);
+    e->reqs[0].tl.retain(bp);
   } catch (const std::exception& ex) {
     return fail(e, ex);
   }
@@ -2235,47 +2346,96 @@ int ls_retain(ls_engine* e, const int64_t* branch_ids, const int64_t* parent_ids
 }
 
 namespace {
-int generate_request(ls_engine* e, const int64_t* prompt, int n_prompt, int max_new, int mode,
-                     const StopRule& stop, int64_t* out_ids, int* n_out, ls_stats* stats) {
-  if (!e || !prompt || !out_ids || !n_out || max_new < 1 || (mode != 0 && mode != 1)) return LS_EINVAL;
+// Prefill each request in turn, then decode all of them together (LoopSpec:
+// one pipeline per request, each cycle over every running request's lanes;
+// AR: one lane per running request per step). per_request[i] receives
+// request i's scheduler counters and tokens; total (optional) the sums plus
+// the batch's work counters, copy volumes and decode timing.
+int generate_batch(ls_engine* e, const int64_t* prompts, const int32_t* lens, int n_req, int max_new,
+                   int mode, const std::vector<StopRule>& stop, const uint64_t* seeds,
+                   int64_t* out_ids, int32_t* n_out, ls_stats* per_request, ls_stats* total) {
+  if (!e || !prompts || !lens || !out_ids || !n_out || n_req < 1 || max_new < 1 ||
+      (mode != 0 && mode != 1) || (int)stop.size() != n_req)
+    return LS_EINVAL;
   try {
-    ls_stats st{};
+    REQUIRE(e->finalized, LS_EINVAL, "engine not finalized");
+    REQUIRE(n_req <= e->max_req, LS_ECAPACITY,
+            "more requests than the engine's max_requests (" + std::to_string(e->max_req) + ")");
     e->h2d_bytes = e->d2h_bytes = 0;
-    const long long first = prefill(*e, prompt, n_prompt, nullptr);
-    float pms = 0.f;
-    CK(cudaEventElapsedTime(&pms, e->ev0, e->ev1));
-    st.prefill_device_ms = pms;
-    REQUIRE(e->prefill_len + max_new < e->max_ctx, LS_ECAPACITY, "prompt + max_new_tokens exceeds max_context");
+    ls_stats tot{};
+    std::vector<long long> first(n_req);
+    long off = 0;
+    for (int i = 0; i < n_req; ++i) {
+      Request& R = e->reqs[i];
+      R.seed = seeds ? seeds[i] : e->sparams.seed + (unsigned long long)i;
+      first[i] = prefill(*e, R, prompts + off, lens[i], nullptr);
+      off += lens[i];
+      float pms = 0.f;
+      CK(cudaEventElapsedTime(&pms, e->ev0, e->ev1));
+      tot.prefill_device_ms += pms;
+      REQUIRE(R.prefill_len + max_new < e->max_ctx, LS_ECAPACITY,
+              "prompt + max_new_tokens exceeds max_context");
+    }
     double t0 = -1.0;
     const int64_t launches0 = e->kernel_launches;
     const int64_t pre0 = e->pre_calls, core0 = e->core_calls, kv0 = e->core_kv_positions,
                   post0 = e->post_calls;
     CK(cudaEventRecord(e->ev0, e->stream));
-    std::vector<long long> ids;
+    std::vector<std::vector<long long>> ids(n_req);
+    std::vector<ls_stats> st(n_req, ls_stats{});
     if (mode == 0) {
-      SchedHooks hk = engine_hooks(*e, stop);
-      ids = run_loopspec(hk, first, max_new, st, t0);
+      std::vector<SchedHooks> hooks;
+      hooks.reserve(n_req);
+      for (int i = 0; i < n_req; ++i) hooks.push_back(engine_hooks(*e, i, stop[i]));
+      std::vector<std::unique_ptr<PipelineRun>> runs;
+      for (int i = 0; i < n_req; ++i)
+        runs.emplace_back(new PipelineRun(hooks[i], i, e->reqs[i].state_base, first[i], max_new, &t0));
+      drive(runs, [e](const std::vector<CycleLane>& cl, std::vector<Dec>& dec) { cycle(*e, cl, dec, nullptr); });
+      for (int i = 0; i < n_req; ++i) {
+        ids[i] = runs[i]->committed;
+        st[i] = runs[i]->st;
+      }
     } else {
-      ids = run_ar(*e, first, max_new, stop, t0);
+      std::vector<int> reqs(n_req);
+      for (int i = 0; i < n_req; ++i) {
+        reqs[i] = i;
+        ids[i] = {first[i]};
+      }
+      run_ar(*e, ids, reqs, stop, max_new, t0);
     }
     CK(cudaEventRecord(e->ev1, e->stream));
     CK(cudaEventSynchronize(e->ev1));
     const double t1 = now_s();
     float dms = 0.f;
     CK(cudaEventElapsedTime(&dms, e->ev0, e->ev1));
-    st.decode_device_ms = dms;
-    st.decode_host_s = t0 >= 0 ? t1 - t0 : 0.0;
-    st.decode_tokens = std::max<int64_t>((int64_t)ids.size() - 1, 0);
-    for (size_t i = 0; i < ids.size(); ++i) out_ids[i] = ids[i];
-    *n_out = (int)ids.size();
-    st.h2d_bytes = e->h2d_bytes;
-    st.d2h_bytes = e->d2h_bytes;
-    st.decode_kernel_launches = e->kernel_launches - launches0;
-    st.pre_calls = e->pre_calls - pre0;
-    st.core_calls = e->core_calls - core0;
-    st.core_kv_positions = e->core_kv_positions - kv0;
-    st.post_calls = e->post_calls - post0;
-    if (stats) *stats = st;
+    for (int i = 0; i < n_req; ++i) {
+      st[i].decode_tokens = std::max<int64_t>((int64_t)ids[i].size() - 1, 0);
+      st[i].decode_device_ms = dms;
+      st[i].decode_host_s = t0 >= 0 ? t1 - t0 : 0.0;
+      for (size_t k = 0; k < ids[i].size(); ++k) out_ids[(long)i * max_new + k] = ids[i][k];
+      n_out[i] = (int32_t)ids[i].size();
+      if (per_request) per_request[i] = st[i];
+      tot.pipeline_cycles += st[i].pipeline_cycles;
+      tot.pre_rows += st[i].pre_rows;
+      tot.recurrent_rows += st[i].recurrent_rows;
+      tot.post_rows += st[i].post_rows;
+      tot.verified_proposals += st[i].verified_proposals;
+      tot.first_rejections += st[i].first_rejections;
+      tot.second_verifications += st[i].second_verifications;
+      tot.second_acceptances += st[i].second_acceptances;
+      tot.second_rejections += st[i].second_rejections;
+      tot.decode_tokens += st[i].decode_tokens;
+    }
+    tot.decode_device_ms = dms;
+    tot.decode_host_s = t0 >= 0 ? t1 - t0 : 0.0;
+    tot.h2d_bytes = e->h2d_bytes;
+    tot.d2h_bytes = e->d2h_bytes;
+    tot.decode_kernel_launches = e->kernel_launches - launches0;
+    tot.pre_calls = e->pre_calls - pre0;
+    tot.core_calls = e->core_calls - core0;
+    tot.core_kv_positions = e->core_kv_positions - kv0;
+    tot.post_calls = e->post_calls - post0;
+    if (total) *total = tot;
   } catch (const std::exception& ex) {
     return fail(e, ex);
   }
@@ -2285,16 +2445,36 @@ int generate_request(ls_engine* e, const int64_t* prompt, int n_prompt, int max_
 
 int ls_generate(ls_engine* e, const int64_t* prompt, int n_prompt, int max_new, int mode,
                 int64_t stop_token, int64_t* out_ids, int* n_out, ls_stats* stats) {
-  return generate_request(e, prompt, n_prompt, max_new, mode, stop_rule(stop_token, nullptr, nullptr),
-                          out_ids, n_out, stats);
+  if (!e || !n_out) return LS_EINVAL;
+  const int32_t len = n_prompt;
+  const uint64_t seed = e->sparams.seed;
+  int32_t n = 0;
+  const int rc = generate_batch(e, prompt, &len, 1, max_new, mode, {stop_rule(stop_token, nullptr, nullptr)},
+                                &seed, out_ids, &n, nullptr, stats);
+  *n_out = n;
+  return rc;
 }
 
 int ls_generate_stream(ls_engine* e, const int64_t* prompt, int n_prompt, int max_new, int mode,
                        int64_t stop_token, ls_commit_fn on_commit, void* user, int64_t* out_ids,
                        int* n_out, ls_stats* stats) {
-  if (!on_commit) return LS_EINVAL;
-  return generate_request(e, prompt, n_prompt, max_new, mode, stop_rule(stop_token, on_commit, user),
-                          out_ids, n_out, stats);
+  if (!e || !on_commit || !n_out) return LS_EINVAL;
+  const int32_t len = n_prompt;
+  const uint64_t seed = e->sparams.seed;
+  int32_t n = 0;
+  const int rc = generate_batch(e, prompt, &len, 1, max_new, mode, {stop_rule(stop_token, on_commit, user)},
+                                &seed, out_ids, &n, nullptr, stats);
+  *n_out = n;
+  return rc;
+}
+
+int ls_generate_batch(ls_engine* e, const int64_t* prompts, const int32_t* prompt_lens, int n_requests,
+                      int max_new_tokens, int mode, int64_t stop_token, const uint64_t* seeds,
+                      int64_t* out_ids, int32_t* n_out, ls_stats* per_request, ls_stats* total) {
+  if (!e || n_requests < 1) return LS_EINVAL;
+  std::vector<StopRule> stops(n_requests, stop_rule(stop_token, nullptr, nullptr));
+  return generate_batch(e, prompts, prompt_lens, n_requests, max_new_tokens, mode, stops, seeds, out_ids,
+                        n_out, per_request, total);
 }
 
 int ls_pipeline_simulate(int stages, int step_size, int second_step, int64_t first_token,
@@ -2322,7 +2502,7 @@ int ls_pipeline_simulate(int stages, int step_size, int second_step, int64_t fir
       for (int t = X; t < depth; ++t) b.push_back(b[t - 1] + b[t - X]);
     }
     for (long v : b) hk.max_rows += (int)v;
-    hk.forward = [&](const std::vector<CycleLane>& cl, std::vector<Dec>& dec) {
+    Forward forward = [&](const std::vector<CycleLane>& cl, std::vector<Dec>& dec) {
       std::vector<int64_t> rows;
       for (auto& l : cl) {
         const int64_t r[7] = {l.stage, l.index, l.token, l.branch, l.parent, l.origin, l.state};
@@ -2346,9 +2526,12 @@ int ls_pipeline_simulate(int stages, int step_size, int second_step, int64_t fir
     hk.should_stop = [stop_token](const std::vector<long long>& ids) {
       return stop_token >= 0 && ids.back() == stop_token;
     };
-    ls_stats st{};
     double t0 = -1.0;
-    std::vector<long long> ids = run_loopspec(hk, first_token, max_new_tokens, st, t0);
+    std::vector<std::unique_ptr<PipelineRun>> runs;
+    runs.emplace_back(new PipelineRun(hk, 0, 0, first_token, max_new_tokens, &t0));
+    drive(runs, forward);
+    ls_stats st = runs[0]->st;
+    const std::vector<long long>& ids = runs[0]->committed;
     st.decode_tokens = std::max<int64_t>((int64_t)ids.size() - 1, 0);
     for (size_t i = 0; i < ids.size(); ++i) out_ids[i] = ids[i];
     *n_out = (int)ids.size();
@@ -2388,9 +2571,10 @@ int ls_role_kernel_count(ls_engine* e, int role, int n, int* count) {
 int ls_time_role(ls_engine* e, int role, int n, int context_len, int iters, double* avg_ms) {
   if (!e || !avg_ms || role < 0 || role > 2 || n < 1 || iters < 1) return LS_EINVAL;
   try {
-    REQUIRE(e->prefill_len >= 0, LS_EINVAL, "ls_time_role needs a prefilled request");
-    REQUIRE(n <= e->max_rows, LS_ECAPACITY, "too many lanes");
-    const int P = e->prefill_len + 1;
+    Request& R = e->reqs.at(0);
+    REQUIRE(R.prefill_len >= 0, LS_EINVAL, "ls_time_role needs a prefilled request");
+    REQUIRE(n <= e->max_state, LS_ECAPACITY, "too many lanes");
+    const int P = R.prefill_len + 1;
     REQUIRE(context_len >= 1 && context_len <= P, LS_EINVAL, "context_len must not exceed the prompt");
     // Synthetic lanes, as decode lanes at different depths: lane b gets a
     // fresh row forking the request's timeline of depth b mod S (core; pre
@@ -2406,12 +2590,12 @@ int ls_time_role(ls_engine* e, int role, int n, int context_len, int iters, doub
       Cursor c;
       if (attn) {
         const int depth = role == kPost ? e->S - 1 : role == kCore ? b % e->S : 0;
-        Cursor* root = e->tl.get_or_create_cursor(role, depth, 0, -1);
-        c.row = e->tl.alloc_row();
+        Cursor* root = R.tl.get_or_create_cursor(role, depth, 0, -1);
+        c.row = R.tl.alloc_row();
         c.seq_len = context_len - 1;
         c.pending_parent_row = root->row;
       }
-      fill_lane(*e, m, b, 1, context_len - 1, attn ? &c : nullptr, b, b);
+      fill_lane(*e, R.tl, m, b, 1, context_len - 1, attn ? &c : nullptr, b, b);
     }
     run_role(*e, role, n, m, true);  // forks the rows
     int* m2 = stage_meta(*e);

@@ -19,7 +19,8 @@
 // and writes the decision row (token, proposed, accepted_code, q1_rejected,
 // q2_rejected) of policy.py:197-283. Draws invert a CDF in chunks of 2048
 // tokens like the reference. Uniforms: words of Philox4x32-10 with counter
-// (cycle, row, 0, 0) and the request's seed as key, u = (w >> 8) * 2^-24.
+// (cycle, readout row of the request, 0, 0) and the request's seed as key,
+// u = (w >> 8) * 2^-24 (cycle, row and seed come with the row's metadata).
 #pragma once
 
 #include "common.cuh"
@@ -320,7 +321,12 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(SampleArgs a) {
   }
   __syncthreads();
 
-  const uint4 w4 = philox_words(prm.seed, cycle, (uint32_t)row);
+  // the request's stream: its seed, cycle counter and readout row
+  const unsigned long long seed =
+      (unsigned long long)(uint32_t)a.meta.get(kMetaSeedLo, a.meta_row0 + row) |
+      ((unsigned long long)(uint32_t)a.meta.get(kMetaSeedHi, a.meta_row0 + row) << 32);
+  const uint32_t draw_row = (uint32_t)a.meta.get(kMetaDrawRow, a.meta_row0 + row);
+  const uint4 w4 = philox_words(seed, cycle, draw_row);
   const float u0 = (float)(w4.x >> 8) * (1.f / 16777216.f);
   const float u1 = (float)(w4.y >> 8) * (1.f / 16777216.f);
   const float u2 = (float)(w4.z >> 8) * (1.f / 16777216.f);

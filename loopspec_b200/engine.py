@@ -26,12 +26,13 @@ def _f32p(a):
 
 
 class Engine:
-    """One looped model on one GPU, one request at a time."""
+    """One looped model on one GPU: one request at a time (`generate`), or up
+    to `max_requests` together (`generate_batch`)."""
 
     def __init__(self, cfg: ModelConfig, schedule: PipelineSchedule, weights: dict, *,
                  device: int = 0, max_context: int = 4096, max_prompt: int | None = None,
                  kv_slots: int = 0, request_rows: int = 0, use_graphs: bool = True,
-                 use_pdl: bool = True):
+                 use_pdl: bool = True, max_requests: int = 1):
         if schedule.stages != cfg.stages:
             raise ValueError("schedule stages must equal the model's recurrence count")
         self.cfg = cfg
@@ -50,7 +51,7 @@ class Engine:
             step_size=schedule.step_size, second_step=schedule.second_step or 0,
             max_context=max_context, max_prompt=max_prompt or max_context // 2,
             kv_slots=kv_slots, request_rows=request_rows, use_graphs=int(use_graphs),
-            use_pdl=int(use_pdl))
+            use_pdl=int(use_pdl), max_requests=int(max_requests))
         handle = ctypes.c_void_p()
         code = self.L.ls_create(ctypes.byref(mc), ctypes.byref(sc), device, ctypes.byref(handle))
         if code != _lib.LS_OK:
@@ -153,6 +154,32 @@ class Engine:
         _lib.check(code, self.h)
         self.prefill_len = None
         return out[: n.value].tolist(), st.as_dict()
+
+    def generate_batch(self, prompts, max_new_tokens, *, mode="loopspec", stop_token=None, seeds=None):
+        """Several requests decoded together (ls_generate_batch): every cycle
+        runs over the lanes of all running requests. Returns (list of ids per
+        request, list of per-request stats, batch stats). Request i commits
+        what it commits alone with seed seeds[i]."""
+        lens = np.ascontiguousarray([len(p) for p in prompts], dtype=np.int32)
+        flat = np.ascontiguousarray([t for p in prompts for t in p], dtype=np.int64)
+        n = len(prompts)
+        out = np.zeros((n, max_new_tokens), dtype=np.int64)
+        n_out = np.zeros(n, dtype=np.int32)
+        per = (_lib.Stats * n)()
+        total = _lib.Stats()
+        sd = None
+        if seeds is not None:
+            sd = np.ascontiguousarray([int(x) & 0xFFFFFFFFFFFFFFFF for x in seeds], dtype=np.uint64)
+        m = 0 if mode == "loopspec" else 1
+        stop = -1 if stop_token is None else int(stop_token)
+        code = self.L.ls_generate_batch(
+            self.h, _i64p(flat), lens.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), n, max_new_tokens, m,
+            stop, None if sd is None else sd.ctypes.data_as(ctypes.POINTER(ctypes.c_uint64)), _i64p(out),
+            n_out.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), per, ctypes.byref(total))
+        _lib.check(code, self.h)
+        self.prefill_len = None
+        ids = [out[i, : n_out[i]].tolist() for i in range(n)]
+        return ids, [per[i].as_dict() for i in range(n)], total.as_dict()
 
     def time_role(self, role, n_lanes, context_len, iters=20):
         ms = ctypes.c_double()

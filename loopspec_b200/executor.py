@@ -13,6 +13,9 @@
   runs the whole request inside the engine (`ls_generate`): prefill, first
   token and the native scheduler loop, with no Python per cycle.
 * `generate_autoregressive` is the unrolled baseline (serving.py:216-239).
+* `generate_loopspec_batch` serves several requests together
+  (`ls_generate_batch`); each commits what it commits alone. The reference
+  serves LoopSpec one request at a time (server/cli.py:88-89).
 """
 
 from __future__ import annotations
@@ -189,3 +192,18 @@ def generate_autoregressive(runner: Engine, prompt_ids: Sequence[int], max_new_t
     """Plain decoding: every token runs pre, all S core iterations, post."""
     apply_sampling(runner, sampling, generator, seed)
     return runner.generate(list(prompt_ids), max_new_tokens, mode="ar", stop_token=stop_token)
+
+
+def generate_loopspec_batch(runner: Engine, prompts: Sequence[Sequence[int]], max_new_tokens: int, *,
+                            sampling=None, seeds=None, stop_token=None, mode="loopspec"):
+    """Generate for several prompts together; returns (ids per request,
+    stats per request, batch stats). `sampling` applies to every request;
+    request i draws from seeds[i] (default: 0, 1, 2, ...), so it commits
+    what generate_loopspec(..., seed=seeds[i]) commits for it alone."""
+    if max_new_tokens <= 0:
+        raise ValueError("a committed first token requires a positive budget")
+    if seeds is None:
+        seeds = list(range(len(prompts)))
+    apply_sampling(runner, sampling, None, seeds[0] if seeds else 0)
+    return runner.generate_batch([list(p) for p in prompts], max_new_tokens, mode=mode,
+                                 stop_token=stop_token, seeds=seeds)
