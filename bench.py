@@ -61,6 +61,11 @@ def parse():
     p.add_argument("--top-p", type=float, default=1.0)
     p.add_argument("--top-k", type=int, default=0)
     p.add_argument("--seed", type=int, default=1234, help="sampling seed of request i is seed + i")
+    p.add_argument("--batch", type=int, default=0,
+                   help="> 0: serve this many requests together per step (ls_generate_batch), split "
+                        "over the ranks; prompt lengths uniform in [--prompt-min, --prompt]")
+    p.add_argument("--prompt-min", type=int, default=0,
+                   help="shortest prompt of a --batch step (0: every prompt has --prompt tokens)")
     p.add_argument("--tp", action="store_true",
                    help="under torchrun: one request split over the ranks by tensor parallelism "
                         "(heads and MLP columns; strong scaling) instead of one replica per GPU")
@@ -426,6 +431,126 @@ def engine_arm(args):
         dist.destroy_process_group()
 
 
+def batch_arm(args):
+    """--batch B: B requests per step, split over the ranks (request i on rank
+    i % N); each rank serves its share together (generate_loopspec_batch),
+    with the autoregressive batch of the same prompts timed beside it."""
+    from loopspec_b200.engine import Engine
+    from loopspec_b200.executor import generate_loopspec_batch
+    from loopspec_b200.weights import init_random_weights
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+
+    def reduce(x, op):
+        if dist is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=op)
+        return float(t.item())
+
+    cfg = get_config(args.config)
+    sch = schedule_for(cfg, args)
+    mine = list(range(rank, args.batch, world))
+    lo = args.prompt_min or args.prompt
+
+    def batch_of(step):
+        g = torch.Generator().manual_seed(5000 + step)
+        lens = torch.randint(lo, args.prompt + 1, (args.batch,), generator=g).tolist()
+        return [make_prompt(cfg, lens[i], 100000 * step + i) for i in mine], [lens[i] for i in mine]
+
+    weights = init_random_weights(cfg, 0, device=f"cuda:{local}", dtype=torch.bfloat16)
+    eng = Engine(cfg, sch, weights, device=local, max_context=args.prompt + args.new_tokens + 64,
+                 max_prompt=args.prompt, max_requests=max(1, len(mine)))
+    samp = sampling_of(args)
+
+    def run(step, mode):
+        prompts, _ = batch_of(step)
+        seeds = [args.seed + 1000 * step + i for i in mine]
+        t0 = time.perf_counter()
+        ids, per, tot = generate_loopspec_batch(eng, prompts, args.new_tokens, sampling=samp, seeds=seeds,
+                                                mode=mode)
+        return ids, tot, time.perf_counter() - t0, prompts
+
+    for i in range(args.warmup):
+        run(i, "loopspec")
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks = Clocks(local)
+    clocks.start()
+    dec_tok = dec_ms = wall = 0.0
+    agg = None
+    useful = 0
+    for i in range(args.steps):
+        ids, tot, dt, prompts = run(args.warmup + i, "loopspec")
+        wall += dt
+        dec_tok += tot["decode_tokens"]
+        dec_ms += tot["decode_device_ms"]
+        useful += roofline.useful_bytes_batch(cfg, [len(x) - 1 for x in ids], [len(p) for p in prompts])
+        agg = tot if agg is None else {k: agg[k] + tot[k] for k in tot}
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ar_ids, ar_tot, _, _ = run(args.warmup, "ar")
+    ls_ids, _, _, _ = run(args.warmup, "loopspec")
+    dec_s_max = reduce(dec_ms / 1e3, dist.ReduceOp.MAX if dist else None)
+    wall_max = reduce(wall, dist.ReduceOp.MAX if dist else None)
+    tok_all = reduce(dec_tok, dist.ReduceOp.SUM if dist else None)
+    new_all = reduce(float(sum(len(x) for x in ls_ids)) * args.steps, dist.ReduceOp.SUM if dist else None)
+    ar_rate = reduce(ar_tot["decode_tokens"] / (ar_tot["decode_device_ms"] / 1e3),
+                     dist.ReduceOp.SUM if dist else None)
+    value = tok_all / dec_s_max
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+        peak_gbs, peak_src = float(peaks["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        peak_gbs, peak_src = 6650.0, "fallback"
+    decode_gbs = roofline.decode_bytes(cfg, agg) / (dec_ms / 1e3) / 1e9
+    useful_gbs = useful / (dec_ms / 1e3) / 1e9
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(1e3 * wall_max / args.steps, 1), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (uniform-random prompt ids and lengths, random-init weights seed 0)",
+            "config": {"workload": f"{cfg.name} LoopSpec first={args.first} second={args.second} "
+                                   f"{decode_mode(args)}, batch {args.batch} (split over {world} GPUs), "
+                                   f"prompts {lo}-{args.prompt}, {args.new_tokens} new tokens",
+                       "global_batch": args.batch, "seq_len": args.prompt + args.new_tokens,
+                       "parallelism": f"requests split over {world} GPUs", "l2": l2_note(cfg)},
+            "loopspec_tok_s": round(value, 2), "ar_tok_s": round(ar_rate, 2),
+            "speedup_vs_ar": round(value / ar_rate, 3),
+            "mean_accept_len": round(accept_length(agg, sch), 4),
+            "counters": {k: int(agg[k]) for k in ("pipeline_cycles", "recurrent_rows", "post_rows",
+                                                  "verified_proposals", "first_rejections",
+                                                  "second_acceptances", "decode_tokens", "core_calls",
+                                                  "core_kv_positions", "post_calls")},
+            "decode_roofline": {"achieved": round(decode_gbs, 1), "peak": peak_gbs, "unit": "GB/s",
+                                "frac": round(decode_gbs / peak_gbs, 4), "peak_source": peak_src,
+                                "useful_frac": round(useful_gbs / peak_gbs, 4),
+                                "useful_formula": "batched AR bytes of the committed tokens (weights "
+                                                  "once per step for all requests, K/V per request)",
+                                "rank": 0},
+            "e2e": {"value": round(new_all / wall_max, 2), "unit": UNIT,
+                    "note": "new tokens / wall time of the batched calls incl. prefill"},
+            "greedy_equal_ar": (ls_ids == ar_ids) if samp is None else None,
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    eng.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -433,7 +558,10 @@ def main():
     else:
         from loopspec_b200.build import build
         build()
-        engine_arm(args)
+        if args.batch > 0:
+            batch_arm(args)
+        else:
+            engine_arm(args)
 
 
 if __name__ == "__main__":

@@ -49,3 +49,19 @@ def useful_bytes(cfg, decode_tokens, prompt_len):
     n = decode_tokens
     positions = n * prompt_len + n * (n + 1) // 2
     return n * (S * w_core + w_pre + w_post + w_lm) + S * kv_row * (positions + n)
+
+
+def useful_bytes_batch(cfg, decode_tokens, prompt_lens):
+    """Bytes batched autoregressive decoding of several requests moves: each
+    step streams the weights once for every request still running (so
+    max(decode_tokens) weight passes), and each request reads its own K/V."""
+    if not decode_tokens:
+        return 0
+    w_core, w_pre, w_post, w_lm = weight_bytes(cfg)
+    S = cfg.stages
+    kv_row = cfg.n_core_layers * cfg.kv_bytes_per_token_layer()
+    steps = max(decode_tokens)
+    kv = 0
+    for n, P in zip(decode_tokens, prompt_lens):
+        kv += S * kv_row * (n * P + n * (n + 1) // 2 + n)
+    return steps * (S * w_core + w_pre + w_post + w_lm) + kv

@@ -36,3 +36,12 @@ def test_counters_sum_over_requests():
     a, b = ar_stats(cfg, 100, 10), ar_stats(cfg, 300, 20)
     both = {k: a[k] + b[k] for k in a}
     assert roofline.decode_bytes(cfg, both) == roofline.decode_bytes(cfg, a) + roofline.decode_bytes(cfg, b)
+
+
+def test_batched_useful_bytes_stream_weights_once_per_step():
+    cfg = get_config("ouro-1.4b")
+    one = roofline.useful_bytes(cfg, 100, 500)
+    assert roofline.useful_bytes_batch(cfg, [100], [500]) == one
+    two = roofline.useful_bytes_batch(cfg, [100, 100], [500, 500])
+    kv = one - 100 * sum(roofline.weight_bytes(cfg)[i] * (cfg.stages if i == 0 else 1) for i in range(4))
+    assert two == one + kv                      # the second request adds only its K/V
