@@ -413,6 +413,10 @@ struct ls_engine {
   long part_elems = 0;
   XBuf x_h, x_attn, x_act, x_cat;
   long long *amax_dev = nullptr, *amax_host = nullptr;
+  // greedy tokens fused into the lm_head GEMM: per-lane tile maxima and the
+  // grid's arrival counter (zero between launches)
+  float* amax_val = nullptr;
+  int *amax_idx = nullptr, *amax_ticket = nullptr;
   float* logits_host = nullptr;
   int* err_dev = nullptr;
   int* err_host = nullptr;      // pinned copy of err_dev, fetched with each step's results
@@ -699,6 +703,9 @@ struct ls_engine {
     mkx(x_act, I);
     if (mc.family == LS_FAMILY_RAVEN) mkx(x_cat, 2 * H);
     amax_dev = dalloc<long long>(cap);
+    amax_val = dalloc<float>((long)cap * cdiv(V, kGemmBM));
+    amax_idx = dalloc<int>((long)cap * cdiv(V, kGemmBM));
+    amax_ticket = dalloc<int>(1);
     CK(cudaMallocHost(&amax_host, sizeof(long long) * cap));
     CK(cudaMallocHost(&logits_host, sizeof(float) * (size_t)V));
     err_dev = dalloc<int>(1);
@@ -749,7 +756,8 @@ struct ls_engine {
   LS_SMEM1(BN, ST, kEpiStore);   \
   LS_SMEM1(BN, ST, kEpiQkvRope); \
   LS_SMEM1(BN, ST, kEpiSwiGLU);  \
-  LS_SMEM1(BN, ST, kEpiSplitStore)
+  LS_SMEM1(BN, ST, kEpiSplitStore);  \
+  LS_SMEM1(BN, ST, kEpiStoreArgmax)
     LS_SMEM(16, 4);
     LS_SMEM(32, 4);
     LS_SMEM(64, 4);
@@ -785,6 +793,8 @@ void gemm(ls_engine& e, const Gemm& g, XBuf& x, const GemmEpi& epi, int kind, in
           int lane0 = 0) {
   REQUIRE(n >= 1 && 2 * (lane0 + n) <= x.rows, LS_EINVAL, "GEMM lane count out of range");
   REQUIRE(g.splits >= 1 && g.splits <= kMaxSplits, LS_EINVAL, "bad split count");
+  REQUIRE(kind != kEpiStoreArgmax || (g.splits == 1 && g.Mw <= e.V), LS_EINVAL,
+          "the fused argmax needs an unsplit GEMM of at most vocab rows");
   // prefill: the wide QKV and gate_up projections run unsplit, on N tiles of
   // at most 64 lanes so that each weight tile is shared by two CTAs
   const bool unsplit = e.prefill_mode && (kind == kEpiQkvRope || kind == kEpiSwiGLU);
@@ -823,6 +833,7 @@ void gemm(ls_engine& e, const Gemm& g, XBuf& x, const GemmEpi& epi, int kind, in
     if (kind == kEpiQkvRope) LS_GEMM_K(BN, ST, kEpiQkvRope);      \
     else if (kind == kEpiSwiGLU) LS_GEMM_K(BN, ST, kEpiSwiGLU);   \
     else if (kind == kEpiSplitStore) LS_GEMM_K(BN, ST, kEpiSplitStore); \
+    else if (kind == kEpiStoreArgmax) LS_GEMM_K(BN, ST, kEpiStoreArgmax); \
     else LS_GEMM_K(BN, ST, kEpiStore);                            \
   } while (0)
   switch (bn) {
@@ -1182,8 +1193,18 @@ void enqueue_role(ls_engine& e, int role, int n, const PostOpts& po = PostOpts()
     }
     if (po.head) {
       const int lanes = po.head_lanes < 0 ? n : po.head_lanes;
-      gemm_store(e, e.g_lm, e.x_h, e.logits, lanes, po.head_lane0);
-      head_decisions(e, meta, po.head_lane0, lanes);
+      if (e.sampling) {
+        gemm_store(e, e.g_lm, e.x_h, e.logits, lanes, po.head_lane0);
+        head_decisions(e, meta, po.head_lane0, lanes);
+      } else {
+        // greedy: the lm_head GEMM also reduces each lane's argmax
+        GemmEpi ep = store_to(e.logits);
+        ep.amax_val = e.amax_val;
+        ep.amax_idx = e.amax_idx;
+        ep.amax_ticket = e.amax_ticket;
+        ep.amax_out = e.amax_dev;
+        gemm(e, e.g_lm, e.x_h, ep, kEpiStoreArgmax, lanes, po.head_lane0);
+      }
     }
   }
 }

@@ -19,6 +19,12 @@
 // DSMEM reduction were measured slower: only 15 eight-CTA clusters fit on the
 // GPU at once, which split the GEMMs into two waves.)
 //   kEpiStore   y -> fp32 out[n][m]
+//   kEpiStoreArgmax  (lm_head, one split) kEpiStore, and each lane's
+//               (max, lowest index of the max) over the tile's rows; the last
+//               CTA of the grid to finish (acquire-release ticket) reduces the
+//               tiles' pairs into each lane's greedy token, so no separate
+//               pass re-reads the [lanes][vocab] logits (torch.argmax
+//               semantics, sglang_recurrent/loopspec/decisions.py:116)
 //   kEpiQkvRope q/k rows get neox RoPE at the lane's position; k and v go to
 //               the layer's KV pool at the lane's slot (bf16), q to fp32
 //   kEpiSwiGLU  the tile holds 64 gate rows and their 64 up rows (two TMA
@@ -39,7 +45,8 @@ constexpr int kGemmBK = 64;   // 64 bf16 = 128 bytes = one swizzle row
 constexpr int kGemmThreads = 128;
 constexpr int kMaxSplits = 32; // K splits per 128-row tile
 
-enum GemmEpiKind : int { kEpiStore = 0, kEpiQkvRope = 1, kEpiSwiGLU = 2, kEpiSplitStore = 3 };
+enum GemmEpiKind : int { kEpiStore = 0, kEpiQkvRope = 1, kEpiSwiGLU = 2, kEpiSplitStore = 3,
+                         kEpiStoreArgmax = 4 };
 
 struct GemmEpi {
   float* out;                 // store: out[n * Mw + m]
@@ -53,6 +60,10 @@ struct GemmEpi {
   int I;
   float* part_ws;             // split partial tiles [tiles][splits][BN/2][128] (splits > 1)
   int* tile_tickets;          // [tiles], zero between launches
+  float* amax_val;            // argmax: per-lane tile maxima [lanes][m_tiles]
+  int* amax_idx;              // ... and their row indices
+  int* amax_ticket;           // ... one counter, zero between launches
+  long long* amax_out;        // ... each lane's token [lanes]
   long split_stride;          // split store: floats between split planes of out
 };
 
@@ -275,7 +286,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
     const int n = n0 / 2 + l;   // lane index
-    if (EPI == kEpiStore) {
+    if (EPI == kEpiStore || EPI == kEpiStoreArgmax) {
       if (m0 + r0 < Mw) epi.out[(long)n * Mw + m0 + r0] = v0;
       if (m0 + r1 < Mw) epi.out[(long)n * Mw + m0 + r1] = v1;
     } else if (EPI == kEpiSwiGLU) {
@@ -311,6 +322,71 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         vr[i] = f2bf(v0);
         vr[i + half] = f2bf(v1);
       }
+    }
+  }
+  if (EPI == kEpiStoreArgmax) {
+    // each lane's best row of this tile: warp w takes lanes w, w + 4, ...;
+    // its 32 threads scan rows r, r + 32, r + 64, r + 96 and shuffle-reduce
+    // (larger value first, then the lower row on ties)
+    const int tiles = gridDim.x;
+    for (int l = warp; l < lanes_here; l += kGemmThreads / 32) {
+      float best = -INFINITY;
+      int bi = 0x7fffffff;
+      for (int r = lane; r < kGemmBM; r += 32) {
+        if (m0 + r >= Mw) break;
+        const float x = red[l * kGemmBM + r];
+        if (x > best || (x == best && m0 + r < bi)) {
+          best = x;
+          bi = m0 + r;
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ob > best || (ob == best && oi < bi)) {
+          best = ob;
+          bi = oi;
+        }
+      }
+      if (lane == 0) {
+        const long at = (long)(n0 / 2 + l) * tiles + blockIdx.x;
+        epi.amax_val[at] = best;
+        epi.amax_idx[at] = bi;
+      }
+    }
+    __shared__ int s_final;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const int total = gridDim.x * gridDim.z;
+      const int t = ticket_take(epi.amax_ticket);
+      s_final = t == total - 1;
+      if (s_final) *epi.amax_ticket = 0;   // every CTA has arrived: ready for the next launch
+    }
+    __syncthreads();
+    if (!s_final) return;
+    // last CTA: reduce every lane over all tiles (L2 loads: other CTAs wrote them)
+    for (int l = warp; l < n_valid; l += kGemmThreads / 32) {
+      float best = -INFINITY;
+      int bi = 0x7fffffff;
+      for (int t = lane; t < tiles; t += 32) {
+        const float x = __ldcg(epi.amax_val + (long)l * tiles + t);
+        const int xi = __ldcg(epi.amax_idx + (long)l * tiles + t);
+        if (x > best || (x == best && xi < bi)) {
+          best = x;
+          bi = xi;
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ob > best || (ob == best && oi < bi)) {
+          best = ob;
+          bi = oi;
+        }
+      }
+      if (lane == 0) epi.amax_out[l] = bi == 0x7fffffff ? 0 : bi;
     }
   }
 }

@@ -39,10 +39,12 @@ def rms_norm(x, w, eps):
 
 
 def rope_neox(x, pos, theta):
-    """x: [heads, d]; rotate the two halves (neox style)."""
+    """x: [heads, d]; rotate the two halves (neox style). The angles are
+    computed in x's precision when it is above fp32."""
     d = x.shape[-1]
     half = d // 2
-    inv_freq = 1.0 / (theta ** (torch.arange(0, d, 2, dtype=torch.float32) / d))
+    ft = torch.float64 if x.dtype == torch.float64 else torch.float32
+    inv_freq = 1.0 / (theta ** (torch.arange(0, d, 2, dtype=ft) / d))
     ang = float(pos) * inv_freq
     cos, sin = torch.cos(ang), torch.sin(ang)
     x1, x2 = x[..., :half], x[..., half:]
@@ -111,12 +113,14 @@ class Timeline:
 class OracleModel:
     """Role forward math for one lane. `cfg` is a plain dict of config fields."""
 
-    def __init__(self, cfg, weights, *, kv_bf16=False):
+    def __init__(self, cfg, weights, *, kv_bf16=False, dtype=torch.float32):
         """kv_bf16: store K/V in bf16 like the reference's KV pool (SGLang keeps
-        the cache in the model dtype); all arithmetic stays fp32."""
+        the cache in the model dtype). dtype: the arithmetic precision (fp32;
+        float64 measures how far two correct restatements drift apart)."""
         self.kv_bf16 = kv_bf16
         self.cfg = cfg
-        self.w = {k: v.detach().to(torch.float32).cpu() for k, v in weights.items()}
+        self.dtype = dtype
+        self.w = {k: v.detach().to(dtype).cpu() for k, v in weights.items()}
         self.family = cfg["family"]
         self.layout = cfg["layout"]
         self.H = cfg["hidden"]
@@ -142,8 +146,8 @@ class OracleModel:
         v = v.view(nkv, hd)
         if self.kv_bf16:
             # the reference's KV pool stores K (after RoPE) and V in the model dtype
-            k = k.to(torch.bfloat16).to(torch.float32)
-            v = v.to(torch.bfloat16).to(torch.float32)
+            k = k.to(torch.bfloat16).to(self.dtype)
+            v = v.to(torch.bfloat16).to(self.dtype)
         if len(tl.k[layer]) != pos:
             raise RuntimeError(f"timeline length {len(tl.k[layer])} != position {pos}")
         tl.k[layer].append(k)
@@ -190,7 +194,7 @@ class OracleModel:
         if self.family == "ouro":
             return h, None
         hid = raven_initial_hidden(cfg["init_seed"], pos, self.H, cfg["init_std"], cfg["embed_scale"])
-        return hid, h
+        return hid.to(self.dtype), h
 
     def core(self, h, injected, pos, tl):
         cfg = self.cfg
