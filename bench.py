@@ -220,6 +220,63 @@ def reference_arm(args):
     print(json.dumps(line), flush=True)
 
 
+def tp_block(args, rank, world, local, dist):
+    """Tensor parallelism beside the replica run (N > 1): the largest Raven
+    model (Raven-OLMo, LoopSpec 2:8) split over all N ranks by heads and MLP
+    columns, one short greedy request, against the same request on one GPU
+    (rank 0). Bounded: every rank builds its shard first and all ranks agree
+    that every engine exists before any kernel runs; a failure is reported in
+    the block instead of ending the benchmark."""
+    from loopspec_b200.engine import Engine
+    from loopspec_b200.executor import generate_loopspec
+    from loopspec_b200.tp import shard_config, shard_weights
+    from loopspec_b200.weights import init_random_weights
+    cfg = get_config("raven-olmo")
+    sch = PipelineSchedule(cfg.stages, 2, 4)
+    n_prompt, n_new = 64, 64
+    prompt = make_prompt(cfg, n_prompt, 77)
+    out = {"model": cfg.name, "ranks": world, "schedule": "LoopSpec first=2 second=8 greedy",
+           "prompt": n_prompt, "new_tokens": n_new}
+    eng = None
+    ok = True
+    try:
+        w = init_random_weights(cfg, 0, device=f"cuda:{local}", dtype=torch.bfloat16)
+        eng = Engine(shard_config(cfg, world), sch, shard_weights(w, cfg, rank, world), device=local,
+                     max_context=256, max_prompt=n_prompt)
+        handle = eng.tp_init(rank, world)
+    except Exception as ex:   # noqa: BLE001 - reported, the replica line still prints
+        ok, handle, out["error"] = False, b"", repr(ex)[:300]
+    got = [None] * world
+    dist.all_gather_object(got, (ok, handle))
+    if all(g[0] for g in got):
+        try:
+            eng.tp_attach([g[1] for g in got])
+            generate_loopspec(eng, prompt, n_new)                      # warm-up / capture
+            ids, st = generate_loopspec(eng, prompt, n_new)
+            out["tp_tok_s"] = round(st["decode_tokens"] / (st["decode_device_ms"] / 1e3), 2)
+            out["tp_ids"] = ids
+        except Exception as ex:   # noqa: BLE001
+            out["error"] = repr(ex)[:300]
+    ms = torch.tensor([out.get("tp_tok_s", 0.0)], dtype=torch.float64, device="cuda")
+    dist.all_reduce(ms, op=dist.ReduceOp.MIN)                         # slowest rank
+    dist.barrier()          # no rank releases its exchange region while a peer may read it
+    if eng is not None:
+        eng.close()
+    if rank == 0 and "error" not in out:
+        out["tp_tok_s"] = round(float(ms.item()), 2)
+        w1 = init_random_weights(cfg, 0, device=f"cuda:{local}", dtype=torch.bfloat16)
+        one = Engine(cfg, sch, w1, device=local, max_context=256, max_prompt=n_prompt)
+        generate_loopspec(one, prompt, n_new)
+        ids1, st1 = generate_loopspec(one, prompt, n_new)
+        one.close()
+        out["single_gpu_tok_s"] = round(st1["decode_tokens"] / (st1["decode_device_ms"] / 1e3), 2)
+        out["tokens_equal_single_gpu"] = ids1 == out.pop("tp_ids")
+        out["speedup_vs_single_gpu"] = round(out["tp_tok_s"] / out["single_gpu_tok_s"], 3)
+    out.pop("tp_ids", None)
+    dist.barrier()
+    return out
+
+
 def engine_arm(args):
     from loopspec_b200.engine import Engine
     from loopspec_b200.executor import generate_autoregressive, generate_loopspec
@@ -358,6 +415,8 @@ def engine_arm(args):
     decode_gbs = decode_bytes / (dec_ms / 1e3) / 1e9
     useful_gbs = useful / (dec_ms / 1e3) / 1e9
 
+    tp_info = tp_block(args, rank, world, local, dist) if dist is not None and not tp else None
+
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
@@ -415,6 +474,8 @@ def engine_arm(args):
                                      "(counted per graph replay by the engine)")
         if synth is not None:
             line["synthetic_acceptance"] = synth
+        if tp_info is not None:
+            line["tensor_parallel"] = tp_info
         if decode_gbs > peak_gbs:
             # more bytes per second than the measured copy peak: the byte
             # count, not the engine, is wrong
@@ -514,6 +575,8 @@ def batch_arm(args):
         peak_gbs, peak_src = 6650.0, "fallback"
     decode_gbs = roofline.decode_bytes(cfg, agg) / (dec_ms / 1e3) / 1e9
     useful_gbs = useful / (dec_ms / 1e3) / 1e9
+    tp_info = tp_block(args, rank, world, local, dist) if dist is not None and not tp else None
+
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
