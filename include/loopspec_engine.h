@@ -209,6 +209,15 @@ int ls_pipeline_simulate(int stages, int step_size, int second_step, int64_t fir
                          ls_cycle_fn on_cycle, ls_retain_fn on_retain, void* user,
                          int64_t* out_ids, int* n_out, ls_stats* stats);
 
+/* ls_pipeline_simulate running the scheduler of the device-resident decode
+ * loop (the fixed-size state that one GPU thread runs between the role calls
+ * of a cycle; no reference counterpart beyond the loop it restates) compiled
+ * for the host: same arguments, callbacks and results. Needs no GPU. */
+int ls_device_loop_simulate(int stages, int step_size, int second_step, int64_t first_token,
+                            int max_new_tokens, int64_t stop_token, ls_decide_fn decide,
+                            ls_cycle_fn on_cycle, ls_retain_fn on_retain, void* user,
+                            int64_t* out_ids, int* n_out, ls_stats* stats);
+
 /* Time one role call of `n_lanes` synthetic lanes (role 0 pre, 1 core, 2
  * post) `iters` times with CUDA events on the engine stream, after a
  * prefill; returns the average device milliseconds per call. Used by the

@@ -1,0 +1,613 @@
+// The LoopSpec scheduler of one greedy request as fixed-size state that a
+// single GPU thread can run between the role calls of a cycle, so that whole
+// cycles run back to back without a host round trip.
+//
+// It restates, with arrays instead of maps and heaps:
+//   continue_pipelined (sglang_recurrent/loopspec/pipeline.py:254-423) with
+//     greedy resolve (loopspec/decisions.py:136-184), the executor's
+//     state-slot pool and counters (loopspec/executor.py:76-107, 239-290);
+//   the branch timeline bookkeeping (loopspec/branching/manager.py:45-482):
+//     cursors per (branch, role, depth), forks that share a parent's prefix,
+//     ownership transfer to a single surviving child and recursive release.
+// The engine's host scheduler (engine.cu, PipelineRun and Timelines) runs the
+// same steps; the host-compiled instantiation of this code is checked against
+// traces of the reference scheduler (ls_device_loop_simulate).
+//
+// KV slots are handed out in increasing order and not recycled before the
+// request ends (the request's pool is sized for that); mapping rows are
+// recycled when a cursor is released. Neither choice changes any lane's
+// numbers: a timeline reads its positions through its mapping row.
+//
+// Every function is __host__ __device__; on the GPU one thread runs it on a
+// copy of the state held in shared memory.
+#pragma once
+
+#include <stdint.h>
+
+#include "common.cuh"
+
+namespace ls {
+
+#define LS_HD __host__ __device__ __forceinline__
+
+enum DsError : int {
+  kDsOk = 0,
+  kDsNoStateSlot = 1,      // pipeline needs more recurrent state slots than configured
+  kDsNoRow = 2,            // mapping rows exhausted
+  kDsNoSlot = 3,           // KV slots exhausted
+  kDsParent = 4,           // branch with an unavailable parent / missing parent timeline
+  kDsFinal = 5,            // several lanes reached the final stage in one cycle
+  kDsOrder = 6,            // commit out of order
+  kDsTree = 7,             // speculative tree exceeded the row limit / capacity
+  kDsDrained = 8,          // pipeline drained before generation completed
+  kDsCapacity = 9,         // a fixed table of this state is full
+};
+
+struct DsLane {
+  int stage, index, token, state, branch, parent, origin, first, second;
+};
+
+template <int MAXD>
+struct DsNode {
+  int id, parent, child_count, live, used;
+  int cur[3][MAXD];   // cursor index per (role, depth), -1 if none
+};
+
+struct DsCursor {
+  int row, seq_len, pending_parent_row, used;
+};
+
+// One lane of a role call, as the host's fill_lane() describes it.
+struct DsFill {
+  int token, pos, row, slot, fork_row, fork_len, state_in, state_out;
+  int kind, first, second;   // post rows
+};
+
+template <int MAXL, int MAXB, int MAXD, int MAXN, int MAXC, int MAXR>
+struct DevSched {
+  // schedule and request
+  int S, K, X, max_rows, max_new, q1, q2, final_stage;
+  int kind_of[MAXD];          // end stage -> 0 q1, 1 q2, 2 final, -1 none
+  int has_pre, has_post;      // pre / post roles with attention layers
+  long long stop_token;
+  int prefill_len, state_base;
+  // pipeline
+  int n_lanes;
+  DsLane lanes[MAXL];
+  int n_par;
+  int par_b[MAXB], par_p[MAXB];   // ancestry: branch -> parent (-1 for the root)
+  int next_branch;
+  unsigned char state_used[MAXL];
+  int committed, done, err;
+  long long last_token;
+  int last_accepted;          // accepted stage of the last retention (-1: none)
+  long long stats[9];   // pipeline_cycles, pre_rows, recurrent_rows, post_rows, verified_proposals,
+                        // first_rejections, second_verifications, second_acceptances, second_rejections
+  // timelines
+  DsNode<MAXD> nodes[MAXN];
+  DsCursor cursors[MAXC];
+  int n_free_rows;
+  int free_rows[MAXR];
+  int next_slot, slot_limit;
+
+  // ------------------------------------------------------------ helpers
+  LS_HD void fail(int code) {
+    if (!err) err = code;
+  }
+
+  LS_HD int node_of(int id) const {
+    for (int i = 0; i < MAXN; ++i)
+      if (nodes[i].used && nodes[i].id == id) return i;
+    return -1;
+  }
+
+  LS_HD int parent_of(int b) const {
+    for (int i = 0; i < n_par; ++i)
+      if (par_b[i] == b) return par_p[i];
+    return -2;   // unknown branch
+  }
+
+  LS_HD void set_parent(int b, int p) {
+    for (int i = 0; i < n_par; ++i)
+      if (par_b[i] == b) {
+        par_p[i] = p;
+        return;
+      }
+    if (n_par >= MAXB) {
+      fail(kDsCapacity);
+      return;
+    }
+    par_b[n_par] = b;
+    par_p[n_par] = p;
+    ++n_par;
+  }
+
+  LS_HD int alloc_row() {
+    if (n_free_rows <= 0) {
+      fail(kDsNoRow);
+      return 0;
+    }
+    return free_rows[--n_free_rows];
+  }
+
+  LS_HD void free_row(int r) {
+    if (n_free_rows < MAXR) free_rows[n_free_rows++] = r;
+  }
+
+  LS_HD int alloc_slot() {
+    if (next_slot >= slot_limit) {
+      fail(kDsNoSlot);
+      return 0;
+    }
+    return next_slot++;
+  }
+
+  LS_HD int new_cursor(int row, int seq_len, int pending) {
+    for (int i = 0; i < MAXC; ++i)
+      if (!cursors[i].used) {
+        cursors[i].used = 1;
+        cursors[i].row = row;
+        cursors[i].seq_len = seq_len;
+        cursors[i].pending_parent_row = pending;
+        return i;
+      }
+    fail(kDsCapacity);
+    return 0;
+  }
+
+  LS_HD int new_node(int id, int parent) {
+    for (int i = 0; i < MAXN; ++i)
+      if (!nodes[i].used) {
+        DsNode<MAXD>& n = nodes[i];
+        n.used = 1;
+        n.id = id;
+        n.parent = parent;
+        n.child_count = 0;
+        n.live = 1;
+        for (int r = 0; r < 3; ++r)
+          for (int d = 0; d < MAXD; ++d) n.cur[r][d] = -1;
+        return i;
+      }
+    fail(kDsCapacity);
+    return 0;
+  }
+
+  // -------------------------------------- timelines (manager.py:207-482)
+  LS_HD int get_or_create_branch(int id, int parent_id) {
+    int n = node_of(id);
+    if (n >= 0) return n;
+    const int p = node_of(parent_id);
+    if (p < 0) {
+      fail(kDsParent);
+      return 0;
+    }
+    n = new_node(id, parent_id);
+    nodes[p].child_count += 1;
+    return n;
+  }
+
+  LS_HD int get_or_create_cursor(int role, int depth, int branch, int parent) {
+    const int n = get_or_create_branch(branch, parent);
+    if (nodes[n].cur[role][depth] >= 0) return nodes[n].cur[role][depth];
+    const int p = nodes[n].parent < 0 ? -1 : node_of(nodes[n].parent);
+    if (p < 0 || nodes[p].cur[role][depth] < 0) {
+      fail(kDsParent);
+      return 0;
+    }
+    const DsCursor& pc = cursors[nodes[p].cur[role][depth]];
+    const int c = new_cursor(alloc_row(), pc.seq_len, pc.row);
+    nodes[n].cur[role][depth] = c;
+    return c;
+  }
+
+  LS_HD void release_cursor(int c) {
+    free_row(cursors[c].row);
+    cursors[c].used = 0;
+  }
+
+  LS_HD void release_unused(int n) {
+    while (n >= 0 && !nodes[n].live && nodes[n].child_count == 0) {
+      for (int r = 0; r < 3; ++r)
+        for (int d = 0; d < MAXD; ++d)
+          if (nodes[n].cur[r][d] >= 0) release_cursor(nodes[n].cur[r][d]);
+      const int pid = nodes[n].parent;
+      nodes[n].used = 0;
+      if (pid < 0) break;
+      const int p = node_of(pid);
+      if (p < 0) break;
+      nodes[p].child_count -= 1;
+      n = p;
+    }
+  }
+
+  LS_HD void detach_from_unused_parent(int n) {
+    const int pid = nodes[n].parent;
+    if (pid < 0) return;
+    const int p = node_of(pid);
+    if (p < 0 || nodes[p].live || nodes[p].child_count != 1) return;
+    for (int r = 0; r < 3; ++r)
+      for (int d = 0; d < MAXD; ++d) {
+        if (nodes[p].cur[r][d] < 0) continue;
+        if (nodes[n].cur[r][d] < 0) {   // the child adopts the parent's timeline
+          nodes[n].cur[r][d] = nodes[p].cur[r][d];
+          nodes[p].cur[r][d] = -1;
+        }
+      }
+    nodes[n].parent = -1;
+    nodes[p].child_count -= 1;
+    release_unused(p);
+  }
+
+  // keep the timelines of these (branch, parent) lanes, release the rest
+  LS_HD void retain(const DsLane* keep, int nk) {
+    // branches are created in (branch, parent) order
+    int order[MAXL];
+    for (int i = 0; i < nk; ++i) order[i] = i;
+    for (int i = 1; i < nk; ++i)
+      for (int j = i; j > 0; --j) {
+        const DsLane &a = keep[order[j - 1]], &b = keep[order[j]];
+        if (a.branch > b.branch || (a.branch == b.branch && a.parent > b.parent)) {
+          const int t = order[j - 1];
+          order[j - 1] = order[j];
+          order[j] = t;
+        } else {
+          break;
+        }
+      }
+    for (int i = 0; i < nk; ++i) {
+      const DsLane& l = keep[order[i]];
+      if (l.branch && node_of(l.branch) < 0) get_or_create_branch(l.branch, l.parent);
+    }
+    // unused live nodes, released from the highest id down
+    int ids[MAXN];
+    int nu = 0;
+    for (int i = 0; i < MAXN; ++i) {
+      if (!nodes[i].used || !nodes[i].live) continue;
+      bool kept = false;
+      for (int k = 0; k < nk && !kept; ++k) kept = keep[k].branch == nodes[i].id;
+      if (!kept) ids[nu++] = i;
+    }
+    sort_by_id(ids, nu, false);
+    for (int k = 0; k < nu; ++k) {
+      const int n = ids[k];
+      if (!nodes[n].used) continue;
+      nodes[n].live = 0;
+      release_unused(n);
+    }
+    // single surviving children adopt their dead parents' timelines (ascending id)
+    int na = 0;
+    for (int i = 0; i < MAXN; ++i)
+      if (nodes[i].used) ids[na++] = i;
+    sort_by_id(ids, na, true);
+    for (int k = 0; k < na; ++k)   // no node is created here, so a freed index stays free
+      if (nodes[ids[k]].used) detach_from_unused_parent(ids[k]);
+  }
+
+  // sort node indices by their ids (insertion sort: a handful of live nodes)
+  LS_HD void sort_by_id(int* idx, int n, bool ascending) const {
+    for (int i = 1; i < n; ++i)
+      for (int j = i; j > 0; --j) {
+        const int a = nodes[idx[j - 1]].id, b = nodes[idx[j]].id;
+        if (ascending ? a > b : a < b) {
+          const int t = idx[j - 1];
+          idx[j - 1] = idx[j];
+          idx[j] = t;
+        } else {
+          break;
+        }
+      }
+  }
+
+  // ------------------------------------ pipeline (pipeline.py:254-423)
+  LS_HD int acquire_state() {
+    for (int s = 0; s < max_rows; ++s)
+      if (!state_used[s]) {
+        state_used[s] = 1;
+        return s;
+      }
+    fail(kDsNoStateSlot);
+    return 0;
+  }
+
+  LS_HD bool descends_from(int b, int anc) const {
+    while (b != -1 && b != anc) {
+      const int p = parent_of(b);
+      b = p == -2 ? -1 : p;
+    }
+    return b == anc;
+  }
+
+  // Give every lane a state slot (executor.forward); returns the lane count.
+  LS_HD int gather() {
+    for (int i = 0; i < n_lanes; ++i)
+      if (lanes[i].state < 0) lanes[i].state = acquire_state();
+    return n_lanes;
+  }
+
+  // One greedy cycle's decisions: dec[i] = argmax token of lane i's readout
+  // (ignored for lanes without a readout). Appends a committed token to
+  // `out` (indexed by the committed count) when the final lane commits.
+  LS_HD void consume(const long long* dec, long long* out) {
+    stats[0] += 1;
+    stats[2] += (long long)n_lanes * K;
+    for (int i = 0; i < n_lanes; ++i) {
+      stats[1] += lanes[i].stage == 0;
+      stats[3] += kind_of[lanes[i].stage + K - 1] >= 0;
+    }
+    DsLane following[MAXL];
+    int nf = 0;
+    DsLane children[MAXL];
+    int nc = 0;
+    int final_idx = -1;
+    long long final_pred = 0;
+    int accepted_stage = -1;
+    for (int i = 0; i < n_lanes; ++i) {
+      DsLane l = lanes[i];
+      const int end_stage = l.stage + K - 1;
+      const int kind = kind_of[end_stage];
+      const long long pred = dec[i];
+      bool proposed = false, fr = false, sr = false;
+      int acc = -1;
+      proposed = kind == 0 || (kind == 1 && (l.first < 0 || pred != l.first));
+      if (kind == 2 && l.first >= 0) {
+        fr = pred != l.first;
+        if (!fr) acc = q1;
+        else if (l.second >= 0) {
+          sr = pred != l.second;
+          if (!sr) acc = q2;
+        }
+      }
+      if (end_stage == final_stage) {
+        if (final_idx >= 0) fail(kDsFinal);
+        final_idx = i;
+        final_pred = pred;
+        accepted_stage = acc;
+        const bool sv = fr && l.second >= 0;
+        stats[4] += 1;
+        stats[5] += fr;
+        stats[6] += sv;
+        stats[7] += sv && acc == q2;
+        stats[8] += sv && sr;
+        continue;
+      }
+      l.stage = end_stage + 1;
+      if ((end_stage == q1 || end_stage == q2) && kind >= 0 && proposed) {
+        if (end_stage == q1) l.first = (int)pred;
+        else l.second = (int)pred;
+        if (l.index + 1 < max_new) {
+          if (nc >= MAXL) {
+            fail(kDsTree);
+            return;
+          }
+          DsLane c{0, l.index + 1, (int)pred, -1, next_branch, l.branch, end_stage, -1, -1};
+          children[nc++] = c;
+          set_parent(next_branch, l.branch);
+          next_branch++;
+        }
+      }
+      if (nf >= MAXL) {
+        fail(kDsTree);
+        return;
+      }
+      following[nf++] = l;
+    }
+    for (int i = 0; i < nc; ++i) {
+      if (nf >= MAXL) {
+        fail(kDsTree);
+        return;
+      }
+      following[nf++] = children[i];
+    }
+    if (final_idx >= 0) {
+      const DsLane fl = lanes[final_idx];
+      if (fl.index != committed) fail(kDsOrder);
+      out[committed++] = final_pred;
+      last_token = final_pred;
+      if ((stop_token >= 0 && final_pred == stop_token) || committed >= max_new) {
+        // the request ends: every branch is released
+        n_lanes = 0;
+        for (int s = 0; s < MAXL; ++s) state_used[s] = 0;
+        last_accepted = -1;
+        retain(lanes, 0);
+        done = 1;
+        return;
+      }
+      accepted_stage = fl.first >= 0 ? accepted_stage : -1;
+      if (fl.index + 1 < max_new) {
+        int sel = -1;
+        for (int j = 0; j < nf; ++j) {
+          const DsLane& c = following[j];
+          if (c.parent == fl.branch && c.token == final_pred && c.origin == accepted_stage &&
+              accepted_stage >= 0) {
+            sel = j;
+            break;
+          }
+        }
+        int keep;
+        if (sel < 0) {
+          if (nf >= MAXL) {
+            fail(kDsTree);
+            return;
+          }
+          DsLane c{0, fl.index + 1, (int)final_pred, -1, next_branch, fl.branch, final_stage, -1, -1};
+          set_parent(next_branch, fl.branch);
+          next_branch++;
+          following[nf++] = c;
+          keep = c.branch;
+        } else {
+          keep = following[sel].branch;
+        }
+        int nk = 0;
+        for (int j = 0; j < nf; ++j)
+          if (descends_from(following[j].branch, keep)) following[nk++] = following[j];
+        nf = nk;
+        prune_ancestry(following, nf, keep);
+      } else {
+        nf = 0;
+        accepted_stage = -1;
+      }
+    }
+    if (nf > max_rows) fail(kDsTree);
+    n_lanes = nf;
+    for (int i = 0; i < nf; ++i) lanes[i] = following[i];
+    // state-slot pool retention: free the slots of lanes that are gone
+    unsigned char keep_s[MAXL];
+    for (int s = 0; s < MAXL; ++s) keep_s[s] = 0;
+    for (int i = 0; i < nf; ++i)
+      if (lanes[i].state >= 0) keep_s[lanes[i].state] = 1;
+    for (int s = 0; s < MAXL; ++s)
+      if (!keep_s[s]) state_used[s] = 0;
+    last_accepted = accepted_stage;
+    retain(lanes, nf);
+    if (nf == 0 && committed < max_new) fail(kDsDrained);
+    if (committed >= max_new) done = 1;
+  }
+
+  // the live ancestry: the root and every ancestor of a lane up to it
+  LS_HD void prune_ancestry(const DsLane* ls, int n, int root) {
+    int live[MAXB];
+    int nl = 0;
+    live[nl++] = root;
+    for (int i = 0; i < n; ++i) {
+      int b = ls[i].branch;
+      while (b != root) {
+        const int p = parent_of(b);
+        if (b == -1 || p == -2) {
+          fail(kDsTree);
+          return;
+        }
+        bool seen = false;
+        for (int k = 0; k < nl && !seen; ++k) seen = live[k] == b;
+        if (!seen) {
+          if (nl >= MAXB) {
+            fail(kDsCapacity);
+            return;
+          }
+          live[nl++] = b;
+        }
+        b = p;
+      }
+    }
+    int nb[MAXB], np[MAXB];
+    for (int k = 0; k < nl; ++k) {
+      nb[k] = live[k];
+      np[k] = live[k] == root ? -1 : parent_of(live[k]);
+    }
+    n_par = nl;
+    for (int k = 0; k < nl; ++k) {
+      par_b[k] = nb[k];
+      par_p[k] = np[k];
+    }
+  }
+
+  // ----------------------------------------- one cycle's role metadata
+  // Fill the lanes of the cycle's role calls as the host's cycle() does:
+  // pre for stage-0 lanes, K core iterations for all lanes, post for readout
+  // lanes; cursors advance after each call. Returns counts through n_*.
+  LS_HD void plan(DsFill* pre, int& n_pre, DsFill* core /*[K][MAXL]*/, DsFill* post, int& n_post) {
+    n_pre = 0;
+    n_post = 0;
+    int cur[MAXL];
+    for (int i = 0; i < n_lanes; ++i) {
+      const DsLane& l = lanes[i];
+      if (l.stage != 0) continue;
+      DsFill& f = pre[n_pre];
+      cur[n_pre] = has_pre ? get_or_create_cursor(0, 0, l.branch, l.parent) : -1;
+      fill(f, l, cur[n_pre], -1, state_base + l.state);
+      ++n_pre;
+    }
+    for (int j = 0; j < n_pre; ++j)
+      if (cur[j] >= 0) advance(cur[j]);
+    for (int off = 0; off < K; ++off) {
+      for (int i = 0; i < n_lanes; ++i) {
+        const DsLane& l = lanes[i];
+        cur[i] = get_or_create_cursor(1, l.stage + off, l.branch, l.parent);
+        fill(core[off * MAXL + i], l, cur[i], state_base + l.state, state_base + l.state);
+      }
+      for (int i = 0; i < n_lanes; ++i) advance(cur[i]);
+    }
+    for (int i = 0; i < n_lanes; ++i) {
+      const DsLane& l = lanes[i];
+      const int end = l.stage + K - 1;
+      if (kind_of[end] < 0) continue;
+      DsFill& f = post[n_post];
+      cur[n_post] = has_post ? get_or_create_cursor(2, end, l.branch, l.parent) : -1;
+      fill(f, l, cur[n_post], state_base + l.state, -1);
+      f.kind = kind_of[end];
+      f.first = l.first;
+      f.second = l.second;
+      ++n_post;
+    }
+    for (int j = 0; j < n_post; ++j)
+      if (cur[j] >= 0) advance(cur[j]);
+  }
+
+  LS_HD void fill(DsFill& f, const DsLane& l, int c, int state_in, int state_out) {
+    f.token = l.token;
+    f.pos = prefill_len + l.index;
+    f.state_in = state_in;
+    f.state_out = state_out;
+    f.kind = -1;
+    f.first = -1;
+    f.second = -1;
+    if (c < 0) {
+      f.row = f.slot = f.fork_row = -1;
+      f.fork_len = 0;
+      return;
+    }
+    const DsCursor& cu = cursors[c];
+    f.row = cu.row;
+    f.slot = alloc_slot();
+    f.fork_row = cu.pending_parent_row;
+    f.fork_len = cu.pending_parent_row >= 0 ? cu.seq_len : 0;
+  }
+
+  LS_HD void advance(int c) {
+    cursors[c].pending_parent_row = -1;
+    cursors[c].seq_len += 1;
+  }
+};
+
+#undef LS_HD
+
+}  // namespace ls
+
+namespace ls {
+
+// Start one request's pipeline after its first token (executor.py:400-434):
+// the schedule, a live root branch 0 and one lane at stage 0 feeding `first`.
+// The root's timelines (cursors) are attached by the caller.
+template <class D>
+inline void ds_start(D& d, int S, int K, int X, int max_rows, int max_new, long long stop_token,
+                     long long first, long long* out) {
+  d.S = S;
+  d.K = K;
+  d.X = X;
+  d.max_rows = max_rows;
+  d.max_new = max_new;
+  d.q1 = K - 1;
+  d.q2 = X ? K * X - 1 : -1;
+  d.final_stage = S - 1;
+  for (int i = 0; i < (int)(sizeof(d.kind_of) / sizeof(int)); ++i) d.kind_of[i] = -1;
+  d.kind_of[K - 1] = 0;
+  if (X) d.kind_of[K * X - 1] = 1;
+  d.kind_of[S - 1] = 2;
+  d.stop_token = stop_token;
+  d.next_branch = 1;
+  d.n_par = 1;
+  d.par_b[0] = 0;
+  d.par_p[0] = -1;
+  d.new_node(0, -1);
+  d.committed = 1;
+  out[0] = first;
+  d.last_token = first;
+  d.last_accepted = -1;
+  if ((stop_token >= 0 && first == stop_token) || max_new <= 1) {
+    d.done = 1;
+    return;
+  }
+  d.n_lanes = 1;
+  d.lanes[0] = DsLane{0, 1, (int)first, -1, 0, -1, -1, -1, -1};
+}
+
+}  // namespace ls

@@ -13,6 +13,7 @@
 
 #include "../../include/loopspec_engine.h"
 #include "common.cuh"
+#include "dev_sched.cuh"
 #include "gemm_tc.cuh"
 #include "kernels.cuh"
 #include "sampler.cuh"
@@ -2496,6 +2497,84 @@ int ls_generate_batch(ls_engine* e, const int64_t* prompts, const int32_t* promp
   std::vector<StopRule> stops(n_requests, stop_rule(stop_token, nullptr, nullptr));
   return generate_batch(e, prompts, prompt_lens, n_requests, max_new_tokens, mode, stops, seeds, out_ids,
                         n_out, per_request, total);
+}
+
+namespace {
+// The device loop's scheduler state compiled for the host, with capacities for
+// every schedule (S <= 32, up to 256 live lanes).
+using HostSched = DevSched<256, 4096, 32, 2048, 16384, 32768>;
+}  // namespace
+
+int ls_device_loop_simulate(int stages, int step_size, int second_step, int64_t first_token,
+                            int max_new_tokens, int64_t stop_token, ls_decide_fn decide,
+                            ls_cycle_fn on_cycle, ls_retain_fn on_retain, void* user,
+                            int64_t* out_ids, int* n_out, ls_stats* stats) {
+  if (!decide || !out_ids || !n_out || max_new_tokens < 1) return LS_EINVAL;
+  try {
+    const int S = stages, K = step_size, X = second_step;
+    REQUIRE(S > 0 && S <= 32, LS_EINVAL, "stages S must be in 1..32");
+    REQUIRE(K >= 1 && K < S && S % K == 0, LS_EINVAL, "step_size K must be a positive divisor of S with K < S");
+    REQUIRE(X == 0 || (X > 1 && X < S / K), LS_EINVAL, "second_step X must satisfy 1 < X < S/K");
+    const int depth = S / K;
+    std::vector<long> b;
+    if (X == 0) b.assign(depth, 1);
+    else {
+      b.assign(X, 1);
+      for (int t = X; t < depth; ++t) b.push_back(b[t - 1] + b[t - X]);
+    }
+    int max_rows = 0;
+    for (long v : b) max_rows += (int)v;
+    REQUIRE(max_rows <= 256, LS_ECAPACITY, "schedule needs more than 256 lanes");
+    std::unique_ptr<HostSched> d(new HostSched());
+    std::vector<long long> out(max_new_tokens);
+    ds_start(*d, S, K, X, max_rows, max_new_tokens, stop_token, first_token, out.data());
+    d->n_free_rows = 0;
+    d->next_slot = 0;
+    d->slot_limit = 0x7fffffff;
+    auto report_retain = [&]() {
+      std::vector<int64_t> pairs;
+      for (int i = 0; i < d->n_lanes; ++i) {
+        pairs.push_back(d->lanes[i].branch);
+        pairs.push_back(d->lanes[i].parent);
+      }
+      if (on_retain) on_retain(user, pairs.data(), (int32_t)d->n_lanes, d->last_accepted);
+    };
+    if (d->done) report_retain();
+    std::vector<long long> dec;
+    while (!d->done && !d->err) {
+      const int n = d->gather();
+      std::vector<int64_t> rows;
+      dec.assign(n, -1);
+      for (int i = 0; i < n; ++i) {
+        const DsLane& l = d->lanes[i];
+        const int64_t r[7] = {l.stage, l.index, l.token, l.branch, l.parent, l.origin, l.state};
+        rows.insert(rows.end(), r, r + 7);
+        const int kind = d->kind_of[l.stage + K - 1];
+        if (kind >= 0) dec[i] = decide(user, l.index, l.token, kind);
+      }
+      if (on_cycle) on_cycle(user, rows.data(), (int32_t)n);
+      d->consume(dec.data(), out.data());
+      report_retain();
+    }
+    REQUIRE(d->err == kDsOk, LS_EPIPELINE, "device scheduler reported error " + std::to_string(d->err));
+    ls_stats st{};
+    st.pipeline_cycles = d->stats[0];
+    st.pre_rows = d->stats[1];
+    st.recurrent_rows = d->stats[2];
+    st.post_rows = d->stats[3];
+    st.verified_proposals = d->stats[4];
+    st.first_rejections = d->stats[5];
+    st.second_verifications = d->stats[6];
+    st.second_acceptances = d->stats[7];
+    st.second_rejections = d->stats[8];
+    st.decode_tokens = std::max(d->committed - 1, 0);
+    for (int i = 0; i < d->committed; ++i) out_ids[i] = out[i];
+    *n_out = d->committed;
+    if (stats) *stats = st;
+  } catch (const std::exception& ex) {
+    return fail(nullptr, ex);
+  }
+  return LS_OK;
 }
 
 int ls_pipeline_simulate(int stages, int step_size, int second_step, int64_t first_token,

@@ -18,8 +18,10 @@ KINDS = ("q1", "q2", "final")
 
 
 def simulate_pipeline(stages, step_size, second_step, first_token, max_new_tokens, decide,
-                      *, stop_token=None):
-    """decide(index, token, kind) -> int. Returns (ids, stats, trace)."""
+                      *, stop_token=None, device_logic=False):
+    """decide(index, token, kind) -> int. Returns (ids, stats, trace).
+    device_logic: run the device loop's scheduler (dev_sched.cuh, compiled for
+    the host) instead of the host scheduler."""
     L = _lib.lib()
     trace = []
     errors = []
@@ -43,7 +45,8 @@ def simulate_pipeline(stages, step_size, second_step, first_token, max_new_token
     out = np.zeros(max(max_new_tokens, 1), dtype=np.int64)
     n = ctypes.c_int32()
     st = _lib.Stats()
-    code = L.ls_pipeline_simulate(
+    fn = L.ls_device_loop_simulate if device_logic else L.ls_pipeline_simulate
+    code = fn(
         stages, step_size, second_step or 0, first_token, max_new_tokens,
         -1 if stop_token is None else stop_token, cb_d, cb_c, cb_r, None,
         out.ctypes.data_as(ctypes.POINTER(ctypes.c_int64)), ctypes.byref(n), ctypes.byref(st))

@@ -16,8 +16,11 @@ def _golden():
         return json.load(f)
 
 
+@pytest.mark.parametrize("device_logic", [False, True], ids=["host", "device-loop"])
 @pytest.mark.parametrize("idx", range(len(CASES)))
-def test_native_scheduler_matches_reference_trace(idx):
+def test_native_scheduler_matches_reference_trace(idx, device_logic):
+    """The host scheduler and the device loop's scheduler (compiled for the
+    host) both reproduce the reference scheduler's traces exactly."""
     from loopspec_b200.simulate import simulate_pipeline
     gold = _golden()[idx]
     S, K, X, q1, q2, n, seed, vocab, stop = CASES[idx]
@@ -26,7 +29,8 @@ def test_native_scheduler_matches_reference_trace(idx):
     def decide(index, token, kind):
         return hash_decision(seed, vocab, q1, q2, index, token, kind)
 
-    ids, stats, trace = simulate_pipeline(S, K, X, first, n, decide, stop_token=stop)
+    ids, stats, trace = simulate_pipeline(S, K, X, first, n, decide, stop_token=stop,
+                                          device_logic=device_logic)
     assert ids == gold["committed"]
     for name in METRICS:
         assert stats[name] == gold["metrics"][name], name
