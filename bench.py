@@ -439,7 +439,7 @@ def engine_arm(args):
                                                   "first_rejections", "second_verifications",
                                                   "second_acceptances", "second_rejections",
                                                   "decode_tokens", "pre_calls", "core_calls",
-                                                  "core_kv_positions", "post_calls")},
+                                                  "core_kv_positions", "post_calls", "host_syncs")},
             "decode_device_s": round(dec_ms / 1e3, 4),
             "roofline": {"bound": "hbm", "kernel": "gemm_tc_kernel (core weight sweep)",
                          "achieved": round(achieved, 1), "peak": peak_gbs, "unit": "GB/s",

@@ -40,7 +40,7 @@ class SchedCfg(ctypes.Structure):
         ("step_size", _i32), ("second_step", _i32),
         ("max_context", _i32), ("max_prompt", _i32),
         ("kv_slots", _i32), ("request_rows", _i32),
-        ("use_graphs", _i32), ("use_pdl", _i32), ("max_requests", _i32),
+        ("use_graphs", _i32), ("use_pdl", _i32), ("max_requests", _i32), ("device_loop", _i32),
     ]
 
 
@@ -52,7 +52,7 @@ class Stats(ctypes.Structure):
         ("second_rejections", _i64), ("decode_tokens", _i64),
         ("decode_device_ms", _f64), ("decode_host_s", _f64), ("prefill_device_ms", _f64),
         ("h2d_bytes", _i64), ("d2h_bytes", _i64), ("decode_kernel_launches", _i64),
-        ("pre_calls", _i64), ("core_calls", _i64), ("core_kv_positions", _i64), ("post_calls", _i64),
+        ("pre_calls", _i64), ("core_calls", _i64), ("core_kv_positions", _i64), ("post_calls", _i64), ("host_syncs", _i64),
     ]
 
     def as_dict(self):

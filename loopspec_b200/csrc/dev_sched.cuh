@@ -1,10 +1,11 @@
-// The LoopSpec scheduler of one greedy request as fixed-size state that a
+// The LoopSpec scheduler of one request as fixed-size state that a
 // single GPU thread can run between the role calls of a cycle, so that whole
 // cycles run back to back without a host round trip.
 //
 // It restates, with arrays instead of maps and heaps:
 //   continue_pipelined (sglang_recurrent/loopspec/pipeline.py:254-423) with
-//     greedy resolve (loopspec/decisions.py:136-184), the executor's
+//     greedy resolve (loopspec/decisions.py:136-184) or the sampled decision
+//     rows' resolve (loopspec/sampling/policy.py:285-308), the executor's
 //     state-slot pool and counters (loopspec/executor.py:76-107, 239-290);
 //   the branch timeline bookkeeping (loopspec/branching/manager.py:45-482):
 //     cursors per (branch, role, depth), forks that share a parent's prefix,
@@ -79,13 +80,19 @@ struct DevSched {
   int next_branch;
   unsigned char state_used[MAXL];
   int committed, done, err;
+  int draw_cycle;             // random-stream cycle counter of the request's readouts
+  unsigned long long seed;    // the request's sampling seed (Philox key of its draws)
+  long long kv_positions;     // sum over core lanes of the timeline length attended
   long long last_token;
   int last_accepted;          // accepted stage of the last retention (-1: none)
   long long stats[9];   // pipeline_cycles, pre_rows, recurrent_rows, post_rows, verified_proposals,
                         // first_rejections, second_verifications, second_acceptances, second_rejections
   // timelines
+  static constexpr int kNodeWords = (MAXN + 63) / 64, kCurWords = (MAXC + 63) / 64;
   DsNode<MAXD> nodes[MAXN];
   DsCursor cursors[MAXC];
+  unsigned long long node_bits[kNodeWords];   // bit i: nodes[i] in use
+  unsigned long long cur_bits[kCurWords];     // bit i: cursors[i] in use
   int n_free_rows;
   int free_rows[MAXR];
   int next_slot, slot_limit;
@@ -95,9 +102,40 @@ struct DevSched {
     if (!err) err = code;
   }
 
+  // Lowest set (or, inverted, clear) bit of a word array; -1 if none. The
+  // scans below visit only the nodes in use, in increasing index, so a
+  // lookup costs a few shared-memory round trips on the GPU thread instead
+  // of one per table entry.
+  static LS_HD int ctz64(unsigned long long x) {
+#ifdef __CUDA_ARCH__
+    return __ffsll((long long)x) - 1;
+#else
+    return __builtin_ctzll(x);
+#endif
+  }
+  template <int W>
+  static LS_HD int first_clear(const unsigned long long (&bits)[W], int limit) {
+    for (int w = 0; w < W; ++w)
+      if (~bits[w]) {
+        const int i = w * 64 + ctz64(~bits[w]);
+        return i < limit ? i : -1;
+      }
+    return -1;
+  }
+  // calls f(i) for every node in use, in increasing index
+  template <class F>
+  LS_HD void for_used_nodes(F f) const {
+    for (int w = 0; w < kNodeWords; ++w)
+      for (unsigned long long m = node_bits[w]; m; m &= m - 1) f(w * 64 + ctz64(m));
+  }
+
   LS_HD int node_of(int id) const {
-    for (int i = 0; i < MAXN; ++i)
-      if (nodes[i].used && nodes[i].id == id) return i;
+    if (id < 0) return -1;
+    for (int w = 0; w < kNodeWords; ++w)
+      for (unsigned long long m = node_bits[w]; m; m &= m - 1) {
+        const int i = w * 64 + ctz64(m);
+        if (nodes[i].id == id) return i;
+      }
     return -1;
   }
 
@@ -143,33 +181,40 @@ struct DevSched {
   }
 
   LS_HD int new_cursor(int row, int seq_len, int pending) {
-    for (int i = 0; i < MAXC; ++i)
-      if (!cursors[i].used) {
-        cursors[i].used = 1;
-        cursors[i].row = row;
-        cursors[i].seq_len = seq_len;
-        cursors[i].pending_parent_row = pending;
-        return i;
-      }
-    fail(kDsCapacity);
-    return 0;
+    const int i = first_clear(cur_bits, MAXC);   // the lowest free entry
+    if (i < 0) {
+      fail(kDsCapacity);
+      return 0;
+    }
+    cur_bits[i / 64] |= 1ull << (i % 64);
+    cursors[i].used = 1;
+    cursors[i].row = row;
+    cursors[i].seq_len = seq_len;
+    cursors[i].pending_parent_row = pending;
+    return i;
   }
 
   LS_HD int new_node(int id, int parent) {
-    for (int i = 0; i < MAXN; ++i)
-      if (!nodes[i].used) {
-        DsNode<MAXD>& n = nodes[i];
-        n.used = 1;
-        n.id = id;
-        n.parent = parent;
-        n.child_count = 0;
-        n.live = 1;
-        for (int r = 0; r < 3; ++r)
-          for (int d = 0; d < MAXD; ++d) n.cur[r][d] = -1;
-        return i;
-      }
-    fail(kDsCapacity);
-    return 0;
+    const int i = first_clear(node_bits, MAXN);   // the lowest free entry
+    if (i < 0) {
+      fail(kDsCapacity);
+      return 0;
+    }
+    node_bits[i / 64] |= 1ull << (i % 64);
+    DsNode<MAXD>& n = nodes[i];
+    n.used = 1;
+    n.id = id;
+    n.parent = parent;
+    n.child_count = 0;
+    n.live = 1;
+    for (int r = 0; r < 3; ++r)
+      for (int d = 0; d < MAXD; ++d) n.cur[r][d] = -1;
+    return i;
+  }
+
+  LS_HD void free_node(int i) {
+    nodes[i].used = 0;
+    node_bits[i / 64] &= ~(1ull << (i % 64));
   }
 
   // -------------------------------------- timelines (manager.py:207-482)
@@ -203,6 +248,7 @@ struct DevSched {
   LS_HD void release_cursor(int c) {
     free_row(cursors[c].row);
     cursors[c].used = 0;
+    cur_bits[c / 64] &= ~(1ull << (c % 64));
   }
 
   LS_HD void release_unused(int n) {
@@ -211,7 +257,7 @@ struct DevSched {
         for (int d = 0; d < MAXD; ++d)
           if (nodes[n].cur[r][d] >= 0) release_cursor(nodes[n].cur[r][d]);
       const int pid = nodes[n].parent;
-      nodes[n].used = 0;
+      free_node(n);
       if (pid < 0) break;
       const int p = node_of(pid);
       if (p < 0) break;
@@ -261,12 +307,12 @@ struct DevSched {
     // unused live nodes, released from the highest id down
     int ids[MAXN];
     int nu = 0;
-    for (int i = 0; i < MAXN; ++i) {
-      if (!nodes[i].used || !nodes[i].live) continue;
+    for_used_nodes([&](int i) {
+      if (!nodes[i].live) return;
       bool kept = false;
       for (int k = 0; k < nk && !kept; ++k) kept = keep[k].branch == nodes[i].id;
       if (!kept) ids[nu++] = i;
-    }
+    });
     sort_by_id(ids, nu, false);
     for (int k = 0; k < nu; ++k) {
       const int n = ids[k];
@@ -276,8 +322,7 @@ struct DevSched {
     }
     // single surviving children adopt their dead parents' timelines (ascending id)
     int na = 0;
-    for (int i = 0; i < MAXN; ++i)
-      if (nodes[i].used) ids[na++] = i;
+    for_used_nodes([&](int i) { ids[na++] = i; });
     sort_by_id(ids, na, true);
     for (int k = 0; k < na; ++k)   // no node is created here, so a freed index stays free
       if (nodes[ids[k]].used) detach_from_unused_parent(ids[k]);
@@ -324,10 +369,12 @@ struct DevSched {
     return n_lanes;
   }
 
-  // One greedy cycle's decisions: dec[i] = argmax token of lane i's readout
-  // (ignored for lanes without a readout). Appends a committed token to
-  // `out` (indexed by the committed count) when the final lane commits.
-  LS_HD void consume(const long long* dec, long long* out) {
+  // One cycle's decisions, `stride` values per lane: greedy (stride 1) the
+  // argmax token of the lane's readout; sampling (stride 5) the row (token,
+  // proposed, accepted_code, q1_rejected, q2_rejected) of policy.py:197-283.
+  // Lanes without a readout are ignored. Appends a committed token to `out`
+  // (indexed by the committed count) when the final lane commits.
+  LS_HD void consume(const long long* dec, int stride, long long* out) {
     stats[0] += 1;
     stats[2] += (long long)n_lanes * K;
     for (int i = 0; i < n_lanes; ++i) {
@@ -345,16 +392,24 @@ struct DevSched {
       DsLane l = lanes[i];
       const int end_stage = l.stage + K - 1;
       const int kind = kind_of[end_stage];
-      const long long pred = dec[i];
+      const long long* d = dec + (long)i * stride;
+      const long long pred = d[0];
       bool proposed = false, fr = false, sr = false;
       int acc = -1;
-      proposed = kind == 0 || (kind == 1 && (l.first < 0 || pred != l.first));
-      if (kind == 2 && l.first >= 0) {
-        fr = pred != l.first;
-        if (!fr) acc = q1;
-        else if (l.second >= 0) {
-          sr = pred != l.second;
-          if (!sr) acc = q2;
+      if (stride >= 5) {   // sampling resolve (policy.py:285-308)
+        proposed = d[1] != 0;
+        acc = d[2] == 1 ? q1 : d[2] == 2 ? q2 : -1;
+        fr = d[3] != 0;
+        sr = d[4] != 0;
+      } else {             // greedy resolve (decisions.py:136-184)
+        proposed = kind == 0 || (kind == 1 && (l.first < 0 || pred != l.first));
+        if (kind == 2 && l.first >= 0) {
+          fr = pred != l.first;
+          if (!fr) acc = q1;
+          else if (l.second >= 0) {
+            sr = pred != l.second;
+            if (!sr) acc = q2;
+          }
         }
       }
       if (end_stage == final_stage) {
@@ -523,6 +578,7 @@ struct DevSched {
         const DsLane& l = lanes[i];
         cur[i] = get_or_create_cursor(1, l.stage + off, l.branch, l.parent);
         fill(core[off * MAXL + i], l, cur[i], state_base + l.state, state_base + l.state);
+        kv_positions += prefill_len + l.index + 1;
       }
       for (int i = 0; i < n_lanes; ++i) advance(cur[i]);
     }
@@ -608,6 +664,140 @@ inline void ds_start(D& d, int S, int K, int X, int max_rows, int max_new, long 
   }
   d.n_lanes = 1;
   d.lanes[0] = DsLane{0, 1, (int)first, -1, 0, -1, -1, -1, -1};
+}
+
+}  // namespace ls
+
+namespace ls {
+
+// ------------------------------------------------ device-resident decode loop
+// The scheduler of one request for the device loop: up to 16 live
+// lanes, S <= 8, 64 branch nodes, 128 cursors, 512 mapping rows.
+using LoopSched = DevSched<16, 64, 8, 64, 128, 512>;
+constexpr int kLoopMaxLanes = 16;
+constexpr int kLoopMaxK = 8;
+constexpr int kLoopThreads = 256;
+
+// Lane metadata of one role call at a fixed width: `n` active lanes, the rest
+// inactive (position -1), which every per-lane kernel skips.
+__device__ inline void write_meta(int* m, int width, const DsFill* f, int n, int draw, bool post,
+                                  unsigned long long seed) {
+  for (int i = threadIdx.x; i < width * kMetaFields; i += blockDim.x) {
+    const int b = i / kMetaFields, k = i % kMetaFields;
+    int v = -1;
+    if (b < n) {
+      const DsFill& x = f[b];
+      switch (k) {
+        case kMetaToken: v = x.token; break;
+        case kMetaPos: v = x.pos; break;
+        case kMetaRow: v = x.row; break;
+        case kMetaSlot: v = x.slot; break;
+        case kMetaForkRow: v = x.fork_row; break;
+        case kMetaForkLen: v = x.fork_len; break;
+        case kMetaStateIn: v = x.state_in; break;
+        case kMetaStateOut: v = x.state_out; break;
+        case kMetaKind: v = post ? x.kind : -1; break;
+        case kMetaFirst: v = post ? x.first : -1; break;
+        case kMetaSecond: v = post ? x.second : -1; break;
+        case kMetaCycle: v = post ? draw : -1; break;
+        case kMetaAhead: v = 0; break;
+        case kMetaDrawRow: v = post ? b : -1; break;
+        case kMetaSeedLo: v = post ? (int)(uint32_t)(seed & 0xFFFFFFFFull) : -1; break;
+        case kMetaSeedHi: v = post ? (int)(uint32_t)(seed >> 32) : -1; break;
+        default: v = -1;
+      }
+    }
+    m[i] = v;
+  }
+}
+
+__device__ inline void load_sched(LoopSched* s, const LoopSched* g) {
+  const int n = (int)(sizeof(LoopSched) / sizeof(int));
+  int* d = reinterpret_cast<int*>(s);
+  const int* src = reinterpret_cast<const int*>(g);
+  for (int i = threadIdx.x; i < n; i += blockDim.x) d[i] = __ldcg(src + i);
+  __syncthreads();
+}
+
+__device__ inline void store_sched(LoopSched* g, const LoopSched* s) {
+  __syncthreads();
+  const int n = (int)(sizeof(LoopSched) / sizeof(int));
+  int* d = reinterpret_cast<int*>(g);
+  const int* src = reinterpret_cast<const int*>(s);
+  for (int i = threadIdx.x; i < n; i += blockDim.x) d[i] = src[i];
+}
+
+// Where the metadata of a cycle's role calls goes: pre, K core records of
+// `stride` ints, post; `width` lanes each (unused lanes inactive).
+struct LoopMeta {
+  int* pre;
+  int* core;
+  long stride;
+  int* post;
+  int width;
+};
+
+// Start of a cycle (thread 0 has planned it into the shared arrays): write
+// the role calls' metadata. A finished request plans no lanes, so its role
+// calls do nothing but stream weights.
+struct LoopPlan {
+  DsFill pre[kLoopMaxLanes], post[kLoopMaxLanes], core[kLoopMaxK * kLoopMaxLanes];
+  int n_pre, n_post, n_core, draw;
+};
+
+__device__ inline void loop_plan(LoopSched& s, LoopPlan& p) {   // thread 0
+  p.n_pre = p.n_post = p.n_core = 0;
+  if (!s.done && !s.err) {
+    p.n_core = s.gather();
+    s.plan(p.pre, p.n_pre, p.core, p.post, p.n_post);
+    s.draw_cycle += 1;
+  }
+  p.draw = s.draw_cycle;
+}
+
+__device__ inline void loop_write_meta(const LoopSched& s, const LoopPlan& p, const LoopMeta& m) {
+  write_meta(m.pre, m.width, p.pre, p.n_pre, p.draw, false, s.seed);
+  for (int k = 0; k < s.K; ++k)
+    write_meta(m.core + k * m.stride, m.width, p.core + k * kLoopMaxLanes, p.n_core, p.draw, false, s.seed);
+  write_meta(m.post, m.width, p.post, p.n_post, p.draw, true, s.seed);
+}
+
+// The first cycle's plan.
+__global__ void __launch_bounds__(kLoopThreads) loop_plan_kernel(LoopSched* g, LoopMeta m) {
+  __shared__ LoopSched s;
+  __shared__ LoopPlan p;
+  load_sched(&s, g);
+  if (threadIdx.x == 0) loop_plan(s, p);
+  __syncthreads();
+  loop_write_meta(s, p, m);
+  store_sched(g, &s);
+}
+
+// End of a cycle and start of the next: the readout lanes' decisions (in
+// readout order: greedy tokens, stride 1, or sampled decision rows, stride 5)
+// resolve the pipeline, commit a token to `out` and retain the surviving
+// branches' timelines; then the next cycle is planned.
+__global__ void __launch_bounds__(kLoopThreads) loop_step_kernel(LoopSched* g, const long long* dec_in, int stride,
+                                                                 long long* out, LoopMeta m) {
+  __shared__ LoopSched s;
+  __shared__ LoopPlan p;
+  load_sched(&s, g);
+  if (threadIdx.x == 0) {
+    if (!s.done && !s.err) {
+      long long dec[kLoopMaxLanes * 5];
+      int j = 0;
+      for (int i = 0; i < s.n_lanes; ++i) {
+        const bool readout = s.kind_of[s.lanes[i].stage + s.K - 1] >= 0;
+        for (int f = 0; f < stride; ++f) dec[i * stride + f] = readout ? dec_in[j * stride + f] : -1;
+        j += readout;
+      }
+      s.consume(dec, stride, out);
+    }
+    loop_plan(s, p);
+  }
+  __syncthreads();
+  loop_write_meta(s, p, m);
+  store_sched(g, &s);
 }
 
 }  // namespace ls

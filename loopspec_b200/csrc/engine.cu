@@ -16,6 +16,7 @@
 #include "dev_sched.cuh"
 #include "gemm_tc.cuh"
 #include "kernels.cuh"
+#include "prefill_attn.cuh"
 #include "sampler.cuh"
 
 #include <algorithm>
@@ -305,6 +306,29 @@ class Timelines {
   }
 
   size_t live_nodes() const { return nodes_.size(); }
+
+  // Hand a freshly prefilled request to the device loop's scheduler `d`
+  // (whose root node is d.nodes[0]): the root's cursors, the free mapping
+  // rows, and the free KV slots, which after a prefill are one contiguous
+  // range [first free, slot_base + slots).
+  template <class D>
+  void export_to(D& d) const {
+    auto it = nodes_.find(0);
+    REQUIRE(it != nodes_.end() && nodes_.size() == 1, LS_EINVAL, "device loop needs a freshly prefilled request");
+    for (int role = 0; role < 3; ++role)
+      for (auto& kv : it->second->cur[role]) {
+        REQUIRE(kv.first < (int)(sizeof(d.kind_of) / sizeof(int)), LS_EINVAL, "timeline depth beyond the device loop");
+        d.nodes[0].cur[role][kv.first] = d.new_cursor(kv.second->row, kv.second->seq_len, -1);
+      }
+    REQUIRE(free_rows_.size() <= sizeof(d.free_rows) / sizeof(int), LS_ECAPACITY, "too many rows for the device loop");
+    d.n_free_rows = (int)free_rows_.size();
+    for (size_t i = 0; i < free_rows_.size(); ++i) d.free_rows[i] = free_rows_[i];
+    REQUIRE(!free_slots_.empty(), LS_ECAPACITY, "KV slot pool exhausted");
+    const int first = free_slots_.back();
+    REQUIRE((int)free_slots_.size() == slot_base_ + slots_ - first, LS_EINVAL, "free KV slots are not contiguous");
+    d.next_slot = first;
+    d.slot_limit = slot_base_ + slots_;
+  }
   size_t free_slots() const { return free_slots_.size(); }
   size_t free_rows() const { return free_rows_.size(); }
 
@@ -406,6 +430,17 @@ struct ls_engine {
   int* map = nullptr;
   float *bank_h = nullptr, *bank_inj = nullptr;
   int* meta_dev = nullptr;      // [3][F][cap]
+  const int* meta_override = nullptr;   // metadata of the role call being enqueued, if not meta_dev's
+  // device-resident decode loop (greedy, one request): the scheduler state,
+  // the metadata of one cycle's role calls ([pre][K core][post], width
+  // max_rows), committed tokens, and the captured cycle graph
+  LoopSched* loop_sched = nullptr;
+  LoopSched* loop_host = nullptr;   // pinned
+  int* loop_meta = nullptr;
+  long long* loop_out = nullptr;
+  cudaGraphExec_t loop_graph = nullptr;
+  int loop_graph_kernels = 0, loop_graph_chunks = 0;
+  bool loop_graph_sampling = false;
   int* meta_host = nullptr;     // pinned [kStaging][F][cap]
   int staging_next = 0;
   static constexpr int kStaging = 64;
@@ -428,7 +463,7 @@ struct ls_engine {
   bool sampling = false;
   SampleParams sparams{1.f, 1.f, 0, 0, 0ull};
   SampleParams* sparams_dev = nullptr;
-  float *q1_bank = nullptr, *r_bank = nullptr, *samp_work = nullptr;
+  float *q1_bank = nullptr, *r_bank = nullptr;
   long long *dec_dev = nullptr, *dec_host = nullptr;
   float* gemm_part = nullptr;   // GEMM split partial tiles
   long gemm_part_elems = 0;
@@ -454,6 +489,7 @@ struct ls_engine {
   int64_t kernel_launches = 0;                        // kernels launched by role calls
   // work counters of role calls (decode stats are differences around the loop)
   int64_t pre_calls = 0, core_calls = 0, core_kv_positions = 0, post_calls = 0;
+  int64_t host_syncs = 0;   // stream synchronisations of decode loops
   int kernels_in_call = 0;
   // The next launch waits for full completion of the previous kernel (no
   // programmatic overlap). Set after the mapping update: every kernel
@@ -498,6 +534,8 @@ struct ls_engine {
   ~ls_engine() {
     if (device >= 0) cudaSetDevice(device);
     for (auto& g : graphs) cudaGraphExecDestroy(g.second);
+    if (loop_graph) cudaGraphExecDestroy(loop_graph);
+    if (loop_host) cudaFreeHost(loop_host);
     for (void* p : tp_opened) cudaIpcCloseMemHandle(p);
     for (void* p : allocs) cudaFree(p);
     if (meta_host) cudaFreeHost(meta_host);
@@ -582,6 +620,13 @@ struct ls_engine {
     }
   }
 
+  // The device-resident loop serves one greedy request of a schedule whose
+  // lanes fit its fixed tables (at most 16 live lanes, S <= 8), on one GPU.
+  bool loop_enabled = false;   // finalize sized the KV pool for the device loop
+  bool device_loop_possible() const {
+    return sc.device_loop && max_rows <= kLoopMaxLanes && S <= 8 && K <= kLoopMaxK && sc.use_graphs;
+  }
+
   // ---------------------------------------------------------------- finalize
   void finalize() {
     REQUIRE(!finalized, LS_EINVAL, "engine already finalized");
@@ -648,6 +693,22 @@ struct ls_engine {
     } else {
       n_slots = n_timelines * (max_ctx + 2 * max_rows) + 2 * rows;
     }
+    // The device loop hands out KV slots without recycling them during a
+    // request: each cycle takes one per lane per role call with attention,
+    // and a token takes at most S / K cycles, so it needs up to
+    // (S / K) * max_ctx * max_rows * (K + pre + post) slots beyond the prompt.
+    // It is used only while that pool stays modest (24 GB of K/V).
+    loop_enabled = false;
+    if (device_loop_possible()) {
+      const long roles = K + (mc.n_pre_layers ? 1 : 0) + (mc.n_post_layers ? 1 : 0);
+      const long need = (long)(S / K) * max_ctx * max_rows * roles + (long)n_timelines * max_ctx;
+      const double kv_bytes = 2.0 * (mc.n_pre_layers + mc.n_core_layers + mc.n_post_layers) *
+                              (double)std::max<long>(need, n_slots) * (mc.n_kv_heads * mc.head_dim) * 2.0;
+      if (sc.kv_slots <= 0 && max_req == 1 && kv_bytes <= 24e9) {
+        n_slots = (int)std::max<long>(need, n_slots);
+        loop_enabled = true;
+      }
+    }
     // per-request capacities (request_rows / kv_slots size one request),
     // disjoint ranges per request
     reqs.assign(max_req, Request());
@@ -685,6 +746,12 @@ struct ls_engine {
     bank_h = dalloc<float>((long)bank_rows * H);
     bank_inj = dalloc<float>((long)bank_rows * H);
     meta_dev = dalloc<int>(3L * kMetaFields * cap);
+    if (loop_enabled) {
+      loop_sched = dalloc<LoopSched>(1);
+      CK(cudaMallocHost(&loop_host, sizeof(LoopSched)));
+      loop_meta = dalloc<int>((long)(K + 2) * kMetaFields * cap);
+      loop_out = dalloc<long long>(max_ctx);
+    }
     CK(cudaMallocHost(&meta_host, sizeof(int) * (size_t)kStaging * kMetaFields * cap));
     h = dalloc<float>((long)cap * H);
     r = dalloc<float>((long)cap * H);
@@ -716,17 +783,18 @@ struct ls_engine {
     CK(cudaMemcpy(sparams_dev, &sparams, sizeof(SampleParams), cudaMemcpyHostToDevice));
     q1_bank = dalloc<float>((long)max_state * V);
     r_bank = dalloc<float>((long)max_state * V);
-    samp_work = dalloc<float>((long)max_state * 2 * V);
     dec_dev = dalloc<long long>((long)cap * 5);
     CK(cudaMallocHost(&dec_host, sizeof(long long) * 5 * (size_t)cap));
     CK(cudaMallocHost(&err_host, sizeof(int)));
     REQUIRE(V <= kSampleChunk * kSampleMaxChunks, LS_EINVAL, "vocabulary above the sampler's limit");
-    if (V <= kSampleSmemVocab) {
-      CK(cudaFuncSetAttribute(sample_kernel<true, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              (int)(V * sizeof(float))));
-      CK(cudaFuncSetAttribute(sample_kernel<true, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              (int)(V * sizeof(float))));
-    }
+    CK(cudaFuncSetAttribute(sample_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                            (int)sample_smem_bytes(V)));
+    CK(cudaFuncSetAttribute(sample_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                            (int)sample_smem_bytes(V)));
+    CK(cudaFuncSetAttribute(prefill_attn_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                            (int)pattn_smem_bytes<128>()));
+    CK(cudaFuncSetAttribute(prefill_attn_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                            (int)pattn_smem_bytes<64>()));
     gemm_tickets = dalloc<int>(gemm_ticket_count);
     std::vector<float> inv(HD / 2);
     for (int i = 0; i < HD / 2; ++i)
@@ -775,6 +843,7 @@ struct ls_engine {
 namespace {
 
 Meta meta_of(ls_engine& e, int role) {
+  if (e.meta_override) return Meta{e.meta_override, e.cap};
   return Meta{e.meta_dev + (long)role * kMetaFields * e.cap, e.cap};
 }
 
@@ -876,6 +945,29 @@ void klaunch(ls_engine& e, void (*kernel)(KArgs...), dim3 grid, dim3 block, size
   e.kernels_in_call++;
 }
 
+// klaunch for a kernel of thread-block clusters of `cluster` CTAs along x.
+template <typename... KArgs, typename... Args>
+void klaunch_cluster(ls_engine& e, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                     int cluster, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = e.stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)cluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = e.sc.use_pdl != 0 && !e.serialize_next ? 2 : 1;
+  CK(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
+  e.serialize_next = false;
+  e.kernels_in_call++;
+}
+
 void map_update(ls_engine& e, Meta meta, int n) {
   klaunch(e, map_update_kernel, dim3(n), dim3(128), 0, meta, n, e.map, e.max_ctx, e.rows, e.err_dev);
   // attention reads slot ids before its wait: unless the update only appends
@@ -918,6 +1010,13 @@ void attention(ls_engine& e, Meta meta, int n, bf16* kp, bf16* vp, const Gemm* p
     a.inv_freq = e.inv_freq;
     a.kpool_w = kp;
     a.vpool_w = vp;
+  }
+  if (!planes && e.prefill_mode && (e.HD == 128 || e.HD == 64)) {
+    // a prompt chunk of one timeline: tensor-core tiles over the shared K/V
+    const dim3 pg(cdiv(n, kPAttnRows), e.NH), pb(kPAttnThreads);
+    if (e.HD == 128) klaunch(e, prefill_attn_kernel<128>, pg, pb, pattn_smem_bytes<128>(), a, n);
+    else klaunch(e, prefill_attn_kernel<64>, pg, pb, pattn_smem_bytes<64>(), a, n);
+    return;
   }
   const dim3 grid(n, e.NKV, e.attn_chunks), blk(kAttnThreads);
   const int G = e.NH / e.NKV;
@@ -1122,15 +1221,14 @@ void head_decisions(ls_engine& e, Meta meta, int lane0, int lanes) {
   if (e.sampling) {
     REQUIRE(lanes <= e.max_state, LS_ECAPACITY, "too many sampled readout rows");
     SampleArgs sa{meta, lane0, e.logits, e.V, e.sparams_dev, e.q1_bank, e.r_bank,
-                  e.max_state, e.samp_work, e.dec_dev, e.err_dev};
-    // rows in 16-byte steps when the vocabulary allows (logits, banks and
-    // scratch rows are then 16-byte aligned)
-    const size_t psm = (size_t)e.V * sizeof(float);
-    const dim3 g(lanes), b(kSampleThreads);
-    if (e.V <= kSampleSmemVocab && e.V % 4 == 0) klaunch(e, sample_kernel<true, 4>, g, b, psm, sa);
-    else if (e.V <= kSampleSmemVocab) klaunch(e, sample_kernel<true, 1>, g, b, psm, sa);
-    else if (e.V % 4 == 0) klaunch(e, sample_kernel<false, 4>, g, b, 0, sa);
-    else klaunch(e, sample_kernel<false, 1>, g, b, 0, sa);
+                  e.max_state, e.dec_dev, e.err_dev};
+    // one cluster of CTAs per row; rows in 16-byte steps when the vocabulary
+    // allows (logits and bank rows are then 16-byte aligned)
+    const int C = sample_ctas(e.V);
+    const dim3 g(lanes * C), b(kSampleThreads);
+    const size_t smem = sample_smem_bytes(e.V);
+    if (e.V % 4 == 0) klaunch_cluster(e, sample_kernel<4>, g, b, smem, C, sa);
+    else klaunch_cluster(e, sample_kernel<1>, g, b, smem, C, sa);
   } else {
     klaunch(e, argmax_kernel, dim3(lanes), dim3(1024), 0, (const float*)e.logits, e.V, (long)e.V,
             e.amax_dev);
@@ -1563,6 +1661,7 @@ void cycle(ls_engine& e, const std::vector<CycleLane>& lanes, std::vector<Dec>& 
   }
   fetch_device_error(e);
   CK(cudaStreamSynchronize(e.stream));
+  e.host_syncs++;
   e.staging_next = 0;
   check_fetched_error(e);
   for (int j = 0; j < M; ++j) {
@@ -1912,6 +2011,7 @@ void run_ar(ls_engine& e, std::vector<std::vector<long long>>& committed, std::v
     e.d2h_bytes += sizeof(long long) * stride * B;
     fetch_device_error(e);
     CK(cudaStreamSynchronize(e.stream));
+    e.host_syncs++;
     e.staging_next = 0;
     check_fetched_error(e);
     for (int j = 0; j < B; ++j) {
@@ -1921,6 +2021,147 @@ void run_ar(ls_engine& e, std::vector<std::vector<long long>>& committed, std::v
     }
   }
   for (int i = 0; i < n; ++i) e.reqs[reqs[i]].tl.retain({});
+}
+
+// ------------------------------------------------ device-resident decode loop
+// Where the scheduler kernels write the role calls' metadata (fixed width
+// max_rows, unused lanes inactive).
+LoopMeta loop_meta_of(const ls_engine& e) {
+  const long F = (long)kMetaFields * e.cap;
+  return LoopMeta{e.loop_meta, e.loop_meta + F, F, e.loop_meta + (1 + e.K) * F, e.max_rows};
+}
+
+// One cycle as one graph: the role calls read the metadata the previous
+// scheduler kernel wrote (the post call's lm_head GEMM reduces each lane's
+// greedy token, or the sampler writes its decision rows), then the step
+// kernel resolves the decisions, commits, retains branches and plans the next
+// cycle. Nothing returns to the host between cycles.
+void capture_loop_graph(ls_engine& e, int chunks) {
+  const int W = e.max_rows;
+  const LoopMeta lm = loop_meta_of(e);
+  int* pre = lm.pre;
+  int* core = lm.core;
+  const long F = lm.stride;
+  int* post = lm.post;
+  if (e.loop_graph) {
+    CK(cudaStreamSynchronize(e.stream));
+    CK(cudaGraphExecDestroy(e.loop_graph));
+    e.loop_graph = nullptr;
+  }
+  int kernels = 0;
+  CK(cudaStreamBeginCapture(e.stream, cudaStreamCaptureModeThreadLocal));
+  try {
+    e.qkv_planes = true;    // one new position per lane
+    e.call_forks = true;    // forks are decided on the device: order every read after the mapping update
+    e.attn_chunks = chunks;
+    e.serialize_next = true;   // the first role kernel reads the metadata the step kernel wrote
+    e.meta_override = pre;
+    enqueue_role(e, kPre, W);
+    kernels += e.kernels_in_call;
+    for (int k = 0; k < e.K; ++k) {
+      e.meta_override = core + k * F;
+      enqueue_role(e, kCore, W);
+      kernels += e.kernels_in_call;
+    }
+    e.meta_override = post;
+    enqueue_role(e, kPost, W);
+    kernels += e.kernels_in_call;
+    e.meta_override = nullptr;
+    if (e.sampling)
+      launch(loop_step_kernel, dim3(1), dim3(kLoopThreads), 0, e.stream, false, e.loop_sched,
+             (const long long*)e.dec_dev, 5, e.loop_out, lm);
+    else
+      launch(loop_step_kernel, dim3(1), dim3(kLoopThreads), 0, e.stream, false, e.loop_sched,
+             (const long long*)e.amax_dev, 1, e.loop_out, lm);
+  } catch (...) {
+    e.meta_override = nullptr;
+    cudaGraph_t g = nullptr;
+    cudaStreamEndCapture(e.stream, &g);
+    if (g) cudaGraphDestroy(g);
+    throw;
+  }
+  cudaGraph_t g = nullptr;
+  CK(cudaStreamEndCapture(e.stream, &g));
+  const cudaError_t ie = cudaGraphInstantiate(&e.loop_graph, g, 0);
+  cudaGraphDestroy(g);
+  CK(ie);
+  e.loop_graph_kernels = kernels + 1;
+  e.loop_graph_chunks = chunks;
+  e.loop_graph_sampling = e.sampling;
+}
+
+const char* loop_error_text(int code) {
+  static const char* names[] = {"ok", "recurrent state slots exhausted", "mapping rows exhausted",
+                                "KV slots exhausted", "branch with an unavailable parent",
+                                "several lanes reached the final stage", "commit out of order",
+                                "speculative tree exceeded the branch row limit",
+                                "pipeline drained before generation completed", "scheduler table full"};
+  return code > 0 && code < 10 ? names[code] : "unknown";
+}
+
+// One greedy request on the device-resident loop, after its prefill. Since a
+// cycle commits at most one token, the host launches as many cycles as tokens
+// remain, then reads the scheduler state; it repeats until the request is done.
+std::vector<long long> run_device_loop(ls_engine& e, Request& R, long long first, int max_new,
+                                       long long stop_token, ls_stats& st, double& decode_t0) {
+  LoopSched& h = *e.loop_host;
+  std::memset(&h, 0, sizeof(LoopSched));
+  long long first_out = 0;
+  ds_start(h, e.S, e.K, e.X, e.max_rows, max_new, stop_token, first, &first_out);
+  h.has_pre = e.mc.n_pre_layers > 0;
+  h.has_post = e.mc.n_post_layers > 0;
+  h.prefill_len = R.prefill_len;
+  h.state_base = R.state_base;
+  h.draw_cycle = (int)R.draw_cycle;
+  h.seed = R.seed;
+  R.tl.export_to(h);
+  decode_t0 = now_s();
+  std::vector<long long> ids{first};
+  if (h.done) return ids;
+  CK(cudaMemcpyAsync(e.loop_sched, &h, sizeof(LoopSched), cudaMemcpyHostToDevice, e.stream));
+  CK(cudaMemcpyAsync(e.loop_out, &first_out, sizeof(long long), cudaMemcpyHostToDevice, e.stream));
+  e.h2d_bytes += sizeof(LoopSched) + sizeof(long long);
+  int chunks = cdiv(R.prefill_len + max_new + 1, kAttnChunk);
+  chunks = std::min(chunks + (chunks & 1), e.max_chunks);
+  if (!e.loop_graph || e.loop_graph_chunks != chunks || e.loop_graph_sampling != e.sampling)
+    capture_loop_graph(e, chunks);
+  launch(loop_plan_kernel, dim3(1), dim3(kLoopThreads), 0, e.stream, false, e.loop_sched, loop_meta_of(e));
+  e.kernel_launches += 1;
+  long cycles = 0;
+  int committed = 1;
+  for (;;) {
+    for (int i = committed; i < max_new; ++i) CK(cudaGraphLaunch(e.loop_graph, e.stream));
+    cycles += max_new - committed;
+    CK(cudaMemcpyAsync(&h, e.loop_sched, sizeof(LoopSched), cudaMemcpyDeviceToHost, e.stream));
+    e.d2h_bytes += sizeof(LoopSched);
+    fetch_device_error(e);
+    CK(cudaStreamSynchronize(e.stream));
+    e.host_syncs++;
+    check_fetched_error(e);
+    REQUIRE(h.err == kDsOk, LS_EPIPELINE, std::string("device loop: ") + loop_error_text(h.err));
+    committed = h.committed;
+    if (h.done || committed >= max_new) break;
+  }
+  ids.resize(h.committed);
+  CK(cudaMemcpy(ids.data(), e.loop_out, sizeof(long long) * h.committed, cudaMemcpyDeviceToHost));
+  e.d2h_bytes += sizeof(long long) * h.committed;
+  st.pipeline_cycles = h.stats[0];
+  st.pre_rows = h.stats[1];
+  st.recurrent_rows = h.stats[2];
+  st.post_rows = h.stats[3];
+  st.verified_proposals = h.stats[4];
+  st.first_rejections = h.stats[5];
+  st.second_verifications = h.stats[6];
+  st.second_acceptances = h.stats[7];
+  st.second_rejections = h.stats[8];
+  // every launched cycle streams the weights of all its role calls
+  e.kernel_launches += cycles * e.loop_graph_kernels;
+  e.core_calls += cycles * e.K;
+  e.post_calls += cycles;
+  if (e.mc.n_pre_layers > 0) e.pre_calls += cycles;
+  e.core_kv_positions += h.kv_positions;
+  R.draw_cycle = (uint32_t)h.draw_cycle;
+  return ids;
 }
 
 SchedHooks engine_hooks(ls_engine& e, int req, StopRule stop) {
@@ -2375,7 +2616,8 @@ namespace {
 // the batch's work counters, copy volumes and decode timing.
 int generate_batch(ls_engine* e, const int64_t* prompts, const int32_t* lens, int n_req, int max_new,
                    int mode, const std::vector<StopRule>& stop, const uint64_t* seeds,
-                   int64_t* out_ids, int32_t* n_out, ls_stats* per_request, ls_stats* total) {
+                   int64_t* out_ids, int32_t* n_out, ls_stats* per_request, ls_stats* total,
+                   long long device_loop_stop = -2) {
   if (!e || !prompts || !lens || !out_ids || !n_out || n_req < 1 || max_new < 1 ||
       (mode != 0 && mode != 1) || (int)stop.size() != n_req)
     return LS_EINVAL;
@@ -2401,11 +2643,17 @@ int generate_batch(ls_engine* e, const int64_t* prompts, const int32_t* lens, in
     double t0 = -1.0;
     const int64_t launches0 = e->kernel_launches;
     const int64_t pre0 = e->pre_calls, core0 = e->core_calls, kv0 = e->core_kv_positions,
-                  post0 = e->post_calls;
+                  post0 = e->post_calls, sync0 = e->host_syncs;
     CK(cudaEventRecord(e->ev0, e->stream));
     std::vector<std::vector<long long>> ids(n_req);
     std::vector<ls_stats> st(n_req, ls_stats{});
-    if (mode == 0) {
+    // a single LoopSpec request whose stop rule is only the EOS id
+    // (device_loop_stop >= -1) runs on the device-resident loop
+    const bool on_device = mode == 0 && n_req == 1 && device_loop_stop >= -1 && e->loop_enabled &&
+                           e->tp_ranks == 1;
+    if (on_device) {
+      ids[0] = run_device_loop(*e, e->reqs[0], first[0], max_new, device_loop_stop, st[0], t0);
+    } else if (mode == 0) {
       std::vector<SchedHooks> hooks;
       hooks.reserve(n_req);
       for (int i = 0; i < n_req; ++i) hooks.push_back(engine_hooks(*e, i, stop[i]));
@@ -2457,6 +2705,7 @@ int generate_batch(ls_engine* e, const int64_t* prompts, const int32_t* lens, in
     tot.core_calls = e->core_calls - core0;
     tot.core_kv_positions = e->core_kv_positions - kv0;
     tot.post_calls = e->post_calls - post0;
+    tot.host_syncs = e->host_syncs - sync0;
     if (total) *total = tot;
   } catch (const std::exception& ex) {
     return fail(e, ex);
@@ -2472,7 +2721,7 @@ int ls_generate(ls_engine* e, const int64_t* prompt, int n_prompt, int max_new, 
   const uint64_t seed = e->sparams.seed;
   int32_t n = 0;
   const int rc = generate_batch(e, prompt, &len, 1, max_new, mode, {stop_rule(stop_token, nullptr, nullptr)},
-                                &seed, out_ids, &n, nullptr, stats);
+                                &seed, out_ids, &n, nullptr, stats, stop_token < 0 ? -1 : stop_token);
   *n_out = n;
   return rc;
 }
@@ -2553,7 +2802,7 @@ int ls_device_loop_simulate(int stages, int step_size, int second_step, int64_t 
         if (kind >= 0) dec[i] = decide(user, l.index, l.token, kind);
       }
       if (on_cycle) on_cycle(user, rows.data(), (int32_t)n);
-      d->consume(dec.data(), out.data());
+      d->consume(dec.data(), 1, out.data());
       report_retain();
     }
     REQUIRE(d->err == kDsOk, LS_EPIPELINE, "device scheduler reported error " + std::to_string(d->err));

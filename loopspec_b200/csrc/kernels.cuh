@@ -5,6 +5,8 @@
 // Every kernel processes each lane (decode token replica) in its own CTA or
 // CTA set with a reduction order that depends only on that lane's data, so a
 // lane's numbers do not depend on the batch it runs in (LoopSpec == AR).
+// A lane whose metadata position is -1 is inactive (the device-resident loop
+// runs every role call at a fixed width): per-lane kernels skip it.
 #pragma once
 
 #include "common.cuh"
@@ -20,7 +22,7 @@ __global__ void map_update_kernel(Meta meta, int B, int* __restrict__ map, int m
   pdl_launch_dependents();
   pdl_wait();
   const int b = blockIdx.x;
-  if (b >= B) return;
+  if (b >= B || meta.get(kMetaPos, b) < 0) return;   // inactive lane
   const int row = meta.get(kMetaRow, b), pos = meta.get(kMetaPos, b);
   const int frow = meta.get(kMetaForkRow, b), flen = meta.get(kMetaForkLen, b);
   if (row < 0 || row >= rows || pos < 0 || pos >= max_ctx) {
@@ -62,7 +64,7 @@ template <int NV>
 __global__ void prep_kernel(PrepArgs a) {
   pdl_launch_dependents();
   const int b = blockIdx.x;
-  if (b >= a.B) return;
+  if (b >= a.B || a.meta.get(kMetaPos, b) < 0) return;   // inactive lane
   __shared__ float red[32];
   const int H = a.H, H4 = H / 4;
   int src;
@@ -118,6 +120,7 @@ __global__ void cat_state_kernel(Meta meta, int H, const float* __restrict__ ban
   pdl_launch_dependents();
   pdl_wait();
   const int b = blockIdx.x;
+  if (meta.get(kMetaPos, b) < 0) return;   // inactive lane
   const int si = meta.get(kMetaStateIn, b);
   if (si < 0 || si >= bank_rows) {
     if (threadIdx.x == 0) atomicExch(err, kDevBadIndex);
@@ -238,7 +241,7 @@ template <int NV, int BATCH, int MAXT, bool TP>
 __global__ void __launch_bounds__(MAXT) resid_epi_kernel(ResidArgs a) {
   pdl_launch_dependents();
   const int b = blockIdx.x;
-  if (b >= a.B) return;
+  if (b >= a.B || a.meta.get(kMetaPos, b) < 0) return;   // inactive lane
   __shared__ float red[32];
   const int H = a.H, H4 = H / 4;
   const float4 z = make_float4(0.f, 0.f, 0.f, 0.f), one = make_float4(1.f, 1.f, 1.f, 1.f);
@@ -354,6 +357,7 @@ __global__ void qkv_epi_kernel(QkvArgs a) {
   extern __shared__ float row[];
   __shared__ float red[32];
   const int b = blockIdx.x;
+  if (a.meta.get(kMetaPos, b) < 0) return;   // inactive lane
   const int qd = a.nh * a.hd, kd = a.nkv * a.hd, D = qd + 2 * kd;
   const bool tp = a.q_norm_w && a.tp.ranks > 1;
   if (tp && a.tp_phase == 2 && !tp_wait(a.tp, kTpSlotQk, a.err)) return;
@@ -515,6 +519,7 @@ __global__ void __launch_bounds__(kAttnThreads, FORM + 2) attn_kernel(AttnArgs a
   // starts; otherwise the update only appends each lane's new position,
   // which this kernel takes from the metadata.
   const int b = blockIdx.x, g = blockIdx.y, c = blockIdx.z;
+  if (!a.lane_len && a.meta.get(kMetaPos, b) < 0) return;   // inactive lane
   const int T = a.lane_len ? a.lane_len[b] : a.meta.get(kMetaPos, b) + 1;
   // the grid holds one CTA per chunk of the call's longest timeline
   if (T < 1 || T > a.max_ctx || (T + kAttnChunk - 1) / kAttnChunk > (int)gridDim.z) {
@@ -868,6 +873,7 @@ __global__ void raven_init_kernel(Meta meta, int H, const float* __restrict__ h,
   pdl_launch_dependents();
   pdl_wait();
   const int b = blockIdx.x;
+  if (meta.get(kMetaPos, b) < 0) return;   // inactive lane
   const int so = meta.get(kMetaStateOut, b);
   if (so < 0 || so >= bank_rows) {
     if (threadIdx.x == 0) atomicExch(err, kDevBadIndex);

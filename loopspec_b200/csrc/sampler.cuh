@@ -1,14 +1,21 @@
 // Fused top-p / top-k / temperature sampling and LoopSpec draft verification.
 //
-// One CTA (1024 threads) per readout row does, on the device and without a
-// host round trip:
+// One thread-block cluster of C CTAs (C = min(8, chunks)) per readout row;
+// CTA r owns the vocabulary chunks [r*nch/C, (r+1)*nch/C) of 2048 tokens and
+// keeps its slice of the row in shared memory. Row-wide sums and maxima are
+// block reductions whose per-CTA results every CTA reads from the others'
+// shared memory after a cluster barrier, always in rank order, so every CTA
+// holds the same value and a row's result is a fixed function of the row.
+// On the device and without a host round trip the cluster does:
 //   P = filter(softmax(logits / T)) renormalised (fp32), where top-p keeps
 //       every probability >= the largest value v with sum_{p >= v} p >= top_p
 //       and top-k every probability >= the k-th largest (ties kept; both ->
 //       the larger cutoff), as the reference's sort / cumsum / searchsorted
-//       filter (sampling/distributions.py:14-86). The cutoffs are found by
-//       bisection over fp32 bit patterns (monotone for non-negative floats)
-//       instead of a full sort.
+//       filter (sampling/distributions.py:14-86). Each cutoff is found over
+//       the fp32 bit patterns (monotone for non-negative floats) in 8 passes
+//       of a 17-bin histogram (16 bins of width 2^s over [lo, lo + 2^(s+4))
+//       and one above), each pass narrowing the bracket to one bin, instead of
+//       a full sort.
 //   q1     draw x ~ P; keep P as the lane's q1 distribution (sampler.py:49-102)
 //   q2     r = max(P - Q1, 0), r[x] = 0; draw y ~ r; R = r / sum r; propose y
 //          iff sum r > 0 and P[x] < Q1[x] (sampler.py:178-344)
@@ -17,7 +24,9 @@
 //          the q2 token y iff u1 < min(1, F[y]/R[y]), else draw from
 //          norm(max(F - R, 0)) (or F) with u2 (sampling/rejection.py:42-97)
 // and writes the decision row (token, proposed, accepted_code, q1_rejected,
-// q2_rejected) of policy.py:197-283. Draws invert a CDF in chunks of 2048
+// q2_rejected) of policy.py:197-283. Single probabilities (P[x], F[y]) are
+// recomputed by every CTA from the logits with the slice loops' operations, so
+// every CTA takes the same branch. Draws invert a CDF in chunks of 2048
 // tokens like the reference. Uniforms: words of Philox4x32-10 with counter
 // (cycle, readout row of the request, 0, 0) and the request's seed as key,
 // u = (w >> 8) * 2^-24 (cycle, row and seed come with the row's metadata).
@@ -28,10 +37,11 @@
 
 namespace ls {
 
-constexpr int kSampleThreads = 1024;
+constexpr int kSampleThreads = 512;
 constexpr int kSampleChunk = 2048;
 constexpr int kSampleMaxChunks = 64;        // vocab <= 131072
-constexpr int kSampleSmemVocab = 51200;     // P kept in shared memory up to this vocab
+constexpr int kSampleCtas = 8;              // CTAs per row (one portable cluster) at most
+constexpr int kSampleBins = 16;             // cutoff search: bins per pass (plus one above)
 
 struct SampleParams {
   float temperature;
@@ -50,40 +60,97 @@ struct SampleArgs {
   float* q1_bank;               // [bank_rows][V] lane q1 distributions, by state slot
   float* r_bank;                // [bank_rows][V] lane q2 residual distributions
   int bank_rows;
-  float* work;                  // [rows][2][V] scratch (P when it does not fit smem, and W)
   long long* decisions;         // [rows][5]
   int* err;
 };
+
+// Vocabulary split of a row over its cluster (host and device agree).
+__host__ __device__ inline int sample_chunks(int V) { return (V + kSampleChunk - 1) / kSampleChunk; }
+__host__ __device__ inline int sample_ctas(int V) {
+  const int n = sample_chunks(V);
+  return n < kSampleCtas ? n : kSampleCtas;
+}
+__host__ __device__ inline int sample_chunk0(int nch, int C, int r) { return (int)((long)r * nch / C); }
+// Dynamic shared memory: the P and W slices and the per-thread histogram.
+inline size_t sample_smem_bytes(int V) {
+  const int nch = sample_chunks(V), C = sample_ctas(V);
+  const int per = (nch + C - 1) / C * kSampleChunk;
+  return (size_t)(2 * per + (kSampleBins + 1) * kSampleThreads) * sizeof(float);
+}
 
 __device__ __forceinline__ uint4 philox_words(unsigned long long seed, uint32_t c0, uint32_t c1) {
   return philox4x32_10(make_uint4(c0, c1, 0u, 0u), (uint32_t)seed, (uint32_t)(seed >> 32));
 }
 
-// Deterministic block reductions over 1024 threads (fixed tree).
-__device__ __forceinline__ float sblock_sum(float v, float* red) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  v = warp_sum(v);
-  __syncthreads();
-  if (lane == 0) red[warp] = v;
-  __syncthreads();
-  float t = lane < (int)(blockDim.x >> 5) ? red[lane] : 0.f;
-  return warp_sum(t);
+// ------------------------------------------------ cluster helpers (PTX ISA 7.8+)
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
 }
 
-__device__ __forceinline__ float sblock_max(float v, float* red) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  v = warp_max(v);
+// Every thread of every CTA of the cluster; orders shared-memory writes before
+// it against reads by any CTA after it.
+__device__ __forceinline__ void cluster_barrier() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Load a float from CTA `rank`'s copy of a shared-memory variable.
+__device__ __forceinline__ float ld_cluster(const float* p, uint32_t rank) {
+  const uint32_t a = (uint32_t)__cvta_generic_to_shared(p);
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(rank));
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(r) : "memory");
+  return v;
+}
+
+struct SampleShared {
+  float red[32 * 2];                 // warp partials of cluster reductions
+  float xch[2][32];                  // this CTA's values read by the cluster (double buffered)
+  float tot[32];                     // cluster totals
+  float ctot[kSampleMaxChunks];      // this CTA's chunk totals
+  float all[kSampleMaxChunks];       // every chunk total of the row
+  float rem;
+  int ch, tok;
+};
+
+// Row-wide sum (or max) of NV per-thread values; every thread of every CTA
+// returns the same totals. `ph` alternates the exchange buffer: a CTA writes
+// buffer ph again only after the next barrier, which every reader of the
+// previous use has passed after its reads.
+template <int NV, bool MAX>
+__device__ __forceinline__ void cl_reduce(float (&v)[NV], SampleShared& sh, int C, int& ph) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const float w = MAX ? warp_max(v[i]) : warp_sum(v[i]);
+    if (lane == 0) sh.red[warp * NV + i] = w;
+  }
   __syncthreads();
-  if (lane == 0) red[warp] = v;
+  if (threadIdx.x < NV) {
+    float t = MAX ? -INFINITY : 0.f;
+    for (int w = 0; w < nw; ++w) t = MAX ? fmaxf(t, sh.red[w * NV + threadIdx.x]) : t + sh.red[w * NV + threadIdx.x];
+    sh.xch[ph][threadIdx.x] = t;
+  }
+  cluster_barrier();
+  if (threadIdx.x < NV) {
+    float t = MAX ? -INFINITY : 0.f;
+    for (int r = 0; r < C; ++r) {
+      const float x = ld_cluster(&sh.xch[ph][threadIdx.x], (uint32_t)r);
+      t = MAX ? fmaxf(t, x) : t + x;
+    }
+    sh.tot[threadIdx.x] = t;
+  }
   __syncthreads();
-  float t = lane < (int)(blockDim.x >> 5) ? red[lane] : -INFINITY;
-  return warp_max(t);
+#pragma unroll
+  for (int i = 0; i < NV; ++i) v[i] = sh.tot[i];
+  ph ^= 1;
 }
 
 // Row loops visit E consecutive elements per step (E = 4 when V % 4 == 0: one
 // 16-byte load or store per step, else 1): thread tid takes steps tid,
-// tid + blockDim.x, ... and, within a step, elements in index order. A row's
-// sums are therefore a fixed function of the row.
+// tid + blockDim.x, ... and, within a step, elements in index order.
 template <int E>
 struct Vf {
   float v[E];
@@ -110,32 +177,67 @@ __device__ __forceinline__ void stv(float* p, int j, const Vf<E>& x) {
   else p[j] = x.v[0];
 }
 
-// Largest value v (an element of p) with F(v) >= target, F(v) = sum or count
-// of the elements >= v, found by bisection over the bit patterns in [0, max].
+// Largest bit pattern v with F(v) >= target, F(v) = sum (or count) of the
+// row's elements >= v (p <= 1 for every element, so [0, 2^30) brackets every
+// pattern). Each pass histograms this CTA's slice over 16 bins of width 2^s
+// starting at lo plus one bin above (per-thread columns of `hist`, summed in
+// a fixed order), adds the cluster's bins, and keeps the highest bin whose
+// suffix sum reaches the target; s goes 26, 22, ..., 2, 0.
 template <bool COUNT, int E>
-__device__ float bisect_cutoff(const float* p, int V, float target, float pmax, float* red) {
-  uint32_t lo = 0u, hi = __float_as_uint(pmax) + 1u;   // F(lo) >= target > F(hi)
-  while (hi - lo > 1u) {
-    const uint32_t mid = lo + (hi - lo) / 2u;
-    const float v = __uint_as_float(mid);
-    float acc = 0.f;
-#pragma unroll 4
-    for (int j = threadIdx.x; j < V / E; j += blockDim.x) {
-      const Vf<E> x = ldv<E>(p, j);
+__device__ float cl_cutoff(const float* P, int n, float target, float* hist, SampleShared& sh, int C,
+                           int& ph) {
+  const int tid = threadIdx.x, nt = blockDim.x, lane = tid & 31, warp = tid >> 5, nw = nt >> 5;
+  uint32_t lo = 0u;
+  int s = 26;
+  for (;;) {
 #pragma unroll
-      for (int i = 0; i < E; ++i)
-        if (x.v[i] >= v) acc += COUNT ? 1.f : x.v[i];
+    for (int i = 0; i <= kSampleBins; ++i) hist[i * nt + tid] = 0.f;
+    for (int j = tid; j < n / E; j += nt) {
+      const Vf<E> x = ldv<E>(P, j);
+#pragma unroll
+      for (int i = 0; i < E; ++i) {
+        const uint32_t b = __float_as_uint(x.v[i]);
+        if (b >= lo) {
+          const uint32_t d = min((b - lo) >> s, (uint32_t)kSampleBins);
+          hist[d * nt + tid] += COUNT ? 1.f : x.v[i];
+        }
+      }
     }
-    const float tot = sblock_sum(acc, red);
-    if (tot >= target) lo = mid;
-    else hi = mid;
+    __syncthreads();
+    for (int bin = warp; bin <= kSampleBins; bin += nw) {
+      float t = 0.f;
+      for (int j = lane; j < nt; j += 32) t += hist[bin * nt + j];
+      t = warp_sum(t);
+      if (lane == 0) sh.xch[ph][bin] = t;
+    }
+    cluster_barrier();
+    if (tid <= kSampleBins) {
+      float t = 0.f;
+      for (int r = 0; r < C; ++r) t += ld_cluster(&sh.xch[ph][tid], (uint32_t)r);
+      sh.tot[tid] = t;
+    }
+    __syncthreads();
+    ph ^= 1;
+    float g = sh.tot[kSampleBins];
+    int pick = 0;
+    for (int i = kSampleBins - 1; i >= 0; --i) {
+      g += sh.tot[i];
+      if (g >= target) {
+        pick = i;
+        break;
+      }
+    }
+    lo += (uint32_t)pick << s;
+    if (s == 0) break;
+    s = s >= 4 ? s - 4 : 0;
   }
   return __uint_as_float(lo);
 }
 
-// Inverse-CDF draw from non-negative weights w (need not be normalised).
-// target = u * total; first 2048-chunk whose inclusive CDF exceeds target, then
-// the first token of it whose inclusive CDF exceeds target - preceding mass.
+// Inverse-CDF draw from non-negative weights w (need not be normalised) over
+// the whole row: target = u * total; the first 2048-chunk whose inclusive CDF
+// exceeds target, then the first token of it whose inclusive CDF exceeds
+// target - preceding mass.
 //
 // A chunk is walked as 64 rows of 32 consecutive tokens, one token per lane
 // (consecutive lanes read consecutive words: no shared-memory bank conflicts),
@@ -152,15 +254,16 @@ __device__ __forceinline__ float warp_incl_scan(float x) {
   return x;
 }
 
-__device__ __forceinline__ float chunk_total(const float* w, int c, int V) {
+// Total of local chunk lc of a slice of n elements.
+__device__ __forceinline__ float chunk_total(const float* w, int lc, int n) {
   const int lane = threadIdx.x & 31;
   float tot = 0.f;
   for (int i0 = 0; i0 < kSampleChunk / 32; i0 += 8) {
     float x[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      const int t = c * kSampleChunk + (i0 + j) * 32 + lane;
-      x[j] = t < V ? w[t] : 0.f;
+      const int t = lc * kSampleChunk + (i0 + j) * 32 + lane;
+      x[j] = t < n ? w[t] : 0.f;
     }
 #pragma unroll
     for (int j = 0; j < 8; ++j) tot += __shfl_sync(0xffffffffu, warp_incl_scan(x[j]), 31);
@@ -168,39 +271,48 @@ __device__ __forceinline__ float chunk_total(const float* w, int c, int V) {
   return tot;
 }
 
-__device__ int block_pick(const float* w, int V, float u, float* s_chunk, float* red, int* s_idx) {
+// Returns the drawn token in the CTA that owns its chunk and -1 in the others.
+// w: this CTA's slice (chunks [c0, c1), n elements).
+__device__ int cl_pick(const float* w, int n, int c0, int c1, int nch, int C, float u, SampleShared& sh) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  const int nch = (V + kSampleChunk - 1) / kSampleChunk;
-  for (int c = warp; c < nch; c += nw) {          // one warp per chunk
-    const float a = chunk_total(w, c, V);
-    if (lane == 0) s_chunk[c] = a;
+  for (int c = c0 + warp; c < c1; c += nw) {          // one warp per chunk
+    const float a = chunk_total(w, c - c0, n);
+    if (lane == 0) sh.ctot[c - c0] = a;
+  }
+  cluster_barrier();
+  if ((int)threadIdx.x < nch) {
+    const int c = threadIdx.x;
+    int r = 0;
+    while (r + 1 < C && sample_chunk0(nch, C, r + 1) <= c) ++r;
+    sh.all[c] = ld_cluster(&sh.ctot[c - sample_chunk0(nch, C, r)], (uint32_t)r);
   }
   __syncthreads();
   if (threadIdx.x == 0) {
     float total = 0.f;
-    for (int c = 0; c < nch; ++c) total += s_chunk[c];
+    for (int c = 0; c < nch; ++c) total += sh.all[c];
     const float target = u * total;
     float cdf = 0.f, pre = 0.f;
     int ch = -1;
     for (int c = 0; c < nch; ++c) {
-      if (cdf + s_chunk[c] > target) {
+      if (cdf + sh.all[c] > target) {
         ch = c;
         pre = cdf;
         break;
       }
-      cdf += s_chunk[c];
+      cdf += sh.all[c];
     }
     if (ch < 0) {
       ch = 0;
       pre = 0.f;
     }
-    s_idx[0] = ch;
-    red[0] = target - pre;
+    sh.ch = ch;
+    sh.rem = target - pre;
   }
   __syncthreads();
-  const int ch = s_idx[0];
-  const float rem = red[0];
-  __syncthreads();
+  const int ch = sh.ch;
+  const float rem = sh.rem;
+  if (ch < c0 || ch >= c1) return -1;
+  const int lc = ch - c0;
   if (warp == 0) {
     int found = -1;                                  // nothing exceeds: first token of the chunk
     float pre = 0.f;
@@ -208,8 +320,8 @@ __device__ int block_pick(const float* w, int V, float u, float* s_chunk, float*
       float x[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const int t = ch * kSampleChunk + (i0 + j) * 32 + lane;
-        x[j] = t < V ? w[t] : 0.f;
+        const int t = lc * kSampleChunk + (i0 + j) * 32 + lane;
+        x[j] = t < n ? w[t] : 0.f;
       }
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
@@ -221,175 +333,195 @@ __device__ int block_pick(const float* w, int V, float u, float* s_chunk, float*
         }
       }
     }
-    if (lane == 0) s_idx[1] = found >= 0 ? found : ch * kSampleChunk;
+    if (lane == 0) sh.tok = found >= 0 ? found : ch * kSampleChunk;
   }
   __syncthreads();
-  const int r = s_idx[1];
-  __syncthreads();
-  return r;
+  return sh.tok;
 }
 
-template <bool SMEM_P, int E>
+__device__ __forceinline__ void put_decision(long long* d, long long t, long long a, long long b, long long c,
+                                             long long e) {
+  d[0] = t;
+  d[1] = a;
+  d[2] = b;
+  d[3] = c;
+  d[4] = e;
+}
+
+// grid = rows x C CTAs, cluster (C, 1, 1), kSampleThreads threads,
+// sample_smem_bytes(V) of dynamic shared memory.
+template <int E>
 __global__ void __launch_bounds__(kSampleThreads) sample_kernel(SampleArgs a) {
   pdl_launch_dependents();
   pdl_wait();
-  extern __shared__ __align__(16) float s_p[];
-  __shared__ float red[32];
-  __shared__ float s_chunk[kSampleMaxChunks];
-  __shared__ int s_idx[2];
-  const int row = blockIdx.x;
-  const int V = a.V;
+  extern __shared__ __align__(16) float s_dyn[];
+  __shared__ SampleShared sh;
+  const int V = a.V, nch = sample_chunks(V), C = sample_ctas(V);
+  const int rank = (int)cluster_rank();
+  const int row = blockIdx.x / C;
+  const int mrow = a.meta_row0 + row;
+  // every CTA of a cluster reads the same metadata, so these exits are
+  // cluster-uniform and come before the first cluster barrier
+  if (a.meta.get(kMetaPos, mrow) < 0) return;   // inactive lane
   const SampleParams prm = *a.params;
-  const int kind = a.meta.get(kMetaKind, a.meta_row0 + row);
-  const int first = a.meta.get(kMetaFirst, a.meta_row0 + row);
-  const int second = a.meta.get(kMetaSecond, a.meta_row0 + row);
-  const int slot = a.meta.get(kMetaStateIn, a.meta_row0 + row);
-  const uint32_t cycle = (uint32_t)a.meta.get(kMetaCycle, a.meta_row0 + row);
-  float* P = SMEM_P ? s_p : a.work + (long)row * 2 * V;
-  float* W = a.work + (long)row * 2 * V + V;
-  const float* lg = a.logits + (long)row * V;
+  const int kind = a.meta.get(kMetaKind, mrow);
+  const int first = a.meta.get(kMetaFirst, mrow);
+  const int second = a.meta.get(kMetaSecond, mrow);
+  const int slot = a.meta.get(kMetaStateIn, mrow);
+  const uint32_t cycle = (uint32_t)a.meta.get(kMetaCycle, mrow);
   const bool need_bank = kind == 0 || kind == 1 || first >= 0;
-  if (need_bank && (slot < 0 || slot >= a.bank_rows)) {
-    if (threadIdx.x == 0) atomicExch(a.err, kDevBadIndex);
+  if ((need_bank && (slot < 0 || slot >= a.bank_rows)) || first >= V || second >= V ||
+      (kind == 1 && first < 0)) {
+    if (rank == 0 && threadIdx.x == 0) atomicExch(a.err, kDevBadIndex);
     return;
   }
-  if ((first >= V) || (second >= V) || ((kind == 1) && first < 0)) {
-    if (threadIdx.x == 0) atomicExch(a.err, kDevBadIndex);
-    return;
-  }
+  const int c0 = sample_chunk0(nch, C, rank), c1 = sample_chunk0(nch, C, rank + 1);
+  const int n0 = c0 * kSampleChunk;
+  const int n = min(c1 * kSampleChunk, V) - n0;
+  const int per = (nch + C - 1) / C * kSampleChunk;
+  float* P = s_dyn;
+  float* W = s_dyn + per;
+  float* hist = s_dyn + 2 * per;
+  const float* lg_row = a.logits + (long)row * V;
+  const float* lg = lg_row + n0;
+  long long* dec = a.decisions + (long)row * 5;
+  int ph = 0;
 
   // softmax(logits / T) in fp32
-  const int NV = V / E, tid = threadIdx.x, nt = blockDim.x;
+  const int NV = n / E, tid = threadIdx.x, nt = blockDim.x;
   const float invT = 1.f / prm.temperature;
-  float m = -INFINITY;
+  float m[1] = {-INFINITY};
 #pragma unroll 4
   for (int j = tid; j < NV; j += nt) {
     const Vf<E> x = ldv<E>(lg, j);
 #pragma unroll
-    for (int i = 0; i < E; ++i) m = fmaxf(m, x.v[i] * invT);
+    for (int i = 0; i < E; ++i) m[0] = fmaxf(m[0], x.v[i] * invT);
   }
-  m = sblock_max(m, red);
-  float s = 0.f;
+  cl_reduce<1, true>(m, sh, C, ph);
+  float s[1] = {0.f};
 #pragma unroll 4
   for (int j = tid; j < NV; j += nt) {
     Vf<E> x = ldv<E>(lg, j);
 #pragma unroll
     for (int i = 0; i < E; ++i) {
-      x.v[i] = expf(x.v[i] * invT - m);
-      s += x.v[i];
+      x.v[i] = expf(fmaf(x.v[i], invT, -m[0]));
+      s[0] += x.v[i];
     }
     stv<E>(P, j, x);
   }
-  s = sblock_sum(s, red);
-  float pmax = 0.f;
+  cl_reduce<1, false>(s, sh, C, ph);
 #pragma unroll 4
   for (int j = tid; j < NV; j += nt) {
     Vf<E> x = ldv<E>(P, j);
 #pragma unroll
-    for (int i = 0; i < E; ++i) {
-      x.v[i] = x.v[i] / s;
-      pmax = fmaxf(pmax, x.v[i]);
-    }
+    for (int i = 0; i < E; ++i) x.v[i] = x.v[i] / s[0];
     stv<E>(P, j, x);
   }
-  pmax = sblock_max(pmax, red);
+  __syncthreads();
   // top-k / top-p cutoffs, then renormalise over the kept support
   const int k = prm.top_k >= V ? 0 : prm.top_k;
-  if (k > 0 || prm.top_p < 1.f) {
-    float cut = 0.f;
-    if (prm.top_p < 1.f) cut = bisect_cutoff<false, E>(P, V, prm.top_p, pmax, red);
-    if (k > 0) cut = fmaxf(cut, bisect_cutoff<true, E>(P, V, (float)k, pmax, red));
-    float kept = 0.f;
+  const bool cutting = k > 0 || prm.top_p < 1.f;
+  float cut = 0.f, kept[1] = {1.f};
+  if (cutting) {
+    if (prm.top_p < 1.f) cut = cl_cutoff<false, E>(P, n, prm.top_p, hist, sh, C, ph);
+    if (k > 0) cut = fmaxf(cut, cl_cutoff<true, E>(P, n, (float)k, hist, sh, C, ph));
+    kept[0] = 0.f;
 #pragma unroll 4
     for (int j = tid; j < NV; j += nt) {
       Vf<E> x = ldv<E>(P, j);
 #pragma unroll
       for (int i = 0; i < E; ++i) {
         x.v[i] = x.v[i] >= cut ? x.v[i] : 0.f;
-        kept += x.v[i];
+        kept[0] += x.v[i];
       }
       stv<E>(P, j, x);
     }
-    kept = sblock_sum(kept, red);
+    cl_reduce<1, false>(kept, sh, C, ph);
 #pragma unroll 4
     for (int j = tid; j < NV; j += nt) {
       Vf<E> x = ldv<E>(P, j);
 #pragma unroll
-      for (int i = 0; i < E; ++i) x.v[i] = x.v[i] / kept;
+      for (int i = 0; i < E; ++i) x.v[i] = x.v[i] / kept[0];
       stv<E>(P, j, x);
     }
   }
   __syncthreads();
+  // P of one token, by the slice loops' operations (same bits in every CTA)
+  auto prob = [&](int t) {
+    float p = expf(fmaf(lg_row[t], invT, -m[0])) / s[0];
+    if (cutting) {
+      p = p >= cut ? p : 0.f;
+      p = p / kept[0];
+    }
+    return p;
+  };
 
   // the request's stream: its seed, cycle counter and readout row
-  const unsigned long long seed =
-      (unsigned long long)(uint32_t)a.meta.get(kMetaSeedLo, a.meta_row0 + row) |
-      ((unsigned long long)(uint32_t)a.meta.get(kMetaSeedHi, a.meta_row0 + row) << 32);
-  const uint32_t draw_row = (uint32_t)a.meta.get(kMetaDrawRow, a.meta_row0 + row);
+  const unsigned long long seed = (unsigned long long)(uint32_t)a.meta.get(kMetaSeedLo, mrow) |
+                                  ((unsigned long long)(uint32_t)a.meta.get(kMetaSeedHi, mrow) << 32);
+  const uint32_t draw_row = (uint32_t)a.meta.get(kMetaDrawRow, mrow);
   const uint4 w4 = philox_words(seed, cycle, draw_row);
   const float u0 = (float)(w4.x >> 8) * (1.f / 16777216.f);
   const float u1 = (float)(w4.y >> 8) * (1.f / 16777216.f);
   const float u2 = (float)(w4.z >> 8) * (1.f / 16777216.f);
-  long long d[5] = {0, 0, 0, 0, 0};
+  const bool lead = threadIdx.x == 0;
 
   if (kind == 0) {                                     // q1: draw and keep P
-    float* q1 = a.q1_bank + (long)slot * V;
+    float* q1 = a.q1_bank + (long)slot * V + n0;
 #pragma unroll 4
     for (int j = tid; j < NV; j += nt) stv<E>(q1, j, ldv<E>(P, j));
-    d[0] = block_pick(P, V, u0, s_chunk, red, s_idx);
-    d[1] = 1;
+    const int x = cl_pick(P, n, c0, c1, nch, C, u0, sh);
+    if (x >= 0 && lead) put_decision(dec, x, 1, 0, 0, 0);
   } else if (kind == 1) {                              // q2: conditional residual
     const float* q1 = a.q1_bank + (long)slot * V;
-    float mass = 0.f;
+    float mass[1] = {0.f};
 #pragma unroll 4
     for (int j = tid; j < NV; j += nt) {
-      const Vf<E> p = ldv<E>(P, j), q = ldv<E>(q1, j);
+      const Vf<E> p = ldv<E>(P, j), q = ldv<E>(q1 + n0, j);
       Vf<E> r;
 #pragma unroll
       for (int i = 0; i < E; ++i) {
-        r.v[i] = j * E + i == first ? 0.f : fmaxf(p.v[i] - q.v[i], 0.f);
-        mass += r.v[i];
+        r.v[i] = n0 + j * E + i == first ? 0.f : fmaxf(p.v[i] - q.v[i], 0.f);
+        mass[0] += r.v[i];
       }
       stv<E>(W, j, r);
     }
-    mass = sblock_sum(mass, red);
-    const int y = block_pick(W, V, u0, s_chunk, red, s_idx);
-    float* R = a.r_bank + (long)slot * V;
+    cl_reduce<1, false>(mass, sh, C, ph);
+    float* R = a.r_bank + (long)slot * V + n0;
 #pragma unroll 4
     for (int j = tid; j < NV; j += nt) {
       Vf<E> r = ldv<E>(W, j);
 #pragma unroll
-      for (int i = 0; i < E; ++i) r.v[i] = mass > 0.f ? r.v[i] / mass : 0.f;
+      for (int i = 0; i < E; ++i) r.v[i] = mass[0] > 0.f ? r.v[i] / mass[0] : 0.f;
       stv<E>(R, j, r);
     }
-    const int action = mass > 0.f && P[first] < q1[first];
-    d[0] = action ? y : first;
-    d[1] = action;
-    d[2] = action;
+    const bool action = mass[0] > 0.f && prob(first) < q1[first];
+    const int y = cl_pick(W, n, c0, c1, nch, C, u0, sh);
+    if (y >= 0 && lead) put_decision(dec, action ? y : first, action, action, 0, 0);
   } else if (first < 0) {                              // final without a proposal
-    d[0] = block_pick(P, V, u0, s_chunk, red, s_idx);
+    const int x = cl_pick(P, n, c0, c1, nch, C, u0, sh);
+    if (x >= 0 && lead) put_decision(dec, x, 0, 0, 0, 0);
   } else {                                             // final verification
     const float* q1 = a.q1_bank + (long)slot * V;
-    const float acc = fminf(1.f, P[first] / q1[first]);
+    const float acc = fminf(1.f, prob(first) / q1[first]);
     if (u0 < acc) {
-      d[0] = first;
-      d[2] = 1;
+      if (rank == 0 && lead) put_decision(dec, first, 0, 1, 0, 0);
     } else {
-      float mF = 0.f, mP = 0.f;
+      float mFP[2] = {0.f, 0.f};
 #pragma unroll 4
       for (int j = tid; j < NV; j += nt) {
-        const Vf<E> p = ldv<E>(P, j), q = ldv<E>(q1, j);
+        const Vf<E> p = ldv<E>(P, j), q = ldv<E>(q1 + n0, j);
         Vf<E> f;
 #pragma unroll
         for (int i = 0; i < E; ++i) {
           f.v[i] = fmaxf(p.v[i] - q.v[i], 0.f);
-          mF += f.v[i];
-          mP += p.v[i];
+          mFP[0] += f.v[i];
+          mFP[1] += p.v[i];
         }
         stv<E>(W, j, f);
       }
-      mF = sblock_sum(mF, red);
-      mP = sblock_sum(mP, red);
+      cl_reduce<2, false>(mFP, sh, C, ph);
+      const float mF = mFP[0], mP = mFP[1];
 #pragma unroll 4
       for (int j = tid; j < NV; j += nt) {
         Vf<E> f = ldv<E>(W, j);
@@ -402,38 +534,39 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(SampleArgs a) {
       bool acc2 = false;
       if (second >= 0) {
         const float* R = a.r_bank + (long)slot * V;
-        acc2 = u1 < fminf(1.f, W[second] / R[second]);
-        float mG = 0.f;
+        const float ps = prob(second);
+        const float fs = mF > 0.f ? fmaxf(ps - q1[second], 0.f) / mF : ps / (mP > 0.f ? mP : 1.f);
+        acc2 = u1 < fminf(1.f, fs / R[second]);
+        float mG[1] = {0.f};
 #pragma unroll 4
         for (int j = tid; j < NV; j += nt) {
-          const Vf<E> f = ldv<E>(W, j), r = ldv<E>(R, j);
+          const Vf<E> f = ldv<E>(W, j), r = ldv<E>(R + n0, j);
 #pragma unroll
-          for (int i = 0; i < E; ++i) mG += fmaxf(f.v[i] - r.v[i], 0.f);
+          for (int i = 0; i < E; ++i) mG[0] += fmaxf(f.v[i] - r.v[i], 0.f);
         }
-        mG = sblock_sum(mG, red);
-        if (mG > 0.f) {
+        cl_reduce<1, false>(mG, sh, C, ph);
+        if (mG[0] > 0.f) {
 #pragma unroll 4
           for (int j = tid; j < NV; j += nt) {
             Vf<E> f = ldv<E>(W, j);
-            const Vf<E> r = ldv<E>(R, j);
+            const Vf<E> r = ldv<E>(R + n0, j);
 #pragma unroll
-            for (int i = 0; i < E; ++i) f.v[i] = fmaxf(f.v[i] - r.v[i], 0.f) / mG;
+            for (int i = 0; i < E; ++i) f.v[i] = fmaxf(f.v[i] - r.v[i], 0.f) / mG[0];
             stv<E>(W, j, f);
           }
         }
         __syncthreads();
       }
-      const int smp = block_pick(W, V, u2, s_chunk, red, s_idx);
-      d[0] = acc2 ? second : smp;
-      d[2] = acc2 ? 2 : 0;
-      d[3] = 1;
-      d[4] = second >= 0 && !acc2;
+      if (acc2) {
+        if (rank == 0 && lead) put_decision(dec, second, 0, 2, 1, 0);
+      } else {
+        const int x = cl_pick(W, n, c0, c1, nch, C, u2, sh);
+        if (x >= 0 && lead) put_decision(dec, x, 0, 0, 1, second >= 0);
+      }
     }
   }
-  if (threadIdx.x == 0) {
-#pragma unroll
-    for (int i = 0; i < 5; ++i) a.decisions[(long)row * 5 + i] = d[i];
-  }
+  // no CTA leaves while another may still read its shared memory
+  cluster_barrier();
 }
 
 }  // namespace ls

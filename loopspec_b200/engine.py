@@ -32,7 +32,7 @@ class Engine:
     def __init__(self, cfg: ModelConfig, schedule: PipelineSchedule, weights: dict, *,
                  device: int = 0, max_context: int = 4096, max_prompt: int | None = None,
                  kv_slots: int = 0, request_rows: int = 0, use_graphs: bool = True,
-                 use_pdl: bool = True, max_requests: int = 1):
+                 use_pdl: bool = True, max_requests: int = 1, device_loop: bool = True):
         if schedule.stages != cfg.stages:
             raise ValueError("schedule stages must equal the model's recurrence count")
         self.cfg = cfg
@@ -51,7 +51,7 @@ class Engine:
             step_size=schedule.step_size, second_step=schedule.second_step or 0,
             max_context=max_context, max_prompt=max_prompt or max_context // 2,
             kv_slots=kv_slots, request_rows=request_rows, use_graphs=int(use_graphs),
-            use_pdl=int(use_pdl), max_requests=int(max_requests))
+            use_pdl=int(use_pdl), max_requests=int(max_requests), device_loop=int(device_loop))
         handle = ctypes.c_void_p()
         code = self.L.ls_create(ctypes.byref(mc), ctypes.byref(sc), device, ctypes.byref(handle))
         if code != _lib.LS_OK:

@@ -36,6 +36,9 @@ def main():
     p.add_argument("--second", type=int, default=2)
     p.add_argument("--sampling", action="store_true",
                    help="post role: top-p 0.9 sampling decisions instead of greedy argmax")
+    p.add_argument("--decode", type=int, default=0,
+                   help="> 0: after a warm-up request, decode this many greedy LoopSpec tokens inside the "
+                        "NVTX range 'decode' (the device-resident loop when the schedule fits)")
     p.add_argument("--prefill-only", action="store_true",
                    help="time the prefill of a --prompt-token prompt (warm-up run, then one run "
                         "inside the NVTX range 'prefill') instead of a decode role call")
@@ -57,6 +60,19 @@ def main():
         torch.cuda.nvtx.range_pop()
         print(json.dumps({"config": cfg.name, "prompt": a.prompt,
                           "prefill_device_ms": round(st["prefill_device_ms"], 3)}))
+        eng.close()
+        return
+    if a.decode:
+        eng.generate(prompt, a.decode)                  # warm-up (captures the graphs)
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_push("decode")
+        _, st = eng.generate(prompt, a.decode)
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
+        print(json.dumps({"config": cfg.name, "prompt": a.prompt, "tokens": a.decode,
+                          "decode_device_ms": round(st["decode_device_ms"], 3),
+                          "cycles": st["pipeline_cycles"], "host_syncs": st["host_syncs"],
+                          "kernel_launches": st["decode_kernel_launches"]}))
         eng.close()
         return
     eng.prefill(prompt)

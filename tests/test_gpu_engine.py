@@ -14,7 +14,7 @@ import torch
 
 from loopspec_b200.config import get_config
 from loopspec_b200.engine import Engine
-from loopspec_b200.executor import B200Executor
+from loopspec_b200.executor import B200Executor, generate_loopspec
 from loopspec_b200.schedule import PipelineSchedule
 from loopspec_b200.weights import init_random_weights
 from oracle.executor import generate_ar_oracle, teacher_forced_logits
@@ -232,3 +232,57 @@ def test_fused_lm_head_argmax_takes_the_lowest_index_of_equal_maxima(lo, hi):
     assert logits[lo] == logits[hi] == logits[a] == logits.max()
     assert first == min(a, lo, hi)
     eng.close()
+
+
+@pytest.mark.parametrize("name,K,X", [("tiny", 1, 2), ("tiny", 1, None), ("tiny", 2, None),
+                                      ("tiny-raven-llama", 2, 2)])
+def test_device_loop_equals_host_loop(name, K, X):
+    """The device-resident loop (scheduler on the GPU, one graph per cycle, no
+    host round trip between cycles) commits the host loop's tokens and counts
+    the same pipeline events, also when an EOS id ends the request early."""
+    cfg, dev, _ = make(name, K, X)
+    _, host, _ = make(name, K, X, device_loop=False)
+    keys = ("pipeline_cycles", "pre_rows", "recurrent_rows", "post_rows", "verified_proposals",
+            "first_rejections", "second_verifications", "second_acceptances", "second_rejections",
+            "decode_tokens", "core_kv_positions")
+    for seed in range(3):
+        p = prompt_for(cfg, 20 + 7 * seed, seed=seed)
+        a, sa = dev.generate(p, 40)
+        b, sb = host.generate(p, 40)
+        assert a == b
+        for k in keys:
+            assert sa[k] == sb[k], k
+        # the host loop waits for every cycle with a readout, the device loop
+        # only when the launched cycles have run out (a cycle commits at most
+        # one token)
+        assert sb["host_syncs"] >= sb["decode_tokens"]
+        assert sa["host_syncs"] * 4 <= sb["host_syncs"]
+        a2, _ = dev.generate(p, 40, stop_token=b[9])
+        b2, _ = host.generate(p, 40, stop_token=b[9])
+        assert a2 == b2 and a2[-1] == b[9] and len(a2) <= 10
+    dev.close()
+    host.close()
+
+
+@pytest.mark.parametrize("name,K,X", [("tiny", 1, 2), ("tiny-raven-llama", 2, 2)])
+def test_sampled_device_loop_equals_host_loop(name, K, X):
+    """Sampled decoding on the device-resident loop: the sampler's decision
+    rows resolve the pipeline on the GPU, with the host loop's random stream
+    (seed, draw cycle, draw row), so both commit the same tokens and count the
+    same events."""
+    cfg, dev, _ = make(name, K, X)
+    _, host, _ = make(name, K, X, device_loop=False)
+    samp = {"temperature": 0.8, "top_k": 40, "top_p": 0.9}
+    keys = ("pipeline_cycles", "pre_rows", "recurrent_rows", "post_rows", "verified_proposals",
+            "first_rejections", "second_verifications", "second_acceptances", "second_rejections",
+            "decode_tokens")
+    for seed in range(2):
+        p = prompt_for(cfg, 17 + 5 * seed, seed=seed)
+        a, sa = generate_loopspec(dev, p, 32, sampling=samp, seed=1000 + seed)
+        b, sb = generate_loopspec(host, p, 32, sampling=samp, seed=1000 + seed)
+        assert a == b
+        for k in keys:
+            assert sa[k] == sb[k], k
+        assert sa["host_syncs"] * 4 <= sb["host_syncs"]
+    dev.close()
+    host.close()
