@@ -66,6 +66,9 @@ def parse():
                         "over the ranks; prompt lengths uniform in [--prompt-min, --prompt]")
     p.add_argument("--prompt-min", type=int, default=0,
                    help="shortest prompt of a --batch step (0: every prompt has --prompt tokens)")
+    p.add_argument("--host-loop", action="store_true",
+                   help="run LoopSpec cycles from the host (one sync per cycle) instead of the "
+                        "device-resident loop")
     p.add_argument("--tp", action="store_true",
                    help="under torchrun: one request split over the ranks by tensor parallelism "
                         "(heads and MLP columns; strong scaling) instead of one replica per GPU")
@@ -321,7 +324,8 @@ def engine_arm(args):
                              max_prompt=args.prompt)
         del weights
     else:
-        eng = Engine(cfg, sch, weights, device=local, max_context=max_ctx, max_prompt=args.prompt)
+        eng = Engine(cfg, sch, weights, device=local, max_context=max_ctx, max_prompt=args.prompt,
+                     device_loop=not args.host_loop)
 
     def prompt_of(i):
         # under tensor parallelism every rank serves the same request
@@ -370,7 +374,8 @@ def engine_arm(args):
         for k in w2:
             if k.endswith(("post_attention_layernorm.weight", "post_feedforward_layernorm.weight")):
                 w2[k].mul_(args.synthetic_accept)
-        eng2 = Engine(cfg, sch, w2, device=local, max_context=max_ctx, max_prompt=args.prompt)
+        eng2 = Engine(cfg, sch, w2, device=local, max_context=max_ctx, max_prompt=args.prompt,
+                      device_loop=not args.host_loop)
         generate_loopspec(eng2, prompt_of(0), args.new_tokens)
         _, s_ls = generate_loopspec(eng2, prompt_of(1), args.new_tokens)
         _, s_ar = generate_autoregressive(eng2, prompt_of(1), args.new_tokens)

@@ -735,6 +735,7 @@ struct LoopMeta {
   long stride;
   int* post;
   int width;
+  int* active;   // live lanes of the pre, core and post calls (a prefix of each)
 };
 
 // Start of a cycle (thread 0 has planned it into the shared arrays): write
@@ -756,6 +757,11 @@ __device__ inline void loop_plan(LoopSched& s, LoopPlan& p) {   // thread 0
 }
 
 __device__ inline void loop_write_meta(const LoopSched& s, const LoopPlan& p, const LoopMeta& m) {
+  if (threadIdx.x == 0) {
+    m.active[0] = p.n_pre;
+    m.active[1] = p.n_core;
+    m.active[2] = p.n_post;
+  }
   write_meta(m.pre, m.width, p.pre, p.n_pre, p.draw, false, s.seed);
   for (int k = 0; k < s.K; ++k)
     write_meta(m.core + k * m.stride, m.width, p.core + k * kLoopMaxLanes, p.n_core, p.draw, false, s.seed);

@@ -438,9 +438,15 @@ struct ls_engine {
   LoopSched* loop_host = nullptr;   // pinned
   int* loop_meta = nullptr;
   long long* loop_out = nullptr;
-  cudaGraphExec_t loop_graph = nullptr;
-  int loop_graph_kernels = 0, loop_graph_chunks = 0;
-  bool loop_graph_sampling = false;
+  struct LoopGraph {
+    cudaGraphExec_t exec = nullptr;
+    int kernels = 0;
+  };
+  // one cycle's graph per (attention chunks, sampling): key chunks * 2 + sampling
+  std::map<int, LoopGraph> loop_graphs;
+  int attn_form_lanes = 0;   // lanes assumed by the attention form choice (0: the call's width)
+  int* loop_active = nullptr;       // live lanes of the device loop's pre, core, post calls
+  const int* gemm_active = nullptr;  // set while the device loop's calls are captured
   int* meta_host = nullptr;     // pinned [kStaging][F][cap]
   int staging_next = 0;
   static constexpr int kStaging = 64;
@@ -480,8 +486,6 @@ struct ls_engine {
   // (RoPE, pool write) itself. Prefill calls (several positions of one
   // timeline) keep the projection's fused RoPE / KV-write epilogue.
   bool qkv_planes = false;
-  // the call forks a timeline (some lane copies a parent's mapping prefix)
-  bool call_forks = false;
   // attention grid depth of the call being enqueued: one CTA per 128-position
   // chunk of its longest timeline (graphs round it up to an even count and are
   // re-captured when it changes)
@@ -534,7 +538,7 @@ struct ls_engine {
   ~ls_engine() {
     if (device >= 0) cudaSetDevice(device);
     for (auto& g : graphs) cudaGraphExecDestroy(g.second);
-    if (loop_graph) cudaGraphExecDestroy(loop_graph);
+    for (auto& g : loop_graphs) cudaGraphExecDestroy(g.second.exec);
     if (loop_host) cudaFreeHost(loop_host);
     for (void* p : tp_opened) cudaIpcCloseMemHandle(p);
     for (void* p : allocs) cudaFree(p);
@@ -750,6 +754,7 @@ struct ls_engine {
       loop_sched = dalloc<LoopSched>(1);
       CK(cudaMallocHost(&loop_host, sizeof(LoopSched)));
       loop_meta = dalloc<int>((long)(K + 2) * kMetaFields * cap);
+      loop_active = dalloc<int>(3);
       loop_out = dalloc<long long>(max_ctx);
     }
     CK(cudaMallocHost(&meta_host, sizeof(int) * (size_t)kStaging * kMetaFields * cap));
@@ -885,6 +890,7 @@ void gemm(ls_engine& e, const Gemm& g, XBuf& x, const GemmEpi& epi, int kind, in
   cfg.numAttrs = e.sc.use_pdl && !e.serialize_next ? 1 : 0;
   e.serialize_next = false;
   GemmEpi ep = epi;
+  ep.active = e.gemm_active;
   ep.part_ws = e.gemm_part;
   ep.tile_tickets = e.gemm_tickets;
   REQUIRE(splits == 1 || (long)cfg.gridDim.x * cfg.gridDim.z <= e.gemm_ticket_count, LS_EINVAL,
@@ -970,11 +976,11 @@ void klaunch_cluster(ls_engine& e, void (*kernel)(KArgs...), dim3 grid, dim3 blo
 
 void map_update(ls_engine& e, Meta meta, int n) {
   klaunch(e, map_update_kernel, dim3(n), dim3(128), 0, meta, n, e.map, e.max_ctx, e.rows, e.err_dev);
-  // attention reads slot ids before its wait: unless the update only appends
-  // each lane's new position and every attention layer takes it from the
-  // metadata (decode form, no fork, no QK-norm layer), later kernels start
-  // after it has completed
-  e.serialize_next = e.call_forks || !e.qkv_planes || e.mc.qk_norm != 0;
+  // attention reads slot ids before its wait (a forking lane after it):
+  // unless the update only appends each lane's new position and every
+  // attention layer takes it from the metadata (decode form, no QK-norm
+  // layer), later kernels start after it has completed
+  e.serialize_next = !e.qkv_planes || e.mc.qk_norm != 0;
 }
 
 // Threads of a per-lane row kernel: one float4 column each, at most 1024.
@@ -1020,7 +1026,8 @@ void attention(ls_engine& e, Meta meta, int n, bf16* kp, bf16* vp, const Gemm* p
   }
   const dim3 grid(n, e.NKV, e.attn_chunks), blk(kAttnThreads);
   const int G = e.NH / e.NKV;
-  const int form = attention_form((long)n * e.NKV * e.attn_chunks, e.num_sms);
+  const long form_lanes = e.attn_form_lanes > 0 ? std::min(n, e.attn_form_lanes) : n;
+  const int form = attention_form(form_lanes * e.NKV * e.attn_chunks, e.num_sms);
   if (form == kAttnWide) launch_attention<kAttnWide>(e, grid, blk, G, a);
   else if (form == kAttnMid) launch_attention<kAttnMid>(e, grid, blk, G, a);
   else launch_attention<kAttnVLate>(e, grid, blk, G, a);
@@ -1343,7 +1350,6 @@ void run_role(ls_engine& e, int role, int n, const int* host_meta, bool graphabl
   }
   const int chunks = cdiv(longest, kAttnChunk);
   e.qkv_planes = single;
-  e.call_forks = forks;
   if (!(graphable && e.sc.use_graphs)) {
     e.attn_chunks = std::min(chunks, e.max_chunks);
     enqueue_role(e, role, n, po);
@@ -2028,7 +2034,7 @@ void run_ar(ls_engine& e, std::vector<std::vector<long long>>& committed, std::v
 // max_rows, unused lanes inactive).
 LoopMeta loop_meta_of(const ls_engine& e) {
   const long F = (long)kMetaFields * e.cap;
-  return LoopMeta{e.loop_meta, e.loop_meta + F, F, e.loop_meta + (1 + e.K) * F, e.max_rows};
+  return LoopMeta{e.loop_meta, e.loop_meta + F, F, e.loop_meta + (1 + e.K) * F, e.max_rows, e.loop_active};
 }
 
 // One cycle as one graph: the role calls read the metadata the previous
@@ -2036,37 +2042,41 @@ LoopMeta loop_meta_of(const ls_engine& e) {
 // greedy token, or the sampler writes its decision rows), then the step
 // kernel resolves the decisions, commits, retains branches and plans the next
 // cycle. Nothing returns to the host between cycles.
-void capture_loop_graph(ls_engine& e, int chunks) {
+const ls_engine::LoopGraph& loop_graph_for(ls_engine& e, int chunks) {
+  const int key = chunks * 2 + (e.sampling ? 1 : 0);
+  auto it = e.loop_graphs.find(key);
+  if (it != e.loop_graphs.end()) return it->second;
   const int W = e.max_rows;
   const LoopMeta lm = loop_meta_of(e);
   int* pre = lm.pre;
   int* core = lm.core;
   const long F = lm.stride;
   int* post = lm.post;
-  if (e.loop_graph) {
-    CK(cudaStreamSynchronize(e.stream));
-    CK(cudaGraphExecDestroy(e.loop_graph));
-    e.loop_graph = nullptr;
-  }
   int kernels = 0;
   CK(cudaStreamBeginCapture(e.stream, cudaStreamCaptureModeThreadLocal));
   try {
     e.qkv_planes = true;    // one new position per lane
-    e.call_forks = true;    // forks are decided on the device: order every read after the mapping update
     e.attn_chunks = chunks;
     e.serialize_next = true;   // the first role kernel reads the metadata the step kernel wrote
+    // about half of the fixed-width lanes are live in a typical cycle; the
+    // attention form is chosen for those (every form computes the same values)
+    e.attn_form_lanes = std::max(1, W / 2);
     e.meta_override = pre;
+    e.gemm_active = lm.active;
     enqueue_role(e, kPre, W);
     kernels += e.kernels_in_call;
+    e.gemm_active = lm.active + 1;
     for (int k = 0; k < e.K; ++k) {
       e.meta_override = core + k * F;
       enqueue_role(e, kCore, W);
       kernels += e.kernels_in_call;
     }
     e.meta_override = post;
+    e.gemm_active = lm.active + 2;
     enqueue_role(e, kPost, W);
     kernels += e.kernels_in_call;
     e.meta_override = nullptr;
+    e.gemm_active = nullptr;
     if (e.sampling)
       launch(loop_step_kernel, dim3(1), dim3(kLoopThreads), 0, e.stream, false, e.loop_sched,
              (const long long*)e.dec_dev, 5, e.loop_out, lm);
@@ -2075,19 +2085,22 @@ void capture_loop_graph(ls_engine& e, int chunks) {
              (const long long*)e.amax_dev, 1, e.loop_out, lm);
   } catch (...) {
     e.meta_override = nullptr;
+    e.gemm_active = nullptr;
+    e.attn_form_lanes = 0;
     cudaGraph_t g = nullptr;
     cudaStreamEndCapture(e.stream, &g);
     if (g) cudaGraphDestroy(g);
     throw;
   }
+  e.attn_form_lanes = 0;
   cudaGraph_t g = nullptr;
   CK(cudaStreamEndCapture(e.stream, &g));
-  const cudaError_t ie = cudaGraphInstantiate(&e.loop_graph, g, 0);
+  ls_engine::LoopGraph lg;
+  const cudaError_t ie = cudaGraphInstantiate(&lg.exec, g, 0);
   cudaGraphDestroy(g);
   CK(ie);
-  e.loop_graph_kernels = kernels + 1;
-  e.loop_graph_chunks = chunks;
-  e.loop_graph_sampling = e.sampling;
+  lg.kernels = kernels + 1;
+  return e.loop_graphs.emplace(key, lg).first->second;
 }
 
 const char* loop_error_text(int code) {
@@ -2099,9 +2112,13 @@ const char* loop_error_text(int code) {
   return code > 0 && code < 10 ? names[code] : "unknown";
 }
 
-// One greedy request on the device-resident loop, after its prefill. Since a
-// cycle commits at most one token, the host launches as many cycles as tokens
-// remain, then reads the scheduler state; it repeats until the request is done.
+// One request on the device-resident loop, after its prefill. A cycle commits
+// at most one token, so the host launches a batch of at most as many cycles as
+// tokens remain (64; 16 when an EOS id may end the request early, which
+// bounds the cycles run after it), then reads the scheduler state, and
+// repeats until the request is done. Each batch uses the graph whose
+// attention grid covers the longest timeline the batch can reach: no lane is
+// more than S positions ahead of the committed tokens.
 std::vector<long long> run_device_loop(ls_engine& e, Request& R, long long first, int max_new,
                                        long long stop_token, ls_stats& st, double& decode_t0) {
   LoopSched& h = *e.loop_host;
@@ -2121,17 +2138,19 @@ std::vector<long long> run_device_loop(ls_engine& e, Request& R, long long first
   CK(cudaMemcpyAsync(e.loop_sched, &h, sizeof(LoopSched), cudaMemcpyHostToDevice, e.stream));
   CK(cudaMemcpyAsync(e.loop_out, &first_out, sizeof(long long), cudaMemcpyHostToDevice, e.stream));
   e.h2d_bytes += sizeof(LoopSched) + sizeof(long long);
-  int chunks = cdiv(R.prefill_len + max_new + 1, kAttnChunk);
-  chunks = std::min(chunks + (chunks & 1), e.max_chunks);
-  if (!e.loop_graph || e.loop_graph_chunks != chunks || e.loop_graph_sampling != e.sampling)
-    capture_loop_graph(e, chunks);
   launch(loop_plan_kernel, dim3(1), dim3(kLoopThreads), 0, e.stream, false, e.loop_sched, loop_meta_of(e));
   e.kernel_launches += 1;
   long cycles = 0;
   int committed = 1;
+  const int batch_max = stop_token >= 0 ? 16 : 64;
   for (;;) {
-    for (int i = committed; i < max_new; ++i) CK(cudaGraphLaunch(e.loop_graph, e.stream));
-    cycles += max_new - committed;
+    const int nb = std::min(max_new - committed, batch_max);
+    int chunks = cdiv(R.prefill_len + committed + nb + e.S + 1, kAttnChunk);
+    chunks = std::min(chunks + (chunks & 1), e.max_chunks);
+    const ls_engine::LoopGraph& lg = loop_graph_for(e, chunks);
+    for (int i = 0; i < nb; ++i) CK(cudaGraphLaunch(lg.exec, e.stream));
+    cycles += nb;
+    e.kernel_launches += (long)nb * lg.kernels;
     CK(cudaMemcpyAsync(&h, e.loop_sched, sizeof(LoopSched), cudaMemcpyDeviceToHost, e.stream));
     e.d2h_bytes += sizeof(LoopSched);
     fetch_device_error(e);
@@ -2155,7 +2174,6 @@ std::vector<long long> run_device_loop(ls_engine& e, Request& R, long long first
   st.second_acceptances = h.stats[7];
   st.second_rejections = h.stats[8];
   // every launched cycle streams the weights of all its role calls
-  e.kernel_launches += cycles * e.loop_graph_kernels;
   e.core_calls += cycles * e.K;
   e.post_calls += cycles;
   if (e.mc.n_pre_layers > 0) e.pre_calls += cycles;

@@ -65,6 +65,8 @@ struct GemmEpi {
   int* amax_ticket;           // ... one counter, zero between launches
   long long* amax_out;        // ... each lane's token [lanes]
   long split_stride;          // split store: floats between split planes of out
+  const int* active;          // device-resident loop: number of live lanes of the call (a prefix
+                              // of the n_valid lanes), read at run time; null: all n_valid
 };
 
 // SUB 64-wide sub-tiles per ring stage along K: the MMA thread's per-stage
@@ -204,7 +206,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const bool have = mbar_wait(acc_bar, 0, err, kDevTimeoutAcc);
   tc_fence_after();
   float* red = reinterpret_cast<float*>(smem);
-  const int lanes_here = min(BN / 2, n_valid - n0 / 2);   // lanes of this N tile
+  // live lanes: the epilogue skips the inactive tail of a fixed-width call
+  const int n_live = epi.active ? max(0, min(n_valid, *epi.active)) : n_valid;
+  const int lanes_here = min(BN / 2, n_live - n0 / 2);   // lanes of this N tile
   const long tile_id = (long)blockIdx.z * gridDim.x + blockIdx.x;
   const long split_floats = (long)(BN / 2) * kGemmBM;
   float* tile_part = epi.part_ws + tile_id * splits * split_floats;
@@ -366,7 +370,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     __syncthreads();
     if (!s_final) return;
     // last CTA: reduce every lane over all tiles (L2 loads: other CTAs wrote them)
-    for (int l = warp; l < n_valid; l += kGemmThreads / 32) {
+    for (int l = warp; l < n_live; l += kGemmThreads / 32) {
       float best = -INFINITY;
       int bi = 0x7fffffff;
       for (int t = lane; t < tiles; t += 32) {

@@ -513,11 +513,12 @@ __global__ void __launch_bounds__(kAttnThreads, FORM + 2) attn_kernel(AttnArgs a
   // and the newest position's K/V), load what earlier work wrote: the lane
   // metadata (uploaded before the role call), the timeline's slot ids of the
   // positions older than this call and the K/V rows of those positions. A
-  // call whose mapping update forks a timeline or appends several positions
-  // per timeline (prefill) launches the kernel after the update without
-  // programmatic overlap, so those entries are final before this kernel
-  // starts; otherwise the update only appends each lane's new position,
-  // which this kernel takes from the metadata.
+  // call whose mapping update appends several positions per timeline
+  // (prefill) launches the kernel after the update without programmatic
+  // overlap, so those entries are final before this kernel starts;
+  // otherwise the update copies forked prefixes (read here from the parent's
+  // row) and appends each lane's new position, which this kernel takes from
+  // the metadata.
   const int b = blockIdx.x, g = blockIdx.y, c = blockIdx.z;
   if (!a.lane_len && a.meta.get(kMetaPos, b) < 0) return;   // inactive lane
   const int T = a.lane_len ? a.lane_len[b] : a.meta.get(kMetaPos, b) + 1;
@@ -554,13 +555,19 @@ __global__ void __launch_bounds__(kAttnThreads, FORM + 2) attn_kernel(AttnArgs a
   // projection writes one position per lane; prefill puts several positions
   // of one timeline in a call)
   const int fresh = T - 1 - (a.lane_len ? 0 : a.meta.get(kMetaAhead, b)) - start;
+  // a lane whose timeline this call forks has its prefix copied into its
+  // mapping row by the call's mapping update, which may still be running:
+  // positions of the prefix are read from the parent's row, whose entries
+  // earlier calls wrote
+  const int frow = a.lane_len ? -1 : a.meta.get(kMetaForkRow, b);
+  const int flen = frow >= 0 && frow < a.rows ? a.meta.get(kMetaForkLen, b) : 0;
   int sv = -1;
   if (threadIdx.x < kAttnChunk && (int)threadIdx.x < n_in) {
     // decode form: the new position's slot comes from the lane metadata, so
-    // its mapping entry (appended by this call's mapping update, which may
-    // still be running) is never read
+    // its mapping entry (appended by this call's mapping update) is never read
+    const int t = start + threadIdx.x;
     sv = a.qkv && (int)threadIdx.x == fresh ? a.meta.get(kMetaSlot, b)
-                                            : a.map[(long)row * a.max_ctx + start + threadIdx.x];
+                                            : a.map[(long)(t < flen ? frow : row) * a.max_ctx + t];
   }
   if (threadIdx.x < kAttnChunk) {
     if ((int)threadIdx.x < n_in && (sv < 0 || sv >= a.n_slots)) {

@@ -12,10 +12,10 @@
 //       and top-k every probability >= the k-th largest (ties kept; both ->
 //       the larger cutoff), as the reference's sort / cumsum / searchsorted
 //       filter (sampling/distributions.py:14-86). Each cutoff is found over
-//       the fp32 bit patterns (monotone for non-negative floats) in 8 passes
-//       of a 17-bin histogram (16 bins of width 2^s over [lo, lo + 2^(s+4))
+//       the fp32 bit patterns (monotone for non-negative floats) in 6 passes
+//       of a 33-bin histogram (32 bins of width 2^s over [lo, lo + 2^(s+5))
 //       and one above), each pass narrowing the bracket to one bin, instead of
-//       a full sort.
+//       a full sort; the last pass also gives the kept mass.
 //   q1     draw x ~ P; keep P as the lane's q1 distribution (sampler.py:49-102)
 //   q2     r = max(P - Q1, 0), r[x] = 0; draw y ~ r; R = r / sum r; propose y
 //          iff sum r > 0 and P[x] < Q1[x] (sampler.py:178-344)
@@ -41,7 +41,8 @@ constexpr int kSampleThreads = 512;
 constexpr int kSampleChunk = 2048;
 constexpr int kSampleMaxChunks = 64;        // vocab <= 131072
 constexpr int kSampleCtas = 8;              // CTAs per row (one portable cluster) at most
-constexpr int kSampleBins = 16;             // cutoff search: bins per pass (plus one above)
+constexpr int kSampleBins = 32;             // cutoff search: bins per pass (plus one above)
+constexpr int kSampleBinShift = 5;          // log2(kSampleBins)
 
 struct SampleParams {
   float temperature;
@@ -107,8 +108,8 @@ __device__ __forceinline__ float ld_cluster(const float* p, uint32_t rank) {
 
 struct SampleShared {
   float red[32 * 2];                 // warp partials of cluster reductions
-  float xch[2][32];                  // this CTA's values read by the cluster (double buffered)
-  float tot[32];                     // cluster totals
+  float xch[2][kSampleBins + 1];     // this CTA's values read by the cluster (double buffered)
+  float tot[kSampleBins + 1];        // cluster totals
   float ctot[kSampleMaxChunks];      // this CTA's chunk totals
   float all[kSampleMaxChunks];       // every chunk total of the row
   float rem;
@@ -148,6 +149,48 @@ __device__ __forceinline__ void cl_reduce(float (&v)[NV], SampleShared& sh, int 
   ph ^= 1;
 }
 
+// Online softmax partials (max m, sum of exp(x - m)) merged over the block
+// and the cluster in a fixed order; every thread returns the row's (m, s).
+__device__ __forceinline__ void sm_merge(float& m, float& s, float m2, float s2) {
+  const float mx = fmaxf(m, m2);
+  const float a = m == -INFINITY ? 0.f : s * expf(m - mx);
+  const float b = m2 == -INFINITY ? 0.f : s2 * expf(m2 - mx);
+  m = mx;
+  s = a + b;
+}
+
+__device__ __forceinline__ void cl_softmax_stats(float& m, float& s, SampleShared& sh, int C, int& ph) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, m, o), s2 = __shfl_xor_sync(0xffffffffu, s, o);
+    sm_merge(m, s, m2, s2);
+  }
+  if (lane == 0) {
+    sh.red[warp * 2] = m;
+    sh.red[warp * 2 + 1] = s;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float mm = -INFINITY, ss = 0.f;
+    for (int w = 0; w < nw; ++w) sm_merge(mm, ss, sh.red[w * 2], sh.red[w * 2 + 1]);
+    sh.xch[ph][0] = mm;
+    sh.xch[ph][1] = ss;
+  }
+  cluster_barrier();
+  if (threadIdx.x == 0) {
+    float mm = -INFINITY, ss = 0.f;
+    for (int r = 0; r < C; ++r)
+      sm_merge(mm, ss, ld_cluster(&sh.xch[ph][0], (uint32_t)r), ld_cluster(&sh.xch[ph][1], (uint32_t)r));
+    sh.tot[0] = mm;
+    sh.tot[1] = ss;
+  }
+  __syncthreads();
+  m = sh.tot[0];
+  s = sh.tot[1];
+  ph ^= 1;
+}
+
 // Row loops visit E consecutive elements per step (E = 4 when V % 4 == 0: one
 // 16-byte load or store per step, else 1): thread tid takes steps tid,
 // tid + blockDim.x, ... and, within a step, elements in index order.
@@ -179,16 +222,17 @@ __device__ __forceinline__ void stv(float* p, int j, const Vf<E>& x) {
 
 // Largest bit pattern v with F(v) >= target, F(v) = sum (or count) of the
 // row's elements >= v (p <= 1 for every element, so [0, 2^30) brackets every
-// pattern). Each pass histograms this CTA's slice over 16 bins of width 2^s
+// pattern). Each pass histograms this CTA's slice over 32 bins of width 2^s
 // starting at lo plus one bin above (per-thread columns of `hist`, summed in
 // a fixed order), adds the cluster's bins, and keeps the highest bin whose
-// suffix sum reaches the target; s goes 26, 22, ..., 2, 0.
+// suffix sum reaches the target; s goes 25, 20, ..., 5, 0. `at_cut` receives
+// F at the result (the last pass's suffix sum of bins of width 1).
 template <bool COUNT, int E>
 __device__ float cl_cutoff(const float* P, int n, float target, float* hist, SampleShared& sh, int C,
-                           int& ph) {
+                           int& ph, float* at_cut) {
   const int tid = threadIdx.x, nt = blockDim.x, lane = tid & 31, warp = tid >> 5, nw = nt >> 5;
   uint32_t lo = 0u;
-  int s = 26;
+  int s = 30 - kSampleBinShift;
   for (;;) {
 #pragma unroll
     for (int i = 0; i <= kSampleBins; ++i) hist[i * nt + tid] = 0.f;
@@ -228,8 +272,11 @@ __device__ float cl_cutoff(const float* P, int n, float target, float* hist, Sam
       }
     }
     lo += (uint32_t)pick << s;
-    if (s == 0) break;
-    s = s >= 4 ? s - 4 : 0;
+    if (s == 0) {
+      *at_cut = g;
+      break;
+    }
+    s = s >= kSampleBinShift ? s - kSampleBinShift : 0;
   }
   return __uint_as_float(lo);
 }
@@ -387,34 +434,30 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(SampleArgs a) {
   long long* dec = a.decisions + (long)row * 5;
   int ph = 0;
 
-  // softmax(logits / T) in fp32
+  // softmax(logits / T) in fp32: online (max, sum) per thread, merged over
+  // the row, then P = exp(x / T - max) / sum
   const int NV = n / E, tid = threadIdx.x, nt = blockDim.x;
   const float invT = 1.f / prm.temperature;
-  float m[1] = {-INFINITY};
+  float mx = -INFINITY, sm = 0.f;
 #pragma unroll 4
   for (int j = tid; j < NV; j += nt) {
     const Vf<E> x = ldv<E>(lg, j);
 #pragma unroll
-    for (int i = 0; i < E; ++i) m[0] = fmaxf(m[0], x.v[i] * invT);
+    for (int i = 0; i < E; ++i) {
+      const float y = x.v[i] * invT;
+      if (y > mx) {
+        sm = mx == -INFINITY ? 0.f : sm * expf(mx - y);
+        mx = y;
+      }
+      sm += expf(y - mx);
+    }
   }
-  cl_reduce<1, true>(m, sh, C, ph);
-  float s[1] = {0.f};
+  cl_softmax_stats(mx, sm, sh, C, ph);
 #pragma unroll 4
   for (int j = tid; j < NV; j += nt) {
     Vf<E> x = ldv<E>(lg, j);
 #pragma unroll
-    for (int i = 0; i < E; ++i) {
-      x.v[i] = expf(fmaf(x.v[i], invT, -m[0]));
-      s[0] += x.v[i];
-    }
-    stv<E>(P, j, x);
-  }
-  cl_reduce<1, false>(s, sh, C, ph);
-#pragma unroll 4
-  for (int j = tid; j < NV; j += nt) {
-    Vf<E> x = ldv<E>(P, j);
-#pragma unroll
-    for (int i = 0; i < E; ++i) x.v[i] = x.v[i] / s[0];
+    for (int i = 0; i < E; ++i) x.v[i] = expf(fmaf(x.v[i], invT, -mx)) / sm;
     stv<E>(P, j, x);
   }
   __syncthreads();
@@ -423,32 +466,39 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(SampleArgs a) {
   const bool cutting = k > 0 || prm.top_p < 1.f;
   float cut = 0.f, kept[1] = {1.f};
   if (cutting) {
-    if (prm.top_p < 1.f) cut = cl_cutoff<false, E>(P, n, prm.top_p, hist, sh, C, ph);
-    if (k > 0) cut = fmaxf(cut, cl_cutoff<true, E>(P, n, (float)k, hist, sh, C, ph));
-    kept[0] = 0.f;
+    float mass_p = 0.f, count_k = 0.f;
+    if (prm.top_p < 1.f) cut = cl_cutoff<false, E>(P, n, prm.top_p, hist, sh, C, ph, &mass_p);
+    if (k > 0) {
+      const float ck = cl_cutoff<true, E>(P, n, (float)k, hist, sh, C, ph, &count_k);
+      cut = prm.top_p < 1.f ? fmaxf(cut, ck) : ck;
+    }
+    if (k == 0) {
+      kept[0] = mass_p;   // the top-p pass summed exactly the elements >= cut
+    } else {
+      kept[0] = 0.f;
+#pragma unroll 4
+      for (int j = tid; j < NV; j += nt) {
+        const Vf<E> x = ldv<E>(P, j);
+#pragma unroll
+        for (int i = 0; i < E; ++i) kept[0] += x.v[i] >= cut ? x.v[i] : 0.f;
+      }
+      cl_reduce<1, false>(kept, sh, C, ph);
+    }
 #pragma unroll 4
     for (int j = tid; j < NV; j += nt) {
       Vf<E> x = ldv<E>(P, j);
 #pragma unroll
       for (int i = 0; i < E; ++i) {
         x.v[i] = x.v[i] >= cut ? x.v[i] : 0.f;
-        kept[0] += x.v[i];
+        x.v[i] = x.v[i] / kept[0];
       }
-      stv<E>(P, j, x);
-    }
-    cl_reduce<1, false>(kept, sh, C, ph);
-#pragma unroll 4
-    for (int j = tid; j < NV; j += nt) {
-      Vf<E> x = ldv<E>(P, j);
-#pragma unroll
-      for (int i = 0; i < E; ++i) x.v[i] = x.v[i] / kept[0];
       stv<E>(P, j, x);
     }
   }
   __syncthreads();
   // P of one token, by the slice loops' operations (same bits in every CTA)
   auto prob = [&](int t) {
-    float p = expf(fmaf(lg_row[t], invT, -m[0])) / s[0];
+    float p = expf(fmaf(lg_row[t], invT, -mx)) / sm;
     if (cutting) {
       p = p >= cut ? p : 0.f;
       p = p / kept[0];

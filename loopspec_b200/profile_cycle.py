@@ -39,6 +39,8 @@ def main():
     p.add_argument("--decode", type=int, default=0,
                    help="> 0: after a warm-up request, decode this many greedy LoopSpec tokens inside the "
                         "NVTX range 'decode' (the device-resident loop when the schedule fits)")
+    p.add_argument("--host-loop", action="store_true",
+                   help="with --decode: run the cycles from the host instead of the device-resident loop")
     p.add_argument("--prefill-only", action="store_true",
                    help="time the prefill of a --prompt-token prompt (warm-up run, then one run "
                         "inside the NVTX range 'prefill') instead of a decode role call")
@@ -48,7 +50,7 @@ def main():
     w = init_random_weights(cfg, 0, device="cuda:0", dtype=torch.bfloat16)
     X = a.second // a.first if a.second else None
     eng = Engine(cfg, PipelineSchedule(cfg.stages, a.first, X), w, device=0,
-                 max_context=max(2048, a.prompt + 64), max_prompt=a.prompt)
+                 max_context=max(2048, a.prompt + 64), max_prompt=a.prompt, device_loop=not a.host_loop)
     g = torch.Generator().manual_seed(0)
     prompt = torch.randint(0, cfg.vocab, (a.prompt,), generator=g).tolist()
     if a.prefill_only:
