@@ -44,6 +44,12 @@ enum DsError : int {
   kDsCapacity = 9,         // a fixed table of this state is full
 };
 
+constexpr int pow2_at_least(int n) {
+  int p = 1;
+  while (p < n) p *= 2;
+  return p;
+}
+
 struct DsLane {
   int stage, index, token, state, branch, parent, origin, first, second;
 };
@@ -65,7 +71,7 @@ struct DsFill {
 };
 
 template <int MAXL, int MAXB, int MAXD, int MAXN, int MAXC, int MAXR>
-struct DevSched {
+struct alignas(16) DevSched {
   // schedule and request
   int S, K, X, max_rows, max_new, q1, q2, final_stage;
   int kind_of[MAXD];          // end stage -> 0 q1, 1 q2, 2 final, -1 none
@@ -75,8 +81,12 @@ struct DevSched {
   // pipeline
   int n_lanes;
   DsLane lanes[MAXL];
+  // ancestry: branch -> parent (-1 for the root), an open-addressing table
+  // keyed by branch id (linear probing, -1 = empty; rebuilt whole by
+  // prune_ancestry, so entries are never deleted one by one)
+  static constexpr int kParSlots = pow2_at_least(2 * MAXB);
   int n_par;
-  int par_b[MAXB], par_p[MAXB];   // ancestry: branch -> parent (-1 for the root)
+  int par_key[kParSlots], par_val[kParSlots];
   int next_branch;
   unsigned char state_used[MAXL];
   int committed, done, err;
@@ -139,25 +149,37 @@ struct DevSched {
     return -1;
   }
 
+  // slot of branch b, or of the empty slot where it would go
+  LS_HD int par_slot(int b) const {
+    int h = b & (kParSlots - 1);
+    for (int k = 0; k < kParSlots; ++k, h = (h + 1) & (kParSlots - 1))
+      if (par_key[h] == b || par_key[h] < 0) return h;
+    return -1;   // full (cannot happen: at most MAXB of kParSlots >= 2 MAXB slots are used)
+  }
+
   LS_HD int parent_of(int b) const {
-    for (int i = 0; i < n_par; ++i)
-      if (par_b[i] == b) return par_p[i];
-    return -2;   // unknown branch
+    const int h = b < 0 ? -1 : par_slot(b);
+    return h >= 0 && par_key[h] == b ? par_val[h] : -2;   // -2: unknown branch
   }
 
   LS_HD void set_parent(int b, int p) {
-    for (int i = 0; i < n_par; ++i)
-      if (par_b[i] == b) {
-        par_p[i] = p;
-        return;
-      }
-    if (n_par >= MAXB) {
+    const int h = par_slot(b);
+    if (h >= 0 && par_key[h] == b) {
+      par_val[h] = p;
+      return;
+    }
+    if (h < 0 || n_par >= MAXB) {
       fail(kDsCapacity);
       return;
     }
-    par_b[n_par] = b;
-    par_p[n_par] = p;
+    par_key[h] = b;
+    par_val[h] = p;
     ++n_par;
+  }
+
+  LS_HD void clear_parents() {
+    for (int i = 0; i < kParSlots; ++i) par_key[i] = -1;
+    n_par = 0;
   }
 
   LS_HD int alloc_row() {
@@ -209,7 +231,7 @@ struct DevSched {
     n.live = 1;
     for (int r = 0; r < 3; ++r)
       for (int d = 0; d < MAXD; ++d) n.cur[r][d] = -1;
-    return i;
+    return i;   // (depths >= S stay -1: loops below stop at S)
   }
 
   LS_HD void free_node(int i) {
@@ -232,7 +254,11 @@ struct DevSched {
   }
 
   LS_HD int get_or_create_cursor(int role, int depth, int branch, int parent) {
-    const int n = get_or_create_branch(branch, parent);
+    return cursor_of_node(get_or_create_branch(branch, parent), role, depth);
+  }
+
+  // the cursor of node n's timeline at (role, depth), forked from its parent's
+  LS_HD int cursor_of_node(int n, int role, int depth) {
     if (nodes[n].cur[role][depth] >= 0) return nodes[n].cur[role][depth];
     const int p = nodes[n].parent < 0 ? -1 : node_of(nodes[n].parent);
     if (p < 0 || nodes[p].cur[role][depth] < 0) {
@@ -254,7 +280,7 @@ struct DevSched {
   LS_HD void release_unused(int n) {
     while (n >= 0 && !nodes[n].live && nodes[n].child_count == 0) {
       for (int r = 0; r < 3; ++r)
-        for (int d = 0; d < MAXD; ++d)
+        for (int d = 0; d < S; ++d)
           if (nodes[n].cur[r][d] >= 0) release_cursor(nodes[n].cur[r][d]);
       const int pid = nodes[n].parent;
       free_node(n);
@@ -272,7 +298,7 @@ struct DevSched {
     const int p = node_of(pid);
     if (p < 0 || nodes[p].live || nodes[p].child_count != 1) return;
     for (int r = 0; r < 3; ++r)
-      for (int d = 0; d < MAXD; ++d) {
+      for (int d = 0; d < S; ++d) {
         if (nodes[p].cur[r][d] < 0) continue;
         if (nodes[n].cur[r][d] < 0) {   // the child adopts the parent's timeline
           nodes[n].cur[r][d] = nodes[p].cur[r][d];
@@ -548,11 +574,8 @@ struct DevSched {
       nb[k] = live[k];
       np[k] = live[k] == root ? -1 : parent_of(live[k]);
     }
-    n_par = nl;
-    for (int k = 0; k < nl; ++k) {
-      par_b[k] = nb[k];
-      par_p[k] = np[k];
-    }
+    clear_parents();
+    for (int k = 0; k < nl; ++k) set_parent(nb[k], np[k]);
   }
 
   // ----------------------------------------- one cycle's role metadata
@@ -563,11 +586,15 @@ struct DevSched {
     n_pre = 0;
     n_post = 0;
     int cur[MAXL];
+    // each lane's branch node, found (or created) once for the cycle's calls;
+    // nodes are only created during planning, so the indices stay valid
+    int node[MAXL];
+    for (int i = 0; i < n_lanes; ++i) node[i] = get_or_create_branch(lanes[i].branch, lanes[i].parent);
     for (int i = 0; i < n_lanes; ++i) {
       const DsLane& l = lanes[i];
       if (l.stage != 0) continue;
       DsFill& f = pre[n_pre];
-      cur[n_pre] = has_pre ? get_or_create_cursor(0, 0, l.branch, l.parent) : -1;
+      cur[n_pre] = has_pre ? cursor_of_node(node[i], 0, 0) : -1;
       fill(f, l, cur[n_pre], -1, state_base + l.state);
       ++n_pre;
     }
@@ -576,7 +603,7 @@ struct DevSched {
     for (int off = 0; off < K; ++off) {
       for (int i = 0; i < n_lanes; ++i) {
         const DsLane& l = lanes[i];
-        cur[i] = get_or_create_cursor(1, l.stage + off, l.branch, l.parent);
+        cur[i] = cursor_of_node(node[i], 1, l.stage + off);
         fill(core[off * MAXL + i], l, cur[i], state_base + l.state, state_base + l.state);
         kv_positions += prefill_len + l.index + 1;
       }
@@ -587,7 +614,7 @@ struct DevSched {
       const int end = l.stage + K - 1;
       if (kind_of[end] < 0) continue;
       DsFill& f = post[n_post];
-      cur[n_post] = has_post ? get_or_create_cursor(2, end, l.branch, l.parent) : -1;
+      cur[n_post] = has_post ? cursor_of_node(node[i], 2, end) : -1;
       fill(f, l, cur[n_post], state_base + l.state, -1);
       f.kind = kind_of[end];
       f.first = l.first;
@@ -650,9 +677,8 @@ inline void ds_start(D& d, int S, int K, int X, int max_rows, int max_new, long 
   d.kind_of[S - 1] = 2;
   d.stop_token = stop_token;
   d.next_branch = 1;
-  d.n_par = 1;
-  d.par_b[0] = 0;
-  d.par_p[0] = -1;
+  d.clear_parents();
+  d.set_parent(0, -1);
   d.new_node(0, -1);
   d.committed = 1;
   out[0] = first;
@@ -711,19 +737,22 @@ __device__ inline void write_meta(int* m, int width, const DsFill* f, int n, int
   }
 }
 
+// The state moves in 16-byte pieces (both copies are 16-byte aligned).
+static_assert(sizeof(LoopSched) % 16 == 0, "scheduler state must be a whole number of 16-byte pieces");
+
 __device__ inline void load_sched(LoopSched* s, const LoopSched* g) {
-  const int n = (int)(sizeof(LoopSched) / sizeof(int));
-  int* d = reinterpret_cast<int*>(s);
-  const int* src = reinterpret_cast<const int*>(g);
+  const int n = (int)(sizeof(LoopSched) / 16);
+  int4* d = reinterpret_cast<int4*>(s);
+  const int4* src = reinterpret_cast<const int4*>(g);
   for (int i = threadIdx.x; i < n; i += blockDim.x) d[i] = __ldcg(src + i);
   __syncthreads();
 }
 
 __device__ inline void store_sched(LoopSched* g, const LoopSched* s) {
   __syncthreads();
-  const int n = (int)(sizeof(LoopSched) / sizeof(int));
-  int* d = reinterpret_cast<int*>(g);
-  const int* src = reinterpret_cast<const int*>(s);
+  const int n = (int)(sizeof(LoopSched) / 16);
+  int4* d = reinterpret_cast<int4*>(g);
+  const int4* src = reinterpret_cast<const int4*>(s);
   for (int i = threadIdx.x; i < n; i += blockDim.x) d[i] = src[i];
 }
 
@@ -770,7 +799,7 @@ __device__ inline void loop_write_meta(const LoopSched& s, const LoopPlan& p, co
 
 // The first cycle's plan.
 __global__ void __launch_bounds__(kLoopThreads) loop_plan_kernel(LoopSched* g, LoopMeta m) {
-  __shared__ LoopSched s;
+  __shared__ __align__(16) LoopSched s;
   __shared__ LoopPlan p;
   load_sched(&s, g);
   if (threadIdx.x == 0) loop_plan(s, p);
@@ -779,22 +808,31 @@ __global__ void __launch_bounds__(kLoopThreads) loop_plan_kernel(LoopSched* g, L
   store_sched(g, &s);
 }
 
+// Launched with programmatic overlap after the post call (its last kernel
+// triggers dependents at its start).
 // End of a cycle and start of the next: the readout lanes' decisions (in
 // readout order: greedy tokens, stride 1, or sampled decision rows, stride 5)
 // resolve the pipeline, commit a token to `out` and retain the surviving
 // branches' timelines; then the next cycle is planned.
 __global__ void __launch_bounds__(kLoopThreads) loop_step_kernel(LoopSched* g, const long long* dec_in, int stride,
                                                                  long long* out, LoopMeta m) {
-  __shared__ LoopSched s;
+  __shared__ __align__(16) LoopSched s;
   __shared__ LoopPlan p;
+  // the state was written by the previous cycle's step: load it while the
+  // post call finishes, then wait for the decisions
+  __shared__ long long s_dec_in[kLoopMaxLanes * 5];
   load_sched(&s, g);
+  pdl_wait();
+  // the readouts' decisions, one global round trip for all of them
+  if ((int)threadIdx.x < kLoopMaxLanes * stride) s_dec_in[threadIdx.x] = __ldcg(dec_in + threadIdx.x);
+  __syncthreads();
   if (threadIdx.x == 0) {
     if (!s.done && !s.err) {
       long long dec[kLoopMaxLanes * 5];
       int j = 0;
       for (int i = 0; i < s.n_lanes; ++i) {
         const bool readout = s.kind_of[s.lanes[i].stage + s.K - 1] >= 0;
-        for (int f = 0; f < stride; ++f) dec[i * stride + f] = readout ? dec_in[j * stride + f] : -1;
+        for (int f = 0; f < stride; ++f) dec[i * stride + f] = readout ? s_dec_in[j * stride + f] : -1;
         j += readout;
       }
       s.consume(dec, stride, out);

@@ -2058,9 +2058,10 @@ const ls_engine::LoopGraph& loop_graph_for(ls_engine& e, int chunks) {
     e.qkv_planes = true;    // one new position per lane
     e.attn_chunks = chunks;
     e.serialize_next = true;   // the first role kernel reads the metadata the step kernel wrote
-    // about half of the fixed-width lanes are live in a typical cycle; the
-    // attention form is chosen for those (every form computes the same values)
-    e.attn_form_lanes = std::max(1, W / 2);
+    // the attention form is chosen for the full width, so that a cycle whose
+    // lanes are all live still runs its attention in one wave (every form
+    // computes the same values)
+    e.attn_form_lanes = W;
     e.meta_override = pre;
     e.gemm_active = lm.active;
     enqueue_role(e, kPre, W);
@@ -2077,11 +2078,12 @@ const ls_engine::LoopGraph& loop_graph_for(ls_engine& e, int chunks) {
     kernels += e.kernels_in_call;
     e.meta_override = nullptr;
     e.gemm_active = nullptr;
+    const bool pdl = e.sc.use_pdl != 0;
     if (e.sampling)
-      launch(loop_step_kernel, dim3(1), dim3(kLoopThreads), 0, e.stream, false, e.loop_sched,
+      launch(loop_step_kernel, dim3(1), dim3(kLoopThreads), 0, e.stream, pdl, e.loop_sched,
              (const long long*)e.dec_dev, 5, e.loop_out, lm);
     else
-      launch(loop_step_kernel, dim3(1), dim3(kLoopThreads), 0, e.stream, false, e.loop_sched,
+      launch(loop_step_kernel, dim3(1), dim3(kLoopThreads), 0, e.stream, pdl, e.loop_sched,
              (const long long*)e.amax_dev, 1, e.loop_out, lm);
   } catch (...) {
     e.meta_override = nullptr;

@@ -107,6 +107,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int kb0 = (int)((long)split * KB / splits);
   const int kb1 = (int)((long)(split + 1) * KB / splits);
   const int nkb = kb1 - kb0;
+  // live lanes: the epilogue skips the inactive tail of a fixed-width call
+  // (the count was written before this graph started; read it early)
+  const int n_live = epi.active ? max(0, min(n_valid, __ldcg(epi.active))) : n_valid;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < ST; ++s) {
@@ -206,8 +209,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const bool have = mbar_wait(acc_bar, 0, err, kDevTimeoutAcc);
   tc_fence_after();
   float* red = reinterpret_cast<float*>(smem);
-  // live lanes: the epilogue skips the inactive tail of a fixed-width call
-  const int n_live = epi.active ? max(0, min(n_valid, *epi.active)) : n_valid;
   const int lanes_here = min(BN / 2, n_live - n0 / 2);   // lanes of this N tile
   const long tile_id = (long)blockIdx.z * gridDim.x + blockIdx.x;
   const long split_floats = (long)(BN / 2) * kGemmBM;

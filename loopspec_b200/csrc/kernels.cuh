@@ -495,8 +495,10 @@ __device__ __forceinline__ float plane_sum(const float* p, int splits, long stri
 //   kAttnWide  (<= 1 CTA per SM): K and V before the wait, 2 CTAs' registers
 //              per SM, no spills;
 //   kAttnMid   (<= 2 CTAs per SM): K and V before the wait, 3 per SM;
-//   kAttnVLate (larger grids): only K before the wait, V after the scores in
-//              K's registers; one more round trip, 4 CTAs per SM.
+//   kAttnVLate (larger grids): only K before the wait into registers, V of
+//              the older positions copied to shared memory (cp.async) before
+//              the wait and read after the scores into K's registers; 4 CTAs
+//              per SM.
 enum AttnForm : int { kAttnWide = 0, kAttnMid = 1, kAttnVLate = 2 };
 
 template <int HD, int G, int FORM>
@@ -542,6 +544,9 @@ __global__ void __launch_bounds__(kAttnThreads, FORM + 2) attn_kernel(AttnArgs a
   __shared__ float sm_m[NW][G], sm_l[NW][G];
   __shared__ float sm_acc[NW][G][HD];
   __shared__ int s_last;
+  // late-V form: each thread's V rows of positions older than this call,
+  // staged by cp.async before the wait (registers stay K's only)
+  __shared__ __align__(16) uint4 s_v[VLATE ? PER : 1][VLATE ? kAttnThreads : 1];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int sub = lane / LPP, sl = lane % LPP;
   const int sg = warp * PPW + sub;
@@ -586,7 +591,9 @@ __global__ void __launch_bounds__(kAttnThreads, FORM + 2) attn_kernel(AttnArgs a
     const bool old_row = slot >= 0 && i < fresh;
     kr[t] = old_row ? *reinterpret_cast<const uint4*>(a.kpool + off) : make_uint4(0, 0, 0, 0);
     if (!VLATE) vr[t] = old_row ? *reinterpret_cast<const uint4*>(a.vpool + off) : make_uint4(0, 0, 0, 0);
+    else if (old_row) cp_async16(&s_v[t][threadIdx.x], a.vpool + off, true);
   }
+  if (VLATE) cp_async_commit();
   pdl_wait();
   // after the QKV projection: this thread's query slice and the newest K/V row
   float qv[G][8];
@@ -674,12 +681,15 @@ __global__ void __launch_bounds__(kAttnThreads, FORM + 2) attn_kernel(AttnArgs a
       sc[h][t] = s_slot[sg + t * NSG] >= 0 ? s : -INFINITY;
     }
   }
-  if (VLATE) {   // every V row now: the new one (decode form) from s_kv, the rest from the pool
+  if (VLATE) {   // every V row now: older positions from the staged copies, the new one
+                 // (decode form) from s_kv, positions this call wrote otherwise from the pool
+    cp_async_wait<0>();
 #pragma unroll
     for (int t = 0; t < PER; ++t) {
       const int i = sg + t * NSG;
       const int slot = s_slot[i];
       if (slot < 0) vr[t] = make_uint4(0, 0, 0, 0);
+      else if (i < fresh) vr[t] = s_v[t][threadIdx.x];
       else if (a.qkv && i == fresh) vr[t] = *reinterpret_cast<const uint4*>(s_kv + HD + sl * 8);
       else vr[t] = *reinterpret_cast<const uint4*>(a.vpool + (long)slot * kd + g * HD + sl * 8);
     }
