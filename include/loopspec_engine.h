@@ -201,6 +201,21 @@ int ls_generate_batch(ls_engine* eng, const int64_t* prompts, const int32_t* pro
                       const uint64_t* seeds, int64_t* out_ids, int32_t* n_out,
                       ls_stats* per_request, ls_stats* total);
 
+/* ls_generate_batch with each request's own sampling parameters, so greedy
+ * and sampled requests share a batch: request i decodes with temperature[i],
+ * top_k[i], top_p[i] (greedy iff temperature == 0 or top_k == 1, the
+ * reference server's rule, server/loopspec_scheduler.py:316-329) and draws
+ * from seeds[i] (required). Each request commits what it commits alone with
+ * the same parameters and seed. The engine's own ls_set_sampling state is
+ * unchanged afterwards. Replaces, per request, the SamplingParams the
+ * reference's server takes with each /generate call (cli.py:88-89 serves one
+ * at a time). */
+int ls_generate_batch_sampling(ls_engine* eng, const int64_t* prompts, const int32_t* prompt_lens,
+                               int n_requests, int max_new_tokens, int mode, int64_t stop_token,
+                               const uint64_t* seeds, const float* temperature,
+                               const int32_t* top_k, const float* top_p, int64_t* out_ids,
+                               int32_t* n_out, ls_stats* per_request, ls_stats* total);
+
 /* The native scheduler loop of ls_generate mode 0 (continue_pipelined,
  * pipeline.py:254-423, with greedy resolve decisions.py:136-184 and the
  * executor's state-slot pool and counters executor.py:76-107,239-290),

@@ -89,6 +89,11 @@ SIGNATURES = [
     ("ls_generate_batch", _i32, [_P, _PI64, ctypes.POINTER(_i32), _i32, _i32, _i32, _i64,
                                  ctypes.POINTER(_u64), _PI64, ctypes.POINTER(_i32),
                                  ctypes.POINTER(Stats), ctypes.POINTER(Stats)]),
+    ("ls_generate_batch_sampling", _i32, [_P, _PI64, ctypes.POINTER(_i32), _i32, _i32, _i32, _i64,
+                                          ctypes.POINTER(_u64), ctypes.POINTER(ctypes.c_float),
+                                          ctypes.POINTER(_i32), ctypes.POINTER(ctypes.c_float), _PI64,
+                                          ctypes.POINTER(_i32), ctypes.POINTER(Stats),
+                                          ctypes.POINTER(Stats)]),
     ("ls_device_loop_simulate", _i32, [_i32, _i32, _i32, _i64, _i32, _i64, DECIDE_FN, CYCLE_FN,
                                        RETAIN_FN, _P, _PI64, ctypes.POINTER(_i32),
                                        ctypes.POINTER(Stats)]),

@@ -41,7 +41,8 @@ enum MetaField : int {
   kMetaDrawRow = 13,  // post rows: index among the request's readouts of this cycle
   kMetaSeedLo = 14,   // post rows: the request's sampling seed, low / high 32 bits
   kMetaSeedHi = 15,
-  kMetaFields = 16,
+  kMetaReq = 16,      // post rows: the request's sampling-parameter slot
+  kMetaFields = 17,
 };
 
 struct Meta {

@@ -730,6 +730,7 @@ __device__ inline void write_meta(int* m, int width, const DsFill* f, int n, int
         case kMetaDrawRow: v = post ? b : -1; break;
         case kMetaSeedLo: v = post ? (int)(uint32_t)(seed & 0xFFFFFFFFull) : -1; break;
         case kMetaSeedHi: v = post ? (int)(uint32_t)(seed >> 32) : -1; break;
+        case kMetaReq: v = post ? 0 : -1; break;   // the single request's parameter slot
         default: v = -1;
       }
     }

@@ -393,7 +393,19 @@ struct Request {
   uint32_t draw_cycle = 0;  // the first token uses draw 0, decode cycles 1, 2, ...
   unsigned long long seed = 0;
   int state_base = 0;
+  bool sampled = false;     // top-p / top-k / temperature decisions (else greedy)
 };
+}  // namespace
+
+namespace {
+// Sampling parameters as the engine stores them: greedy iff top_k == 1
+// (temperature 0 is normalised to it), as the reference server decides
+// (server/loopspec_scheduler.py:316-329).
+SampleParams sample_params(float temperature, int top_k, float top_p, unsigned long long seed) {
+  const bool greedy = temperature == 0.f || top_k == 1;
+  return SampleParams{temperature == 0.f ? 1.f : temperature, top_p, greedy ? 1 : top_k, 0, seed};
+}
+bool params_sampled(const SampleParams& p) { return p.top_k != 1; }
 }  // namespace
 
 // ======================================================================= engine
@@ -784,8 +796,10 @@ struct ls_engine {
     err_dev = dalloc<int>(1);
     attn_tickets = dalloc<int>((long)cap * NKV);
     gemm_part = dalloc<float>(gemm_part_elems);
-    sparams_dev = dalloc<SampleParams>(1);
-    CK(cudaMemcpy(sparams_dev, &sparams, sizeof(SampleParams), cudaMemcpyHostToDevice));
+    // one parameter slot per request (slot i: request i; single-request calls use slot 0)
+    sparams_dev = dalloc<SampleParams>(max_req);
+    for (int i = 0; i < max_req; ++i)
+      CK(cudaMemcpy(sparams_dev + i, &sparams, sizeof(SampleParams), cudaMemcpyHostToDevice));
     q1_bank = dalloc<float>((long)max_state * V);
     r_bank = dalloc<float>((long)max_state * V);
     dec_dev = dalloc<long long>((long)cap * 5);
@@ -1227,7 +1241,7 @@ void prep(ls_engine& e, Meta meta, int n, bool embed_mode, float* bank_out, bool
 void head_decisions(ls_engine& e, Meta meta, int lane0, int lanes) {
   if (e.sampling) {
     REQUIRE(lanes <= e.max_state, LS_ECAPACITY, "too many sampled readout rows");
-    SampleArgs sa{meta, lane0, e.logits, e.V, e.sparams_dev, e.q1_bank, e.r_bank,
+    SampleArgs sa{meta, lane0, e.logits, e.V, e.sparams_dev, e.max_req, e.q1_bank, e.r_bank,
                   e.max_state, e.dec_dev, e.err_dev};
     // one cluster of CTAs per row; rows in 16-byte steps when the vocabulary
     // allows (logits and bank rows are then 16-byte aligned)
@@ -1467,6 +1481,7 @@ void advance(Cursor* c, int slot, bool owned) {
 // The random stream of a readout row: the request's seed and cycle counter,
 // and the row's index among the request's readouts of that cycle.
 void set_draw(ls_engine& e, int* m, int b, const Request& R, int draw, int draw_row) {
+  put(e, m, kMetaReq, b, (int)(&R - e.reqs.data()));
   put(e, m, kMetaCycle, b, draw);
   put(e, m, kMetaDrawRow, b, draw_row);
   put(e, m, kMetaSeedLo, b, (int)(uint32_t)(R.seed & 0xFFFFFFFFull));
@@ -2191,7 +2206,7 @@ SchedHooks engine_hooks(ls_engine& e, int req, StopRule stop) {
   hk.X = e.X;
   hk.max_rows = e.max_rows;
   hk.endpoint_kind = e.endpoint_kind;
-  hk.sampling = e.sampling;
+  hk.sampling = e.reqs[req].sampled;
   hk.retain = [&e, req](const std::vector<PLane>& lanes, int) {
     std::vector<std::pair<int, int>> bp;
     for (auto& l : lanes) bp.emplace_back(l.branch, l.parent);
@@ -2569,12 +2584,11 @@ int ls_set_sampling(ls_engine* e, float temperature, int top_k, float top_p, uin
     REQUIRE(e->finalized, LS_EINVAL, "engine not finalized");
     REQUIRE(temperature >= 0.f && top_k >= 0 && top_p > 0.f && top_p <= 1.f, LS_EINVAL,
             "sampling needs temperature >= 0, top_k >= 0, 0 < top_p <= 1");
-    // greedy iff top_k == 1 (temperature 0 is normalised to it), as the
-    // reference server decides (server/loopspec_scheduler.py:316-329)
-    e->sampling = !(temperature == 0.f || top_k == 1);
-    e->sparams = SampleParams{temperature == 0.f ? 1.f : temperature, top_p, top_k, 0, seed};
+    e->sparams = sample_params(temperature, top_k, top_p, seed);
+    e->sampling = params_sampled(e->sparams);
     CK(cudaStreamSynchronize(e->stream));
-    CK(cudaMemcpy(e->sparams_dev, &e->sparams, sizeof(SampleParams), cudaMemcpyHostToDevice));
+    for (int i = 0; i < e->max_req; ++i)
+      CK(cudaMemcpy(e->sparams_dev + i, &e->sparams, sizeof(SampleParams), cudaMemcpyHostToDevice));
   } catch (const std::exception& ex) {
     return fail(e, ex);
   }
@@ -2586,6 +2600,7 @@ int ls_prefill(ls_engine* e, const int64_t* prompt, int n, float* out_logits, in
   try {
     REQUIRE(e->finalized, LS_EINVAL, "engine not finalized");
     e->reqs[0].seed = e->sparams.seed;
+    e->reqs[0].sampled = e->sampling;
     *first = prefill(*e, e->reqs[0], prompt, n, out_logits);
   } catch (const std::exception& ex) {
     return fail(e, ex);
@@ -2637,7 +2652,7 @@ namespace {
 int generate_batch(ls_engine* e, const int64_t* prompts, const int32_t* lens, int n_req, int max_new,
                    int mode, const std::vector<StopRule>& stop, const uint64_t* seeds,
                    int64_t* out_ids, int32_t* n_out, ls_stats* per_request, ls_stats* total,
-                   long long device_loop_stop = -2) {
+                   long long device_loop_stop = -2, const SampleParams* params = nullptr) {
   if (!e || !prompts || !lens || !out_ids || !n_out || n_req < 1 || max_new < 1 ||
       (mode != 0 && mode != 1) || (int)stop.size() != n_req)
     return LS_EINVAL;
@@ -2646,11 +2661,35 @@ int generate_batch(ls_engine* e, const int64_t* prompts, const int32_t* lens, in
     REQUIRE(n_req <= e->max_req, LS_ECAPACITY,
             "more requests than the engine's max_requests (" + std::to_string(e->max_req) + ")");
     e->h2d_bytes = e->d2h_bytes = 0;
+    // per-request parameters (else the engine's for every request): slot i
+    // holds request i's; the post calls run the sampler when any request
+    // samples (greedy rows of it take the argmax); restored afterwards
+    struct ParamScope {
+      ls_engine* e;
+      bool active, saved;
+      ~ParamScope() {
+        if (!active) return;
+        e->sampling = saved;
+        cudaStreamSynchronize(e->stream);
+        for (int i = 0; i < e->max_req; ++i)
+          cudaMemcpy(e->sparams_dev + i, &e->sparams, sizeof(SampleParams), cudaMemcpyHostToDevice);
+      }
+    } scope{e, params != nullptr, e->sampling};
+    if (params) {
+      bool any = false;
+      CK(cudaStreamSynchronize(e->stream));
+      for (int i = 0; i < n_req; ++i) {
+        any = any || params_sampled(params[i]);
+        CK(cudaMemcpy(e->sparams_dev + i, &params[i], sizeof(SampleParams), cudaMemcpyHostToDevice));
+      }
+      e->sampling = any;
+    }
     ls_stats tot{};
     std::vector<long long> first(n_req);
     long off = 0;
     for (int i = 0; i < n_req; ++i) {
       Request& R = e->reqs[i];
+      R.sampled = params ? params_sampled(params[i]) : e->sampling;
       R.seed = seeds ? seeds[i] : e->sparams.seed + (unsigned long long)i;
       first[i] = prefill(*e, R, prompts + off, lens[i], nullptr);
       off += lens[i];
@@ -2766,6 +2805,26 @@ int ls_generate_batch(ls_engine* e, const int64_t* prompts, const int32_t* promp
   std::vector<StopRule> stops(n_requests, stop_rule(stop_token, nullptr, nullptr));
   return generate_batch(e, prompts, prompt_lens, n_requests, max_new_tokens, mode, stops, seeds, out_ids,
                         n_out, per_request, total);
+}
+
+int ls_generate_batch_sampling(ls_engine* e, const int64_t* prompts, const int32_t* prompt_lens,
+                               int n_requests, int max_new_tokens, int mode, int64_t stop_token,
+                               const uint64_t* seeds, const float* temperature, const int32_t* top_k,
+                               const float* top_p, int64_t* out_ids, int32_t* n_out, ls_stats* per_request,
+                               ls_stats* total) {
+  if (!e || n_requests < 1 || !seeds || !temperature || !top_k || !top_p) return LS_EINVAL;
+  std::vector<SampleParams> params(n_requests);
+  for (int i = 0; i < n_requests; ++i) {
+    if (!(temperature[i] >= 0.f && top_k[i] >= 0 && top_p[i] > 0.f && top_p[i] <= 1.f)) {
+      e->last_error = "sampling needs temperature >= 0, top_k >= 0, 0 < top_p <= 1 (request " +
+                      std::to_string(i) + ")";
+      return LS_EINVAL;
+    }
+    params[i] = sample_params(temperature[i], top_k[i], top_p[i], seeds[i]);
+  }
+  std::vector<StopRule> stops(n_requests, stop_rule(stop_token, nullptr, nullptr));
+  return generate_batch(e, prompts, prompt_lens, n_requests, max_new_tokens, mode, stops, seeds, out_ids,
+                        n_out, per_request, total, -2, params.data());
 }
 
 namespace {
@@ -2965,6 +3024,8 @@ int ls_time_role(ls_engine* e, int role, int n, int context_len, int iters, doub
         c.pending_parent_row = root->row;
       }
       fill_lane(*e, R.tl, m, b, 1, context_len - 1, attn ? &c : nullptr, b, b);
+      // post lanes read out as final verifications without a proposal
+      if (role == kPost) set_final_readout(*e, m, b, R, 1, b);
     }
     run_role(*e, role, n, m, true);  // forks the rows
     int* m2 = stage_meta(*e);

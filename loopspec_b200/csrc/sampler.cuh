@@ -24,7 +24,9 @@
 //          the q2 token y iff u1 < min(1, F[y]/R[y]), else draw from
 //          norm(max(F - R, 0)) (or F) with u2 (sampling/rejection.py:42-97)
 // and writes the decision row (token, proposed, accepted_code, q1_rejected,
-// q2_rejected) of policy.py:197-283. Single probabilities (P[x], F[y]) are
+// q2_rejected) of policy.py:197-283. A row whose request decodes greedily
+// (top_k == 1) in a batch with sampled requests takes the argmax of its
+// logits (lowest index on ties, as the greedy path) as the row's token. Single probabilities (P[x], F[y]) are
 // recomputed by every CTA from the logits with the slice loops' operations, so
 // every CTA takes the same branch. Draws invert a CDF in chunks of 2048
 // tokens like the reference. Uniforms: words of Philox4x32-10 with counter
@@ -57,7 +59,8 @@ struct SampleArgs {
   int meta_row0;                // metadata record of row 0 (head lanes may start later)
   const float* logits;          // [rows][V]
   int V;
-  const SampleParams* params;   // device copy (graphs read it at run time)
+  const SampleParams* params;   // per-request slots, device copies (graphs read them at run time)
+  int n_params;
   float* q1_bank;               // [bank_rows][V] lane q1 distributions, by state slot
   float* r_bank;                // [bank_rows][V] lane q2 residual distributions
   int bank_rows;
@@ -106,14 +109,21 @@ __device__ __forceinline__ float ld_cluster(const float* p, uint32_t rank) {
   return v;
 }
 
+// Every CTA's copy of one shared float, all loads issued before the first is
+// used (one distributed-shared-memory round trip), in rank order.
+__device__ __forceinline__ void ld_cluster_all(const float* p, int C, float (&v)[kSampleCtas]) {
+#pragma unroll
+  for (int r = 0; r < kSampleCtas; ++r) v[r] = r < C ? ld_cluster(p, (uint32_t)r) : 0.f;
+}
+
 struct SampleShared {
   float red[32 * 2];                 // warp partials of cluster reductions
   float xch[2][kSampleBins + 1];     // this CTA's values read by the cluster (double buffered)
   float tot[kSampleBins + 1];        // cluster totals
   float ctot[kSampleMaxChunks];      // this CTA's chunk totals
   float all[kSampleMaxChunks];       // every chunk total of the row
-  float rem;
-  int ch, tok;
+  float rem, gpick;
+  int ch, tok, pick;
 };
 
 // Row-wide sum (or max) of NV per-thread values; every thread of every CTA
@@ -136,11 +146,9 @@ __device__ __forceinline__ void cl_reduce(float (&v)[NV], SampleShared& sh, int 
   }
   cluster_barrier();
   if (threadIdx.x < NV) {
-    float t = MAX ? -INFINITY : 0.f;
-    for (int r = 0; r < C; ++r) {
-      const float x = ld_cluster(&sh.xch[ph][threadIdx.x], (uint32_t)r);
-      t = MAX ? fmaxf(t, x) : t + x;
-    }
+    float t = MAX ? -INFINITY : 0.f, x[kSampleCtas];
+    ld_cluster_all(&sh.xch[ph][threadIdx.x], C, x);
+    for (int r = 0; r < C; ++r) t = MAX ? fmaxf(t, x[r]) : t + x[r];
     sh.tot[threadIdx.x] = t;
   }
   __syncthreads();
@@ -179,15 +187,57 @@ __device__ __forceinline__ void cl_softmax_stats(float& m, float& s, SampleShare
   }
   cluster_barrier();
   if (threadIdx.x == 0) {
-    float mm = -INFINITY, ss = 0.f;
-    for (int r = 0; r < C; ++r)
-      sm_merge(mm, ss, ld_cluster(&sh.xch[ph][0], (uint32_t)r), ld_cluster(&sh.xch[ph][1], (uint32_t)r));
+    float mm = -INFINITY, ss = 0.f, xm[kSampleCtas], xs[kSampleCtas];
+    ld_cluster_all(&sh.xch[ph][0], C, xm);
+    ld_cluster_all(&sh.xch[ph][1], C, xs);
+    for (int r = 0; r < C; ++r) sm_merge(mm, ss, xm[r], xs[r]);
     sh.tot[0] = mm;
     sh.tot[1] = ss;
   }
   __syncthreads();
   m = sh.tot[0];
   s = sh.tot[1];
+  ph ^= 1;
+}
+
+// Row-wide (max value, lowest index) over the cluster; every thread returns it.
+__device__ __forceinline__ void am_merge(float& v, int& i, float v2, int i2) {
+  if (v2 > v || (v2 == v && i2 < i)) {
+    v = v2;
+    i = i2;
+  }
+}
+
+__device__ __forceinline__ void cl_argmax(float& v, int& i, SampleShared& sh, int C, int& ph) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+    am_merge(v, i, __shfl_xor_sync(0xffffffffu, v, o), __shfl_xor_sync(0xffffffffu, i, o));
+  if (lane == 0) {
+    sh.red[warp * 2] = v;
+    sh.red[warp * 2 + 1] = __int_as_float(i);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int w = 0; w < nw; ++w) am_merge(bv, bi, sh.red[w * 2], __float_as_int(sh.red[w * 2 + 1]));
+    sh.xch[ph][0] = bv;
+    sh.xch[ph][1] = __int_as_float(bi);
+  }
+  cluster_barrier();
+  if (threadIdx.x == 0) {
+    float bv = -INFINITY, xv[kSampleCtas], xi[kSampleCtas];
+    int bi = 0x7fffffff;
+    ld_cluster_all(&sh.xch[ph][0], C, xv);
+    ld_cluster_all(&sh.xch[ph][1], C, xi);
+    for (int r = 0; r < C; ++r) am_merge(bv, bi, xv[r], __float_as_int(xi[r]));
+    sh.tot[0] = bv;
+    sh.tot[1] = __int_as_float(bi);
+  }
+  __syncthreads();
+  v = sh.tot[0];
+  i = __float_as_int(sh.tot[1]);
   ph ^= 1;
 }
 
@@ -256,21 +306,35 @@ __device__ float cl_cutoff(const float* P, int n, float target, float* hist, Sam
     }
     cluster_barrier();
     if (tid <= kSampleBins) {
-      float t = 0.f;
-      for (int r = 0; r < C; ++r) t += ld_cluster(&sh.xch[ph][tid], (uint32_t)r);
+      float t = 0.f, x[kSampleCtas];
+      ld_cluster_all(&sh.xch[ph][tid], C, x);
+      for (int r = 0; r < C; ++r) t += x[r];
       sh.tot[tid] = t;
     }
     __syncthreads();
     ph ^= 1;
-    float g = sh.tot[kSampleBins];
-    int pick = 0;
-    for (int i = kSampleBins - 1; i >= 0; --i) {
-      g += sh.tot[i];
-      if (g >= target) {
-        pick = i;
-        break;
+    if (warp == 0) {
+      // suffix sums G[i] = above + sum_{j >= i} bin[j] (a fixed shuffle tree),
+      // and the highest bin whose G reaches the target (bin 0 if none)
+      static_assert(kSampleBins == 32, "one bin per lane");
+      float v = sh.tot[lane];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float y = __shfl_down_sync(0xffffffffu, v, o);
+        if (lane + o < 32) v += y;
+      }
+      v += sh.tot[kSampleBins];
+      const unsigned ok = __ballot_sync(0xffffffffu, v >= target);
+      const int pk = ok ? 31 - __clz(ok) : 0;
+      const float gk = __shfl_sync(0xffffffffu, v, pk);
+      if (lane == 0) {
+        sh.pick = pk;
+        sh.gpick = gk;
       }
     }
+    __syncthreads();
+    const int pick = sh.pick;
+    const float g = sh.gpick;
     lo += (uint32_t)pick << s;
     if (s == 0) {
       *at_cut = g;
@@ -410,7 +474,12 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(SampleArgs a) {
   // every CTA of a cluster reads the same metadata, so these exits are
   // cluster-uniform and come before the first cluster barrier
   if (a.meta.get(kMetaPos, mrow) < 0) return;   // inactive lane
-  const SampleParams prm = *a.params;
+  const int rq = a.meta.get(kMetaReq, mrow);
+  if (rq < 0 || rq >= a.n_params) {
+    if (rank == 0 && threadIdx.x == 0) atomicExch(a.err, kDevBadIndex);
+    return;
+  }
+  const SampleParams prm = a.params[rq];
   const int kind = a.meta.get(kMetaKind, mrow);
   const int first = a.meta.get(kMetaFirst, mrow);
   const int second = a.meta.get(kMetaSecond, mrow);
@@ -433,10 +502,28 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(SampleArgs a) {
   const float* lg = lg_row + n0;
   long long* dec = a.decisions + (long)row * 5;
   int ph = 0;
+  const int NV = n / E, tid = threadIdx.x, nt = blockDim.x;
+
+  if (prm.top_k == 1) {   // greedy row: argmax, the lowest index on ties
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int j = tid; j < NV; j += nt) {
+      const Vf<E> x = ldv<E>(lg, j);
+#pragma unroll
+      for (int i = 0; i < E; ++i)
+        if (x.v[i] > bv) {   // indices increase within a thread, so ties keep the lower
+          bv = x.v[i];
+          bi = n0 + j * E + i;
+        }
+    }
+    cl_argmax(bv, bi, sh, C, ph);
+    if (rank == 0 && threadIdx.x == 0) put_decision(dec, bi == 0x7fffffff ? 0 : bi, 0, 0, 0, 0);
+    cluster_barrier();   // no CTA leaves while another may still read its shared memory
+    return;
+  }
 
   // softmax(logits / T) in fp32: online (max, sum) per thread, merged over
   // the row, then P = exp(x / T - max) / sum
-  const int NV = n / E, tid = threadIdx.x, nt = blockDim.x;
   const float invT = 1.f / prm.temperature;
   float mx = -INFINITY, sm = 0.f;
 #pragma unroll 4

@@ -155,11 +155,15 @@ class Engine:
         self.prefill_len = None
         return out[: n.value].tolist(), st.as_dict()
 
-    def generate_batch(self, prompts, max_new_tokens, *, mode="loopspec", stop_token=None, seeds=None):
+    def generate_batch(self, prompts, max_new_tokens, *, mode="loopspec", stop_token=None, seeds=None,
+                       sampling=None):
         """Several requests decoded together (ls_generate_batch): every cycle
         runs over the lanes of all running requests. Returns (list of ids per
         request, list of per-request stats, batch stats). Request i commits
-        what it commits alone with seed seeds[i]."""
+        what it commits alone with seed seeds[i]. `sampling`, if given, is one
+        entry per request: None (greedy) or {temperature, top_k, top_p}
+        (ls_generate_batch_sampling; seeds are then required); otherwise every
+        request uses the engine's set_sampling state."""
         lens = np.ascontiguousarray([len(p) for p in prompts], dtype=np.int32)
         flat = np.ascontiguousarray([t for p in prompts for t in p], dtype=np.int64)
         n = len(prompts)
@@ -172,6 +176,25 @@ class Engine:
             sd = np.ascontiguousarray([int(x) & 0xFFFFFFFFFFFFFFFF for x in seeds], dtype=np.uint64)
         m = 0 if mode == "loopspec" else 1
         stop = -1 if stop_token is None else int(stop_token)
+        if sampling is not None:
+            if sd is None or len(sampling) != n:
+                raise ValueError("per-request sampling needs one entry and one seed per request")
+            f32 = ctypes.POINTER(ctypes.c_float)
+            temp = np.ascontiguousarray([0.0 if s is None else float(s.get("temperature", 1.0))
+                                         for s in sampling], dtype=np.float32)
+            topk = np.ascontiguousarray([1 if s is None else int(s.get("top_k", 0)) for s in sampling],
+                                        dtype=np.int32)
+            topp = np.ascontiguousarray([1.0 if s is None else float(s.get("top_p", 1.0))
+                                         for s in sampling], dtype=np.float32)
+            code = self.L.ls_generate_batch_sampling(
+                self.h, _i64p(flat), lens.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), n, max_new_tokens,
+                m, stop, sd.ctypes.data_as(ctypes.POINTER(ctypes.c_uint64)), temp.ctypes.data_as(f32),
+                topk.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), topp.ctypes.data_as(f32), _i64p(out),
+                n_out.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), per, ctypes.byref(total))
+            _lib.check(code, self.h)
+            self.prefill_len = None
+            return ([out[i, : n_out[i]].tolist() for i in range(n)], [per[i].as_dict() for i in range(n)],
+                    total.as_dict())
         code = self.L.ls_generate_batch(
             self.h, _i64p(flat), lens.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), n, max_new_tokens, m,
             stop, None if sd is None else sd.ctypes.data_as(ctypes.POINTER(ctypes.c_uint64)), _i64p(out),

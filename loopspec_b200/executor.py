@@ -197,13 +197,18 @@ def generate_autoregressive(runner: Engine, prompt_ids: Sequence[int], max_new_t
 def generate_loopspec_batch(runner: Engine, prompts: Sequence[Sequence[int]], max_new_tokens: int, *,
                             sampling=None, seeds=None, stop_token=None, mode="loopspec"):
     """Generate for several prompts together; returns (ids per request,
-    stats per request, batch stats). `sampling` applies to every request;
-    request i draws from seeds[i] (default: 0, 1, 2, ...), so it commits
-    what generate_loopspec(..., seed=seeds[i]) commits for it alone."""
+    stats per request, batch stats). `sampling` applies to every request, or
+    is a list with one entry per request (None = greedy), so greedy and
+    sampled requests share a batch; request i draws from seeds[i] (default:
+    0, 1, 2, ...), so it commits what generate_loopspec(..., sampling=its
+    entry, seed=seeds[i]) commits for it alone."""
     if max_new_tokens <= 0:
         raise ValueError("a committed first token requires a positive budget")
     if seeds is None:
         seeds = list(range(len(prompts)))
+    if isinstance(sampling, (list, tuple)):
+        return runner.generate_batch([list(p) for p in prompts], max_new_tokens, mode=mode,
+                                     stop_token=stop_token, seeds=seeds, sampling=list(sampling))
     apply_sampling(runner, sampling, None, seeds[0] if seeds else 0)
     return runner.generate_batch([list(p) for p in prompts], max_new_tokens, mode=mode,
                                  stop_token=stop_token, seeds=seeds)

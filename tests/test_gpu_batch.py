@@ -13,7 +13,7 @@ import pytest
 import torch
 
 from loopspec_b200._lib import EngineError
-from loopspec_b200.executor import generate_loopspec, generate_loopspec_batch
+from loopspec_b200.executor import generate_autoregressive, generate_loopspec, generate_loopspec_batch
 from oracle.executor import teacher_forced_logits
 
 from test_gpu_engine import LOGIT_TOL, make, prompt_for
@@ -62,6 +62,30 @@ def test_batched_sampled_requests_equal_their_batch1_runs():
     # the seed, not the batch position, selects the stream
     ids2, _, _ = generate_loopspec_batch(eng, prompts[::-1], 32, sampling=samp, seeds=seeds[::-1])
     assert ids2[::-1] == ids
+    eng.close()
+
+
+@pytest.mark.parametrize("mode", ["loopspec", "ar"])
+def test_mixed_greedy_and_sampled_requests_equal_their_batch1_runs(mode):
+    """Per-request sampling parameters (ls_generate_batch_sampling): greedy and
+    sampled requests share the batch's calls; each commits what it commits
+    alone with its own parameters and seed."""
+    cfg, eng, _ = make("tiny", 1, 2, max_requests=4)
+    prompts = _prompts(cfg, [9, 25, 14, 3], seed=31)
+    samp = [None, {"temperature": 1.0, "top_k": 0, "top_p": 0.9}, None,
+            {"temperature": 0.8, "top_k": 40, "top_p": 1.0}]
+    seeds = [7, 8, 9, 10]
+    ids, per, _ = generate_loopspec_batch(eng, prompts, 24, sampling=samp, seeds=seeds, mode=mode)
+    alone_fn = generate_loopspec if mode == "loopspec" else generate_autoregressive
+    for i, p in enumerate(prompts):
+        alone, st = alone_fn(eng, p, 24, sampling=samp[i], seed=seeds[i])
+        assert ids[i] == alone, (i, mode)
+        if mode == "loopspec":
+            for k in COUNTERS:
+                assert per[i][k] == st[k], (i, k)
+    # greedy requests of the batch took the argmax: they equal AR-greedy alone
+    g0, _ = generate_autoregressive(eng, prompts[0], 24)
+    assert ids[0] == g0
     eng.close()
 
 
