@@ -66,6 +66,9 @@ def parse():
                         "over the ranks; prompt lengths uniform in [--prompt-min, --prompt]")
     p.add_argument("--prompt-min", type=int, default=0,
                    help="shortest prompt of a --batch step (0: every prompt has --prompt tokens)")
+    p.add_argument("--mixed", action="store_true",
+                   help="with --batch and --temperature: every other request decodes greedily "
+                        "(per-request parameters, as config 5 mixes greedy and top-p requests)")
     p.add_argument("--host-loop", action="store_true",
                    help="run LoopSpec cycles from the host (one sync per cycle) instead of the "
                         "device-resident loop")
@@ -226,57 +229,76 @@ def reference_arm(args):
 def tp_block(args, rank, world, local, dist):
     """Tensor parallelism beside the replica run (N > 1): the largest Raven
     model (Raven-OLMo, LoopSpec 2:8) split over all N ranks by heads and MLP
-    columns, one short greedy request, against the same request on one GPU
-    (rank 0). Bounded: every rank builds its shard first and all ranks agree
-    that every engine exists before any kernel runs; a failure is reported in
-    the block instead of ending the benchmark."""
+    columns, against the same work on one GPU (rank 0): one short greedy
+    request, then a batch of 8 (4 greedy, 4 top-p 0.9 requests with their own
+    parameters, as config 5 mixes them). Bounded: every rank builds its shard
+    first and all ranks agree that every engine exists before any kernel
+    runs; a failure is reported in the block instead of ending the
+    benchmark."""
     from loopspec_b200.engine import Engine
-    from loopspec_b200.executor import generate_loopspec
+    from loopspec_b200.executor import generate_loopspec, generate_loopspec_batch
     from loopspec_b200.tp import shard_config, shard_weights
     from loopspec_b200.weights import init_random_weights
     cfg = get_config("raven-olmo")
     sch = PipelineSchedule(cfg.stages, 2, 4)
-    n_prompt, n_new = 64, 64
-    prompt = make_prompt(cfg, n_prompt, 77)
-    out = {"model": cfg.name, "ranks": world, "schedule": "LoopSpec first=2 second=8 greedy",
+    n_prompt, n_new, n_batch = 64, 64, 8
+    prompts = [make_prompt(cfg, n_prompt, 77 + i) for i in range(n_batch)]
+    samp = [None if i % 2 == 0 else {"temperature": 1.0, "top_k": 0, "top_p": 0.9} for i in range(n_batch)]
+    seeds = [4242 + i for i in range(n_batch)]
+    out = {"model": cfg.name, "ranks": world, "schedule": "LoopSpec first=2 second=8",
            "prompt": n_prompt, "new_tokens": n_new}
-    eng = None
-    ok = True
-    try:
-        w = init_random_weights(cfg, 0, device=f"cuda:{local}", dtype=torch.bfloat16)
-        eng = Engine(shard_config(cfg, world), sch, shard_weights(w, cfg, rank, world), device=local,
-                     max_context=256, max_prompt=n_prompt)
-        handle = eng.tp_init(rank, world)
-    except Exception as ex:   # noqa: BLE001 - reported, the replica line still prints
-        ok, handle, out["error"] = False, b"", repr(ex)[:300]
-    got = [None] * world
-    dist.all_gather_object(got, (ok, handle))
-    if all(g[0] for g in got):
+
+    def decode(eng, n_req):
+        if n_req == 1:
+            generate_loopspec(eng, prompts[0], n_new)                  # warm-up / capture
+            ids, st = generate_loopspec(eng, prompts[0], n_new)
+            return [ids], st["decode_tokens"] / (st["decode_device_ms"] / 1e3)
+        generate_loopspec_batch(eng, prompts, n_new, sampling=samp, seeds=seeds)
+        ids, _, tot = generate_loopspec_batch(eng, prompts, n_new, sampling=samp, seeds=seeds)
+        return ids, tot["decode_tokens"] / (tot["decode_device_ms"] / 1e3)
+
+    def measure(n_req):
+        res = {}
+        eng = None
+        ok = True
         try:
-            eng.tp_attach([g[1] for g in got])
-            generate_loopspec(eng, prompt, n_new)                      # warm-up / capture
-            ids, st = generate_loopspec(eng, prompt, n_new)
-            out["tp_tok_s"] = round(st["decode_tokens"] / (st["decode_device_ms"] / 1e3), 2)
-            out["tp_ids"] = ids
-        except Exception as ex:   # noqa: BLE001
-            out["error"] = repr(ex)[:300]
-    ms = torch.tensor([out.get("tp_tok_s", 0.0)], dtype=torch.float64, device="cuda")
-    dist.all_reduce(ms, op=dist.ReduceOp.MIN)                         # slowest rank
-    dist.barrier()          # no rank releases its exchange region while a peer may read it
-    if eng is not None:
-        eng.close()
-    if rank == 0 and "error" not in out:
-        out["tp_tok_s"] = round(float(ms.item()), 2)
-        w1 = init_random_weights(cfg, 0, device=f"cuda:{local}", dtype=torch.bfloat16)
-        one = Engine(cfg, sch, w1, device=local, max_context=256, max_prompt=n_prompt)
-        generate_loopspec(one, prompt, n_new)
-        ids1, st1 = generate_loopspec(one, prompt, n_new)
-        one.close()
-        out["single_gpu_tok_s"] = round(st1["decode_tokens"] / (st1["decode_device_ms"] / 1e3), 2)
-        out["tokens_equal_single_gpu"] = ids1 == out.pop("tp_ids")
-        out["speedup_vs_single_gpu"] = round(out["tp_tok_s"] / out["single_gpu_tok_s"], 3)
-    out.pop("tp_ids", None)
-    dist.barrier()
+            w = init_random_weights(cfg, 0, device=f"cuda:{local}", dtype=torch.bfloat16)
+            eng = Engine(shard_config(cfg, world), sch, shard_weights(w, cfg, rank, world), device=local,
+                         max_context=256, max_prompt=n_prompt, max_requests=n_req)
+            del w
+            handle = eng.tp_init(rank, world)
+        except Exception as ex:   # noqa: BLE001 - reported, the replica line still prints
+            ok, handle, res["error"] = False, b"", repr(ex)[:300]
+        got = [None] * world
+        dist.all_gather_object(got, (ok, handle))
+        ids = None
+        if all(g[0] for g in got):
+            try:
+                eng.tp_attach([g[1] for g in got])
+                ids, rate = decode(eng, n_req)
+                res["tp_tok_s"] = round(rate, 2)
+            except Exception as ex:   # noqa: BLE001
+                res["error"] = repr(ex)[:300]
+        ms = torch.tensor([res.get("tp_tok_s", 0.0)], dtype=torch.float64, device="cuda")
+        dist.all_reduce(ms, op=dist.ReduceOp.MIN)                     # slowest rank
+        dist.barrier()      # no rank releases its exchange region while a peer may read it
+        if eng is not None:
+            eng.close()
+        if rank == 0 and "error" not in res:
+            res["tp_tok_s"] = round(float(ms.item()), 2)
+            w1 = init_random_weights(cfg, 0, device=f"cuda:{local}", dtype=torch.bfloat16)
+            one = Engine(cfg, sch, w1, device=local, max_context=256, max_prompt=n_prompt,
+                         max_requests=n_req)
+            ids1, rate1 = decode(one, n_req)
+            one.close()
+            res["single_gpu_tok_s"] = round(rate1, 2)
+            res["tokens_equal_single_gpu"] = ids1 == ids
+            res["speedup_vs_single_gpu"] = round(res["tp_tok_s"] / res["single_gpu_tok_s"], 3)
+        dist.barrier()
+        return res
+
+    out.update(measure(1))
+    out["batch8_mixed"] = measure(n_batch)
     return out
 
 
@@ -535,6 +557,8 @@ def batch_arm(args):
     eng = Engine(cfg, sch, weights, device=local, max_context=args.prompt + args.new_tokens + 64,
                  max_prompt=args.prompt, max_requests=max(1, len(mine)))
     samp = sampling_of(args)
+    if args.mixed and samp is not None:
+        samp = [None if i % 2 == 0 else samp for i in mine]
 
     def run(step, mode):
         prompts, _ = batch_of(step)
@@ -590,7 +614,8 @@ def batch_arm(args):
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (uniform-random prompt ids and lengths, random-init weights seed 0)",
             "config": {"workload": f"{cfg.name} LoopSpec first={args.first} second={args.second} "
-                                   f"{decode_mode(args)}, batch {args.batch} (split over {world} GPUs), "
+                                   f"{decode_mode(args)}{' (every other request greedy)' if args.mixed else ''}, "
+                                   f"batch {args.batch} (split over {world} GPUs), "
                                    f"prompts {lo}-{args.prompt}, {args.new_tokens} new tokens",
                        "global_batch": args.batch, "seq_len": args.prompt + args.new_tokens,
                        "parallelism": f"requests split over {world} GPUs", "l2": l2_note(cfg)},

@@ -1078,7 +1078,8 @@ void resid(ls_engine& e, ResidArgs a, int n) {
 }
 
 // ------------------------------------------------------- tensor parallelism
-constexpr size_t kTpEpochOff = 64;   // byte offset of the epoch counter in a region
+constexpr size_t kTpEpochOff = 64;    // byte offset of the epoch counter in a region
+constexpr size_t kTpTicketOff = 128;  // this rank's publish tickets, one per slot (not read by peers)
 
 // Every rank's buffer at byte offset `off` of its region, in rank order.
 TpView tp_view(const ls_engine& e, size_t off) {
@@ -1101,9 +1102,14 @@ void tp_publish(ls_engine& e, int slot) {
 // A row-sharded projection (O or down): this rank's split planes go to its
 // exchange region and are published; the residual kernel that follows adds
 // every rank's planes.
+// The GEMM's last CTA publishes (no separate publish launch).
 void tp_split_store(ls_engine& e, const Gemm& g, XBuf& x, int n, ResidArgs& ra, size_t off, int slot) {
-  gemm_split_store(e, g, x, n, reinterpret_cast<float*>(e.tp_region + off));
-  tp_publish(e, slot);
+  GemmEpi ep = store_to(reinterpret_cast<float*>(e.tp_region + off));
+  ep.split_stride = (long)e.cap * g.Mw;
+  ep.pub_epoch = reinterpret_cast<int*>(e.tp_region + kTpEpochOff);
+  ep.pub_flag = reinterpret_cast<int*>(e.tp_region) + slot;
+  ep.pub_ticket = reinterpret_cast<int*>(e.tp_region + kTpTicketOff) + slot;
+  gemm(e, g, x, ep, kEpiSplitStore, n);
   ra.tp = tp_view(e, off);
   ra.tp_slot = slot;
 }

@@ -67,6 +67,11 @@ struct GemmEpi {
   long split_stride;          // split store: floats between split planes of out
   const int* active;          // device-resident loop: number of live lanes of the call (a prefix
                               // of the n_valid lanes), read at run time; null: all n_valid
+  // split store into a tensor-parallel exchange region: the last CTA to
+  // finish advances this rank's epoch and raises its flag (null: no publish)
+  int* pub_epoch;
+  int* pub_flag;
+  int* pub_ticket;            // zero between launches
 };
 
 // SUB 64-wide sub-tiles per ring stage along K: the MMA thread's per-stage
@@ -238,7 +243,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __shared__ int s_last;
   __syncthreads();
   if (warp == 2) tmem_dealloc(tmem, L::kTmemCols);
-  if (EPI == kEpiSplitStore) return;
+  if (EPI == kEpiSplitStore) {
+    if (epi.pub_flag && threadIdx.x == 0) {
+      // the barrier above ordered the CTA's plane stores before this thread's
+      // system-scope fence; the last CTA's fence after its ticket orders every
+      // CTA's stores before the flag the peers acquire
+      __threadfence_system();
+      const int total = gridDim.x * gridDim.y * gridDim.z;
+      if (atomicAdd(epi.pub_ticket, 1) == total - 1) {
+        __threadfence_system();
+        *epi.pub_ticket = 0;   // ready for the next launch
+        const int ep = atomicAdd(epi.pub_epoch, 1) + 1;
+        asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(epi.pub_flag), "r"(ep) : "memory");
+      }
+    }
+    return;
+  }
   if (splits > 1) {
     if (threadIdx.x == 0) {
       int* tk = epi.tile_tickets + tile_id;

@@ -201,8 +201,7 @@ __global__ void tp_publish_kernel(int* epoch, int* flags, int slot) {
   pdl_wait();
   if (threadIdx.x == 0) {
     __threadfence_system();
-    const int e = *epoch + 1;
-    *epoch = e;
+    const int e = atomicAdd(epoch, 1) + 1;   // (the O / down GEMMs advance it the same way)
     st_release_sys(flags + slot, e);
   }
 }
