@@ -26,9 +26,10 @@
 // and writes the decision row (token, proposed, accepted_code, q1_rejected,
 // q2_rejected) of policy.py:197-283. A row whose request decodes greedily
 // (top_k == 1) in a batch with sampled requests takes the argmax of its
-// logits (lowest index on ties, as the greedy path) as the row's token. Single probabilities (P[x], F[y]) are
-// recomputed by every CTA from the logits with the slice loops' operations, so
-// every CTA takes the same branch. Draws invert a CDF in chunks of 2048
+// logits (lowest index on ties, as the greedy path) as the row's token.
+// Single probabilities (P[x], F[y]) are recomputed by every CTA from the
+// logits with the slice loops' operations, so every CTA takes the same
+// branch. Draws invert a CDF in chunks of 2048
 // tokens like the reference. Uniforms: words of Philox4x32-10 with counter
 // (cycle, readout row of the request, 0, 0) and the request's seed as key,
 // u = (w >> 8) * 2^-24 (cycle, row and seed come with the row's metadata).
