@@ -104,6 +104,7 @@ struct Gemm {
   CUtensorMap map;      // 128-row weight boxes
   CUtensorMap map64;    // 64-row boxes (gate/up halves of the SwiGLU tile)
   bool has_map64 = false;
+  bool cluster = false;  // split store: the tile's splits add their partials in the GEMM (one plane)
 };
 
 struct XBuf {
@@ -587,6 +588,12 @@ struct ls_engine {
     return std::max(1, std::min(std::min(s, KB), kMaxSplits));
   }
 
+  Gemm cluster_gemm(const bf16* w, int Mw, int Kd) {
+    Gemm g = make_gemm(w, Mw, Kd, std::min(choose_splits(Mw, Kd), kMaxClusterSplits));
+    g.cluster = g.splits > 1;
+    return g;
+  }
+
   Gemm make_gemm(const bf16* w, int Mw, int Kd, int splits = 0, bool swiglu = false) {
     Gemm g;
     g.w = w;
@@ -630,9 +637,11 @@ struct ls_engine {
         lw.kn = W(p + "self_attn.k_norm.weight", {KVD});
       }
       lw.g_qkv = make_gemm(lw.qkv, QD + 2 * KVD, H);
-      lw.g_o = make_gemm(lw.o, H, QD);
+      // O and down (and the adapter): at most 16 K splits, added inside the
+      // GEMM by each tile's cluster, so the row kernel after them reads one plane
+      lw.g_o = cluster_gemm(lw.o, H, QD);
       lw.g_gu = make_gemm(lw.gu, 2 * I, H, 0, true);
-      lw.g_down = make_gemm(lw.down, H, I);
+      lw.g_down = cluster_gemm(lw.down, H, I);
     }
   }
 
@@ -747,7 +756,7 @@ struct ls_engine {
     if (mc.family == LS_FAMILY_OURO) {
       step_norm = W("recurrent_executor.step_norm.weight", {H});
     } else {
-      g_adapter = make_gemm(W("recurrent_executor.adapter.weight", {H, 2 * H}), H, 2 * H);
+      g_adapter = cluster_gemm(W("recurrent_executor.adapter.weight", {H, 2 * H}), H, 2 * H);
       if (mc.adapter_bias) adapter_b = W("recurrent_executor.adapter.bias", {H});
       final_norm = W("post_executor.final_norm.weight", {H});
     }
@@ -845,7 +854,10 @@ struct ls_engine {
   LS_SMEM1(BN, ST, kEpiQkvRope); \
   LS_SMEM1(BN, ST, kEpiSwiGLU);  \
   LS_SMEM1(BN, ST, kEpiSplitStore);  \
-  LS_SMEM1(BN, ST, kEpiStoreArgmax)
+  LS_SMEM1(BN, ST, kEpiStoreArgmax); \
+  LS_SMEM1(BN, ST, kEpiClusterStore); \
+  CK(cudaFuncSetAttribute(gemm_tc_kernel<BN, ST, kEpiClusterStore>,  \
+                          cudaFuncAttributeNonPortableClusterSizeAllowed, 1))
     LS_SMEM(16, 4);
     LS_SMEM(32, 4);
     LS_SMEM(64, 4);
@@ -897,20 +909,32 @@ void gemm(ls_engine& e, const Gemm& g, XBuf& x, const GemmEpi& epi, int kind, in
   cfg.gridDim = dim3(m_tiles, splits, cdiv(2 * n, bn));
   cfg.blockDim = dim3(kGemmThreads);
   cfg.stream = e.stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (kind == kEpiClusterStore) {   // the K splits of a tile form one cluster
+    REQUIRE(splits >= 1 && splits <= kMaxClusterSplits, LS_EINVAL, "cluster store needs <= 16 splits");
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = 1;
+    attr[na].val.clusterDim.y = (unsigned)splits;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  if (e.sc.use_pdl && !e.serialize_next) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = e.sc.use_pdl && !e.serialize_next ? 1 : 0;
+  cfg.numAttrs = na;
   e.serialize_next = false;
   GemmEpi ep = epi;
   ep.active = e.gemm_active;
   ep.part_ws = e.gemm_part;
   ep.tile_tickets = e.gemm_tickets;
-  REQUIRE(splits == 1 || (long)cfg.gridDim.x * cfg.gridDim.z <= e.gemm_ticket_count, LS_EINVAL,
-          "GEMM tile tickets too small");
+  REQUIRE(splits == 1 || kind == kEpiClusterStore ||
+              (long)cfg.gridDim.x * cfg.gridDim.z <= e.gemm_ticket_count, LS_EINVAL, "GEMM tile tickets too small");
   REQUIRE((long)cfg.gridDim.x * cfg.gridDim.z * splits * (bn / 2) * kGemmBM <= e.gemm_part_elems ||
-              splits == 1, LS_EINVAL, "GEMM partial scratch too small");
+              splits == 1 || kind == kEpiClusterStore, LS_EINVAL, "GEMM partial scratch too small");
   const CUtensorMap& wm = kind == kEpiSwiGLU ? g.map64 : g.map;
 #define LS_GEMM_K(BN, ST, EPI)                                                                     \
   do {                                                                                              \
@@ -923,6 +947,7 @@ void gemm(ls_engine& e, const Gemm& g, XBuf& x, const GemmEpi& epi, int kind, in
     if (kind == kEpiQkvRope) LS_GEMM_K(BN, ST, kEpiQkvRope);      \
     else if (kind == kEpiSwiGLU) LS_GEMM_K(BN, ST, kEpiSwiGLU);   \
     else if (kind == kEpiSplitStore) LS_GEMM_K(BN, ST, kEpiSplitStore); \
+    else if (kind == kEpiClusterStore) LS_GEMM_K(BN, ST, kEpiClusterStore); \
     else if (kind == kEpiStoreArgmax) LS_GEMM_K(BN, ST, kEpiStoreArgmax); \
     else LS_GEMM_K(BN, ST, kEpiStore);                            \
   } while (0)
@@ -948,13 +973,19 @@ void gemm_store(ls_engine& e, const Gemm& g, XBuf& x, float* out, int n, int lan
   gemm(e, g, x, store_to(out), kEpiStore, n, lane0);
 }
 
-// y as g.splits partial planes [split][cap][Mw] in e.part, for a row kernel
-// that adds them in split order (no split-K ticket or re-read in the GEMM).
+// y as partial planes [plane][cap][Mw] in e.part (or `planes`) for a
+// consumer that adds them in plane order. For a cluster GEMM (O, down,
+// adapter) the splits of each tile add their partials inside the GEMM through
+// distributed shared memory and leave one plane (plane_count); otherwise each
+// split writes its own plane (no split-K ticket or re-read either way).
 void gemm_split_store(ls_engine& e, const Gemm& g, XBuf& x, int n, float* planes = nullptr) {
   GemmEpi ep = store_to(planes ? planes : e.part);
   ep.split_stride = (long)e.cap * g.Mw;
-  gemm(e, g, x, ep, kEpiSplitStore, n);
+  gemm(e, g, x, ep, g.cluster && !planes ? kEpiClusterStore : kEpiSplitStore, n);
 }
+
+// Planes gemm_split_store leaves in e.part for its consumer.
+int plane_count(const Gemm& g) { return g.cluster ? 1 : g.splits; }
 
 template <typename... KArgs, typename... Args>
 void klaunch(ls_engine& e, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
@@ -1025,7 +1056,7 @@ void attention(ls_engine& e, Meta meta, int n, bf16* kp, bf16* vp, const Gemm* p
              nullptr, nullptr, 1.0f / std::sqrt((float)e.HD), e.err_dev};
   if (planes) {
     a.qkv = e.part;
-    a.qkv_splits = planes->splits;
+    a.qkv_splits = plane_count(*planes);
     a.qkv_stride = (long)e.cap * planes->Mw;
     a.inv_freq = e.inv_freq;
     a.kpool_w = kp;
@@ -1052,7 +1083,7 @@ ResidArgs resid_base(ls_engine& e, Meta meta, const Gemm& g) {
   a.meta = meta;
   a.H = e.H;
   a.part = e.part;   // the GEMM's split planes (gemm_split_store)
-  a.splits = g.splits;
+  a.splits = plane_count(g);   // (the TP exchange keeps every split's plane)
   a.split_stride = (long)e.cap * g.Mw;
   a.bank_rows = e.bank_rows;
   a.eps = e.mc.rms_eps;
@@ -1111,6 +1142,7 @@ void tp_split_store(ls_engine& e, const Gemm& g, XBuf& x, int n, ResidArgs& ra, 
   ep.pub_ticket = reinterpret_cast<int*>(e.tp_region + kTpTicketOff) + slot;
   gemm(e, g, x, ep, kEpiSplitStore, n);
   ra.tp = tp_view(e, off);
+  ra.splits = g.splits;
   ra.tp_slot = slot;
 }
 
@@ -1138,7 +1170,7 @@ void run_stack(ls_engine& e, Stack& st, int n, Meta meta, const StackEnd& end) {
     if (w.qn) {
       // OLMo2 QK-norm needs whole-row sums: plain GEMM, then the QKV kernel.
       gemm_split_store(e, w.g_qkv, e.x_h, n);
-      QkvArgs qa{meta, e.NH, e.NKV, e.HD, e.part, w.g_qkv.splits, (long)e.cap * w.g_qkv.Mw,
+      QkvArgs qa{meta, e.NH, e.NKV, e.HD, e.part, plane_count(w.g_qkv), (long)e.cap * w.g_qkv.Mw,
                  w.qn, w.kn, e.inv_freq, e.mc.rms_eps,
                  e.q, kp, vp, e.n_slots, e.err_dev};
       const size_t smem = (size_t)(e.QD + 2 * e.KVD) * sizeof(float);

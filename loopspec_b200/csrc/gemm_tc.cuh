@@ -46,7 +46,27 @@ constexpr int kGemmThreads = 128;
 constexpr int kMaxSplits = 32; // K splits per 128-row tile
 
 enum GemmEpiKind : int { kEpiStore = 0, kEpiQkvRope = 1, kEpiSwiGLU = 2, kEpiSplitStore = 3,
-                         kEpiStoreArgmax = 4 };
+                         kEpiStoreArgmax = 4, kEpiClusterStore = 5 };
+
+// kEpiClusterStore: the K splits of one output tile form a thread-block
+// cluster (1, splits, 1); each parks its partial tile in shared memory, and
+// after a cluster barrier split r adds every split's values for its 1/splits
+// of the tile, in split order, through distributed shared memory and writes
+// the one summed plane. The consumer reads one plane instead of `splits`.
+constexpr int kMaxClusterSplits = 16;   // non-portable cluster size
+
+__device__ __forceinline__ void gemm_cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ float gemm_ld_cluster(const float* p, uint32_t rank) {
+  const uint32_t a = (uint32_t)__cvta_generic_to_shared(p);
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(rank));
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(r) : "memory");
+  return v;
+}
 
 struct GemmEpi {
   float* out;                 // store: out[n * Mw + m]
@@ -235,7 +255,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           continue;
         }
         red[(c0 / 2 + j) * kGemmBM + r] = s;
-        if (splits > 1) tile_part[split * split_floats + (c0 / 2 + j) * kGemmBM + r] = s;
+        if (EPI != kEpiClusterStore && splits > 1)
+          tile_part[split * split_floats + (c0 / 2 + j) * kGemmBM + r] = s;
       }
     }
   }
@@ -243,6 +264,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __shared__ int s_last;
   __syncthreads();
   if (warp == 2) tmem_dealloc(tmem, L::kTmemCols);
+  if (EPI == kEpiClusterStore) {
+    // every CTA of the cluster reaches both barriers (lanes_here is the same
+    // for all splits of a tile)
+    gemm_cluster_sync();   // every split's partial tile is parked
+    const int E = max(0, lanes_here) * kGemmBM;
+    const int e0 = (int)((long)split * E / splits), e1 = (int)((long)(split + 1) * E / splits);
+    for (int e = e0 + (int)threadIdx.x; e < e1; e += blockDim.x) {
+      float v[kMaxClusterSplits];
+#pragma unroll
+      for (int s = 0; s < kMaxClusterSplits; ++s) v[s] = s < splits ? gemm_ld_cluster(red + e, (uint32_t)s) : 0.f;
+      float t = 0.f;
+#pragma unroll
+      for (int s = 0; s < kMaxClusterSplits; ++s)
+        if (s < splits) t += v[s];
+      const int l = e / kGemmBM, rr = e - l * kGemmBM;
+      if (m0 + rr < Mw) epi.out[(long)(n0 / 2 + l) * Mw + m0 + rr] = t;
+    }
+    gemm_cluster_sync();   // no CTA leaves while another may still read its tile
+    return;
+  }
   if (EPI == kEpiSplitStore) {
     if (epi.pub_flag && threadIdx.x == 0) {
       // the barrier above ordered the CTA's plane stores before this thread's
