@@ -57,6 +57,8 @@ struct DsLane {
 template <int MAXD>
 struct DsNode {
   int id, parent, child_count, live, used;
+  int prev, next;     // neighbours in the list of nodes in use by ascending id (-1: none)
+  int mapped;         // 1 if the id map's slot of `id` holds this node
   int cur[3][MAXD];   // cursor index per (role, depth), -1 if none
 };
 
@@ -70,7 +72,7 @@ struct DsFill {
   int kind, first, second;   // post rows
 };
 
-template <int MAXL, int MAXB, int MAXD, int MAXN, int MAXC, int MAXR>
+template <int MAXL, int MAXB, int MAXD, int MAXN, int MAXC, int MAXR, int IDS = pow2_at_least(4 * MAXN)>
 struct alignas(16) DevSched {
   // schedule and request
   int S, K, X, max_rows, max_new, q1, q2, final_stage;
@@ -99,8 +101,17 @@ struct alignas(16) DevSched {
                         // first_rejections, second_verifications, second_acceptances, second_rejections
   // timelines
   static constexpr int kNodeWords = (MAXN + 63) / 64, kCurWords = (MAXC + 63) / 64;
+  // branch id -> node index, direct-mapped on id mod kIdSlots (-1 = empty).
+  // Live ids are a narrow window of a counter, so two nodes in use rarely
+  // share a slot; one that finds its slot taken is counted in n_unmapped and
+  // found by a scan.
+  static constexpr int kIdSlots = IDS;
+  static_assert((IDS & (IDS - 1)) == 0, "the id map's size is a power of two");
   DsNode<MAXD> nodes[MAXN];
   DsCursor cursors[MAXC];
+  int id_slot[kIdSlots];
+  int n_unmapped;
+  int node_head, node_tail;                   // ends of the ascending-id list
   unsigned long long node_bits[kNodeWords];   // bit i: nodes[i] in use
   unsigned long long cur_bits[kCurWords];     // bit i: cursors[i] in use
   int n_free_rows;
@@ -112,10 +123,8 @@ struct alignas(16) DevSched {
     if (!err) err = code;
   }
 
-  // Lowest set (or, inverted, clear) bit of a word array; -1 if none. The
-  // scans below visit only the nodes in use, in increasing index, so a
-  // lookup costs a few shared-memory round trips on the GPU thread instead
-  // of one per table entry.
+  // Lowest set (or, inverted, clear) bit of a word array; -1 if none. A
+  // scan of the bits visits only the entries in use, in increasing index.
   static LS_HD int ctz64(unsigned long long x) {
 #ifdef __CUDA_ARCH__
     return __ffsll((long long)x) - 1;
@@ -132,15 +141,13 @@ struct alignas(16) DevSched {
       }
     return -1;
   }
-  // calls f(i) for every node in use, in increasing index
-  template <class F>
-  LS_HD void for_used_nodes(F f) const {
-    for (int w = 0; w < kNodeWords; ++w)
-      for (unsigned long long m = node_bits[w]; m; m &= m - 1) f(w * 64 + ctz64(m));
-  }
-
+  // the node of branch `id`, or -1: one id-map probe, a scan of the nodes in
+  // use only while some node is unmapped
   LS_HD int node_of(int id) const {
     if (id < 0) return -1;
+    const int m = id_slot[id & (kIdSlots - 1)];
+    if (m >= 0 && nodes[m].id == id) return m;   // a slot only ever holds a node in use
+    if (n_unmapped == 0) return -1;
     for (int w = 0; w < kNodeWords; ++w)
       for (unsigned long long m = node_bits[w]; m; m &= m - 1) {
         const int i = w * 64 + ctz64(m);
@@ -231,12 +238,40 @@ struct alignas(16) DevSched {
     n.live = 1;
     for (int r = 0; r < 3; ++r)
       for (int d = 0; d < MAXD; ++d) n.cur[r][d] = -1;
+    int& slot = id_slot[id & (kIdSlots - 1)];
+    n.mapped = slot < 0;
+    if (n.mapped) slot = i;
+    else ++n_unmapped;
+    // ids come from a counter, so a new node almost always goes at the tail
+    int t = node_tail;
+    while (t >= 0 && nodes[t].id > id) t = nodes[t].prev;
+    n.prev = t;
+    n.next = t >= 0 ? nodes[t].next : node_head;
+    if (n.next >= 0) nodes[n.next].prev = i;
+    else node_tail = i;
+    if (t >= 0) nodes[t].next = i;
+    else node_head = i;
     return i;   // (depths >= S stay -1: loops below stop at S)
   }
 
   LS_HD void free_node(int i) {
-    nodes[i].used = 0;
+    DsNode<MAXD>& n = nodes[i];
+    n.used = 0;
     node_bits[i / 64] &= ~(1ull << (i % 64));
+    if (n.mapped) id_slot[n.id & (kIdSlots - 1)] = -1;
+    else --n_unmapped;
+    if (n.prev >= 0) nodes[n.prev].next = n.next;
+    else node_head = n.next;
+    if (n.next >= 0) nodes[n.next].prev = n.prev;
+    else node_tail = n.prev;
+  }
+
+  // an empty node table (before the root is created)
+  LS_HD void clear_nodes() {
+    for (int w = 0; w < kNodeWords; ++w) node_bits[w] = 0;
+    for (int h = 0; h < kIdSlots; ++h) id_slot[h] = -1;
+    n_unmapped = 0;
+    node_head = node_tail = -1;
   }
 
   // -------------------------------------- timelines (manager.py:207-482)
@@ -331,15 +366,16 @@ struct alignas(16) DevSched {
       if (l.branch && node_of(l.branch) < 0) get_or_create_branch(l.branch, l.parent);
     }
     // unused live nodes, released from the highest id down
+    unsigned long long kept[kNodeWords];
+    for (int w = 0; w < kNodeWords; ++w) kept[w] = 0;
+    for (int k = 0; k < nk; ++k) {
+      const int n = node_of(keep[k].branch);
+      if (n >= 0) kept[n / 64] |= 1ull << (n % 64);
+    }
     int ids[MAXN];
     int nu = 0;
-    for_used_nodes([&](int i) {
-      if (!nodes[i].live) return;
-      bool kept = false;
-      for (int k = 0; k < nk && !kept; ++k) kept = keep[k].branch == nodes[i].id;
-      if (!kept) ids[nu++] = i;
-    });
-    sort_by_id(ids, nu, false);
+    for (int i = node_tail; i >= 0; i = nodes[i].prev)
+      if (nodes[i].live && !(kept[i / 64] >> (i % 64) & 1)) ids[nu++] = i;
     for (int k = 0; k < nu; ++k) {
       const int n = ids[k];
       if (!nodes[n].used) continue;
@@ -348,25 +384,9 @@ struct alignas(16) DevSched {
     }
     // single surviving children adopt their dead parents' timelines (ascending id)
     int na = 0;
-    for_used_nodes([&](int i) { ids[na++] = i; });
-    sort_by_id(ids, na, true);
+    for (int i = node_head; i >= 0; i = nodes[i].next) ids[na++] = i;
     for (int k = 0; k < na; ++k)   // no node is created here, so a freed index stays free
       if (nodes[ids[k]].used) detach_from_unused_parent(ids[k]);
-  }
-
-  // sort node indices by their ids (insertion sort: a handful of live nodes)
-  LS_HD void sort_by_id(int* idx, int n, bool ascending) const {
-    for (int i = 1; i < n; ++i)
-      for (int j = i; j > 0; --j) {
-        const int a = nodes[idx[j - 1]].id, b = nodes[idx[j]].id;
-        if (ascending ? a > b : a < b) {
-          const int t = idx[j - 1];
-          idx[j - 1] = idx[j];
-          idx[j] = t;
-        } else {
-          break;
-        }
-      }
   }
 
   // ------------------------------------ pipeline (pipeline.py:254-423)
@@ -679,6 +699,7 @@ inline void ds_start(D& d, int S, int K, int X, int max_rows, int max_new, long 
   d.next_branch = 1;
   d.clear_parents();
   d.set_parent(0, -1);
+  d.clear_nodes();
   d.new_node(0, -1);
   d.committed = 1;
   out[0] = first;

@@ -2869,7 +2869,76 @@ namespace {
 // The device loop's scheduler state compiled for the host, with capacities for
 // every schedule (S <= 32, up to 256 live lanes).
 using HostSched = DevSched<256, 4096, 32, 2048, 16384, 32768>;
+// The same with a 4-slot id map, so that most lookups take the scan fallback.
+using HostSchedNarrowMap = DevSched<256, 4096, 32, 2048, 16384, 32768, 4>;
+constexpr int kSimRows = 16384;   // mapping rows of a simulated request
 }  // namespace
+
+extern "C++" {
+namespace {
+
+// Invariants of a scheduler's node, cursor and row tables: the ascending-id
+// list holds exactly the nodes in use, every node is found by its id, the id
+// map and unmapped count agree with the nodes (an unmapped node's slot may
+// have emptied since), and the cursors of the nodes in use are distinct, in
+// use, and on distinct rows that are not free.
+template <class D>
+void check_tables(const D& d, std::vector<int>& row_seen, std::vector<int>& cur_seen) {
+  int n_used = 0;
+  for (int i = 0; i < (int)(sizeof(d.nodes) / sizeof(d.nodes[0])); ++i) n_used += d.nodes[i].used;
+  int n_list = 0, n_unmapped = 0, prev = -1;
+  for (int i = d.node_head; i >= 0; i = d.nodes[i].next) {
+    const auto& n = d.nodes[i];
+    REQUIRE(n.used && n.prev == prev && (prev < 0 || d.nodes[prev].id < n.id), LS_EPIPELINE,
+            "device scheduler: node list out of order");
+    REQUIRE(d.node_of(n.id) == i, LS_EPIPELINE, "device scheduler: node lookup failed");
+    const int h = n.id & (D::kIdSlots - 1);
+    REQUIRE(n.mapped ? d.id_slot[h] == i : d.id_slot[h] != i, LS_EPIPELINE,
+            "device scheduler: id map out of step");
+    n_unmapped += !n.mapped;
+    prev = i;
+    ++n_list;
+  }
+  REQUIRE(n_list == n_used && d.node_tail == prev && n_unmapped == d.n_unmapped, LS_EPIPELINE,
+          "device scheduler: node list incomplete");
+  std::fill(row_seen.begin(), row_seen.end(), 0);
+  std::fill(cur_seen.begin(), cur_seen.end(), 0);
+  for (int k = 0; k < d.n_free_rows; ++k) row_seen[d.free_rows[k]] += 1;
+  for (int i = d.node_head; i >= 0; i = d.nodes[i].next)
+    for (int r = 0; r < 3; ++r)
+      for (int t = 0; t < d.S; ++t) {
+        const int c = d.nodes[i].cur[r][t];
+        if (c < 0) continue;
+        REQUIRE(d.cursors[c].used && cur_seen[c]++ == 0, LS_EPIPELINE, "device scheduler: cursor shared or freed");
+        row_seen[d.cursors[c].row] += 1;
+      }
+  for (int v : row_seen)
+    REQUIRE(v == 1, LS_EPIPELINE, "device scheduler: mapping row lost or shared");
+}
+
+// Start a simulated request: rows 0..kSimRows-1 free, unbounded KV slots, and
+// root cursors for every role and depth, so that plan() forks and releases
+// timelines as on the GPU.
+template <class D>
+void sim_start(D& d, int S, int K, int X, int max_rows, int max_new, long long stop_token, long long first,
+               long long* out) {
+  ds_start(d, S, K, X, max_rows, max_new, stop_token, first, out);
+  d.has_pre = d.has_post = 1;
+  d.n_free_rows = kSimRows;
+  for (int r = 0; r < kSimRows; ++r) d.free_rows[r] = kSimRows - 1 - r;
+  d.next_slot = 0;
+  d.slot_limit = 0x7fffffff;
+  for (int r = 0; r < 3; ++r)
+    for (int t = 0; t < S; ++t) d.nodes[0].cur[r][t] = d.new_cursor(d.alloc_row(), 0, -1);
+}
+
+template <class D>
+void sim_plan(D& d, std::vector<DsFill>& pre, std::vector<DsFill>& core, std::vector<DsFill>& post) {
+  int n_pre = 0, n_post = 0;
+  d.plan(pre.data(), n_pre, core.data(), post.data(), n_post);
+}
+}  // namespace
+}  // extern "C++"
 
 int ls_device_loop_simulate(int stages, int step_size, int second_step, int64_t first_token,
                             int max_new_tokens, int64_t stop_token, ls_decide_fn decide,
@@ -2891,12 +2960,32 @@ int ls_device_loop_simulate(int stages, int step_size, int second_step, int64_t 
     int max_rows = 0;
     for (long v : b) max_rows += (int)v;
     REQUIRE(max_rows <= 256, LS_ECAPACITY, "schedule needs more than 256 lanes");
+    // the scheduler, and a shadow with a 4-slot id map fed the same decisions:
+    // apart from their id maps the two must stay identical
     std::unique_ptr<HostSched> d(new HostSched());
-    std::vector<long long> out(max_new_tokens);
-    ds_start(*d, S, K, X, max_rows, max_new_tokens, stop_token, first_token, out.data());
-    d->n_free_rows = 0;
-    d->next_slot = 0;
-    d->slot_limit = 0x7fffffff;
+    std::unique_ptr<HostSchedNarrowMap> w(new HostSchedNarrowMap());
+    std::vector<long long> out(max_new_tokens), out_w(max_new_tokens);
+    sim_start(*d, S, K, X, max_rows, max_new_tokens, stop_token, first_token, out.data());
+    sim_start(*w, S, K, X, max_rows, max_new_tokens, stop_token, first_token, out_w.data());
+    std::vector<DsFill> pre(256), core(256 * 32), post(256);
+    std::vector<int> row_seen(kSimRows), cur_seen(16384);
+    auto check = [&]() {
+      check_tables(*d, row_seen, cur_seen);
+      check_tables(*w, row_seen, cur_seen);
+      bool same = d->n_lanes == w->n_lanes && d->committed == w->committed && d->err == w->err &&
+                  d->done == w->done && d->next_slot == w->next_slot && d->n_free_rows == w->n_free_rows;
+      for (int i = 0; same && i < d->n_lanes; ++i)
+        same = std::memcmp(&d->lanes[i], &w->lanes[i], sizeof(DsLane)) == 0;
+      for (int i = 0; same && i < (int)(sizeof(d->nodes) / sizeof(d->nodes[0])); ++i) {
+        const auto &a = d->nodes[i], &b = w->nodes[i];
+        same = a.used == b.used &&
+               (!a.used || (a.id == b.id && a.parent == b.parent && a.child_count == b.child_count &&
+                            a.live == b.live && a.prev == b.prev && a.next == b.next &&
+                            std::memcmp(a.cur, b.cur, sizeof(a.cur)) == 0));
+      }
+      REQUIRE(same, LS_EPIPELINE, "device scheduler: the narrow-map shadow diverged");
+    };
+    check();
     auto report_retain = [&]() {
       std::vector<int64_t> pairs;
       for (int i = 0; i < d->n_lanes; ++i) {
@@ -2909,6 +2998,9 @@ int ls_device_loop_simulate(int stages, int step_size, int second_step, int64_t 
     std::vector<long long> dec;
     while (!d->done && !d->err) {
       const int n = d->gather();
+      w->gather();
+      sim_plan(*d, pre, core, post);
+      sim_plan(*w, pre, core, post);
       std::vector<int64_t> rows;
       dec.assign(n, -1);
       for (int i = 0; i < n; ++i) {
@@ -2920,6 +3012,8 @@ int ls_device_loop_simulate(int stages, int step_size, int second_step, int64_t 
       }
       if (on_cycle) on_cycle(user, rows.data(), (int32_t)n);
       d->consume(dec.data(), 1, out.data());
+      w->consume(dec.data(), 1, out_w.data());
+      check();
       report_retain();
     }
     REQUIRE(d->err == kDsOk, LS_EPIPELINE, "device scheduler reported error " + std::to_string(d->err));
