@@ -843,6 +843,9 @@ __global__ void __launch_bounds__(kLoopThreads) loop_step_kernel(LoopSched* g, c
   // the state was written by the previous cycle's step: load it while the
   // post call finishes, then wait for the decisions
   __shared__ long long s_dec_in[kLoopMaxLanes * 5];
+  // the next cycle's first kernel may start now: it reads nothing before its
+  // own wait, which ends when this kernel has completed
+  pdl_launch_dependents();
   load_sched(&s, g);
   pdl_wait();
   // the readouts' decisions, one global round trip for all of them

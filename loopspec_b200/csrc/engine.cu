@@ -513,6 +513,7 @@ struct ls_engine {
   // triggers its dependents at its start, and attention reads the
   // timeline's slot ids before its own wait.
   bool serialize_next = false;
+  int meta_after_wait = 0;   // the next prep kernel reads its metadata only after its PDL wait
   // Set while prefill runs: its calls are up to 128 lanes wide, where the
   // QKV and gate_up projections are compute-bound, so they run unsplit (the
   // epilogue then reads the tile from shared memory instead of re-reading
@@ -1269,6 +1270,8 @@ void prep(ls_engine& e, Meta meta, int n, bool embed_mode, float* bank_out, bool
   pa.eps = e.mc.rms_eps;
   pa.vocab = e.V;
   pa.err = e.err_dev;
+  pa.meta_after_wait = e.meta_after_wait;
+  e.meta_after_wait = 0;
   const int thr = row_threads(e.H);
   const dim3 grid(n);
   if (cdiv(e.H / 4, thr) == 1) klaunch(e, prep_kernel<1>, grid, dim3(thr), 0, pa);
@@ -2090,13 +2093,16 @@ LoopMeta loop_meta_of(const ls_engine& e) {
   return LoopMeta{e.loop_meta, e.loop_meta + F, F, e.loop_meta + (1 + e.K) * F, e.max_rows, e.loop_active};
 }
 
-// One cycle as one graph: the role calls read the metadata the previous
-// scheduler kernel wrote (the post call's lm_head GEMM reduces each lane's
-// greedy token, or the sampler writes its decision rows), then the step
-// kernel resolves the decisions, commits, retains branches and plans the next
-// cycle. Nothing returns to the host between cycles.
-const ls_engine::LoopGraph& loop_graph_for(ls_engine& e, int chunks) {
-  const int key = chunks * 2 + (e.sampling ? 1 : 0);
+// `cycles` cycles as one graph. In each, the role calls read the metadata the
+// previous scheduler kernel wrote (the post call's lm_head GEMM reduces each
+// lane's greedy token, or the sampler writes its decision rows), then the
+// step kernel resolves the decisions, commits, retains branches and plans the
+// next cycle. Nothing returns to the host between cycles. Inside a graph, an
+// Ouro cycle's first kernel (the embedding prep) is launched while the step
+// kernel before it still runs, and reads the metadata after its PDL wait.
+constexpr int kLoopGraphCycles = 8;
+const ls_engine::LoopGraph& loop_graph_for(ls_engine& e, int chunks, int cycles) {
+  const int key = (chunks * 2 + (e.sampling ? 1 : 0)) * (kLoopGraphCycles + 1) + cycles;
   auto it = e.loop_graphs.find(key);
   if (it != e.loop_graphs.end()) return it->second;
   const int W = e.max_rows;
@@ -2106,41 +2112,48 @@ const ls_engine::LoopGraph& loop_graph_for(ls_engine& e, int chunks) {
   const long F = lm.stride;
   int* post = lm.post;
   int kernels = 0;
+  const bool early_prep = e.mc.family == LS_FAMILY_OURO && e.sc.use_pdl != 0;
   CK(cudaStreamBeginCapture(e.stream, cudaStreamCaptureModeThreadLocal));
   try {
-    e.qkv_planes = true;    // one new position per lane
-    e.attn_chunks = chunks;
-    e.serialize_next = true;   // the first role kernel reads the metadata the step kernel wrote
-    // the attention form is chosen for the full width, so that a cycle whose
-    // lanes are all live still runs its attention in one wave (every form
-    // computes the same values)
-    e.attn_form_lanes = W;
-    e.meta_override = pre;
-    e.gemm_active = lm.active;
-    enqueue_role(e, kPre, W);
-    kernels += e.kernels_in_call;
-    e.gemm_active = lm.active + 1;
-    for (int k = 0; k < e.K; ++k) {
-      e.meta_override = core + k * F;
-      enqueue_role(e, kCore, W);
+    for (int cyc = 0; cyc < cycles; ++cyc) {
+      e.qkv_planes = true;    // one new position per lane
+      e.attn_chunks = chunks;
+      // the first role kernel reads the metadata the step kernel wrote
+      if (cyc > 0 && early_prep) e.meta_after_wait = 1;
+      else e.serialize_next = true;
+      // the attention form is chosen for the full width, so that a cycle whose
+      // lanes are all live still runs its attention in one wave (every form
+      // computes the same values)
+      e.attn_form_lanes = W;
+      e.meta_override = pre;
+      e.gemm_active = lm.active;
+      enqueue_role(e, kPre, W);
       kernels += e.kernels_in_call;
+      e.gemm_active = lm.active + 1;
+      for (int k = 0; k < e.K; ++k) {
+        e.meta_override = core + k * F;
+        enqueue_role(e, kCore, W);
+        kernels += e.kernels_in_call;
+      }
+      e.meta_override = post;
+      e.gemm_active = lm.active + 2;
+      enqueue_role(e, kPost, W);
+      kernels += e.kernels_in_call;
+      e.meta_override = nullptr;
+      e.gemm_active = nullptr;
+      const bool pdl = e.sc.use_pdl != 0;
+      if (e.sampling)
+        launch(loop_step_kernel, dim3(1), dim3(kLoopThreads), 0, e.stream, pdl, e.loop_sched,
+               (const long long*)e.dec_dev, 5, e.loop_out, lm);
+      else
+        launch(loop_step_kernel, dim3(1), dim3(kLoopThreads), 0, e.stream, pdl, e.loop_sched,
+               (const long long*)e.amax_dev, 1, e.loop_out, lm);
+      kernels += 1;
     }
-    e.meta_override = post;
-    e.gemm_active = lm.active + 2;
-    enqueue_role(e, kPost, W);
-    kernels += e.kernels_in_call;
-    e.meta_override = nullptr;
-    e.gemm_active = nullptr;
-    const bool pdl = e.sc.use_pdl != 0;
-    if (e.sampling)
-      launch(loop_step_kernel, dim3(1), dim3(kLoopThreads), 0, e.stream, pdl, e.loop_sched,
-             (const long long*)e.dec_dev, 5, e.loop_out, lm);
-    else
-      launch(loop_step_kernel, dim3(1), dim3(kLoopThreads), 0, e.stream, pdl, e.loop_sched,
-             (const long long*)e.amax_dev, 1, e.loop_out, lm);
   } catch (...) {
     e.meta_override = nullptr;
     e.gemm_active = nullptr;
+    e.meta_after_wait = 0;
     e.attn_form_lanes = 0;
     cudaGraph_t g = nullptr;
     cudaStreamEndCapture(e.stream, &g);
@@ -2154,7 +2167,7 @@ const ls_engine::LoopGraph& loop_graph_for(ls_engine& e, int chunks) {
   const cudaError_t ie = cudaGraphInstantiate(&lg.exec, g, 0);
   cudaGraphDestroy(g);
   CK(ie);
-  lg.kernels = kernels + 1;
+  lg.kernels = kernels;
   return e.loop_graphs.emplace(key, lg).first->second;
 }
 
@@ -2202,10 +2215,15 @@ std::vector<long long> run_device_loop(ls_engine& e, Request& R, long long first
     const int nb = std::min(max_new - committed, batch_max);
     int chunks = cdiv(R.prefill_len + committed + nb + e.S + 1, kAttnChunk);
     chunks = std::min(chunks + (chunks & 1), e.max_chunks);
-    const ls_engine::LoopGraph& lg = loop_graph_for(e, chunks);
-    for (int i = 0; i < nb; ++i) CK(cudaGraphLaunch(lg.exec, e.stream));
+    const ls_engine::LoopGraph& lg = loop_graph_for(e, chunks, kLoopGraphCycles);
+    for (int i = 0; i < nb / kLoopGraphCycles; ++i) CK(cudaGraphLaunch(lg.exec, e.stream));
+    e.kernel_launches += (long)(nb / kLoopGraphCycles) * lg.kernels;
+    if (nb % kLoopGraphCycles) {
+      const ls_engine::LoopGraph& l1 = loop_graph_for(e, chunks, 1);
+      for (int i = 0; i < nb % kLoopGraphCycles; ++i) CK(cudaGraphLaunch(l1.exec, e.stream));
+      e.kernel_launches += (long)(nb % kLoopGraphCycles) * l1.kernels;
+    }
     cycles += nb;
-    e.kernel_launches += (long)nb * lg.kernels;
     CK(cudaMemcpyAsync(&h, e.loop_sched, sizeof(LoopSched), cudaMemcpyDeviceToHost, e.stream));
     e.d2h_bytes += sizeof(LoopSched);
     fetch_device_error(e);

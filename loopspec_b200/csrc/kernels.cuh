@@ -58,10 +58,14 @@ struct PrepArgs {
   float eps;
   int vocab;
   int* err;
+  int meta_after_wait;         // the lane metadata comes from the kernel before this one
 };
 
 template <int NV>
 __global__ void prep_kernel(PrepArgs a) {
+  // with metadata written by the preceding kernel, nothing is read and no
+  // dependent starts (its pre-wait reads take the metadata) before the wait
+  if (a.meta_after_wait) pdl_wait();
   pdl_launch_dependents();
   const int b = blockIdx.x;
   if (b >= a.B || a.meta.get(kMetaPos, b) < 0) return;   // inactive lane
