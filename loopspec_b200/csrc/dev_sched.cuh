@@ -23,6 +23,7 @@
 // copy of the state held in shared memory.
 #pragma once
 
+#include <stddef.h>
 #include <stdint.h>
 
 #include "common.cuh"
@@ -726,34 +727,27 @@ constexpr int kLoopMaxK = 8;
 constexpr int kLoopThreads = 256;
 
 // Lane metadata of one role call at a fixed width: `n` active lanes, the rest
-// inactive (position -1), which every per-lane kernel skips.
+// inactive (position -1), which every per-lane kernel skips. Fields 0..10 are
+// DsFill's members in order; each value is picked by selects, so the threads
+// of a warp (17 fields per lane) do not split into one path per field.
+static_assert(sizeof(DsFill) == (kMetaSecond + 1) * sizeof(int) && offsetof(DsFill, token) == 0 &&
+                  offsetof(DsFill, state_out) == kMetaStateOut * sizeof(int) &&
+                  offsetof(DsFill, kind) == kMetaKind * sizeof(int) &&
+                  offsetof(DsFill, second) == kMetaSecond * sizeof(int),
+              "DsFill holds the metadata fields token..second in order");
 __device__ inline void write_meta(int* m, int width, const DsFill* f, int n, int draw, bool post,
                                   unsigned long long seed) {
+  const int lo = (int)(uint32_t)(seed & 0xFFFFFFFFull), hi = (int)(uint32_t)(seed >> 32);
   for (int i = threadIdx.x; i < width * kMetaFields; i += blockDim.x) {
     const int b = i / kMetaFields, k = i % kMetaFields;
     int v = -1;
     if (b < n) {
-      const DsFill& x = f[b];
-      switch (k) {
-        case kMetaToken: v = x.token; break;
-        case kMetaPos: v = x.pos; break;
-        case kMetaRow: v = x.row; break;
-        case kMetaSlot: v = x.slot; break;
-        case kMetaForkRow: v = x.fork_row; break;
-        case kMetaForkLen: v = x.fork_len; break;
-        case kMetaStateIn: v = x.state_in; break;
-        case kMetaStateOut: v = x.state_out; break;
-        case kMetaKind: v = post ? x.kind : -1; break;
-        case kMetaFirst: v = post ? x.first : -1; break;
-        case kMetaSecond: v = post ? x.second : -1; break;
-        case kMetaCycle: v = post ? draw : -1; break;
-        case kMetaAhead: v = 0; break;
-        case kMetaDrawRow: v = post ? b : -1; break;
-        case kMetaSeedLo: v = post ? (int)(uint32_t)(seed & 0xFFFFFFFFull) : -1; break;
-        case kMetaSeedHi: v = post ? (int)(uint32_t)(seed >> 32) : -1; break;
-        case kMetaReq: v = post ? 0 : -1; break;   // the single request's parameter slot
-        default: v = -1;
-      }
+      const int stored = reinterpret_cast<const int*>(f + b)[min(k, (int)kMetaSecond)];
+      // post rows: kind, first, second, the draw counter and row, the seed, and
+      // the single request's parameter slot 0
+      const int readout = k == kMetaCycle ? draw : k == kMetaDrawRow ? b : k == kMetaSeedLo ? lo
+                        : k == kMetaSeedHi ? hi : k == kMetaReq ? 0 : stored;
+      v = k <= kMetaStateOut ? stored : k == kMetaAhead ? 0 : post ? readout : -1;
     }
     m[i] = v;
   }
