@@ -60,14 +60,15 @@ typedef struct ls_sched_cfg {
   int32_t use_pdl;           /* programmatic dependent launch between kernels */
   int32_t max_requests;      /* requests ls_generate_batch serves together (0: 1);
                                 request_rows / kv_slots size each of them      */
-  int32_t device_loop;       /* 1: ls_generate runs a greedy LoopSpec request as
-                                one captured graph per cycle with the scheduler
-                                on the GPU (no host round trip between cycles),
-                                when the schedule fits (<= 16 live lanes, S <= 8,
-                                K <= 8), one request is configured, kv_slots is 0
-                                and its KV pool stays within 24 GB; otherwise,
-                                and for sampling, streaming callbacks or batches,
-                                the host drives each cycle                       */
+  int32_t device_loop;       /* 1: ls_generate runs a LoopSpec request, greedy
+                                or sampled, as captured graphs of 8 cycles with
+                                the scheduler on the GPU (no host round trip
+                                between cycles), when the schedule fits (<= 16
+                                live lanes, S <= 8, K <= 8), one request is
+                                configured, kv_slots is 0 and its KV pool stays
+                                within 24 GB; otherwise, and for streaming
+                                callbacks, tensor parallelism or batches, the
+                                host drives each cycle                           */
 } ls_sched_cfg;
 
 /* Counters of sglang_recurrent/loopspec/executor.py:35-45 plus timing. */

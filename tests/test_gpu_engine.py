@@ -237,7 +237,7 @@ def test_fused_lm_head_argmax_takes_the_lowest_index_of_equal_maxima(lo, hi):
 @pytest.mark.parametrize("name,K,X", [("tiny", 1, 2), ("tiny", 1, None), ("tiny", 2, None),
                                       ("tiny-raven-llama", 2, 2)])
 def test_device_loop_equals_host_loop(name, K, X):
-    """The device-resident loop (scheduler on the GPU, one graph per cycle, no
+    """The device-resident loop (scheduler on the GPU, 8 cycles per graph, no
     host round trip between cycles) commits the host loop's tokens and counts
     the same pipeline events, also when an EOS id ends the request early."""
     cfg, dev, _ = make(name, K, X)
